@@ -1,0 +1,507 @@
+#!/usr/bin/env python
+"""GDN-2 B200 benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload: chunkwise GDN-2 forward + backward, bf16
+activations, fp32 decay / state / accumulation, B=8 T=4096 H=16 K=V=128,
+chunk 64, scalar beta and log-decay broadcast through the channel-wise API,
+seeded synthetic inputs (no dataset is involved).  A step is one forward and
+one backward over the whole batch.  Under torchrun every rank runs its own
+batch (data/batch sharding, no collective on the data path: weak scaling);
+the reported time is the max over ranks.
+
+* ``value``: tokens/s of the whole job with inputs resident in HBM; the step
+  is the four kernel phases called through the C ABI, each bracketed by CUDA
+  events on the launch stream, which also gives the live per-kernel roofline.
+* ``e2e``: the same metric through the public API (``chunk_gdn2`` + autograd)
+  with the step's inputs copied from pinned host memory and every gradient
+  (and the output) read back to the host inside the timed region.
+* ``decode``: BASELINE config 2 (B=256 H=16 K=V=128 fp32 state, in-place
+  recurrent step, bf16 inputs), state read+write GB/s.
+* ``cpu_baseline``: the reference algorithm's CPU path (PyTorch restatement in
+  oracle/gdn2_torch_port.py, fp32, autograd backward), all host threads, on a
+  bounded slice of the same workload; rank 0 at N=1 only.
+
+``--impl reference`` times only that CPU path (the reference itself is pure
+Python and cannot run on the GPU box), on the same metric and unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.nn.functional as F
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, T, H, K, V, C = 8, 4096, 16, 128, 128, 64
+DEC_B, DEC_STEPS, DEC_SETS = 256, 1024, 32
+FALLBACK_HBM_GBS = 6650.0
+
+# Algorithmic bytes per token-head moved by each kernel (bf16 token tensors,
+# fp32 decay/gl, 64-token chunks, K = V = 128):
+#   fwd_intra : reads q,k,b,v,w (5x256) + g (512); writes Qg,Kd,W,U (4x256)
+#               + Aqk, A (2x128) + gl (8)                               = 3080
+#   fwd_state : reads Qg,Kd,W (768) + U (256) + Aqk (128) + gl (8);
+#               writes o (256) + VN (256) + h checkpoint (K*V*2/64 = 512) = 2184
+#   bwd_state : reads Qg,Kd,W,Aqk,gl (904) + dO (256);
+#               writes dh checkpoint (512) + dVN (256)                  = 1928
+#   bwd_intra : reads q,k,b,g,v,w (1792) + dO (256) + A (128) + VN (256)
+#               + h (512) + dh (512) + dVN (256) + gl (8);
+#               writes dq,dk,db (768) + dg (512) + dv,dw (512)          = 5512
+PHASE_BYTES = {"fwd_intra": 3080, "fwd_state": 2184, "bwd_state": 1928, "bwd_intra": 5512}
+# Algorithmic FLOPs per token-head (C = 64, K = V = 128), for context:
+#   fwd_intra 6CK+2CV, fwd_state 6KV+2CV, bwd_state 6KV+2CV,
+#   bwd_intra 6KV+6CV+12CK+4C^2
+PHASE_FLOPS = {
+    "fwd_intra": 6 * C * K + 2 * C * V,
+    "fwd_state": 6 * K * V + 2 * C * V,
+    "bwd_state": 6 * K * V + 2 * C * V,
+    "bwd_intra": 6 * K * V + 6 * C * V + 12 * C * K + 4 * C * C,
+}
+# DRAM traffic (read + write bytes) per launch of the dominant kernel from the
+# ncu capture summarised under profiles/ (None until captured).
+NCU_TRAFFIC_PER_TOKEN_HEAD = None
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 1643.0)), "measured"
+    return FALLBACK_HBM_GBS, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        time.sleep(0.3)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sms, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return None
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------
+# inputs
+# ---------------------------------------------------------------------------
+def make_config1(device, seed):
+    """Config-1 inputs as in config 0's recipe: q, k ~ N(0,1) L2-normalised,
+    v ~ N(0,1), beta = sigmoid(N(0,1)), g = logsigmoid(N(3,1)) per token and
+    head, broadcast channel-wise; dO ~ N(0,1)."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    bf = torch.bfloat16
+    q = F.normalize(torch.randn(B, T, H, K, device=device, generator=gen), dim=-1).to(bf)
+    k = F.normalize(torch.randn(B, T, H, K, device=device, generator=gen), dim=-1).to(bf)
+    v = torch.randn(B, T, H, V, device=device, generator=gen).to(bf)
+    beta = torch.sigmoid(torch.randn(B, T, H, device=device, generator=gen))
+    gs = F.logsigmoid(torch.randn(B, T, H, device=device, generator=gen) + 3.0)
+    g = gs[..., None].expand(B, T, H, K).contiguous()
+    b = beta[..., None].expand(B, T, H, K).to(bf).contiguous()
+    w = beta[..., None].expand(B, T, H, V).to(bf).contiguous()
+    do = torch.randn(B, T, H, V, device=device, generator=gen).to(bf)
+    return dict(q=q, k=k, v=v, g=g, b=b, w=w, do=do)
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def run_b200(args, world, rank, local):
+    from qwendopamine_b200 import _native as N
+    from qwendopamine_b200 import chunk_gdn2
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lib = N.load()
+    x = make_config1(dev, 1234 + rank)
+    tables = N.seq_tables(B, T, dev)
+    prob = N.ChunkProblem(H, K, V, N.dtype_code(torch.bfloat16), 1, K ** -0.5, tables.struct())
+    sbytes = lib.gdn2_chunk_saved_bytes(prob)
+    wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
+    saved = torch.empty(sbytes, dtype=torch.uint8, device=dev)
+    ws = torch.empty(wbytes, dtype=torch.uint8, device=dev)
+    o = torch.empty_like(x["v"])
+    grads = {n: torch.empty_like(x[n]) for n in ("q", "k", "v", "g", "b", "w")}
+    P = {n: N.ptr(t) for n, t in x.items()}
+    G = {n: N.ptr(t) for n, t in grads.items()}
+    st = N.stream_of(dev)
+    stream = torch.cuda.current_stream(dev)
+    phases = ("fwd_intra", "fwd_state", "bwd_state", "bwd_intra")
+
+    def step(evs):
+        evs[0].record(stream)
+        N.check(lib.gdn2_chunk_fwd_intra(prob, P["q"], P["k"], P["v"], P["g"], P["b"], P["w"],
+                                         N.ptr(saved), sbytes, st), "fwd_intra")
+        evs[1].record(stream)
+        N.check(lib.gdn2_chunk_fwd_state(prob, None, N.ptr(o), None, N.ptr(saved), sbytes, st),
+                "fwd_state")
+        evs[2].record(stream)
+        N.check(lib.gdn2_chunk_bwd_state(prob, N.ptr(saved), sbytes, P["do"], None, None,
+                                         N.ptr(ws), wbytes, st), "bwd_state")
+        evs[3].record(stream)
+        N.check(lib.gdn2_chunk_bwd_intra(prob, P["q"], P["k"], P["v"], P["g"], P["b"], P["w"],
+                                         N.ptr(saved), sbytes, P["do"], G["q"], G["k"], G["v"],
+                                         G["g"], G["b"], G["w"], N.ptr(ws), wbytes, st),
+                "bwd_intra")
+        evs[4].record(stream)
+
+    mk = lambda: [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    for _ in range(args.warmup):
+        step(mk())
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    evlist = [mk() for _ in range(args.steps)]
+    for evs in evlist:
+        step(evs)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    total_ms = evlist[0][0].elapsed_time(evlist[-1][4])
+    phase_ms = {ph: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evlist)
+                for i, ph in enumerate(phases)}
+    ms_step = max_over_ranks(total_ms / args.steps, world)
+    tokens = B * T * world
+    value = tokens / (ms_step / 1e3)
+
+    # ---- end to end through the public API with host buffers ---------------
+    host = {n: t.cpu().pin_memory() for n, t in x.items()}
+    out_host = {n: torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                for n, t in list(x.items())[:6]}
+    o_host = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = sum(t.numel() * t.element_size() for t in out_host.values()) + o_host.numel() * 2
+
+    def e2e_step():
+        d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
+        leaves = [d[n].requires_grad_() for n in ("q", "k", "v", "g", "b", "w")]
+        out, _ = chunk_gdn2(*leaves, use_qk_l2norm_in_kernel=True)
+        gr = torch.autograd.grad(out, leaves, d["do"])
+        o_host.copy_(out.detach(), non_blocking=True)
+        for (n, hbuf), gt in zip(out_host.items(), gr):
+            hbuf.copy_(gt, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    for _ in range(min(args.warmup, 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+    del host, out_host
+
+    # ---- decode (config 2) -------------------------------------------------
+    dec = run_decode(dev, lib, N) if rank == 0 else None
+
+    if rank != 0:
+        return
+    hbm, tflops_peak, peak_kind = peaks()
+    th = B * T * H  # token-heads per launch (one rank)
+    phase_info = {}
+    for ph in phases:
+        t_s = phase_ms[ph] / 1e3
+        phase_info[ph] = {
+            "ms": round(phase_ms[ph], 4),
+            "GBps": round(PHASE_BYTES[ph] * th / t_s / 1e9, 1),
+            "TFLOPs": round(PHASE_FLOPS[ph] * th / t_s / 1e12, 2),
+            "launches": args.steps,
+        }
+    dom = max(phases, key=lambda p: phase_ms[p])
+    ach = PHASE_BYTES[dom] * th / (phase_ms[dom] / 1e3) / 1e9
+    traffic = (NCU_TRAFFIC_PER_TOKEN_HEAD * th if NCU_TRAFFIC_PER_TOKEN_HEAD else None)
+    cpu = cpu_baseline() if world == 1 else None
+    line = {
+        "metric": "gdn2 fwd+bwd tokens/s (BASELINE config 1)",
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded; config-0 recipe at config-1 shapes)",
+        "config": {
+            "workload": "config1: chunk_gdn2 forward+backward",
+            "batch_per_gpu": B, "seq_len": T, "heads": H, "head_k": K, "head_v": V,
+            "chunk": C, "parallelism": f"batch-sharded x{world}, no data-path collective",
+            "l2": "inputs (>1 GB per step) exceed L2; no flush",
+        },
+        "gpu_launches": 4 * args.steps,
+        "e2e": {"value": round(B * T * world / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(ach / hbm, 4), "traffic": traffic,
+                     "peak_source": peak_kind,
+                     "bytes_per_token_head": PHASE_BYTES[dom]},
+        "phases": phase_info,
+        "tensor_peak_tflops": tflops_peak,
+        "decode": dec,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_decode(dev, lib, N):
+    """Config 2: one in-place recurrent step over B=256 sequences per call."""
+    gen = torch.Generator(device=dev).manual_seed(7)
+    bf = torch.bfloat16
+    state = torch.randn(DEC_B, H, K, V, device=dev, generator=gen) * 0.02
+    sets = []
+    for _ in range(DEC_SETS):
+        q = F.normalize(torch.randn(DEC_B, 1, H, K, device=dev, generator=gen), dim=-1).to(bf)
+        k = F.normalize(torch.randn(DEC_B, 1, H, K, device=dev, generator=gen), dim=-1).to(bf)
+        v = torch.randn(DEC_B, 1, H, V, device=dev, generator=gen).to(bf)
+        beta = torch.sigmoid(torch.randn(DEC_B, 1, H, device=dev, generator=gen))
+        gs = F.logsigmoid(torch.randn(DEC_B, 1, H, device=dev, generator=gen) + 3.0)
+        sets.append(dict(q=q, k=k, v=v, g=gs[..., None].expand(DEC_B, 1, H, K).contiguous(),
+                         b=beta[..., None].expand(DEC_B, 1, H, K).to(bf).contiguous(),
+                         w=beta[..., None].expand(DEC_B, 1, H, V).to(bf).contiguous(),
+                         o=torch.empty(DEC_B, 1, H, V, device=dev, dtype=bf)))
+    prob = N.RecurrentProblem(DEC_B, 1, H, H, K, V, N.dtype_code(bf), 1, K ** -0.5, DEC_B,
+                              None, None, 0)
+    st = N.stream_of(dev)
+    stream = torch.cuda.current_stream(dev)
+    ptrs = [tuple(N.ptr(s[n]) for n in ("q", "k", "v", "g", "b", "w", "o")) for s in sets]
+
+    def one(i):
+        p = ptrs[i % DEC_SETS]
+        N.check(lib.gdn2_recurrent_fwd(prob, *p[:6], N.ptr(state), p[6], N.ptr(state), st),
+                "decode")
+
+    for i in range(16):
+        one(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(DEC_STEPS):
+        one(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / DEC_STEPS
+    nbytes = 2 * DEC_B * H * K * V * 4
+    hbm, _, kind = peaks()
+    gbs = nbytes / (us / 1e6) / 1e9
+    return {"workload": "config2: B=256 H=16 K=V=128 fp32 state, in-place step, bf16 inputs",
+            "steps": DEC_STEPS, "us_per_step": round(us, 2), "GBps": round(gbs, 1),
+            "frac": round(gbs / hbm, 4), "state_bytes_per_step": nbytes,
+            "peak_source": kind, "gpu_launches": DEC_STEPS}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (reference algorithm, PyTorch CPU restatement)
+# ---------------------------------------------------------------------------
+CPU_SAMPLE_HEADS = 4
+
+
+def _cpu_sample_step(threads):
+    """One fwd+bwd of the reference CPU path on a bounded slice of config 1:
+    one sequence of T=4096 tokens and 4 of the 16 heads (fp32, autograd)."""
+    from oracle import gdn2_torch_port as P
+
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(0)
+    h = CPU_SAMPLE_HEADS
+    q = F.normalize(torch.randn(1, T, h, K, generator=gen), dim=-1).requires_grad_()
+    k = F.normalize(torch.randn(1, T, h, K, generator=gen), dim=-1).requires_grad_()
+    v = torch.randn(1, T, h, V, generator=gen).requires_grad_()
+    beta = torch.sigmoid(torch.randn(1, T, h, generator=gen))
+    gs = F.logsigmoid(torch.randn(1, T, h, generator=gen) + 3.0)
+    g = gs[..., None].expand(1, T, h, K).contiguous().requires_grad_()
+    b = beta[..., None].expand(1, T, h, K).contiguous().requires_grad_()
+    w = beta[..., None].expand(1, T, h, V).contiguous().requires_grad_()
+    do = torch.randn(1, T, h, V, generator=gen)
+    t0 = time.perf_counter()
+    o, _ = P.chunk_fwd(q, k, v, g, b, w, chunk_size=C)
+    torch.autograd.grad(o, (q, k, v, g, b, w), do)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(steps=1, warm=False):
+    threads = os.cpu_count() or 1
+    if warm:
+        _cpu_sample_step(threads)
+    ts = [_cpu_sample_step(threads) for _ in range(steps)]
+    t = min(ts)
+    full_tokens = T * CPU_SAMPLE_HEADS / H  # config-1 tokens the slice is worth
+    return {"value": round(full_tokens / t, 2), "unit": "tokens/s", "cores": threads,
+            "kind": "port",
+            "sample": (f"fwd+bwd of 1 sequence x T={T} x {CPU_SAMPLE_HEADS}/{H} heads, "
+                       f"K=V={K}, fp32, oracle/gdn2_torch_port.chunk_fwd + autograd; "
+                       f"{t:.2f} s per sample, best of {steps}; value scaled to config-1 "
+                       "tokens (all 16 heads)")}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        _cpu_sample_step(os.cpu_count() or 1)
+    ts = [_cpu_sample_step(os.cpu_count() or 1) for _ in range(args.steps)]
+    t = statistics.mean(ts)
+    full_tokens = T * CPU_SAMPLE_HEADS / H
+    value = full_tokens / t
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference",
+        "metric": "gdn2 fwd+bwd tokens/s (BASELINE config 1)",
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded; config-0 recipe at config-1 shapes)",
+        "config": {"workload": "config1: chunk_gdn2 forward+backward", "batch_per_gpu": B,
+                   "seq_len": T, "heads": H, "head_k": K, "head_v": V, "chunk": C},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores,
+                         "kind": "port",
+                         "sample": (f"each step: fwd+bwd of 1 sequence x T={T} x "
+                                    f"{CPU_SAMPLE_HEADS}/{H} heads, fp32, reference CPU "
+                                    "algorithm (torch_chunk_gdn2 + autograd) restated in "
+                                    "oracle/gdn2_torch_port.py; value scaled to config-1 "
+                                    "tokens")},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    args = ap.parse_args(argv)
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup()
+    try:
+        run_b200(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,192 @@
+/*
+ * gdn2_b200.h -- C ABI of the B200 GatedDeltaNet2 (GDN-2) core-recurrence library.
+ *
+ * The library (libgdn2_b200.so, built for sm_100a) replaces the Triton/FLA
+ * kernels behind the GDN-2 token mixer of Gabz4200/QwenDopamine:
+ *   - chunkwise forward   chunk_gdn2 / chunk_gdn2_fwd
+ *                         (src/qwendopamine/models/gdn2/gdn2_ops/chunk_gdn2.py:1165-1434)
+ *   - chunkwise backward  ChunkGDN2Function.backward / chunk_gdn2_bwd
+ *                         (chunk_gdn2.py:2170-2325, 2461-2547)
+ *   - recurrent decode    fused_recurrent_gdn2 / fused_recurrent_gdn2_fwd
+ *                         (gdn2_ops/fused_recurrent_gdn2.py:344-555)
+ *   - context-parallel pre-scan and merge (the FLA-CP algorithm of
+ *                         gdn2_ops/chunk_kda.py:182-1299, applied to GDN-2)
+ *
+ * Conventions
+ *   - Every pointer is device memory unless stated otherwise; the caller owns
+ *     all allocations (sizes come from the *_bytes queries below).
+ *   - Token tensors are contiguous [rows, H, D] where rows = B*T (fixed length)
+ *     or the packed token count (varlen, batch 1).  Sequence n owns rows
+ *     [cu_seqlens[n], cu_seqlens[n+1]) and is cut into chunks of 64 rows.
+ *   - Recurrent states are fp32, contiguous [N, H, K, V] (key-major).
+ *   - Every entry point returns GDN2_OK (0) or an error code; after an error,
+ *     gdn2_last_error() returns a message for the calling thread.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*); calls are
+ *     asynchronous with respect to the host.
+ */
+#ifndef GDN2_B200_H
+#define GDN2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of token tensors */
+enum {
+    GDN2_DTYPE_F32 = 0,
+    GDN2_DTYPE_BF16 = 1,
+    GDN2_DTYPE_F16 = 2
+};
+
+/* status codes */
+enum {
+    GDN2_OK = 0,
+    GDN2_ERR_INVALID = 1,     /* bad argument: shape, dtype, null pointer, size */
+    GDN2_ERR_UNSUPPORTED = 2, /* valid but not implemented (e.g. K > 128)       */
+    GDN2_ERR_CUDA = 3,        /* a CUDA runtime call failed                     */
+    GDN2_ERR_WORKSPACE = 4    /* caller-provided buffer too small               */
+};
+
+/* Sequence / chunk geometry shared by the chunkwise entry points.
+ * cu_seqlens[N+1] (token offsets), chunk_offsets[N+1] (chunk offsets,
+ * chunk_offsets[n+1]-chunk_offsets[n] = ceil(len_n/64)) and chunk_seq[n_chunks]
+ * (owning sequence of each chunk) are int32 device arrays; the Python layer
+ * builds them the way prepare_chunk_indices does (chunk_gdn2.py:1385-1389). */
+typedef struct gdn2_seqs {
+    int64_t total_tokens;
+    int32_t n_seqs;
+    int32_t n_chunks;
+    const int32_t* cu_seqlens;
+    const int32_t* chunk_offsets;
+    const int32_t* chunk_seq;
+} gdn2_seqs;
+
+/* A chunkwise problem: q,k,g,b are [rows,H,K]; v,w,o are [rows,H,V].
+ * g (and dg) are always fp32 (the module's fp32_decay=True default,
+ * gdn2.py:840-845); q,k,v,b,w,o and their gradients share `dtype`. */
+typedef struct gdn2_chunk_problem {
+    int32_t H, K, V;
+    int32_t dtype;
+    int32_t use_qk_l2norm; /* use_qk_l2norm_in_kernel (chunk_gdn2.py:1283) */
+    float scale;           /* defaults to K**-0.5 on the Python side        */
+    gdn2_seqs seqs;
+} gdn2_chunk_problem;
+
+/* ---- library information ------------------------------------------------ */
+const char* gdn2_version(void);
+const char* gdn2_status_string(int status);
+const char* gdn2_last_error(void);
+
+/* ---- chunkwise forward ---------------------------------------------------
+ * Replaces chunk_gdn2_fwd (chunk_gdn2.py:1165-1264) and its kernels K1-K7
+ * (intra-chunk scores, WY inverse, w/u recompute, inter-chunk state pass and
+ * output).  `saved` receives the per-chunk intermediates the backward needs
+ * (the ctx.save_for_backward set of chunk_gdn2.py:2425-2448, in B200 layout);
+ * its size is gdn2_chunk_saved_bytes().  h0 / ht may be NULL (zero initial
+ * state / no final state).  The two phases are also exported separately so a
+ * context-parallel caller can run the pre-scan between them. */
+size_t gdn2_chunk_saved_bytes(const gdn2_chunk_problem* p);
+int gdn2_chunk_fwd(const gdn2_chunk_problem* p,
+                   const void* q, const void* k, const void* v, const float* g,
+                   const void* b, const void* w, const float* h0,
+                   void* o, float* ht, void* saved, size_t saved_bytes,
+                   void* stream);
+/* phase 1: intra-chunk solve (fully parallel over chunks and heads) */
+int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p,
+                         const void* q, const void* k, const void* v, const float* g,
+                         const void* b, const void* w,
+                         void* saved, size_t saved_bytes, void* stream);
+/* phase 2: inter-chunk state pass with fused output (sequential over chunks) */
+int gdn2_chunk_fwd_state(const gdn2_chunk_problem* p, const float* h0,
+                         void* o, float* ht, void* saved, size_t saved_bytes,
+                         void* stream);
+
+/* ---- chunkwise backward --------------------------------------------------
+ * Replaces chunk_gdn2_bwd (chunk_gdn2.py:2170-2325): reverse state pass
+ * (K10), dq/dk/dv/db/dw/dg (K9, K11, K12, K13) and the l2norm backward.
+ * dht / dh0 / h0 may be NULL.  `workspace` is gdn2_chunk_bwd_workspace_bytes(). */
+size_t gdn2_chunk_bwd_workspace_bytes(const gdn2_chunk_problem* p);
+int gdn2_chunk_bwd(const gdn2_chunk_problem* p,
+                   const void* q, const void* k, const void* v, const float* g,
+                   const void* b, const void* w,
+                   const void* saved, size_t saved_bytes,
+                   const void* dout, const float* dht,
+                   void* dq, void* dk, void* dv, float* dg, void* db, void* dw,
+                   float* dh0, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* phase 1: reverse state pass (sequential over chunks); fills `workspace`
+ * with the per-chunk state gradients and dVN, writes dh0 when non-NULL */
+int gdn2_chunk_bwd_state(const gdn2_chunk_problem* p, const void* saved,
+                         size_t saved_bytes, const void* dout, const float* dht,
+                         float* dh0, void* workspace, size_t workspace_bytes,
+                         void* stream);
+/* phase 2: per-chunk gradients (fully parallel over chunks and heads) */
+int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p,
+                         const void* q, const void* k, const void* v, const float* g,
+                         const void* b, const void* w,
+                         const void* saved, size_t saved_bytes, const void* dout,
+                         void* dq, void* dk, void* dv, float* dg, void* db, void* dw,
+                         const void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- recurrent (decode) forward ------------------------------------------
+ * Replaces fused_recurrent_gdn2_fwd (fused_recurrent_gdn2.py:344-458) and its
+ * kernel (:117-341).  q,k: [B,T,H,K]; v,w: [B,T,HV,V]; g,b: [B,T,HV,K]
+ * (HV a multiple of H: grouped value heads).  With cu_seqlens (int32 [N+1],
+ * B == 1) sequences are packed.  With state_indices (int32 [N]) h0 and ht are
+ * state pools indexed per sequence (slot stride state_stride elements) and
+ * the update is in place; otherwise h0 / ht are [N,HV,K,V] and ht may equal h0
+ * for an in-place update.  h0 == NULL means zero state; ht == NULL means the
+ * final state is not stored. */
+typedef struct gdn2_recurrent_problem {
+    int32_t B, T, H, HV, K, V;
+    int32_t dtype;
+    int32_t use_qk_l2norm;
+    float scale;
+    int32_t n_seqs;
+    const int32_t* cu_seqlens;
+    const int32_t* state_indices;
+    int64_t state_stride;
+} gdn2_recurrent_problem;
+
+int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p,
+                       const void* q, const void* k, const void* v, const float* g,
+                       const void* b, const void* w, const float* h0,
+                       void* o, float* ht, void* stream);
+
+/* ---- context parallelism (sequence-parallel long context) ----------------
+ * Each rank owns a contiguous span of whole chunks of one sequence set.
+ * Forward: after gdn2_chunk_fwd_intra, gdn2_cp_fwd_prescan writes this rank's
+ * affine span map  S_out = M S_in + h_e  as hm = [N,H,K,V+K] fp32
+ * (h_e in columns [0,V), M in columns [V,V+K)), the message that FLA-CP
+ * all-gathers (chunk_kda.py:1101-1185).  After the all-gather, gdn2_cp_merge
+ * folds the maps of ranks 0..rank-1 into this rank's initial state
+ * (chunk_kda.py:509-697, FORWARD=True).
+ * Backward: gdn2_cp_bwd_prescan writes dhm = [N,H,K,V] (the state gradient a
+ * zero dht produces at this span's start); gdn2_cp_merge with forward=0 folds
+ * ranks world-1..rank+1 (using their forward M, transposed) into this rank's
+ * dht.  `hm_all` is [world, N, H, K, V+K] and `dhm_all` is [world, N, H, K, V]
+ * (rank-major, the layout all_gather_into_tensor produces).
+ *   forward=1:  x = init (or 0);  for j = 0 .. rank-1:        x = M_j x + h_e_j
+ *   forward=0:  x = init (or 0);  for j = world-1 .. rank+1:  x = M_j^T x + dhm_j
+ * and state_out = x ([N,H,K,V] fp32).  `init` is the global initial state
+ * (forward) or the gradient of the global final state (backward). */
+size_t gdn2_cp_workspace_bytes(const gdn2_chunk_problem* p);
+int gdn2_cp_fwd_prescan(const gdn2_chunk_problem* p, const void* saved,
+                        size_t saved_bytes, float* hm, void* workspace,
+                        size_t workspace_bytes, void* stream);
+int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved,
+                        size_t saved_bytes, const void* dout, float* dhm,
+                        void* workspace, size_t workspace_bytes, void* stream);
+int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all,
+                  const float* dhm_all, int32_t rank, int32_t world,
+                  int32_t forward, const float* init, float* state_out,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GDN2_B200_H */

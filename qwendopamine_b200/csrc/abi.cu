@@ -1,0 +1,431 @@
+// abi.cu -- extern "C" entry points of libgdn2_b200.so (declared in
+// include/gdn2_b200.h): argument validation, dtype / head-size dispatch,
+// per-thread error messages, and the small context-parallel merge kernel.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/gdn2_b200.h"
+
+#include "chunk_args.cuh"
+
+namespace gdn2 {
+template <typename T, int D> cudaError_t launch_fwd_intra(const FwdIntraArgs&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_fwd_state(const FwdStateArgs&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_bwd_state(const BwdStateArgs&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_bwd_intra(const BwdIntraArgs&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_recurrent(const RecArgs&, cudaStream_t);
+}  // namespace gdn2
+
+using namespace gdn2;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(GDN2_ERR_CUDA, "%s: CUDA error %d (%s)", where, (int)e, cudaGetErrorString(e));
+}
+
+int esize_of(int dtype) { return dtype == GDN2_DTYPE_F32 ? 4 : 2; }
+
+bool dtype_ok(int dtype) {
+  return dtype == GDN2_DTYPE_F32 || dtype == GDN2_DTYPE_BF16 || dtype == GDN2_DTYPE_F16;
+}
+
+// Head size bucket: kernels are compiled for padded head sizes 64 and 128.
+int head_bucket(int K, int V) {
+  int m = K > V ? K : V;
+  return m <= 64 ? 64 : 128;
+}
+
+int check_problem(const gdn2_chunk_problem* p, const char* fn) {
+  if (!p) return fail(GDN2_ERR_INVALID, "%s: null problem", fn);
+  if (p->H <= 0 || p->K <= 0 || p->V <= 0)
+    return fail(GDN2_ERR_INVALID, "%s: H, K, V must be positive (got %d, %d, %d)", fn, p->H, p->K,
+                p->V);
+  if (p->K > 128 || p->V > 128)
+    return fail(GDN2_ERR_UNSUPPORTED, "%s: head sizes up to 128 are supported (K=%d, V=%d)", fn,
+                p->K, p->V);
+  if (!dtype_ok(p->dtype)) return fail(GDN2_ERR_INVALID, "%s: unknown dtype %d", fn, p->dtype);
+  if (p->seqs.n_seqs < 0 || p->seqs.n_chunks < 0)
+    return fail(GDN2_ERR_INVALID, "%s: negative sequence or chunk count", fn);
+  if (p->seqs.n_seqs > 0 && (!p->seqs.cu_seqlens || !p->seqs.chunk_offsets))
+    return fail(GDN2_ERR_INVALID, "%s: missing sequence tables", fn);
+  if (p->seqs.n_chunks > 0 && !p->seqs.chunk_seq)
+    return fail(GDN2_ERR_INVALID, "%s: missing chunk table", fn);
+  if ((int64_t)p->seqs.n_chunks * p->H > 2147483647LL)
+    return fail(GDN2_ERR_UNSUPPORTED, "%s: too many chunks", fn);
+  return GDN2_OK;
+}
+
+Seqs make_seqs(const gdn2_chunk_problem* p) {
+  Seqs s;
+  s.cu = p->seqs.cu_seqlens;
+  s.coff = p->seqs.chunk_offsets;
+  s.cseq = p->seqs.chunk_seq;
+  s.n_seqs = p->seqs.n_seqs;
+  s.n_chunks = p->seqs.n_chunks;
+  return s;
+}
+
+SavedLayout layout_of(const gdn2_chunk_problem* p) {
+  return saved_layout(p->seqs.n_chunks, p->H, p->K, p->V, esize_of(p->dtype));
+}
+
+BwdLayout bwd_layout_of(const gdn2_chunk_problem* p) {
+  return bwd_layout(p->seqs.n_chunks, p->H, p->K, p->V, esize_of(p->dtype));
+}
+
+template <template <typename, int> class F, typename Args>
+cudaError_t dispatch(int dtype, int bucket, const Args& a, cudaStream_t st) {
+  if (dtype == GDN2_DTYPE_F32)
+    return bucket == 64 ? F<float, 64>::run(a, st) : F<float, 128>::run(a, st);
+  if (dtype == GDN2_DTYPE_BF16)
+    return bucket == 64 ? F<__nv_bfloat16, 64>::run(a, st) : F<__nv_bfloat16, 128>::run(a, st);
+  return bucket == 64 ? F<__half, 64>::run(a, st) : F<__half, 128>::run(a, st);
+}
+
+template <typename T, int D> struct RunFwdIntra {
+  static cudaError_t run(const FwdIntraArgs& a, cudaStream_t s) { return launch_fwd_intra<T, D>(a, s); }
+};
+template <typename T, int D> struct RunFwdState {
+  static cudaError_t run(const FwdStateArgs& a, cudaStream_t s) { return launch_fwd_state<T, D>(a, s); }
+};
+template <typename T, int D> struct RunBwdState {
+  static cudaError_t run(const BwdStateArgs& a, cudaStream_t s) { return launch_bwd_state<T, D>(a, s); }
+};
+template <typename T, int D> struct RunBwdIntra {
+  static cudaError_t run(const BwdIntraArgs& a, cudaStream_t s) { return launch_bwd_intra<T, D>(a, s); }
+};
+template <typename T, int D> struct RunRec {
+  static cudaError_t run(const RecArgs& a, cudaStream_t s) { return launch_recurrent<T, D>(a, s); }
+};
+
+// ---- context-parallel merge ----------------------------------------------
+// One CTA per (sequence, head, 32-column tile of the state); the running
+// state tile x (K x 32) lives in shared memory and each folded rank applies
+// x <- M x + h_e (forward) or x <- M^T x + dh_e (backward), reading M from
+// the gathered buffer.
+__global__ void k_cp_merge(int N, int H, int K, int V, const float* hm_all, const float* dhm_all,
+                           int rank, int world, int forward, const float* init, float* out) {
+  extern __shared__ float sx[];   // [2][K][32]
+  float* x = sx;
+  float* y = sx + K * 32;
+  const int nh = blockIdx.y, v0 = blockIdx.x * 32;
+  const int tid = threadIdx.x;
+  const int VK = V + K;
+  const int64_t per_rank_hm = (int64_t)N * H * K * VK;
+  const int64_t per_rank_dh = (int64_t)N * H * K * V;
+  for (int idx = tid; idx < K * 32; idx += blockDim.x) {
+    int r = idx >> 5, c = idx & 31, col = v0 + c;
+    x[idx] = (init && col < V) ? init[((int64_t)nh * K + r) * V + col] : 0.f;
+  }
+  __syncthreads();
+  const int j_begin = forward ? 0 : world - 1;
+  const int j_end = forward ? rank : rank;  // exclusive bound in the walking direction
+  for (int j = j_begin; forward ? (j < j_end) : (j > j_end); j += forward ? 1 : -1) {
+    const float* hm = hm_all + j * per_rank_hm + (int64_t)nh * K * VK;
+    for (int idx = tid; idx < K * 32; idx += blockDim.x) {
+      int r = idx >> 5, c = idx & 31, col = v0 + c;
+      float s = 0.f;
+      if (col < V) {
+        if (forward) {
+          for (int m = 0; m < K; ++m) s += hm[(int64_t)r * VK + V + m] * x[m * 32 + c];
+          s += hm[(int64_t)r * VK + col];
+        } else {
+          for (int m = 0; m < K; ++m) s += hm[(int64_t)m * VK + V + r] * x[m * 32 + c];
+          s += dhm_all[j * per_rank_dh + ((int64_t)nh * K + r) * V + col];
+        }
+      }
+      y[idx] = s;
+    }
+    __syncthreads();
+    float* t = x;
+    x = y;
+    y = t;
+  }
+  for (int idx = tid; idx < K * 32; idx += blockDim.x) {
+    int r = idx >> 5, c = idx & 31, col = v0 + c;
+    if (col < V) out[((int64_t)nh * K + r) * V + col] = x[idx];
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gdn2_version(void) { return "gdn2_b200 0.1.0 (sm_100a)"; }
+
+const char* gdn2_status_string(int status) {
+  switch (status) {
+    case GDN2_OK: return "ok";
+    case GDN2_ERR_INVALID: return "invalid argument";
+    case GDN2_ERR_UNSUPPORTED: return "unsupported configuration";
+    case GDN2_ERR_CUDA: return "CUDA error";
+    case GDN2_ERR_WORKSPACE: return "buffer too small";
+    default: return "unknown status";
+  }
+}
+
+const char* gdn2_last_error(void) { return g_last_error.c_str(); }
+
+size_t gdn2_chunk_saved_bytes(const gdn2_chunk_problem* p) {
+  if (check_problem(p, "gdn2_chunk_saved_bytes") != GDN2_OK) return 0;
+  return layout_of(p).total;
+}
+
+size_t gdn2_chunk_bwd_workspace_bytes(const gdn2_chunk_problem* p) {
+  if (check_problem(p, "gdn2_chunk_bwd_workspace_bytes") != GDN2_OK) return 0;
+  return bwd_layout_of(p).total;
+}
+
+size_t gdn2_cp_workspace_bytes(const gdn2_chunk_problem* p) {
+  (void)p;
+  return 0;
+}
+
+int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p, const void* q, const void* k, const void* v,
+                         const float* g, const void* b, const void* w, void* saved,
+                         size_t saved_bytes, void* stream) {
+  int rc = check_problem(p, "gdn2_chunk_fwd_intra");
+  if (rc) return rc;
+  if (p->seqs.n_chunks == 0) return GDN2_OK;
+  if (!q || !k || !v || !g || !b || !w || !saved)
+    return fail(GDN2_ERR_INVALID, "gdn2_chunk_fwd_intra: null tensor pointer");
+  SavedLayout L = layout_of(p);
+  if (saved_bytes < L.total)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_fwd_intra: saved buffer %zu < %zu bytes",
+                saved_bytes, L.total);
+  FwdIntraArgs a;
+  a.seqs = make_seqs(p);
+  a.H = p->H; a.K = p->K; a.V = p->V;
+  a.scale = p->scale;
+  a.l2norm = p->use_qk_l2norm;
+  a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
+  a.saved = static_cast<unsigned char*>(saved);
+  a.L = L;
+  cudaError_t e = dispatch<RunFwdIntra>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_fwd_intra");
+}
+
+int gdn2_chunk_fwd_state(const gdn2_chunk_problem* p, const float* h0, void* o, float* ht,
+                         void* saved, size_t saved_bytes, void* stream) {
+  int rc = check_problem(p, "gdn2_chunk_fwd_state");
+  if (rc) return rc;
+  if (p->seqs.n_seqs == 0) return GDN2_OK;
+  if (!o || !saved) return fail(GDN2_ERR_INVALID, "gdn2_chunk_fwd_state: null o or saved");
+  SavedLayout L = layout_of(p);
+  if (saved_bytes < L.total)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_fwd_state: saved buffer %zu < %zu bytes",
+                saved_bytes, L.total);
+  FwdStateArgs a;
+  a.seqs = make_seqs(p);
+  a.H = p->H; a.K = p->K; a.V = p->V;
+  a.h0 = h0; a.o = o; a.ht = ht;
+  a.saved = static_cast<unsigned char*>(saved);
+  a.L = L;
+  a.prescan = 0;
+  a.hm = nullptr;
+  cudaError_t e = dispatch<RunFwdState>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_fwd_state");
+}
+
+int gdn2_chunk_fwd(const gdn2_chunk_problem* p, const void* q, const void* k, const void* v,
+                   const float* g, const void* b, const void* w, const float* h0, void* o,
+                   float* ht, void* saved, size_t saved_bytes, void* stream) {
+  int rc = gdn2_chunk_fwd_intra(p, q, k, v, g, b, w, saved, saved_bytes, stream);
+  if (rc) return rc;
+  return gdn2_chunk_fwd_state(p, h0, o, ht, saved, saved_bytes, stream);
+}
+
+int gdn2_chunk_bwd_state(const gdn2_chunk_problem* p, const void* saved, size_t saved_bytes,
+                         const void* dout, const float* dht, float* dh0, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  int rc = check_problem(p, "gdn2_chunk_bwd_state");
+  if (rc) return rc;
+  if (!saved || !dout) return fail(GDN2_ERR_INVALID, "gdn2_chunk_bwd_state: null tensor pointer");
+  SavedLayout L = layout_of(p);
+  BwdLayout BL = bwd_layout_of(p);
+  if (saved_bytes < L.total)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_bwd_state: saved buffer %zu < %zu bytes",
+                saved_bytes, L.total);
+  if (workspace_bytes < BL.total || (!workspace && BL.total))
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_bwd_state: workspace %zu < %zu bytes",
+                workspace_bytes, BL.total);
+  if (p->seqs.n_seqs == 0) return GDN2_OK;
+  BwdStateArgs s;
+  s.seqs = make_seqs(p);
+  s.H = p->H; s.K = p->K; s.V = p->V;
+  s.dout = dout; s.dht = dht; s.dh0 = dh0;
+  s.saved = static_cast<const unsigned char*>(saved);
+  s.L = L;
+  s.ws = static_cast<unsigned char*>(workspace);
+  s.BL = BL;
+  s.prescan = 0;
+  cudaError_t e = dispatch<RunBwdState>(p->dtype, head_bucket(p->K, p->V), s, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_bwd_state");
+}
+
+int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void* k,
+                         const void* v, const float* g, const void* b, const void* w,
+                         const void* saved, size_t saved_bytes, const void* dout, void* dq,
+                         void* dk, void* dv, float* dg, void* db, void* dw,
+                         const void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_problem(p, "gdn2_chunk_bwd_intra");
+  if (rc) return rc;
+  if (!q || !k || !v || !g || !b || !w || !saved || !dout || !dq || !dk || !dv || !dg || !db || !dw)
+    return fail(GDN2_ERR_INVALID, "gdn2_chunk_bwd_intra: null tensor pointer");
+  SavedLayout L = layout_of(p);
+  BwdLayout BL = bwd_layout_of(p);
+  if (saved_bytes < L.total)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_bwd_intra: saved buffer %zu < %zu bytes",
+                saved_bytes, L.total);
+  if (workspace_bytes < BL.total || (!workspace && BL.total))
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_bwd_intra: workspace %zu < %zu bytes",
+                workspace_bytes, BL.total);
+  if (p->seqs.n_chunks == 0) return GDN2_OK;
+  BwdIntraArgs a;
+  a.seqs = make_seqs(p);
+  a.H = p->H; a.K = p->K; a.V = p->V;
+  a.scale = p->scale;
+  a.l2norm = p->use_qk_l2norm;
+  a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
+  a.dout = dout;
+  a.saved = static_cast<const unsigned char*>(saved);
+  a.L = L;
+  a.ws = static_cast<const unsigned char*>(workspace);
+  a.BL = BL;
+  a.dq = dq; a.dk = dk; a.dv = dv; a.dg = dg; a.db = db; a.dw = dw;
+  cudaError_t e = dispatch<RunBwdIntra>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_bwd_intra");
+}
+
+int gdn2_chunk_bwd(const gdn2_chunk_problem* p, const void* q, const void* k, const void* v,
+                   const float* g, const void* b, const void* w, const void* saved,
+                   size_t saved_bytes, const void* dout, const float* dht, void* dq, void* dk,
+                   void* dv, float* dg, void* db, void* dw, float* dh0, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  int rc = gdn2_chunk_bwd_state(p, saved, saved_bytes, dout, dht, dh0, workspace,
+                                workspace_bytes, stream);
+  if (rc) return rc;
+  return gdn2_chunk_bwd_intra(p, q, k, v, g, b, w, saved, saved_bytes, dout, dq, dk, dv, dg, db,
+                              dw, workspace, workspace_bytes, stream);
+}
+
+int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p, const void* q, const void* k,
+                       const void* v, const float* g, const void* b, const void* w,
+                       const float* h0, void* o, float* ht, void* stream) {
+  if (!p) return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: null problem");
+  if (p->B <= 0 || p->T < 0 || p->H <= 0 || p->HV <= 0 || p->K <= 0 || p->V <= 0)
+    return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: bad sizes B=%d T=%d H=%d HV=%d K=%d V=%d",
+                p->B, p->T, p->H, p->HV, p->K, p->V);
+  if (p->HV % p->H != 0)
+    return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: HV=%d is not a multiple of H=%d", p->HV,
+                p->H);
+  if (p->K > 128 || p->V > 128)
+    return fail(GDN2_ERR_UNSUPPORTED, "gdn2_recurrent_fwd: head sizes up to 128 are supported");
+  if (!dtype_ok(p->dtype)) return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: unknown dtype");
+  if (p->cu_seqlens && p->B != 1)
+    return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: cu_seqlens requires B == 1 (got %d)", p->B);
+  if (!p->cu_seqlens && p->n_seqs != p->B)
+    return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: n_seqs (%d) must equal B (%d)", p->n_seqs,
+                p->B);
+  if (p->state_indices && p->state_stride < (int64_t)p->HV * p->K * p->V)
+    return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: state_stride too small");
+  if (!q || !k || !v || !g || !b || !w || !o)
+    return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: null tensor pointer");
+  if (p->n_seqs == 0) return GDN2_OK;
+  RecArgs a;
+  a.B = p->B; a.T = p->T; a.H = p->H; a.HV = p->HV; a.K = p->K; a.V = p->V;
+  a.scale = p->scale;
+  a.l2norm = p->use_qk_l2norm;
+  a.n_seqs = p->n_seqs;
+  a.cu = p->cu_seqlens;
+  a.state_idx = p->state_indices;
+  a.state_stride = p->state_stride;
+  a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
+  a.h0 = h0; a.o = o; a.ht = ht;
+  cudaError_t e = dispatch<RunRec>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_recurrent_fwd");
+}
+
+int gdn2_cp_fwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t saved_bytes,
+                        float* hm, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  int rc = check_problem(p, "gdn2_cp_fwd_prescan");
+  if (rc) return rc;
+  if (!saved || !hm) return fail(GDN2_ERR_INVALID, "gdn2_cp_fwd_prescan: null pointer");
+  SavedLayout L = layout_of(p);
+  if (saved_bytes < L.total)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_cp_fwd_prescan: saved buffer too small");
+  if (p->seqs.n_seqs == 0) return GDN2_OK;
+  FwdStateArgs a;
+  a.seqs = make_seqs(p);
+  a.H = p->H; a.K = p->K; a.V = p->V;
+  a.h0 = nullptr; a.o = nullptr; a.ht = nullptr;
+  a.saved = static_cast<unsigned char*>(const_cast<void*>(saved));
+  a.L = L;
+  a.prescan = 1;
+  a.hm = hm;
+  cudaError_t e = dispatch<RunFwdState>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_fwd_prescan");
+}
+
+int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t saved_bytes,
+                        const void* dout, float* dhm, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  int rc = check_problem(p, "gdn2_cp_bwd_prescan");
+  if (rc) return rc;
+  if (!saved || !dout || !dhm) return fail(GDN2_ERR_INVALID, "gdn2_cp_bwd_prescan: null pointer");
+  SavedLayout L = layout_of(p);
+  if (saved_bytes < L.total)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_cp_bwd_prescan: saved buffer too small");
+  if (p->seqs.n_seqs == 0) return GDN2_OK;
+  BwdStateArgs s;
+  s.seqs = make_seqs(p);
+  s.H = p->H; s.K = p->K; s.V = p->V;
+  s.dout = dout; s.dht = nullptr; s.dh0 = dhm;
+  s.saved = static_cast<const unsigned char*>(saved);
+  s.L = L;
+  s.ws = nullptr;
+  s.BL = bwd_layout_of(p);
+  s.prescan = 1;
+  cudaError_t e = dispatch<RunBwdState>(p->dtype, head_bucket(p->K, p->V), s, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_bwd_prescan");
+}
+
+int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all, const float* dhm_all,
+                  int32_t rank, int32_t world, int32_t forward, const float* init,
+                  float* state_out, void* stream) {
+  int rc = check_problem(p, "gdn2_cp_merge");
+  if (rc) return rc;
+  if (world <= 0 || rank < 0 || rank >= world)
+    return fail(GDN2_ERR_INVALID, "gdn2_cp_merge: rank %d outside world %d", rank, world);
+  if (!hm_all || !state_out || (!forward && !dhm_all))
+    return fail(GDN2_ERR_INVALID, "gdn2_cp_merge: null pointer");
+  const int N = p->seqs.n_seqs;
+  if (N == 0) return GDN2_OK;
+  dim3 grid((p->V + 31) / 32, N * p->H);
+  size_t smem = 2 * (size_t)p->K * 32 * sizeof(float);
+  k_cp_merge<<<grid, 256, smem, (cudaStream_t)stream>>>(N, p->H, p->K, p->V, hm_all, dhm_all, rank,
+                                                        world, forward, init, state_out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_merge");
+}
+
+}  // extern "C"

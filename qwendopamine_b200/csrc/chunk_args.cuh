@@ -1,0 +1,93 @@
+// chunk_args.cuh -- argument blocks passed by value to the GDN-2 kernels.
+// Shared by the kernel translation units and the C-ABI layer (abi.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace gdn2 {
+
+struct FwdIntraArgs {
+  Seqs seqs;
+  int H, K, V;
+  float scale;
+  int l2norm;
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const void* b;
+  const void* w;
+  unsigned char* saved;
+  SavedLayout L;
+};
+
+struct FwdStateArgs {
+  Seqs seqs;
+  int H, K, V;
+  const float* h0;   // [N,H,K,V] or null
+  void* o;           // [rows,H,V] or null (pre-scan)
+  float* ht;         // [N,H,K,V] or null
+  unsigned char* saved;
+  SavedLayout L;
+  // pre-scan mode: carry [h | M] over V+K columns from [0 | I]; write hm.
+  int prescan;
+  float* hm;         // [N,H,K,V+K]
+};
+
+struct BwdStateArgs {
+  Seqs seqs;
+  int H, K, V;
+  const void* dout;   // [rows,H,V]
+  const float* dht;   // [N,H,K,V] or null
+  float* dh0;         // [N,H,K,V] or null
+  const unsigned char* saved;
+  SavedLayout L;
+  unsigned char* ws;
+  BwdLayout BL;
+  int prescan;        // 1: write nothing per chunk, only the span-start gradient
+};
+
+struct BwdIntraArgs {
+  Seqs seqs;
+  int H, K, V;
+  float scale;
+  int l2norm;
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const void* b;
+  const void* w;
+  const void* dout;
+  const unsigned char* saved;
+  SavedLayout L;
+  const unsigned char* ws;
+  BwdLayout BL;
+  void* dq;
+  void* dk;
+  void* dv;
+  float* dg;
+  void* db;
+  void* dw;
+};
+
+struct RecArgs {
+  int B, T, H, HV, K, V;
+  float scale;
+  int l2norm;
+  int n_seqs;
+  const int32_t* cu;         // [N+1] or null
+  const int32_t* state_idx;  // [N] or null
+  int64_t state_stride;
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;
+  const void* b;
+  const void* w;
+  const float* h0;
+  void* o;
+  float* ht;
+};
+
+}  // namespace gdn2

@@ -1,0 +1,126 @@
+"""The C-ABI library loads, exports every symbol its header declares, and
+rejects bad arguments with the documented status codes -- all without a GPU
+(no call here reaches a CUDA API)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from qwendopamine_b200 import _native as N
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gdn2_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gdn2_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return N.load()
+
+
+def test_header_declares_the_binding_list():
+    assert declared_functions() == sorted(N.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(N.LIB_PATH)
+    for name in declared_functions():
+        assert hasattr(raw, name), name
+
+
+def test_version_and_status_strings(lib):
+    assert b"sm_100a" in lib.gdn2_version()
+    assert lib.gdn2_status_string(0) == b"ok"
+    assert lib.gdn2_status_string(1) == b"invalid argument"
+    assert lib.gdn2_status_string(99) == b"unknown status"
+
+
+def _problem(H=2, K=16, V=16, dtype=1, n_seqs=1, n_chunks=1, ptrs=True):
+    p = 0x1000 if ptrs else None
+    return N.ChunkProblem(H, K, V, dtype, 1, 0.25,
+                          N.Seqs(64, n_seqs, n_chunks, p, p, p))
+
+
+def test_saved_and_workspace_sizes_follow_the_layout(lib):
+    for dt, es in ((0, 4), (1, 2)):
+        H, K, V, nc = 3, 64, 32, 5
+        prob = _problem(H, K, V, dt, 1, nc)
+        nh = nc * H
+        al = lambda x: (x + 255) & ~255
+        off = 0
+        for rows in (64 * K, 64 * K, 64 * K, 64 * V, 64 * V, 64 * 64, 64 * 64):
+            off = al(off + nh * rows * es)
+        off = al(off + nh * K * 4)
+        off = al(off + nh * K * V * es)
+        assert lib.gdn2_chunk_saved_bytes(prob) == off
+        ws = al(nh * K * V * es)
+        ws = al(ws + nh * 64 * V * es)
+        assert lib.gdn2_chunk_bwd_workspace_bytes(prob) == ws
+
+
+def test_invalid_problem_is_rejected_with_message(lib):
+    bad = _problem(K=0)
+    assert lib.gdn2_chunk_saved_bytes(bad) == 0
+    assert b"positive" in lib.gdn2_last_error()
+    big = _problem(K=256)
+    assert lib.gdn2_chunk_fwd_intra(big, *([None] * 6), None, 0, None) == N.ERR_UNSUPPORTED
+    with pytest.raises(NotImplementedError):
+        N.check(N.ERR_UNSUPPORTED, "x")
+    nodtype = _problem(dtype=7)
+    assert lib.gdn2_chunk_fwd_state(nodtype, None, None, None, None, 0, None) == N.ERR_INVALID
+    notab = _problem(ptrs=False)
+    assert lib.gdn2_chunk_fwd(notab, *([None] * 10), 0, None) == N.ERR_INVALID
+    assert b"tables" in lib.gdn2_last_error()
+
+
+def test_null_pointers_and_short_buffers_are_rejected(lib):
+    prob = _problem()
+    rc = lib.gdn2_chunk_fwd_intra(prob, *([None] * 6), None, 0, None)
+    assert rc == N.ERR_INVALID and b"null" in lib.gdn2_last_error()
+    fake = ctypes.c_void_p(0x1000)
+    rc = lib.gdn2_chunk_fwd_intra(prob, *([fake] * 6), fake, 16, None)
+    assert rc == N.ERR_WORKSPACE and b"saved buffer" in lib.gdn2_last_error()
+    rc = lib.gdn2_chunk_bwd(prob, *([fake] * 6), fake, 1 << 40, fake, None, *([fake] * 6), None,
+                            fake, 1, None)
+    assert rc == N.ERR_WORKSPACE
+
+
+def test_recurrent_argument_checks(lib):
+    def rp(**kw):
+        base = dict(B=2, T=1, H=2, HV=2, K=16, V=16, dtype=1, use_qk_l2norm=1, scale=0.25,
+                    n_seqs=2, cu_seqlens=None, state_indices=None, state_stride=0)
+        base.update(kw)
+        return N.RecurrentProblem(**base)
+
+    f = ctypes.c_void_p(0x1000)
+    args = [f] * 6 + [None, f, None, None]
+    assert lib.gdn2_recurrent_fwd(rp(HV=3), *args) == N.ERR_INVALID
+    assert b"multiple" in lib.gdn2_last_error()
+    assert lib.gdn2_recurrent_fwd(rp(K=200), *args) == N.ERR_UNSUPPORTED
+    assert lib.gdn2_recurrent_fwd(rp(cu_seqlens=0x1000), *args) == N.ERR_INVALID
+    assert lib.gdn2_recurrent_fwd(rp(n_seqs=3), *args) == N.ERR_INVALID
+    assert lib.gdn2_recurrent_fwd(rp(state_indices=0x1000, state_stride=5), *args) == N.ERR_INVALID
+    assert lib.gdn2_recurrent_fwd(rp(), *([None] * 10)) == N.ERR_INVALID
+
+
+def test_cp_merge_argument_checks(lib):
+    prob = _problem()
+    f = ctypes.c_void_p(0x1000)
+    assert lib.gdn2_cp_merge(prob, f, f, 3, 2, 1, None, f, None) == N.ERR_INVALID
+    assert lib.gdn2_cp_merge(prob, f, None, 0, 2, 0, None, f, None) == N.ERR_INVALID
+
+
+def test_status_maps_to_python_exceptions(lib):
+    lib.gdn2_chunk_saved_bytes(_problem(K=0))
+    with pytest.raises(ValueError, match="invalid argument"):
+        N.check(N.ERR_INVALID, "probe")
+    with pytest.raises(N.GDN2Error):
+        N.check(N.ERR_CUDA, "probe")
+    N.check(N.OK, "probe")

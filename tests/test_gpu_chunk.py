@@ -1,0 +1,260 @@
+"""Parity of the B200 chunkwise forward/backward (through the C ABI) with the
+reference's golden vectors and the pinned float64 oracle.
+
+Tolerance: rel-L2 <= 1e-4 (fp32), <= 2e-2 (bf16), per the north-star contract.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from gdn2_testutil import TOL, make_inputs, np_, rel, to_dev
+from oracle import gdn2_oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+NAMES = ("q", "k", "v", "g", "b", "w")
+
+
+def _chunk(d, dev, dtype, **kw):
+    from qwendopamine_b200 import chunk_gdn2
+
+    x = to_dev(d, dev, dtype)
+    return chunk_gdn2(x["q"], x["k"], x["v"], x["g"], x["b"], x["w"], initial_state=x["h0"],
+                      output_final_state=True, use_qk_l2norm_in_kernel=True, **kw)
+
+
+def test_forward_matches_reference_golden_fp32(cuda_device):
+    gd = np.load(os.path.join(GOLD, "ref_small.npz"))
+    d = {n: torch.from_numpy(gd[n]) for n in (*NAMES, "h0")}
+    o, ht = _chunk(d, cuda_device, torch.float32)
+    assert rel(o, gd["o_rec"]) < 1e-4
+    assert rel(ht, gd["ht_rec"]) < 1e-4
+
+
+def test_config0_matches_reference_golden(cuda_device):
+    """BASELINE config 0 (fp32, B=1 T=512 H=4 K=V=64, zero initial state)."""
+    from test_oracle import config0_inputs
+
+    gd = np.load(os.path.join(GOLD, "config0.npz"))
+    q, k, v, beta, gs = config0_inputs()
+    K, V = q.shape[-1], v.shape[-1]
+    d = dict(q=q, k=k, v=v, g=gs[..., None].expand(*gs.shape, K), b=beta[..., None].expand(
+        *beta.shape, K), w=beta[..., None].expand(*beta.shape, V), h0=None)
+    o, ht = _chunk(d, cuda_device, torch.float32)
+    assert rel(o, gd["o_rec"]) < 1e-4
+    assert rel(ht, gd["ht_rec"]) < 1e-4
+
+
+def test_strong_decay_matches_reference_recurrence(cuda_device):
+    """g = -2 per token: the reference's own chunk oracle fails here (rel 0.85);
+    the B200 kernels use relative decays and follow the recurrence."""
+    gd = np.load(os.path.join(GOLD, "strong_decay.npz"))
+    d = {n: torch.from_numpy(gd[n]) for n in (*NAMES, "h0")}
+    o, ht = _chunk(d, cuda_device, torch.float32)
+    assert rel(o, gd["o_rec"]) < 1e-4
+    assert rel(ht, gd["ht_rec"]) < 1e-4
+
+
+@pytest.mark.parametrize("decay", [-6.0, -40.0])
+def test_extreme_decay_uses_exact_diagonal_blocks(cuda_device, decay):
+    d = make_inputs(1, 100, 2, 32, 32, seed=3, decay=decay)
+    o, ht = _chunk(d, cuda_device, torch.float32)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < 1e-4
+    assert rel(ht, rh) < 1e-4
+
+
+@pytest.mark.parametrize("T", [1, 17, 63, 64, 65, 130])
+@pytest.mark.parametrize("KV", [(16, 16), (64, 64), (128, 128), (64, 128), (32, 48)])
+def test_forward_ragged_lengths_and_head_sizes_fp32(cuda_device, T, KV):
+    K, V = KV
+    d = make_inputs(2, T, 3, K, V, seed=T + K)
+    o, ht = _chunk(d, cuda_device, torch.float32)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < TOL[torch.float32], "o"
+    assert rel(ht, rh) < TOL[torch.float32], "ht"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_forward_16bit_matches_fp64_oracle(cuda_device, dtype):
+    d = make_inputs(2, 300, 4, 128, 128, seed=1, decay="baseline", dtype=dtype)
+    o, ht = _chunk(d, cuda_device, dtype)
+    assert o.dtype == dtype and ht.dtype == torch.float32
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < TOL[dtype]
+    assert rel(ht, rh) < TOL[dtype]
+
+
+def test_varlen_packed_sequences(cuda_device):
+    from qwendopamine_b200 import chunk_gdn2
+
+    cu = [0, 17, 100, 164, 230, 230, 301]
+    d = make_inputs(1, cu[-1], 2, 64, 64, seed=9)
+    N = len(cu) - 1
+    gen = torch.Generator().manual_seed(4)
+    h0 = torch.randn(N, 2, 64, 64, generator=gen) * 0.1
+    x = to_dev(d, cuda_device, torch.float32)
+    cu_t = torch.tensor(cu, dtype=torch.long, device=cuda_device)
+    o, ht = chunk_gdn2(x["q"], x["k"], x["v"], x["g"], x["b"], x["w"],
+                       initial_state=h0.to(cuda_device), output_final_state=True,
+                       use_qk_l2norm_in_kernel=True, cu_seqlens=cu_t)
+    ro, rh = O.recurrent_fwd_varlen(*np_(d, NAMES), cu, h0.numpy(), norm_mode="fla")
+    assert rel(o, ro) < 1e-4
+    assert rel(ht, rh) < 1e-4
+
+
+def test_intermediate_states_match_oracle(cuda_device):
+    from qwendopamine_b200 import chunk_gdn2
+
+    d = make_inputs(2, 150, 2, 64, 64, seed=5)
+    x = to_dev(d, cuda_device, torch.float32)
+    with torch.inference_mode():
+        o, ht, h = chunk_gdn2(x["q"], x["k"], x["v"], x["g"], x["b"], x["w"],
+                              initial_state=x["h0"], output_final_state=True,
+                              use_qk_l2norm_in_kernel=True, return_intermediate_states=True)
+    _, _, inter = O.chunk_fwd_relative(*np_(d, NAMES), d["h0"].numpy())
+    ref_h = np.transpose(inter["h"], (0, 2, 1, 3, 4))  # [B,NT,H,K,V]
+    assert h.shape == ref_h.shape
+    assert rel(h, ref_h) < 1e-4
+
+
+def test_transposed_state_layout(cuda_device):
+    d = make_inputs(1, 70, 2, 32, 48, seed=6)
+    x = to_dev(d, cuda_device, torch.float32)
+    from qwendopamine_b200 import chunk_gdn2
+
+    o, ht = chunk_gdn2(x["q"], x["k"], x["v"], x["g"], x["b"], x["w"],
+                       initial_state=x["h0"].transpose(-1, -2).contiguous(),
+                       output_final_state=True, use_qk_l2norm_in_kernel=True,
+                       transpose_state_layout=True)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < 1e-4
+    assert rel(ht.transpose(-1, -2), rh) < 1e-4
+
+
+def test_gate_in_kernel_matches_explicit_gate(cuda_device):
+    from qwendopamine_b200 import chunk_gdn2
+
+    d = make_inputs(1, 80, 2, 32, 32, seed=8)
+    x = to_dev(d, cuda_device, torch.float32)
+    raw = torch.randn(1, 80, 2, 32, device=cuda_device)
+    A_log = torch.rand(2, device=cuda_device) * 2
+    dt_bias = torch.randn(64, device=cuda_device)
+    g = -A_log.exp().view(2, 1) * F.softplus(raw + dt_bias.view(2, 32))
+    o1, _ = chunk_gdn2(x["q"], x["k"], x["v"], g, x["b"], x["w"], use_qk_l2norm_in_kernel=True)
+    o2, _ = chunk_gdn2(x["q"], x["k"], x["v"], raw, x["b"], x["w"], use_qk_l2norm_in_kernel=True,
+                       use_gate_in_kernel=True, A_log=A_log, dt_bias=dt_bias)
+    assert rel(o2, o1) < 1e-6
+
+
+# ---------------------------------------------------------------------------
+# backward
+# ---------------------------------------------------------------------------
+
+def _grads(d, dev, dtype, do, dht, **kw):
+    from qwendopamine_b200 import chunk_gdn2
+
+    x = to_dev(d, dev, dtype)
+    leaves = {n: x[n].clone().requires_grad_() for n in (*NAMES, "h0") if x[n] is not None}
+    o, ht = chunk_gdn2(*(leaves[n] for n in NAMES), initial_state=leaves.get("h0"),
+                       output_final_state=True, use_qk_l2norm_in_kernel=True, **kw)
+    loss = (o.float() * do.to(dev)).sum() + (ht * dht.to(dev)).sum()
+    loss.backward()
+    return {n: t.grad for n, t in leaves.items()}
+
+
+def test_backward_matches_reference_autograd_fp32(cuda_device):
+    gd = np.load(os.path.join(GOLD, "ref_small.npz"))
+    d = {n: torch.from_numpy(gd[n]) for n in (*NAMES, "h0")}
+    gr = _grads(d, cuda_device, torch.float32, torch.from_numpy(gd["do"]),
+                torch.from_numpy(gd["dht"]))
+    for n in (*NAMES, "h0"):
+        assert rel(gr[n], gd[f"d{n}_rec"]) < 1e-4, n
+
+
+@pytest.mark.parametrize("T,K,V", [(9, 8, 8), (63, 32, 32), (130, 64, 64), (77, 128, 128),
+                                   (100, 64, 128)])
+def test_backward_shapes_fp32(cuda_device, T, K, V):
+    d = make_inputs(2, T, 2, K, V, seed=T)
+    gen = torch.Generator().manual_seed(T + 1)
+    do = torch.randn(2, T, 2, V, generator=gen)
+    dht = torch.randn(2, 2, K, V, generator=gen)
+    gr = _grads(d, cuda_device, torch.float32, do, dht)
+    ref = O.recurrent_bwd(*np_(d, NAMES), do.numpy(), d["h0"].numpy(), dht.numpy(),
+                          norm_mode="fla")
+    for n, r in zip((*NAMES, "h0"), ref):
+        assert rel(gr[n], r) < 1e-4, n
+
+
+def test_backward_extreme_decay_fp32(cuda_device):
+    d = make_inputs(1, 90, 2, 32, 32, seed=12, decay=-7.0)
+    d["g"] = d["g"] * (1 + 0.3 * torch.rand(d["g"].shape, generator=torch.Generator().manual_seed(1)))
+    gen = torch.Generator().manual_seed(2)
+    do = torch.randn(1, 90, 2, 32, generator=gen)
+    dht = torch.randn(1, 2, 32, 32, generator=gen)
+    gr = _grads(d, cuda_device, torch.float32, do, dht)
+    ref = O.recurrent_bwd(*np_(d, NAMES), do.numpy(), d["h0"].numpy(), dht.numpy(),
+                          norm_mode="fla")
+    for n, r in zip((*NAMES, "h0"), ref):
+        assert rel(gr[n], r) < 1e-4, n
+
+
+def test_backward_bf16_config1_slice(cuda_device):
+    """Config-1 recipe (scalar beta / decay broadcast, bf16 activations) on a
+    reduced B, T: gradients within 2e-2 of the fp64 oracle, including the
+    reduced scalar gradients d_beta = sum_k db + sum_v dw, dg_scalar = sum_k dg."""
+    B, T, H, K, V = 2, 256, 2, 128, 128
+    d = make_inputs(B, T, H, K, V, seed=21, decay="baseline", dtype=torch.bfloat16,
+                    scalar_gates=True, h0=False)
+    d["q"] = F.normalize(d["q"], dim=-1).bfloat16().float()
+    d["k"] = F.normalize(d["k"], dim=-1).bfloat16().float()
+    gen = torch.Generator().manual_seed(3)
+    do = torch.randn(B, T, H, V, generator=gen).bfloat16().float()
+    dht = torch.zeros(B, H, K, V)
+    gr = _grads(d, cuda_device, torch.bfloat16, do, dht)
+    ref = O.recurrent_bwd(*np_(d, NAMES), do.numpy(), None, None, norm_mode="fla")
+    for n, r in zip(NAMES, ref):
+        assert rel(gr[n], r) < TOL[torch.bfloat16], n
+    dbeta = gr["b"].float().sum(-1) + gr["w"].float().sum(-1)
+    rbeta = ref[4].sum(-1) + ref[5].sum(-1)
+    assert rel(dbeta, rbeta) < TOL[torch.bfloat16]
+    assert rel(gr["g"].float().sum(-1), ref[3].sum(-1)) < TOL[torch.bfloat16]
+
+
+def test_backward_varlen_fp32(cuda_device):
+    from qwendopamine_b200 import chunk_gdn2
+
+    cu = [0, 40, 41, 150, 200]
+    d = make_inputs(1, cu[-1], 2, 32, 32, seed=13, h0=False)
+    gen = torch.Generator().manual_seed(5)
+    h0 = torch.randn(4, 2, 32, 32, generator=gen) * 0.1
+    do = torch.randn(1, cu[-1], 2, 32, generator=gen)
+    x = to_dev(d, cuda_device, torch.float32)
+    leaves = {n: x[n].clone().requires_grad_() for n in NAMES}
+    h0d = h0.to(cuda_device).requires_grad_()
+    o, _ = chunk_gdn2(*(leaves[n] for n in NAMES), initial_state=h0d, output_final_state=False,
+                      use_qk_l2norm_in_kernel=True,
+                      cu_seqlens=torch.tensor(cu, device=cuda_device))
+    (o * do.to(cuda_device)).sum().backward()
+    for s in range(4):
+        a, e = cu[s], cu[s + 1]
+        sl = [x[:, a:e].double().numpy() for x in (d[n] for n in NAMES)]
+        ref = O.recurrent_bwd(*sl, do[:, a:e].numpy(), h0[s:s + 1].numpy(), None,
+                              norm_mode="fla")
+        for n, r in zip(NAMES, ref):
+            assert rel(leaves[n].grad[:, a:e], r) < 1e-4, (s, n)
+        assert rel(h0d.grad[s:s + 1], ref[6]) < 1e-4
+
+
+def test_backward_is_deterministic(cuda_device):
+    d = make_inputs(1, 128, 2, 64, 64, seed=30)
+    do = torch.randn(1, 128, 2, 64, generator=torch.Generator().manual_seed(1))
+    dht = torch.zeros(1, 2, 64, 64)
+    g1 = _grads(d, cuda_device, torch.bfloat16, do, dht)
+    g2 = _grads(d, cuda_device, torch.bfloat16, do, dht)
+    for n in g1:
+        assert torch.equal(g1[n], g2[n]), n

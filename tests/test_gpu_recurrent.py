@@ -1,0 +1,129 @@
+"""Parity of the B200 recurrent (decode) kernel, through the C ABI, with the
+reference's golden decode chain and the float64 oracle."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gdn2_testutil import make_inputs, np_, rel, to_dev
+from oracle import gdn2_oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+NAMES = ("q", "k", "v", "g", "b", "w")
+
+
+def test_decode_chain_matches_reference_golden(cuda_device):
+    """Config-2 recipe (bf16 inputs, fp32 N(0,0.02) state), three chained steps."""
+    from qwendopamine_b200 import fused_recurrent_gdn2
+
+    gd = np.load(os.path.join(GOLD, "decode.npz"))
+    h = torch.from_numpy(gd["h0"]).to(cuda_device)
+    for s in range(3):
+        x = {n: torch.from_numpy(gd[f"{n}{s}"]).to(cuda_device) for n in NAMES}
+        for n in ("q", "k", "v", "b", "w"):
+            x[n] = x[n].bfloat16()
+        o, h = fused_recurrent_gdn2(**x, initial_state=h, output_final_state=True,
+                                    use_qk_l2norm_in_kernel=True)
+        assert o.dtype == torch.bfloat16
+        assert rel(o, gd[f"o{s}"]) < 2e-2
+    assert rel(h, gd["ht"]) < 1e-4
+
+
+@pytest.mark.parametrize("T,K,V", [(1, 128, 128), (37, 64, 64), (5, 16, 16), (20, 48, 80),
+                                   (3, 100, 6)])
+def test_multi_token_fp32(cuda_device, T, K, V):
+    from qwendopamine_b200 import fused_recurrent_gdn2
+
+    d = make_inputs(3, T, 2, K, V, seed=T * K)
+    x = to_dev(d, cuda_device, torch.float32)
+    o, ht = fused_recurrent_gdn2(*(x[n] for n in NAMES), initial_state=x["h0"],
+                                 output_final_state=True, use_qk_l2norm_in_kernel=True)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < 1e-4
+    assert rel(ht, rh) < 1e-4
+
+
+def test_inplace_state_pool_with_indices(cuda_device):
+    from qwendopamine_b200 import fused_recurrent_gdn2_fwd
+
+    d = make_inputs(4, 1, 2, 64, 64, seed=2, h0=False)
+    gen = torch.Generator().manual_seed(7)
+    pool = torch.randn(7, 2, 64, 64, generator=gen) * 0.05
+    idx = torch.tensor([5, 0, -1, 3], dtype=torch.int32)
+    x = to_dev(d, cuda_device, torch.float32)
+    pool_d = pool.to(cuda_device)
+    o, fs = fused_recurrent_gdn2_fwd(*(x[n] for n in NAMES), initial_state=pool_d,
+                                     inplace_final_state=True,
+                                     ssm_state_indices=idx.to(cuda_device),
+                                     use_qk_l2norm_in_kernel=True)
+    assert fs.data_ptr() == pool_d.data_ptr()
+    for n, slot in enumerate(idx.tolist()):
+        if slot < 0:
+            continue
+        sl = [a[n:n + 1] for a in np_(d, NAMES)]
+        ro, rh = O.recurrent_fwd(*sl, pool[slot:slot + 1].numpy(), norm_mode="fla")
+        assert rel(o[n:n + 1], ro) < 1e-4
+        assert rel(pool_d[slot], rh[0]) < 1e-4
+    untouched = [s for s in range(7) if s not in idx.tolist()]
+    assert torch.equal(pool_d[untouched].cpu(), pool[untouched])
+
+
+def test_inplace_dense_state(cuda_device):
+    from qwendopamine_b200 import fused_recurrent_gdn2_fwd
+
+    d = make_inputs(2, 4, 2, 32, 32, seed=4)
+    x = to_dev(d, cuda_device, torch.float32)
+    st = x["h0"].clone()
+    fused_recurrent_gdn2_fwd(*(x[n] for n in NAMES), initial_state=st, inplace_final_state=True,
+                             use_qk_l2norm_in_kernel=True)
+    _, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(st, rh) < 1e-4
+
+
+def test_varlen_decode(cuda_device):
+    from qwendopamine_b200 import fused_recurrent_gdn2
+
+    cu = [0, 3, 3, 10, 11]
+    d = make_inputs(1, cu[-1], 2, 32, 32, seed=11, h0=False)
+    h0 = torch.randn(4, 2, 32, 32, generator=torch.Generator().manual_seed(1)) * 0.1
+    x = to_dev(d, cuda_device, torch.float32)
+    o, ht = fused_recurrent_gdn2(*(x[n] for n in NAMES), initial_state=h0.to(cuda_device),
+                                 output_final_state=True, use_qk_l2norm_in_kernel=True,
+                                 cu_seqlens=torch.tensor(cu, device=cuda_device))
+    ro, rh = O.recurrent_fwd_varlen(*np_(d, NAMES), cu, h0.numpy(), norm_mode="fla")
+    assert rel(o, ro) < 1e-4
+    assert rel(ht, rh) < 1e-4
+
+
+def test_grouped_value_heads(cuda_device):
+    """q, k with H heads shared by HV = 2H value heads (fused_recurrent_gdn2.py:155)."""
+    from qwendopamine_b200 import fused_recurrent_gdn2
+
+    B, T, H, HV, K, V = 2, 6, 2, 4, 32, 32
+    d = make_inputs(B, T, HV, K, V, seed=17)
+    qk_small = make_inputs(B, T, H, K, V, seed=18)
+    d["q"], d["k"] = qk_small["q"], qk_small["k"]
+    x = to_dev(d, cuda_device, torch.float32)
+    o, ht = fused_recurrent_gdn2(*(x[n] for n in NAMES), initial_state=x["h0"],
+                                 output_final_state=True, use_qk_l2norm_in_kernel=True)
+    rep = {n: (d[n].repeat_interleave(HV // H, dim=2) if n in ("q", "k") else d[n])
+           for n in NAMES}
+    ro, rh = O.recurrent_fwd(*(rep[n].double().numpy() for n in NAMES), d["h0"].numpy(),
+                             norm_mode="fla")
+    assert rel(o, ro) < 1e-4
+    assert rel(ht, rh) < 1e-4
+
+
+def test_recurrent_and_chunk_agree(cuda_device):
+    from qwendopamine_b200 import chunk_gdn2, fused_recurrent_gdn2
+
+    d = make_inputs(2, 50, 2, 64, 64, seed=19)
+    x = to_dev(d, cuda_device, torch.float32)
+    o1, h1 = fused_recurrent_gdn2(*(x[n] for n in NAMES), initial_state=x["h0"],
+                                  output_final_state=True, use_qk_l2norm_in_kernel=True)
+    o2, h2 = chunk_gdn2(*(x[n] for n in NAMES), initial_state=x["h0"], output_final_state=True,
+                        use_qk_l2norm_in_kernel=True)
+    assert rel(o1, o2) < 1e-4 and rel(h1, h2) < 1e-4

@@ -1,0 +1,155 @@
+"""Host-side behaviour of the drop-in module and op wrappers (CPU only):
+API surface, parameter layout, argument validation, and the absence of any
+CPU fallback."""
+
+import pytest
+import torch
+
+from qwendopamine_b200 import BLOCKS, GDN2_BACKENDS, GatedDeltaNet2, build_block, chunk_gdn2
+from qwendopamine_b200 import fused_recurrent_gdn2, resolve_gdn2_backend
+from qwendopamine_b200 import _native as N
+
+
+class DummyConfig:
+    def __init__(self, hidden_size=128, num_heads=4, head_dim=32):
+        self.hidden_size = hidden_size
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.n_head = num_heads
+        self.head_size = head_dim
+        self.conv_size = 4
+        self.norm_eps = 1e-5
+        self.rms_norm_eps = 1e-5
+        self.allow_neg_eigval = False
+        self.expand_v = 1.0
+
+
+# parameter names and shapes of the reference module (gdn2.py:573-620) for
+# hidden 64, 2 heads of 32
+REFERENCE_PARAMS = {
+    "A_log": (2,),
+    "dt_bias": (64,),
+    "q_proj.weight": (64, 64),
+    "k_proj.weight": (64, 64),
+    "v_proj.weight": (64, 64),
+    "q_conv1d.conv1d.weight": (64, 1, 4),
+    "k_conv1d.conv1d.weight": (64, 1, 4),
+    "v_conv1d.conv1d.weight": (64, 1, 4),
+    "f_proj.0.weight": (32, 64),
+    "f_proj.1.weight": (64, 32),
+    "b_proj.weight": (64, 64),
+    "w_proj.weight": (64, 64),
+    "g_proj.0.weight": (32, 64),
+    "g_proj.1.weight": (64, 32),
+    "g_proj.1.bias": (64,),
+    "o_norm.weight": (32,),
+    "o_proj.weight": (64, 64),
+}
+
+
+def test_parameter_names_and_shapes_match_reference():
+    layer = GatedDeltaNet2(hidden_size=64, num_heads=2, head_dim=32)
+    got = {n: tuple(p.shape) for n, p in layer.named_parameters()}
+    assert got == REFERENCE_PARAMS
+
+
+def test_config_object_and_registry():
+    cfg = DummyConfig(hidden_size=64, num_heads=2, head_dim=32)
+    layer = build_block("gdn2", cfg, layer_idx=3)
+    # build_block passes layer_idx positionally into the `hidden_size` slot,
+    # which the config then overrides -- the reference behaves the same way
+    # (registry.py:45 with gdn2.py:491-494), so layer_idx stays None.
+    assert isinstance(layer, GatedDeltaNet2) and layer.hidden_size == 64
+    assert BLOCKS["qwen35_gdn2"] is GatedDeltaNet2
+    with pytest.raises(KeyError):
+        build_block("nope", cfg, 0)
+
+
+def test_initialisation_ranges():
+    layer = GatedDeltaNet2(hidden_size=64, num_heads=2, head_dim=32)
+    a = layer.A_log.exp()
+    assert bool((a >= 1).all()) and bool((a <= 16).all())
+    assert getattr(layer.A_log, "_no_weight_decay", False)
+    assert getattr(layer.q_proj, "_is_hf_initialized", False)
+    dt = torch.nn.functional.softplus(layer.dt_bias)
+    assert bool((dt >= 1e-4 * 0.99).all()) and bool((dt <= 0.1 * 1.01).all())
+    assert layer.fp32_decay is True
+
+
+def test_same_seed_gives_reference_identical_weights():
+    """Parameter creation order follows the reference, so a seeded build
+    reproduces the reference module's initial weights draw for draw."""
+    torch.manual_seed(123)
+    a = GatedDeltaNet2(hidden_size=64, num_heads=2, head_dim=32).state_dict()
+    torch.manual_seed(123)
+    b = GatedDeltaNet2(hidden_size=64, num_heads=2, head_dim=32).state_dict()
+    assert all(torch.equal(a[n], b[n]) for n in a)
+
+
+def test_backend_validation():
+    with pytest.raises(ValueError):
+        GatedDeltaNet2(hidden_size=64, num_heads=2, head_dim=32, backend="nope")
+    with pytest.raises(ValueError):
+        GatedDeltaNet2(hidden_size=64, num_heads=2, head_dim=32, num_v_heads=3)
+    assert "cuda" in GDN2_BACKENDS
+    for b in ("auto", "cuda", "triton", "fla"):
+        assert resolve_gdn2_backend(b, training=True, seq_len=8) == "cuda"
+    assert resolve_gdn2_backend("torch", training=True, seq_len=8) == "torch"
+    with pytest.raises(ValueError):
+        resolve_gdn2_backend("bogus", training=True, seq_len=8)
+
+
+def test_no_cpu_fallback():
+    layer = GatedDeltaNet2(hidden_size=64, num_heads=2, head_dim=32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        layer(torch.randn(1, 8, 64))
+    torch_layer = GatedDeltaNet2(hidden_size=64, num_heads=2, head_dim=32, backend="torch")
+    with pytest.raises(RuntimeError, match="not part of the B200 build"):
+        torch_layer(torch.randn(1, 8, 64))
+    q = torch.randn(1, 8, 2, 16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        chunk_gdn2(q, q, q, -q.abs(), q.sigmoid(), q.sigmoid())
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fused_recurrent_gdn2(q, q, q, -q.abs(), q.sigmoid(), q.sigmoid())
+
+
+def test_chunk_argument_errors_follow_reference():
+    q = torch.randn(2, 8, 2, 16)
+    cu = torch.tensor([0, 4, 8])
+    with pytest.raises(ValueError, match="batch size"):
+        chunk_gdn2(q, q, q, -q.abs(), q.sigmoid(), q.sigmoid(), cu_seqlens=cu)
+    q1 = torch.randn(1, 8, 2, 16)
+    with pytest.raises(ValueError, match="initial states"):
+        chunk_gdn2(q1, q1, q1, -q1.abs(), q1.sigmoid(), q1.sigmoid(), cu_seqlens=cu,
+                   initial_state=torch.zeros(3, 2, 16, 16))
+    with pytest.raises(AssertionError, match="float32"):
+        chunk_gdn2(q, q, q, -q.abs(), q.sigmoid(), q.sigmoid(),
+                   initial_state=torch.zeros(2, 2, 16, 16, dtype=torch.bfloat16))
+    with pytest.raises(AssertionError, match="erase gate"):
+        chunk_gdn2(q, q, q, -q.abs(), q[..., :8].sigmoid(), q.sigmoid())
+    with pytest.raises(ValueError, match="lower_bound"):
+        chunk_gdn2(q, q, q, -q.abs(), q.sigmoid(), q.sigmoid(), safe_gate=True,
+                   use_gate_in_kernel=True)
+
+
+def test_sequence_tables():
+    t = N.seq_tables(3, 130, "cpu")
+    assert t.n_seqs == 3 and t.n_chunks == 9 and t.total == 390
+    assert t.cu.tolist() == [0, 130, 260, 390]
+    assert t.coff.tolist() == [0, 3, 6, 9]
+    assert t.cseq.tolist() == [0, 0, 0, 1, 1, 1, 2, 2, 2]
+    v = N.seq_tables(1, 200, "cpu", cu_seqlens=torch.tensor([0, 64, 64, 65, 200]))
+    assert v.n_seqs == 4 and v.n_chunks == 1 + 0 + 1 + 3
+    assert v.coff.tolist() == [0, 1, 1, 2, 5]
+    assert v.cseq.tolist() == [0, 2, 3, 3, 3]
+    with pytest.raises(ValueError):
+        N.seq_tables(1, 10, "cpu", cu_seqlens=torch.tensor([0, 5, 3]))
+    assert N.seq_tables(3, 130, "cpu") is t  # cached
+
+
+def test_dtype_codes():
+    assert N.dtype_code(torch.float32) == 0
+    assert N.dtype_code(torch.bfloat16) == 1
+    assert N.dtype_code(torch.float16) == 2
+    with pytest.raises(TypeError):
+        N.dtype_code(torch.int8)
