@@ -71,13 +71,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_bwd_state(BwdStateArgs a) {
   for (int c = c_end - 1; c >= c_begin; --c) {
     const size_t ch = (size_t)c * H + h;
     const ChunkPos cp = chunk_pos(a.seqs, c);
-    load_tile<T>(sQg, LD, reinterpret_cast<const T*>(a.saved + a.L.qg) + ch * tileK, K, kChunk, K, D);
-    load_tile<T>(sKd, LD, reinterpret_cast<const T*>(a.saved + a.L.kd) + ch * tileK, K, kChunk, K, D);
-    load_tile<T>(sW, LD, reinterpret_cast<const T*>(a.saved + a.L.w) + ch * tileK, K, kChunk, K, D);
-    load_tile<T>(sAqk, LDC, reinterpret_cast<const T*>(a.saved + a.L.aqk) + ch * kChunk * kChunk,
-                 kChunk, kChunk, kChunk, kChunk);
+    load_tile<T, kChunk, D>(sQg, LD, reinterpret_cast<const T*>(a.saved + a.L.qg) + ch * tileK, K,
+                            kChunk, K);
+    load_tile<T, kChunk, D>(sKd, LD, reinterpret_cast<const T*>(a.saved + a.L.kd) + ch * tileK, K,
+                            kChunk, K);
+    load_tile<T, kChunk, D>(sW, LD, reinterpret_cast<const T*>(a.saved + a.L.w) + ch * tileK, K,
+                            kChunk, K);
+    load_tile<T, kChunk, kChunk>(sAqk, LDC,
+                                 reinterpret_cast<const T*>(a.saved + a.L.aqk) + ch * kChunk * kChunk,
+                                 kChunk, kChunk, kChunk);
     const T* gdo = reinterpret_cast<const T*>(a.dout) + cp.row0 * ldo + (int64_t)h * V + v0;
-    load_tile<T>(sDO, LDB, gdo, ldo, cp.len, min(kBV, V - v0), kBV);
+    load_tile<T, kChunk, kBV>(sDO, LDB, gdo, ldo, cp.len, min(kBV, V - v0));
     const float* gGl = reinterpret_cast<const float*>(a.saved + a.L.gl) + ch * K;
     for (int idx = tid; idx < D; idx += blockDim.x) sGl[idx] = idx < K ? gGl[idx] : 0.f;
     if (!a.prescan) {
@@ -159,12 +163,13 @@ struct BIntraSmem {
   static constexpr int LDC = kChunk + 4;
   static constexpr int LDB = kBV + 4;
   static constexpr int phaseV = 2 * D * LDB + 6 * kChunk * LDB;
-  static constexpr int colblk = 5 * kChunk * LDB + 32 * LDB;
+  static constexpr int colblk = 7 * kChunk * LDB + 32 * LDB;
   static constexpr int phaseK = 2 * kChunk * LDC + 3 * kChunk * LD + colblk;
   static constexpr int region = phaseV > phaseK ? phaseV : phaseK;
-  static constexpr int misc = D + 2 * kChunk + 64;
+  static constexpr int misc = D + 4 * kChunk + 64;
   static constexpr int floats = kChunk * LDC + misc + region;
   static constexpr size_t bytes = (size_t)floats * sizeof(float);
+  static_assert(2 * kChunk * LD <= region, "q/k staging must fit the work region");
 };
 
 template <typename T, int D>
@@ -175,10 +180,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_bwd_intra(BwdIntraArgs a) {
   constexpr int NT = D / 16;
   extern __shared__ __align__(16) float sm[];
   float* sA = sm;                        // [64][LDC]
-  float* sDGL = sA + kChunk * LDC;       // [D]
-  float* sRq = sDGL + D;                 // [64] rsqrt norms
-  float* sRk = sRq + kChunk;             // [64]
-  float* sGLc = sRk + kChunk;            // [32] dG_last of the current key block
+  float* sDGL = sA + kChunk * LDC;       // [D] d(gl)
+  float* sRq = sDGL + D;                 // [64] rsqrt norms of q rows
+  float* sRk = sRq + kChunk;             // [64] ... of k rows
+  float* sDiag = sRk + kChunk;           // [64] diagonal of dAqk
+  float* sGLc = sDiag + kChunk;          // [32] d(G_last) of the current key block
   int* sFlag = reinterpret_cast<int*>(sGLc + 32);
   float* R = sm + kChunk * LDC + S::misc;
   // phase V
@@ -194,15 +200,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_bwd_intra(BwdIntraArgs a) {
   float* sDAqk = R;
   float* sDAkk = sDAqk + kChunk * LDC;
   float* sDQ = sDAkk + kChunk * LDC;     // [64][LD] dq (pre-norm)
-  float* sDKn = sDQ + kChunk * LD;       // [64][LD] dKd -> dk_dir -> dk (pre-norm)
-  float* sDKB = sDKn + kChunk * LD;      // [64][LD] dW -> dkb
-  float* sCq = sDKB + kChunk * LD;       // [64][LDB] column block buffers
+  float* sDKn = sDQ + kChunk * LD;       // [64][LD] dKd -> Kd part of dk -> dk (pre-norm)
+  float* sDKB = sDKn + kChunk * LD;      // [64][LD] dW -> d(b*k)
+  float* sCq = sDKB + kChunk * LD;       // [64][LDB] key-block buffers
   float* sCk = sCq + kChunk * LDB;
   float* sCb = sCk + kChunk * LDB;
   float* sCg = sCb + kChunk * LDB;
-  float* sCx = sCg + kChunk * LDB;
-  float* sCl = sCx + kChunk * LDB;       // [32][LDB]
-  float* sT = sCq;                       // [64][LDC] temp, aliases the column buffers
+  float* sCx = sCg + kChunk * LDB;       // scaled keys, then dG
+  float* sCy = sCx + kChunk * LDB;       // Kd part of dG, shifted one row down
+  float* sCd = sCy + kChunk * LDB;       // score i-side gradient of k
+  float* sCl = sCd + kChunk * LDB;       // [32][LDB]
+  float* sT = sCq;                       // [64][LDC] temp, aliases the key-block buffers
 
   const int c = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -218,27 +226,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_bwd_intra(BwdIntraArgs a) {
   const T* gb = reinterpret_cast<const T*>(a.b) + offk;
   const float* gg = a.g + offk;
 
-  // ---- phase 0: row norms, A --------------------------------------------
-  for (int r = warp; r < kChunk; r += kThreads / 32) {
-    float sq = 0.f, sk = 0.f;
-    if (r < len) {
-      for (int cc = lane; cc < K; cc += 32) {
-        float x = to_f<T>(gq[r * ldk + cc]), y = to_f<T>(gk[r * ldk + cc]);
+  // ---- phase 0: row norms of q and k (from staged tiles), A ----------------
+  {
+    float* tq = R;
+    float* tk = R + kChunk * LD;
+    load_tile<T, kChunk, D>(tq, LD, gq, ldk, len, K);
+    load_tile<T, kChunk, D>(tk, LD, gk, ldk, len, K);
+    load_tile<T, kChunk, kChunk>(sA, LDC,
+                                 reinterpret_cast<const T*>(a.saved + a.L.a) + ch * kChunk * kChunk,
+                                 kChunk, kChunk, kChunk);
+    for (int idx = tid; idx < D; idx += blockDim.x) sDGL[idx] = 0.f;
+    __syncthreads();
+    for (int r = warp; r < kChunk; r += kThreads / 32) {
+      float sq = 0.f, sk = 0.f;
+#pragma unroll
+      for (int cc = lane; cc < D; cc += 32) {
+        float x = tq[r * LD + cc], y = tk[r * LD + cc];
         sq += x * x;
         sk += y * y;
       }
+      sq = warp_sum(sq);
+      sk = warp_sum(sk);
+      if (lane == 0) {
+        sRq[r] = a.l2norm ? rsqrtf(sq + kNormEps) : 1.f;
+        sRk[r] = a.l2norm ? rsqrtf(sk + kNormEps) : 1.f;
+      }
     }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    if (lane == 0) {
-      sRq[r] = a.l2norm ? rsqrtf(sq + kNormEps) : 1.f;
-      sRk[r] = a.l2norm ? rsqrtf(sk + kNormEps) : 1.f;
-    }
+    __syncthreads();
   }
-  load_tile<T>(sA, LDC, reinterpret_cast<const T*>(a.saved + a.L.a) + ch * kChunk * kChunk, kChunk,
-               kChunk, kChunk, kChunk);
-  for (int idx = tid; idx < D; idx += blockDim.x) sDGL[idx] = 0.f;
-  __syncthreads();
 
   // ---- phase V ------------------------------------------------------------
   const int wr = warp & 3, wc = warp >> 2, m0 = wr * 16;
@@ -260,13 +275,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_bwd_intra(BwdIntraArgs a) {
   T* gdw = reinterpret_cast<T*>(a.dw) + offv;
   for (int v0 = 0; v0 < V; v0 += kBV) {
     const int nv = min(kBV, V - v0);
-    load_tile<T>(sHs, LDB, gh + v0, V, K, nv, kBV, D);
-    load_tile<T>(sDHs, LDB, gdh + v0, V, K, nv, kBV, D);
-    load_tile<T>(sDOs, LDB, gdo + v0, ldv, len, nv, kBV);
-    load_tile<T>(sVNs, LDB, gvn + v0, V, kChunk, nv, kBV);
-    load_tile<T>(sDVNs, LDB, gdvn + v0, V, kChunk, nv, kBV);
-    load_tile<T>(sVs, LDB, gv + v0, ldv, len, nv, kBV);
-    load_tile<T>(sWs, LDB, gw + v0, ldv, len, nv, kBV);
+    load_tile<T, D, kBV>(sHs, LDB, gh + v0, V, K, nv);
+    load_tile<T, D, kBV>(sDHs, LDB, gdh + v0, V, K, nv);
+    load_tile<T, kChunk, kBV>(sDOs, LDB, gdo + v0, ldv, len, nv);
+    load_tile<T, kChunk, kBV>(sVNs, LDB, gvn + v0, V, kChunk, nv);
+    load_tile<T, kChunk, kBV>(sDVNs, LDB, gdvn + v0, V, kChunk, nv);
+    load_tile<T, kChunk, kBV>(sVs, LDB, gv + v0, ldv, len, nv);
+    load_tile<T, kChunk, kBV>(sWs, LDB, gw + v0, ldv, len, nv);
     __syncthreads();
     for (int idx = tid; idx < kChunk * kBV; idx += blockDim.x) {
       int r = idx / kBV, cc = idx - r * kBV;
@@ -300,42 +315,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_bwd_intra(BwdIntraArgs a) {
   }
 
   // ---- dump value-side results into the key-side buffers -------------------
+  // The diagonal of dAqk (a token's score with itself) is kept apart: its
+  // contributions to dG through q and through k cancel exactly, so it is
+  // added to dq and dk only after dG is formed (no rounding residue in dg).
   acc_foreach(accQ, [&](int rr, int cc, float val) { sDQ[(m0 + rr) * LD + n0k + cc] = val; });
   acc_foreach(accKd, [&](int rr, int cc, float val) { sDKn[(m0 + rr) * LD + n0k + cc] = val; });
   acc_foreach(accW, [&](int rr, int cc, float val) { sDKB[(m0 + rr) * LD + n0k + cc] = -val; });
   acc_foreach(accAqk, [&](int rr, int cc, float val) {
     int r = m0 + rr, i = 32 * wc + cc;
-    sDAqk[r * LDC + i] = (i <= r) ? val : 0.f;
+    sDAqk[r * LDC + i] = (i < r) ? val : 0.f;
+    if (i == r) sDiag[r] = val;
   });
   __syncthreads();
 
   // ---- key blocks, pass 1: dA += dW E^T ------------------------------------
   auto load_cols = [&](int c0, bool need_q) {
     const int nk = min(32, K - c0);
+    if (need_q) load_tile<T, kChunk, 32>(sCq, LDB, gq + c0, ldk, len, nk);
+    load_tile<T, kChunk, 32>(sCk, LDB, gk + c0, ldk, len, nk);
+    load_tile<T, kChunk, 32>(sCb, LDB, gb + c0, ldk, len, nk);
+    load_tile<float, kChunk, 32>(sCg, LDB, gg + c0, ldk, len, nk);
+    __syncthreads();
     for (int idx = tid; idx < kChunk * 32; idx += blockDim.x) {
       int r = idx >> 5, cc = idx & 31;
-      float xq = 0.f, xk = 0.f, xb = 0.f, xg = 0.f;
-      if (r < len && cc < nk) {
-        int64_t o = (int64_t)r * ldk + c0 + cc;
-        if (need_q) xq = to_f<T>(gq[o]) * sRq[r];
-        xk = to_f<T>(gk[o]) * sRk[r];
-        xb = to_f<T>(gb[o]);
-        xg = gg[o];
-      }
-      sCq[r * LDB + cc] = xq;
-      sCk[r * LDB + cc] = xk;
-      sCb[r * LDB + cc] = xb;
-      sCg[r * LDB + cc] = xg;
+      sCk[r * LDB + cc] *= sRk[r];
+      if (need_q) sCq[r * LDB + cc] *= sRq[r];
     }
-    __syncthreads();
-    if (tid < 32) {
-      float run = 0.f;
-      for (int r = 0; r < kChunk; ++r) {
-        run += sCg[r * LDB + tid];
-        sCg[r * LDB + tid] = run * kLog2e;
-      }
-    }
-    __syncthreads();
+    col_cumsum64<32>(sCg, LDB, kLog2e, sCl);
   };
   for (int c0 = 0; c0 < K; c0 += 32) {
     load_cols(c0, false);
@@ -393,23 +399,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_bwd_intra(BwdIntraArgs a) {
       int r = m0 + rr, col = 16 * wc + cc;
       sDKB[r * LD + c0 + col] = val * exp2f(sCg[r * LDB + col]);
     });
+    // dq <- scale 2^G dQg;  Kd part of dk <- dKd 2^(G_L - G);  its dG share
+    // X_r = k_r * (Kd part)_r goes to sCy shifted one row down, so that a
+    // prefix scan yields sum_{r<t} X_r without subtracting anything.
     for (int idx = tid; idx < kChunk * 32; idx += blockDim.x) {
       int r = idx >> 5, cc = idx & 31;
       float G = sCg[r * LDB + cc], GL = sCg[(kChunk - 1) * LDB + cc];
       sDQ[r * LD + c0 + cc] *= scale * exp2f(G);
-      sDKn[r * LD + c0 + cc] *= exp2f(GL - G);
+      float kd = sDKn[r * LD + c0 + cc] * exp2f(GL - G);
+      sDKn[r * LD + c0 + cc] = kd;
+      if (r + 1 < kChunk) sCy[(r + 1) * LDB + cc] = sCk[r * LDB + cc] * kd;
+      if (r == 0) sCy[cc] = 0.f;
+      sCd[r * LDB + cc] = 0.f;
     }
-    __syncthreads();
     if (tid < 32) {
-      float s = 0.f;
-      for (int r = 0; r < kChunk; ++r) s += sCk[r * LDB + tid] * sDKn[r * LD + c0 + tid];
       float gl = (tid < nk) ? gGl[c0 + tid] : 0.f;
-      sGLc[tid] = s + sDGL[c0 + tid] * gl;
+      sGLc[tid] = sDGL[c0 + tid] * gl;
     }
     // score blocks
     for (int bI = 0; bI < 4; ++bI) {
       const int r0 = 16 * bI, ni = 16 * (bI + 1);
       const int jmax = safe ? ni : 16 * bI;
+      __syncthreads();
       for (int idx = tid; idx < 16 * 32; idx += blockDim.x) {
         int rr = idx >> 5, cc = idx & 31, r = r0 + rr;
         float f = exp2f(sCg[r * LDB + cc] - sCg[r0 * LDB + cc]);
@@ -451,77 +462,92 @@ __global__ void __launch_bounds__(kThreads, 1) k_bwd_intra(BwdIntraArgs a) {
           acc_foreach(acc, [&](int rr, int cc, float val) {
             int i = 16 * mt + rr, col = 8 * nt + cc;
             float e = fminf(sCg[r0 * LDB + col] - sCg[i * LDB + col], 120.f);
-            sDKn[i * LD + c0 + col] += val * exp2f(e);
+            sCd[i * LDB + col] += val * exp2f(e);
           });
         }
       }
-      __syncthreads();
       if (!safe) {
-        // exact diagonal block
+        __syncthreads();
+        // exact diagonal block (off-diagonal pairs only; the diagonal itself
+        // is handled apart, see above)
         for (int idx = tid; idx < 16 * 32; idx += blockDim.x) {
           int rr = idx >> 5, cc = idx & 31, r = r0 + rr;
           float sq = 0.f, sk = 0.f, sy = 0.f;
-          for (int ii = 0; ii <= rr; ++ii) {
+          for (int ii = 0; ii < rr; ++ii) {
             int i = r0 + ii;
             float e = exp2f(sCg[r * LDB + cc] - sCg[i * LDB + cc]) * sCk[i * LDB + cc];
             sq += sDAqk[r * LDC + i] * e;
-            if (ii < rr) sk += sDAkk[r * LDC + i] * e;
+            sk += sDAkk[r * LDC + i] * e;
           }
-          // i-side: this thread's row plays i = r
-          for (int r2 = rr; r2 < 16; ++r2) {
+          for (int r2 = rr + 1; r2 < 16; ++r2) {
             int rb = r0 + r2;
             float e = exp2f(sCg[rb * LDB + cc] - sCg[r * LDB + cc]);
-            float t = scale * sDAqk[rb * LDC + r] * sCq[rb * LDB + cc];
-            if (r2 > rr) t += sDAkk[rb * LDC + r] * sCb[rb * LDB + cc] * sCk[rb * LDB + cc];
+            float t = scale * sDAqk[rb * LDC + r] * sCq[rb * LDB + cc] +
+                      sDAkk[rb * LDC + r] * sCb[rb * LDB + cc] * sCk[rb * LDB + cc];
             sy += t * e;
           }
           sDQ[r * LD + c0 + cc] += scale * sq;
           sDKB[r * LD + c0 + cc] += sk;
-          sDKn[r * LD + c0 + cc] += sy;
+          sCd[r * LDB + cc] += sy;
         }
-        __syncthreads();
       }
     }
-    // per-element chain: dG, db, dk_total
+    __syncthreads();
+    // per-element chain: dG (without the Kd part and the diagonal), db, dk
     for (int idx = tid; idx < kChunk * 32; idx += blockDim.x) {
       int r = idx >> 5, cc = idx & 31;
       float qn = sCq[r * LDB + cc], kn = sCk[r * LDB + cc], bb = sCb[r * LDB + cc];
-      float dqn = sDQ[r * LD + c0 + cc], dkb = sDKB[r * LD + c0 + cc], dkd = sDKn[r * LD + c0 + cc];
-      sCx[r * LDB + cc] = qn * dqn + bb * kn * dkb - kn * dkd;
-      sDKn[r * LD + c0 + cc] = dkd + dkb * bb;
+      float dqn = sDQ[r * LD + c0 + cc], dkb = sDKB[r * LD + c0 + cc], dy = sCd[r * LDB + cc];
+      float dG = qn * dqn + bb * kn * dkb - kn * dy;
+      if (r == len - 1) dG += sGLc[cc];
+      sCx[r * LDB + cc] = dG;
+      const float dgn = scale * sDiag[r];
+      sDQ[r * LD + c0 + cc] = dqn + dgn * kn;
+      sDKn[r * LD + c0 + cc] += dy + dkb * bb + dgn * qn;
       if (r < len && cc < nk) gdb[(int64_t)r * ldk + c0 + cc] = from_f<T>(dkb * kn);
     }
     __syncthreads();
-    if (tid < nk) {
-      float run = sGLc[tid];
-      for (int r = len - 1; r >= 0; --r) {
-        run += sCx[r * LDB + tid];
-        gdg[(int64_t)r * ldk + c0 + tid] = run;
-      }
+    // dg_t = sum_{r>=t} dG_r + sum_{r<t} X_r
+    col_scan64<32, true>(sCx, LDB, sCl);
+    col_scan64<32, false>(sCy, LDB, sCl);
+    for (int idx = tid; idx < kChunk * 32; idx += blockDim.x) {
+      int r = idx >> 5, cc = idx & 31;
+      if (r < len && cc < nk)
+        gdg[(int64_t)r * ldk + c0 + cc] = sCx[r * LDB + cc] + sCy[r * LDB + cc];
     }
     __syncthreads();
   }
 
   // ---- l2norm backward and dq / dk out -------------------------------------
-  for (int r = warp; r < len; r += kThreads / 32) {
-    const float rq = sRq[r], rk = sRk[r];
-    float pq = 0.f, pk = 0.f;
-    if (a.l2norm) {
-      for (int cc = lane; cc < K; cc += 32) {
-        pq += to_f<T>(gq[r * ldk + cc]) * rq * sDQ[r * LD + cc];
-        pk += to_f<T>(gk[r * ldk + cc]) * rk * sDKn[r * LD + cc];
-      }
-      pq = warp_sum(pq);
-      pk = warp_sum(pk);
-    }
-    for (int cc = lane; cc < K; cc += 32) {
-      float dqv = sDQ[r * LD + cc], dkv = sDKn[r * LD + cc];
+  {
+    // stage the raw q, k rows in the key-block area (free now; it does not
+    // overlap sDQ / sDKn)
+    static_assert(2 * kChunk * LD <= S::colblk, "q/k staging must fit the key-block area");
+    float* tq = sCq;
+    float* tk = sCq + kChunk * LD;
+    load_tile<T, kChunk, D>(tq, LD, gq, ldk, len, K);
+    load_tile<T, kChunk, D>(tk, LD, gk, ldk, len, K);
+    __syncthreads();
+    for (int r = warp; r < len; r += kThreads / 32) {
+      const float rq = sRq[r], rk = sRk[r];
+      float pq = 0.f, pk = 0.f;
       if (a.l2norm) {
-        dqv = (dqv - to_f<T>(gq[r * ldk + cc]) * rq * pq) * rq;
-        dkv = (dkv - to_f<T>(gk[r * ldk + cc]) * rk * pk) * rk;
+        for (int cc = lane; cc < K; cc += 32) {
+          pq += tq[r * LD + cc] * rq * sDQ[r * LD + cc];
+          pk += tk[r * LD + cc] * rk * sDKn[r * LD + cc];
+        }
+        pq = warp_sum(pq);
+        pk = warp_sum(pk);
       }
-      gdq[r * ldk + cc] = from_f<T>(dqv);
-      gdk[r * ldk + cc] = from_f<T>(dkv);
+      for (int cc = lane; cc < K; cc += 32) {
+        float dqv = sDQ[r * LD + cc], dkv = sDKn[r * LD + cc];
+        if (a.l2norm) {
+          dqv = (dqv - tq[r * LD + cc] * rq * pq) * rq;
+          dkv = (dkv - tk[r * LD + cc] * rk * pk) * rk;
+        }
+        gdq[r * ldk + cc] = from_f<T>(dqv);
+        gdk[r * ldk + cc] = from_f<T>(dkv);
+      }
     }
   }
 }

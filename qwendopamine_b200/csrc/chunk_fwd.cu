@@ -102,10 +102,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_intra(FwdIntraArgs a) {
   const int64_t offv = cp.row0 * ldv + (int64_t)h * V;
 
   // ---- loads ---------------------------------------------------------------
-  load_tile<float>(sG, LD, a.g + offk, ldk, len, K, D);
-  load_tile<T>(sQ, LD, reinterpret_cast<const T*>(a.q) + offk, ldk, len, K, D);
-  load_tile<T>(sK, LD, reinterpret_cast<const T*>(a.k) + offk, ldk, len, K, D);
-  load_tile<T>(sKB, LD, reinterpret_cast<const T*>(a.b) + offk, ldk, len, K, D);
+  load_tile<float, kChunk, D>(sG, LD, a.g + offk, ldk, len, K);
+  load_tile<T, kChunk, D>(sQ, LD, reinterpret_cast<const T*>(a.q) + offk, ldk, len, K);
+  load_tile<T, kChunk, D>(sK, LD, reinterpret_cast<const T*>(a.k) + offk, ldk, len, K);
+  load_tile<T, kChunk, D>(sKB, LD, reinterpret_cast<const T*>(a.b) + offk, ldk, len, K);
   for (int idx = tid; idx < kChunk * LDC; idx += blockDim.x) {
     sAqk[idx] = 0.f;
     sAkk[idx] = 0.f;
@@ -113,14 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_intra(FwdIntraArgs a) {
   if (tid == 0) sFlag[0] = 1;
   __syncthreads();
 
-  // chunk-local cumulative decay (log2 domain), one column per thread
-  if (tid < D) {
-    float run = 0.f;
-    for (int r = 0; r < kChunk; ++r) {
-      run += sG[r * LD + tid];
-      sG[r * LD + tid] = run * kLog2e;
-    }
-  }
+  // chunk-local cumulative decay (log2 domain)
+  col_cumsum64<D>(sG, LD, kLog2e, sX);
   // L2 normalisation of q and k rows: x * rsqrt(sum x^2 + eps)
   if (a.l2norm) {
     for (int r = warp; r < kChunk; r += kThreads / 32) {
@@ -236,8 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_intra(FwdIntraArgs a) {
     int r = idx / D, cc = idx - r * D;
     sKB[r * LD + cc] *= exp2f(sG[r * LD + cc]);
   }
-  load_tile<T>(sQ, LD, reinterpret_cast<const T*>(a.v) + offv, ldv, len, V, D);
-  load_tile<T>(sK, LD, reinterpret_cast<const T*>(a.w) + offv, ldv, len, V, D);
+  load_tile<T, kChunk, D>(sQ, LD, reinterpret_cast<const T*>(a.v) + offv, ldv, len, V);
+  load_tile<T, kChunk, D>(sK, LD, reinterpret_cast<const T*>(a.w) + offv, ldv, len, V);
   __syncthreads();
   for (int idx = tid; idx < kChunk * D; idx += blockDim.x) {
     int r = idx / D, cc = idx - r * D;
@@ -324,15 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_fwd_state(FwdStateArgs a) {
     const T* gU = reinterpret_cast<const T*>(a.saved + a.L.u) + ch * tileV;
     const T* gAqk = reinterpret_cast<const T*>(a.saved + a.L.aqk) + ch * kChunk * kChunk;
     const float* gGl = reinterpret_cast<const float*>(a.saved + a.L.gl) + ch * K;
-    if (!a.prescan) load_tile<T>(sQg, LD, gQg, K, kChunk, K, D);
-    load_tile<T>(sKd, LD, gKd, K, kChunk, K, D);
-    load_tile<T>(sW, LD, gW, K, kChunk, K, D);
-    if (!a.prescan) load_tile<T>(sAqk, LDC, gAqk, kChunk, kChunk, kChunk, kChunk);
+    if (!a.prescan) load_tile<T, kChunk, D>(sQg, LD, gQg, K, kChunk, K);
+    load_tile<T, kChunk, D>(sKd, LD, gKd, K, kChunk, K);
+    load_tile<T, kChunk, D>(sW, LD, gW, K, kChunk, K);
+    if (!a.prescan) load_tile<T, kChunk, kChunk>(sAqk, LDC, gAqk, kChunk, kChunk, kChunk);
     // U tile (columns beyond V are the M part of the pre-scan: zero)
-    for (int idx = tid; idx < kChunk * kBV; idx += blockDim.x) {
-      int r = idx / kBV, cc = idx - r * kBV, col = v0 + cc;
-      sU[r * LDB + cc] = (col < V) ? to_f<T>(gU[(size_t)r * V + col]) : 0.f;
-    }
+    load_tile<T, kChunk, kBV>(sU, LDB, gU + v0, V, kChunk, max(0, min(kBV, V - v0)));
     for (int idx = tid; idx < D; idx += blockDim.x) sGl[idx] = idx < K ? gGl[idx] : 0.f;
     if (!a.prescan) {
       // checkpoint of the state entering this chunk (for the backward)

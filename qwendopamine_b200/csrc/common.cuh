@@ -133,26 +133,115 @@ __device__ __forceinline__ void acc_foreach(float (&acc)[MT][NT][4], F&& f) {
 // ---------------------------------------------------------------------------
 // tile movement between global token tensors and shared memory
 // ---------------------------------------------------------------------------
-// Load rows [0,64) x cols [0,DP) of a [rows, ld] global view into a float
-// shared tile with row stride lds.  Rows >= nrows and cols >= ncols are zero.
-template <typename T>
-__device__ __forceinline__ void load_tile(float* s, int lds, const T* g, int64_t ldg, int nrows,
-                                          int ncols, int DP, int rows = kChunk) {
-  for (int idx = threadIdx.x; idx < rows * DP; idx += blockDim.x) {
-    int r = idx / DP, c = idx - r * DP;
-    float v = 0.f;
-    if (r < nrows && c < ncols) v = to_f<T>(g[(int64_t)r * ldg + c]);
-    s[r * lds + c] = v;
+// Load a ROWS x COLS tile of a [rows, ldg] global view into a float shared
+// tile (row stride lds, a multiple of 4).  Rows >= nrows and cols >= ncols
+// are zero-filled.  Every thread first issues all of its 16-byte loads
+// (ITERS of them, unrolled) and only then converts and stores, so a tile
+// costs one memory round trip instead of one per element.  Falls back to
+// element loads (still batched) when the view is not 16-byte aligned.
+template <typename T, int ROWS, int COLS>
+__device__ __forceinline__ void load_tile(float* __restrict__ s, int lds, const T* __restrict__ g,
+                                          int64_t ldg, int nrows, int ncols) {
+  constexpr int VEC = 16 / sizeof(T);
+  static_assert(COLS % VEC == 0, "tile width must be a multiple of 16 bytes");
+  constexpr int CPR = COLS / VEC;
+  constexpr int TOTAL = ROWS * CPR;
+  constexpr int ITERS = (TOTAL + kThreads - 1) / kThreads;
+  const bool vec = ((ncols % VEC) == 0) && ((ldg % VEC) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(g) & 15) == 0);
+  uint4 buf[ITERS];
+  if (vec) {
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const int idx = threadIdx.x + it * kThreads;
+      const int r = idx / CPR, c = (idx - r * CPR) * VEC;
+      buf[it] = make_uint4(0u, 0u, 0u, 0u);
+      if (idx < TOTAL && r < nrows && c < ncols)
+        buf[it] = __ldg(reinterpret_cast<const uint4*>(g + (int64_t)r * ldg + c));
+    }
+  } else {
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+      const int idx = threadIdx.x + it * kThreads;
+      const int r = idx / CPR, c = (idx - r * CPR) * VEC;
+      T tmp[VEC];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        tmp[e] = from_f<T>(0.f);
+        if (idx < TOTAL && r < nrows && c + e < ncols) tmp[e] = g[(int64_t)r * ldg + c + e];
+      }
+      buf[it] = *reinterpret_cast<uint4*>(tmp);
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < ITERS; ++it) {
+    const int idx = threadIdx.x + it * kThreads;
+    if (idx < TOTAL) {
+      const int r = idx / CPR, c = (idx - r * CPR) * VEC;
+      const T* e = reinterpret_cast<const T*>(&buf[it]);
+      float* d = s + r * lds + c;
+#pragma unroll
+      for (int j = 0; j < VEC; j += 4)
+        *reinterpret_cast<float4*>(d + j) =
+            make_float4(to_f<T>(e[j]), to_f<T>(e[j + 1]), to_f<T>(e[j + 2]), to_f<T>(e[j + 3]));
+    }
   }
 }
 
-template <typename T>
-__device__ __forceinline__ void store_tile(T* g, int64_t ldg, const float* s, int lds, int nrows,
-                                           int ncols) {
-  for (int idx = threadIdx.x; idx < nrows * ncols; idx += blockDim.x) {
-    int r = idx / ncols, c = idx - r * ncols;
-    g[(int64_t)r * ldg + c] = from_f<T>(s[r * lds + c]);
+// In-place inclusive scan down the rows of a 64 x NC float tile (row stride
+// lds): prefix sums when REV is false, suffix sums when REV is true.  Same
+// segmented scheme as col_cumsum64; `tmp` needs 256 floats.
+template <int NC, bool REV>
+__device__ __forceinline__ void col_scan64(float* s, int lds, float* tmp) {
+  constexpr int NSEG = kThreads / NC;
+  constexpr int RPS = kChunk / NSEG;
+  const int col = threadIdx.x % NC, seg = threadIdx.x / NC;
+  float run = 0.f;
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) {
+    const int r = REV ? (kChunk - 1 - (seg * RPS + i)) : (seg * RPS + i);
+    float* p = s + r * lds + col;
+    run += *p;
+    *p = run;
   }
+  tmp[seg * NC + col] = run;
+  __syncthreads();
+  float off = 0.f;
+  for (int j = 0; j < seg; ++j) off += tmp[j * NC + col];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) {
+    const int r = REV ? (kChunk - 1 - (seg * RPS + i)) : (seg * RPS + i);
+    s[r * lds + col] += off;
+  }
+  __syncthreads();
+}
+
+// In-place inclusive prefix sum down the rows of a 64 x NC float tile
+// (row stride lds), times `mul`.  The 256 threads split into NC columns x
+// (256/NC) row segments: each segment scans its rows, segment totals are
+// exchanged through `tmp` (>= 256 floats), then offsets are added.
+template <int NC>
+__device__ __forceinline__ void col_cumsum64(float* s, int lds, float mul, float* tmp) {
+  constexpr int NSEG = kThreads / NC;
+  constexpr int RPS = kChunk / NSEG;
+  const int col = threadIdx.x % NC, seg = threadIdx.x / NC;
+  float run = 0.f;
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) {
+    float* p = s + (seg * RPS + i) * lds + col;
+    run += *p;
+    *p = run;
+  }
+  tmp[seg * NC + col] = run;
+  __syncthreads();
+  float off = 0.f;
+  for (int j = 0; j < seg; ++j) off += tmp[j * NC + col];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) {
+    float* p = s + (seg * RPS + i) * lds + col;
+    *p = (*p + off) * mul;
+  }
+  __syncthreads();
 }
 
 __device__ __forceinline__ float warp_sum(float x) {
