@@ -350,6 +350,41 @@ def run_b200(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_profile_case(args, local):
+    """Small case for ncu captures: the config-1 step at batch ``args.batch``
+    (inputs still larger than L2), ``args.warmup`` + ``args.steps`` steps of
+    the four phases, no end-to-end, decode or CPU legs."""
+    from qwendopamine_b200 import _native as N
+
+    global B
+    B = args.batch
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lib = N.load()
+    x = make_config1(dev, 99)
+    tables = N.seq_tables(B, T, dev)
+    prob = N.ChunkProblem(H, K, V, N.dtype_code(torch.bfloat16), 1, K ** -0.5, tables.struct())
+    sbytes = lib.gdn2_chunk_saved_bytes(prob)
+    wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
+    saved = torch.empty(sbytes, dtype=torch.uint8, device=dev)
+    ws = torch.empty(wbytes, dtype=torch.uint8, device=dev)
+    o = torch.empty_like(x["v"])
+    gr = {n: torch.empty_like(x[n]) for n in ("q", "k", "v", "g", "b", "w")}
+    P = {n: N.ptr(t) for n, t in x.items()}
+    G = {n: N.ptr(t) for n, t in gr.items()}
+    st = N.stream_of(dev)
+    for _ in range(args.warmup + args.steps):
+        N.check(lib.gdn2_chunk_fwd(prob, P["q"], P["k"], P["v"], P["g"], P["b"], P["w"], None,
+                                   N.ptr(o), None, N.ptr(saved), sbytes, st), "fwd")
+        N.check(lib.gdn2_chunk_bwd(prob, P["q"], P["k"], P["v"], P["g"], P["b"], P["w"],
+                                   N.ptr(saved), sbytes, P["do"], None, G["q"], G["k"], G["v"],
+                                   G["g"], G["b"], G["w"], None, N.ptr(ws), wbytes, st), "bwd")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": {"batch": B, "T": T, "H": H, "K": K, "V": V,
+                                       "launches_per_step": 4,
+                                       "steps": args.warmup + args.steps}}))
+
+
 def run_decode(dev, lib, N):
     """Config 2: one in-place recurrent step over B=256 sequences per call."""
     gen = torch.Generator(device=dev).manual_seed(7)
@@ -485,7 +520,13 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--profile", action="store_true",
+                    help="small ncu case: config-1 phases at --batch, nothing else")
+    ap.add_argument("--batch", type=int, default=2, help="batch of the --profile case")
     args = ap.parse_args(argv)
+    if args.profile:
+        run_profile_case(args, int(os.environ.get("LOCAL_RANK", "0")))
+        return
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
     if args.impl == "reference":
