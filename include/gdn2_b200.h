@@ -132,6 +132,31 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p,
                          void* dq, void* dk, void* dv, float* dg, void* db, void* dw,
                          const void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- chunkwise backward without allocation -------------------------------
+ * No counterpart in the reference.  gdn2_chunk_bwd with its workspace taken
+ * from a scratch array built into the library (GDN2_NOALLOC_SCRATCH_BYTES per
+ * GPU, held until the process exits) instead of from the caller.  For callers
+ * that cannot allocate device memory while they run the backward: a plugin
+ * host that owns all device memory and hands an op only its inputs and
+ * outputs, or a loop that has reserved nearly all HBM and must not risk an
+ * allocation failure or the device synchronisation cudaMalloc/cudaFree can
+ * cause mid-step.  It allocates nothing itself.
+ *   - Problems whose gdn2_chunk_bwd_workspace_bytes() exceeds the built-in
+ *     size are rejected with GDN2_ERR_WORKSPACE (the message gives both sizes).
+ *   - The first call on a device (with that device current) looks up the
+ *     array's device address once; make it before any stream capture.
+ *   - All calls on a device share the array and leave their data in it;
+ *     nothing needs to start at zero.  Calls that overlap on the GPU race:
+ *     order them (one stream, or events). */
+#define GDN2_NOALLOC_SCRATCH_BYTES (32u << 20)
+int gdn2_chunk_bwd_noalloc(const gdn2_chunk_problem* p,
+                           const void* q, const void* k, const void* v, const float* g,
+                           const void* b, const void* w,
+                           const void* saved, size_t saved_bytes,
+                           const void* dout, const float* dht,
+                           void* dq, void* dk, void* dv, float* dg, void* db, void* dw,
+                           float* dh0, void* stream);
+
 /* ---- recurrent (decode) forward ------------------------------------------
  * Replaces fused_recurrent_gdn2_fwd (fused_recurrent_gdn2.py:344-458) and its
  * kernel (:117-341).  q,k: [B,T,H,K]; v,w: [B,T,HV,V]; g,b: [B,T,HV,K]

@@ -20,6 +20,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgdn2_b20
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = range(5)
+NOALLOC_SCRATCH_BYTES = 32 << 20  # GDN2_NOALLOC_SCRATCH_BYTES in include/gdn2_b200.h
 
 EXPORTS = (
     "gdn2_version",
@@ -33,6 +34,7 @@ EXPORTS = (
     "gdn2_chunk_bwd",
     "gdn2_chunk_bwd_state",
     "gdn2_chunk_bwd_intra",
+    "gdn2_chunk_bwd_noalloc",
     "gdn2_recurrent_fwd",
     "gdn2_cp_workspace_bytes",
     "gdn2_cp_fwd_prescan",
@@ -114,6 +116,8 @@ def _declare(lib):
         "gdn2_chunk_bwd_state": ([cp, v, c_size_t, v, v, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_chunk_bwd_intra": ([cp, v, v, v, v, v, v, v, c_size_t, v, v, v, v, v, v, v, v,
                                   c_size_t, v], ctypes.c_int),
+        "gdn2_chunk_bwd_noalloc": ([cp, v, v, v, v, v, v, v, c_size_t, v, v, v, v, v, v, v, v,
+                                    v, v], ctypes.c_int),
         "gdn2_recurrent_fwd": ([rp, v, v, v, v, v, v, v, v, v, v], ctypes.c_int),
         "gdn2_cp_fwd_prescan": ([cp, v, c_size_t, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_cp_bwd_prescan": ([cp, v, c_size_t, v, v, v, c_size_t, v], ctypes.c_int),

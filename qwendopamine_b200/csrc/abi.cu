@@ -164,6 +164,15 @@ __global__ void k_cp_merge(int N, int H, int K, int V, const float* hm_all, cons
 
 }  // namespace
 
+namespace gdn2 {
+// Record an error for gdn2_last_error() from another translation unit of the
+// library; returns `code`.
+int set_error(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+}  // namespace gdn2
+
 extern "C" {
 
 const char* gdn2_version(void) { return "gdn2_b200 0.1.0 (sm_100a)"; }
