@@ -190,8 +190,9 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p,
  * all-gathers (chunk_kda.py:1101-1185).  After the all-gather, gdn2_cp_merge
  * folds the maps of ranks 0..rank-1 into this rank's initial state
  * (chunk_kda.py:509-697, FORWARD=True).
- * Backward: gdn2_cp_bwd_prescan writes dhm = [N,H,K,V] (the state gradient a
- * zero dht produces at this span's start); gdn2_cp_merge with forward=0 folds
+ * Backward: gdn2_cp_bwd_prescan writes dhm = [N,H,K,V], the state gradient
+ * this span's outputs (and `dht`, the gradient of its end state if that is
+ * the sequence's final state; NULL otherwise) produce at the span's start; gdn2_cp_merge with forward=0 folds
  * ranks world-1..rank+1 (using their forward M, transposed) into this rank's
  * dht.  `hm_all` is [world, N, H, K, V+K] and `dhm_all` is [world, N, H, K, V]
  * (rank-major, the layout all_gather_into_tensor produces).
@@ -204,8 +205,9 @@ int gdn2_cp_fwd_prescan(const gdn2_chunk_problem* p, const void* saved,
                         size_t saved_bytes, float* hm, void* workspace,
                         size_t workspace_bytes, void* stream);
 int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved,
-                        size_t saved_bytes, const void* dout, float* dhm,
-                        void* workspace, size_t workspace_bytes, void* stream);
+                        size_t saved_bytes, const void* dout, const float* dht,
+                        float* dhm, void* workspace, size_t workspace_bytes,
+                        void* stream);
 int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all,
                   const float* dhm_all, int32_t rank, int32_t world,
                   int32_t forward, const float* init, float* state_out,

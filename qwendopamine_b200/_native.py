@@ -120,7 +120,7 @@ def _declare(lib):
                                     v, v], ctypes.c_int),
         "gdn2_recurrent_fwd": ([rp, v, v, v, v, v, v, v, v, v, v], ctypes.c_int),
         "gdn2_cp_fwd_prescan": ([cp, v, c_size_t, v, v, c_size_t, v], ctypes.c_int),
-        "gdn2_cp_bwd_prescan": ([cp, v, c_size_t, v, v, v, c_size_t, v], ctypes.c_int),
+        "gdn2_cp_bwd_prescan": ([cp, v, c_size_t, v, v, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_cp_merge": ([cp, v, v, c_int32, c_int32, c_int32, v, v, v], ctypes.c_int),
     }
     for name, (args, res) in sig.items():

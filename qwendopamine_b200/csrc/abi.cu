@@ -394,8 +394,8 @@ int gdn2_cp_fwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t s
 }
 
 int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t saved_bytes,
-                        const void* dout, float* dhm, void* workspace, size_t workspace_bytes,
-                        void* stream) {
+                        const void* dout, const float* dht, float* dhm, void* workspace,
+                        size_t workspace_bytes, void* stream) {
   (void)workspace;
   (void)workspace_bytes;
   int rc = check_problem(p, "gdn2_cp_bwd_prescan");
@@ -408,7 +408,7 @@ int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t s
   BwdStateArgs s;
   s.seqs = make_seqs(p);
   s.H = p->H; s.K = p->K; s.V = p->V;
-  s.dout = dout; s.dht = nullptr; s.dh0 = dhm;
+  s.dout = dout; s.dht = dht; s.dh0 = dhm;
   s.saved = static_cast<const unsigned char*>(saved);
   s.L = L;
   s.ws = nullptr;

@@ -1,0 +1,170 @@
+"""Sequence (context) parallel chunkwise GDN-2 on B200.
+
+The reference has context parallelism only for KDA, through FLA-CP
+(``gdn2_ops/chunk_kda.py:182-1299``): each rank runs a pre-scan over its span,
+the per-rank results are all-gathered, and each rank folds its predecessors
+into its initial state.  This module applies that algorithm to GDN-2 with the
+B200 kernels:
+
+forward (rank r owns a contiguous span of whole 64-token chunks):
+    1. ``gdn2_chunk_fwd_intra`` on the local span;
+    2. ``gdn2_cp_fwd_prescan``: the span's affine map ``S_out = M S_in + h_e``
+       as ``hm = [h_e | M]`` (``[N, H, K, V+K]`` fp32);
+    3. all-gather of ``hm`` over the group (NCCL on GPUs);
+    4. ``gdn2_cp_merge``: ``x = h0;  x = M_j x + h_e_j`` for ``j < r``;
+    5. ``gdn2_chunk_fwd_state`` from ``x``: local outputs and end state.
+backward:
+    1. ``gdn2_cp_bwd_prescan``: the span-start state gradient produced by the
+       local outputs (plus, on the last rank, the final-state gradient);
+    2. all-gather of it;
+    3. ``gdn2_cp_merge``: ``x = 0;  x = M_j^T x + dh_j`` for ``j > r`` -- the
+       gradient w.r.t. this span's end state;
+    4. ``gdn2_chunk_bwd`` with that end-state gradient.
+Each rank's local backward then yields exact gradients for its own inputs.
+
+The gather is a plain function argument so the same code runs over NCCL,
+over gloo (CPU tests of the exchange) or emulated inside one process.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+
+from .. import _native as N
+from .chunk_gdn2 import _require_cuda
+
+__all__ = ["chunk_gdn2_cp", "CPChunkGDN2Function", "gather_span_maps"]
+
+Gather = Callable[[torch.Tensor], torch.Tensor]
+
+
+def gather_span_maps(t: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather ``t`` over ``group`` into a rank-major ``[world, *t.shape]``
+    tensor (``all_gather_into_tensor`` on NCCL, a list gather otherwise)."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    out = t.new_empty((world, *t.shape))
+    t = t.contiguous()
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, t, group=group)
+    else:
+        parts = list(out.unbind(0))
+        dist.all_gather(parts, t, group=group)
+    return out
+
+
+def _problem(H, K, V, dtype, l2norm, scale, tables):
+    return N.ChunkProblem(H, K, V, N.dtype_code(dtype), int(bool(l2norm)), float(scale),
+                          tables.struct())
+
+
+class CPChunkGDN2Function(torch.autograd.Function):
+    """Autograd wrapper of the sequence-parallel forward/backward for one rank."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, b, w, initial_state, scale, l2norm, rank, world, gather):
+        lib = N.load()
+        B, T, H, K = q.shape
+        V = v.shape[-1]
+        dev = q.device
+        tables = N.seq_tables(B, T, dev)
+        prob = _problem(H, K, V, q.dtype, l2norm, scale, tables)
+        st = N.stream_of(dev)
+        sbytes = lib.gdn2_chunk_saved_bytes(prob)
+        saved = torch.empty(max(sbytes, 1), dtype=torch.uint8, device=dev)
+        N.check(lib.gdn2_chunk_fwd_intra(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
+                                         N.ptr(w), N.ptr(saved), sbytes, st),
+                "gdn2_chunk_fwd_intra")
+        hm = torch.empty(B, H, K, V + K, dtype=torch.float32, device=dev)
+        N.check(lib.gdn2_cp_fwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(hm), None, 0, st),
+                "gdn2_cp_fwd_prescan")
+        hm_all = gather(hm)
+        h0 = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
+        N.check(lib.gdn2_cp_merge(prob, N.ptr(hm_all), None, rank, world, 1,
+                                  N.ptr(initial_state), N.ptr(h0), st), "gdn2_cp_merge")
+        o = torch.empty_like(v)
+        ht = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
+        N.check(lib.gdn2_chunk_fwd_state(prob, N.ptr(h0), N.ptr(o), N.ptr(ht), N.ptr(saved),
+                                         sbytes, st), "gdn2_chunk_fwd_state")
+        ctx.save_for_backward(q, k, v, g, b, w, saved, h0, hm_all)
+        ctx.meta = (scale, l2norm, rank, world, gather, tables, initial_state is not None)
+        return o, ht
+
+    @staticmethod
+    def backward(ctx, do, dht):
+        q, k, v, g, b, w, saved, h0, hm_all = ctx.saved_tensors
+        scale, l2norm, rank, world, gather, tables, had_h0 = ctx.meta
+        lib = N.load()
+        B, T, H, K = q.shape
+        V = v.shape[-1]
+        dev = q.device
+        prob = _problem(H, K, V, q.dtype, l2norm, scale, tables)
+        st = N.stream_of(dev)
+        sbytes = lib.gdn2_chunk_saved_bytes(prob)
+        do = do.to(q.dtype).contiguous()
+        last = rank == world - 1
+        # Only the last rank's end state is the sequence's final state.
+        dht_final = dht.float().contiguous() if (last and dht is not None) else None
+        # Span-start gradient of the local outputs (and of the final state).
+        dhm = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
+        N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do), N.ptr(dht_final),
+                                        N.ptr(dhm), None, 0, st), "gdn2_cp_bwd_prescan")
+        wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
+        ws = torch.empty(max(wbytes, 1), dtype=torch.uint8, device=dev)
+        dhm_all = gather(dhm)
+        if last:
+            dht_local = dht_final
+        else:
+            dht_local = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
+            N.check(lib.gdn2_cp_merge(prob, N.ptr(hm_all), N.ptr(dhm_all), rank, world, 0, None,
+                                      N.ptr(dht_local), st), "gdn2_cp_merge (backward)")
+        grads = {n: torch.empty_like(t) for n, t in zip("qkvgbw", (q, k, v, g, b, w))}
+        dh0 = torch.empty_like(h0)
+        N.check(lib.gdn2_chunk_bwd(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
+                                   N.ptr(w), N.ptr(saved), sbytes, N.ptr(do), N.ptr(dht_local),
+                                   *(N.ptr(grads[n]) for n in "qkvgbw"), N.ptr(dh0), N.ptr(ws),
+                                   wbytes, st), "gdn2_chunk_bwd")
+        # dh0 on rank 0 is the gradient of the global initial state; on later
+        # ranks the initial state is an internal value whose gradient has been
+        # routed to the earlier ranks through their end-state gradients.
+        dinit = dh0 if (had_h0 and rank == 0) else None
+        return (grads["q"], grads["k"], grads["v"], grads["g"], grads["b"], grads["w"], dinit,
+                None, None, None, None, None)
+
+
+def chunk_gdn2_cp(q, k, v, g, b, w, *, rank: int, world: int, gather: Gather,
+                  scale: float | None = None, initial_state: torch.Tensor | None = None,
+                  use_qk_l2norm_in_kernel: bool = True):
+    """Sequence-parallel GDN-2 for the span this rank owns.
+
+    q, k, b, g: ``[B, T_r, H, K]``; v, w: ``[B, T_r, H, V]`` -- rank r's
+    contiguous slice of every sequence; every rank but the last must hold a
+    whole number of 64-token chunks.  ``initial_state`` is the global initial
+    state (``[B, H, K, V]`` fp32, the same on every rank, or None).
+    ``gather(t)`` must return the rank-major all-gather ``[world, *t.shape]``
+    (:func:`gather_span_maps` over a process group).
+
+    Returns ``(o_r, S_r)``: the local outputs and the state at the end of this
+    rank's span (on the last rank: the sequence's final state).
+    """
+    _require_cuda(q, k, v, g, b, w, initial_state)
+    assert q.shape == k.shape == g.shape == b.shape, "q, k, g, b must have the same shape."
+    assert w.shape == v.shape and v.shape[:3] == q.shape[:3], "v, w must be [B, T, H, V]."
+    if rank < world - 1 and q.shape[1] % N.CHUNK != 0:
+        raise ValueError(
+            f"rank {rank} holds {q.shape[1]} tokens: every rank but the last must own whole "
+            f"{N.CHUNK}-token chunks")
+    if initial_state is not None:
+        assert initial_state.dtype == torch.float32, "initial_state must be in float32."
+        initial_state = initial_state.contiguous()
+    if scale is None:
+        scale = k.shape[-1] ** -0.5
+    dt = q.dtype
+    q, k, v, b, w = (x.to(dt).contiguous() for x in (q, k, v, b, w))
+    g = g.float().contiguous()
+    with torch.cuda.device(q.device):
+        return CPChunkGDN2Function.apply(q, k, v, g, b, w, initial_state, scale,
+                                         use_qk_l2norm_in_kernel, rank, world, gather)

@@ -1,0 +1,143 @@
+"""Multi-process tests of the sequence-parallel exchange on CPU (gloo, 2 ranks).
+
+The GPU kernels are not needed here: each rank computes its span map with the
+oracle, the product's ``gather_span_maps`` exchanges them over gloo, and the
+fold recurrences documented for ``gdn2_cp_merge`` are checked against the
+whole-sequence oracle -- forward (initial states) and backward (end-state
+gradients).  A second test makes one rank fail before the exchange and checks
+that the survivor gets an error from the short process-group timeout instead
+of hanging.
+"""
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    gen = torch.Generator().manual_seed(0)
+    B, T, H, K, V = 1, 96, 2, 8, 8
+    q = torch.randn(B, T, H, K, generator=gen)
+    k = torch.randn(B, T, H, K, generator=gen)
+    v = torch.randn(B, T, H, V, generator=gen)
+    g = -torch.rand(B, T, H, K, generator=gen)
+    b = torch.sigmoid(torch.randn(B, T, H, K, generator=gen))
+    w = torch.sigmoid(torch.randn(B, T, H, V, generator=gen))
+    h0 = torch.randn(B, H, K, V, generator=gen) * 0.1
+    do = torch.randn(B, T, H, V, generator=gen)
+    return [x.double().numpy() for x in (q, k, v, g, b, w, h0, do)]
+
+
+def _worker_exchange(rank, world, port, out_q):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    from oracle import gdn2_oracle as O
+    from qwendopamine_b200.gdn2_ops.cp import gather_span_maps
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        q, k, v, g, b, w, h0, do = _inputs()
+        T = q.shape[1]
+        span = T // world
+        a, e = rank * span, (rank + 1) * span
+        sl = lambda x: x[:, a:e]
+        M, he = O.span_transition(*(sl(x) for x in (q, k, v, g, b, w)), norm_mode="torch")
+        K, V = q.shape[-1], v.shape[-1]
+        hm = np.concatenate([he, M], axis=-1)[0]               # [H, K, V+K]
+        hm_all = gather_span_maps(torch.from_numpy(hm), None).numpy()
+        # forward fold: x = h0; x = M_j x + h_e_j for j < rank
+        x = h0[0]
+        for j in range(rank):
+            x = np.einsum("hkm,hmv->hkv", hm_all[j][..., V:], x) + hm_all[j][..., :V]
+        # this rank's initial state must be the whole-sequence state at `a`
+        _, ref_state = O.recurrent_fwd(*(x_[:, :a] for x_ in (q, k, v, g, b, w)), h0,
+                                       norm_mode="torch")
+        fwd_err = float(np.abs(x - ref_state[0]).max()) if a > 0 else float(np.abs(x - h0[0]).max())
+        # backward: span-start gradient of the local outputs with zero end gradient
+        *_, dh_start = O.recurrent_bwd(*(sl(x_) for x_ in (q, k, v, g, b, w)), sl(do), x[None],
+                                       None, norm_mode="torch")
+        dh_all = gather_span_maps(torch.from_numpy(dh_start[0]), None).numpy()
+        y = np.zeros_like(dh_start[0])
+        for j in range(world - 1, rank, -1):
+            y = np.einsum("hmk,hmv->hkv", hm_all[j][..., V:], y) + dh_all[j]
+        # reference end-state gradient: gradient of the later outputs w.r.t. S_e
+        if rank < world - 1:
+            *_, ref_dh = O.recurrent_bwd(*(x_[:, e:] for x_ in (q, k, v, g, b, w)), do[:, e:],
+                                         np.zeros((1,) + y.shape), None, norm_mode="torch")
+            bwd_err = float(np.abs(y - ref_dh[0]).max())
+        else:
+            bwd_err = float(np.abs(y).max())
+        order_ok = bool(np.allclose(hm_all[rank], hm))
+        out_q.put((rank, fwd_err, bwd_err, order_ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def _worker_fail(rank, world, port, out_q):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    from qwendopamine_b200.gdn2_ops.cp import gather_span_maps
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        out_q.put((rank, "raised"))
+        raise SystemExit(3)  # this rank dies before the exchange
+    try:
+        gather_span_maps(torch.zeros(4), None)
+        out_q.put((rank, "no-error"))
+    except Exception as exc:  # the timeout surfaces as an error, not a hang
+        out_q.put((rank, f"error:{type(exc).__name__}"))
+
+
+def _run(fn, world, timeout):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    for _ in range(world):
+        results.append(q.get(timeout=timeout))
+    for p in procs:
+        p.join(timeout=timeout)
+        if p.is_alive():
+            p.kill()
+    return sorted(results)
+
+
+def test_span_map_exchange_and_fold_over_gloo():
+    res = _run(_worker_exchange, 2, timeout=120)
+    assert [r[0] for r in res] == [0, 1]
+    for rank, fwd_err, bwd_err, order_ok in res:
+        assert order_ok, rank
+        assert fwd_err < 1e-10, (rank, fwd_err)
+        assert bwd_err < 1e-10, (rank, bwd_err)
+
+
+def test_dead_rank_surfaces_as_error_not_hang():
+    res = _run(_worker_fail, 2, timeout=120)
+    assert res[1] == (1, "raised")
+    assert res[0][0] == 0 and res[0][1].startswith("error:")
