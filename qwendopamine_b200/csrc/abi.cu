@@ -16,6 +16,8 @@ template <typename T, int D> cudaError_t launch_fwd_state(const FwdStateArgs&, c
 template <typename T, int D> cudaError_t launch_bwd_state(const BwdStateArgs&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_intra(const BwdIntraArgs&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_recurrent(const RecArgs&, cudaStream_t);
+template <typename T, int D, int BV> cudaError_t launch_fwd_state16(const FwdStateArgs&, cudaStream_t);
+template <typename T, int D, int BV> cudaError_t launch_bwd_state16(const BwdStateArgs&, cudaStream_t);
 }  // namespace gdn2
 
 using namespace gdn2;
@@ -112,6 +114,52 @@ template <typename T, int D> struct RunBwdIntra {
 template <typename T, int D> struct RunRec {
   static cudaError_t run(const RecArgs& a, cudaStream_t s) { return launch_recurrent<T, D>(a, s); }
 };
+
+// State passes: 16-bit inputs whose head sizes are multiples of 8 take the
+// ldmatrix / m16n8k16 kernels (state16.cu); everything else the generic ones.
+// The value tile is 128 columns when that still gives one CTA per SM or more,
+// else 64.
+template <typename T, int D, int BV>
+cudaError_t launch_state16(const FwdStateArgs& a, cudaStream_t st) {
+  return launch_fwd_state16<T, D, BV>(a, st);
+}
+template <typename T, int D, int BV>
+cudaError_t launch_state16(const BwdStateArgs& a, cudaStream_t st) {
+  return launch_bwd_state16<T, D, BV>(a, st);
+}
+
+template <typename T, typename Args>
+cudaError_t run_state16(const Args& a, int bucket, int cols, int n_seqs, int H, cudaStream_t st) {
+  if (bucket == 64) return launch_state16<T, 64, 64>(a, st);
+  const long ctas128 = (long)n_seqs * H * ((cols + 127) / 128);
+  if (ctas128 >= 148) return launch_state16<T, 128, 128>(a, st);
+  return launch_state16<T, 128, 64>(a, st);
+}
+
+bool use16(const gdn2_chunk_problem* p) {
+  return p->dtype != GDN2_DTYPE_F32 && (p->K % 8) == 0 && (p->V % 8) == 0;
+}
+
+cudaError_t fwd_state_dispatch(const gdn2_chunk_problem* p, const FwdStateArgs& a, cudaStream_t st) {
+  const int bucket = head_bucket(p->K, p->V);
+  if (use16(p)) {
+    const int cols = a.prescan ? p->V + p->K : p->V;
+    if (p->dtype == GDN2_DTYPE_BF16)
+      return run_state16<__nv_bfloat16>(a, bucket, cols, p->seqs.n_seqs, p->H, st);
+    return run_state16<__half>(a, bucket, cols, p->seqs.n_seqs, p->H, st);
+  }
+  return dispatch<RunFwdState>(p->dtype, bucket, a, st);
+}
+
+cudaError_t bwd_state_dispatch(const gdn2_chunk_problem* p, const BwdStateArgs& a, cudaStream_t st) {
+  const int bucket = head_bucket(p->K, p->V);
+  if (use16(p)) {
+    if (p->dtype == GDN2_DTYPE_BF16)
+      return run_state16<__nv_bfloat16>(a, bucket, p->V, p->seqs.n_seqs, p->H, st);
+    return run_state16<__half>(a, bucket, p->V, p->seqs.n_seqs, p->H, st);
+  }
+  return dispatch<RunBwdState>(p->dtype, bucket, a, st);
+}
 
 // ---- context-parallel merge ----------------------------------------------
 // One CTA per (sequence, head, 32-column tile of the state); the running
@@ -247,7 +295,7 @@ int gdn2_chunk_fwd_state(const gdn2_chunk_problem* p, const float* h0, void* o, 
   a.L = L;
   a.prescan = 0;
   a.hm = nullptr;
-  cudaError_t e = dispatch<RunFwdState>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  cudaError_t e = fwd_state_dispatch(p, a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_fwd_state");
 }
 
@@ -283,7 +331,7 @@ int gdn2_chunk_bwd_state(const gdn2_chunk_problem* p, const void* saved, size_t 
   s.ws = static_cast<unsigned char*>(workspace);
   s.BL = BL;
   s.prescan = 0;
-  cudaError_t e = dispatch<RunBwdState>(p->dtype, head_bucket(p->K, p->V), s, (cudaStream_t)stream);
+  cudaError_t e = bwd_state_dispatch(p, s, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_bwd_state");
 }
 
@@ -389,7 +437,7 @@ int gdn2_cp_fwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t s
   a.L = L;
   a.prescan = 1;
   a.hm = hm;
-  cudaError_t e = dispatch<RunFwdState>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  cudaError_t e = fwd_state_dispatch(p, a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_fwd_prescan");
 }
 
@@ -414,7 +462,7 @@ int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t s
   s.ws = nullptr;
   s.BL = bwd_layout_of(p);
   s.prescan = 1;
-  cudaError_t e = dispatch<RunBwdState>(p->dtype, head_bucket(p->K, p->V), s, (cudaStream_t)stream);
+  cudaError_t e = bwd_state_dispatch(p, s, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_bwd_prescan");
 }
 

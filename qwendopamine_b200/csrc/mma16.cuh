@@ -1,0 +1,163 @@
+// mma16.cuh -- 16-bit tensor-core tiles from shared memory (bf16 / fp16).
+//
+// Operands live in shared memory as row-major 16-bit tiles whose row pitch is
+// a multiple of 16 bytes and not a multiple of 128 bytes (e.g. D + 8
+// elements), so ldmatrix row fetches are bank-conflict free.  A warp computes
+// acc[(16*MT) x (8*NT)] (fp32) += A[(16*MT) x kd] * B[kd x (8*NT)] with
+// mma.sync m16n8k16 and fp32 accumulation; ldmatrix (.trans when needed)
+// turns either storage orientation of A or B into the register fragments:
+//   A_KMAJOR:  A(m,k) = A[m*lda + k]   (else A(m,k) = A[k*lda + m])
+//   B_KMAJOR:  B(k,n) = B[n*ldb + k]   (else B(k,n) = B[k*ldb + n])
+// Also: cp.async 16-byte global->shared copies with zero fill.
+#pragma once
+
+#include "common.cuh"
+
+namespace gdn2 {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+template <typename T> struct Mma16;
+template <> struct Mma16<__nv_bfloat16> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                             uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+template <> struct Mma16<__half> {
+  static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                             uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+};
+
+// A fragment (16 x 16 at rows m0, cols k0 of the logical A).
+template <bool A_KMAJOR, typename T>
+__device__ __forceinline__ void load_a16(uint32_t (&a)[4], const T* A, int lda, int m0, int k0) {
+  const int lane = threadIdx.x & 31;
+  if (A_KMAJOR) {
+    const int r = m0 + (lane & 15), c = k0 + ((lane >> 4) << 3);
+    ldsm_x4(a, A + r * lda + c);
+  } else {
+    const int j = lane >> 3, rr = lane & 7;
+    const int k = k0 + rr + ((j >> 1) << 3), m = m0 + ((j & 1) << 3);
+    ldsm_x4_t(a, A + k * lda + m);
+  }
+}
+
+// Two B fragments (k0..k0+15 x n0..n0+15): b[0],b[1] for n0..n0+7 and
+// b[2],b[3] for n0+8..n0+15.
+template <bool B_KMAJOR, typename T>
+__device__ __forceinline__ void load_b16x2(uint32_t (&b)[4], const T* B, int ldb, int k0, int n0) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane >> 3, rr = lane & 7;
+  if (B_KMAJOR) {
+    const int n = n0 + rr + ((j >> 1) << 3), k = k0 + ((j & 1) << 3);
+    ldsm_x4(b, B + n * ldb + k);
+  } else {
+    const int k = k0 + rr + ((j & 1) << 3), n = n0 + ((j >> 1) << 3);
+    ldsm_x4_t(b, B + k * ldb + n);
+  }
+}
+
+// acc[16*MT x 8*NT] += A[rows m0.., k 0..kd) * B[k 0..kd, cols n0..); NT even.
+template <int MT, int NT, bool A_KMAJOR, bool B_KMAJOR, typename T>
+__device__ __forceinline__ void warp_mma16(float (&acc)[MT][NT][4], const T* A, int lda, int m0,
+                                           const T* B, int ldb, int n0, int kd) {
+  static_assert(NT % 2 == 0, "NT must be even");
+#pragma unroll 2
+  for (int k0 = 0; k0 < kd; k0 += 16) {
+    uint32_t a[MT][4];
+#pragma unroll
+    for (int i = 0; i < MT; ++i) load_a16<A_KMAJOR>(a[i], A, lda, m0 + 16 * i, k0);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      load_b16x2<B_KMAJOR>(b, B, ldb, k0, n0 + 8 * j);
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        Mma16<T>::run(acc[i][j], a[i], b[0], b[1]);
+        Mma16<T>::run(acc[i][j + 1], a[i], b[2], b[3]);
+      }
+    }
+  }
+}
+
+// Pack two floats into a 16-bit pair (low half = first).
+template <typename T> __device__ __forceinline__ uint32_t pack2(float x, float y);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float x, float y) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float x, float y) {
+  __half2 v = __floats2half2_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// ---------------------------------------------------------------------------
+// cp.async
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)),
+               "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// Copy a ROWS x COLS 16-bit tile (global row stride ldg elements, 16-byte
+// aligned rows) into shared memory (row stride lds), asynchronously.  Rows
+// >= nrows / cols >= ncols (ncols a multiple of 8) are zero-filled.
+template <typename T, int ROWS, int COLS, int NTH>
+__device__ __forceinline__ void cp_tile16(T* s, int lds, const T* g, int64_t ldg, int nrows,
+                                          int ncols) {
+  constexpr int CPR = COLS / 8;
+  constexpr int TOTAL = ROWS * CPR;
+#pragma unroll
+  for (int it = 0; it < (TOTAL + NTH - 1) / NTH; ++it) {
+    const int idx = threadIdx.x + it * NTH;
+    if (idx < TOTAL) {
+      const int r = idx / CPR, c = (idx - r * CPR) * 8;
+      const bool ok = r < nrows && c < ncols;
+      cp_async16(s + r * lds + c, ok ? (const void*)(g + (int64_t)r * ldg + c) : (const void*)g,
+                 ok);
+    }
+  }
+}
+
+// Same for an fp32 vector of n floats (n a multiple of 4), zero beyond n.
+template <int N, int NTH>
+__device__ __forceinline__ void cp_vec32(float* s, const float* g, int n) {
+  constexpr int CH = N / 4;
+  for (int idx = threadIdx.x; idx < CH; idx += NTH) {
+    const bool ok = idx * 4 < n;
+    cp_async16(s + idx * 4, ok ? (const void*)(g + idx * 4) : (const void*)g, ok);
+  }
+}
+
+}  // namespace gdn2

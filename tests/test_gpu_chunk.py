@@ -258,3 +258,23 @@ def test_backward_is_deterministic(cuda_device):
     g2 = _grads(d, cuda_device, torch.bfloat16, do, dht)
     for n in g1:
         assert torch.equal(g1[n], g2[n]), n
+
+
+@pytest.mark.parametrize("B,T,H,K,V", [
+    (10, 70, 16, 128, 128),   # >= 148 sequence-heads: 128-column state tiles
+    (3, 150, 4, 64, 64),      # 64-wide head bucket
+    (2, 100, 4, 64, 128),     # K < V in the 128 bucket, 64-column state tiles
+])
+def test_forward_backward_16bit_state_tiles(cuda_device, B, T, H, K, V):
+    d = make_inputs(B, T, H, K, V, seed=B * T + K, dtype=torch.bfloat16)
+    gen = torch.Generator().manual_seed(B + T)
+    do = torch.randn(B, T, H, V, generator=gen).bfloat16().float()
+    dht = torch.randn(B, H, K, V, generator=gen)
+    o, ht = _chunk(d, cuda_device, torch.bfloat16)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < TOL[torch.bfloat16] and rel(ht, rh) < TOL[torch.bfloat16]
+    gr = _grads(d, cuda_device, torch.bfloat16, do, dht)
+    ref = O.recurrent_bwd(*np_(d, NAMES), do.numpy(), d["h0"].numpy(), dht.numpy(),
+                          norm_mode="fla")
+    for n, r in zip((*NAMES, "h0"), ref):
+        assert rel(gr[n], r) < TOL[torch.bfloat16], n
