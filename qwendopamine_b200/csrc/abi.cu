@@ -18,6 +18,7 @@ template <typename T, int D> cudaError_t launch_bwd_intra(const BwdIntraArgs&, c
 template <typename T, int D> cudaError_t launch_recurrent(const RecArgs&, cudaStream_t);
 template <typename T, int D, int BV> cudaError_t launch_fwd_state16(const FwdStateArgs&, cudaStream_t);
 template <typename T, int D, int BV> cudaError_t launch_bwd_state16(const BwdStateArgs&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_bwd_intra16(const BwdIntraArgs&, cudaStream_t);
 }  // namespace gdn2
 
 using namespace gdn2;
@@ -159,6 +160,18 @@ cudaError_t bwd_state_dispatch(const gdn2_chunk_problem* p, const BwdStateArgs& 
     return run_state16<__half>(a, bucket, p->V, p->seqs.n_seqs, p->H, st);
   }
   return dispatch<RunBwdState>(p->dtype, bucket, a, st);
+}
+
+cudaError_t bwd_intra_dispatch(const gdn2_chunk_problem* p, const BwdIntraArgs& a, cudaStream_t st) {
+  const int bucket = head_bucket(p->K, p->V);
+  if (use16(p)) {
+    if (p->dtype == GDN2_DTYPE_BF16)
+      return bucket == 64 ? launch_bwd_intra16<__nv_bfloat16, 64>(a, st)
+                          : launch_bwd_intra16<__nv_bfloat16, 128>(a, st);
+    return bucket == 64 ? launch_bwd_intra16<__half, 64>(a, st)
+                        : launch_bwd_intra16<__half, 128>(a, st);
+  }
+  return dispatch<RunBwdIntra>(p->dtype, bucket, a, st);
 }
 
 // ---- context-parallel merge ----------------------------------------------
@@ -365,7 +378,7 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.ws = static_cast<const unsigned char*>(workspace);
   a.BL = BL;
   a.dq = dq; a.dk = dk; a.dv = dv; a.dg = dg; a.db = db; a.dw = dw;
-  cudaError_t e = dispatch<RunBwdIntra>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  cudaError_t e = bwd_intra_dispatch(p, a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_bwd_intra");
 }
 

@@ -1,0 +1,563 @@
+// bwd16.cu -- per-chunk GDN-2 gradients for 16-bit inputs (bf16 / fp16).
+//
+// One CTA of 16 warps per (chunk, head).  Same mathematics as k_bwd_intra
+// (chunk_bwd.cu), organised so that almost nothing waits on memory:
+//   * one cp.async round trip brings q, k, b (16-bit), g (fp32) and A;
+//   * the value side streams 32-column slices of h, dh, dO, VN, dVN, v, w
+//     through a cp.async double buffer while the previous slice computes
+//     (dQg = dO h^T, dKd = VN dh^T, dW = -dVN h^T, dAqk = dO VN^T,
+//      dA = dVN (w v)^T, dZ = A^T dVN -> dv, dw);
+//   * the key side needs no further loads.  Each warp owns a 16-row x D/4
+//     column tile and keeps its dq, d(b k), dk, dG and Kd-term accumulators
+//     in registers; the score backward products are issued so that their
+//     outputs land on the owning warp (block-row I of the X products on the
+//     warps of row block I, block-column J of the Y products on those of J).
+// All products: ldmatrix fragments, mma.sync m16n8k16, fp32 accumulation.
+// As in k_bwd_intra, the dAqk diagonal and the last-row Kd term are kept out
+// of dG (they cancel exactly), and dg is a suffix scan of dG plus a prefix
+// scan of the Kd terms.
+#include "chunk_args.cuh"
+#include "mma16.cuh"
+
+namespace gdn2 {
+
+constexpr int kThreadsB16 = 512;
+
+template <int D>
+struct Bwd16Layout {
+  static constexpr int LDK = D + 8;      // 16-bit 64 x D tiles
+  static constexpr int LDG = D + 4;      // fp32 64 x D tiles
+  static constexpr int LDC = kChunk + 8; // 16-bit 64 x 64 tiles
+  static constexpr int LDS = 32 + 8;     // 16-bit value slices
+  // persistent region (bytes)
+  static constexpr int oQ = 0;
+  static constexpr int oK = oQ + kChunk * LDK * 2;
+  static constexpr int oB = oK + kChunk * LDK * 2;
+  static constexpr int oG = oB + kChunk * LDK * 2;
+  static constexpr int oA = oG + kChunk * LDG * 4;
+  static constexpr int oMisc = oA + kChunk * LDC * 2;
+  // misc floats: rq[64] rk[64] dgl[D] diag[64] pdq[4][64] pdk[4][64] flag
+  static constexpr int nMisc = 64 + 64 + D + 64 + 256 + 256 + 4;
+  static constexpr int oW = oMisc + nMisc * 4;
+  // phase V (offsets inside W)
+  static constexpr int vH = 0;
+  static constexpr int vDH = vH + D * LDS * 2;
+  static constexpr int vDO = vDH + D * LDS * 2;
+  static constexpr int vVN = vDO + kChunk * LDS * 2;
+  static constexpr int vDVN = vVN + kChunk * LDS * 2;
+  static constexpr int vV = vDVN + kChunk * LDS * 2;
+  static constexpr int vWg = vV + kChunk * LDS * 2;
+  static constexpr int slot = vWg + kChunk * LDS * 2;
+  static constexpr int vZ = 2 * slot;
+  static constexpr int phaseV = vZ + kChunk * LDS * 2;
+  // phase K
+  static constexpr int kDAqk = 0;
+  static constexpr int kDAkk = kDAqk + kChunk * LDC * 2;
+  static constexpr int kR2 = kDAkk + kChunk * LDC * 2;
+  static constexpr int kDW = kR2;
+  static constexpr int kE = kDW + kChunk * LDK * 2;
+  static constexpr int kT1 = kE + kChunk * LDK * 2;
+  static constexpr int kT2 = kT1 + kChunk * LDC * 2;
+  static constexpr int kQs = kR2;
+  static constexpr int kKBs = kQs + kChunk * LDK * 2;
+  static constexpr int kKs = kKBs + kChunk * LDK * 2;
+  static constexpr int kEnd = kKs + 160 * LDK * 2;
+  static constexpr int kdG = 0;
+  static constexpr int kX = kdG + kChunk * LDG * 4;
+  static constexpr int kTmp = kX + kChunk * LDG * 4;
+  static constexpr int kScanEnd = kTmp + kThreadsB16 * 4;
+  static constexpr int W = phaseV > kEnd ? (phaseV > kScanEnd ? phaseV : kScanEnd)
+                                         : (kEnd > kScanEnd ? kEnd : kScanEnd);
+  static constexpr size_t bytes = (size_t)oW + W;
+  static_assert(kT2 + kChunk * LDC * 2 <= kEnd || kT2 + kChunk * LDC * 2 <= W, "layout");
+  static_assert(oW % 16 == 0 && slot % 16 == 0, "alignment");
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) {
+  using L = Bwd16Layout<D>;
+  constexpr int LDK = L::LDK, LDG = L::LDG, LDC = L::LDC, LDS = L::LDS;
+  constexpr int NTH = kThreadsB16;
+  constexpr int DQ = D / 4;    // owner tile width
+  constexpr int NTO = DQ / 8;  // n8 fragments per owner tile
+  extern __shared__ __align__(16) unsigned char sm[];
+  T* sq = reinterpret_cast<T*>(sm + L::oQ);
+  T* sk = reinterpret_cast<T*>(sm + L::oK);
+  T* sb = reinterpret_cast<T*>(sm + L::oB);
+  float* sG = reinterpret_cast<float*>(sm + L::oG);
+  T* sA = reinterpret_cast<T*>(sm + L::oA);
+  float* misc = reinterpret_cast<float*>(sm + L::oMisc);
+  float* rq = misc;
+  float* rk = rq + 64;
+  float* dgl = rk + 64;
+  float* sDiag = dgl + D;
+  float* pdq = sDiag + 64;  // [4][64]
+  float* pdk = pdq + 256;   // [4][64]
+  int* sFlag = reinterpret_cast<int*>(pdk + 256);
+  unsigned char* W = sm + L::oW;
+
+  const int c = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int wr = warp & 3, wc = warp >> 2;
+  const int H = a.H, K = a.K, V = a.V;
+  const ChunkPos cp = chunk_pos(a.seqs, c);
+  const int len = cp.len;
+  const int64_t ldk = (int64_t)H * K, ldv = (int64_t)H * V;
+  const int64_t offk = cp.row0 * ldk + (int64_t)h * K;
+  const int64_t offv = cp.row0 * ldv + (int64_t)h * V;
+  const size_t ch = (size_t)c * H + h;
+  const float scale = a.scale;
+
+  const T* gh = reinterpret_cast<const T*>(a.saved + a.L.h) + ch * (size_t)K * V;
+  const T* gdh = reinterpret_cast<const T*>(a.ws + a.BL.dh) + ch * (size_t)K * V;
+  const T* gvn = reinterpret_cast<const T*>(a.saved + a.L.vn) + ch * (size_t)kChunk * V;
+  const T* gdvn = reinterpret_cast<const T*>(a.ws + a.BL.dvn) + ch * (size_t)kChunk * V;
+  const T* gdo = reinterpret_cast<const T*>(a.dout) + offv;
+  const T* gv = reinterpret_cast<const T*>(a.v) + offv;
+  const T* gw = reinterpret_cast<const T*>(a.w) + offv;
+
+  auto slotp = [&](int s, int off) { return reinterpret_cast<T*>(W + s * L::slot + off); };
+  auto issue_slice = [&](int v0, int s) {
+    const int nv = min(32, V - v0);
+    cp_tile16<T, D, 32, NTH>(slotp(s, L::vH), LDS, gh + v0, V, K, nv);
+    cp_tile16<T, D, 32, NTH>(slotp(s, L::vDH), LDS, gdh + v0, V, K, nv);
+    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vDO), LDS, gdo + v0, ldv, len, nv);
+    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vVN), LDS, gvn + v0, V, kChunk, nv);
+    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vDVN), LDS, gdvn + v0, V, kChunk, nv);
+    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vV), LDS, gv + v0, ldv, len, nv);
+    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vWg), LDS, gw + v0, ldv, len, nv);
+  };
+
+  // ---- phase 0: one round trip for q, k, b, g, A and the first slice -------
+  cp_tile16<T, kChunk, D, NTH>(sq, LDK, reinterpret_cast<const T*>(a.q) + offk, ldk, len, K);
+  cp_tile16<T, kChunk, D, NTH>(sk, LDK, reinterpret_cast<const T*>(a.k) + offk, ldk, len, K);
+  cp_tile16<T, kChunk, D, NTH>(sb, LDK, reinterpret_cast<const T*>(a.b) + offk, ldk, len, K);
+  cp_tile32<kChunk, D, NTH>(sG, LDG, a.g + offk, ldk, len, K);
+  cp_tile16<T, kChunk, kChunk, NTH>(
+      sA, LDC, reinterpret_cast<const T*>(a.saved + a.L.a) + ch * kChunk * kChunk, kChunk, kChunk,
+      kChunk);
+  issue_slice(0, 0);
+  cp_async_commit();
+  for (int i = tid; i < D; i += NTH) dgl[i] = 0.f;
+  cp_async_wait<0>();
+  __syncthreads();
+  // chunk-local log2 cumulative decay; row norms
+  col_scan64_t<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(W + L::vZ));
+  for (int i = tid; i < kChunk * D; i += NTH) {
+    const int r = i / D, cc = i - r * D;
+    sG[r * LDG + cc] *= kLog2e;
+  }
+  for (int r = warp; r < kChunk; r += NTH / 32) {
+    float s1 = 0.f, s2 = 0.f;
+    for (int cc = lane; cc < D; cc += 32) {
+      const float x = to_f<T>(sq[r * LDK + cc]), y = to_f<T>(sk[r * LDK + cc]);
+      s1 += x * x;
+      s2 += y * y;
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) {
+      rq[r] = a.l2norm ? rsqrtf(s1 + kNormEps) : 1.f;
+      rk[r] = a.l2norm ? rsqrtf(s2 + kNormEps) : 1.f;
+    }
+  }
+
+  // ---- phase V --------------------------------------------------------------
+  float accQ[1][NTO][4], accKd[1][NTO][4], accW[1][NTO][4], accAqk[1][2][4], accDA[1][2][4];
+  acc_zero(accQ);
+  acc_zero(accKd);
+  acc_zero(accW);
+  acc_zero(accAqk);
+  acc_zero(accDA);
+  T* sZ = reinterpret_cast<T*>(W + L::vZ);
+  T* gdv = reinterpret_cast<T*>(a.dv) + offv;
+  T* gdw = reinterpret_cast<T*>(a.dw) + offv;
+  const int nslices = (V + 31) / 32;
+  for (int s = 0; s < nslices; ++s) {
+    const int cur = s & 1, v0 = 32 * s, nv = min(32, V - v0);
+    if (s + 1 < nslices) {
+      __syncthreads();  // the other slot's last readers are done
+      issue_slice(v0 + 32, cur ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    T* hs = slotp(cur, L::vH);
+    T* dhs = slotp(cur, L::vDH);
+    T* dos = slotp(cur, L::vDO);
+    T* vns = slotp(cur, L::vVN);
+    T* dvns = slotp(cur, L::vDVN);
+    T* vs = slotp(cur, L::vV);
+    T* ws = slotp(cur, L::vWg);
+    for (int i = tid; i < kChunk * 16; i += NTH) {
+      const int r = i >> 4, cc = (i & 15) * 2;
+      const float z0 = to_f<T>(vs[r * LDS + cc]) * to_f<T>(ws[r * LDS + cc]);
+      const float z1 = to_f<T>(vs[r * LDS + cc + 1]) * to_f<T>(ws[r * LDS + cc + 1]);
+      *reinterpret_cast<uint32_t*>(sZ + r * LDS + cc) = pack2<T>(z0, z1);
+    }
+    if (tid < D) {
+      float acc = 0.f;
+#pragma unroll 8
+      for (int cc = 0; cc < 32; ++cc)
+        acc += to_f<T>(hs[tid * LDS + cc]) * to_f<T>(dhs[tid * LDS + cc]);
+      dgl[tid] += acc;
+    }
+    __syncthreads();
+    warp_mma16<1, NTO, true, true>(accQ, dos, LDS, 16 * wr, hs, LDS, wc * DQ, 32);
+    warp_mma16<1, NTO, true, true>(accKd, vns, LDS, 16 * wr, dhs, LDS, wc * DQ, 32);
+    warp_mma16<1, NTO, true, true>(accW, dvns, LDS, 16 * wr, hs, LDS, wc * DQ, 32);
+    warp_mma16<1, 2, true, true>(accAqk, dos, LDS, 16 * wr, vns, LDS, 16 * wc, 32);
+    warp_mma16<1, 2, true, true>(accDA, dvns, LDS, 16 * wr, sZ, LDS, 16 * wc, 32);
+    if (warp < 8) {
+      float accZ[1][2][4];
+      acc_zero(accZ);
+      const int zm = 16 * (warp & 3), zn = 16 * (warp >> 2);
+      warp_mma16<1, 2, false, false>(accZ, sA, LDC, zm, dvns, LDS, zn, kChunk);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int r = zm + gid + 8 * hf, cl = zn + 8 * j + 2 * tig;
+          if (r < len && cl < nv) {
+            const float z0 = accZ[0][j][2 * hf], z1 = accZ[0][j][2 * hf + 1];
+            const float w0 = to_f<T>(ws[r * LDS + cl]), w1 = to_f<T>(ws[r * LDS + cl + 1]);
+            const float x0 = to_f<T>(vs[r * LDS + cl]), x1 = to_f<T>(vs[r * LDS + cl + 1]);
+            *reinterpret_cast<uint32_t*>(gdv + r * ldv + v0 + cl) = pack2<T>(z0 * w0, z1 * w1);
+            *reinterpret_cast<uint32_t*>(gdw + r * ldv + v0 + cl) = pack2<T>(z0 * x0, z1 * x1);
+          }
+        }
+    }
+  }
+  __syncthreads();  // phase V buffers are dead from here on
+
+  // ---- dump dW and dAqk ------------------------------------------------------
+  T* sDAqk = reinterpret_cast<T*>(W + L::kDAqk);
+  T* sDAkk = reinterpret_cast<T*>(W + L::kDAkk);
+  T* sDW = reinterpret_cast<T*>(W + L::kDW);
+  T* sE = reinterpret_cast<T*>(W + L::kE);
+  T* sT1 = reinterpret_cast<T*>(W + L::kT1);
+  T* sT2 = reinterpret_cast<T*>(W + L::kT2);
+#pragma unroll
+  for (int j = 0; j < NTO; ++j)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
+      *reinterpret_cast<uint32_t*>(sDW + r * LDK + cl) =
+          pack2<T>(-accW[0][j][2 * hf], -accW[0][j][2 * hf + 1]);
+    }
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = 16 * wr + gid + ((e >> 1) << 3), i = 16 * wc + 8 * j + 2 * tig + (e & 1);
+      sDAqk[r * LDC + i] = from_f<T>(i < r ? accAqk[0][j][e] : 0.f);
+      if (i == r) sDiag[r] = accAqk[0][j][e];
+    }
+  // E = b * k_n * 2^G
+  for (int i = tid; i < kChunk * (D / 2); i += NTH) {
+    const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
+    const float e0 = to_f<T>(sb[r * LDK + cc]) * to_f<T>(sk[r * LDK + cc]) * rk[r] *
+                     exp2f(sG[r * LDG + cc]);
+    const float e1 = to_f<T>(sb[r * LDK + cc + 1]) * to_f<T>(sk[r * LDK + cc + 1]) * rk[r] *
+                     exp2f(sG[r * LDG + cc + 1]);
+    *reinterpret_cast<uint32_t*>(sE + r * LDK + cc) = pack2<T>(e0, e1);
+  }
+  __syncthreads();
+  // dA += dW E^T ; dAkk = -tril_strict(A^T dA A^T)
+  warp_mma16<1, 2, true, true>(accDA, sDW, LDK, 16 * wr, sE, LDK, 16 * wc, D);
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = 16 * wr + gid + 8 * hf, cl = 16 * wc + 8 * j + 2 * tig;
+      *reinterpret_cast<uint32_t*>(sT1 + r * LDC + cl) =
+          pack2<T>(accDA[0][j][2 * hf], accDA[0][j][2 * hf + 1]);
+    }
+  __syncthreads();
+  {
+    float t[1][2][4];
+    acc_zero(t);
+    warp_mma16<1, 2, false, false>(t, sA, LDC, 16 * wr, sT1, LDC, 16 * wc, kChunk);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = 16 * wr + gid + 8 * hf, cl = 16 * wc + 8 * j + 2 * tig;
+        *reinterpret_cast<uint32_t*>(sT2 + r * LDC + cl) = pack2<T>(t[0][j][2 * hf], t[0][j][2 * hf + 1]);
+      }
+    __syncthreads();
+    acc_zero(t);
+    warp_mma16<1, 2, true, true>(t, sT2, LDC, 16 * wr, sA, LDC, 16 * wc, kChunk);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = 16 * wr + gid + ((e >> 1) << 3), i = 16 * wc + 8 * j + 2 * tig + (e & 1);
+        sDAkk[r * LDC + i] = from_f<T>(i < r ? -t[0][j][e] : 0.f);
+      }
+  }
+  // dE = A^T dW (owner tile)
+  float accE[1][NTO][4];
+  acc_zero(accE);
+  warp_mma16<1, NTO, false, false>(accE, sA, LDC, 16 * wr, sDW, LDK, wc * DQ, kChunk);
+
+  // ---- owner initialisation ---------------------------------------------
+  // dq <- scale 2^G dQg, dkb <- 2^G dE, dk <- Kd part, X <- k_n * Kd part,
+  // dG <- q_n dq + b k_n dkb
+  float (&dq)[1][NTO][4] = accQ;
+  float (&dkb)[1][NTO][4] = accE;
+  float (&dkn)[1][NTO][4] = accKd;
+  float (&dG)[1][NTO][4] = accW;
+  float X[NTO][4];
+#pragma unroll
+  for (int j = 0; j < NTO; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
+      const float G = sG[r * LDG + cl], GL = sG[(kChunk - 1) * LDG + cl];
+      const float gam = exp2f(G);
+      const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
+      const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
+      const float bb = to_f<T>(sb[r * LDK + cl]);
+      dq[0][j][e] = scale * gam * dq[0][j][e];
+      dkb[0][j][e] = gam * dkb[0][j][e];
+      const float kd = dkn[0][j][e] * exp2f(GL - G);
+      dkn[0][j][e] = kd;
+      X[j][e] = kn * kd;
+      dG[0][j][e] = qn * dq[0][j][e] + bb * kn * dkb[0][j][e];
+    }
+  __syncthreads();  // sDW / sE / sT* are dead; R2 becomes the score tiles
+
+  // ---- score backward ---------------------------------------------------------
+  T* sQs = reinterpret_cast<T*>(W + L::kQs);
+  T* sKBs = reinterpret_cast<T*>(W + L::kKBs);
+  T* sKs = reinterpret_cast<T*>(W + L::kKs);
+  if (tid == 0) sFlag[0] = 1;
+  __syncthreads();
+  for (int i = tid; i < kChunk * (D / 2); i += NTH) {
+    const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
+    const int rb = r & ~15;
+    float q2[2], kb2[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float f = exp2f(sG[r * LDG + cc + t] - sG[rb * LDG + cc + t]);
+      const float kn = to_f<T>(sk[r * LDK + cc + t]) * rk[r];
+      q2[t] = scale * to_f<T>(sq[r * LDK + cc + t]) * rq[r] * f;
+      kb2[t] = to_f<T>(sb[r * LDK + cc + t]) * kn * f;
+    }
+    *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(q2[0], q2[1]);
+    *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kb2[0], kb2[1]);
+  }
+  for (int i = tid; i < 160 * (D / 2); i += NTH) {
+    const int row = i / (D / 2), cc = (i - row * (D / 2)) * 2;
+    // rows [0,16) for block 0, [16,48) for block 1, [48,96) block 2, [96,160) block 3
+    const int I = row < 16 ? 0 : row < 48 ? 1 : row < 96 ? 2 : 3;
+    const int base = 8 * I * (I + 1);
+    const int r = row - base, r0 = 16 * I;
+    float k2[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float e = fminf(sG[r0 * LDG + cc + t] - sG[r * LDG + cc + t], 120.f);
+      k2[t] = to_f<T>(sk[r * LDK + cc + t]) * rk[r] * exp2f(e);
+    }
+    *reinterpret_cast<uint32_t*>(sKs + row * LDK + cc) = pack2<T>(k2[0], k2[1]);
+  }
+  for (int i = tid; i < 4 * D; i += NTH) {
+    const int bI = i / D, cc = i - bI * D;
+    const float rng = sG[(16 * bI) * LDG + cc] - sG[(16 * bI + 15) * LDG + cc];
+    if (!(rng <= kSafeLog2Range)) sFlag[0] = 0;
+  }
+  __syncthreads();
+  const bool safe = sFlag[0] != 0;
+  {
+    // X products: rows of block I = wr
+    const int I = wr, jmax = safe ? 16 * (I + 1) : 16 * I;
+    if (jmax > 0) {
+      const T* KsI = sKs + 8 * I * (I + 1) * LDK;
+      float tq[1][NTO][4], tk[1][NTO][4];
+      acc_zero(tq);
+      acc_zero(tk);
+      warp_mma16<1, NTO, true, false>(tq, sDAqk, LDC, 16 * I, KsI, LDK, wc * DQ, jmax);
+      warp_mma16<1, NTO, true, false>(tk, sDAkk, LDC, 16 * I, KsI, LDK, wc * DQ, jmax);
+#pragma unroll
+      for (int j = 0; j < NTO; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
+          const float f = exp2f(sG[r * LDG + cl] - sG[(16 * I) * LDG + cl]);
+          const float xq = scale * tq[0][j][e] * f, xk = tk[0][j][e] * f;
+          const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
+          const float kb = to_f<T>(sb[r * LDK + cl]) * to_f<T>(sk[r * LDK + cl]) * rk[r];
+          dq[0][j][e] += xq;
+          dkb[0][j][e] += xk;
+          dG[0][j][e] += qn * xq + kb * xk;
+        }
+    }
+    // Y products: columns of block J = wr, from block rows I >= J
+    const int J = wr;
+    for (int I = J; I < 4; ++I) {
+      if (I == J && !safe) continue;
+      float ty[1][NTO][4];
+      acc_zero(ty);
+      warp_mma16<1, NTO, false, false>(ty, sDAqk + 16 * I * LDC, LDC, 16 * J,
+                                       sQs + 16 * I * LDK, LDK, wc * DQ, 16);
+      warp_mma16<1, NTO, false, false>(ty, sDAkk + 16 * I * LDC, LDC, 16 * J,
+                                       sKBs + 16 * I * LDK, LDK, wc * DQ, 16);
+#pragma unroll
+      for (int j = 0; j < NTO; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
+          const float ee = exp2f(fminf(sG[(16 * I) * LDG + cl] - sG[r * LDG + cl], 120.f));
+          const float y = ty[0][j][e] * ee;
+          const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
+          dkn[0][j][e] += y;
+          dG[0][j][e] -= kn * y;
+        }
+    }
+    if (!safe) {
+      // exact diagonal block, off-diagonal pairs only
+#pragma unroll
+      for (int j = 0; j < NTO; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
+          const float Gr = sG[r * LDG + cl];
+          const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
+          const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
+          const float kb = to_f<T>(sb[r * LDK + cl]) * kn;
+          float xq = 0.f, xk = 0.f, y = 0.f;
+          for (int ii = 16 * wr; ii < 16 * wr + 16; ++ii) {
+            if (ii < r) {
+              const float ex = exp2f(Gr - sG[ii * LDG + cl]) * to_f<T>(sk[ii * LDK + cl]) * rk[ii];
+              xq += scale * to_f<T>(sDAqk[r * LDC + ii]) * ex;
+              xk += to_f<T>(sDAkk[r * LDC + ii]) * ex;
+            } else if (ii > r) {
+              const float ex = exp2f(sG[ii * LDG + cl] - Gr);
+              const float qi = to_f<T>(sq[ii * LDK + cl]) * rq[ii];
+              const float kbi = to_f<T>(sb[ii * LDK + cl]) * to_f<T>(sk[ii * LDK + cl]) * rk[ii];
+              y += (scale * to_f<T>(sDAqk[ii * LDC + r]) * qi +
+                    to_f<T>(sDAkk[ii * LDC + r]) * kbi) * ex;
+            }
+          }
+          dq[0][j][e] += xq;
+          dkb[0][j][e] += xk;
+          dkn[0][j][e] += y;
+          dG[0][j][e] += qn * xq + kb * xk - kn * y;
+        }
+    }
+  }
+  __syncthreads();  // score tiles are dead; W becomes the scan area
+
+  // ---- dg = suffix scan of dG + prefix scan of the Kd terms -----------------
+  float* sdG = reinterpret_cast<float*>(W + L::kdG);
+  float* sX = reinterpret_cast<float*>(W + L::kX);
+  float* sTmp = reinterpret_cast<float*>(W + L::kTmp);
+#pragma unroll
+  for (int j = 0; j < NTO; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
+      float v = dG[0][j][e];
+      if (r == len - 1) v += dgl[cl] * exp2f(sG[(kChunk - 1) * LDG + cl]);
+      sdG[r * LDG + cl] = v;
+      if (r + 1 < kChunk) sX[(r + 1) * LDG + cl] = X[j][e];
+    }
+  for (int i = tid; i < D; i += NTH) sX[i] = 0.f;
+  __syncthreads();
+  col_scan64_t<D, NTH, true>(sdG, LDG, sTmp);
+  col_scan64_t<D, NTH, false>(sX, LDG, sTmp);
+  float* gdg = a.dg + offk;
+  for (int i = tid; i < kChunk * D; i += NTH) {
+    const int r = i / D, cc = i - r * D;
+    if (r < len && cc < K) gdg[(int64_t)r * ldk + cc] = sdG[r * LDG + cc] + sX[r * LDG + cc];
+  }
+
+  // ---- db, dk, dq with the l2norm backward -------------------------------------
+  T* gdq = reinterpret_cast<T*>(a.dq) + offk;
+  T* gdk = reinterpret_cast<T*>(a.dk) + offk;
+  T* gdb = reinterpret_cast<T*>(a.db) + offk;
+  float pq[2] = {0.f, 0.f}, pk[2] = {0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < NTO; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int hf = e >> 1;
+      const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
+      const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
+      const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
+      const float bb = to_f<T>(sb[r * LDK + cl]);
+      const float dgn = scale * sDiag[r];
+      const float dkbv = dkb[0][j][e];
+      dq[0][j][e] += dgn * kn;
+      dkn[0][j][e] += dkbv * bb + dgn * qn;
+      dkb[0][j][e] = dkbv * kn;  // db
+      pq[hf] += qn * dq[0][j][e];
+      pk[hf] += kn * dkn[0][j][e];
+    }
+  if (a.l2norm) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      pq[hf] += __shfl_xor_sync(0xffffffffu, pq[hf], 1);
+      pq[hf] += __shfl_xor_sync(0xffffffffu, pq[hf], 2);
+      pk[hf] += __shfl_xor_sync(0xffffffffu, pk[hf], 1);
+      pk[hf] += __shfl_xor_sync(0xffffffffu, pk[hf], 2);
+    }
+    if (tig == 0) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        pdq[wc * 64 + 16 * wr + gid + 8 * hf] = pq[hf];
+        pdk[wc * 64 + 16 * wr + gid + 8 * hf] = pk[hf];
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < NTO; ++j)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
+      if (r >= len || cl >= K) continue;
+      float oq[2], ok[2];
+      const float dotq = a.l2norm ? pdq[r] + pdq[64 + r] + pdq[128 + r] + pdq[192 + r] : 0.f;
+      const float dotk = a.l2norm ? pdk[r] + pdk[64 + r] + pdk[128 + r] + pdk[192 + r] : 0.f;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int e = 2 * hf + t;
+        float vq = dq[0][j][e], vk = dkn[0][j][e];
+        if (a.l2norm) {
+          const float qn = to_f<T>(sq[r * LDK + cl + t]) * rq[r];
+          const float kn = to_f<T>(sk[r * LDK + cl + t]) * rk[r];
+          vq = (vq - qn * dotq) * rq[r];
+          vk = (vk - kn * dotk) * rk[r];
+        }
+        oq[t] = vq;
+        ok[t] = vk;
+      }
+      *reinterpret_cast<uint32_t*>(gdq + (int64_t)r * ldk + cl) = pack2<T>(oq[0], oq[1]);
+      *reinterpret_cast<uint32_t*>(gdk + (int64_t)r * ldk + cl) = pack2<T>(ok[0], ok[1]);
+      *reinterpret_cast<uint32_t*>(gdb + (int64_t)r * ldk + cl) =
+          pack2<T>(dkb[0][j][2 * hf], dkb[0][j][2 * hf + 1]);
+    }
+}
+
+template <typename T, int D>
+cudaError_t launch_bwd_intra16(const BwdIntraArgs& a, cudaStream_t st) {
+  auto kern = k_bwd_intra16<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)Bwd16Layout<D>::bytes);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.seqs.n_chunks, a.H);
+  kern<<<grid, kThreadsB16, Bwd16Layout<D>::bytes, st>>>(a);
+  return cudaGetLastError();
+}
+
+template cudaError_t launch_bwd_intra16<__nv_bfloat16, 64>(const BwdIntraArgs&, cudaStream_t);
+template cudaError_t launch_bwd_intra16<__nv_bfloat16, 128>(const BwdIntraArgs&, cudaStream_t);
+template cudaError_t launch_bwd_intra16<__half, 64>(const BwdIntraArgs&, cudaStream_t);
+template cudaError_t launch_bwd_intra16<__half, 128>(const BwdIntraArgs&, cudaStream_t);
+
+}  // namespace gdn2

@@ -150,6 +150,53 @@ __device__ __forceinline__ void cp_tile16(T* s, int lds, const T* g, int64_t ldg
   }
 }
 
+// Copy a ROWS x COLS fp32 tile (16-byte aligned rows) asynchronously; rows
+// >= nrows / cols >= ncols (ncols a multiple of 4) are zero-filled.
+template <int ROWS, int COLS, int NTH>
+__device__ __forceinline__ void cp_tile32(float* s, int lds, const float* g, int64_t ldg,
+                                          int nrows, int ncols) {
+  constexpr int CPR = COLS / 4;
+  constexpr int TOTAL = ROWS * CPR;
+#pragma unroll
+  for (int it = 0; it < (TOTAL + NTH - 1) / NTH; ++it) {
+    const int idx = threadIdx.x + it * NTH;
+    if (idx < TOTAL) {
+      const int r = idx / CPR, c = (idx - r * CPR) * 4;
+      const bool ok = r < nrows && c < ncols;
+      cp_async16(s + r * lds + c, ok ? (const void*)(g + (int64_t)r * ldg + c) : (const void*)g,
+                 ok);
+    }
+  }
+}
+
+// Segmented inclusive scan down the 64 rows of an fp32 tile with NC columns
+// (row stride lds) using NTH threads: prefix sums (REV false) or suffix sums
+// (REV true).  `tmp` holds NTH floats.  Contains __syncthreads().
+template <int NC, int NTH, bool REV>
+__device__ __forceinline__ void col_scan64_t(float* s, int lds, float* tmp) {
+  constexpr int NSEG = NTH / NC;
+  constexpr int RPS = kChunk / NSEG;
+  static_assert(NSEG * NC == NTH && RPS * NSEG == kChunk, "scan shape");
+  const int col = threadIdx.x % NC, seg = threadIdx.x / NC;
+  float run = 0.f;
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) {
+    const int r = REV ? (kChunk - 1 - (seg * RPS + i)) : (seg * RPS + i);
+    run += s[r * lds + col];
+    s[r * lds + col] = run;
+  }
+  tmp[seg * NC + col] = run;
+  __syncthreads();
+  float off = 0.f;
+  for (int j = 0; j < seg; ++j) off += tmp[j * NC + col];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) {
+    const int r = REV ? (kChunk - 1 - (seg * RPS + i)) : (seg * RPS + i);
+    s[r * lds + col] += off;
+  }
+  __syncthreads();
+}
+
 // Same for an fp32 vector of n floats (n a multiple of 4), zero beyond n.
 template <int N, int NTH>
 __device__ __forceinline__ void cp_vec32(float* s, const float* g, int n) {
