@@ -19,6 +19,7 @@ template <typename T, int D> cudaError_t launch_recurrent(const RecArgs&, cudaSt
 template <typename T, int D, int BV> cudaError_t launch_fwd_state16(const FwdStateArgs&, cudaStream_t);
 template <typename T, int D, int BV> cudaError_t launch_bwd_state16(const BwdStateArgs&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_intra16(const BwdIntraArgs&, cudaStream_t);
+template <typename T, int D> cudaError_t launch_fwd_intra16(const FwdIntraArgs&, cudaStream_t);
 }  // namespace gdn2
 
 using namespace gdn2;
@@ -137,17 +138,19 @@ cudaError_t run_state16(const Args& a, int bucket, int cols, int n_seqs, int H, 
   return launch_state16<T, 128, 64>(a, st);
 }
 
+// The ldmatrix / m16n8k16 kernels serve bf16 with head sizes that are
+// multiples of 8.  Their decay-scaled operands span up to 2^+-100, which
+// bf16 represents (8-bit exponent) and fp16 does not, so fp16 problems stay
+// on the fp32-staged kernels.
 bool use16(const gdn2_chunk_problem* p) {
-  return p->dtype != GDN2_DTYPE_F32 && (p->K % 8) == 0 && (p->V % 8) == 0;
+  return p->dtype == GDN2_DTYPE_BF16 && (p->K % 8) == 0 && (p->V % 8) == 0;
 }
 
 cudaError_t fwd_state_dispatch(const gdn2_chunk_problem* p, const FwdStateArgs& a, cudaStream_t st) {
   const int bucket = head_bucket(p->K, p->V);
   if (use16(p)) {
     const int cols = a.prescan ? p->V + p->K : p->V;
-    if (p->dtype == GDN2_DTYPE_BF16)
-      return run_state16<__nv_bfloat16>(a, bucket, cols, p->seqs.n_seqs, p->H, st);
-    return run_state16<__half>(a, bucket, cols, p->seqs.n_seqs, p->H, st);
+    return run_state16<__nv_bfloat16>(a, bucket, cols, p->seqs.n_seqs, p->H, st);
   }
   return dispatch<RunFwdState>(p->dtype, bucket, a, st);
 }
@@ -155,21 +158,25 @@ cudaError_t fwd_state_dispatch(const gdn2_chunk_problem* p, const FwdStateArgs& 
 cudaError_t bwd_state_dispatch(const gdn2_chunk_problem* p, const BwdStateArgs& a, cudaStream_t st) {
   const int bucket = head_bucket(p->K, p->V);
   if (use16(p)) {
-    if (p->dtype == GDN2_DTYPE_BF16)
-      return run_state16<__nv_bfloat16>(a, bucket, p->V, p->seqs.n_seqs, p->H, st);
-    return run_state16<__half>(a, bucket, p->V, p->seqs.n_seqs, p->H, st);
+    return run_state16<__nv_bfloat16>(a, bucket, p->V, p->seqs.n_seqs, p->H, st);
   }
   return dispatch<RunBwdState>(p->dtype, bucket, a, st);
+}
+
+cudaError_t fwd_intra_dispatch(const gdn2_chunk_problem* p, const FwdIntraArgs& a, cudaStream_t st) {
+  const int bucket = head_bucket(p->K, p->V);
+  if (use16(p)) {
+    return bucket == 64 ? launch_fwd_intra16<__nv_bfloat16, 64>(a, st)
+                        : launch_fwd_intra16<__nv_bfloat16, 128>(a, st);
+  }
+  return dispatch<RunFwdIntra>(p->dtype, bucket, a, st);
 }
 
 cudaError_t bwd_intra_dispatch(const gdn2_chunk_problem* p, const BwdIntraArgs& a, cudaStream_t st) {
   const int bucket = head_bucket(p->K, p->V);
   if (use16(p)) {
-    if (p->dtype == GDN2_DTYPE_BF16)
-      return bucket == 64 ? launch_bwd_intra16<__nv_bfloat16, 64>(a, st)
-                          : launch_bwd_intra16<__nv_bfloat16, 128>(a, st);
-    return bucket == 64 ? launch_bwd_intra16<__half, 64>(a, st)
-                        : launch_bwd_intra16<__half, 128>(a, st);
+    return bucket == 64 ? launch_bwd_intra16<__nv_bfloat16, 64>(a, st)
+                        : launch_bwd_intra16<__nv_bfloat16, 128>(a, st);
   }
   return dispatch<RunBwdIntra>(p->dtype, bucket, a, st);
 }
@@ -286,7 +293,7 @@ int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
   a.saved = static_cast<unsigned char*>(saved);
   a.L = L;
-  cudaError_t e = dispatch<RunFwdIntra>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  cudaError_t e = fwd_intra_dispatch(p, a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_fwd_intra");
 }
 

@@ -1,4 +1,4 @@
-// bwd16.cu -- per-chunk GDN-2 gradients for 16-bit inputs (bf16 / fp16).
+// bwd16.cu -- per-chunk GDN-2 gradients for bf16 inputs.
 //
 // One CTA of 16 warps per (chunk, head).  Same mathematics as k_bwd_intra
 // (chunk_bwd.cu), organised so that almost nothing waits on memory:
@@ -557,7 +557,5 @@ cudaError_t launch_bwd_intra16(const BwdIntraArgs& a, cudaStream_t st) {
 
 template cudaError_t launch_bwd_intra16<__nv_bfloat16, 64>(const BwdIntraArgs&, cudaStream_t);
 template cudaError_t launch_bwd_intra16<__nv_bfloat16, 128>(const BwdIntraArgs&, cudaStream_t);
-template cudaError_t launch_bwd_intra16<__half, 64>(const BwdIntraArgs&, cudaStream_t);
-template cudaError_t launch_bwd_intra16<__half, 128>(const BwdIntraArgs&, cudaStream_t);
 
 }  // namespace gdn2

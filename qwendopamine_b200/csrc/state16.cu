@@ -1,4 +1,4 @@
-// state16.cu -- inter-chunk state passes for 16-bit inputs (bf16 / fp16).
+// state16.cu -- inter-chunk state passes for bf16 inputs.
 //
 // One CTA of 16 warps per (sequence, head, BV-column value tile) walks the
 // sequence's chunks in order (forward) or in reverse (backward).  The fp32
@@ -415,8 +415,5 @@ cudaError_t launch_bwd_state16(const BwdStateArgs& a, cudaStream_t st) {
 GDN2_INST_STATE16(__nv_bfloat16, 64, 64)
 GDN2_INST_STATE16(__nv_bfloat16, 128, 64)
 GDN2_INST_STATE16(__nv_bfloat16, 128, 128)
-GDN2_INST_STATE16(__half, 64, 64)
-GDN2_INST_STATE16(__half, 128, 64)
-GDN2_INST_STATE16(__half, 128, 128)
 
 }  // namespace gdn2
