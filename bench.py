@@ -385,6 +385,77 @@ def run_profile_case(args, local):
                                        "steps": args.warmup + args.steps}}))
 
 
+SP_T, SP_H = 262144, 32
+
+
+def run_config4(args, world, rank, local, mode):
+    """B=1 T=262144 H=32 K=V=128 bf16 forward+backward.
+
+    mode "sp": every rank owns T/world contiguous tokens (whole chunks); the
+    span maps cross GPUs through one NCCL all-gather per direction
+    (chunk_gdn2_cp).  mode "heads": every rank owns H/world heads of the whole
+    sequence, no communication.  Total work is fixed: strong scaling.
+    """
+    from qwendopamine_b200 import chunk_gdn2
+    from qwendopamine_b200.gdn2_ops.cp import chunk_gdn2_cp, gather_span_maps
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if mode == "sp":
+        Tl, Hl = SP_T // world, SP_H
+    else:
+        Tl, Hl = SP_T, SP_H // world
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    bf = torch.bfloat16
+    q = F.normalize(torch.randn(1, Tl, Hl, K, device=dev, generator=gen), dim=-1).to(bf)
+    k = F.normalize(torch.randn(1, Tl, Hl, K, device=dev, generator=gen), dim=-1).to(bf)
+    v = torch.randn(1, Tl, Hl, V, device=dev, generator=gen).to(bf)
+    beta = torch.sigmoid(torch.randn(1, Tl, Hl, device=dev, generator=gen))
+    gs = F.logsigmoid(torch.randn(1, Tl, Hl, device=dev, generator=gen) + 3.0)
+    g = gs[..., None].expand(1, Tl, Hl, K).contiguous()
+    b = beta[..., None].expand(1, Tl, Hl, K).to(bf).contiguous()
+    w = beta[..., None].expand(1, Tl, Hl, V).to(bf).contiguous()
+    do = torch.randn(1, Tl, Hl, V, device=dev, generator=gen).to(bf)
+    leaves = [t.requires_grad_() for t in (q, k, v, g, b, w)]
+    gather = (lambda t: gather_span_maps(t, None)) if world > 1 else (lambda t: t[None])
+
+    def step():
+        if mode == "sp":
+            o, _ = chunk_gdn2_cp(*leaves, rank=rank, world=world, gather=gather)
+        else:
+            o, _ = chunk_gdn2(*leaves, use_qk_l2norm_in_kernel=True)
+        torch.autograd.grad(o, leaves, do)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    if rank != 0:
+        return
+    launches = (8 if world > 1 else 6) if mode == "sp" else 4
+    print(json.dumps({
+        "metric": "gdn2 fwd+bwd tokens/s (BASELINE config 4)",
+        "value": round(SP_T / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; config-0 recipe at config-4 shapes)",
+        "config": {"workload": f"config4 {mode}", "batch": 1, "seq_len": SP_T, "heads": SP_H,
+                   "head_k": K, "head_v": V, "chunk": C,
+                   "parallelism": (f"sequence-parallel x{world} (NCCL all-gather of span maps)"
+                                   if mode == "sp" else f"head-sharded x{world}, no collective")},
+        "gpu_launches": launches * args.steps,
+    }), flush=True)
+
+
 def run_decode(dev, lib, N):
     """Config 2: one in-place recurrent step over B=256 sequences per call."""
     gen = torch.Generator(device=dev).manual_seed(7)
@@ -520,6 +591,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--workload", choices=("config1", "sp", "heads"), default="config1",
+                    help="config1 (headline), or config 4 sequence-parallel / head-sharded")
     ap.add_argument("--profile", action="store_true",
                     help="small ncu case: config-1 phases at --batch, nothing else")
     ap.add_argument("--batch", type=int, default=2, help="batch of the --profile case")
@@ -536,7 +609,10 @@ def main(argv=None):
         return
     world, rank, local = dist_setup()
     try:
-        run_b200(args, world, rank, local)
+        if args.workload == "config1":
+            run_b200(args, world, rank, local)
+        else:
+            run_config4(args, world, rank, local, args.workload)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -1,0 +1,77 @@
+"""Worker for tests/test_gpu_cp_nccl.py: one process per GPU under torchrun.
+
+Every rank builds the same seeded sequence, runs its span through
+chunk_gdn2_cp with the NCCL all-gather, and checks outputs, the final state
+and all gradients of its span against chunk_gdn2 run on the whole sequence on
+its own GPU.  Exit status 0 means every rank agreed.
+"""
+
+import datetime
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from qwendopamine_b200 import chunk_gdn2  # noqa: E402
+from qwendopamine_b200.gdn2_ops.cp import chunk_gdn2_cp, gather_span_maps  # noqa: E402
+
+
+def rel(a, b):
+    return float((a.double() - b.double()).norm() / b.double().norm().clamp_min(1e-30))
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", local)
+    B, H, K, V = 1, 4, 128, 128
+    T = 256 * world
+    gen = torch.Generator(device=dev).manual_seed(0)
+    bf = torch.bfloat16
+    q = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf)
+    k = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf)
+    v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    g = -torch.rand(B, T, H, K, device=dev, generator=gen)
+    b = torch.sigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)).to(bf)
+    w = torch.sigmoid(torch.randn(B, T, H, V, device=dev, generator=gen)).to(bf)
+    h0 = torch.randn(B, H, K, V, device=dev, generator=gen) * 0.1
+    do = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    dht = torch.randn(B, H, K, V, device=dev, generator=gen)
+    names = ("q", "k", "v", "g", "b", "w")
+    full = {n: t.clone().requires_grad_() for n, t in zip(names, (q, k, v, g, b, w))}
+    hf = h0.clone().requires_grad_()
+    o_ref, ht_ref = chunk_gdn2(*(full[n] for n in names), initial_state=hf,
+                               output_final_state=True, use_qk_l2norm_in_kernel=True)
+    ((o_ref.float() * do.float()).sum() + (ht_ref * dht).sum()).backward()
+    span = T // world
+    a, e = rank * span, (rank + 1) * span
+    loc = {n: t[:, a:e].detach().clone().requires_grad_() for n, t in zip(names, (q, k, v, g, b, w))}
+    hl = h0.clone().requires_grad_()
+    o, ht = chunk_gdn2_cp(*(loc[n] for n in names), rank=rank, world=world,
+                          gather=lambda t: gather_span_maps(t, None), initial_state=hl)
+    loss = (o.float() * do[:, a:e].float()).sum()
+    if rank == world - 1:
+        loss = loss + (ht * dht).sum()
+    loss.backward()
+    errs = {"o": rel(o, o_ref[:, a:e])}
+    if rank == world - 1:
+        errs["ht"] = rel(ht, ht_ref)
+    for n in names:
+        errs["d" + n] = rel(loc[n].grad, full[n].grad[:, a:e])
+    if rank == 0:
+        errs["dh0"] = rel(hl.grad, hf.grad)
+    bad = {n: x for n, x in errs.items() if not x < 2e-2}
+    print(f"rank {rank}: " + " ".join(f"{n}={x:.1e}" for n, x in errs.items()), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(1 if bad else 0)
+
+
+if __name__ == "__main__":
+    main()
