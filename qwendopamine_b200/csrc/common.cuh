@@ -265,6 +265,16 @@ struct ChunkPos {
   int len;       // valid rows (1..64)
 };
 
+// Position of chunk c of a sequence whose first token row is bos, whose end
+// row is eos and whose first chunk is c0 (no table lookups).
+__device__ __forceinline__ ChunkPos chunk_pos_in_seq(int64_t bos, int64_t eos, int c0, int c) {
+  ChunkPos p;
+  p.row0 = bos + (int64_t)(c - c0) * kChunk;
+  const int64_t rem = eos - p.row0;
+  p.len = rem < kChunk ? (int)rem : kChunk;
+  return p;
+}
+
 __device__ __forceinline__ ChunkPos chunk_pos(const Seqs& s, int c) {
   int n = s.cseq[c];
   int j = c - s.coff[n];

@@ -87,7 +87,7 @@ template <int MT, int NT, bool A_KMAJOR, bool B_KMAJOR, typename T>
 __device__ __forceinline__ void warp_mma16(float (&acc)[MT][NT][4], const T* A, int lda, int m0,
                                            const T* B, int ldb, int n0, int kd) {
   static_assert(NT % 2 == 0, "NT must be even");
-#pragma unroll 2
+#pragma unroll
   for (int k0 = 0; k0 < kd; k0 += 16) {
     uint32_t a[MT][4];
 #pragma unroll

@@ -50,6 +50,7 @@ __global__ void __launch_bounds__(kThreads16, 1) k_fwd_state16(FwdStateArgs a) {
   const int v0 = blockIdx.x * BV;
   const int Vx = a.prescan ? V + K : V;
   const int c_begin = a.seqs.coff[n], c_end = a.seqs.coff[n + 1];
+  const int64_t bos = a.seqs.cu[n], eos = a.seqs.cu[n + 1];
   const size_t tileK = (size_t)kChunk * K, tileV = (size_t)kChunk * V;
   const int64_t ldo = (int64_t)H * V;
   const int nU = max(0, min(BV, V - v0));  // U columns present in this tile
@@ -180,7 +181,7 @@ __global__ void __launch_bounds__(kThreads16, 1) k_fwd_state16(FwdStateArgs a) {
     __syncthreads();  // sVN visible
     // o = Qg h + Aqk VN
     if (!a.prescan) {
-      const ChunkPos cp = chunk_pos(a.seqs, c);
+      const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
       float acc[1][NT1][4];
       acc_zero(acc);
       warp_mma16<1, NT1, true, false>(acc, sQg, LDK, wm1, sH, LDV, wn1, D);
@@ -245,6 +246,7 @@ __global__ void __launch_bounds__(kThreads16, 1) k_bwd_state16(BwdStateArgs a) {
   const int nh = blockIdx.y, n = nh / H, h = nh - n * H;
   const int v0 = blockIdx.x * BV;
   const int c_begin = a.seqs.coff[n], c_end = a.seqs.coff[n + 1];
+  const int64_t bos = a.seqs.cu[n], eos = a.seqs.cu[n + 1];
   const size_t tileK = (size_t)kChunk * K, tileV = (size_t)kChunk * V;
   const int64_t ldo = (int64_t)H * V;
   const int nV = max(0, min(BV, V - v0));
@@ -254,7 +256,7 @@ __global__ void __launch_bounds__(kThreads16, 1) k_bwd_state16(BwdStateArgs a) {
   auto tiles = [&](int slot) { return base + slot * S::buf; };
   auto issue = [&](int c, int slot) {
     const size_t ch = (size_t)c * H + h;
-    const ChunkPos cp = chunk_pos(a.seqs, c);
+    const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
     T* sW = tiles(slot);
     T* sKd = sW + kChunk * LDK;
     T* sQg = sKd + kChunk * LDK;

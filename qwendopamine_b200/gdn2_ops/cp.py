@@ -162,6 +162,13 @@ def chunk_gdn2_cp(q, k, v, g, b, w, *, rank: int, world: int, gather: Gather,
         initial_state = initial_state.contiguous()
     if scale is None:
         scale = k.shape[-1] ** -0.5
+    if world == 1:
+        # a single span: no span maps to exchange
+        from .chunk_gdn2 import chunk_gdn2
+
+        return chunk_gdn2(q, k, v, g, b, w, scale=scale, initial_state=initial_state,
+                          output_final_state=True,
+                          use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
     dt = q.dtype
     q, k, v, b, w = (x.to(dt).contiguous() for x in (q, k, v, b, w))
     g = g.float().contiguous()
