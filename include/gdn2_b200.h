@@ -213,6 +213,16 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all,
                   int32_t forward, const float* init, float* state_out,
                   void* stream);
 
+/* Device-side fault bits.  Kernels that wait on asynchronous copies or on
+ * tensor-core completion bound every wait in time (about one second); a wait
+ * that runs out makes the kernel release its tensor memory, return without
+ * finishing, and set bit 0 of a per-device fault word.  gdn2_fault_status
+ * synchronises `stream` (the default stream when NULL), returns the fault
+ * word of the current device (0 = no fault) and resets it when `clear` is
+ * nonzero; a negative return is a CUDA error.  No counterpart in the
+ * reference, whose kernels contain no bounded waits. */
+int gdn2_fault_status(void* stream, int32_t clear);
+
 #ifdef __cplusplus
 }
 #endif

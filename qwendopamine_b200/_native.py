@@ -40,6 +40,7 @@ EXPORTS = (
     "gdn2_cp_fwd_prescan",
     "gdn2_cp_bwd_prescan",
     "gdn2_cp_merge",
+    "gdn2_fault_status",
 )
 
 
@@ -122,6 +123,7 @@ def _declare(lib):
         "gdn2_cp_fwd_prescan": ([cp, v, c_size_t, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_cp_bwd_prescan": ([cp, v, c_size_t, v, v, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_cp_merge": ([cp, v, v, c_int32, c_int32, c_int32, v, v, v], ctypes.c_int),
+        "gdn2_fault_status": ([v, c_int32], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -157,6 +159,17 @@ def check(status: int, fn: str) -> None:
     if status == ERR_UNSUPPORTED:
         raise NotImplementedError(text)
     raise GDN2Error(status, text)
+
+
+def fault_status(device=None, clear: bool = True) -> int:
+    """Synchronise ``device``'s current stream and return the device fault
+    word (nonzero when a kernel's bounded wait ran out); reset it if ``clear``."""
+    lib = load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    r = lib.gdn2_fault_status(stream_of(dev), 1 if clear else 0)
+    if r < 0:
+        raise GDN2Error(ERR_CUDA, f"gdn2_fault_status: {lib.gdn2_last_error().decode()}")
+    return r
 
 
 def ptr(t):

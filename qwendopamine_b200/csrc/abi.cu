@@ -20,6 +20,9 @@ template <typename T, int D, int BV> cudaError_t launch_fwd_state16(const FwdSta
 template <typename T, int D, int BV> cudaError_t launch_bwd_state16(const BwdStateArgs&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_intra16(const BwdIntraArgs&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_fwd_intra16(const FwdIntraArgs&, cudaStream_t);
+bool fwd_state_tc_ok(const FwdStateArgs&, int dtype_bf16);
+cudaError_t launch_fwd_state_tc(const FwdStateArgs&, cudaStream_t);
+cudaError_t read_fault_bits(unsigned int* bits, bool clear);
 }  // namespace gdn2
 
 using namespace gdn2;
@@ -146,8 +149,11 @@ bool use16(const gdn2_chunk_problem* p) {
   return p->dtype == GDN2_DTYPE_BF16 && (p->K % 8) == 0 && (p->V % 8) == 0;
 }
 
+// bf16 with K = V = 128 (the pre-scan excepted) runs the forward state pass
+// on tcgen05 / TMEM / TMA (state_tc.cu).
 cudaError_t fwd_state_dispatch(const gdn2_chunk_problem* p, const FwdStateArgs& a, cudaStream_t st) {
   const int bucket = head_bucket(p->K, p->V);
+  if (fwd_state_tc_ok(a, p->dtype == GDN2_DTYPE_BF16)) return launch_fwd_state_tc(a, st);
   if (use16(p)) {
     const int cols = a.prescan ? p->V + p->K : p->V;
     return run_state16<__nv_bfloat16>(a, bucket, cols, p->seqs.n_seqs, p->H, st);
@@ -503,6 +509,21 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all, const float*
                                                         world, forward, init, state_out);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_merge");
+}
+
+int gdn2_fault_status(void* stream, int32_t clear) {
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    cuda_fail(e, "gdn2_fault_status");
+    return -1;
+  }
+  unsigned int bits = 0;
+  e = read_fault_bits(&bits, clear != 0);
+  if (e != cudaSuccess) {
+    cuda_fail(e, "gdn2_fault_status");
+    return -1;
+  }
+  return (int)(bits & 0x7fffffffu);
 }
 
 }  // extern "C"

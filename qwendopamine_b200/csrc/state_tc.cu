@@ -1,0 +1,428 @@
+// state_tc.cu -- forward inter-chunk state pass on the 5th-generation tensor
+// cores (tcgen05 + TMEM + TMA), bf16 inputs, K = V = 128.
+//
+// One CTA of 8 warps per (sequence, head) walks the sequence's chunks in
+// order.  Tensor memory (256 columns x 128 lanes, fp32) holds
+//   cols [0,128)   the state h           (lane = key row k, column = value v)
+//   cols [128,192) VN^T = h^T W^T, then U^T - that  (lane = v, column = token)
+//   cols [192,256) o^T = h^T Qg^T + VN^T Aqk^T      (lane = v, column = token)
+// so the state never leaves the SM between chunks.  Per chunk:
+//   1. one thread issues  VN^T = h^T W^T  and  o^T = h^T Qg^T  (A = bf16 h in
+//      shared memory, MN-major; B = W / Qg tiles, K-major), commits;
+//   2. all warps read VN^T, form VN = U - W h, write bf16 VN^T (K-major) to
+//      shared memory and VN to the saved buffer;
+//   3. one thread issues  o^T += VN^T Aqk^T  and  h += Kd^T VN  (A = Kd tile,
+//      MN-major; B = VN^T, K-major) onto the state already scaled by 2^G_last;
+//   4. all warps store o, read the new state, write its bf16 copy (operand of
+//      the next chunk and the saved checkpoint) and scale it by the next
+//      chunk's 2^G_last in place.
+// The per-chunk tiles (W, Qg, Kd, Aqk: 128-byte swizzled; U: plain; gl: bulk)
+// arrive by TMA into a two-slot ring, two chunks ahead.  Every wait on an
+// mbarrier is bounded in time; a wait that runs out marks the CTA aborted,
+// all warps leave the chunk loop together, in-flight copies are waited for
+// (bounded), the tensor memory is freed and a fault bit is set in
+// g_gdn2_fault for gdn2_fault_status() to report.
+//
+// Same recurrence and rounding points as k_fwd_state16 (state16.cu): fp32
+// state, bf16 copies of h and VN as product operands, fp32 accumulation.
+#include <cuda.h>
+
+#include "chunk_args.cuh"
+#include "tc.cuh"
+
+namespace gdn2 {
+
+__device__ unsigned int g_gdn2_fault;
+
+namespace {
+
+constexpr int kTcThreads = 256;
+constexpr uint32_t kBox = 8192;  // one 64-row x 128-byte TMA box
+// per-chunk slot (bytes, 1024-aligned pieces)
+constexpr uint32_t kOffW = 0;
+constexpr uint32_t kOffQg = 2 * kBox;
+constexpr uint32_t kOffKd = 4 * kBox;
+constexpr uint32_t kOffAqk = 6 * kBox;
+constexpr uint32_t kOffU = 7 * kBox;  // [64][128] bf16, unswizzled
+constexpr uint32_t kOffGl = 9 * kBox; // [128] fp32
+constexpr uint32_t kGlBytes = 128 * 4;
+constexpr uint32_t kSlotBytes = 9 * kBox + 1024;
+constexpr uint32_t kTxBytes = 9 * kBox + kGlBytes;
+// persistent operands
+constexpr uint32_t kOffH = 2 * kSlotBytes;     // bf16 h [k][v], MN-major SW128 (32 KB)
+constexpr uint32_t kOffVN = kOffH + 4 * kBox;  // bf16 VN^T [v][t], K-major SW128 (16 KB)
+constexpr uint32_t kOffBar = kOffVN + 2 * kBox;
+constexpr uint32_t kSmemBytes = kOffBar + 64 + 1024;  // + alignment slack
+
+constexpr uint32_t kColH = 0, kColVN = 128, kColO = 192, kTmemCols = 256;
+
+// instruction descriptors
+constexpr uint32_t kIdHW = tc::idesc_bf16(128, 64, 1, 0);    // h^T W^T, h^T Qg^T
+constexpr uint32_t kIdVA = tc::idesc_bf16(128, 64, 0, 0);    // VN^T Aqk^T
+constexpr uint32_t kIdKV = tc::idesc_bf16(128, 128, 1, 0);   // Kd^T VN
+
+__device__ __forceinline__ uint64_t desc_k(const void* p) {  // K-major, 128B swizzle
+  return tc::sdesc(p, 16, 1024, tc::kSwizzle128);
+}
+__device__ __forceinline__ uint64_t desc_mn(const void* p, uint32_t mn_stride) {  // MN-major
+  return tc::sdesc(p, mn_stride, 1024, tc::kSwizzle128);
+}
+
+__device__ __forceinline__ void st_shared_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(smem_u32(p)), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    k_fwd_state_tc(FwdStateArgs a, const __grid_constant__ CUtensorMap mW,
+                   const __grid_constant__ CUtensorMap mQg, const __grid_constant__ CUtensorMap mKd,
+                   const __grid_constant__ CUtensorMap mAqk, const __grid_constant__ CUtensorMap mU) {
+  using T = __nv_bfloat16;
+  constexpr int K = 128, V = 128;
+  extern __shared__ unsigned char smraw[];
+  unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);  // [2]
+  uint64_t* mma1 = full + 2;
+  uint64_t* mma2 = full + 3;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(full + 4);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+  unsigned char* sH = sm + kOffH;
+  unsigned char* sVN = sm + kOffVN;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int row = quad * 32 + lane;  // the TMEM lane this thread reads
+  const int H = a.H;
+  const int nh = blockIdx.x, n = nh / H, h = nh - n * H;
+  const int c_begin = a.seqs.coff[n], c_end = a.seqs.coff[n + 1];
+  const int64_t bos = a.seqs.cu[n], eos = a.seqs.cu[n + 1];
+  const int64_t ldo = (int64_t)H * V;
+  const float* h0 = a.h0 ? a.h0 + (int64_t)nh * K * V : nullptr;
+  float* ht = a.ht ? a.ht + (int64_t)nh * K * V : nullptr;
+
+  if (c_begin >= c_end) {  // empty sequence: the state passes through
+    if (ht)
+      for (int i = tid; i < K * V; i += kTcThreads) ht[i] = h0 ? h0[i] : 0.f;
+    return;
+  }
+
+  if (tid == 0) {
+    tc::mbar_init(&full[0], 1);
+    tc::mbar_init(&full[1], 1);
+    tc::mbar_init(mma1, 1);
+    tc::mbar_init(mma2, 1);
+    *sAbort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(sTmem, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const uint32_t tlane = tmem + ((uint32_t)(quad * 32) << 16);
+
+  // ---- producer (thread 0) --------------------------------------------------
+  int next_issue = c_begin;  // meaningful in thread 0 only
+  int mma1_commits = 0, mma2_commits = 0;
+  auto issue = [&](int c) {
+    const int slot = (c - c_begin) & 1;
+    unsigned char* p = sm + slot * kSlotBytes;
+    const size_t ch = (size_t)c * H + h;
+    const int y = (int)(ch * kChunk);
+    tc::mbar_expect_tx(&full[slot], kTxBytes);
+    tc::tma_load_2d(p + kOffW, &mW, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kOffW + kBox, &mW, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kOffQg, &mQg, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kOffQg + kBox, &mQg, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kOffKd, &mKd, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kOffKd + kBox, &mKd, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kOffAqk, &mAqk, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kOffU, &mU, 0, y, &full[slot]);
+    tc::bulk_load(p + kOffGl, a.saved + a.L.gl + ch * K * sizeof(float), kGlBytes, &full[slot]);
+    next_issue = c + 1;
+  };
+  if (tid == 0) {
+    issue(c_begin);
+    if (c_begin + 1 < c_end) issue(c_begin + 1);
+  }
+
+  // bf16 copy of this thread's 64 state values (row k = `row`, columns
+  // 64*half ..) into the MN-major operand and into checkpoint `c`.
+  auto emit_state = [&](const float (&s)[64], int c) {
+    T* gh = reinterpret_cast<T*>(a.saved + a.L.h) + ((size_t)c * H + h) * (size_t)K * V +
+            (size_t)row * V + 64 * half;
+    unsigned char* srow = sH + half * (4 * kBox / 2) + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t p0 = pack2<T>(s[8 * q + 0], s[8 * q + 1]);
+      const uint32_t p1 = pack2<T>(s[8 * q + 2], s[8 * q + 3]);
+      const uint32_t p2 = pack2<T>(s[8 * q + 4], s[8 * q + 5]);
+      const uint32_t p3 = pack2<T>(s[8 * q + 6], s[8 * q + 7]);
+      st_shared_v4(srow + ((q ^ (row & 7)) << 4), p0, p1, p2, p3);
+      *reinterpret_cast<uint4*>(gh + 8 * q) = make_uint4(p0, p1, p2, p3);
+    }
+  };
+  auto scale_store = [&](float (&s)[64], int slot) {
+    const float gl = reinterpret_cast<const float*>(sm + slot * kSlotBytes + kOffGl)[row];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) s[i] *= gl;
+    float lo[32], hi[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      lo[i] = s[i];
+      hi[i] = s[32 + i];
+    }
+    tc::tmem_st32(tlane + kColH + 64 * half, lo);
+    tc::tmem_st32(tlane + kColH + 64 * half + 32, hi);
+  };
+
+  // ---- initial state ----------------------------------------------------------
+  {
+    const bool ok = tc::warp_wait(&full[0], 0);
+    if (ok) {
+      float s[64];
+      if (h0) {
+        const float4* src = reinterpret_cast<const float4*>(h0 + (size_t)row * V + 64 * half);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 x = src[i];
+          s[4 * i] = x.x;
+          s[4 * i + 1] = x.y;
+          s[4 * i + 2] = x.z;
+          s[4 * i + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[i] = 0.f;
+      }
+      emit_state(s, c_begin);
+      scale_store(s, 0);
+    } else if (lane == 0) {
+      *sAbort = 1;
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+  }
+
+  int c = c_begin;
+  if (!*sAbort) {
+    for (; c < c_end; ++c) {
+      const int i = c - c_begin, slot = i & 1;
+      unsigned char* p = sm + slot * kSlotBytes;
+      const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
+
+      // 1. VN^T = h^T W^T,  o^T = h^T Qg^T
+      if (tid == 0) {
+        if (!tc::mbar_wait(&full[slot], par_full)) {
+          *sAbort = 1;
+        } else {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::umma_bf16(tmem + kColVN, desc_mn(sH + j * 2048, 4 * kBox / 2),
+                          desc_k(p + kOffW + (j >> 2) * kBox + (j & 3) * 32), kIdHW, j > 0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::umma_bf16(tmem + kColO, desc_mn(sH + j * 2048, 4 * kBox / 2),
+                          desc_k(p + kOffQg + (j >> 2) * kBox + (j & 3) * 32), kIdHW, j > 0);
+          tc::umma_commit(mma1);
+          ++mma1_commits;
+        }
+      }
+      // 2. VN = U - W h
+      {
+        bool ok = tc::warp_wait(mma1, par_mma);
+        if (ok) ok = tc::warp_wait(&full[slot], par_full);
+        if (ok) {
+          tc::tc_fence_after();
+          float x[32];
+          tc::tmem_ld32(tlane + kColVN + 32 * half, x);
+          const T* sU = reinterpret_cast<const T*>(p + kOffU);
+          T* gvn = reinterpret_cast<T*>(a.saved + a.L.vn) + ((size_t)c * H + h) * kChunk * V + row;
+          unsigned char* vrow = sVN + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int t0 = 32 * half + 8 * q + 2 * e;
+              const float y0 = to_f<T>(sU[t0 * V + row]) - x[8 * q + 2 * e];
+              const float y1 = to_f<T>(sU[(t0 + 1) * V + row]) - x[8 * q + 2 * e + 1];
+              pk[e] = pack2<T>(y0, y1);
+              const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&pk[e]);
+              gvn[(size_t)t0 * V] = b2.x;
+              gvn[(size_t)(t0 + 1) * V] = b2.y;
+            }
+            st_shared_v4(vrow + (((4 * half + q) ^ (row & 7)) << 4), pk[0], pk[1], pk[2], pk[3]);
+          }
+        } else if (lane == 0) {
+          *sAbort = 1;
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+      // 3. o^T += VN^T Aqk^T,  h += Kd^T VN
+      if (tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_bf16(tmem + kColO, desc_k(sVN + j * 32), desc_k(p + kOffAqk + j * 32), kIdVA, 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_bf16(tmem + kColH, desc_mn(p + kOffKd + j * 2048, kBox), desc_k(sVN + j * 32),
+                        kIdKV, 1);
+        tc::umma_commit(mma2);
+        ++mma2_commits;
+      }
+      // 4. o out; new state -> bf16 operand + checkpoint; scale by next 2^G_last
+      {
+        const bool has_next = c + 1 < c_end;
+        bool ok = tc::warp_wait(mma2, par_mma);
+        if (ok && has_next) ok = tc::warp_wait(&full[slot ^ 1], ((i + 1) >> 1) & 1);
+        if (ok) {
+          tc::tc_fence_after();
+          const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
+          float x[32];
+          tc::tmem_ld32(tlane + kColO + 32 * half, x);
+          T* go = reinterpret_cast<T*>(a.o) + cp.row0 * ldo + (int64_t)h * V + row;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int t = 32 * half + e;
+            if (t < cp.len) go[(int64_t)t * ldo] = from_f<T>(x[e]);
+          }
+          float s[64];
+          {
+            float lo[32], hi[32];
+            tc::tmem_ld32(tlane + kColH + 64 * half, lo);
+            tc::tmem_ld32(tlane + kColH + 64 * half + 32, hi);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              s[e] = lo[e];
+              s[32 + e] = hi[e];
+            }
+          }
+          if (has_next) {
+            emit_state(s, c + 1);
+            scale_store(s, slot ^ 1);
+          } else if (ht) {
+            float4* dst = reinterpret_cast<float4*>(ht + (size_t)row * V + 64 * half);
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              dst[e] = make_float4(s[4 * e], s[4 * e + 1], s[4 * e + 2], s[4 * e + 3]);
+          }
+        } else if (lane == 0) {
+          *sAbort = 1;
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+      if (tid == 0 && c + 2 < c_end) issue(c + 2);
+    }
+  }
+
+  // ---- teardown ---------------------------------------------------------------
+  const bool aborted = *sAbort != 0;
+  if (aborted && tid == 0) {
+    // let copies and products already in flight finish before the shared
+    // and tensor memory they target is released (each wait bounded)
+    for (int j = c; j < next_issue; ++j) {
+      const int ij = j - c_begin;
+      tc::mbar_wait(&full[ij & 1], (ij >> 1) & 1);
+    }
+    if (mma1_commits > 0) tc::mbar_wait(mma1, (mma1_commits - 1) & 1);
+    if (mma2_commits > 0) tc::mbar_wait(mma2, (mma2_commits - 1) & 1);
+    atomicOr(&g_gdn2_fault, 1u);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- host side -----------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D bf16 map over `rows` rows of `inner` elements; box = box_x x 64 rows.
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_x,
+              bool swizzle) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_x, 64};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+// True when k_fwd_state_tc can serve the problem (bf16, K = V = 128, no
+// pre-scan, 16-byte aligned saved buffer, tile rows addressable by TMA).
+bool fwd_state_tc_ok(const FwdStateArgs& a, int dtype_bf16) {
+  if (!dtype_bf16 || a.K != 128 || a.V != 128 || a.prescan || !a.o) return false;
+  if ((reinterpret_cast<uintptr_t>(a.saved) & 15) != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(a.h0) & 15) != 0 || (reinterpret_cast<uintptr_t>(a.ht) & 15) != 0)
+    return false;
+  if ((int64_t)a.seqs.n_chunks * a.H * kChunk >= (int64_t)1 << 31) return false;
+  return encode_fn() != nullptr;
+}
+
+cudaError_t launch_fwd_state_tc(const FwdStateArgs& a, cudaStream_t st) {
+  const uint64_t rows = (uint64_t)a.seqs.n_chunks * a.H * kChunk;
+  CUtensorMap mW, mQg, mKd, mAqk, mU;
+  if (!make_map(&mW, a.saved + a.L.w, 128, rows, 64, true) ||
+      !make_map(&mQg, a.saved + a.L.qg, 128, rows, 64, true) ||
+      !make_map(&mKd, a.saved + a.L.kd, 128, rows, 64, true) ||
+      !make_map(&mAqk, a.saved + a.L.aqk, 64, rows, 64, true) ||
+      !make_map(&mU, a.saved + a.L.u, 128, rows, 128, false))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(k_fwd_state_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int grid = a.seqs.n_seqs * a.H;
+  if (grid == 0) return cudaSuccess;
+  k_fwd_state_tc<<<grid, kTcThreads, kSmemBytes, st>>>(a, mW, mQg, mKd, mAqk, mU);
+  return cudaGetLastError();
+}
+
+// Fault bits recorded by bounded waits that ran out (device of the current
+// context); `clear` resets them.
+cudaError_t read_fault_bits(unsigned int* bits, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(bits, g_gdn2_fault, sizeof(unsigned int));
+  if (e != cudaSuccess || !clear) return e;
+  const unsigned int zero = 0;
+  return cudaMemcpyToSymbol(g_gdn2_fault, &zero, sizeof(unsigned int));
+}
+
+}  // namespace gdn2

@@ -1,0 +1,90 @@
+"""Forward state pass on tcgen05 / TMEM / TMA (bf16, K = V = 128).
+
+The chunkwise forward routes bf16 problems with K = V = 128 through
+k_fwd_state_tc.  These cases check its outputs, final states and per-chunk
+checkpoints against the float64 oracle (rel-L2 <= 2e-2, the bf16 tolerance),
+on ragged and empty packed sequences and on a 64-chunk sequence that cycles
+the two-slot copy ring many times, and check that no bounded wait ran out.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from gdn2_testutil import TOL, make_inputs, np_, rel, to_dev
+from oracle import gdn2_oracle as O
+
+pytestmark = pytest.mark.gpu
+NAMES = ("q", "k", "v", "g", "b", "w")
+BF = torch.bfloat16
+
+
+def _fault_word():
+    from qwendopamine_b200 import _native as N
+
+    return N.fault_status(clear=True)
+
+
+def test_tc_state_varlen_ragged_and_empty(cuda_device):
+    from qwendopamine_b200 import chunk_gdn2
+
+    _fault_word()
+    cu = [0, 1, 64, 129, 129, 300, 364, 500]
+    N = len(cu) - 1
+    H = 3
+    d = make_inputs(1, cu[-1], H, 128, 128, seed=41, dtype=BF, h0=False)
+    gen = torch.Generator().manual_seed(8)
+    h0 = torch.randn(N, H, 128, 128, generator=gen) * 0.1
+    x = to_dev(d, cuda_device, BF)
+    o, ht = chunk_gdn2(x["q"], x["k"], x["v"], x["g"], x["b"], x["w"],
+                       initial_state=h0.to(cuda_device), output_final_state=True,
+                       use_qk_l2norm_in_kernel=True,
+                       cu_seqlens=torch.tensor(cu, device=cuda_device))
+    ro, rh = O.recurrent_fwd_varlen(*np_(d, NAMES), cu, h0.numpy(), norm_mode="fla")
+    assert rel(o, ro) < TOL[BF]
+    assert rel(ht, rh) < TOL[BF]
+    # the empty sequence passes its initial state through unchanged
+    assert torch.equal(ht[3].cpu(), h0[3])
+    assert _fault_word() == 0
+
+
+def test_tc_state_long_sequence_and_checkpoints(cuda_device):
+    from qwendopamine_b200 import chunk_gdn2
+
+    _fault_word()
+    B, T, H = 1, 4096, 2
+    d = make_inputs(B, T, H, 128, 128, seed=42, dtype=BF, decay="baseline")
+    x = to_dev(d, cuda_device, BF)
+    with torch.inference_mode():
+        o, ht, h = chunk_gdn2(x["q"], x["k"], x["v"], x["g"], x["b"], x["w"],
+                              initial_state=x["h0"], output_final_state=True,
+                              use_qk_l2norm_in_kernel=True, return_intermediate_states=True)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < TOL[BF]
+    assert rel(ht, rh) < TOL[BF]
+    # checkpoint j is the state entering chunk j: the recurrence's state after
+    # 64*j tokens (j = 0: the initial state)
+    hs = h.float().cpu().numpy()  # [B, NT, H, K, V]
+    for j in (0, 1, 17, 63):
+        if j == 0:
+            ref = d["h0"].numpy()
+        else:
+            _, ref = O.recurrent_fwd(*(a[:, :64 * j] for a in np_(d, NAMES)),
+                                     d["h0"].numpy(), norm_mode="fla")
+        assert rel(hs[:, j], ref) < TOL[BF], j
+    assert _fault_word() == 0
+
+
+@pytest.mark.parametrize("B,T,H", [(8, 256, 16), (1, 65, 1), (20, 64, 9)])
+def test_tc_state_batched_shapes(cuda_device, B, T, H):
+    _fault_word()
+    d = make_inputs(B, T, H, 128, 128, seed=B * 7 + T + H, dtype=BF)
+    from qwendopamine_b200 import chunk_gdn2
+
+    x = to_dev(d, cuda_device, BF)
+    o, ht = chunk_gdn2(x["q"], x["k"], x["v"], x["g"], x["b"], x["w"], initial_state=x["h0"],
+                       output_final_state=True, use_qk_l2norm_in_kernel=True)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < TOL[BF]
+    assert rel(ht, rh) < TOL[BF]
+    assert _fault_word() == 0
