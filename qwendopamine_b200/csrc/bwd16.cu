@@ -29,6 +29,7 @@ struct Bwd16Layout {
   static constexpr int LDG = D + 4;      // fp32 64 x D tiles
   static constexpr int LDC = kChunk + 8; // 16-bit 64 x 64 tiles
   static constexpr int LDS = 32 + 8;     // 16-bit value slices
+  static constexpr int LDT = kChunk + 8; // 16-bit VN^T slice [32][64]
   // persistent region (bytes)
   static constexpr int oQ = 0;
   static constexpr int oK = oQ + kChunk * LDK * 2;
@@ -71,12 +72,13 @@ struct Bwd16Layout {
   static constexpr size_t bytes = (size_t)oW + W;
   static_assert(kT2 + kChunk * LDC * 2 <= kEnd || kT2 + kChunk * LDC * 2 <= W, "layout");
   static_assert(oW % 16 == 0 && slot % 16 == 0, "alignment");
+  static_assert(32 * LDT <= kChunk * LDS, "VN^T slice fits its region");
 };
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) {
   using L = Bwd16Layout<D>;
-  constexpr int LDK = L::LDK, LDG = L::LDG, LDC = L::LDC, LDS = L::LDS;
+  constexpr int LDK = L::LDK, LDG = L::LDG, LDC = L::LDC, LDS = L::LDS, LDT = L::LDT;
   constexpr int NTH = kThreadsB16;
   constexpr int DQ = D / 4;    // owner tile width
   constexpr int NTO = DQ / 8;  // n8 fragments per owner tile
@@ -123,7 +125,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     cp_tile16<T, D, 32, NTH>(slotp(s, L::vH), LDS, gh + v0, V, K, nv);
     cp_tile16<T, D, 32, NTH>(slotp(s, L::vDH), LDS, gdh + v0, V, K, nv);
     cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vDO), LDS, gdo + v0, ldv, len, nv);
-    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vVN), LDS, gvn + v0, V, kChunk, nv);
+    cp_tile16<T, 32, kChunk, NTH>(slotp(s, L::vVN), LDT, gvn + (size_t)v0 * kChunk, kChunk, nv,
+                                  kChunk);
     cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vDVN), LDS, gdvn + v0, V, kChunk, nv);
     cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vV), LDS, gv + v0, ldv, len, nv);
     cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vWg), LDS, gw + v0, ldv, len, nv);
@@ -207,9 +210,9 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     }
     __syncthreads();
     warp_mma16<1, NTO, true, true>(accQ, dos, LDS, 16 * wr, hs, LDS, wc * DQ, 32);
-    warp_mma16<1, NTO, true, true>(accKd, vns, LDS, 16 * wr, dhs, LDS, wc * DQ, 32);
+    warp_mma16<1, NTO, false, true>(accKd, vns, LDT, 16 * wr, dhs, LDS, wc * DQ, 32);
     warp_mma16<1, NTO, true, true>(accW, dvns, LDS, 16 * wr, hs, LDS, wc * DQ, 32);
-    warp_mma16<1, 2, true, true>(accAqk, dos, LDS, 16 * wr, vns, LDS, 16 * wc, 32);
+    warp_mma16<1, 2, true, false>(accAqk, dos, LDS, 16 * wr, vns, LDT, 16 * wc, 32);
     warp_mma16<1, 2, true, true>(accDA, dvns, LDS, 16 * wr, sZ, LDS, 16 * wc, 32);
     if (warp < 8) {
       float accZ[1][2][4];

@@ -289,7 +289,10 @@ __device__ __forceinline__ ChunkPos chunk_pos(const Seqs& s, int c) {
 
 // Layout of the buffer the forward fills for the backward.  Per (chunk, head):
 //   Qg, Kd, W : [64][K]  (T)   scale*q*2^G,  k*2^(G_last-G),  A (b*k*2^G)
-//   U, VN     : [64][V]  (T)   A (w*v),  U - W h
+//   U         : [64][V]  (T)   A (w*v)
+//   VN        : [64][V]  (T)   U - W h;  stored transposed, [V][64], by the
+//                              bf16 tensor-core path (state16.cu,
+//                              state_tc.cu -> bwd16.cu)
 //   Aqk, A    : [64][64] (T)   causal scores (scale folded in), (I+Akk)^-1
 //   gl        : [K]      (f32) 2^G_last
 //   h         : [K][V]   (T)   state entering the chunk

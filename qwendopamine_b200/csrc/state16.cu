@@ -174,8 +174,10 @@ __global__ void __launch_bounds__(kThreads16, 1) k_fwd_state16(FwdStateArgs a) {
           const float x0 = u0 - acc[0][j][2 * hf], x1 = u1 - acc[0][j][2 * hf + 1];
           const uint32_t pk = pack2<T>(x0, x1);
           *reinterpret_cast<uint32_t*>(sVN + r * LDV + cl) = pk;
-          if (!a.prescan && v0 + cl < V)
-            *reinterpret_cast<uint32_t*>(gVN + (size_t)r * V + v0 + cl) = pk;
+          if (!a.prescan && v0 + cl < V) {  // saved VN^T: [V][64]
+            gVN[(size_t)(v0 + cl) * kChunk + r] = from_f<T>(x0);
+            if (v0 + cl + 1 < V) gVN[(size_t)(v0 + cl + 1) * kChunk + r] = from_f<T>(x1);
+          }
         }
     }
     __syncthreads();  // sVN visible

@@ -8,14 +8,19 @@
 //   cols [192,256) o^T = h^T Qg^T + VN^T Aqk^T      (lane = v, column = token)
 // so the state never leaves the SM between chunks.  Per chunk:
 //   1. one thread issues  VN^T = h^T W^T  and  o^T = h^T Qg^T  (A = bf16 h in
-//      shared memory, MN-major; B = W / Qg tiles, K-major), commits;
-//   2. all warps read VN^T, form VN = U - W h, write bf16 VN^T (K-major) to
-//      shared memory and VN to the saved buffer;
+//      shared memory, MN-major; B = W / Qg tiles, K-major), commits; the
+//      other threads meanwhile copy the chunk's checkpoint and the previous
+//      chunk's o out of their shared-memory staging tiles;
+//   2. all warps read VN^T, form VN = U - W h and write bf16 VN^T (K-major)
+//      to shared memory;
 //   3. one thread issues  o^T += VN^T Aqk^T  and  h += Kd^T VN  (A = Kd tile,
 //      MN-major; B = VN^T, K-major) onto the state already scaled by 2^G_last;
-//   4. all warps store o, read the new state, write its bf16 copy (operand of
-//      the next chunk and the saved checkpoint) and scale it by the next
-//      chunk's 2^G_last in place.
+//      meanwhile VN^T is copied to the saved buffer;
+//   4. all warps stage o, read the new state, write its bf16 copy (operand of
+//      the next chunk and its checkpoint) and scale it in place by the next
+//      chunk's 2^G_last.
+// Every global store is a 16-byte vector and each warp instruction writes
+// 512 contiguous bytes (a transposing store from TMEM lanes would scatter).
 // The per-chunk tiles (W, Qg, Kd, Aqk: 128-byte swizzled; U: plain; gl: bulk)
 // arrive by TMA into a two-slot ring, two chunks ahead.  Every wait on an
 // mbarrier is bounded in time; a wait that runs out marks the CTA aborted,
@@ -48,10 +53,12 @@ constexpr uint32_t kOffGl = 9 * kBox; // [128] fp32
 constexpr uint32_t kGlBytes = 128 * 4;
 constexpr uint32_t kSlotBytes = 9 * kBox + 1024;
 constexpr uint32_t kTxBytes = 9 * kBox + kGlBytes;
-// persistent operands
+// persistent operands and staging
 constexpr uint32_t kOffH = 2 * kSlotBytes;     // bf16 h [k][v], MN-major SW128 (32 KB)
+constexpr uint32_t kHalfH = 2 * kBox;          // v-halves of it are 16 KB apart
 constexpr uint32_t kOffVN = kOffH + 4 * kBox;  // bf16 VN^T [v][t], K-major SW128 (16 KB)
-constexpr uint32_t kOffBar = kOffVN + 2 * kBox;
+constexpr uint32_t kOffO = kOffVN + 2 * kBox;  // bf16 o [t][v], row-major (16 KB)
+constexpr uint32_t kOffBar = kOffO + 2 * kBox;
 constexpr uint32_t kSmemBytes = kOffBar + 64 + 1024;  // + alignment slack
 
 constexpr uint32_t kColH = 0, kColVN = 128, kColO = 192, kTmemCols = 256;
@@ -68,11 +75,17 @@ __device__ __forceinline__ uint64_t desc_mn(const void* p, uint32_t mn_stride) {
   return tc::sdesc(p, mn_stride, 1024, tc::kSwizzle128);
 }
 
-__device__ __forceinline__ void st_shared_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
-                                             uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(smem_u32(p)), "r"(a), "r"(b),
-               "r"(c), "r"(d)
+__device__ __forceinline__ void st_shared_v4(void* p, uint4 x) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};\n" ::"r"(smem_u32(p)), "r"(x.x), "r"(x.y),
+               "r"(x.z), "r"(x.w)
                : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(const void* p) {
+  uint4 x;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w)
+               : "r"(smem_u32(p)));
+  return x;
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -90,6 +103,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
   unsigned char* sH = sm + kOffH;
   unsigned char* sVN = sm + kOffVN;
+  unsigned char* sO = sm + kOffO;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2;
@@ -152,33 +166,64 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   // bf16 copy of this thread's 64 state values (row k = `row`, columns
-  // 64*half ..) into the MN-major operand and into checkpoint `c`.
-  auto emit_state = [&](const float (&s)[64], int c) {
-    T* gh = reinterpret_cast<T*>(a.saved + a.L.h) + ((size_t)c * H + h) * (size_t)K * V +
-            (size_t)row * V + 64 * half;
-    unsigned char* srow = sH + half * (4 * kBox / 2) + (row >> 3) * 1024 + (row & 7) * 128;
+  // 64*half ..) into the MN-major operand tile.
+  auto emit_state = [&](const float (&s)[64]) {
+    unsigned char* srow = sH + half * kHalfH + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const uint32_t p0 = pack2<T>(s[8 * q + 0], s[8 * q + 1]);
-      const uint32_t p1 = pack2<T>(s[8 * q + 2], s[8 * q + 3]);
-      const uint32_t p2 = pack2<T>(s[8 * q + 4], s[8 * q + 5]);
-      const uint32_t p3 = pack2<T>(s[8 * q + 6], s[8 * q + 7]);
-      st_shared_v4(srow + ((q ^ (row & 7)) << 4), p0, p1, p2, p3);
-      *reinterpret_cast<uint4*>(gh + 8 * q) = make_uint4(p0, p1, p2, p3);
+      uint4 x;
+      x.x = pack2<T>(s[8 * q + 0], s[8 * q + 1]);
+      x.y = pack2<T>(s[8 * q + 2], s[8 * q + 3]);
+      x.z = pack2<T>(s[8 * q + 4], s[8 * q + 5]);
+      x.w = pack2<T>(s[8 * q + 6], s[8 * q + 7]);
+      st_shared_v4(srow + ((q ^ (row & 7)) << 4), x);
     }
   };
   auto scale_store = [&](float (&s)[64], int slot) {
     const float gl = reinterpret_cast<const float*>(sm + slot * kSlotBytes + kOffGl)[row];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) s[i] *= gl;
     float lo[32], hi[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      lo[i] = s[i];
-      hi[i] = s[32 + i];
+      lo[i] = s[i] * gl;
+      hi[i] = s[32 + i] * gl;
     }
     tc::tmem_st32(tlane + kColH + 64 * half, lo);
     tc::tmem_st32(tlane + kColH + 64 * half + 32, hi);
+  };
+  // Coalesced copies out of the staging tiles (all 256 threads; each warp
+  // instruction moves 512 contiguous bytes).
+  auto copy_ckpt = [&](int c) {  // sH -> checkpoint of chunk c, [K][V]
+    T* gh = reinterpret_cast<T*>(a.saved + a.L.h) + ((size_t)c * H + h) * (size_t)K * V;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int k = idx >> 4, ci = idx & 15;
+      const uint4 x = ld_shared_v4(sH + (ci >> 3) * kHalfH + (k >> 3) * 1024 + (k & 7) * 128 +
+                                   (((ci & 7) ^ (k & 7)) << 4));
+      *reinterpret_cast<uint4*>(gh + (size_t)k * V + 8 * ci) = x;
+    }
+  };
+  auto copy_vn = [&](int c) {  // sVN -> VN^T of chunk c, [V][64]
+    T* gv = reinterpret_cast<T*>(a.saved + a.L.vn) + ((size_t)c * H + h) * (size_t)kChunk * V;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int v = idx >> 3, ci = idx & 7;
+      const uint4 x = ld_shared_v4(sVN + (v >> 3) * 1024 + (v & 7) * 128 + ((ci ^ (v & 7)) << 4));
+      *reinterpret_cast<uint4*>(gv + (size_t)v * kChunk + 8 * ci) = x;
+    }
+  };
+  auto copy_o = [&](int c) {  // sO -> output rows of chunk c
+    const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
+    T* go = reinterpret_cast<T*>(a.o) + cp.row0 * ldo + (int64_t)h * V;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int t = idx >> 4, ci = idx & 15;
+      if (t < cp.len)
+        *reinterpret_cast<uint4*>(go + (int64_t)t * ldo + 8 * ci) =
+            ld_shared_v4(sO + t * (V * 2) + ci * 16);
+    }
   };
 
   // ---- initial state ----------------------------------------------------------
@@ -200,7 +245,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int i = 0; i < 64; ++i) s[i] = 0.f;
       }
-      emit_state(s, c_begin);
+      emit_state(s);
       scale_store(s, 0);
     } else if (lane == 0) {
       *sAbort = 1;
@@ -217,7 +262,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       unsigned char* p = sm + slot * kSlotBytes;
       const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
 
-      // 1. VN^T = h^T W^T,  o^T = h^T Qg^T
+      // 1. VN^T = h^T W^T,  o^T = h^T Qg^T;  meanwhile the checkpoint of
+      //    chunk c and the previous chunk's o leave through the copy units.
       if (tid == 0) {
         if (!tc::mbar_wait(&full[slot], par_full)) {
           *sAbort = 1;
@@ -225,41 +271,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            tc::umma_bf16(tmem + kColVN, desc_mn(sH + j * 2048, 4 * kBox / 2),
+            tc::umma_bf16(tmem + kColVN, desc_mn(sH + j * 2048, kHalfH),
                           desc_k(p + kOffW + (j >> 2) * kBox + (j & 3) * 32), kIdHW, j > 0);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            tc::umma_bf16(tmem + kColO, desc_mn(sH + j * 2048, 4 * kBox / 2),
+            tc::umma_bf16(tmem + kColO, desc_mn(sH + j * 2048, kHalfH),
                           desc_k(p + kOffQg + (j >> 2) * kBox + (j & 3) * 32), kIdHW, j > 0);
           tc::umma_commit(mma1);
           ++mma1_commits;
         }
       }
-      // 2. VN = U - W h
+      copy_ckpt(c);
+      if (c > c_begin) copy_o(c - 1);
+      // 2. VN = U - W h  -> bf16 VN^T operand tile
       {
         bool ok = tc::warp_wait(mma1, par_mma);
         if (ok) ok = tc::warp_wait(&full[slot], par_full);
         if (ok) {
           tc::tc_fence_after();
-          float x[32];
+          uint32_t x[32];
           tc::tmem_ld32(tlane + kColVN + 32 * half, x);
-          const T* sU = reinterpret_cast<const T*>(p + kOffU);
-          T* gvn = reinterpret_cast<T*>(a.saved + a.L.vn) + ((size_t)c * H + h) * kChunk * V + row;
+          const T* sU = reinterpret_cast<const T*>(p + kOffU) + row;
+          float u[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) u[e] = to_f<T>(sU[(32 * half + e) * V]);
+          tc::tmem_wait_ld();
           unsigned char* vrow = sVN + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int t0 = 32 * half + 8 * q + 2 * e;
-              const float y0 = to_f<T>(sU[t0 * V + row]) - x[8 * q + 2 * e];
-              const float y1 = to_f<T>(sU[(t0 + 1) * V + row]) - x[8 * q + 2 * e + 1];
-              pk[e] = pack2<T>(y0, y1);
-              const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&pk[e]);
-              gvn[(size_t)t0 * V] = b2.x;
-              gvn[(size_t)(t0 + 1) * V] = b2.y;
-            }
-            st_shared_v4(vrow + (((4 * half + q) ^ (row & 7)) << 4), pk[0], pk[1], pk[2], pk[3]);
+            uint4 y;
+            y.x = pack2<T>(u[8 * q + 0] - __uint_as_float(x[8 * q + 0]),
+                           u[8 * q + 1] - __uint_as_float(x[8 * q + 1]));
+            y.y = pack2<T>(u[8 * q + 2] - __uint_as_float(x[8 * q + 2]),
+                           u[8 * q + 3] - __uint_as_float(x[8 * q + 3]));
+            y.z = pack2<T>(u[8 * q + 4] - __uint_as_float(x[8 * q + 4]),
+                           u[8 * q + 5] - __uint_as_float(x[8 * q + 5]));
+            y.w = pack2<T>(u[8 * q + 6] - __uint_as_float(x[8 * q + 6]),
+                           u[8 * q + 7] - __uint_as_float(x[8 * q + 7]));
+            st_shared_v4(vrow + (((4 * half + q) ^ (row & 7)) << 4), y);
           }
         } else if (lane == 0) {
           *sAbort = 1;
@@ -269,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncthreads();
         if (*sAbort) break;
       }
-      // 3. o^T += VN^T Aqk^T,  h += Kd^T VN
+      // 3. o^T += VN^T Aqk^T,  h += Kd^T VN;  meanwhile VN^T leaves.
       if (tid == 0) {
         tc::tc_fence_after();
 #pragma unroll
@@ -282,35 +331,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc::umma_commit(mma2);
         ++mma2_commits;
       }
-      // 4. o out; new state -> bf16 operand + checkpoint; scale by next 2^G_last
+      copy_vn(c);
+      // 4. o -> staging; new state -> bf16 operand tile (the next checkpoint),
+      //    scaled in place by the next chunk's 2^G_last
       {
         const bool has_next = c + 1 < c_end;
         bool ok = tc::warp_wait(mma2, par_mma);
         if (ok && has_next) ok = tc::warp_wait(&full[slot ^ 1], ((i + 1) >> 1) & 1);
         if (ok) {
           tc::tc_fence_after();
-          const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
-          float x[32];
-          tc::tmem_ld32(tlane + kColO + 32 * half, x);
-          T* go = reinterpret_cast<T*>(a.o) + cp.row0 * ldo + (int64_t)h * V + row;
+          {
+            uint32_t x[32];
+            tc::tmem_ld32(tlane + kColO + 32 * half, x);
+            tc::tmem_wait_ld();
+            T* orow = reinterpret_cast<T*>(sO) + row;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int t = 32 * half + e;
-            if (t < cp.len) go[(int64_t)t * ldo] = from_f<T>(x[e]);
+            for (int e = 0; e < 32; ++e) orow[(32 * half + e) * V] = from_f<T>(__uint_as_float(x[e]));
           }
           float s[64];
           {
-            float lo[32], hi[32];
+            uint32_t lo[32], hi[32];
             tc::tmem_ld32(tlane + kColH + 64 * half, lo);
             tc::tmem_ld32(tlane + kColH + 64 * half + 32, hi);
+            tc::tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-              s[e] = lo[e];
-              s[32 + e] = hi[e];
+              s[e] = __uint_as_float(lo[e]);
+              s[32 + e] = __uint_as_float(hi[e]);
             }
           }
           if (has_next) {
-            emit_state(s, c + 1);
+            emit_state(s);
             scale_store(s, slot ^ 1);
           } else if (ht) {
             float4* dst = reinterpret_cast<float4*>(ht + (size_t)row * V + 64 * half);
@@ -332,6 +383,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   // ---- teardown ---------------------------------------------------------------
   const bool aborted = *sAbort != 0;
+  if (!aborted) copy_o(c_end - 1);
   if (aborted && tid == 0) {
     // let copies and products already in flight finish before the shared
     // and tensor memory they target is released (each wait bounded)

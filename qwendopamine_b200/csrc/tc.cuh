@@ -106,9 +106,9 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // 32 consecutive fp32 columns of this thread's TMEM lane (warp w reads lanes
-// 32*(w%4) .. +31; taddr must carry that lane base in bits 16+).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// 32*(w%4) .. +31; taddr must carry that lane base in bits 16+).  The values
+// are valid only after tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -119,9 +119,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
@@ -182,16 +182,6 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
                    smem_u32(bar))
                : "memory");
-}
-
-// Byte offset of element (row, k) inside a K-major tile stored as 128-byte
-// swizzled atoms: k-blocks of 64 elements (kb_stride bytes apart), 8-row
-// atoms of 1024 bytes, 16-byte chunks XOR-ed with the row within the atom.
-__device__ __forceinline__ uint32_t sw128_offset(int row, int k, uint32_t kb_stride) {
-  const int kb = k >> 6, kk = k & 63;
-  const int chunk = (kk >> 3) ^ (row & 7);
-  return (uint32_t)kb * kb_stride + (uint32_t)(row >> 3) * 1024u + (uint32_t)(row & 7) * 128u +
-         (uint32_t)chunk * 16u + (uint32_t)(kk & 7) * 2u;
 }
 
 }  // namespace tc
