@@ -1,16 +1,20 @@
 // fwd16.cu -- intra-chunk forward solve for bf16 inputs.
 //
 // One CTA of 16 warps per (chunk, head); same mathematics as k_fwd_intra
-// (chunk_fwd.cu).  One cp.async round trip brings q, k, b, v, w and g.  The
-// score operands are 16-bit tiles scaled by relative decays:
-//   Qs[r] = scale q_n[r] 2^(G_r - G_b(r)),  KBs[r] = (b k_n)[r] 2^(G_r - G_b(r))
-// (b(r): first row of r's 16-row block) and, for block row I, the keys
-//   Ks_I[i] = k_n[i] 2^(G_16I - G_i), i < 16(I+1),
-// so that every product of an Aqk / Akk block carries exactly
-// 2^(G_r - G_i).  The scores, W = A E and U = A Z are mma.sync m16n8k16
-// products from ldmatrix fragments; the unit-lower inverse A = (I+Akk)^-1
-// stays in fp32.  Diagonal blocks whose 16-row decay range exceeds the fp32
-// exponent budget are recomputed elementwise.
+// (chunk_fwd.cu).  One cp.async round trip brings q, k, b, v, w and g.  After
+// the decay scan and the row norms, a single elementwise pass writes Qg and
+// Kd, forms E = b k_n 2^G and Z = v w in place of w and v, and builds the
+// 16-bit score operands with per-16-row-block references
+//   Qs[r] = scale q_n[r] 2^(G_r - G_b(r)),  KBs[r] = (b k_n)[r] 2^(G_r - G_b(r)),
+//   Kb[i] = k_n[i] 2^(G_e(i) - G_i)
+// (b(r) / e(i): first / last row of the row's block).  Every factor is <= 1.
+// Block (I, J) of the scores uses the keys of block J scaled by
+// 2^(G_16I - G_(16J+15)) while their fragments are loaded, so every product
+// carries exactly 2^(G_r - G_i).  The scores, W = A E and U = A Z are
+// mma.sync m16n8k16 products from ldmatrix fragments; the unit-lower inverse
+// A = (I+Akk)^-1 stays in fp32 (register substitution for the diagonal
+// blocks, 3-pass TF32 products for the rest).  Diagonal blocks whose 16-row
+// decay range exceeds the fp32 exponent budget are recomputed elementwise.
 #include "chunk_args.cuh"
 #include "inverse.cuh"
 #include "mma16.cuh"
@@ -25,35 +29,59 @@ struct Fwd16Layout {
   static constexpr int LDG = D + 4;
   static constexpr int LDC = kChunk + 8;   // 16-bit 64 x 64
   static constexpr int LDF = kChunk + 4;   // fp32 64 x 64
+  static constexpr int tile16 = kChunk * LDK * 2;
   static constexpr int oQ = 0;
-  static constexpr int oK = oQ + kChunk * LDK * 2;
-  static constexpr int oB = oK + kChunk * LDK * 2;
-  static constexpr int oV = oB + kChunk * LDK * 2;
-  static constexpr int oW = oV + kChunk * LDK * 2;
-  static constexpr int oG = oW + kChunk * LDK * 2;
+  static constexpr int oK = oQ + tile16;
+  static constexpr int oB = oK + tile16;
+  static constexpr int oV = oB + tile16;  // v, then Z = v * w
+  static constexpr int oW = oV + tile16;  // w, then E = b k_n 2^G
+  static constexpr int oG = oW + tile16;
   static constexpr int oMisc = oG + kChunk * LDG * 4;
-  static constexpr int nMisc = 64 + 64 + 4;
+  // misc floats: rq[64] rk[64] flag[4] Pb[4][D] Qe[4][D] F[10][D]
+  static constexpr int nMisc = 64 + 64 + 4 + 18 * D;
   static constexpr int oR = oMisc + nMisc * 4;  // work region
   // scores
   static constexpr int rQs = 0;
-  static constexpr int rKBs = rQs + kChunk * LDK * 2;
-  static constexpr int rKs = rKBs + kChunk * LDK * 2;
-  static constexpr int rAkk = rKs + 160 * LDK * 2;
+  static constexpr int rKBs = rQs + tile16;
+  static constexpr int rKb = rKBs + tile16;
+  static constexpr int rAkk = rKb + tile16;
   static constexpr int rEndScores = rAkk + kChunk * LDF * 4;
-  // inverse (Akk stays in place)
+  // inverse (reads Akk; Inv and the T tiles reuse the dead Qs / KBs / Kb)
   static constexpr int rInv = 0;
-  static constexpr int rTmp = rInv + kChunk * LDF * 4;
-  // W, U
-  static constexpr int rA16 = rTmp + 3 * 256 * 4;
-  static constexpr int rE = rA16 + kChunk * LDC * 2;
-  static constexpr int rZ = rE + kChunk * LDK * 2;
-  static constexpr int rEndWU = rZ + kChunk * LDK * 2;
-  // sA16 / sE / sZ are written only after the inverse has finished reading
-  // Akk, so they may overlap it; they never overlap sInv or each other.
-  static constexpr int R = rEndScores > rEndWU ? rEndScores : rEndWU;
+  static constexpr int rT = rInv + kChunk * LDF * 4;
+  static constexpr int rA16 = rT + 3 * 16 * 20 * 4;  // written after the inverse
+  static constexpr int rEndInv = rA16 + kChunk * LDC * 2;
+  static constexpr int R = rEndScores > rEndInv ? rEndScores : rEndInv;
   static constexpr size_t bytes = (size_t)oR + R;
+  static_assert(rT + 3 * 16 * 20 * 4 <= rAkk, "T tiles overlap Akk");
   static_assert(oR % 16 == 0 && rAkk % 16 == 0 && rA16 % 16 == 0, "alignment");
 };
+
+// acc_q / acc_k (16 x 16) += A_q / A_k (16 rows at m0, D columns) times the
+// 16 key rows at n0 of Kb (K-major), each key column c scaled by F[c].
+template <typename T, int D>
+__device__ __forceinline__ void score_block16(float (&aq)[1][2][4], float (&ak)[1][2][4],
+                                              const T* Aq, const T* Ak, int lda, int m0,
+                                              const T* Kb, int n0, const float* F) {
+  const int tig = threadIdx.x & 3;
+#pragma unroll
+  for (int k0 = 0; k0 < D; k0 += 16) {
+    uint32_t a1[4], a2[4], b[4];
+    load_a16<true>(a1, Aq, lda, m0, k0);
+    load_a16<true>(a2, Ak, lda, m0, k0);
+    load_b16x2<true>(b, Kb, lda, k0, n0);
+    const float2 f0 = *reinterpret_cast<const float2*>(F + k0 + 2 * tig);
+    const float2 f1 = *reinterpret_cast<const float2*>(F + k0 + 8 + 2 * tig);
+    b[0] = scale_pair<T>(b[0], f0);
+    b[1] = scale_pair<T>(b[1], f1);
+    b[2] = scale_pair<T>(b[2], f0);
+    b[3] = scale_pair<T>(b[3], f1);
+    Mma16<T>::run(aq[0][0], a1, b[0], b[1]);
+    Mma16<T>::run(aq[0][1], a1, b[2], b[3]);
+    Mma16<T>::run(ak[0][0], a2, b[0], b[1]);
+    Mma16<T>::run(ak[0][1], a2, b[2], b[3]);
+  }
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) {
@@ -71,10 +99,13 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
   float* rq = reinterpret_cast<float*>(sm + L::oMisc);
   float* rk = rq + 64;
   int* sFlag = reinterpret_cast<int*>(rk + 64);
+  float* sPb = rk + 64 + 4;  // [4][D]  2^G at each block's first row
+  float* sQe = sPb + 4 * D;  // [4][D]  2^(G_63 - G) at each block's last row
+  float* sF = sQe + 4 * D;   // [10][D] 2^(G_16I - G_(16J+15)), pair I(I+1)/2 + J
   unsigned char* R = sm + L::oR;
   T* sQs = reinterpret_cast<T*>(R + L::rQs);
   T* sKBs = reinterpret_cast<T*>(R + L::rKBs);
-  T* sKs = reinterpret_cast<T*>(R + L::rKs);
+  T* sKb = reinterpret_cast<T*>(R + L::rKb);
   float* sAkk = reinterpret_cast<float*>(R + L::rAkk);
 
   const int c = blockIdx.x, h = blockIdx.y;
@@ -99,50 +130,100 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
   cp_tile16<T, kChunk, D, NTH>(sv, LDK, reinterpret_cast<const T*>(a.v) + offv, ldv, len, V);
   cp_tile16<T, kChunk, D, NTH>(sw, LDK, reinterpret_cast<const T*>(a.w) + offv, ldv, len, V);
   cp_async_commit();
-  for (int i = tid; i < kChunk * LDF; i += NTH) sAkk[i] = 0.f;
   if (tid == 0) sFlag[0] = 1;
   cp_async_wait<1>();
   __syncthreads();
-  col_scan64_t<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(R + L::rQs));
-  for (int i = tid; i < kChunk * D; i += NTH) {
-    const int r = i / D, cc = i - r * D;
-    sG[r * LDG + cc] *= kLog2e;
-  }
-  for (int r = warp; r < kChunk; r += NTH / 32) {
-    float s1 = 0.f, s2 = 0.f;
-    for (int cc = lane; cc < D; cc += 32) {
-      const float x = to_f<T>(sq[r * LDK + cc]), y = to_f<T>(sk[r * LDK + cc]);
-      s1 += x * x;
-      s2 += y * y;
+  // chunk-local log2 cumulative decay
+  col_scan64_reg<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(R), kLog2e);
+  // row norms: warp w owns rows 4w .. 4w+3
+  {
+    constexpr int EPL = D / 32;
+    float s1[4], s2[4];
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const int r = 4 * warp + rr;
+      s1[rr] = 0.f;
+      s2[rr] = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float x = to_f<T>(sq[r * LDK + EPL * lane + e]);
+        const float y = to_f<T>(sk[r * LDK + EPL * lane + e]);
+        s1[rr] += x * x;
+        s2[rr] += y * y;
+      }
     }
-    s1 = warp_sum(s1);
-    s2 = warp_sum(s2);
-    if (lane == 0) {
-      rq[r] = a.l2norm ? rsqrtf(s1 + kNormEps) : 1.f;
-      rk[r] = a.l2norm ? rsqrtf(s2 + kNormEps) : 1.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+        s1[rr] += __shfl_xor_sync(0xffffffffu, s1[rr], o);
+        s2[rr] += __shfl_xor_sync(0xffffffffu, s2[rr], o);
+      }
+    if (lane < 4) {
+      const int r = 4 * warp + lane;
+      const float x1 = lane == 0 ? s1[0] : lane == 1 ? s1[1] : lane == 2 ? s1[2] : s1[3];
+      const float x2 = lane == 0 ? s2[0] : lane == 1 ? s2[1] : lane == 2 ? s2[2] : s2[3];
+      rq[r] = a.l2norm ? rsqrtf(x1 + kNormEps) : 1.f;
+      rk[r] = a.l2norm ? rsqrtf(x2 + kNormEps) : 1.f;
     }
   }
+  // per-block decay factors, diagonal-block safety, gl out
+  float* gGl = reinterpret_cast<float*>(a.saved + a.L.gl) + ch * K;
+  for (int i = tid; i < 18 * D; i += NTH) {
+    const int p = i / D, cc = i - p * D;
+    const float GL = sG[(kChunk - 1) * LDG + cc];
+    float x;
+    if (p < 4) {
+      x = exp2f(sG[16 * p * LDG + cc]);
+    } else if (p < 8) {
+      x = exp2f(GL - sG[(16 * (p - 4) + 15) * LDG + cc]);
+    } else {
+      const int q = p - 8;
+      const int I = q >= 6 ? 3 : q >= 3 ? 2 : q >= 1 ? 1 : 0;
+      const int J = q - I * (I + 1) / 2;
+      x = exp2f(fminf(sG[16 * I * LDG + cc] - sG[(16 * J + 15) * LDG + cc], 120.f));
+    }
+    sPb[i] = x;  // sPb, sQe, sF are contiguous
+  }
+  for (int i = tid; i < 4 * D; i += NTH) {
+    const int bI = i / D, cc = i - bI * D;
+    const float rng = sG[(16 * bI) * LDG + cc] - sG[(16 * bI + 15) * LDG + cc];
+    if (!(rng <= kSafeLog2Range)) sFlag[0] = 0;
+  }
+  for (int i = tid; i < K; i += NTH) gGl[i] = exp2f(sG[(kChunk - 1) * LDG + i]);
+  cp_async_wait<0>();  // v, w
   __syncthreads();
+  const bool safe = sFlag[0] != 0;
 
-  // ---- Qg, Kd, gl out; score operands -----------------------------------------
+  // ---- one elementwise pass: Qg, Kd out; Qs, KBs, Kb score operands;
+  //      E = b k_n 2^G over w, Z = v w over v -------------------------------------
   const size_t tileK = (size_t)kChunk * K, tileV = (size_t)kChunk * V;
   T* gQg = reinterpret_cast<T*>(a.saved + a.L.qg) + ch * tileK;
   T* gKd = reinterpret_cast<T*>(a.saved + a.L.kd) + ch * tileK;
-  float* gGl = reinterpret_cast<float*>(a.saved + a.L.gl) + ch * K;
-  for (int i = tid; i < kChunk * (D / 2); i += NTH) {
+#pragma unroll 2
+  for (int it = 0; it < kChunk * (D / 2) / NTH; ++it) {
+    const int i = tid + it * NTH;
     const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
-    const int rb = r & ~15;
-    float qg[2], kd[2], qs[2], kbs[2];
+    const int blk = r >> 4, rb = r & ~15, re = rb + 15;
+    float qg[2], kd[2], qs[2], kbs[2], kb[2], e2[2], z2[2];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      const float G = sG[r * LDG + cc + t], GL = sG[(kChunk - 1) * LDG + cc + t];
-      const float qn = to_f<T>(sq[r * LDK + cc + t]) * rq[r];
-      const float kn = to_f<T>(sk[r * LDK + cc + t]) * rk[r];
-      const float f = exp2f(G - sG[rb * LDG + cc + t]);
-      qg[t] = scale * qn * exp2f(G);
-      kd[t] = kn * exp2f(GL - G);
+      const int col = cc + t;
+      const float G = sG[r * LDG + col];
+      const float f = exp2f(G - sG[rb * LDG + col]);   // <= 1
+      const float fe = exp2f(sG[re * LDG + col] - G);  // <= 1
+      const float qn = to_f<T>(sq[r * LDK + col]) * rq[r];
+      const float kn = to_f<T>(sk[r * LDK + col]) * rk[r];
+      const float bb = to_f<T>(sb[r * LDK + col]);
+      const float eG = sPb[blk * D + col] * f;   // 2^G
+      const float eK = sQe[blk * D + col] * fe;  // 2^(G_63 - G)
+      qg[t] = scale * qn * eG;
+      kd[t] = kn * eK;
       qs[t] = scale * qn * f;
-      kbs[t] = to_f<T>(sb[r * LDK + cc + t]) * kn * f;
+      kbs[t] = bb * kn * f;
+      kb[t] = kn * fe;
+      e2[t] = bb * kn * eG;
+      z2[t] = to_f<T>(sv[r * LDK + col]) * to_f<T>(sw[r * LDK + col]);
     }
     if (cc < K) {
       *reinterpret_cast<uint32_t*>(gQg + r * K + cc) = pack2<T>(qg[0], qg[1]);
@@ -150,39 +231,24 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
     }
     *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(qs[0], qs[1]);
     *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kbs[0], kbs[1]);
-  }
-  for (int i = tid; i < K; i += NTH) gGl[i] = exp2f(sG[(kChunk - 1) * LDG + i]);
-  for (int i = tid; i < 160 * (D / 2); i += NTH) {
-    const int row = i / (D / 2), cc = (i - row * (D / 2)) * 2;
-    const int I = row < 16 ? 0 : row < 48 ? 1 : row < 96 ? 2 : 3;
-    const int r = row - 8 * I * (I + 1), r0 = 16 * I;
-    float k2[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const float e = fminf(sG[r0 * LDG + cc + t] - sG[r * LDG + cc + t], 120.f);
-      k2[t] = to_f<T>(sk[r * LDK + cc + t]) * rk[r] * exp2f(e);
-    }
-    *reinterpret_cast<uint32_t*>(sKs + row * LDK + cc) = pack2<T>(k2[0], k2[1]);
-  }
-  for (int i = tid; i < 4 * D; i += NTH) {
-    const int bI = i / D, cc = i - bI * D;
-    const float rng = sG[(16 * bI) * LDG + cc] - sG[(16 * bI + 15) * LDG + cc];
-    if (!(rng <= kSafeLog2Range)) sFlag[0] = 0;
+    *reinterpret_cast<uint32_t*>(sKb + r * LDK + cc) = pack2<T>(kb[0], kb[1]);
+    *reinterpret_cast<uint32_t*>(sw + r * LDK + cc) = pack2<T>(e2[0], e2[1]);
+    *reinterpret_cast<uint32_t*>(sv + r * LDK + cc) = pack2<T>(z2[0], z2[1]);
   }
   __syncthreads();
-  const bool safe = sFlag[0] != 0;
 
-  // ---- score blocks: warp (I = wr, column block wc <= I) -------------------------
+  // ---- score blocks: warp (I = wr, column block J = wc <= I) ----------------------
+  // key i of block J enters block row I as Kb[i] 2^(G_16I - G_(16J+15)), so
+  // every product carries exactly 2^(G_r - G_i).
   T* gAqk = reinterpret_cast<T*>(a.saved + a.L.aqk) + ch * kChunk * kChunk;
   {
     const int I = wr, J = wc;
     if (J <= I && (safe || J < I)) {
-      const T* KsI = sKs + 8 * I * (I + 1) * LDK;
       float aq[1][2][4], ak[1][2][4];
       acc_zero(aq);
       acc_zero(ak);
-      warp_mma16<1, 2, true, true>(aq, sQs, LDK, 16 * I, KsI, LDK, 16 * J, D);
-      warp_mma16<1, 2, true, true>(ak, sKBs, LDK, 16 * I, KsI, LDK, 16 * J, D);
+      score_block16<T, D>(aq, ak, sQs, sKBs, LDK, 16 * I, sKb, 16 * J,
+                          sF + (I * (I + 1) / 2 + J) * D);
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -230,30 +296,15 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
 
   // ---- A = (I + Akk)^-1 ----------------------------------------------------------
   float* sInv = reinterpret_cast<float*>(R + L::rInv);
-  unit_lower_inverse<LDF>(sAkk, sInv, reinterpret_cast<float*>(R + L::rTmp));
+  unit_lower_inverse_mma<LDF>(sAkk, sInv, reinterpret_cast<float*>(R + L::rT));
   T* sA16 = reinterpret_cast<T*>(R + L::rA16);
-  T* sE = reinterpret_cast<T*>(R + L::rE);
-  T* sZ = reinterpret_cast<T*>(R + L::rZ);
   T* gA = reinterpret_cast<T*>(a.saved + a.L.a) + ch * kChunk * kChunk;
   for (int i = tid; i < kChunk * 32; i += NTH) {
     const int r = i >> 5, cc = (i & 31) * 2;
-    const uint32_t pk = pack2<T>(sInv[r * LDF + cc], sInv[r * LDF + cc + 1]);
+    const uint32_t pk =
+        (cc >> 4) <= (r >> 4) ? pack2<T>(sInv[r * LDF + cc], sInv[r * LDF + cc + 1]) : 0u;
     *reinterpret_cast<uint32_t*>(sA16 + r * LDC + cc) = pk;
     *reinterpret_cast<uint32_t*>(gA + r * kChunk + cc) = pk;
-  }
-  cp_async_wait<0>();  // v, w
-  __syncthreads();
-  for (int i = tid; i < kChunk * (D / 2); i += NTH) {
-    const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
-    float e2[2], z2[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      e2[t] = to_f<T>(sb[r * LDK + cc + t]) * to_f<T>(sk[r * LDK + cc + t]) * rk[r] *
-              exp2f(sG[r * LDG + cc + t]);
-      z2[t] = to_f<T>(sv[r * LDK + cc + t]) * to_f<T>(sw[r * LDK + cc + t]);
-    }
-    *reinterpret_cast<uint32_t*>(sE + r * LDK + cc) = pack2<T>(e2[0], e2[1]);
-    *reinterpret_cast<uint32_t*>(sZ + r * LDK + cc) = pack2<T>(z2[0], z2[1]);
   }
   __syncthreads();
 
@@ -263,7 +314,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
     T* gU = reinterpret_cast<T*>(a.saved + a.L.u) + ch * tileV;
     float acc[1][NTO][4];
     acc_zero(acc);
-    warp_mma16<1, NTO, true, false>(acc, sA16, LDC, 16 * wr, sE, LDK, wc * DQ, kChunk);
+    warp_mma16<1, NTO, true, false>(acc, sA16, LDC, 16 * wr, sw, LDK, wc * DQ, kChunk);
 #pragma unroll
     for (int j = 0; j < NTO; ++j)
 #pragma unroll
@@ -274,7 +325,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
               pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
       }
     acc_zero(acc);
-    warp_mma16<1, NTO, true, false>(acc, sA16, LDC, 16 * wr, sZ, LDK, wc * DQ, kChunk);
+    warp_mma16<1, NTO, true, false>(acc, sA16, LDC, 16 * wr, sv, LDK, wc * DQ, kChunk);
 #pragma unroll
     for (int j = 0; j < NTO; ++j)
 #pragma unroll

@@ -197,6 +197,44 @@ __device__ __forceinline__ void col_scan64_t(float* s, int lds, float* tmp) {
   __syncthreads();
 }
 
+// Register-staged variant of col_scan64_t: each thread loads its whole row
+// segment first, scans it in registers, and writes (prefix + offset) * mul
+// once.  Same summation order as col_scan64_t.  Contains __syncthreads().
+template <int NC, int NTH, bool REV>
+__device__ __forceinline__ void col_scan64_reg(float* s, int lds, float* tmp, float mul) {
+  constexpr int NSEG = NTH / NC;
+  constexpr int RPS = kChunk / NSEG;
+  static_assert(NSEG * NC == NTH && RPS * NSEG == kChunk, "scan shape");
+  const int col = threadIdx.x % NC, seg = threadIdx.x / NC;
+  float x[RPS];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) {
+    const int r = REV ? (kChunk - 1 - (seg * RPS + i)) : (seg * RPS + i);
+    x[i] = s[r * lds + col];
+  }
+#pragma unroll
+  for (int i = 1; i < RPS; ++i) x[i] += x[i - 1];
+  tmp[seg * NC + col] = x[RPS - 1];
+  __syncthreads();
+  float off = 0.f;
+#pragma unroll
+  for (int j = 0; j < NSEG - 1; ++j)
+    if (j < seg) off += tmp[j * NC + col];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) {
+    const int r = REV ? (kChunk - 1 - (seg * RPS + i)) : (seg * RPS + i);
+    s[r * lds + col] = (x[i] + off) * mul;
+  }
+  __syncthreads();
+}
+
+// Scale the two 16-bit values packed in x by (f.x, f.y).
+template <typename T>
+__device__ __forceinline__ uint32_t scale_pair(uint32_t x, float2 f) {
+  const T* v = reinterpret_cast<const T*>(&x);
+  return pack2<T>(to_f<T>(v[0]) * f.x, to_f<T>(v[1]) * f.y);
+}
+
 // Same for an fp32 vector of n floats (n a multiple of 4), zero beyond n.
 template <int N, int NTH>
 __device__ __forceinline__ void cp_vec32(float* s, const float* g, int n) {
