@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <string>
 
 #include "../../include/gdn2_b200.h"
@@ -23,6 +24,7 @@ template <typename T, int D> cudaError_t launch_fwd_intra16(const FwdIntraArgs&,
 bool fwd_state_tc_ok(const FwdStateArgs&, int dtype_bf16);
 cudaError_t launch_fwd_state_tc(const FwdStateArgs&, cudaStream_t);
 cudaError_t read_fault_bits(unsigned int* bits, bool clear);
+cudaError_t fault_word(unsigned int** ptr);
 }  // namespace gdn2
 
 using namespace gdn2;
@@ -147,6 +149,20 @@ cudaError_t run_state16(const Args& a, int bucket, int cols, int n_seqs, int H, 
 // on the fp32-staged kernels.
 bool use16(const gdn2_chunk_problem* p) {
   return p->dtype == GDN2_DTYPE_BF16 && (p->K % 8) == 0 && (p->V % 8) == 0;
+}
+
+bool aligned16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; }
+
+// The 16-bit kernels move token rows with bulk async copies, which need
+// 16-byte aligned rows.
+int check_aligned16(const gdn2_chunk_problem* p, const char* fn,
+                    std::initializer_list<const void*> ptrs) {
+  if (!use16(p)) return GDN2_OK;
+  for (const void* x : ptrs)
+    if (x && !aligned16(x))
+      return fail(GDN2_ERR_INVALID,
+                  "%s: bf16 tensors must start on a 16-byte boundary (got %p)", fn, x);
+  return GDN2_OK;
 }
 
 // bf16 with K = V = 128 (the pre-scan excepted) runs the forward state pass
@@ -291,6 +307,8 @@ int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   if (saved_bytes < L.total)
     return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_fwd_intra: saved buffer %zu < %zu bytes",
                 saved_bytes, L.total);
+  rc = check_aligned16(p, "gdn2_chunk_fwd_intra", {q, k, v, g, b, w, saved});
+  if (rc) return rc;
   FwdIntraArgs a;
   a.seqs = make_seqs(p);
   a.H = p->H; a.K = p->K; a.V = p->V;
@@ -299,7 +317,9 @@ int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
   a.saved = static_cast<unsigned char*>(saved);
   a.L = L;
-  cudaError_t e = fwd_intra_dispatch(p, a, (cudaStream_t)stream);
+  cudaError_t e = fault_word(&a.fault);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn2_chunk_fwd_intra");
+  e = fwd_intra_dispatch(p, a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_fwd_intra");
 }
 
@@ -379,6 +399,8 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
     return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_bwd_intra: workspace %zu < %zu bytes",
                 workspace_bytes, BL.total);
   if (p->seqs.n_chunks == 0) return GDN2_OK;
+  rc = check_aligned16(p, "gdn2_chunk_bwd_intra", {q, k, v, g, b, w, saved, dout, workspace});
+  if (rc) return rc;
   BwdIntraArgs a;
   a.seqs = make_seqs(p);
   a.H = p->H; a.K = p->K; a.V = p->V;
@@ -391,7 +413,9 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.ws = static_cast<const unsigned char*>(workspace);
   a.BL = BL;
   a.dq = dq; a.dk = dk; a.dv = dv; a.dg = dg; a.db = db; a.dw = dw;
-  cudaError_t e = bwd_intra_dispatch(p, a, (cudaStream_t)stream);
+  cudaError_t e = fault_word(&a.fault);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn2_chunk_bwd_intra");
+  e = bwd_intra_dispatch(p, a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_bwd_intra");
 }
 

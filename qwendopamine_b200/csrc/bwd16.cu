@@ -37,8 +37,8 @@ struct Bwd16Layout {
   static constexpr int oG = oB + kChunk * LDK * 2;
   static constexpr int oA = oG + kChunk * LDG * 4;
   static constexpr int oMisc = oA + kChunk * LDC * 2;
-  // misc floats: rq[64] rk[64] dgl[D] diag[64] pdq[4][64] pdk[4][64] flag
-  static constexpr int nMisc = 64 + 64 + D + 64 + 256 + 256 + 4;
+  // misc floats: rq[64] rk[64] dgl[D] diag[64] pdq[4][64] pdk[4][64] flag[4] F[10][D]
+  static constexpr int nMisc = 64 + 64 + D + 64 + 256 + 256 + 4 + 10 * D;
   static constexpr int oW = oMisc + nMisc * 4;
   // phase V (offsets inside W)
   static constexpr int vH = 0;
@@ -61,8 +61,8 @@ struct Bwd16Layout {
   static constexpr int kT2 = kT1 + kChunk * LDC * 2;
   static constexpr int kQs = kR2;
   static constexpr int kKBs = kQs + kChunk * LDK * 2;
-  static constexpr int kKs = kKBs + kChunk * LDK * 2;
-  static constexpr int kEnd = kKs + 160 * LDK * 2;
+  static constexpr int kKb = kKBs + kChunk * LDK * 2;
+  static constexpr int kEnd = kKb + kChunk * LDK * 2;
   static constexpr int kdG = 0;
   static constexpr int kX = kdG + kChunk * LDG * 4;
   static constexpr int kTmp = kX + kChunk * LDG * 4;
@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   float* pdq = sDiag + 64;  // [4][64]
   float* pdk = pdq + 256;   // [4][64]
   int* sFlag = reinterpret_cast<int*>(pdk + 256);
+  float* sF = pdk + 256 + 4;  // [10][D] 2^(G_16I - G_(16J+15)), pair I(I+1)/2 + J
   unsigned char* W = sm + L::oW;
 
   const int c = blockIdx.x, h = blockIdx.y;
@@ -146,25 +147,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   cp_async_wait<0>();
   __syncthreads();
   // chunk-local log2 cumulative decay; row norms
-  col_scan64_t<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(W + L::vZ));
-  for (int i = tid; i < kChunk * D; i += NTH) {
-    const int r = i / D, cc = i - r * D;
-    sG[r * LDG + cc] *= kLog2e;
-  }
-  for (int r = warp; r < kChunk; r += NTH / 32) {
-    float s1 = 0.f, s2 = 0.f;
-    for (int cc = lane; cc < D; cc += 32) {
-      const float x = to_f<T>(sq[r * LDK + cc]), y = to_f<T>(sk[r * LDK + cc]);
-      s1 += x * x;
-      s2 += y * y;
-    }
-    s1 = warp_sum(s1);
-    s2 = warp_sum(s2);
-    if (lane == 0) {
-      rq[r] = a.l2norm ? rsqrtf(s1 + kNormEps) : 1.f;
-      rk[r] = a.l2norm ? rsqrtf(s2 + kNormEps) : 1.f;
-    }
-  }
+  col_scan64_reg<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(W + L::vZ), kLog2e);
+  row_norms16<T, D, NTH>(sq, sk, LDK, rq, rk, a.l2norm);
 
   // ---- phase V --------------------------------------------------------------
   float accQ[1][NTO][4], accKd[1][NTO][4], accW[1][NTO][4], accAqk[1][2][4], accDA[1][2][4];
@@ -335,38 +319,33 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   __syncthreads();  // sDW / sE / sT* are dead; R2 becomes the score tiles
 
   // ---- score backward ---------------------------------------------------------
+  // Operands with per-16-row-block references (every factor <= 1):
+  //   Qs[r] = scale q_n[r] 2^(G_r - G_b(r)),  KBs[r] = (b k_n)[r] 2^(G_r - G_b(r)),
+  //   Kb[i] = k_n[i] 2^(G_e(i) - G_i);
+  // key block J enters block row I scaled by F_IJ = 2^(G_16I - G_(16J+15)).
   T* sQs = reinterpret_cast<T*>(W + L::kQs);
   T* sKBs = reinterpret_cast<T*>(W + L::kKBs);
-  T* sKs = reinterpret_cast<T*>(W + L::kKs);
+  T* sKb = reinterpret_cast<T*>(W + L::kKb);
   if (tid == 0) sFlag[0] = 1;
+  block_factors<D, NTH>(sG, LDG, sF);
   __syncthreads();
   for (int i = tid; i < kChunk * (D / 2); i += NTH) {
     const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
-    const int rb = r & ~15;
-    float q2[2], kb2[2];
+    const int rb = r & ~15, re = rb + 15;
+    float q2[2], kb2[2], k2[2];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      const float f = exp2f(sG[r * LDG + cc + t] - sG[rb * LDG + cc + t]);
+      const float G = sG[r * LDG + cc + t];
+      const float f = exp2f(G - sG[rb * LDG + cc + t]);
+      const float fe = exp2f(sG[re * LDG + cc + t] - G);
       const float kn = to_f<T>(sk[r * LDK + cc + t]) * rk[r];
       q2[t] = scale * to_f<T>(sq[r * LDK + cc + t]) * rq[r] * f;
       kb2[t] = to_f<T>(sb[r * LDK + cc + t]) * kn * f;
+      k2[t] = kn * fe;
     }
     *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(q2[0], q2[1]);
     *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kb2[0], kb2[1]);
-  }
-  for (int i = tid; i < 160 * (D / 2); i += NTH) {
-    const int row = i / (D / 2), cc = (i - row * (D / 2)) * 2;
-    // rows [0,16) for block 0, [16,48) for block 1, [48,96) block 2, [96,160) block 3
-    const int I = row < 16 ? 0 : row < 48 ? 1 : row < 96 ? 2 : 3;
-    const int base = 8 * I * (I + 1);
-    const int r = row - base, r0 = 16 * I;
-    float k2[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const float e = fminf(sG[r0 * LDG + cc + t] - sG[r * LDG + cc + t], 120.f);
-      k2[t] = to_f<T>(sk[r * LDK + cc + t]) * rk[r] * exp2f(e);
-    }
-    *reinterpret_cast<uint32_t*>(sKs + row * LDK + cc) = pack2<T>(k2[0], k2[1]);
+    *reinterpret_cast<uint32_t*>(sKb + r * LDK + cc) = pack2<T>(k2[0], k2[1]);
   }
   for (int i = tid; i < 4 * D; i += NTH) {
     const int bI = i / D, cc = i - bI * D;
@@ -376,15 +355,30 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   __syncthreads();
   const bool safe = sFlag[0] != 0;
   {
-    // X products: rows of block I = wr
-    const int I = wr, jmax = safe ? 16 * (I + 1) : 16 * I;
-    if (jmax > 0) {
-      const T* KsI = sKs + 8 * I * (I + 1) * LDK;
+    // X products: rows of block I = wr, one 16-key block J at a time
+    const int I = wr, nJ = safe ? I + 1 : I;
+    if (nJ > 0) {
       float tq[1][NTO][4], tk[1][NTO][4];
       acc_zero(tq);
       acc_zero(tk);
-      warp_mma16<1, NTO, true, false>(tq, sDAqk, LDC, 16 * I, KsI, LDK, wc * DQ, jmax);
-      warp_mma16<1, NTO, true, false>(tk, sDAkk, LDC, 16 * I, KsI, LDK, wc * DQ, jmax);
+      for (int J = 0; J < nJ; ++J) {
+        float pq[1][NTO][4], pk[1][NTO][4];
+        acc_zero(pq);
+        acc_zero(pk);
+        warp_mma16<1, NTO, true, false>(pq, sDAqk + 16 * J, LDC, 16 * I, sKb + 16 * J * LDK, LDK,
+                                        wc * DQ, 16);
+        warp_mma16<1, NTO, true, false>(pk, sDAkk + 16 * J, LDC, 16 * I, sKb + 16 * J * LDK, LDK,
+                                        wc * DQ, 16);
+        const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
+#pragma unroll
+        for (int j = 0; j < NTO; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float F = FIJ[wc * DQ + 8 * j + 2 * tig + (e & 1)];
+            tq[0][j][e] += F * pq[0][j][e];
+            tk[0][j][e] += F * pk[0][j][e];
+          }
+      }
 #pragma unroll
       for (int j = 0; j < NTO; ++j)
 #pragma unroll
@@ -399,8 +393,14 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
           dG[0][j][e] += qn * xq + kb * xk;
         }
     }
-    // Y products: columns of block J = wr, from block rows I >= J
+    // Y products: columns of block J = wr, from block rows I >= J; the key
+    // side factor 2^(G_16I - G_r) = F_IJ 2^(G_(16J+15) - G_r)
     const int J = wr;
+    float ys[NTO][4];
+#pragma unroll
+    for (int j = 0; j < NTO; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ys[j][e] = 0.f;
     for (int I = J; I < 4; ++I) {
       if (I == J && !safe) continue;
       float ty[1][NTO][4];
@@ -409,18 +409,24 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
                                        sQs + 16 * I * LDK, LDK, wc * DQ, 16);
       warp_mma16<1, NTO, false, false>(ty, sDAkk + 16 * I * LDC, LDC, 16 * J,
                                        sKBs + 16 * I * LDK, LDK, wc * DQ, 16);
+      const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
 #pragma unroll
       for (int j = 0; j < NTO; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
-          const float ee = exp2f(fminf(sG[(16 * I) * LDG + cl] - sG[r * LDG + cl], 120.f));
-          const float y = ty[0][j][e] * ee;
-          const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
-          dkn[0][j][e] += y;
-          dG[0][j][e] -= kn * y;
-        }
+        for (int e = 0; e < 4; ++e)
+          ys[j][e] += FIJ[wc * DQ + 8 * j + 2 * tig + (e & 1)] * ty[0][j][e];
     }
+#pragma unroll
+    for (int j = 0; j < NTO; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
+        const float fe = exp2f(sG[(16 * J + 15) * LDG + cl] - sG[r * LDG + cl]);
+        const float y = ys[j][e] * fe;
+        const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
+        dkn[0][j][e] += y;
+        dG[0][j][e] -= kn * y;
+      }
     if (!safe) {
       // exact diagonal block, off-diagonal pairs only
 #pragma unroll
@@ -471,8 +477,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     }
   for (int i = tid; i < D; i += NTH) sX[i] = 0.f;
   __syncthreads();
-  col_scan64_t<D, NTH, true>(sdG, LDG, sTmp);
-  col_scan64_t<D, NTH, false>(sX, LDG, sTmp);
+  col_scan64_reg<D, NTH, true>(sdG, LDG, sTmp, 1.f);
+  col_scan64_reg<D, NTH, false>(sX, LDG, sTmp, 1.f);
   float* gdg = a.dg + offk;
   for (int i = tid; i < kChunk * D; i += NTH) {
     const int r = i / D, cc = i - r * D;

@@ -19,6 +19,7 @@ struct FwdIntraArgs {
   const void* w;
   unsigned char* saved;
   SavedLayout L;
+  unsigned int* fault;  // device fault word (bounded waits that ran out)
 };
 
 struct FwdStateArgs {
@@ -69,6 +70,7 @@ struct BwdIntraArgs {
   float* dg;
   void* db;
   void* dw;
+  unsigned int* fault;  // device fault word (bounded waits that ran out)
 };
 
 struct RecArgs {

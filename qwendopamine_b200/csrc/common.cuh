@@ -250,6 +250,14 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
+// Number of SMs of the current device (persistent-kernel grids).
+inline cudaError_t num_sms(int* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  return cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, dev);
+}
+
 // ---------------------------------------------------------------------------
 // geometry
 // ---------------------------------------------------------------------------

@@ -50,14 +50,72 @@ __device__ void unit_lower_inverse(const float* sL, float* sInv, float* sTmp) {
   }
 }
 
+// acc (16 x 16) = A (16 x KD) B (KD x 16) on the tensor cores with the
+// 3-term TF32 split (hi*hi + hi*lo + lo*hi, about fp32 accuracy); the two
+// accumulator chains run independently.  A(m,k) = A[m*lda + k],
+// B(k,n) = B[k*ldb + n] (fp32 shared memory).
+template <int KD>
+__device__ __forceinline__ void mma16x16_tf32x3(float (&acc)[1][2][4], const float* A, int lda,
+                                                const float* B, int ldb) {
+  const int lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  float hh[2][4], mx[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) hh[j][e] = mx[j][e] = 0.f;
+#pragma unroll
+  for (int k0 = 0; k0 < KD; k0 += 8) {
+    const float* a = A + gid * lda + k0 + tig;
+    const float x[4] = {a[0], a[8 * lda], a[4], a[8 * lda + 4]};
+    uint32_t ah[4], al[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      ah[e] = tf32_bits(x[e]);
+      al[e] = tf32_bits(x[e] - __uint_as_float(ah[e]));
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float* bp = B + (k0 + tig) * ldb + j * 8 + gid;
+      const float y0 = bp[0], y1 = bp[4 * ldb];
+      const uint32_t bh0 = tf32_bits(y0), bh1 = tf32_bits(y1);
+      const uint32_t bl0 = tf32_bits(y0 - __uint_as_float(bh0));
+      const uint32_t bl1 = tf32_bits(y1 - __uint_as_float(bh1));
+      mma_tf32(hh[j], ah, bh0, bh1);
+      mma_tf32(mx[j], al, bh0, bh1);
+      mma_tf32(mx[j], ah, bl0, bl1);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[0][j][e] = hh[j][e] + mx[j][e];
+}
+
+// Blocks at distance d = I - J of the inverse, one warp per block:
+//   T = sum_{M=J}^{I-1} L_IM Inv_MJ,   Inv_IJ = -Inv_II T.
+template <int LDC, int DIST>
+__device__ __forceinline__ void inverse_level(const float* sL, float* sInv, float* sT) {
+  const int warp = threadIdx.x >> 5;
+  if (warp < 4 - DIST) {
+    const int J = warp, I = warp + DIST;
+    float* t = sT + warp * (16 * 20);
+    float acc[1][2][4];
+    mma16x16_tf32x3<16 * DIST>(acc, sL + 16 * I * LDC + 16 * J, LDC, sInv + 16 * J * LDC + 16 * J,
+                               LDC);
+    acc_foreach(acc, [&](int r, int c, float v) { t[r * 20 + c] = v; });
+    __syncwarp();
+    mma16x16_tf32x3<16>(acc, sInv + 16 * I * LDC + 16 * I, LDC, t, 20);
+    acc_foreach(acc, [&](int r, int c, float v) { sInv[(16 * I + r) * LDC + 16 * J + c] = -v; });
+  }
+}
+
 // Same inverse for CTAs of >= 4 warps, reading only the strictly-lower
 // blocks of sL (the upper blocks of sL and of sInv are neither read nor
 // written; callers treat them as zero).  The diagonal 16x16 blocks are
 // solved right-looking in registers (lane j of warp I holds column j of
 // Inv_II, so the dependent chain is one FMA per row); the off-diagonal blocks
-// follow by distance d = I - J with one warp per block and 3-pass TF32
-// tensor-core products (about fp32 accuracy):
-//   T = sum_{M=J}^{I-1} L_IM Inv_MJ,   Inv_IJ = -Inv_II T.
+// follow by distance with 3-term TF32 tensor-core products (inverse_level).
 // sT holds 3 [16][20] fp32 tiles.
 template <int LDC>
 __device__ void unit_lower_inverse_mma(const float* sL, float* sInv, float* sT) {
@@ -76,23 +134,12 @@ __device__ void unit_lower_inverse_mma(const float* sL, float* sInv, float* sT) 
     for (int r = 0; r < 16; ++r) sInv[(o + r) * LDC + o + j] = x[r];
   }
   __syncthreads();
-  for (int d = 1; d < 4; ++d) {
-    if (warp < 4 - d) {
-      const int J = warp, I = warp + d;
-      float* t = sT + warp * (16 * 20);
-      float acc[1][2][4];
-      acc_zero(acc);
-      warp_mma<1, 2, 3>(acc, sL + 16 * I * LDC + 16 * J, LDC, 1, sInv + 16 * J * LDC + 16 * J, LDC,
-                        1, 16 * d);
-      acc_foreach(acc, [&](int r, int c, float v) { t[r * 20 + c] = v; });
-      __syncwarp();
-      float acc2[1][2][4];
-      acc_zero(acc2);
-      warp_mma<1, 2, 3>(acc2, sInv + 16 * I * LDC + 16 * I, LDC, 1, t, 20, 1, 16);
-      acc_foreach(acc2, [&](int r, int c, float v) { sInv[(16 * I + r) * LDC + 16 * J + c] = -v; });
-    }
-    __syncthreads();
-  }
+  inverse_level<LDC, 1>(sL, sInv, sT);
+  __syncthreads();
+  inverse_level<LDC, 2>(sL, sInv, sT);
+  __syncthreads();
+  inverse_level<LDC, 3>(sL, sInv, sT);
+  __syncthreads();
 }
 
 }  // namespace gdn2

@@ -228,6 +228,59 @@ __device__ __forceinline__ void col_scan64_reg(float* s, int lds, float* tmp, fl
   __syncthreads();
 }
 
+// Row norms of the 64-row q and k tiles (row stride ld): each warp owns
+// 64 / (NTH/32) consecutive rows and reduces them together.
+// rq[r] = rsqrt(sum q^2 + eps) (1 without l2norm), same for rk.
+template <typename T, int D, int NTH>
+__device__ __forceinline__ void row_norms16(const T* sq, const T* sk, int ld, float* rq, float* rk,
+                                            int l2norm) {
+  constexpr int RPW = kChunk / (NTH / 32);
+  constexpr int EPL = D / 32;
+  static_assert(RPW * (NTH / 32) == kChunk && RPW <= 32 && EPL * 32 == D, "norm shape");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float s1[RPW], s2[RPW];
+#pragma unroll
+  for (int rr = 0; rr < RPW; ++rr) {
+    const int r = RPW * warp + rr;
+    s1[rr] = 0.f;
+    s2[rr] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const float x = to_f<T>(sq[r * ld + EPL * lane + e]);
+      const float y = to_f<T>(sk[r * ld + EPL * lane + e]);
+      s1[rr] += x * x;
+      s2[rr] += y * y;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr) {
+      s1[rr] += __shfl_xor_sync(0xffffffffu, s1[rr], o);
+      s2[rr] += __shfl_xor_sync(0xffffffffu, s2[rr], o);
+    }
+#pragma unroll
+  for (int rr = 0; rr < RPW; ++rr)
+    if (lane == rr) {
+      const int r = RPW * warp + rr;
+      rq[r] = l2norm ? rsqrtf(s1[rr] + kNormEps) : 1.f;
+      rk[r] = l2norm ? rsqrtf(s2[rr] + kNormEps) : 1.f;
+    }
+}
+
+// Per-16-row-block decay factors F[I(I+1)/2 + J][c] = 2^(G_16I - G_(16J+15))
+// for J <= I (exponent capped at 120; only the diagonal pairs can be
+// positive), from the log2 cumulative decay tile G (row stride ldg).
+template <int D, int NTH>
+__device__ __forceinline__ void block_factors(const float* G, int ldg, float* F) {
+  for (int i = threadIdx.x; i < 10 * D; i += NTH) {
+    const int q = i / D, cc = i - q * D;
+    const int I = q >= 6 ? 3 : q >= 3 ? 2 : q >= 1 ? 1 : 0;
+    const int J = q - I * (I + 1) / 2;
+    F[i] = exp2f(fminf(G[16 * I * ldg + cc] - G[(16 * J + 15) * ldg + cc], 120.f));
+  }
+}
+
 // Scale the two 16-bit values packed in x by (f.x, f.y).
 template <typename T>
 __device__ __forceinline__ uint32_t scale_pair(uint32_t x, float2 f) {

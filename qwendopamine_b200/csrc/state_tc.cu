@@ -468,6 +468,26 @@ cudaError_t launch_fwd_state_tc(const FwdStateArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Address of the fault word on the current device (looked up once per
+// device; kernels of other translation units receive it as an argument).
+cudaError_t fault_word(unsigned int** ptr) {
+  constexpr int kMaxDev = 64;
+  static unsigned int* cache[kMaxDev] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < kMaxDev && cache[dev]) {
+    *ptr = cache[dev];
+    return cudaSuccess;
+  }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_gdn2_fault);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < kMaxDev) cache[dev] = static_cast<unsigned int*>(p);
+  *ptr = static_cast<unsigned int*>(p);
+  return cudaSuccess;
+}
+
 // Fault bits recorded by bounded waits that ran out (device of the current
 // context); `clear` resets them.
 cudaError_t read_fault_bits(unsigned int* bits, bool clear) {

@@ -33,6 +33,12 @@ def _require_cuda(*ts):
                 "chunk_gdn2: inputs must be CUDA tensors -- the B200 build has no CPU path")
 
 
+def _aligned16(*ts):
+    """The C ABI's 16-bit path moves rows with bulk copies and needs tensors
+    that start on a 16-byte boundary; copy the (rare) misaligned views."""
+    return tuple(t if t is None or t.data_ptr() % 16 == 0 else t.clone() for t in ts)
+
+
 def chunk_gdn2_fwd(q, k, v, g, b, w, scale, initial_state, output_final_state, tables,
                    use_qk_l2norm, keep_saved=True):
     """Run the forward; returns ``(o, final_state, saved)``.
@@ -43,6 +49,7 @@ def chunk_gdn2_fwd(q, k, v, g, b, w, scale, initial_state, output_final_state, t
     lib = N.load()
     B, T, H, K = q.shape
     V = v.shape[-1]
+    q, k, v, g, b, w = _aligned16(q, k, v, g, b, w)
     prob = _problem(H, K, V, q.dtype, use_qk_l2norm, scale, tables)
     nbytes = lib.gdn2_chunk_saved_bytes(prob)
     if nbytes == 0 and tables.n_chunks > 0:
@@ -64,6 +71,7 @@ def chunk_gdn2_bwd(q, k, v, g, b, w, saved, do, dht, scale, initial_state, table
     lib = N.load()
     B, T, H, K = q.shape
     V = v.shape[-1]
+    q, k, v, g, b, w, do = _aligned16(q, k, v, g, b, w, do)
     prob = _problem(H, K, V, q.dtype, use_qk_l2norm, scale, tables)
     nbytes = lib.gdn2_chunk_saved_bytes(prob)
     wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)

@@ -33,7 +33,7 @@ from typing import Callable
 import torch
 
 from .. import _native as N
-from .chunk_gdn2 import _require_cuda
+from .chunk_gdn2 import _aligned16, _require_cuda
 
 __all__ = ["chunk_gdn2_cp", "CPChunkGDN2Function", "gather_span_maps"]
 
@@ -67,6 +67,7 @@ class CPChunkGDN2Function(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, g, b, w, initial_state, scale, l2norm, rank, world, gather):
         lib = N.load()
+        q, k, v, g, b, w = _aligned16(q, k, v, g, b, w)
         B, T, H, K = q.shape
         V = v.shape[-1]
         dev = q.device
@@ -104,7 +105,7 @@ class CPChunkGDN2Function(torch.autograd.Function):
         prob = _problem(H, K, V, q.dtype, l2norm, scale, tables)
         st = N.stream_of(dev)
         sbytes = lib.gdn2_chunk_saved_bytes(prob)
-        do = do.to(q.dtype).contiguous()
+        (do,) = _aligned16(do.to(q.dtype).contiguous())
         last = rank == world - 1
         # Only the last rank's end state is the sequence's final state.
         dht_final = dht.float().contiguous() if (last and dht is not None) else None

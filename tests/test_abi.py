@@ -92,6 +92,19 @@ def test_null_pointers_and_short_buffers_are_rejected(lib):
     assert rc == N.ERR_WORKSPACE
 
 
+def test_misaligned_16bit_tensors_are_rejected(lib):
+    """The bf16 kernels move token rows with bulk async copies: tensors must
+    start on a 16-byte boundary (the Python wrappers copy misaligned views)."""
+    prob = _problem(K=64, V=64, dtype=1)
+    ok, odd = ctypes.c_void_p(0x1000), ctypes.c_void_p(0x1002)
+    big = 1 << 40
+    rc = lib.gdn2_chunk_fwd_intra(prob, ok, odd, ok, ok, ok, ok, ok, big, None)
+    assert rc == N.ERR_INVALID and b"16-byte" in lib.gdn2_last_error()
+    rc = lib.gdn2_chunk_bwd_intra(prob, ok, ok, ok, ok, ok, ok, ok, big, odd, *([ok] * 6), ok, big,
+                                  None)
+    assert rc == N.ERR_INVALID and b"16-byte" in lib.gdn2_last_error()
+
+
 def test_recurrent_argument_checks(lib):
     def rp(**kw):
         base = dict(B=2, T=1, H=2, HV=2, K=16, V=16, dtype=1, use_qk_l2norm=1, scale=0.25,

@@ -335,3 +335,27 @@ def test_ragged_lengths_16bit_forward_backward(cuda_device, T, KV):
                           norm_mode="fla")
     for n, r in zip((*NAMES, "h0"), ref):
         assert rel(gr[n], r) < TOL[torch.bfloat16], n
+
+
+def test_misaligned_16bit_views_give_the_same_result(cuda_device):
+    """Views that do not start on a 16-byte boundary are copied by the wrapper
+    before the bulk-copy kernels see them."""
+    from qwendopamine_b200 import chunk_gdn2
+
+    d = make_inputs(1, 100, 2, 64, 64, seed=17, dtype=torch.bfloat16)
+    x = to_dev(d, cuda_device, torch.bfloat16)
+
+    def shifted(t):
+        buf = torch.empty(t.numel() + 1, dtype=t.dtype, device=t.device)
+        v = buf[1:].view(t.shape)
+        v.copy_(t)
+        assert v.data_ptr() % 16 != 0
+        return v
+
+    args = [x[n] for n in NAMES]
+    o1, h1 = chunk_gdn2(*args, initial_state=x["h0"], output_final_state=True,
+                        use_qk_l2norm_in_kernel=True)
+    o2, h2 = chunk_gdn2(*(shifted(t) if n != "g" else t for n, t in zip(NAMES, args)),
+                        initial_state=x["h0"], output_final_state=True,
+                        use_qk_l2norm_in_kernel=True)
+    assert torch.equal(o1, o2) and torch.equal(h1, h2)
