@@ -73,6 +73,7 @@ struct Bwd16Layout {
   static_assert(kT2 + kChunk * LDC * 2 <= kEnd || kT2 + kChunk * LDC * 2 <= W, "layout");
   static_assert(oW % 16 == 0 && slot % 16 == 0, "alignment");
   static_assert(32 * LDT <= kChunk * LDS, "VN^T slice fits its region");
+  static_assert(3 * kChunk * LDK * 2 <= W, "gradient staging fits the work region");
 };
 
 template <typename T, int D>
@@ -489,6 +490,10 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   T* gdq = reinterpret_cast<T*>(a.dq) + offk;
   T* gdk = reinterpret_cast<T*>(a.dk) + offk;
   T* gdb = reinterpret_cast<T*>(a.db) + offk;
+  // staging tiles for coalesced stores (the scan area is dead after dg)
+  T* stq = reinterpret_cast<T*>(W);
+  T* stk = stq + kChunk * LDK;
+  T* stb = stk + kChunk * LDK;
   float pq[2] = {0.f, 0.f}, pk[2] = {0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < NTO; ++j)
@@ -546,11 +551,15 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
         oq[t] = vq;
         ok[t] = vk;
       }
-      *reinterpret_cast<uint32_t*>(gdq + (int64_t)r * ldk + cl) = pack2<T>(oq[0], oq[1]);
-      *reinterpret_cast<uint32_t*>(gdk + (int64_t)r * ldk + cl) = pack2<T>(ok[0], ok[1]);
-      *reinterpret_cast<uint32_t*>(gdb + (int64_t)r * ldk + cl) =
+      *reinterpret_cast<uint32_t*>(stq + r * LDK + cl) = pack2<T>(oq[0], oq[1]);
+      *reinterpret_cast<uint32_t*>(stk + r * LDK + cl) = pack2<T>(ok[0], ok[1]);
+      *reinterpret_cast<uint32_t*>(stb + r * LDK + cl) =
           pack2<T>(dkb[0][j][2 * hf], dkb[0][j][2 * hf + 1]);
     }
+  __syncthreads();
+  store_tile16<T, kChunk, D, NTH>(gdq, ldk, stq, LDK, len, K);
+  store_tile16<T, kChunk, D, NTH>(gdk, ldk, stk, LDK, len, K);
+  store_tile16<T, kChunk, D, NTH>(gdb, ldk, stb, LDK, len, K);
 }
 
 template <typename T, int D>

@@ -54,6 +54,8 @@ struct Fwd16Layout {
   static constexpr int R = rEndScores > rEndInv ? rEndScores : rEndInv;
   static constexpr size_t bytes = (size_t)oR + R;
   static_assert(rT + 3 * 16 * 20 * 4 <= rAkk, "T tiles overlap Akk");
+  // W / U staging: W over the dead Inv / T tiles below sA16, U past sA16
+  static_assert(tile16 <= rA16 && rEndInv + tile16 <= R, "W / U staging tiles");
   static_assert(oR % 16 == 0 && rAkk % 16 == 0 && rA16 % 16 == 0, "alignment");
 };
 
@@ -345,10 +347,10 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
     }
     __syncthreads();
 
-    // ---- W = A E, U = A Z (owner tiles 16 x D/4) -----------------------------------
+    // ---- W = A E, U = A Z (owner tiles 16 x D/4), staged for coalesced stores
     {
-      T* gW = reinterpret_cast<T*>(a.saved + a.L.w) + ch * tileK;
-      T* gU = reinterpret_cast<T*>(a.saved + a.L.u) + ch * tileV;
+      T* stW = reinterpret_cast<T*>(R + L::rInv);  // Inv is dead after the pack
+      T* stU = reinterpret_cast<T*>(R + L::rEndInv);  // past sA16 (read by both products)
       float acc[1][NTO][4];
       acc_zero(acc);
       warp_mma16<1, NTO, true, false>(acc, sA16, LDC, 16 * wr, sw, LDK, wc * DQ, kChunk);
@@ -357,9 +359,8 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
-          if (cl < K)
-            *reinterpret_cast<uint32_t*>(gW + r * K + cl) =
-                pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
+          *reinterpret_cast<uint32_t*>(stW + r * LDK + cl) =
+              pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
         }
       acc_zero(acc);
       warp_mma16<1, NTO, true, false>(acc, sA16, LDC, 16 * wr, sv, LDK, wc * DQ, kChunk);
@@ -368,10 +369,14 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
-          if (cl < V)
-            *reinterpret_cast<uint32_t*>(gU + r * V + cl) =
-                pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
+          *reinterpret_cast<uint32_t*>(stU + r * LDK + cl) =
+              pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
         }
+      __syncthreads();
+      store_tile16<T, kChunk, D, NTH>(reinterpret_cast<T*>(a.saved + a.L.w) + ch * tileK, K, stW,
+                                      LDK, kChunk, K);
+      store_tile16<T, kChunk, D, NTH>(reinterpret_cast<T*>(a.saved + a.L.u) + ch * tileV, V, stU,
+                                      LDK, kChunk, V);
     }
     __syncthreads();
     if (next < n_items) issue_vw(next);  // v, w (now E, Z) are dead

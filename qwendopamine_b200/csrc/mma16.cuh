@@ -288,6 +288,27 @@ __device__ __forceinline__ uint32_t scale_pair(uint32_t x, float2 f) {
   return pack2<T>(to_f<T>(v[0]) * f.x, to_f<T>(v[1]) * f.y);
 }
 
+// Copy a ROWS x COLS 16-bit tile from shared memory (row stride lds) to
+// global memory (row stride ldg elements, 16-byte aligned rows): rows <
+// nrows, columns < ncols (a multiple of 8).  Each thread moves 16 bytes, so a
+// warp instruction writes whole rows instead of fragment-shaped pieces.
+template <typename T, int ROWS, int COLS, int NTH>
+__device__ __forceinline__ void store_tile16(T* g, int64_t ldg, const T* s, int lds, int nrows,
+                                             int ncols) {
+  constexpr int CPR = COLS / 8;
+  constexpr int TOTAL = ROWS * CPR;
+#pragma unroll
+  for (int it = 0; it < (TOTAL + NTH - 1) / NTH; ++it) {
+    const int idx = threadIdx.x + it * NTH;
+    if (idx < TOTAL) {
+      const int r = idx / CPR, c = (idx - r * CPR) * 8;
+      if (r < nrows && c < ncols)
+        *reinterpret_cast<uint4*>(g + (int64_t)r * ldg + c) =
+            *reinterpret_cast<const uint4*>(s + r * lds + c);
+    }
+  }
+}
+
 // Same for an fp32 vector of n floats (n a multiple of 4), zero beyond n.
 template <int N, int NTH>
 __device__ __forceinline__ void cp_vec32(float* s, const float* g, int n) {
