@@ -69,9 +69,11 @@ PHASE_FLOPS = {
     "bwd_state": 6 * K * V + 2 * C * V,
     "bwd_intra": 6 * K * V + 6 * C * V + 12 * C * K + 4 * C * C,
 }
-# DRAM traffic (read + write bytes) per launch of the dominant kernel from the
-# ncu capture summarised under profiles/ (None until captured).
-NCU_TRAFFIC_PER_TOKEN_HEAD = None
+# DRAM traffic (read + write) of the dominant kernel, k_bwd_intra16, per
+# token-head, from one ncu --set full capture at batch 2 (701.3 MB over
+# 131,072 token-heads; traffic grows with token-heads, so it scales to a
+# config-1 launch).  Summary under profiles/.
+NCU_TRAFFIC_PER_TOKEN_HEAD = 5350.4
 
 
 def peaks():
@@ -312,7 +314,8 @@ def run_b200(args, world, rank, local):
         }
     dom = max(phases, key=lambda p: phase_ms[p])
     ach = PHASE_BYTES[dom] * th / (phase_ms[dom] / 1e3) / 1e9
-    traffic = (NCU_TRAFFIC_PER_TOKEN_HEAD * th if NCU_TRAFFIC_PER_TOKEN_HEAD else None)
+    traffic = (round(NCU_TRAFFIC_PER_TOKEN_HEAD * th)
+               if NCU_TRAFFIC_PER_TOKEN_HEAD and dom == "bwd_intra" else None)
     cpu = cpu_baseline() if world == 1 else None
     line = {
         "metric": "gdn2 fwd+bwd tokens/s (BASELINE config 1)",
