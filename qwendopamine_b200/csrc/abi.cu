@@ -23,6 +23,8 @@ template <typename T, int D> cudaError_t launch_bwd_intra16(const BwdIntraArgs&,
 template <typename T, int D> cudaError_t launch_fwd_intra16(const FwdIntraArgs&, cudaStream_t);
 bool fwd_state_tc_ok(const FwdStateArgs&, int dtype_bf16);
 cudaError_t launch_fwd_state_tc(const FwdStateArgs&, cudaStream_t);
+bool bwd_state_tc_ok(const BwdStateArgs&, int dtype_bf16);
+cudaError_t launch_bwd_state_tc(const BwdStateArgs&, cudaStream_t);
 cudaError_t read_fault_bits(unsigned int* bits, bool clear);
 cudaError_t fault_word(unsigned int** ptr);
 }  // namespace gdn2
@@ -179,6 +181,7 @@ cudaError_t fwd_state_dispatch(const gdn2_chunk_problem* p, const FwdStateArgs& 
 
 cudaError_t bwd_state_dispatch(const gdn2_chunk_problem* p, const BwdStateArgs& a, cudaStream_t st) {
   const int bucket = head_bucket(p->K, p->V);
+  if (bwd_state_tc_ok(a, p->dtype == GDN2_DTYPE_BF16)) return launch_bwd_state_tc(a, st);
   if (use16(p)) {
     return run_state16<__nv_bfloat16>(a, bucket, p->V, p->seqs.n_seqs, p->H, st);
   }
@@ -377,6 +380,7 @@ int gdn2_chunk_bwd_state(const gdn2_chunk_problem* p, const void* saved, size_t 
   s.ws = static_cast<unsigned char*>(workspace);
   s.BL = BL;
   s.prescan = 0;
+  s.total_rows = p->seqs.total_tokens;
   cudaError_t e = bwd_state_dispatch(p, s, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_bwd_state");
 }
@@ -512,6 +516,7 @@ int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t s
   s.ws = nullptr;
   s.BL = bwd_layout_of(p);
   s.prescan = 1;
+  s.total_rows = p->seqs.total_tokens;
   cudaError_t e = bwd_state_dispatch(p, s, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_bwd_prescan");
 }

@@ -4,6 +4,7 @@
 // (chunk_bwd.cu), organised so that almost nothing waits on memory:
 //   * one cp.async round trip brings q, k, b (16-bit), g (fp32) and A;
 //   * the value side streams 32-column slices of h, dh, dO, VN, dVN, v, w
+//     (VN and dVN are stored value-major, [V][64], by the bf16 state passes)
 //     through a cp.async double buffer while the previous slice computes
 //     (dQg = dO h^T, dKd = VN dh^T, dW = -dVN h^T, dAqk = dO VN^T,
 //      dA = dVN (w v)^T, dZ = A^T dVN -> dv, dw);
@@ -29,7 +30,7 @@ struct Bwd16Layout {
   static constexpr int LDG = D + 4;      // fp32 64 x D tiles
   static constexpr int LDC = kChunk + 8; // 16-bit 64 x 64 tiles
   static constexpr int LDS = 32 + 8;     // 16-bit value slices
-  static constexpr int LDT = kChunk + 8; // 16-bit VN^T slice [32][64]
+  static constexpr int LDT = kChunk + 8; // 16-bit VN^T / dVN^T slices [32][64]
   // persistent region (bytes)
   static constexpr int oQ = 0;
   static constexpr int oK = oQ + kChunk * LDK * 2;
@@ -129,7 +130,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vDO), LDS, gdo + v0, ldv, len, nv);
     cp_tile16<T, 32, kChunk, NTH>(slotp(s, L::vVN), LDT, gvn + (size_t)v0 * kChunk, kChunk, nv,
                                   kChunk);
-    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vDVN), LDS, gdvn + v0, V, kChunk, nv);
+    cp_tile16<T, 32, kChunk, NTH>(slotp(s, L::vDVN), LDT, gdvn + (size_t)v0 * kChunk, kChunk, nv,
+                                  kChunk);
     cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vV), LDS, gv + v0, ldv, len, nv);
     cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vWg), LDS, gw + v0, ldv, len, nv);
   };
@@ -196,14 +198,14 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     __syncthreads();
     warp_mma16<1, NTO, true, true>(accQ, dos, LDS, 16 * wr, hs, LDS, wc * DQ, 32);
     warp_mma16<1, NTO, false, true>(accKd, vns, LDT, 16 * wr, dhs, LDS, wc * DQ, 32);
-    warp_mma16<1, NTO, true, true>(accW, dvns, LDS, 16 * wr, hs, LDS, wc * DQ, 32);
+    warp_mma16<1, NTO, false, true>(accW, dvns, LDT, 16 * wr, hs, LDS, wc * DQ, 32);
     warp_mma16<1, 2, true, false>(accAqk, dos, LDS, 16 * wr, vns, LDT, 16 * wc, 32);
-    warp_mma16<1, 2, true, true>(accDA, dvns, LDS, 16 * wr, sZ, LDS, 16 * wc, 32);
+    warp_mma16<1, 2, false, true>(accDA, dvns, LDT, 16 * wr, sZ, LDS, 16 * wc, 32);
     if (warp < 8) {
       float accZ[1][2][4];
       acc_zero(accZ);
       const int zm = 16 * (warp & 3), zn = 16 * (warp >> 2);
-      warp_mma16<1, 2, false, false>(accZ, sA, LDC, zm, dvns, LDS, zn, kChunk);
+      warp_mma16<1, 2, false, true>(accZ, sA, LDC, zm, dvns, LDT, zn, kChunk);
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll

@@ -46,6 +46,7 @@ struct BwdStateArgs {
   unsigned char* ws;
   BwdLayout BL;
   int prescan;        // 1: write nothing per chunk, only the span-start gradient
+  int64_t total_rows; // token rows of dout (bounds of its TMA view)
 };
 
 struct BwdIntraArgs {

@@ -330,7 +330,8 @@ __host__ __device__ inline SavedLayout saved_layout(int64_t n_chunks, int H, int
 }
 
 // Backward workspace per (chunk, head):  dh : [K][V] (T)  gradient w.r.t. the
-// state leaving the chunk;  dVN : [64][V] (T).
+// state leaving the chunk;  dVN : [64][V] (T), stored transposed ([V][64]) by
+// the bf16 tensor-core path, like VN.
 struct BwdLayout {
   size_t dh, dvn, total;
 };

@@ -357,8 +357,10 @@ __global__ void __launch_bounds__(kThreads16, 1) k_bwd_state16(BwdStateArgs a) {
           const int cl = wn1 + 8 * j + 2 * tig;
           const float x0 = acc[0][j][2 * hf], x1 = acc[0][j][2 * hf + 1];
           *reinterpret_cast<uint32_t*>(sNDVN + r * LDV + cl) = pack2<T>(-x0, -x1);
-          if (!a.prescan && v0 + cl < V)
-            *reinterpret_cast<uint32_t*>(gdvn + (size_t)r * V + v0 + cl) = pack2<T>(x0, x1);
+          if (!a.prescan && v0 + cl < V) {  // dVN^T: [V][64]
+            gdvn[(size_t)(v0 + cl) * kChunk + r] = from_f<T>(x0);
+            if (v0 + cl + 1 < V) gdvn[(size_t)(v0 + cl + 1) * kChunk + r] = from_f<T>(x1);
+          }
         }
     }
     __syncthreads();

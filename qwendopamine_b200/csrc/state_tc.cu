@@ -403,6 +403,323 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Backward state pass, reverse over the chunks of one (sequence, head):
+//   dVN = Aqk^T dO + Kd dh,   dh <- gl * dh + Qg^T dO - W^T dVN
+// TMEM: cols [0,128) dh (lane = key row k), cols [128,192) dVN^T (lane = v).
+// dO arrives by TMA through a 3-D view [rows][H][V] (rows of a partial chunk
+// past the sequence's end are zeroed in shared memory before use).  Per
+// chunk: checkpoint dh (bf16, the gradient of the state leaving the chunk)
+// while  dVN^T = dO^T Aqk + dh^T Kd^T  runs (A = dO tile, MN-major; B = Aqk,
+// MN-major / A = bf16 dh, MN-major; B = Kd, K-major); warps store -dVN^T
+// (K-major) for  dh += Qg^T dO + W^T (-dVN)  (A = Qg / W tiles, MN-major;
+// B = dO, MN-major / -dVN^T, K-major) and copy dVN^T out while it runs; then
+// the new dh becomes the next operand, scaled in TMEM by the next chunk's
+// 2^G_last.  Same rounding points as k_bwd_state16.
+constexpr uint32_t kOffDO = kOffU;  // dO takes U's place: 2 swizzled boxes
+constexpr uint32_t kIdOA = tc::idesc_bf16(128, 64, 1, 1);   // dO^T Aqk
+constexpr uint32_t kIdQO = tc::idesc_bf16(128, 128, 1, 1);  // Qg^T dO
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    k_bwd_state_tc(BwdStateArgs a, const __grid_constant__ CUtensorMap mW,
+                   const __grid_constant__ CUtensorMap mQg, const __grid_constant__ CUtensorMap mKd,
+                   const __grid_constant__ CUtensorMap mAqk, const __grid_constant__ CUtensorMap mDO) {
+  using T = __nv_bfloat16;
+  constexpr int K = 128, V = 128;
+  extern __shared__ unsigned char smraw[];
+  unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kOffBar);  // [2]
+  uint64_t* mma1 = full + 2;
+  uint64_t* mma2 = full + 3;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(full + 4);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+  unsigned char* sH = sm + kOffH;    // bf16 dh [k][v], MN-major
+  unsigned char* sVN = sm + kOffVN;  // bf16 -dVN^T [v][t], K-major
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int row = quad * 32 + lane;
+  const int H = a.H;
+  const int nh = blockIdx.x, n = nh / H, h = nh - n * H;
+  const int c_begin = a.seqs.coff[n], c_end = a.seqs.coff[n + 1];
+  const int64_t bos = a.seqs.cu[n], eos = a.seqs.cu[n + 1];
+  const float* dht = a.dht ? a.dht + (int64_t)nh * K * V : nullptr;
+  float* dh0 = a.dh0 ? a.dh0 + (int64_t)nh * K * V : nullptr;
+
+  if (c_begin >= c_end) {  // empty sequence: the gradient passes through
+    if (dh0)
+      for (int i = tid; i < K * V; i += kTcThreads) dh0[i] = dht ? dht[i] : 0.f;
+    return;
+  }
+
+  if (tid == 0) {
+    tc::mbar_init(&full[0], 1);
+    tc::mbar_init(&full[1], 1);
+    tc::mbar_init(mma1, 1);
+    tc::mbar_init(mma2, 1);
+    *sAbort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(sTmem, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const uint32_t tlane = tmem + ((uint32_t)(quad * 32) << 16);
+
+  // chunk c sits in slot (c_end - 1 - c) & 1
+  int next_issue = c_end - 1;  // next chunk to request (thread 0), counting down
+  int mma1_commits = 0, mma2_commits = 0;
+  auto issue = [&](int c) {
+    const int slot = (c_end - 1 - c) & 1;
+    unsigned char* p = sm + slot * kSlotBytes;
+    const size_t ch = (size_t)c * H + h;
+    const int y = (int)(ch * kChunk);
+    const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
+    tc::mbar_expect_tx(&full[slot], kTxBytes);
+    tc::tma_load_2d(p + kOffW, &mW, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kOffW + kBox, &mW, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kOffQg, &mQg, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kOffQg + kBox, &mQg, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kOffKd, &mKd, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kOffKd + kBox, &mKd, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kOffAqk, &mAqk, 0, y, &full[slot]);
+    tc::tma_load_3d(p + kOffDO, &mDO, 0, h, (int)cp.row0, &full[slot]);
+    tc::tma_load_3d(p + kOffDO + kBox, &mDO, 64, h, (int)cp.row0, &full[slot]);
+    tc::bulk_load(p + kOffGl, a.saved + a.L.gl + ch * K * sizeof(float), kGlBytes, &full[slot]);
+    next_issue = c - 1;
+  };
+  if (tid == 0) {
+    issue(c_end - 1);
+    if (c_end - 2 >= c_begin) issue(c_end - 2);
+  }
+
+  auto emit_state = [&](const float (&s)[64]) {
+    unsigned char* srow = sH + half * kHalfH + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      uint4 x;
+      x.x = pack2<T>(s[8 * q + 0], s[8 * q + 1]);
+      x.y = pack2<T>(s[8 * q + 2], s[8 * q + 3]);
+      x.z = pack2<T>(s[8 * q + 4], s[8 * q + 5]);
+      x.w = pack2<T>(s[8 * q + 6], s[8 * q + 7]);
+      st_shared_v4(srow + ((q ^ (row & 7)) << 4), x);
+    }
+  };
+  auto scale_store = [&](float (&s)[64], int slot) {
+    const float gl = reinterpret_cast<const float*>(sm + slot * kSlotBytes + kOffGl)[row];
+    float lo[32], hi[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      lo[i] = s[i] * gl;
+      hi[i] = s[32 + i] * gl;
+    }
+    tc::tmem_st32(tlane + kColH + 64 * half, lo);
+    tc::tmem_st32(tlane + kColH + 64 * half + 32, hi);
+  };
+  auto copy_ckpt = [&](int c) {  // sH -> dh of chunk c, [K][V]
+    T* gh = reinterpret_cast<T*>(a.ws + a.BL.dh) + ((size_t)c * H + h) * (size_t)K * V;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int k = idx >> 4, ci = idx & 15;
+      const uint4 x = ld_shared_v4(sH + (ci >> 3) * kHalfH + (k >> 3) * 1024 + (k & 7) * 128 +
+                                   (((ci & 7) ^ (k & 7)) << 4));
+      *reinterpret_cast<uint4*>(gh + (size_t)k * V + 8 * ci) = x;
+    }
+  };
+  auto copy_dvn = [&](int c) {  // -sVN -> dVN^T of chunk c, [V][64]
+    T* gv = reinterpret_cast<T*>(a.ws + a.BL.dvn) + ((size_t)c * H + h) * (size_t)kChunk * V;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int v = idx >> 3, ci = idx & 7;
+      uint4 x = ld_shared_v4(sVN + (v >> 3) * 1024 + (v & 7) * 128 + ((ci ^ (v & 7)) << 4));
+      x.x ^= 0x80008000u;  // flip the bf16 signs back
+      x.y ^= 0x80008000u;
+      x.z ^= 0x80008000u;
+      x.w ^= 0x80008000u;
+      *reinterpret_cast<uint4*>(gv + (size_t)v * kChunk + 8 * ci) = x;
+    }
+  };
+
+  // ---- initial gradient -----------------------------------------------------
+  {
+    const bool ok = tc::warp_wait(&full[0], 0);
+    if (ok) {
+      float s[64];
+      if (dht) {
+        const float4* src = reinterpret_cast<const float4*>(dht + (size_t)row * V + 64 * half);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 x = src[i];
+          s[4 * i] = x.x;
+          s[4 * i + 1] = x.y;
+          s[4 * i + 2] = x.z;
+          s[4 * i + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s[i] = 0.f;
+      }
+      emit_state(s);
+      scale_store(s, 0);
+    } else if (lane == 0) {
+      *sAbort = 1;
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+  }
+
+  int c = c_end - 1;
+  if (!*sAbort) {
+    for (; c >= c_begin; --c) {
+      const int i = c_end - 1 - c, slot = i & 1;
+      unsigned char* p = sm + slot * kSlotBytes;
+      const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
+      const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
+
+      // 0. a partial chunk's dO rows past the sequence end hold the next
+      //    sequence's tokens: zero them before any product reads the tile
+      if (cp.len < kChunk) {
+        const bool ok = tc::warp_wait(&full[slot], par_full);
+        if (ok) {
+          for (int e = tid; e < (kChunk - cp.len) * 16; e += kTcThreads) {
+            const int r = cp.len + (e >> 4), bx = (e >> 3) & 1, ci = e & 7;
+            st_shared_v4(p + kOffDO + bx * kBox + r * 128 + ci * 16, make_uint4(0u, 0u, 0u, 0u));
+          }
+        } else if (lane == 0) {
+          *sAbort = 1;
+        }
+        tc::fence_async_smem();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+
+      // 1. dVN^T = dO^T Aqk + dh^T Kd^T;  meanwhile dh is checkpointed
+      if (tid == 0) {
+        if (!tc::mbar_wait(&full[slot], par_full)) {
+          *sAbort = 1;
+        } else {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tc::umma_bf16(tmem + kColVN, desc_mn(p + kOffDO + j * 2048, kBox),
+                          desc_mn(p + kOffAqk + j * 2048, kBox), kIdOA, j > 0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::umma_bf16(tmem + kColVN, desc_mn(sH + j * 2048, kHalfH),
+                          desc_k(p + kOffKd + (j >> 2) * kBox + (j & 3) * 32), kIdHW, 1);
+          tc::umma_commit(mma1);
+          ++mma1_commits;
+        }
+      }
+      copy_ckpt(c);
+      // 2. -dVN^T -> bf16 operand tile
+      {
+        const bool ok = tc::warp_wait(mma1, par_mma);
+        if (ok) {
+          tc::tc_fence_after();
+          uint32_t x[32];
+          tc::tmem_ld32(tlane + kColVN + 32 * half, x);
+          tc::tmem_wait_ld();
+          unsigned char* vrow = sVN + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 y;
+            y.x = pack2<T>(-__uint_as_float(x[8 * q + 0]), -__uint_as_float(x[8 * q + 1]));
+            y.y = pack2<T>(-__uint_as_float(x[8 * q + 2]), -__uint_as_float(x[8 * q + 3]));
+            y.z = pack2<T>(-__uint_as_float(x[8 * q + 4]), -__uint_as_float(x[8 * q + 5]));
+            y.w = pack2<T>(-__uint_as_float(x[8 * q + 6]), -__uint_as_float(x[8 * q + 7]));
+            st_shared_v4(vrow + (((4 * half + q) ^ (row & 7)) << 4), y);
+          }
+        } else if (lane == 0) {
+          *sAbort = 1;
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+      // 3. dh += Qg^T dO + W^T (-dVN);  meanwhile dVN^T leaves
+      if (tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_bf16(tmem + kColH, desc_mn(p + kOffQg + j * 2048, kBox),
+                        desc_mn(p + kOffDO + j * 2048, kBox), kIdQO, 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_bf16(tmem + kColH, desc_mn(p + kOffW + j * 2048, kBox), desc_k(sVN + j * 32),
+                        kIdKV, 1);
+        tc::umma_commit(mma2);
+        ++mma2_commits;
+      }
+      copy_dvn(c);
+      // 4. new dh -> bf16 operand tile (the next checkpoint), scaled in place
+      //    by the next chunk's 2^G_last; or dh0
+      {
+        const bool has_next = c - 1 >= c_begin;
+        bool ok = tc::warp_wait(mma2, par_mma);
+        if (ok && has_next) ok = tc::warp_wait(&full[slot ^ 1], ((i + 1) >> 1) & 1);
+        if (ok) {
+          tc::tc_fence_after();
+          float s[64];
+          {
+            uint32_t lo[32], hi[32];
+            tc::tmem_ld32(tlane + kColH + 64 * half, lo);
+            tc::tmem_ld32(tlane + kColH + 64 * half + 32, hi);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              s[e] = __uint_as_float(lo[e]);
+              s[32 + e] = __uint_as_float(hi[e]);
+            }
+          }
+          if (has_next) {
+            emit_state(s);
+            scale_store(s, slot ^ 1);
+          } else if (dh0) {
+            float4* dst = reinterpret_cast<float4*>(dh0 + (size_t)row * V + 64 * half);
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              dst[e] = make_float4(s[4 * e], s[4 * e + 1], s[4 * e + 2], s[4 * e + 3]);
+          }
+        } else if (lane == 0) {
+          *sAbort = 1;
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+      if (tid == 0 && c - 2 >= c_begin) issue(c - 2);
+    }
+  }
+
+  // ---- teardown ---------------------------------------------------------------
+  const bool aborted = *sAbort != 0;
+  if (aborted && tid == 0) {
+    for (int j = c; j > next_issue; --j) {
+      const int ij = c_end - 1 - j;
+      tc::mbar_wait(&full[ij & 1], (ij >> 1) & 1);
+    }
+    if (mma1_commits > 0) tc::mbar_wait(mma1, (mma1_commits - 1) & 1);
+    if (mma2_commits > 0) tc::mbar_wait(mma2, (mma2_commits - 1) & 1);
+    atomicOr(&g_gdn2_fault, 1u);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 // ---- host side -----------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -437,7 +754,52 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, u
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D bf16 map over token rows [rows][H][V] (dO): box 64 columns x 1 head x
+// 64 rows, 128-byte swizzle.
+bool make_map_rows(CUtensorMap* m, const void* base, uint64_t V, uint64_t H, uint64_t rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {V, H, rows};
+  cuuint64_t strides[2] = {V * 2, H * V * 2};
+  cuuint32_t box[3] = {64, 1, 64};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
+
+// True when k_bwd_state_tc can serve the problem (bf16, K = V = 128, no
+// pre-scan, 16-byte aligned buffers, TMA-addressable rows).
+bool bwd_state_tc_ok(const BwdStateArgs& a, int dtype_bf16) {
+  if (!dtype_bf16 || a.K != 128 || a.V != 128 || a.prescan || !a.dout || !a.ws) return false;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a.saved) | reinterpret_cast<uintptr_t>(a.ws) |
+                       reinterpret_cast<uintptr_t>(a.dout) | reinterpret_cast<uintptr_t>(a.dht) |
+                       reinterpret_cast<uintptr_t>(a.dh0);
+  if ((al & 15) != 0) return false;
+  if ((int64_t)a.seqs.n_chunks * a.H * kChunk >= (int64_t)1 << 31) return false;
+  if (a.total_rows <= 0 || a.total_rows >= (int64_t)1 << 31) return false;
+  return encode_fn() != nullptr;
+}
+
+cudaError_t launch_bwd_state_tc(const BwdStateArgs& a, cudaStream_t st) {
+  const uint64_t rows = (uint64_t)a.seqs.n_chunks * a.H * kChunk;
+  CUtensorMap mW, mQg, mKd, mAqk, mDO;
+  if (!make_map(&mW, a.saved + a.L.w, 128, rows, 64, true) ||
+      !make_map(&mQg, a.saved + a.L.qg, 128, rows, 64, true) ||
+      !make_map(&mKd, a.saved + a.L.kd, 128, rows, 64, true) ||
+      !make_map(&mAqk, a.saved + a.L.aqk, 64, rows, 64, true) ||
+      !make_map_rows(&mDO, a.dout, 128, (uint64_t)a.H, (uint64_t)a.total_rows))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(k_bwd_state_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int grid = a.seqs.n_seqs * a.H;
+  if (grid == 0) return cudaSuccess;
+  k_bwd_state_tc<<<grid, kTcThreads, kSmemBytes, st>>>(a, mW, mQg, mKd, mAqk, mDO);
+  return cudaGetLastError();
+}
 
 // True when k_fwd_state_tc can serve the problem (bf16, K = V = 128, no
 // pre-scan, 16-byte aligned saved buffer, tile rows addressable by TMA).

@@ -88,3 +88,38 @@ def test_tc_state_batched_shapes(cuda_device, B, T, H):
     assert rel(o, ro) < TOL[BF]
     assert rel(ht, rh) < TOL[BF]
     assert _fault_word() == 0
+
+
+def test_tc_state_backward_varlen_ragged_and_empty(cuda_device):
+    """Backward state pass on tcgen05: packed sequences with partial last
+    chunks (whose dO rows past the end belong to the next sequence), an empty
+    and a single-token sequence; gradients per sequence against the oracle."""
+    from qwendopamine_b200 import chunk_gdn2
+
+    _fault_word()
+    cu = [0, 1, 64, 129, 129, 300, 364, 500]
+    N, H, K = len(cu) - 1, 2, 128
+    d = make_inputs(1, cu[-1], H, K, K, seed=43, dtype=BF, h0=False)
+    gen = torch.Generator().manual_seed(9)
+    h0 = torch.randn(N, H, K, K, generator=gen) * 0.1
+    do = torch.randn(1, cu[-1], H, K, generator=gen).bfloat16().float()
+    dht = torch.randn(N, H, K, K, generator=gen)
+    x = to_dev(d, cuda_device, BF)
+    leaves = {n: x[n].clone().requires_grad_() for n in NAMES}
+    h0d = h0.to(cuda_device).requires_grad_()
+    o, ht = chunk_gdn2(*(leaves[n] for n in NAMES), initial_state=h0d, output_final_state=True,
+                       use_qk_l2norm_in_kernel=True,
+                       cu_seqlens=torch.tensor(cu, device=cuda_device))
+    ((o.float() * do.to(cuda_device)).sum() + (ht * dht.to(cuda_device)).sum()).backward()
+    for s in range(N):
+        a_, e_ = cu[s], cu[s + 1]
+        if e_ == a_:
+            assert torch.equal(h0d.grad[s].cpu(), dht[s]), "empty sequence: dh0 = dht"
+            continue
+        sl = [t[:, a_:e_].double().numpy() for t in (d[n] for n in NAMES)]
+        ref = O.recurrent_bwd(*sl, do[:, a_:e_].numpy(), h0[s:s + 1].numpy(),
+                              dht[s:s + 1].numpy(), norm_mode="fla")
+        for n, r in zip(NAMES, ref):
+            assert rel(leaves[n].grad[:, a_:e_], r) < TOL[BF], (s, n)
+        assert rel(h0d.grad[s:s + 1], ref[6]) < TOL[BF], (s, "h0")
+    assert _fault_word() == 0
