@@ -320,6 +320,7 @@ int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
   a.saved = static_cast<unsigned char*>(saved);
   a.L = L;
+  a.total_rows = p->seqs.total_tokens;
   cudaError_t e = fault_word(&a.fault);
   if (e != cudaSuccess) return cuda_fail(e, "gdn2_chunk_fwd_intra");
   e = fwd_intra_dispatch(p, a, (cudaStream_t)stream);

@@ -250,9 +250,9 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   for (int i = tid; i < kChunk * (D / 2); i += NTH) {
     const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
     const float e0 = to_f<T>(sb[r * LDK + cc]) * to_f<T>(sk[r * LDK + cc]) * rk[r] *
-                     exp2f(sG[r * LDG + cc]);
+                     fast_exp2(sG[r * LDG + cc]);
     const float e1 = to_f<T>(sb[r * LDK + cc + 1]) * to_f<T>(sk[r * LDK + cc + 1]) * rk[r] *
-                     exp2f(sG[r * LDG + cc + 1]);
+                     fast_exp2(sG[r * LDG + cc + 1]);
     *reinterpret_cast<uint32_t*>(sE + r * LDK + cc) = pack2<T>(e0, e1);
   }
   __syncthreads();
@@ -308,13 +308,13 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     for (int e = 0; e < 4; ++e) {
       const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
       const float G = sG[r * LDG + cl], GL = sG[(kChunk - 1) * LDG + cl];
-      const float gam = exp2f(G);
+      const float gam = fast_exp2(G);
       const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
       const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
       const float bb = to_f<T>(sb[r * LDK + cl]);
       dq[0][j][e] = scale * gam * dq[0][j][e];
       dkb[0][j][e] = gam * dkb[0][j][e];
-      const float kd = dkn[0][j][e] * exp2f(GL - G);
+      const float kd = dkn[0][j][e] * fast_exp2(GL - G);
       dkn[0][j][e] = kd;
       X[j][e] = kn * kd;
       dG[0][j][e] = qn * dq[0][j][e] + bb * kn * dkb[0][j][e];
@@ -339,8 +339,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
       const float G = sG[r * LDG + cc + t];
-      const float f = exp2f(G - sG[rb * LDG + cc + t]);
-      const float fe = exp2f(sG[re * LDG + cc + t] - G);
+      const float f = fast_exp2(G - sG[rb * LDG + cc + t]);
+      const float fe = fast_exp2(sG[re * LDG + cc + t] - G);
       const float kn = to_f<T>(sk[r * LDK + cc + t]) * rk[r];
       q2[t] = scale * to_f<T>(sq[r * LDK + cc + t]) * rq[r] * f;
       kb2[t] = to_f<T>(sb[r * LDK + cc + t]) * kn * f;
@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
-          const float f = exp2f(sG[r * LDG + cl] - sG[(16 * I) * LDG + cl]);
+          const float f = fast_exp2(sG[r * LDG + cl] - sG[(16 * I) * LDG + cl]);
           const float xq = scale * tq[0][j][e] * f, xk = tk[0][j][e] * f;
           const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
           const float kb = to_f<T>(sb[r * LDK + cl]) * to_f<T>(sk[r * LDK + cl]) * rk[r];
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
-        const float fe = exp2f(sG[(16 * J + 15) * LDG + cl] - sG[r * LDG + cl]);
+        const float fe = fast_exp2(sG[(16 * J + 15) * LDG + cl] - sG[r * LDG + cl]);
         const float y = ys[j][e] * fe;
         const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
         dkn[0][j][e] += y;

@@ -20,6 +20,7 @@ struct FwdIntraArgs {
   unsigned char* saved;
   SavedLayout L;
   unsigned int* fault;  // device fault word (bounded waits that ran out)
+  int64_t total_rows;   // token rows of q, k, v, g, b, w (bounds of their TMA views)
 };
 
 struct FwdStateArgs {

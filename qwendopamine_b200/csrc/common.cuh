@@ -244,6 +244,15 @@ __device__ __forceinline__ void col_cumsum64(float* s, int lds, float mul, float
   __syncthreads();
 }
 
+// 2^x with the hardware base-2 exponential (PTX ex2.approx.ftz.f32: relative
+// error about 2^-22; results below 2^-126 flush to zero, far below what the
+// 16-bit operands it scales can hold).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);

@@ -1,7 +1,9 @@
 // fwd16.cu -- intra-chunk forward solve for bf16 inputs.
 //
-// One CTA of 16 warps per (chunk, head); same mathematics as k_fwd_intra
-// (chunk_fwd.cu).  One cp.async round trip brings q, k, b, v, w and g.  After
+// Persistent: one CTA of 16 warps per SM walks (chunk, head) items; same
+// mathematics as k_fwd_intra (chunk_fwd.cu).  q, k, b, g and v, w arrive as
+// TMA boxes (128-byte swizzled, read through swz<>) requested by one thread
+// for the next item as soon as the current item is done with them.  After
 // the decay scan and the row norms, a single elementwise pass writes Qg and
 // Kd, forms E = b k_n 2^G and Z = v w in place of w and v, and builds the
 // 16-bit score operands with per-16-row-block references
@@ -18,28 +20,40 @@
 #include "chunk_args.cuh"
 #include "inverse.cuh"
 #include "mma16.cuh"
+#include "tc.cuh"
 
 namespace gdn2 {
 
 constexpr int kThreadsF16 = 512;
 
+// Byte offset of element (r, c) of a 64-row tile of EB-byte elements stored
+// as TMA boxes of 128 bytes x 64 rows with the 128-byte swizzle (box b holds
+// bytes [128 b, 128 b + 128) of every row; 16-byte chunks XOR-ed with r % 8).
+template <int EB>
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  const uint32_t byte = (uint32_t)c * EB;
+  return (byte >> 7) * 8192u + (uint32_t)r * 128u + ((((byte >> 4) & 7u) ^ (uint32_t)(r & 7)) << 4) +
+         (byte & 15u);
+}
+
 template <int D>
 struct Fwd16Layout {
-  static constexpr int LDK = D + 8;
-  static constexpr int LDG = D + 4;
+  static constexpr int LDK = D + 8;        // padded 16-bit work tiles
   static constexpr int LDC = kChunk + 8;   // 16-bit 64 x 64
   static constexpr int LDF = kChunk + 4;   // fp32 64 x 64
   static constexpr int tile16 = kChunk * LDK * 2;
+  static constexpr int sw16 = (D / 64) * 8192;  // swizzled bf16 [64][D] (TMA)
+  static constexpr int swG = (D / 32) * 8192;   // swizzled fp32 [64][D] (TMA)
   static constexpr int oQ = 0;
-  static constexpr int oK = oQ + tile16;
-  static constexpr int oB = oK + tile16;
-  static constexpr int oV = oB + tile16;  // v, then Z = v * w
-  static constexpr int oW = oV + tile16;  // w, then E = b k_n 2^G
-  static constexpr int oG = oW + tile16;
-  static constexpr int oMisc = oG + kChunk * LDG * 4;
-  // misc floats: rq[64] rk[64] flag[4] Pb[4][D] Qe[4][D] F[10][D]
-  static constexpr int nMisc = 64 + 64 + 4 + 18 * D;
-  static constexpr int oR = oMisc + nMisc * 4;  // work region
+  static constexpr int oK = oQ + sw16;
+  static constexpr int oB = oK + sw16;
+  static constexpr int oV = oB + sw16;  // v, then Z = v * w
+  static constexpr int oW = oV + sw16;  // w, then E = b k_n 2^G
+  static constexpr int oG = oW + sw16;
+  static constexpr int oMisc = oG + swG;
+  // misc floats: rq[64] rk[64] flag[4] Pb[4][D] Qe[4][D] F[10][D] mbar[2] (as 4)
+  static constexpr int nMisc = 64 + 64 + 4 + 18 * D + 4;
+  static constexpr int oR = (oMisc + nMisc * 4 + 15) / 16 * 16;  // work region
   // scores
   static constexpr int rQs = 0;
   static constexpr int rKBs = rQs + tile16;
@@ -52,11 +66,11 @@ struct Fwd16Layout {
   static constexpr int rA16 = rT + 3 * 16 * 20 * 4;  // written after the inverse
   static constexpr int rEndInv = rA16 + kChunk * LDC * 2;
   static constexpr int R = rEndScores > rEndInv ? rEndScores : rEndInv;
-  static constexpr size_t bytes = (size_t)oR + R;
+  static constexpr size_t bytes = (size_t)oR + R + 1024;  // + alignment slack
   static_assert(rT + 3 * 16 * 20 * 4 <= rAkk, "T tiles overlap Akk");
   // W / U staging: W over the dead Inv / T tiles below sA16, U past sA16
   static_assert(tile16 <= rA16 && rEndInv + tile16 <= R, "W / U staging tiles");
-  static_assert(oR % 16 == 0 && rAkk % 16 == 0 && rA16 % 16 == 0, "alignment");
+  static_assert(rAkk % 16 == 0 && rA16 % 16 == 0, "alignment");
 };
 
 // acc_q / acc_k (16 x 16) += A_q / A_k (16 rows at m0, D columns) times the
@@ -85,25 +99,79 @@ __device__ __forceinline__ void score_block16(float (&aq)[1][2][4], float (&ak)[
   }
 }
 
+// acc (16 x 8*NT) += A (16 rows at m0 of a padded K-major tile, kd columns)
+// times B (kd rows x 8*NT columns at n0 of a swizzled [64][D] tile).
+template <int NT, typename T>
+__device__ __forceinline__ void mma_a_swb(float (&acc)[1][NT][4], const T* A, int lda, int m0,
+                                          const unsigned char* Bsw, int n0, int kd) {
+  const int lane = threadIdx.x & 31;
+  const int j8 = lane >> 3, rr = lane & 7;
+#pragma unroll
+  for (int k0 = 0; k0 < kd; k0 += 16) {
+    uint32_t a[4];
+    load_a16<true>(a, A, lda, m0, k0);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      const int k = k0 + rr + ((j8 & 1) << 3), n = n0 + 8 * j + ((j8 >> 1) << 3);
+      ldsm_x4_t(b, Bsw + swz<2>(k, n));
+      Mma16<T>::run(acc[0][j], a, b[0], b[1]);
+      Mma16<T>::run(acc[0][j + 1], a, b[2], b[3]);
+    }
+  }
+}
+
+// Inclusive prefix sum down the 64 rows of a swizzled fp32 tile, times mul
+// (register-staged, same summation order as col_scan64_t).
+template <int NC, int NTH>
+__device__ __forceinline__ void col_scan64_sw(unsigned char* s, float* tmp, float mul) {
+  constexpr int NSEG = NTH / NC;
+  constexpr int RPS = kChunk / NSEG;
+  static_assert(NSEG * NC == NTH && RPS * NSEG == kChunk, "scan shape");
+  const int col = threadIdx.x % NC, seg = threadIdx.x / NC;
+  float x[RPS];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) x[i] = *reinterpret_cast<const float*>(s + swz<4>(seg * RPS + i, col));
+#pragma unroll
+  for (int i = 1; i < RPS; ++i) x[i] += x[i - 1];
+  tmp[seg * NC + col] = x[RPS - 1];
+  __syncthreads();
+  float off = 0.f;
+#pragma unroll
+  for (int j = 0; j < NSEG - 1; ++j)
+    if (j < seg) off += tmp[j * NC + col];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i)
+    *reinterpret_cast<float*>(s + swz<4>(seg * RPS + i, col)) = (x[i] + off) * mul;
+  __syncthreads();
+}
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) {
+__global__ void __launch_bounds__(kThreadsF16, 1)
+    k_fwd_intra16(FwdIntraArgs a, const __grid_constant__ CUtensorMap mQ,
+                  const __grid_constant__ CUtensorMap mK, const __grid_constant__ CUtensorMap mB,
+                  const __grid_constant__ CUtensorMap mV, const __grid_constant__ CUtensorMap mW,
+                  const __grid_constant__ CUtensorMap mG) {
   using L = Fwd16Layout<D>;
-  constexpr int LDK = L::LDK, LDG = L::LDG, LDC = L::LDC, LDF = L::LDF;
+  constexpr int LDK = L::LDK, LDC = L::LDC, LDF = L::LDF;
   constexpr int NTH = kThreadsF16;
   constexpr int DQ = D / 4, NTO = DQ / 8;
-  extern __shared__ __align__(16) unsigned char sm[];
-  T* sq = reinterpret_cast<T*>(sm + L::oQ);
-  T* sk = reinterpret_cast<T*>(sm + L::oK);
-  T* sb = reinterpret_cast<T*>(sm + L::oB);
-  T* sv = reinterpret_cast<T*>(sm + L::oV);
-  T* sw = reinterpret_cast<T*>(sm + L::oW);
-  float* sG = reinterpret_cast<float*>(sm + L::oG);
+  extern __shared__ unsigned char smraw[];
+  unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  unsigned char* sq = sm + L::oQ;  // swizzled TMA tiles
+  unsigned char* sk = sm + L::oK;
+  unsigned char* sb = sm + L::oB;
+  unsigned char* sv = sm + L::oV;
+  unsigned char* sw = sm + L::oW;
+  unsigned char* sG = sm + L::oG;
   float* rq = reinterpret_cast<float*>(sm + L::oMisc);
   float* rk = rq + 64;
   int* sFlag = reinterpret_cast<int*>(rk + 64);
   float* sPb = rk + 64 + 4;  // [4][D]  2^G at each block's first row
   float* sQe = sPb + 4 * D;  // [4][D]  2^(G_63 - G) at each block's last row
   float* sF = sQe + 4 * D;   // [10][D] 2^(G_16I - G_(16J+15)), pair I(I+1)/2 + J
+  uint64_t* barA = reinterpret_cast<uint64_t*>(sF + 10 * D);  // q, k, b, g landed
+  uint64_t* barB = barA + 1;                                  // v, w landed
   unsigned char* R = sm + L::oR;
   T* sQs = reinterpret_cast<T*>(R + L::rQs);
   T* sKBs = reinterpret_cast<T*>(R + L::rKBs);
@@ -116,44 +184,86 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
   const int gid = lane >> 2, tig = lane & 3;
   const int wr = warp & 3, wc = warp >> 2;
   const int H = a.H, K = a.K, V = a.V;
-  const int64_t ldk = (int64_t)H * K, ldv = (int64_t)H * V;
   const size_t tileK = (size_t)kChunk * K, tileV = (size_t)kChunk * V;
   const float scale = a.scale;
   const int n_items = a.seqs.n_chunks * H;
+  const int nbK = (K + 63) / 64, nbV = (V + 63) / 64, nbG = (K + 31) / 32;
+  auto G_ = [&](int r, int c) -> float { return *reinterpret_cast<const float*>(sG + swz<4>(r, c)); };
+  auto E16 = [&](const unsigned char* t, int r, int c) -> float {
+    return to_f<T>(*reinterpret_cast<const T*>(t + swz<2>(r, c)));
+  };
 
   // Items (chunk c, head h) = (item / H, item % H), strided over the grid.
-  // q, k, b, g of the next item stream in (cp.async) once this item's scores
-  // are done (they are dead from there on); v, w once its W / U products are.
-  auto issue_qkbg = [&](int item) {
-    const int c = item / H, h = item - (item / H) * H;
-    const ChunkPos cp = chunk_pos(a.seqs, c);
-    const int64_t offk = cp.row0 * ldk + (int64_t)h * K;
-    cp_tile16<T, kChunk, D, NTH>(sq, LDK, reinterpret_cast<const T*>(a.q) + offk, ldk, cp.len, K);
-    cp_tile16<T, kChunk, D, NTH>(sk, LDK, reinterpret_cast<const T*>(a.k) + offk, ldk, cp.len, K);
-    cp_tile16<T, kChunk, D, NTH>(sb, LDK, reinterpret_cast<const T*>(a.b) + offk, ldk, cp.len, K);
-    cp_tile32<kChunk, D, NTH>(sG, LDG, a.g + offk, ldk, cp.len, K);
-    cp_async_commit();
+  // Thread 0 requests each item's tiles as TMA boxes (3-D views [rows][H][D],
+  // 64 rows x 128 bytes each) completing on an mbarrier: q, k, b, g of the
+  // next item once this item's scores are done (they are dead from there
+  // on), v, w once its W / U products are done.
+  // (row0 of the item's chunk comes from the sequence tables, looked up one
+  // item ahead so the dependent global loads stay off the critical path)
+  auto issue_qkbg = [&](int item, int row0) {
+    const int h = item - (item / H) * H;
+    tc::mbar_expect_tx(barA, (uint32_t)(3 * nbK + nbG) * 8192u);
+    for (int bx = 0; bx < nbK; ++bx) {
+      tc::tma_load_3d(sq + bx * 8192, &mQ, 64 * bx, h, row0, barA);
+      tc::tma_load_3d(sk + bx * 8192, &mK, 64 * bx, h, row0, barA);
+      tc::tma_load_3d(sb + bx * 8192, &mB, 64 * bx, h, row0, barA);
+    }
+    for (int bx = 0; bx < nbG; ++bx) tc::tma_load_3d(sG + bx * 8192, &mG, 32 * bx, h, row0, barA);
   };
-  auto issue_vw = [&](int item) {
-    const int c = item / H, h = item - (item / H) * H;
-    const ChunkPos cp = chunk_pos(a.seqs, c);
-    const int64_t offv = cp.row0 * ldv + (int64_t)h * V;
-    cp_tile16<T, kChunk, D, NTH>(sv, LDK, reinterpret_cast<const T*>(a.v) + offv, ldv, cp.len, V);
-    cp_tile16<T, kChunk, D, NTH>(sw, LDK, reinterpret_cast<const T*>(a.w) + offv, ldv, cp.len, V);
-    cp_async_commit();
+  auto issue_vw = [&](int item, int row0) {
+    const int h = item - (item / H) * H;
+    tc::mbar_expect_tx(barB, (uint32_t)(2 * nbV) * 8192u);
+    for (int bx = 0; bx < nbV; ++bx) {
+      tc::tma_load_3d(sv + bx * 8192, &mV, 64 * bx, h, row0, barB);
+      tc::tma_load_3d(sw + bx * 8192, &mW, 64 * bx, h, row0, barB);
+    }
   };
-  issue_qkbg(blockIdx.x);
-  issue_vw(blockIdx.x);
+  // rows past a partial chunk's end hold the next sequence's tokens
+  auto zero_rows = [&](unsigned char* t, int nbox, int len) {
+    for (int e = tid; e < (kChunk - len) * nbox * 8; e += NTH) {
+      const int r = len + e / (nbox * 8), rest = e - (e / (nbox * 8)) * (nbox * 8);
+      *reinterpret_cast<uint4*>(t + (rest >> 3) * 8192 + r * 128 + (rest & 7) * 16) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  // boxes past K / V are never loaded and stay zero
+  for (int i = tid; i < (5 * L::sw16 + L::swG) / 16; i += NTH)
+    reinterpret_cast<uint4*>(sm)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid == 0) {
+    tc::mbar_init(barA, 1);
+    tc::mbar_init(barB, 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_async_smem();
+  __syncthreads();
+  ChunkPos cur = chunk_pos(a.seqs, blockIdx.x / H);
+  if (tid == 0) {
+    issue_qkbg(blockIdx.x, (int)cur.row0);
+    issue_vw(blockIdx.x, (int)cur.row0);
+  }
+  int fault = 0;
+  uint32_t phase = 0;
 
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const int next = item + gridDim.x;
     const int c = item / H, h = item - (item / H) * H;
     const size_t ch = (size_t)c * H + h;
+    const int len = cur.len;
+    ChunkPos nxt = cur;
+    if (next < n_items) nxt = chunk_pos(a.seqs, next / H);
     if (tid == 0) sFlag[0] = 1;
-    cp_async_wait<1>();  // q, k, b, g of this item
-    __syncthreads();
+    if (!tc::mbar_wait(barA, phase)) fault = 1;  // q, k, b, g of this item
+    if (__syncthreads_or(fault)) break;
+    if (len < kChunk) {
+      zero_rows(sq, nbK, len);
+      zero_rows(sk, nbK, len);
+      zero_rows(sb, nbK, len);
+      zero_rows(sG, nbG, len);
+      tc::fence_async_smem();
+      __syncthreads();
+    }
     // chunk-local log2 cumulative decay
-    col_scan64_reg<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(R), kLog2e);
+    col_scan64_sw<D, NTH>(sG, reinterpret_cast<float*>(R), kLog2e);
     // row norms: warp w owns rows 4w .. 4w+3
     {
       constexpr int EPL = D / 32;
@@ -163,10 +273,21 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
         const int r = 4 * warp + rr;
         s1[rr] = 0.f;
         s2[rr] = 0.f;
+        // the lane's EPL columns are contiguous inside one 16-byte chunk
+        const uint32_t o = swz<2>(r, EPL * lane);
+        uint32_t uq[EPL / 2], uk[EPL / 2];
+        if constexpr (EPL == 4) {
+          const uint2 x = *reinterpret_cast<const uint2*>(sq + o);
+          const uint2 y = *reinterpret_cast<const uint2*>(sk + o);
+          uq[0] = x.x; uq[1] = x.y; uk[0] = y.x; uk[1] = y.y;
+        } else {
+          uq[0] = *reinterpret_cast<const uint32_t*>(sq + o);
+          uk[0] = *reinterpret_cast<const uint32_t*>(sk + o);
+        }
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
-          const float x = to_f<T>(sq[r * LDK + EPL * lane + e]);
-          const float y = to_f<T>(sk[r * LDK + EPL * lane + e]);
+          const float x = to_f<T>(reinterpret_cast<const T*>(uq)[e]);
+          const float y = to_f<T>(reinterpret_cast<const T*>(uk)[e]);
           s1[rr] += x * x;
           s2[rr] += y * y;
         }
@@ -190,28 +311,34 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
     float* gGl = reinterpret_cast<float*>(a.saved + a.L.gl) + ch * K;
     for (int i = tid; i < 18 * D; i += NTH) {
       const int p = i / D, cc = i - p * D;
-      const float GL = sG[(kChunk - 1) * LDG + cc];
+      const float GL = G_(kChunk - 1, cc);
       float x;
       if (p < 4) {
-        x = exp2f(sG[16 * p * LDG + cc]);
+        x = fast_exp2(G_(16 * p, cc));
       } else if (p < 8) {
-        x = exp2f(GL - sG[(16 * (p - 4) + 15) * LDG + cc]);
+        x = fast_exp2(GL - G_(16 * (p - 4) + 15, cc));
       } else {
         const int q = p - 8;
         const int I = q >= 6 ? 3 : q >= 3 ? 2 : q >= 1 ? 1 : 0;
         const int J = q - I * (I + 1) / 2;
-        x = exp2f(fminf(sG[16 * I * LDG + cc] - sG[(16 * J + 15) * LDG + cc], 120.f));
+        x = fast_exp2(fminf(G_(16 * I, cc) - G_(16 * J + 15, cc), 120.f));
       }
       sPb[i] = x;  // sPb, sQe, sF are contiguous
     }
     for (int i = tid; i < 4 * D; i += NTH) {
       const int bI = i / D, cc = i - bI * D;
-      const float rng = sG[(16 * bI) * LDG + cc] - sG[(16 * bI + 15) * LDG + cc];
+      const float rng = G_(16 * bI, cc) - G_(16 * bI + 15, cc);
       if (!(rng <= kSafeLog2Range)) sFlag[0] = 0;
     }
-    for (int i = tid; i < K; i += NTH) gGl[i] = exp2f(sG[(kChunk - 1) * LDG + i]);
-    cp_async_wait<0>();  // v, w
-    __syncthreads();
+    for (int i = tid; i < K; i += NTH) gGl[i] = exp2f(G_(kChunk - 1, i));
+    if (!tc::mbar_wait(barB, phase)) fault = 1;  // v, w
+    if (__syncthreads_or(fault)) break;
+    if (len < kChunk) {
+      zero_rows(sv, nbV, len);
+      zero_rows(sw, nbV, len);
+      tc::fence_async_smem();
+      __syncthreads();
+    }
     const bool safe = sFlag[0] != 0;
 
     // ---- one elementwise pass: Qg, Kd out; Qs, KBs, Kb score operands;
@@ -225,19 +352,20 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
       const int blk = r0 >> 4, rb = r0 & ~15, re = rb + 15;
       T* gQg = reinterpret_cast<T*>(a.saved + a.L.qg) + ch * tileK;
       T* gKd = reinterpret_cast<T*>(a.saved + a.L.kd) + ch * tileK;
-      const float2 Gb = *reinterpret_cast<const float2*>(sG + rb * LDG + cc);
-      const float2 Ge = *reinterpret_cast<const float2*>(sG + re * LDG + cc);
+      const float2 Gb = *reinterpret_cast<const float2*>(sG + swz<4>(rb, cc));
+      const float2 Ge = *reinterpret_cast<const float2*>(sG + swz<4>(re, cc));
       const float2 Pb = *reinterpret_cast<const float2*>(sPb + blk * D + cc);
       const float2 Qe = *reinterpret_cast<const float2*>(sQe + blk * D + cc);
 #pragma unroll 4
       for (int j = 0; j < RPT; ++j) {
         const int r = r0 + j;
-        const float2 G = *reinterpret_cast<const float2*>(sG + r * LDG + cc);
-        const uint32_t uq = *reinterpret_cast<const uint32_t*>(sq + r * LDK + cc);
-        const uint32_t uk = *reinterpret_cast<const uint32_t*>(sk + r * LDK + cc);
-        const uint32_t ub = *reinterpret_cast<const uint32_t*>(sb + r * LDK + cc);
-        const uint32_t uv = *reinterpret_cast<const uint32_t*>(sv + r * LDK + cc);
-        const uint32_t uw = *reinterpret_cast<const uint32_t*>(sw + r * LDK + cc);
+        const uint32_t o16 = swz<2>(r, cc);
+        const float2 G = *reinterpret_cast<const float2*>(sG + swz<4>(r, cc));
+        const uint32_t uq = *reinterpret_cast<const uint32_t*>(sq + o16);
+        const uint32_t uk = *reinterpret_cast<const uint32_t*>(sk + o16);
+        const uint32_t ub = *reinterpret_cast<const uint32_t*>(sb + o16);
+        const uint32_t uv = *reinterpret_cast<const uint32_t*>(sv + o16);
+        const uint32_t uw = *reinterpret_cast<const uint32_t*>(sw + o16);
         const T* pq = reinterpret_cast<const T*>(&uq);
         const T* pk = reinterpret_cast<const T*>(&uk);
         const T* pb = reinterpret_cast<const T*>(&ub);
@@ -249,8 +377,8 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
         float qg[2], kd[2], qs[2], kbs[2], kb[2], e2[2], z2[2];
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          const float f = exp2f(g2[t] - gb2[t]);   // <= 1
-          const float fe = exp2f(ge2[t] - g2[t]);  // <= 1
+          const float f = fast_exp2(g2[t] - gb2[t]);   // <= 1
+          const float fe = fast_exp2(ge2[t] - g2[t]);  // <= 1
           const float qn = to_f<T>(pq[t]) * nq;
           const float kn = to_f<T>(pk[t]) * nk;
           const float bkn = to_f<T>(pb[t]) * kn;
@@ -271,8 +399,8 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
         *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(qs[0], qs[1]);
         *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kbs[0], kbs[1]);
         *reinterpret_cast<uint32_t*>(sKb + r * LDK + cc) = pack2<T>(kb[0], kb[1]);
-        *reinterpret_cast<uint32_t*>(sw + r * LDK + cc) = pack2<T>(e2[0], e2[1]);
-        *reinterpret_cast<uint32_t*>(sv + r * LDK + cc) = pack2<T>(z2[0], z2[1]);
+        *reinterpret_cast<uint32_t*>(sw + o16) = pack2<T>(e2[0], e2[1]);
+        *reinterpret_cast<uint32_t*>(sv + o16) = pack2<T>(z2[0], z2[1]);
       }
     }
     __syncthreads();
@@ -320,10 +448,9 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
         float sqv = 0.f, skv = 0.f;
         if (ii <= rr) {
           for (int cc = 0; cc < D; ++cc) {
-            const float f = exp2f(sG[r * LDG + cc] - sG[i * LDG + cc]) *
-                            to_f<T>(sk[i * LDK + cc]) * rk[i];
-            sqv += to_f<T>(sq[r * LDK + cc]) * f;
-            skv += to_f<T>(sb[r * LDK + cc]) * to_f<T>(sk[r * LDK + cc]) * f;
+            const float f = exp2f(G_(r, cc) - G_(i, cc)) * E16(sk, i, cc) * rk[i];
+            sqv += E16(sq, r, cc) * f;
+            skv += E16(sb, r, cc) * E16(sk, r, cc) * f;
           }
           sqv *= scale * rq[r];
           skv *= rk[r];
@@ -332,8 +459,9 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
         sAkk[r * LDF + i] = (ii < rr) ? skv : 0.f;
       }
     }
+    tc::fence_async_smem();
     __syncthreads();
-    if (next < n_items) issue_qkbg(next);  // q, k, b, g are dead for this item
+    if (tid == 0 && next < n_items) issue_qkbg(next, (int)nxt.row0);  // q, k, b, g are dead
 
     // ---- A = (I + Akk)^-1 ----------------------------------------------------------
     unit_lower_inverse_mma<LDF>(sAkk, sInv, reinterpret_cast<float*>(R + L::rT));
@@ -349,11 +477,11 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
 
     // ---- W = A E, U = A Z (owner tiles 16 x D/4), staged for coalesced stores
     {
-      T* stW = reinterpret_cast<T*>(R + L::rInv);  // Inv is dead after the pack
+      T* stW = reinterpret_cast<T*>(R + L::rInv);     // Inv is dead after the pack
       T* stU = reinterpret_cast<T*>(R + L::rEndInv);  // past sA16 (read by both products)
       float acc[1][NTO][4];
       acc_zero(acc);
-      warp_mma16<1, NTO, true, false>(acc, sA16, LDC, 16 * wr, sw, LDK, wc * DQ, kChunk);
+      mma_a_swb<NTO, T>(acc, sA16, LDC, 16 * wr, sw, wc * DQ, kChunk);
 #pragma unroll
       for (int j = 0; j < NTO; ++j)
 #pragma unroll
@@ -363,7 +491,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
               pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
         }
       acc_zero(acc);
-      warp_mma16<1, NTO, true, false>(acc, sA16, LDC, 16 * wr, sv, LDK, wc * DQ, kChunk);
+      mma_a_swb<NTO, T>(acc, sA16, LDC, 16 * wr, sv, wc * DQ, kChunk);
 #pragma unroll
       for (int j = 0; j < NTO; ++j)
 #pragma unroll
@@ -372,31 +500,45 @@ __global__ void __launch_bounds__(kThreadsF16, 1) k_fwd_intra16(FwdIntraArgs a) 
           *reinterpret_cast<uint32_t*>(stU + r * LDK + cl) =
               pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
         }
+      tc::fence_async_smem();
       __syncthreads();
+      if (tid == 0 && next < n_items) issue_vw(next, (int)nxt.row0);  // v, w (now E, Z) are dead
       store_tile16<T, kChunk, D, NTH>(reinterpret_cast<T*>(a.saved + a.L.w) + ch * tileK, K, stW,
                                       LDK, kChunk, K);
       store_tile16<T, kChunk, D, NTH>(reinterpret_cast<T*>(a.saved + a.L.u) + ch * tileV, V, stU,
                                       LDK, kChunk, V);
     }
     __syncthreads();
-    if (next < n_items) issue_vw(next);  // v, w (now E, Z) are dead
+    phase ^= 1u;
+    cur = nxt;
   }
-  cp_async_wait<0>();
+  if (fault && tid == 0) {
+    // a copy never landed: wait (bounded) for what is still in flight, flag it
+    tc::mbar_wait(barA, phase);
+    tc::mbar_wait(barB, phase);
+    atomicOr(a.fault, 2u);
+  }
 }
 
 template <typename T, int D>
 cudaError_t launch_fwd_intra16(const FwdIntraArgs& a, cudaStream_t st) {
   auto kern = k_fwd_intra16<T, D>;
+  const int n_items = a.seqs.n_chunks * a.H;
+  if (n_items == 0) return cudaSuccess;
+  const uint64_t rows = (uint64_t)a.total_rows, H = (uint64_t)a.H;
+  CUtensorMap mQ, mK, mB, mV, mW, mG;
+  if (!tmap_rows(&mQ, a.q, a.K, H, rows, 64, 2) || !tmap_rows(&mK, a.k, a.K, H, rows, 64, 2) ||
+      !tmap_rows(&mB, a.b, a.K, H, rows, 64, 2) || !tmap_rows(&mV, a.v, a.V, H, rows, 64, 2) ||
+      !tmap_rows(&mW, a.w, a.V, H, rows, 64, 2) || !tmap_rows(&mG, a.g, a.K, H, rows, 32, 4))
+    return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)Fwd16Layout<D>::bytes);
   if (e != cudaSuccess) return e;
-  const int n_items = a.seqs.n_chunks * a.H;
-  if (n_items == 0) return cudaSuccess;
   int sms = 0;
   e = num_sms(&sms);
   if (e != cudaSuccess) return e;
   const int grid = n_items < sms ? n_items : sms;  // persistent: one CTA per SM
-  kern<<<grid, kThreadsF16, Fwd16Layout<D>::bytes, st>>>(a);
+  kern<<<grid, kThreadsF16, Fwd16Layout<D>::bytes, st>>>(a, mQ, mK, mB, mV, mW, mG);
   return cudaGetLastError();
 }
 

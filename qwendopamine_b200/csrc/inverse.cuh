@@ -51,7 +51,7 @@ __device__ void unit_lower_inverse(const float* sL, float* sInv, float* sTmp) {
 }
 
 // acc (16 x 16) = A (16 x KD) B (KD x 16) on the tensor cores with the
-// 3-term TF32 split (hi*hi + hi*lo + lo*hi, about fp32 accuracy); the two
+// 3-term TF32 split (hi*hi + hi*lo + lo*hi, about fp32 accuracy); the three
 // accumulator chains run independently.  A(m,k) = A[m*lda + k],
 // B(k,n) = B[k*ldb + n] (fp32 shared memory).
 template <int KD>
@@ -59,11 +59,11 @@ __device__ __forceinline__ void mma16x16_tf32x3(float (&acc)[1][2][4], const flo
                                                 const float* B, int ldb) {
   const int lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  float hh[2][4], mx[2][4];
+  float hh[2][4], lh[2][4], hl[2][4];
 #pragma unroll
   for (int j = 0; j < 2; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) hh[j][e] = mx[j][e] = 0.f;
+    for (int e = 0; e < 4; ++e) hh[j][e] = lh[j][e] = hl[j][e] = 0.f;
 #pragma unroll
   for (int k0 = 0; k0 < KD; k0 += 8) {
     const float* a = A + gid * lda + k0 + tig;
@@ -82,14 +82,14 @@ __device__ __forceinline__ void mma16x16_tf32x3(float (&acc)[1][2][4], const flo
       const uint32_t bl0 = tf32_bits(y0 - __uint_as_float(bh0));
       const uint32_t bl1 = tf32_bits(y1 - __uint_as_float(bh1));
       mma_tf32(hh[j], ah, bh0, bh1);
-      mma_tf32(mx[j], al, bh0, bh1);
-      mma_tf32(mx[j], ah, bl0, bl1);
+      mma_tf32(lh[j], al, bh0, bh1);
+      mma_tf32(hl[j], ah, bl0, bl1);
     }
   }
 #pragma unroll
   for (int j = 0; j < 2; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[0][j][e] = hh[j][e] + mx[j][e];
+    for (int e = 0; e < 4; ++e) acc[0][j][e] = hh[j][e] + (lh[j][e] + hl[j][e]);
 }
 
 // Blocks at distance d = I - J of the inverse, one warp per block:

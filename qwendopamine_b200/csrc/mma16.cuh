@@ -277,7 +277,7 @@ __device__ __forceinline__ void block_factors(const float* G, int ldg, float* F)
     const int q = i / D, cc = i - q * D;
     const int I = q >= 6 ? 3 : q >= 3 ? 2 : q >= 1 ? 1 : 0;
     const int J = q - I * (I + 1) / 2;
-    F[i] = exp2f(fminf(G[16 * I * ldg + cc] - G[(16 * J + 15) * ldg + cc], 120.f));
+    F[i] = fast_exp2(fminf(G[16 * I * ldg + cc] - G[(16 * J + 15) * ldg + cc], 120.f));
   }
 }
 

@@ -721,52 +721,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ---- host side -----------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = []() -> EncodeTiledFn {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
-                                         &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
-// 2-D bf16 map over `rows` rows of `inner` elements; box = box_x x 64 rows.
 bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_x,
               bool swizzle) {
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return false;
-  cuuint64_t dims[2] = {inner, rows};
-  cuuint64_t strides[1] = {inner * 2};
-  cuuint32_t box[2] = {box_x, 64};
-  cuuint32_t estr[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-             estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return tmap_2d_bf16(m, base, inner, rows, box_x, swizzle);
 }
-
-// 3-D bf16 map over token rows [rows][H][V] (dO): box 64 columns x 1 head x
-// 64 rows, 128-byte swizzle.
 bool make_map_rows(CUtensorMap* m, const void* base, uint64_t V, uint64_t H, uint64_t rows) {
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return false;
-  cuuint64_t dims[3] = {V, H, rows};
-  cuuint64_t strides[2] = {V * 2, H * V * 2};
-  cuuint32_t box[3] = {64, 1, 64};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
-             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return tmap_rows(m, base, V, H, rows, 64, 2);
 }
+bool encode_ok() { return tmap_available(); }
 
 }  // namespace
 
@@ -780,7 +742,7 @@ bool bwd_state_tc_ok(const BwdStateArgs& a, int dtype_bf16) {
   if ((al & 15) != 0) return false;
   if ((int64_t)a.seqs.n_chunks * a.H * kChunk >= (int64_t)1 << 31) return false;
   if (a.total_rows <= 0 || a.total_rows >= (int64_t)1 << 31) return false;
-  return encode_fn() != nullptr;
+  return encode_ok();
 }
 
 cudaError_t launch_bwd_state_tc(const BwdStateArgs& a, cudaStream_t st) {
@@ -809,7 +771,7 @@ bool fwd_state_tc_ok(const FwdStateArgs& a, int dtype_bf16) {
   if ((reinterpret_cast<uintptr_t>(a.h0) & 15) != 0 || (reinterpret_cast<uintptr_t>(a.ht) & 15) != 0)
     return false;
   if ((int64_t)a.seqs.n_chunks * a.H * kChunk >= (int64_t)1 << 31) return false;
-  return encode_fn() != nullptr;
+  return encode_ok();
 }
 
 cudaError_t launch_fwd_state_tc(const FwdStateArgs& a, cudaStream_t st) {

@@ -195,4 +195,17 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 }
 
 }  // namespace tc
+
+// ---- host: TMA tensor maps (tmap.cu) ------------------------------------------
+// Whether cuTensorMapEncodeTiled is reachable.
+bool tmap_available();
+// 2-D bf16 map over `rows` rows of `inner` elements; box = box_x x 64 rows,
+// 128-byte swizzle (or none).
+bool tmap_2d_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_x,
+                  bool swizzle);
+// 3-D map over token rows [rows][H][D] of 2- or 4-byte elements: box box_x
+// columns (128 bytes) x 1 head x 64 rows, 128-byte swizzle.
+bool tmap_rows(CUtensorMap* m, const void* base, uint64_t D, uint64_t H, uint64_t rows,
+               uint32_t box_x, int elem_bytes);
+
 }  // namespace gdn2
