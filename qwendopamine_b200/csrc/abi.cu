@@ -469,7 +469,9 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p, const void* q, const voi
   a.state_stride = p->state_stride;
   a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
   a.h0 = h0; a.o = o; a.ht = ht;
-  cudaError_t e = dispatch<RunRec>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  cudaError_t e = fault_word(&a.fault);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn2_recurrent_fwd");
+  e = dispatch<RunRec>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_recurrent_fwd");
 }
 

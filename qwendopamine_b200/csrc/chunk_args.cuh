@@ -92,6 +92,7 @@ struct RecArgs {
   const float* h0;
   void* o;
   float* ht;
+  unsigned int* fault;  // device fault word (bounded waits that ran out)
 };
 
 }  // namespace gdn2

@@ -9,6 +9,7 @@
 // with q, k L2-normalised in kernel (x / sqrt(sum x^2 + 1e-6), as the Triton
 // kernel does at :252-254) and q scaled after normalisation.
 #include "chunk_args.cuh"
+#include "tc.cuh"
 
 namespace gdn2 {
 
@@ -179,8 +180,286 @@ __global__ void __launch_bounds__(kThreads, 3) k_recurrent(RecArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Streaming variant for full states (K = V = D): a persistent CTA of 512
+// threads per SM walks (sequence, value head) units.  Each unit's whole fp32
+// state (D x D, contiguous) and its first token's q, k, b, g, v, w arrive by
+// 1-D bulk async copies into a two-buffer shared-memory ring one unit ahead,
+// so HBM streams the next state while this one is updated; the new state
+// leaves from registers with 128-bit streaming stores.  Same arithmetic,
+// order and reductions as k_recurrent (thread (rg, cg) holds rows
+// [rg*RPT, +RPT) x columns [4cg, 4cg+4)).
+struct RecUnit {
+  int64_t bos, Tn;
+  const float* h0;
+  float* ht;
+  int hv, hq, skip;
+};
+
+__device__ __forceinline__ RecUnit rec_unit(const RecArgs& a, int u) {
+  RecUnit r;
+  const int n = u / a.HV, hv = u - (u / a.HV) * a.HV;
+  r.hv = hv;
+  r.hq = hv / (a.HV / a.H);
+  if (a.cu) {
+    r.bos = a.cu[n];
+    r.Tn = a.cu[n + 1] - r.bos;
+  } else {
+    r.bos = (int64_t)n * a.T;
+    r.Tn = a.T;
+  }
+  r.h0 = nullptr;
+  r.ht = nullptr;
+  r.skip = 0;
+  const int64_t KV = (int64_t)a.K * a.V;
+  if (a.state_idx) {
+    const int64_t slot = a.state_idx[n];
+    if (slot < 0) {
+      r.skip = 1;
+      return r;
+    }
+    if (a.h0) r.h0 = a.h0 + slot * a.state_stride + (int64_t)hv * KV;
+    if (a.ht) r.ht = a.ht + slot * a.state_stride + (int64_t)hv * KV;
+  } else {
+    if (a.h0) r.h0 = a.h0 + ((int64_t)n * a.HV + hv) * KV;
+    if (a.ht) r.ht = a.ht + ((int64_t)n * a.HV + hv) * KV;
+  }
+  return r;
+}
+
+template <int D>
+struct RecStreamSmem {
+  static constexpr int NTH = 512;
+  static constexpr int CG = D / 4, RG = NTH / CG, RPT = D / RG;
+  static constexpr uint32_t state = D * D * 4;     // one state buffer
+  static constexpr uint32_t raw = 24 * D;           // q, k, b, v, w (<= 4 B each) and g of one token
+  static constexpr uint32_t oState = 0;
+  static constexpr uint32_t oRaw = 2 * state;
+  static constexpr uint32_t oF = oRaw + 2 * raw;                   // sq sk sg sb sv sw floats
+  static constexpr uint32_t oRed = oF + 6 * D * 4;                 // red[RG][D]
+  static constexpr uint32_t oUnit = oRed + RG * D * 4;             // RecUnit[2]
+  static constexpr uint32_t oBar = oUnit + 2 * sizeof(RecUnit);    // mbarrier[2]
+  static constexpr uint32_t oNorm = oBar + 16;
+  static constexpr uint32_t bytes = oNorm + 16 + 128;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
+  using S_ = RecStreamSmem<D>;
+  constexpr int NTH = S_::NTH, CG = S_::CG, RG = S_::RG, RPT = S_::RPT;
+  constexpr int EB = (int)sizeof(T);
+  extern __shared__ __align__(128) unsigned char sm[];
+  float* sq = reinterpret_cast<float*>(sm + S_::oF);
+  float* sk = sq + D;
+  float* sg = sk + D;
+  float* sb = sg + D;
+  float* sv = sb + D;
+  float* sw = sv + D;
+  float(*red)[D] = reinterpret_cast<float(*)[D]>(sm + S_::oRed);
+  RecUnit* sUnit = reinterpret_cast<RecUnit*>(sm + S_::oUnit);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + S_::oBar);
+  float* snorm = reinterpret_cast<float*>(sm + S_::oNorm);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int H = a.H, HV = a.HV;
+  const int n_units = a.n_seqs * HV;
+  const int cg = tid % CG, rg = tid / CG, col0 = 4 * cg;
+  const T* q = reinterpret_cast<const T*>(a.q);
+  const T* k = reinterpret_cast<const T*>(a.k);
+  const T* v = reinterpret_cast<const T*>(a.v);
+  const T* b = reinterpret_cast<const T*>(a.b);
+  const T* w = reinterpret_cast<const T*>(a.w);
+  T* o = reinterpret_cast<T*>(a.o);
+
+  // raw token buffer: q k b (D*EB each) | g (D*4) | v w (D*EB each)
+  auto raw_q = [&](int buf) { return sm + S_::oRaw + buf * S_::raw; };
+  auto issue = [&](int u, int buf) {  // thread 0
+    const RecUnit ui = rec_unit(a, u);
+    sUnit[buf] = ui;
+    uint32_t bytes = 0;
+    const bool st = !ui.skip && ui.h0;
+    const bool tok = !ui.skip && ui.Tn > 0;
+    if (st) bytes += S_::state;
+    if (tok) bytes += 5 * D * EB + D * 4;
+    tc::mbar_expect_tx(&bar[buf], bytes);
+    if (st) tc::bulk_load(sm + S_::oState + buf * S_::state, ui.h0, S_::state, &bar[buf]);
+    if (tok) {
+      const int64_t oq = (ui.bos * H + ui.hq) * D, og = (ui.bos * HV + ui.hv) * D;
+      unsigned char* r = raw_q(buf);
+      tc::bulk_load(r, q + oq, D * EB, &bar[buf]);
+      tc::bulk_load(r + D * EB, k + oq, D * EB, &bar[buf]);
+      tc::bulk_load(r + 2 * D * EB, b + og, D * EB, &bar[buf]);
+      tc::bulk_load(r + 3 * D * EB, a.g + og, D * 4, &bar[buf]);
+      tc::bulk_load(r + 3 * D * EB + D * 4, v + og, D * EB, &bar[buf]);
+      tc::bulk_load(r + 4 * D * EB + D * 4, w + og, D * EB, &bar[buf]);
+    }
+  };
+
+  if (tid == 0) {
+    tc::mbar_init(&bar[0], 1);
+    tc::mbar_init(&bar[1], 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0 && (int)blockIdx.x < n_units) issue(blockIdx.x, 0);
+
+  int fault = 0;
+  int it = 0;  // after a fault: the iteration whose copy did not land
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
+    const int buf = it & 1;
+    const uint32_t par = (uint32_t)(it >> 1) & 1u;
+    if (!tc::mbar_wait(&bar[buf], par)) fault = 1;
+    if (__syncthreads_or(fault)) break;
+    // the other buffer's unit is done (its state went to registers and its
+    // token was read before the previous unit's last barrier)
+    if (tid == 0 && u + (int)gridDim.x < n_units) issue(u + gridDim.x, buf ^ 1);
+    const RecUnit ui = sUnit[buf];
+    if (ui.skip) continue;
+
+    float S[RPT][4];
+    const float* st = reinterpret_cast<const float*>(sm + S_::oState + buf * S_::state);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const int r = rg * RPT + i;
+      if (ui.h0) {
+        const float4 x = *reinterpret_cast<const float4*>(st + r * D + col0);
+        S[i][0] = x.x; S[i][1] = x.y; S[i][2] = x.z; S[i][3] = x.w;
+      } else {
+        S[i][0] = S[i][1] = S[i][2] = S[i][3] = 0.f;
+      }
+    }
+
+    for (int64_t t = 0; t < ui.Tn; ++t) {
+      const int64_t row = ui.bos + t;
+      const int64_t oq = (row * H + ui.hq) * D, og = (row * HV + ui.hv) * D;
+      if (t == 0) {
+        const unsigned char* r = raw_q(buf);
+        for (int idx = tid; idx < D; idx += NTH) {
+          sq[idx] = to_f<T>(reinterpret_cast<const T*>(r)[idx]);
+          sk[idx] = to_f<T>(reinterpret_cast<const T*>(r + D * EB)[idx]);
+          sb[idx] = to_f<T>(reinterpret_cast<const T*>(r + 2 * D * EB)[idx]);
+          sg[idx] = expf(reinterpret_cast<const float*>(r + 3 * D * EB)[idx]);
+          sv[idx] = to_f<T>(reinterpret_cast<const T*>(r + 3 * D * EB + D * 4)[idx]);
+          sw[idx] = to_f<T>(reinterpret_cast<const T*>(r + 4 * D * EB + D * 4)[idx]);
+        }
+      } else {
+        for (int idx = tid; idx < D; idx += NTH) {
+          sq[idx] = to_f<T>(q[oq + idx]);
+          sk[idx] = to_f<T>(k[oq + idx]);
+          sb[idx] = to_f<T>(b[og + idx]);
+          sg[idx] = expf(a.g[og + idx]);
+          sv[idx] = to_f<T>(v[og + idx]);
+          sw[idx] = to_f<T>(w[og + idx]);
+        }
+      }
+      __syncthreads();
+      if (warp < 2) {
+        const float* x = warp == 0 ? sq : sk;
+        float s = 0.f;
+        for (int idx = lane; idx < D; idx += 32) s += x[idx] * x[idx];
+        s = warp_sum(s);
+        if (lane == 0) {
+          const float inv = a.l2norm ? rsqrtf(s + kNormEps) : 1.f;
+          snorm[warp] = warp == 0 ? inv * a.scale : inv;
+        }
+      }
+      __syncthreads();
+      const float nq = snorm[0], nk = snorm[1];
+      // decay, then erase-read r = S^T (b*k)
+      float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const int r = rg * RPT + i;
+        const float dec = sg[r], kb = sb[r] * sk[r] * nk;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          S[i][j] *= dec;
+          part[j] += S[i][j] * kb;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red[rg][col0 + j] = part[j];
+      __syncthreads();
+      float dlt[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float s = 0.f;
+#pragma unroll
+        for (int x = 0; x < RG; ++x) s += red[x][col0 + j];
+        dlt[j] = sw[col0 + j] * sv[col0 + j] - s;
+      }
+      __syncthreads();
+      // rank-1 write and read-out
+#pragma unroll
+      for (int j = 0; j < 4; ++j) part[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const int r = rg * RPT + i;
+        const float kr = sk[r] * nk, qr = sq[r] * nq;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          S[i][j] += kr * dlt[j];
+          part[j] += S[i][j] * qr;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red[rg][col0 + j] = part[j];
+      __syncthreads();
+      for (int idx = tid; idx < D; idx += NTH) {
+        float s = 0.f;
+#pragma unroll
+        for (int x = 0; x < RG; ++x) s += red[x][idx];
+        o[og + idx] = from_f<T>(s);
+      }
+      __syncthreads();
+    }
+
+    if (ui.ht) {
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const int r = rg * RPT + i;
+        __stcs(reinterpret_cast<float4*>(ui.ht + (int64_t)r * D + col0),
+               make_float4(S[i][0], S[i][1], S[i][2], S[i][3]));
+      }
+    }
+  }
+  if (fault && tid == 0) {
+    tc::mbar_wait(&bar[it & 1], (uint32_t)(it >> 1) & 1u);  // bounded: let it land
+    atomicOr(a.fault, 4u);
+  }
+}
+
+// The streaming kernel serves full K = V = D states whose rows and vectors
+// are 16-byte aligned (bulk copies); anything else takes k_recurrent.
+template <typename T, int D>
+bool recurrent_stream_ok(const RecArgs& a) {
+  if (a.K != D || a.V != D || !a.fault) return false;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                       reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.b) |
+                       reinterpret_cast<uintptr_t>(a.w) | reinterpret_cast<uintptr_t>(a.g) |
+                       reinterpret_cast<uintptr_t>(a.h0) | reinterpret_cast<uintptr_t>(a.ht) |
+                       reinterpret_cast<uintptr_t>(a.o);
+  if ((al & 15) != 0) return false;
+  if (a.state_idx && (a.state_stride % 4) != 0) return false;
+  return true;
+}
+
 template <typename T, int D>
 cudaError_t launch_recurrent(const RecArgs& a, cudaStream_t st) {
+  if (recurrent_stream_ok<T, D>(a)) {
+    const int n_units = a.n_seqs * a.HV;
+    if (n_units == 0) return cudaSuccess;
+    auto kern = k_recurrent_stream<T, D>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)RecStreamSmem<D>::bytes);
+    if (e != cudaSuccess) return e;
+    int sms = 0;
+    e = num_sms(&sms);
+    if (e != cudaSuccess) return e;
+    const int grid = n_units < sms ? n_units : sms;
+    kern<<<grid, 512, RecStreamSmem<D>::bytes, st>>>(a);
+    return cudaGetLastError();
+  }
   constexpr int VB = 64;
   const int nvs = (a.V + VB - 1) / VB;
   dim3 grid(a.n_seqs * a.HV * nvs);

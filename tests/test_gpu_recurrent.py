@@ -127,3 +127,78 @@ def test_recurrent_and_chunk_agree(cuda_device):
     o2, h2 = chunk_gdn2(*(x[n] for n in NAMES), initial_state=x["h0"], output_final_state=True,
                         use_qk_l2norm_in_kernel=True)
     assert rel(o1, o2) < 1e-4 and rel(h1, h2) < 1e-4
+
+
+def _fault_word():
+    from qwendopamine_b200 import _native as N
+
+    return N.fault_status(clear=True)
+
+
+@pytest.mark.parametrize("K", [128, 64])
+def test_stream_decode_many_units_bf16(cuda_device, K):
+    """Full-state streaming kernel (K = V): 600 (sequence, head) units, more
+    than one per SM, so the two-buffer copy ring cycles; bf16 tokens."""
+    from qwendopamine_b200 import fused_recurrent_gdn2
+
+    _fault_word()
+    d = make_inputs(300, 1, 2, K, K, seed=K + 1, dtype=torch.bfloat16)
+    x = to_dev(d, cuda_device, torch.bfloat16)
+    o, ht = fused_recurrent_gdn2(*(x[n] for n in NAMES), initial_state=x["h0"],
+                                 output_final_state=True, use_qk_l2norm_in_kernel=True)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < 2e-2
+    assert rel(ht, rh) < 1e-4
+    assert _fault_word() == 0
+
+
+def test_stream_state_pool_varlen_gva_no_h0(cuda_device):
+    """Streaming kernel with a state pool (skipped slots, in place), packed
+    sequences (one empty), grouped value heads, and a call without state."""
+    from qwendopamine_b200 import fused_recurrent_gdn2, fused_recurrent_gdn2_fwd
+
+    _fault_word()
+    K = 128
+    # pool + indices, in place
+    d = make_inputs(5, 1, 2, K, K, seed=21, h0=False, dtype=torch.bfloat16)
+    gen = torch.Generator().manual_seed(22)
+    pool = torch.randn(9, 2, K, K, generator=gen) * 0.05
+    idx = torch.tensor([7, -1, 0, 4, -1], dtype=torch.int32)
+    x = to_dev(d, cuda_device, torch.bfloat16)
+    pool_d = pool.to(cuda_device)
+    o, _ = fused_recurrent_gdn2_fwd(*(x[n] for n in NAMES), initial_state=pool_d,
+                                    inplace_final_state=True,
+                                    ssm_state_indices=idx.to(cuda_device),
+                                    use_qk_l2norm_in_kernel=True)
+    for n, slot in enumerate(idx.tolist()):
+        if slot < 0:
+            continue
+        sl = [a[n:n + 1] for a in np_(d, NAMES)]
+        ro, rh = O.recurrent_fwd(*sl, pool[slot:slot + 1].numpy(), norm_mode="fla")
+        assert rel(o[n:n + 1], ro) < 2e-2
+        assert rel(pool_d[slot], rh[0]) < 1e-4
+    untouched = [s for s in range(9) if s not in idx.tolist()]
+    assert torch.equal(pool_d[untouched].cpu(), pool[untouched])
+    # packed sequences with an empty one
+    cu = [0, 2, 2, 7, 8]
+    dv = make_inputs(1, cu[-1], 2, K, K, seed=23, h0=False)
+    h0 = torch.randn(4, 2, K, K, generator=gen) * 0.1
+    xv = to_dev(dv, cuda_device, torch.float32)
+    o, ht = fused_recurrent_gdn2(*(xv[n] for n in NAMES), initial_state=h0.to(cuda_device),
+                                 output_final_state=True, use_qk_l2norm_in_kernel=True,
+                                 cu_seqlens=torch.tensor(cu, device=cuda_device))
+    ro, rh = O.recurrent_fwd_varlen(*np_(dv, NAMES), cu, h0.numpy(), norm_mode="fla")
+    assert rel(o, ro) < 1e-4 and rel(ht, rh) < 1e-4
+    # grouped value heads (HV = 2H) and no initial state
+    B, T, H, HV = 3, 4, 2, 4
+    dg = make_inputs(B, T, HV, K, K, seed=24, h0=False)
+    qk = make_inputs(B, T, H, K, K, seed=25)
+    dg["q"], dg["k"] = qk["q"], qk["k"]
+    xg = to_dev(dg, cuda_device, torch.float32)
+    o, ht = fused_recurrent_gdn2(*(xg[n] for n in NAMES), initial_state=None,
+                                 output_final_state=True, use_qk_l2norm_in_kernel=True)
+    rep = {n: (dg[n].repeat_interleave(HV // H, dim=2) if n in ("q", "k") else dg[n])
+           for n in NAMES}
+    ro, rh = O.recurrent_fwd(*(rep[n].double().numpy() for n in NAMES), None, norm_mode="fla")
+    assert rel(o, ro) < 1e-4 and rel(ht, rh) < 1e-4
+    assert _fault_word() == 0
