@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_recurrent(RecArgs a) {
 // Streaming variant for full states (K = V = D): a persistent CTA of 512
 // threads per SM walks (sequence, value head) units.  Each unit's whole fp32
 // state (D x D, contiguous) and its first token's q, k, b, g, v, w arrive by
-// 1-D bulk async copies into a two-buffer shared-memory ring one unit ahead,
+// 1-D bulk async copies into a three-buffer shared-memory ring two units ahead,
 // so HBM streams the next state while this one is updated; the new state
 // leaves from registers with 128-bit streaming stores.  Same arithmetic,
 // order and reductions as k_recurrent (thread (rg, cg) holds rows
@@ -230,23 +230,24 @@ __device__ __forceinline__ RecUnit rec_unit(const RecArgs& a, int u) {
 template <int D>
 struct RecStreamSmem {
   static constexpr int NTH = 512;
+  static constexpr int NBUF = 3;
   static constexpr int CG = D / 4, RG = NTH / CG, RPT = D / RG;
   static constexpr uint32_t state = D * D * 4;     // one state buffer
   static constexpr uint32_t raw = 24 * D;           // q, k, b, v, w (<= 4 B each) and g of one token
   static constexpr uint32_t oState = 0;
-  static constexpr uint32_t oRaw = 2 * state;
-  static constexpr uint32_t oF = oRaw + 2 * raw;                   // sq sk sg sb sv sw floats
+  static constexpr uint32_t oRaw = NBUF * state;
+  static constexpr uint32_t oF = oRaw + NBUF * raw;                // sq sk sg sb sv sw floats
   static constexpr uint32_t oRed = oF + 6 * D * 4;                 // red[RG][D]
-  static constexpr uint32_t oUnit = oRed + RG * D * 4;             // RecUnit[2]
-  static constexpr uint32_t oBar = oUnit + 2 * sizeof(RecUnit);    // mbarrier[2]
-  static constexpr uint32_t oNorm = oBar + 16;
+  static constexpr uint32_t oUnit = oRed + RG * D * 4;             // RecUnit[NBUF]
+  static constexpr uint32_t oBar = oUnit + NBUF * sizeof(RecUnit);  // mbarrier[NBUF]
+  static constexpr uint32_t oNorm = oBar + 8 * NBUF;
   static constexpr uint32_t bytes = oNorm + 16 + 128;
 };
 
 template <typename T, int D>
 __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
   using S_ = RecStreamSmem<D>;
-  constexpr int NTH = S_::NTH, CG = S_::CG, RG = S_::RG, RPT = S_::RPT;
+  constexpr int NTH = S_::NTH, CG = S_::CG, RG = S_::RG, RPT = S_::RPT, NBUF = S_::NBUF;
   constexpr int EB = (int)sizeof(T);
   extern __shared__ __align__(128) unsigned char sm[];
   float* sq = reinterpret_cast<float*>(sm + S_::oF);
@@ -296,23 +297,27 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
   };
 
   if (tid == 0) {
-    tc::mbar_init(&bar[0], 1);
-    tc::mbar_init(&bar[1], 1);
+    for (int i = 0; i < NBUF; ++i) tc::mbar_init(&bar[i], 1);
     tc::fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0 && (int)blockIdx.x < n_units) issue(blockIdx.x, 0);
+  if (tid == 0)
+    for (int i = 0; i < NBUF - 1; ++i)
+      if ((int)blockIdx.x + i * (int)gridDim.x < n_units) issue(blockIdx.x + i * gridDim.x, i);
 
   int fault = 0;
   int it = 0;  // after a fault: the iteration whose copy did not land
   for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
-    const int buf = it & 1;
-    const uint32_t par = (uint32_t)(it >> 1) & 1u;
+    const int buf = it % NBUF;
+    const uint32_t par = (uint32_t)(it / NBUF) & 1u;
     if (!tc::mbar_wait(&bar[buf], par)) fault = 1;
     if (__syncthreads_or(fault)) break;
-    // the other buffer's unit is done (its state went to registers and its
-    // token was read before the previous unit's last barrier)
-    if (tid == 0 && u + (int)gridDim.x < n_units) issue(u + gridDim.x, buf ^ 1);
+    // the buffer NBUF-1 units ahead held the previous unit, which is done (its
+    // state went to registers and its token was read before its last barrier)
+    {
+      const int ahead = u + (NBUF - 1) * (int)gridDim.x;
+      if (tid == 0 && ahead < n_units) issue(ahead, (it + NBUF - 1) % NBUF);
+    }
     const RecUnit ui = sUnit[buf];
     if (ui.skip) continue;
 
@@ -424,7 +429,8 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
     }
   }
   if (fault && tid == 0) {
-    tc::mbar_wait(&bar[it & 1], (uint32_t)(it >> 1) & 1u);  // bounded: let it land
+    // bounded waits: let the copies still in flight land
+    for (int j = it; j < it + NBUF - 1; ++j) tc::mbar_wait(&bar[j % NBUF], (uint32_t)(j / NBUF) & 1u);
     atomicOr(a.fault, 4u);
   }
 }
