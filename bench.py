@@ -15,8 +15,13 @@ the reported time is the max over ranks.
   is the four kernel phases called through the C ABI, each bracketed by CUDA
   events on the launch stream, which also gives the live per-kernel roofline.
 * ``e2e``: the same metric through the public API (``chunk_gdn2`` + autograd)
-  with the step's inputs copied from pinned host memory and every gradient
-  (and the output) read back to the host inside the timed region.
+  as a training step sees it: every step copies its inputs from pinned host
+  memory -- q, k, v, the upstream gradient dO, and the config's per-(token,
+  head) beta and log-decay, broadcast channel-wise on the device -- runs the
+  forward, forms the loss sum(o * dO) (whose gradient with respect to o is
+  dO), runs the backward into device gradients and reads the loss back to the
+  host.  The next step's copy runs on a second stream while the current step
+  computes (a double-buffered loader); every copy is inside the timed region.
 * ``decode``: BASELINE config 2 (B=256 H=16 K=V=128 fp32 state, in-place
   recurrent step, bf16 inputs), state read+write GB/s.
 * ``cpu_baseline``: the reference algorithm's CPU path (PyTorch restatement in
@@ -198,7 +203,7 @@ def make_config1(device, seed):
     b = beta[..., None].expand(B, T, H, K).to(bf).contiguous()
     w = beta[..., None].expand(B, T, H, V).to(bf).contiguous()
     do = torch.randn(B, T, H, V, device=device, generator=gen).to(bf)
-    return dict(q=q, k=k, v=v, g=g, b=b, w=w, do=do)
+    return dict(q=q, k=k, v=v, g=g, b=b, w=w, do=do), dict(beta=beta.to(bf), g=gs)
 
 
 # ---------------------------------------------------------------------------
@@ -211,7 +216,7 @@ def run_b200(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     lib = N.load()
-    x = make_config1(dev, 1234 + rank)
+    x, x_scalar = make_config1(dev, 1234 + rank)
     tables = N.seq_tables(B, T, dev)
     prob = N.ChunkProblem(H, K, V, N.dtype_code(torch.bfloat16), 1, K ** -0.5, tables.struct())
     sbytes = lib.gdn2_chunk_saved_bytes(prob)
@@ -266,35 +271,67 @@ def run_b200(args, world, rank, local):
     value = tokens / (ms_step / 1e3)
 
     # ---- end to end through the public API with host buffers ---------------
-    host = {n: t.cpu().pin_memory() for n, t in x.items()}
-    out_host = {n: torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-                for n, t in list(x.items())[:6]}
-    o_host = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+    # Host holds the config's own draws: q, k, v, dO [B,T,H,D] and the
+    # per-(token, head) beta and log-decay [B,T,H]; the channel-wise b, w, g
+    # the API takes are broadcast on the device.  Step i+1's inputs are copied
+    # on a second stream into the other half of a double buffer while step i
+    # computes; every copy is inside the timed region.
+    host = {n: x[n].cpu().pin_memory() for n in ("q", "k", "v", "do")}
+    host.update({n: t.cpu().pin_memory() for n, t in x_scalar.items()})
+    bufs = [{n: torch.empty_like(t, device=dev) for n, t in host.items()} for _ in range(2)]
+    loss_host = torch.empty((), dtype=torch.float32, pin_memory=True)
     h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = sum(t.numel() * t.element_size() for t in out_host.values()) + o_host.numel() * 2
+    d2h = loss_host.numel() * loss_host.element_size()
+    copy_stream = torch.cuda.Stream(dev)
+    ev_copied = [torch.cuda.Event() for _ in range(2)]
+    ev_consumed = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
+    grads = []
 
-    def e2e_step():
-        d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
-        leaves = [d[n].requires_grad_() for n in ("q", "k", "v", "g", "b", "w")]
+    def issue_copy(i, after=None):
+        j = i % 2
+        with torch.cuda.stream(copy_stream):
+            if after is not None:
+                copy_stream.wait_event(after)
+            if used[j]:
+                copy_stream.wait_event(ev_consumed[j])
+            for n, t in host.items():
+                bufs[j][n].copy_(t, non_blocking=True)
+            ev_copied[j].record(copy_stream)
+        used[j] = True
+
+    def compute(i):
+        j = i % 2
+        stream.wait_event(ev_copied[j])
+        d = bufs[j]
+        b_ = d["beta"][..., None].expand(B, T, H, K).contiguous()
+        w_ = d["beta"][..., None].expand(B, T, H, V).contiguous()
+        g_ = d["g"][..., None].expand(B, T, H, K).contiguous()
+        leaves = [t.detach().requires_grad_() for t in (d["q"], d["k"], d["v"], g_, b_, w_)]
         out, _ = chunk_gdn2(*leaves, use_qk_l2norm_in_kernel=True)
-        gr = torch.autograd.grad(out, leaves, d["do"])
-        o_host.copy_(out.detach(), non_blocking=True)
-        for (n, hbuf), gt in zip(out_host.items(), gr):
-            hbuf.copy_(gt, non_blocking=True)
+        loss = (out * d["do"]).sum(dtype=torch.float32)
+        grads[:] = torch.autograd.grad(loss, leaves)  # stay on the device
+        loss_host.copy_(loss.detach(), non_blocking=True)
+        ev_consumed[j].record(stream)
+
+    def e2e_run(n, start=None):
+        issue_copy(0, start)
+        for i in range(n):
+            if i + 1 < n:
+                issue_copy(i + 1)
+            compute(i)
 
     e2e_steps = max(1, min(args.steps, 5))
-    for _ in range(min(args.warmup, 2)):
-        e2e_step()
+    e2e_run(min(args.warmup, 2))
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    e2e_run(e2e_steps, e0)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
-    del host, out_host
+    del host, bufs, grads
 
     # ---- decode (config 2) -------------------------------------------------
     dec = run_decode(dev, lib, N) if rank == 0 else None
@@ -364,7 +401,7 @@ def run_profile_case(args, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     lib = N.load()
-    x = make_config1(dev, 99)
+    x, _ = make_config1(dev, 99)
     tables = N.seq_tables(B, T, dev)
     prob = N.ChunkProblem(H, K, V, N.dtype_code(torch.bfloat16), 1, K ** -0.5, tables.struct())
     sbytes = lib.gdn2_chunk_saved_bytes(prob)
@@ -534,8 +571,16 @@ def _cpu_sample_step(threads):
     return time.perf_counter() - t0
 
 
-def cpu_baseline(steps=1, warm=False):
-    threads = os.cpu_count() or 1
+def host_threads():
+    """Cores this process may run on (the container's share, not the host's)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(steps=3, warm=True):
+    threads = host_threads()
     if warm:
         _cpu_sample_step(threads)
     ts = [_cpu_sample_step(threads) for _ in range(steps)]
@@ -553,12 +598,12 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     for _ in range(args.warmup):
-        _cpu_sample_step(os.cpu_count() or 1)
-    ts = [_cpu_sample_step(os.cpu_count() or 1) for _ in range(args.steps)]
+        _cpu_sample_step(host_threads())
+    ts = [_cpu_sample_step(host_threads()) for _ in range(args.steps)]
     t = statistics.mean(ts)
     full_tokens = T * CPU_SAMPLE_HEADS / H
     value = full_tokens / t
-    cores = os.cpu_count() or 1
+    cores = host_threads()
     line = {
         "impl": "reference",
         "metric": "gdn2 fwd+bwd tokens/s (BASELINE config 1)",
