@@ -136,22 +136,33 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vWg), LDS, gw + v0, ldv, len, nv);
   };
 
-  // ---- phase 0: one round trip for q, k, b, g, A and the first slice -------
-  cp_tile16<T, kChunk, D, NTH>(sq, LDK, reinterpret_cast<const T*>(a.q) + offk, ldk, len, K);
-  cp_tile16<T, kChunk, D, NTH>(sk, LDK, reinterpret_cast<const T*>(a.k) + offk, ldk, len, K);
-  cp_tile16<T, kChunk, D, NTH>(sb, LDK, reinterpret_cast<const T*>(a.b) + offk, ldk, len, K);
-  cp_tile32<kChunk, D, NTH>(sG, LDG, a.g + offk, ldk, len, K);
+  // The value side needs only A and the value slices; q, k, b, g (key side)
+  // ride along with the next-slice copies (q with slice 1, k and b with
+  // slice 2, g with slice 3; all remaining ones with the last) so their
+  // latency hides behind the value-side products.
+  auto issue_key_part = [&](int part) {
+    if (part == 0) {
+      cp_tile16<T, kChunk, D, NTH>(sq, LDK, reinterpret_cast<const T*>(a.q) + offk, ldk, len, K);
+    } else if (part == 1) {
+      cp_tile16<T, kChunk, D, NTH>(sk, LDK, reinterpret_cast<const T*>(a.k) + offk, ldk, len, K);
+      cp_tile16<T, kChunk, D, NTH>(sb, LDK, reinterpret_cast<const T*>(a.b) + offk, ldk, len, K);
+    } else {
+      cp_tile32<kChunk, D, NTH>(sG, LDG, a.g + offk, ldk, len, K);
+    }
+  };
+
+  // ---- phase 0: A and the first slice --------------------------------------
   cp_tile16<T, kChunk, kChunk, NTH>(
       sA, LDC, reinterpret_cast<const T*>(a.saved + a.L.a) + ch * kChunk * kChunk, kChunk, kChunk,
       kChunk);
   issue_slice(0, 0);
   cp_async_commit();
+  const int nslices = (V + 31) / 32;
+  if (nslices == 1) {
+    for (int part = 0; part < 3; ++part) issue_key_part(part);
+    cp_async_commit();
+  }
   for (int i = tid; i < D; i += NTH) dgl[i] = 0.f;
-  cp_async_wait<0>();
-  __syncthreads();
-  // chunk-local log2 cumulative decay; row norms
-  col_scan64_reg<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(W + L::vZ), kLog2e);
-  row_norms16<T, D, NTH>(sq, sk, LDK, rq, rk, a.l2norm);
 
   // ---- phase V --------------------------------------------------------------
   float accQ[1][NTO][4], accKd[1][NTO][4], accW[1][NTO][4], accAqk[1][2][4], accDA[1][2][4];
@@ -163,12 +174,16 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   T* sZ = reinterpret_cast<T*>(W + L::vZ);
   T* gdv = reinterpret_cast<T*>(a.dv) + offv;
   T* gdw = reinterpret_cast<T*>(a.dw) + offv;
-  const int nslices = (V + 31) / 32;
   for (int s = 0; s < nslices; ++s) {
     const int cur = s & 1, v0 = 32 * s, nv = min(32, V - v0);
     if (s + 1 < nslices) {
       __syncthreads();  // the other slot's last readers are done
       issue_slice(v0 + 32, cur ^ 1);
+      if (s + 2 == nslices) {
+        for (int part = s; part < 3; ++part) issue_key_part(part);
+      } else if (s < 3) {
+        issue_key_part(s);
+      }
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -221,7 +236,10 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
         }
     }
   }
-  __syncthreads();  // phase V buffers are dead from here on
+  __syncthreads();  // phase V buffers are dead from here on; q, k, b, g have landed
+  // chunk-local log2 cumulative decay; row norms
+  col_scan64_reg<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(W + L::vZ), kLog2e);
+  row_norms16<T, D, NTH>(sq, sk, LDK, rq, rk, a.l2norm);
 
   // ---- dump dW and dAqk ------------------------------------------------------
   T* sDAqk = reinterpret_cast<T*>(W + L::kDAqk);
