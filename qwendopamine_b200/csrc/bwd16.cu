@@ -67,7 +67,7 @@ struct Bwd16Layout {
   static constexpr int kdG = 0;
   static constexpr int kX = kdG + kChunk * LDG * 4;
   static constexpr int kTmp = kX + kChunk * LDG * 4;
-  static constexpr int kScanEnd = kTmp + kThreadsB16 * 4;
+  static constexpr int kScanEnd = kTmp + 2 * kThreadsB16 * 4;
   static constexpr int W = phaseV > kEnd ? (phaseV > kScanEnd ? phaseV : kScanEnd)
                                          : (kEnd > kScanEnd ? kEnd : kScanEnd);
   static constexpr size_t bytes = (size_t)oW + W;
@@ -498,13 +498,39 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     }
   for (int i = tid; i < D; i += NTH) sX[i] = 0.f;
   __syncthreads();
-  col_scan64_reg<D, NTH, true>(sdG, LDG, sTmp, 1.f);
-  col_scan64_reg<D, NTH, false>(sX, LDG, sTmp, 1.f);
-  float* gdg = a.dg + offk;
-  for (int i = tid; i < kChunk * D; i += NTH) {
-    const int r = i / D, cc = i - r * D;
-    if (r < len && cc < K) gdg[(int64_t)r * ldk + cc] = sdG[r * LDG + cc] + sX[r * LDG + cc];
+  // one register-staged pass: suffix sums of dG and prefix sums of the
+  // shifted Kd terms down each column, added and stored straight to dg
+  {
+    constexpr int NSEG = NTH / D, RPS = kChunk / NSEG;
+    static_assert(NSEG * D == NTH && RPS * NSEG == kChunk, "scan shape");
+    const int col = tid % D, seg = tid / D;
+    float su[RPS], pr[RPS];
+#pragma unroll
+    for (int i = 0; i < RPS; ++i) {
+      su[i] = sdG[(seg * RPS + i) * LDG + col];
+      pr[i] = sX[(seg * RPS + i) * LDG + col];
+    }
+#pragma unroll
+    for (int i = 1; i < RPS; ++i) pr[i] += pr[i - 1];
+#pragma unroll
+    for (int i = RPS - 2; i >= 0; --i) su[i] += su[i + 1];
+    sTmp[seg * D + col] = pr[RPS - 1];
+    sTmp[NTH + seg * D + col] = su[0];
+    __syncthreads();
+    float offp = 0.f, offs = 0.f;
+#pragma unroll
+    for (int j = 0; j < NSEG; ++j) {
+      if (j < seg) offp += sTmp[j * D + col];
+      if (j > seg) offs += sTmp[NTH + j * D + col];
+    }
+    float* gdg = a.dg + offk;
+#pragma unroll
+    for (int i = 0; i < RPS; ++i) {
+      const int r = seg * RPS + i;
+      if (r < len && col < K) gdg[(int64_t)r * ldk + col] = (su[i] + offs) + (pr[i] + offp);
+    }
   }
+  // (the staging tiles below reuse this area after the next barrier)
 
   // ---- db, dk, dq with the l2norm backward -------------------------------------
   T* gdq = reinterpret_cast<T*>(a.dq) + offk;
