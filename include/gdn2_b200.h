@@ -165,7 +165,15 @@ int gdn2_chunk_bwd_noalloc(const gdn2_chunk_problem* p,
  * state pools indexed per sequence (slot stride state_stride elements) and
  * the update is in place; otherwise h0 / ht are [N,HV,K,V] and ht may equal h0
  * for an in-place update.  h0 == NULL means zero state; ht == NULL means the
- * final state is not stored. */
+ * final state is not stored.
+ * Speculative decoding (fused_recurrent_gdn2.py:217-226, 311-324): with
+ * state_indices_stride > 0, state_indices is [N, state_indices_stride]; the
+ * sequence starts from slot state_indices[n][a-1] (a = num_accepted_tokens[n],
+ * or 1 when num_accepted_tokens is NULL) and the state after its token t is
+ * written to slot state_indices[n][t] of ht (the pool, normally == h0).
+ * Negative slots are skipped (a negative starting slot skips the sequence).
+ * With state_indices_stride == 0 the indices are [N] and only the final state
+ * is written, to slot state_indices[n]. */
 typedef struct gdn2_recurrent_problem {
     int32_t B, T, H, HV, K, V;
     int32_t dtype;
@@ -175,6 +183,8 @@ typedef struct gdn2_recurrent_problem {
     const int32_t* cu_seqlens;
     const int32_t* state_indices;
     int64_t state_stride;
+    int64_t state_indices_stride;
+    const int32_t* num_accepted_tokens;
 } gdn2_recurrent_problem;
 
 int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p,

@@ -82,6 +82,8 @@ class RecurrentProblem(ctypes.Structure):
         ("cu_seqlens", c_void_p),
         ("state_indices", c_void_p),
         ("state_stride", c_int64),
+        ("state_indices_stride", c_int64),
+        ("num_accepted_tokens", c_void_p),
     ]
 
 

@@ -456,6 +456,12 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p, const void* q, const voi
                 p->B);
   if (p->state_indices && p->state_stride < (int64_t)p->HV * p->K * p->V)
     return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: state_stride too small");
+  if (p->state_indices_stride < 0 || (p->state_indices_stride > 0 && !p->state_indices))
+    return fail(GDN2_ERR_INVALID,
+                "gdn2_recurrent_fwd: state_indices_stride needs 2-D state_indices");
+  if (p->num_accepted_tokens && p->state_indices_stride == 0)
+    return fail(GDN2_ERR_INVALID,
+                "gdn2_recurrent_fwd: num_accepted_tokens needs 2-D state_indices");
   if (!q || !k || !v || !g || !b || !w || !o)
     return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: null tensor pointer");
   if (p->n_seqs == 0) return GDN2_OK;
@@ -467,6 +473,8 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p, const void* q, const voi
   a.cu = p->cu_seqlens;
   a.state_idx = p->state_indices;
   a.state_stride = p->state_stride;
+  a.idx_stride = p->state_indices_stride;
+  a.n_accepted = p->num_accepted_tokens;
   a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
   a.h0 = h0; a.o = o; a.ht = ht;
   cudaError_t e = fault_word(&a.fault);

@@ -81,8 +81,10 @@ struct RecArgs {
   int l2norm;
   int n_seqs;
   const int32_t* cu;         // [N+1] or null
-  const int32_t* state_idx;  // [N] or null
+  const int32_t* state_idx;  // [N] or [N][idx_stride] or null
   int64_t state_stride;
+  int64_t idx_stride;        // > 0: speculative decoding, a state slot per token
+  const int32_t* n_accepted; // [N] or null (speculative decoding)
   const void* q;
   const void* k;
   const void* v;

@@ -45,11 +45,19 @@ __global__ void __launch_bounds__(kThreads, 3) k_recurrent(RecArgs a) {
   }
   const float* h0p = nullptr;
   float* htp = nullptr;
+  const int32_t* tok_idx = nullptr;  // speculative decoding: a slot per token
   if (a.state_idx) {
-    const int64_t slot = a.state_idx[n];
+    int64_t slot;
+    if (a.idx_stride > 0) {
+      tok_idx = a.state_idx + (int64_t)n * a.idx_stride;
+      const int acc = a.n_accepted ? a.n_accepted[n] : 1;
+      slot = acc >= 1 ? tok_idx[acc - 1] : -1;
+    } else {
+      slot = a.state_idx[n];
+    }
     if (slot < 0) return;  // padded slot: nothing to do
     if (a.h0) h0p = a.h0 + slot * a.state_stride + (int64_t)hv * K * V;
-    if (a.ht) htp = a.ht + slot * a.state_stride + (int64_t)hv * K * V;
+    if (a.ht && !tok_idx) htp = a.ht + slot * a.state_stride + (int64_t)hv * K * V;
   } else {
     if (a.h0) h0p = a.h0 + ((int64_t)n * HV + hv) * K * V;
     if (a.ht) htp = a.ht + ((int64_t)n * HV + hv) * K * V;
@@ -76,6 +84,23 @@ __global__ void __launch_bounds__(kThreads, 3) k_recurrent(RecArgs a) {
       }
     }
   }
+
+  auto store_state = [&](float* dst) {
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const int r = rg * RPT + i;
+      if (r < K) {
+        if (vec && gcol < V) {
+          __stcs(reinterpret_cast<float4*>(dst + (int64_t)r * V + gcol),
+                 make_float4(S[i][0], S[i][1], S[i][2], S[i][3]));
+        } else if (!vec) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (gcol + j < V) dst[(int64_t)r * V + gcol + j] = S[i][j];
+        }
+      }
+    }
+  };
 
   const T* q = reinterpret_cast<const T*>(a.q);
   const T* k = reinterpret_cast<const T*>(a.k);
@@ -160,24 +185,13 @@ __global__ void __launch_bounds__(kThreads, 3) k_recurrent(RecArgs a) {
       }
     }
     __syncthreads();
-  }
-
-  if (htp) {
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      const int r = rg * RPT + i;
-      if (r < K) {
-        if (vec && gcol < V) {
-          __stcs(reinterpret_cast<float4*>(htp + (int64_t)r * V + gcol),
-                 make_float4(S[i][0], S[i][1], S[i][2], S[i][3]));
-        } else if (!vec) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (gcol + j < V) htp[(int64_t)r * V + gcol + j] = S[i][j];
-        }
-      }
+    if (tok_idx && a.ht) {  // the state after token t goes to its own slot
+      const int64_t slot = tok_idx[t];
+      if (slot >= 0) store_state(a.ht + slot * a.state_stride + (int64_t)hv * K * V);
     }
   }
+
+  if (htp) store_state(htp);
 }
 
 // ---------------------------------------------------------------------------
@@ -193,6 +207,7 @@ struct RecUnit {
   int64_t bos, Tn;
   const float* h0;
   float* ht;
+  const int32_t* tok_idx;  // speculative decoding: the state slot of each token
   int hv, hq, skip;
 };
 
@@ -210,16 +225,24 @@ __device__ __forceinline__ RecUnit rec_unit(const RecArgs& a, int u) {
   }
   r.h0 = nullptr;
   r.ht = nullptr;
+  r.tok_idx = nullptr;
   r.skip = 0;
   const int64_t KV = (int64_t)a.K * a.V;
   if (a.state_idx) {
-    const int64_t slot = a.state_idx[n];
+    int64_t slot;
+    if (a.idx_stride > 0) {
+      r.tok_idx = a.state_idx + (int64_t)n * a.idx_stride;
+      const int acc = a.n_accepted ? a.n_accepted[n] : 1;
+      slot = acc >= 1 ? r.tok_idx[acc - 1] : -1;
+    } else {
+      slot = a.state_idx[n];
+    }
     if (slot < 0) {
       r.skip = 1;
       return r;
     }
     if (a.h0) r.h0 = a.h0 + slot * a.state_stride + (int64_t)hv * KV;
-    if (a.ht) r.ht = a.ht + slot * a.state_stride + (int64_t)hv * KV;
+    if (a.ht && !r.tok_idx) r.ht = a.ht + slot * a.state_stride + (int64_t)hv * KV;
   } else {
     if (a.h0) r.h0 = a.h0 + ((int64_t)n * a.HV + hv) * KV;
     if (a.ht) r.ht = a.ht + ((int64_t)n * a.HV + hv) * KV;
@@ -417,6 +440,16 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
         o[og + idx] = from_f<T>(s);
       }
       __syncthreads();
+      if (ui.tok_idx && a.ht) {  // the state after token t goes to its own slot
+        const int64_t slot = ui.tok_idx[t];
+        if (slot >= 0) {
+          float* dst = a.ht + slot * a.state_stride + (int64_t)ui.hv * D * D;
+#pragma unroll
+          for (int i = 0; i < RPT; ++i)
+            __stcs(reinterpret_cast<float4*>(dst + (int64_t)(rg * RPT + i) * D + col0),
+                   make_float4(S[i][0], S[i][1], S[i][2], S[i][3]));
+        }
+      }
     }
 
     if (ui.ht) {

@@ -5,7 +5,10 @@
 signatures and semantics (fused_recurrent_gdn2.py:344-555): fp32 state
 ``[N, HV, K, V]`` (``[N, HV, V, K]`` with ``transpose_state_layout``), grouped
 value heads (HV a multiple of H), packed sequences through ``cu_seqlens``,
-state pools through ``ssm_state_indices`` with an in-place update, and an
+state pools through ``ssm_state_indices`` with an in-place update,
+speculative decoding (2-D ``ssm_state_indices`` with ``num_accepted_tokens``:
+start from slot ``indices[n, accepted[n]-1]`` and write the state after token
+``t`` to slot ``indices[n, t]``, reference :217-226, :311-324), and an
 optional preallocated ``out``.  The work is one launch of
 ``gdn2_recurrent_fwd`` from ``libgdn2_b200.so``; there is no CPU path.
 """
@@ -54,14 +57,18 @@ def fused_recurrent_gdn2_fwd(
             raise RuntimeError(
                 "fused_recurrent_gdn2: inputs must be CUDA tensors -- the B200 build has no "
                 "CPU path")
-    if num_accepted_tokens is not None:
+    spec = ssm_state_indices is not None and ssm_state_indices.ndim == 2
+    if num_accepted_tokens is not None and not spec:
+        raise ValueError(
+            "fused_recurrent_gdn2_fwd: num_accepted_tokens needs 2-D ssm_state_indices")
+    if spec and not inplace_final_state:
         raise NotImplementedError(
-            "fused_recurrent_gdn2_fwd: speculative decoding (num_accepted_tokens) is not "
-            "implemented in the B200 build")
-    if ssm_state_indices is not None and ssm_state_indices.ndim != 1:
+            "fused_recurrent_gdn2_fwd: 2-D ssm_state_indices are served in place (the state "
+            "after each token goes to its pool slot); inplace_final_state=False is not "
+            "supported with them")
+    if spec and transpose_state_layout:
         raise NotImplementedError(
-            "fused_recurrent_gdn2_fwd: 2-D ssm_state_indices (speculative decoding) are not "
-            "implemented in the B200 build")
+            "fused_recurrent_gdn2_fwd: 2-D ssm_state_indices with transpose_state_layout")
     if scale is None:
         scale = k.shape[-1] ** -0.5
     if use_gate_in_kernel:
@@ -100,13 +107,19 @@ def fused_recurrent_gdn2_fwd(
         cu32 = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
     idx32 = None
     stride = 0
+    idx_stride = 0
+    nat32 = None
     if ssm_state_indices is not None:
         idx32 = ssm_state_indices.to(device=q.device, dtype=torch.int32).contiguous()
         stride = h0.stride(0) if h0 is not None else HV * K * V
+        if spec:
+            idx_stride = idx32.shape[1]
+        if num_accepted_tokens is not None:
+            nat32 = num_accepted_tokens.to(device=q.device, dtype=torch.int32).contiguous()
     lib = N.load()
     prob = N.RecurrentProblem(B, T, H, HV, K, V, N.dtype_code(dt),
                               int(bool(use_qk_l2norm_in_kernel)), float(scale), Nseq,
-                              N.ptr(cu32), N.ptr(idx32), stride)
+                              N.ptr(cu32), N.ptr(idx32), stride, idx_stride, N.ptr(nat32))
     with torch.cuda.device(q.device):
         N.check(lib.gdn2_recurrent_fwd(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
                                        N.ptr(w), N.ptr(h0), N.ptr(out), N.ptr(final_state),

@@ -202,3 +202,49 @@ def test_stream_state_pool_varlen_gva_no_h0(cuda_device):
     ro, rh = O.recurrent_fwd(*(rep[n].double().numpy() for n in NAMES), None, norm_mode="fla")
     assert rel(o, ro) < 1e-4 and rel(ht, rh) < 1e-4
     assert _fault_word() == 0
+
+
+@pytest.mark.parametrize("K", [128, 32])
+def test_speculative_decoding_slots(cuda_device, K):
+    """2-D ssm_state_indices with num_accepted_tokens (reference
+    fused_recurrent_gdn2.py:217-226, 311-324): sequence n starts from slot
+    indices[n, accepted[n]-1] and the state after its token t lands in slot
+    indices[n, t]; negative slots are skipped; other slots stay untouched."""
+    from qwendopamine_b200 import fused_recurrent_gdn2_fwd
+
+    _fault_word()
+    cu = [0, 3, 4, 8]
+    idx = torch.tensor([[2, 7, 5, -1], [9, -1, -1, -1], [0, 4, 11, 6]], dtype=torch.int32)
+    acc = torch.tensor([2, 1, 3], dtype=torch.int32)
+    H = 2
+    d = make_inputs(1, cu[-1], H, K, K, seed=31 + K, h0=False)
+    gen = torch.Generator().manual_seed(32)
+    pool = torch.randn(12, H, K, K, generator=gen) * 0.05
+    x = to_dev(d, cuda_device, torch.float32)
+    pool_d = pool.to(cuda_device)
+    o, fs = fused_recurrent_gdn2_fwd(*(x[n] for n in NAMES), initial_state=pool_d,
+                                     inplace_final_state=True,
+                                     cu_seqlens=torch.tensor(cu, device=cuda_device),
+                                     ssm_state_indices=idx.to(cuda_device),
+                                     num_accepted_tokens=acc.to(cuda_device),
+                                     use_qk_l2norm_in_kernel=True)
+    assert fs.data_ptr() == pool_d.data_ptr()
+    expect = pool.clone()
+    written = set()
+    for n in range(3):
+        a_, e_ = cu[n], cu[n + 1]
+        sl = [t[:, a_:e_] for t in np_(d, NAMES)]
+        s0 = pool[int(idx[n, acc[n] - 1])][None].numpy()
+        ro, _, states = O.recurrent_fwd(*sl, s0, norm_mode="fla", return_states=True)
+        assert rel(o[:, a_:e_], ro) < 1e-4, n
+        for t in range(e_ - a_):
+            slot = int(idx[n, t])
+            if slot >= 0:
+                expect[slot] = torch.from_numpy(states[t + 1][0]).float()
+                written.add(slot)
+    for slot in range(12):
+        if slot in written:
+            assert rel(pool_d[slot], expect[slot]) < 1e-4, slot
+        else:
+            assert torch.equal(pool_d[slot].cpu(), pool[slot]), slot
+    assert _fault_word() == 0
