@@ -173,7 +173,12 @@ int gdn2_chunk_bwd_noalloc(const gdn2_chunk_problem* p,
  * written to slot state_indices[n][t] of ht (the pool, normally == h0).
  * Negative slots are skipped (a negative starting slot skips the sequence).
  * With state_indices_stride == 0 the indices are [N] and only the final state
- * is written, to slot state_indices[n]. */
+ * is written, to slot state_indices[n].
+ * Gate in kernel (fused_recurrent_gdn2.py:257-272): gate = 0 takes g as the
+ * log-decay; gate = 1 uses -exp(A_log[h]) * softplus(g + dt_bias[h][k]) and
+ * gate = 2 uses lower_bound * sigmoid(exp(A_log[h]) * (g + dt_bias[h][k])),
+ * h the key head of the value head (A_log fp32 [H], dt_bias fp32 [H*K] or
+ * NULL). */
 typedef struct gdn2_recurrent_problem {
     int32_t B, T, H, HV, K, V;
     int32_t dtype;
@@ -185,6 +190,10 @@ typedef struct gdn2_recurrent_problem {
     int64_t state_stride;
     int64_t state_indices_stride;
     const int32_t* num_accepted_tokens;
+    const float* A_log;
+    const float* dt_bias;
+    int32_t gate;
+    float lower_bound;
 } gdn2_recurrent_problem;
 
 int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p,

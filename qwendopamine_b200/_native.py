@@ -84,6 +84,10 @@ class RecurrentProblem(ctypes.Structure):
         ("state_stride", c_int64),
         ("state_indices_stride", c_int64),
         ("num_accepted_tokens", c_void_p),
+        ("A_log", c_void_p),
+        ("dt_bias", c_void_p),
+        ("gate", c_int32),
+        ("lower_bound", c_float),
     ]
 
 

@@ -462,6 +462,9 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p, const void* q, const voi
   if (p->num_accepted_tokens && p->state_indices_stride == 0)
     return fail(GDN2_ERR_INVALID,
                 "gdn2_recurrent_fwd: num_accepted_tokens needs 2-D state_indices");
+  if (p->gate < 0 || p->gate > 2 || (p->gate && !p->A_log))
+    return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: gate %d needs A_log (modes 0..2)",
+                p->gate);
   if (!q || !k || !v || !g || !b || !w || !o)
     return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: null tensor pointer");
   if (p->n_seqs == 0) return GDN2_OK;
@@ -475,6 +478,10 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p, const void* q, const voi
   a.state_stride = p->state_stride;
   a.idx_stride = p->state_indices_stride;
   a.n_accepted = p->num_accepted_tokens;
+  a.A_log = p->A_log;
+  a.dt_bias = p->dt_bias;
+  a.gate = p->gate;
+  a.lower_bound = p->lower_bound;
   a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
   a.h0 = h0; a.o = o; a.ht = ht;
   cudaError_t e = fault_word(&a.fault);

@@ -85,6 +85,10 @@ struct RecArgs {
   int64_t state_stride;
   int64_t idx_stride;        // > 0: speculative decoding, a state slot per token
   const int32_t* n_accepted; // [N] or null (speculative decoding)
+  const float* A_log;        // [H] (gate in kernel)
+  const float* dt_bias;      // [H*K] or null
+  int gate;                  // 0: g is the log-decay; 1: softplus gate; 2: lower-bound gate
+  float lower_bound;
   const void* q;
   const void* k;
   const void* v;

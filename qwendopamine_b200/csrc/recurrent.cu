@@ -13,6 +13,18 @@
 
 namespace gdn2 {
 
+// Log-decay of channel c from the raw gate input x (gate in kernel,
+// fused_recurrent_gdn2.py:257-272); hq is the key head.
+__device__ __forceinline__ float gate_logdecay(const RecArgs& a, float x, int hq, int c) {
+  if (a.gate == 0) return x;
+  if (a.dt_bias) x += a.dt_bias[hq * a.K + c];
+  const float A = expf(a.A_log[hq]);
+  if (a.gate == 2) return a.lower_bound / (1.f + expf(-A * x));  // lower_bound * sigmoid(A x)
+  const float sp = x > 20.f ? x : log1pf(expf(x));               // softplus
+  return -A * sp;
+}
+
+
 // One CTA per (sequence, value head, VB-column slice of the state): the
 // slice's K x VB fp32 block lives in registers, thread (rg, cg) holding rows
 // [rg*RPT, rg*RPT+RPT) x columns [4cg, 4cg+4) of the slice, so a warp moves
@@ -115,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 3) k_recurrent(RecArgs a) {
       const bool kk = idx < K;
       sq[idx] = kk ? to_f<T>(q[oq + idx]) : 0.f;
       sk[idx] = kk ? to_f<T>(k[oq + idx]) : 0.f;
-      sg[idx] = kk ? expf(a.g[og + idx]) : 0.f;
+      sg[idx] = kk ? expf(gate_logdecay(a, a.g[og + idx], hq, idx)) : 0.f;
       sb[idx] = kk ? to_f<T>(b[og + idx]) : 0.f;
     }
     for (int idx = tid; idx < VB; idx += blockDim.x) {
@@ -366,7 +378,8 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
           sq[idx] = to_f<T>(reinterpret_cast<const T*>(r)[idx]);
           sk[idx] = to_f<T>(reinterpret_cast<const T*>(r + D * EB)[idx]);
           sb[idx] = to_f<T>(reinterpret_cast<const T*>(r + 2 * D * EB)[idx]);
-          sg[idx] = expf(reinterpret_cast<const float*>(r + 3 * D * EB)[idx]);
+          sg[idx] = expf(gate_logdecay(a, reinterpret_cast<const float*>(r + 3 * D * EB)[idx],
+                                       ui.hq, idx));
           sv[idx] = to_f<T>(reinterpret_cast<const T*>(r + 3 * D * EB + D * 4)[idx]);
           sw[idx] = to_f<T>(reinterpret_cast<const T*>(r + 4 * D * EB + D * 4)[idx]);
         }
@@ -375,7 +388,7 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
           sq[idx] = to_f<T>(q[oq + idx]);
           sk[idx] = to_f<T>(k[oq + idx]);
           sb[idx] = to_f<T>(b[og + idx]);
-          sg[idx] = expf(a.g[og + idx]);
+          sg[idx] = expf(gate_logdecay(a, a.g[og + idx], ui.hq, idx));
           sv[idx] = to_f<T>(v[og + idx]);
           sw[idx] = to_f<T>(w[og + idx]);
         }

@@ -18,7 +18,6 @@ from __future__ import annotations
 import torch
 
 from .. import _native as N
-from .chunk_gdn2 import _gate
 
 __all__ = ["fused_recurrent_gdn2", "fused_recurrent_gdn2_fwd"]
 
@@ -71,10 +70,21 @@ def fused_recurrent_gdn2_fwd(
             "fused_recurrent_gdn2_fwd: 2-D ssm_state_indices with transpose_state_layout")
     if scale is None:
         scale = k.shape[-1] ** -0.5
+    gate, A32, dt32 = 0, None, None
     if use_gate_in_kernel:
+        # fused in the kernel, indexed by key head as the reference does
+        # (fused_recurrent_gdn2.py:257-272)
         if A_log is None:
             raise ValueError("A_log must be provided when use_gate_in_kernel=True.")
-        g = _gate(g, A_log, dt_bias, lower_bound)
+        gate = 2 if lower_bound is not None else 1
+        A32 = A_log.to(device=q.device, dtype=torch.float32).contiguous()
+        if A32.numel() < k.shape[2]:
+            raise ValueError(f"A_log needs one entry per key head ({k.shape[2]}); "
+                             f"got {A32.numel()}")
+        if dt_bias is not None:
+            dt32 = dt_bias.to(device=q.device, dtype=torch.float32).contiguous()
+            if dt32.numel() < k.shape[2] * k.shape[-1]:
+                raise ValueError("dt_bias needs H*K entries")
 
     B, T, H, K = k.shape
     HV, V = v.shape[2], v.shape[-1]
@@ -119,7 +129,9 @@ def fused_recurrent_gdn2_fwd(
     lib = N.load()
     prob = N.RecurrentProblem(B, T, H, HV, K, V, N.dtype_code(dt),
                               int(bool(use_qk_l2norm_in_kernel)), float(scale), Nseq,
-                              N.ptr(cu32), N.ptr(idx32), stride, idx_stride, N.ptr(nat32))
+                              N.ptr(cu32), N.ptr(idx32), stride, idx_stride, N.ptr(nat32),
+                              N.ptr(A32), N.ptr(dt32), gate,
+                              float(lower_bound) if lower_bound is not None else 0.0)
     with torch.cuda.device(q.device):
         N.check(lib.gdn2_recurrent_fwd(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
                                        N.ptr(w), N.ptr(h0), N.ptr(out), N.ptr(final_state),

@@ -248,3 +248,43 @@ def test_speculative_decoding_slots(cuda_device, K):
         else:
             assert torch.equal(pool_d[slot].cpu(), pool[slot]), slot
     assert _fault_word() == 0
+
+
+@pytest.mark.parametrize("K", [128, 32])
+@pytest.mark.parametrize("lower_bound", [None, -2.0])
+def test_gate_in_kernel_decode(cuda_device, K, lower_bound):
+    """Gate fused in the decode kernels (fused_recurrent_gdn2.py:257-272):
+    -exp(A_log[h]) softplus(g + dt_bias[h]) or lower_bound sigmoid(exp(A_log[h])
+    (g + dt_bias[h])), h the key head of each value head (grouped heads here)."""
+    from qwendopamine_b200 import fused_recurrent_gdn2
+
+    _fault_word()
+    B, T, H, HV = 3, 2, 2, 4
+    d = make_inputs(B, T, HV, K, K, seed=41 + K)
+    qk = make_inputs(B, T, H, K, K, seed=42 + K)
+    d["q"], d["k"] = qk["q"], qk["k"]
+    gen = torch.Generator().manual_seed(43)
+    raw = torch.randn(B, T, HV, K, generator=gen) * 2
+    A_log = torch.rand(H, generator=gen) * 2 - 1
+    dt_bias = torch.randn(H * K, generator=gen)
+    x = to_dev(d, cuda_device, torch.float32)
+    o, ht = fused_recurrent_gdn2(x["q"], x["k"], x["v"], raw.to(cuda_device), x["b"], x["w"],
+                                 A_log=A_log.to(cuda_device), dt_bias=dt_bias.to(cuda_device),
+                                 initial_state=x["h0"], output_final_state=True,
+                                 use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True,
+                                 lower_bound=lower_bound)
+    hk = torch.arange(HV) // (HV // H)  # key head of each value head
+    xx = raw.double() + dt_bias.double().view(H, K)[hk]
+    a = A_log.double().exp()[hk].view(HV, 1)
+    if lower_bound is None:
+        geff = -a * torch.nn.functional.softplus(xx)
+    else:
+        geff = lower_bound * torch.sigmoid(a * xx)
+    rep = {n: (d[n].repeat_interleave(HV // H, dim=2) if n in ("q", "k") else d[n])
+           for n in NAMES}
+    rep["g"] = geff
+    ro, rh = O.recurrent_fwd(*(rep[n].double().numpy() for n in NAMES), d["h0"].numpy(),
+                             norm_mode="fla")
+    assert rel(o, ro) < 1e-4
+    assert rel(ht, rh) < 1e-4
+    assert _fault_word() == 0
