@@ -66,13 +66,26 @@ typedef struct gdn2_seqs {
 
 /* A chunkwise problem: q,k,g,b are [rows,H,K]; v,w,o are [rows,H,V].
  * g (and dg) are always fp32 (the module's fp32_decay=True default,
- * gdn2.py:840-845); q,k,v,b,w,o and their gradients share `dtype`. */
+ * gdn2.py:840-845); q,k,v,b,w,o and their gradients share `dtype`.
+ * Gate in kernel (use_gate_in_kernel, chunk_gdn2.py:1194-1204, 2316-2323;
+ * bf16 problems with K and V multiples of 8 only): gate = 1 reads g as the raw
+ * pre-activation and uses -exp(A_log[h]) * softplus(g + dt_bias[h][k]) as the
+ * log-decay, gate = 2 uses lower_bound * sigmoid(exp(A_log[h]) * (g +
+ * dt_bias[h][k])); A_log fp32 [H], dt_bias fp32 [H*K] or NULL.  The backward
+ * then returns dg for the raw input and ADDS dL/dA_log into dA_log [H] and
+ * dL/d dt_bias into ddt_bias [H*K] (fp32; the caller zeroes them). */
 typedef struct gdn2_chunk_problem {
     int32_t H, K, V;
     int32_t dtype;
     int32_t use_qk_l2norm; /* use_qk_l2norm_in_kernel (chunk_gdn2.py:1283) */
     float scale;           /* defaults to K**-0.5 on the Python side        */
     gdn2_seqs seqs;
+    const float* A_log;
+    const float* dt_bias;
+    int32_t gate;          /* 0: g is the log-decay; 1, 2: gate in kernel   */
+    float lower_bound;
+    float* dA_log;
+    float* ddt_bias;
 } gdn2_chunk_problem;
 
 /* ---- library information ------------------------------------------------ */

@@ -64,6 +64,12 @@ class ChunkProblem(ctypes.Structure):
         ("use_qk_l2norm", c_int32),
         ("scale", c_float),
         ("seqs", Seqs),
+        ("A_log", c_void_p),
+        ("dt_bias", c_void_p),
+        ("gate", c_int32),
+        ("lower_bound", c_float),
+        ("dA_log", c_void_p),
+        ("ddt_bias", c_void_p),
     ]
 
 

@@ -78,7 +78,23 @@ int check_problem(const gdn2_chunk_problem* p, const char* fn) {
     return fail(GDN2_ERR_INVALID, "%s: missing chunk table", fn);
   if ((int64_t)p->seqs.n_chunks * p->H > 2147483647LL)
     return fail(GDN2_ERR_UNSUPPORTED, "%s: too many chunks", fn);
+  if (p->gate < 0 || p->gate > 2 || (p->gate && !p->A_log))
+    return fail(GDN2_ERR_INVALID, "%s: gate %d needs A_log (modes 0..2)", fn, p->gate);
+  if (p->gate && !(p->dtype == GDN2_DTYPE_BF16 && p->K % 8 == 0 && p->V % 8 == 0))
+    return fail(GDN2_ERR_UNSUPPORTED,
+                "%s: the gate in kernel is served by the bf16 kernels (K, V multiples of 8)", fn);
   return GDN2_OK;
+}
+
+GateArgs gate_of(const gdn2_chunk_problem* p) {
+  GateArgs g;
+  g.A_log = p->A_log;
+  g.dt_bias = p->dt_bias;
+  g.mode = p->gate;
+  g.lower_bound = p->lower_bound;
+  g.dA_log = p->dA_log;
+  g.ddt_bias = p->ddt_bias;
+  return g;
 }
 
 Seqs make_seqs(const gdn2_chunk_problem* p) {
@@ -317,6 +333,7 @@ int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.H = p->H; a.K = p->K; a.V = p->V;
   a.scale = p->scale;
   a.l2norm = p->use_qk_l2norm;
+  a.gate = gate_of(p);
   a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
   a.saved = static_cast<unsigned char*>(saved);
   a.L = L;
@@ -411,6 +428,7 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.H = p->H; a.K = p->K; a.V = p->V;
   a.scale = p->scale;
   a.l2norm = p->use_qk_l2norm;
+  a.gate = gate_of(p);
   a.q = q; a.k = k; a.v = v; a.g = g; a.b = b; a.w = w;
   a.dout = dout;
   a.saved = static_cast<const unsigned char*>(saved);

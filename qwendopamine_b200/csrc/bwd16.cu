@@ -39,7 +39,8 @@ struct Bwd16Layout {
   static constexpr int oA = oG + kChunk * LDG * 4;
   static constexpr int oMisc = oA + kChunk * LDC * 2;
   // misc floats: rq[64] rk[64] dgl[D] diag[64] pdq[4][64] pdk[4][64] flag[4] F[10][D]
-  static constexpr int nMisc = 64 + 64 + D + 64 + 256 + 256 + 4 + 10 * D;
+  //              dApart[16]
+  static constexpr int nMisc = 64 + 64 + D + 64 + 256 + 256 + 4 + 10 * D + 16;
   static constexpr int oW = oMisc + nMisc * 4;
   // phase V (offsets inside W)
   static constexpr int vH = 0;
@@ -99,6 +100,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   float* pdk = pdq + 256;   // [4][64]
   int* sFlag = reinterpret_cast<int*>(pdk + 256);
   float* sF = pdk + 256 + 4;  // [10][D] 2^(G_16I - G_(16J+15)), pair I(I+1)/2 + J
+  float* sDApart = sF + 10 * D;  // [16] per-warp dL/dA_log partial sums (gate in kernel)
   unsigned char* W = sm + L::oW;
 
   const int c = blockIdx.x, h = blockIdx.y;
@@ -237,6 +239,13 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     }
   }
   __syncthreads();  // phase V buffers are dead from here on; q, k, b, g have landed
+  if (a.gate.mode) {  // gate in kernel: raw input -> log-decay (valid rows / channels)
+    for (int i = tid; i < kChunk * D; i += NTH) {
+      const int r = i / D, cc = i - r * D;
+      if (r < len && cc < K) sG[r * LDG + cc] = gate_apply(a.gate, sG[r * LDG + cc], h, cc, K);
+    }
+    __syncthreads();
+  }
   // chunk-local log2 cumulative decay; row norms
   col_scan64_reg<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(W + L::vZ), kLog2e);
   row_norms16<T, D, NTH>(sq, sk, LDK, rq, rk, a.l2norm);
@@ -524,10 +533,32 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
       if (j > seg) offs += sTmp[NTH + j * D + col];
     }
     float* gdg = a.dg + offk;
+    if (!a.gate.mode) {
 #pragma unroll
-    for (int i = 0; i < RPS; ++i) {
-      const int r = seg * RPS + i;
-      if (r < len && col < K) gdg[(int64_t)r * ldk + col] = (su[i] + offs) + (pr[i] + offp);
+      for (int i = 0; i < RPS; ++i) {
+        const int r = seg * RPS + i;
+        if (r < len && col < K) gdg[(int64_t)r * ldk + col] = (su[i] + offs) + (pr[i] + offp);
+      }
+    } else {
+      // gate in kernel: dg of the raw input, plus this chunk's share of
+      // dL/d dt_bias (per channel) and dL/dA_log (per head)
+      const float* graw = a.g + offk;
+      float sdt = 0.f, sA = 0.f;
+#pragma unroll
+      for (int i = 0; i < RPS; ++i) {
+        const int r = seg * RPS + i;
+        if (r < len && col < K) {
+          float dAc;
+          const float dg = gate_grad(a.gate, graw[(int64_t)r * ldk + col],
+                                     (su[i] + offs) + (pr[i] + offp), h, col, K, &dAc);
+          gdg[(int64_t)r * ldk + col] = dg;
+          sdt += dg;
+          sA += dAc;
+        }
+      }
+      if (a.gate.ddt_bias && col < K) atomicAdd(a.gate.ddt_bias + h * K + col, sdt);
+      sA = warp_sum(sA);
+      if (lane == 0) sDApart[warp] = sA;
     }
   }
   // (the staging tiles below reuse this area after the next barrier)
@@ -575,6 +606,11 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     }
   }
   __syncthreads();
+  if (a.gate.mode && tid == 0 && a.gate.dA_log) {
+    float sA = 0.f;
+    for (int i = 0; i < NTH / 32; ++i) sA += sDApart[i];
+    atomicAdd(a.gate.dA_log + h, sA);
+  }
 #pragma unroll
   for (int j = 0; j < NTO; ++j)
 #pragma unroll

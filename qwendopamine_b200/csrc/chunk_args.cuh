@@ -6,11 +6,50 @@
 
 namespace gdn2 {
 
+// Gate in kernel: the raw g becomes the log-decay -exp(A_log[h]) *
+// softplus(g + dt_bias[h][k]) (mode 1) or lower_bound * sigmoid(exp(A_log[h])
+// * (g + dt_bias[h][k])) (mode 2); mode 0 takes g as it is.
+struct GateArgs {
+  const float* A_log;
+  const float* dt_bias;
+  int mode;
+  float lower_bound;
+  float* dA_log;    // backward: += dL/dA_log [H]
+  float* ddt_bias;  // backward: += dL/d dt_bias [H*K] or null
+};
+
+// Log-decay from the raw gate input g of head h, channel c.
+__device__ __forceinline__ float gate_apply(const GateArgs& gt, float g, int h, int c, int K) {
+  const float x = gt.dt_bias ? g + gt.dt_bias[h * K + c] : g;
+  const float A = expf(gt.A_log[h]);
+  if (gt.mode == 2) return gt.lower_bound / (1.f + expf(-A * x));
+  return -A * (x > 20.f ? x : log1pf(expf(x)));
+}
+
+// Backward of gate_apply (the reference's kda_gate_bwd): from dyg, the
+// gradient of the log-decay, the gradient of the raw input (returned) and the
+// term this element adds to dL/dA_log (*dA).
+__device__ __forceinline__ float gate_grad(const GateArgs& gt, float g, float dyg, int h, int c,
+                                           int K, float* dA) {
+  const float x = gt.dt_bias ? g + gt.dt_bias[h * K + c] : g;
+  const float A = expf(gt.A_log[h]);
+  if (gt.mode == 2) {
+    const float sig = 1.f / (1.f + expf(-A * x));
+    const float dg = dyg * gt.lower_bound * sig * (1.f - sig) * A;
+    *dA = dg * x;
+    return dg;
+  }
+  const float sig = 1.f / (1.f + expf(-x));
+  *dA = dyg * (-A * (x > 20.f ? x : log1pf(expf(x))));
+  return -A * dyg * sig;
+}
+
 struct FwdIntraArgs {
   Seqs seqs;
   int H, K, V;
   float scale;
   int l2norm;
+  GateArgs gate;
   const void* q;
   const void* k;
   const void* v;
@@ -55,6 +94,7 @@ struct BwdIntraArgs {
   int H, K, V;
   float scale;
   int l2norm;
+  GateArgs gate;
   const void* q;
   const void* k;
   const void* v;

@@ -262,6 +262,16 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
       tc::fence_async_smem();
       __syncthreads();
     }
+    if (a.gate.mode) {  // gate in kernel: raw input -> log-decay (valid rows / channels)
+      for (int i = tid; i < kChunk * D; i += NTH) {
+        const int r = i / D, cc = i - r * D;
+        if (r < len && cc < K) {
+          float* pg = reinterpret_cast<float*>(sG + swz<4>(r, cc));
+          *pg = gate_apply(a.gate, *pg, h, cc, K);
+        }
+      }
+      __syncthreads();
+    }
     // chunk-local log2 cumulative decay
     col_scan64_sw<D, NTH>(sG, reinterpret_cast<float*>(R), kLog2e);
     // row norms: warp w owns rows 4w .. 4w+3

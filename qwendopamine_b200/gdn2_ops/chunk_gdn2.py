@@ -21,9 +21,35 @@ from .. import _native as N
 __all__ = ["ChunkGDN2Function", "chunk_gdn2", "chunk_gdn2_fwd", "chunk_gdn2_bwd"]
 
 
-def _problem(H, K, V, dtype, l2norm, scale, tables):
-    return N.ChunkProblem(H, K, V, N.dtype_code(dtype), int(bool(l2norm)), float(scale),
+class GateParams:
+    """Gate-in-kernel parameters for the C ABI: fp32 ``A_log`` [H] and
+    ``dt_bias`` [H*K] (or None); mode 1 is ``-exp(A_log) * softplus(g +
+    dt_bias)``, mode 2 ``lower_bound * sigmoid(exp(A_log) * (g + dt_bias))``."""
+
+    def __init__(self, A_log, dt_bias, lower_bound):
+        self.A_log = A_log
+        self.dt_bias = dt_bias
+        self.mode = 1 if lower_bound is None else 2
+        self.lower_bound = 0.0 if lower_bound is None else float(lower_bound)
+
+
+def _problem(H, K, V, dtype, l2norm, scale, tables, gate=None, dA_log=None, ddt_bias=None):
+    prob = N.ChunkProblem(H, K, V, N.dtype_code(dtype), int(bool(l2norm)), float(scale),
                           tables.struct())
+    if gate is not None:
+        prob.A_log = N.ptr(gate.A_log)
+        prob.dt_bias = N.ptr(gate.dt_bias)
+        prob.gate = gate.mode
+        prob.lower_bound = gate.lower_bound
+        prob.dA_log = N.ptr(dA_log)
+        prob.ddt_bias = N.ptr(ddt_bias)
+    return prob
+
+
+def _gate_in_kernel_ok(dtype, K, V):
+    """The bf16 kernels apply the gate themselves (the C ABI's 16-bit path:
+    bf16, K and V multiples of 8); other problems gate with torch ops."""
+    return dtype == torch.bfloat16 and K % 8 == 0 and V % 8 == 0
 
 
 def _require_cuda(*ts):
@@ -40,17 +66,18 @@ def _aligned16(*ts):
 
 
 def chunk_gdn2_fwd(q, k, v, g, b, w, scale, initial_state, output_final_state, tables,
-                   use_qk_l2norm, keep_saved=True):
+                   use_qk_l2norm, keep_saved=True, gate=None):
     """Run the forward; returns ``(o, final_state, saved)``.
 
-    q, k, b: [B, T, H, K]; v, w: [B, T, H, V] (one dtype); g: fp32 [B, T, H, K];
+    q, k, b: [B, T, H, K]; v, w: [B, T, H, V] (one dtype); g: fp32 [B, T, H, K]
+    (the raw gate input when ``gate`` is a :class:`GateParams`);
     initial_state: fp32 [N, H, K, V] or None.
     """
     lib = N.load()
     B, T, H, K = q.shape
     V = v.shape[-1]
     q, k, v, g, b, w = _aligned16(q, k, v, g, b, w)
-    prob = _problem(H, K, V, q.dtype, use_qk_l2norm, scale, tables)
+    prob = _problem(H, K, V, q.dtype, use_qk_l2norm, scale, tables, gate)
     nbytes = lib.gdn2_chunk_saved_bytes(prob)
     if nbytes == 0 and tables.n_chunks > 0:
         N.check(N.ERR_INVALID, "gdn2_chunk_saved_bytes")
@@ -66,13 +93,19 @@ def chunk_gdn2_fwd(q, k, v, g, b, w, scale, initial_state, output_final_state, t
 
 
 def chunk_gdn2_bwd(q, k, v, g, b, w, saved, do, dht, scale, initial_state, tables,
-                   use_qk_l2norm):
-    """Run the backward; returns ``(dq, dk, dv, dg, db, dw, dh0)``."""
+                   use_qk_l2norm, gate=None):
+    """Run the backward; returns ``(dq, dk, dv, dg, db, dw, dh0)``, plus
+    ``(dA_log, ddt_bias)`` (fp32 [H], [H*K] or None) when ``gate`` is given."""
     lib = N.load()
     B, T, H, K = q.shape
     V = v.shape[-1]
     q, k, v, g, b, w, do = _aligned16(q, k, v, g, b, w, do)
-    prob = _problem(H, K, V, q.dtype, use_qk_l2norm, scale, tables)
+    dA_log = ddt_bias = None
+    if gate is not None:
+        dA_log = torch.zeros(H, dtype=torch.float32, device=q.device)
+        if gate.dt_bias is not None:
+            ddt_bias = torch.zeros(H * K, dtype=torch.float32, device=q.device)
+    prob = _problem(H, K, V, q.dtype, use_qk_l2norm, scale, tables, gate, dA_log, ddt_bias)
     nbytes = lib.gdn2_chunk_saved_bytes(prob)
     wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
     ws = torch.empty(max(wbytes, 1), dtype=torch.uint8, device=q.device)
@@ -91,6 +124,8 @@ def chunk_gdn2_bwd(q, k, v, g, b, w, saved, do, dht, scale, initial_state, table
                                N.ptr(saved), nbytes, N.ptr(do), N.ptr(dht), N.ptr(dq), N.ptr(dk),
                                N.ptr(dv), N.ptr(dg), N.ptr(db), N.ptr(dw), N.ptr(dh0), N.ptr(ws),
                                wbytes, st), "gdn2_chunk_bwd")
+    if gate is not None:
+        return dq, dk, dv, dg, db, dw, dh0, dA_log, ddt_bias
     return dq, dk, dv, dg, db, dw, dh0
 
 
@@ -120,17 +155,22 @@ class ChunkGDN2Function(torch.autograd.Function):
     """Autograd wrapper around the B200 chunkwise forward/backward.
 
     Positional arguments after the six token tensors mirror the reference's
-    ``ChunkGDN2Function.forward`` (chunk_gdn2.py:2339-2361), with the gate
-    already applied (``use_gate_in_kernel`` is resolved by :func:`chunk_gdn2`
-    before this function runs).
+    ``ChunkGDN2Function.forward`` (chunk_gdn2.py:2339-2361).  With ``A_log``
+    given, ``g`` is the raw gate input and the kernels apply the gate
+    (``use_gate_in_kernel``, chunk_gdn2.py:2316-2323); the backward then also
+    returns dA_log and d dt_bias.  Otherwise ``g`` is already the log-decay.
     """
 
     @staticmethod
     def forward(ctx, q, k, v, g, b, w, scale, initial_state, output_final_state,
-                use_qk_l2norm_in_kernel, tables, g_dtype):
+                use_qk_l2norm_in_kernel, tables, g_dtype, A_log=None, dt_bias=None,
+                lower_bound=None):
+        gate = GateParams(A_log, dt_bias, lower_bound) if A_log is not None else None
         o, ht, saved = chunk_gdn2_fwd(q, k, v, g, b, w, scale, initial_state,
-                                      output_final_state, tables, use_qk_l2norm_in_kernel)
-        ctx.save_for_backward(q, k, v, g, b, w, initial_state, saved)
+                                      output_final_state, tables, use_qk_l2norm_in_kernel,
+                                      gate=gate)
+        ctx.save_for_backward(q, k, v, g, b, w, initial_state, saved, A_log, dt_bias)
+        ctx.lower_bound = lower_bound
         ctx.scale = scale
         ctx.tables = tables
         ctx.l2 = use_qk_l2norm_in_kernel
@@ -141,17 +181,21 @@ class ChunkGDN2Function(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, do, dht):
-        q, k, v, g, b, w, h0, saved = ctx.saved_tensors
+        q, k, v, g, b, w, h0, saved, A_log, dt_bias = ctx.saved_tensors
         do = do.contiguous()
         if do.dtype != q.dtype:
             do = do.to(q.dtype)
         if dht is not None:
             dht = dht.float().contiguous()
-        dq, dk, dv, dg, db, dw, dh0 = chunk_gdn2_bwd(q, k, v, g, b, w, saved, do, dht,
-                                                     ctx.scale, h0, ctx.tables, ctx.l2)
-        # g entered as fp32 (chunk_gdn2 casts it), so its gradient stays fp32;
-        # autograd casts back through that conversion.
-        return (dq, dk, dv, dg, db, dw, None, dh0, None, None, None, None)
+        gate = GateParams(A_log, dt_bias, ctx.lower_bound) if A_log is not None else None
+        grads = chunk_gdn2_bwd(q, k, v, g, b, w, saved, do, dht, ctx.scale, h0, ctx.tables,
+                               ctx.l2, gate=gate)
+        dq, dk, dv, dg, db, dw, dh0 = grads[:7]
+        dA_log, ddt_bias = grads[7:] if gate is not None else (None, None)
+        # g, A_log and dt_bias entered as fp32 (chunk_gdn2 casts them), so their
+        # gradients stay fp32; autograd casts back through that conversion.
+        return (dq, dk, dv, dg, db, dw, None, dh0, None, None, None, None, dA_log, ddt_bias,
+                None)
 
 
 def chunk_gdn2(
@@ -237,12 +281,17 @@ def chunk_gdn2(
     if scale is None:
         scale = k.shape[-1] ** -0.5
 
+    B, T, H, K = q.shape
+    A32 = dt32 = lb = None
     if use_gate_in_kernel:
         assert "A_log" in kwargs, "A_log must be provided when use_gate_in_kernel=True."
         A_log, dt_bias = kwargs["A_log"], kwargs.get("dt_bias")
-        g = _gate(g, A_log, dt_bias, lower_bound if safe_gate else None)
-
-    B, T, H, K = q.shape
+        lb = lower_bound if safe_gate else None
+        if _gate_in_kernel_ok(q.dtype, K, v.shape[-1]):
+            A32 = A_log.float().reshape(H).contiguous()
+            dt32 = dt_bias.float().reshape(H * K).contiguous() if dt_bias is not None else None
+        else:
+            g = _gate(g, A_log, dt_bias, lb)
     dt = q.dtype
     g_dtype = g.dtype
     q, k, v, b, w = (x.to(dt).contiguous() for x in (q, k, v, b, w))
@@ -257,14 +306,15 @@ def chunk_gdn2(
         if cu_seqlens is not None and tables.total > T:
             raise ValueError(f"cu_seqlens[-1]={tables.total} exceeds the sequence length {T}")
         if return_intermediate_states:
+            gate = GateParams(A32, dt32, lb) if A32 is not None else None
             o, ht, saved = chunk_gdn2_fwd(q, k, v, g, b, w, scale, h0, output_final_state,
-                                          tables, use_qk_l2norm_in_kernel)
+                                          tables, use_qk_l2norm_in_kernel, gate=gate)
             hs = _intermediate_states(saved, tables, B, T, H, K, v.shape[-1], dt)
             if ht is not None and transpose_state_layout:
                 ht = ht.transpose(-1, -2)
             return o, ht, hs
         o, ht = ChunkGDN2Function.apply(q, k, v, g, b, w, scale, h0, output_final_state,
-                                        use_qk_l2norm_in_kernel, tables, g_dtype)
+                                        use_qk_l2norm_in_kernel, tables, g_dtype, A32, dt32, lb)
     if ht is not None and transpose_state_layout:
         ht = ht.transpose(-1, -2)
     return o, ht

@@ -137,3 +137,20 @@ def test_status_maps_to_python_exceptions(lib):
     with pytest.raises(N.GDN2Error):
         N.check(N.ERR_CUDA, "probe")
     N.check(N.OK, "probe")
+
+
+def test_gate_in_kernel_arguments_are_checked(lib):
+    """Gate in kernel: modes 0..2 only, A_log required, served by the bf16
+    kernels only (fp32 problems gate with torch ops on the Python side)."""
+    prob = _problem(dtype=1)
+    prob.gate = 3
+    prob.A_log = 0x1000
+    assert lib.gdn2_chunk_saved_bytes(prob) == 0
+    assert b"gate" in lib.gdn2_last_error()
+    prob.gate, prob.A_log = 1, None
+    assert lib.gdn2_chunk_fwd_intra(prob, *([None] * 6), None, 0, None) == N.ERR_INVALID
+    prob.A_log = 0x1000
+    assert lib.gdn2_chunk_saved_bytes(prob) > 0
+    f32 = _problem(dtype=0)
+    f32.gate, f32.A_log = 2, 0x1000
+    assert lib.gdn2_chunk_fwd_intra(f32, *([None] * 6), None, 0, None) == N.ERR_UNSUPPORTED

@@ -151,6 +151,65 @@ def test_gate_in_kernel_matches_explicit_gate(cuda_device):
     assert rel(o2, o1) < 1e-6
 
 
+def _gated_run(x, raw, A_log, dt_bias, lb, in_kernel, cu, do, dht):
+    """Forward + backward with the gate applied by the bf16 kernels
+    (``in_kernel``) or by torch ops on the same raw input."""
+    from qwendopamine_b200 import chunk_gdn2
+
+    leaves = {n: x[n].clone().requires_grad_() for n in NAMES if n != "g"}
+    graw = raw.clone().requires_grad_()
+    A = A_log.clone().requires_grad_()
+    dt = dt_bias.clone().requires_grad_() if dt_bias is not None else None
+    kw = dict(initial_state=x["h0"], output_final_state=True, use_qk_l2norm_in_kernel=True,
+              cu_seqlens=cu)
+    if in_kernel:
+        o, ht = chunk_gdn2(leaves["q"], leaves["k"], leaves["v"], graw, leaves["b"], leaves["w"],
+                           use_gate_in_kernel=True, A_log=A, dt_bias=dt,
+                           safe_gate=lb is not None, lower_bound=lb, **kw)
+    else:
+        H, K = raw.shape[-2:]
+        xg = graw + (dt.view(H, K) if dt is not None else 0)
+        a = A.exp().view(H, 1)
+        g = lb * torch.sigmoid(a * xg) if lb is not None else -a * F.softplus(xg)
+        o, ht = chunk_gdn2(leaves["q"], leaves["k"], leaves["v"], g, leaves["b"], leaves["w"], **kw)
+    ((o.float() * do).sum() + (ht * dht).sum()).backward()
+    out = {"o": o, "ht": ht, "g": graw.grad, "A_log": A.grad}
+    out.update({n: t.grad for n, t in leaves.items()})
+    if dt is not None:
+        out["dt_bias"] = dt.grad
+    return out
+
+
+@pytest.mark.parametrize("lb", [None, -3.0])
+@pytest.mark.parametrize("KV", [(128, 128), (64, 64), (64, 128)])
+@pytest.mark.parametrize("with_dt", [True, False])
+def test_gate_in_kernel_16bit_forward_backward(cuda_device, lb, KV, with_dt):
+    """bf16 with the gate applied inside the intra-chunk kernels (forward:
+    raw input -> log-decay before the cumulative scan; backward: dg of the raw
+    input plus dA_log and d dt_bias accumulated by the kernel) against the same
+    kernels fed the torch-computed gate, on packed ragged sequences."""
+    K, V = KV
+    H = 3
+    cu_l = [0, 5, 64, 150, 200]
+    T = cu_l[-1]
+    d = make_inputs(1, T, H, K, V, seed=K + V + (lb is None), dtype=torch.bfloat16, h0=False)
+    gen = torch.Generator().manual_seed(K + 11)
+    x = to_dev(d, cuda_device, torch.bfloat16)
+    x["h0"] = (torch.randn(len(cu_l) - 1, H, K, V, generator=gen) * 0.1).to(cuda_device)
+    raw = (torch.randn(1, T, H, K, generator=gen) * 2).to(cuda_device)
+    A_log = (torch.rand(H, generator=gen) * 2 - 1).to(cuda_device)
+    dt_bias = torch.randn(H * K, generator=gen).to(cuda_device) if with_dt else None
+    do = torch.randn(1, T, H, V, generator=gen).bfloat16().float().to(cuda_device)
+    dht = torch.randn(len(cu_l) - 1, H, K, V, generator=gen).to(cuda_device)
+    cu = torch.tensor(cu_l, device=cuda_device)
+    a = _gated_run(x, raw, A_log, dt_bias, lb, True, cu, do, dht)
+    r = _gated_run(x, raw, A_log, dt_bias, lb, False, cu, do, dht)
+    assert set(a) == set(r)
+    for n in r:
+        # the two gates differ only in fp32 rounding; outputs are bf16
+        assert rel(a[n], r[n]) < 5e-3, n
+
+
 # ---------------------------------------------------------------------------
 # backward
 # ---------------------------------------------------------------------------
