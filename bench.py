@@ -24,6 +24,11 @@ the reported time is the max over ranks.
   computes (a double-buffered loader); every copy is inside the timed region.
 * ``decode``: BASELINE config 2 (B=256 H=16 K=V=128 fp32 state, in-place
   recurrent step, bf16 inputs), state read+write GB/s.
+* ``block_ops``: the block's prologue / epilogue kernels at config-1 shapes
+  (bf16): the causal conv + SiLU over one [8, 4096, 2048] projection, forward
+  and backward, and the gated RMSNorm over o [8*4096*16, 128], forward and
+  backward; algorithmic bytes (each tensor read or written once) per launch
+  over the CUDA-event time, two alternating input sets (> L2).
 * ``cpu_baseline``: the reference algorithm's CPU path (PyTorch restatement in
   oracle/gdn2_torch_port.py, fp32, autograd backward), all host threads, on a
   bounded slice of the same workload; rank 0 at N=1 only.
@@ -335,6 +340,7 @@ def run_b200(args, world, rank, local):
 
     # ---- decode (config 2) -------------------------------------------------
     dec = run_decode(dev, lib, N) if rank == 0 else None
+    blk = run_block_ops(dev, lib, N) if rank == 0 else None
 
     if rank != 0:
         return
@@ -384,6 +390,7 @@ def run_b200(args, world, rank, local):
         "phases": phase_info,
         "tensor_peak_tflops": tflops_peak,
         "decode": dec,
+        "block_ops": blk,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
@@ -540,6 +547,62 @@ def run_decode(dev, lib, N):
             "steps": DEC_STEPS, "us_per_step": round(us, 2), "GBps": round(gbs, 1),
             "frac": round(gbs / hbm, 4), "state_bytes_per_step": nbytes,
             "peak_source": kind, "gpu_launches": DEC_STEPS}
+
+
+def run_block_ops(dev, lib, N, iters=20):
+    """Conv + SiLU and gated RMSNorm kernels at config-1 shapes (bf16)."""
+    bf = torch.bfloat16
+    gen = torch.Generator(device=dev).manual_seed(9)
+    D, Wc, rows = H * K, 4, B * T * H
+    st = N.stream_of(dev)
+    stream = torch.cuda.current_stream(dev)
+    hbm, _, kind = peaks()
+    sets = [dict(x=torch.randn(B, T, D, device=dev, generator=gen).to(bf),
+                 dy=torch.randn(B, T, D, device=dev, generator=gen).to(bf)) for _ in range(2)]
+    w = torch.randn(D, Wc, device=dev, generator=gen) * 0.5
+    y, dx = torch.empty_like(sets[0]["x"]), torch.empty_like(sets[0]["x"])
+    cp = N.ConvProblem(B, T, D, Wc, N.dtype_code(bf), 1)
+    cws = torch.empty(lib.gdn2_conv_bwd_workspace_bytes(cp), dtype=torch.uint8, device=dev)
+    dw = torch.empty(D, Wc, device=dev)
+    nw = 1 + 0.1 * torch.randn(V, device=dev, generator=gen).to(bf)
+    npb = N.NormProblem(rows, V, N.dtype_code(bf), N.dtype_code(bf), 1e-5, 0)
+    nws = torch.empty(lib.gdn2_gated_norm_bwd_workspace_bytes(npb), dtype=torch.uint8, device=dev)
+    ndw = torch.empty(V, device=dev)
+    nsets = [dict(x=s["x"].view(rows, V), z=s["dy"].view(rows, V)) for s in sets]
+    ny, ndx, ndz = (torch.empty(rows, V, device=dev, dtype=bf) for _ in range(3))
+
+    calls = {
+        "conv_fwd": (lambda s: lib.gdn2_conv_fwd(cp, N.ptr(s["x"]), N.ptr(w), None, None,
+                                                 N.ptr(y), None, st), 2),
+        "conv_bwd": (lambda s: lib.gdn2_conv_bwd(cp, N.ptr(s["x"]), N.ptr(w), None, None,
+                                                 N.ptr(s["dy"]), N.ptr(dx), N.ptr(dw), None, None,
+                                                 N.ptr(cws), cws.numel(), st), 3),
+        "norm_fwd": (lambda s: lib.gdn2_gated_norm_fwd(npb, N.ptr(s["x"]), N.ptr(s["z"]),
+                                                       N.ptr(nw), N.ptr(ny), st), 3),
+        "norm_bwd": (lambda s: lib.gdn2_gated_norm_bwd(npb, N.ptr(s["x"]), N.ptr(s["z"]),
+                                                       N.ptr(nw), N.ptr(ny), N.ptr(ndx),
+                                                       N.ptr(ndz), N.ptr(ndw), N.ptr(nws),
+                                                       nws.numel(), st), 5),
+    }
+    out = {"workload": "config1 shapes, bf16: conv+SiLU over [8,4096,2048] (W=4), gated "
+                       "RMSNorm over [524288,128]", "peak_source": kind}
+    tensor_bytes = B * T * D * 2
+    for name, (fn, ntensors) in calls.items():
+        src = nsets if name.startswith("norm") else sets
+        for i in range(3):
+            N.check(fn(src[i % 2]), name)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(iters):
+            N.check(fn(src[i % 2]), name)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / iters
+        gbs = ntensors * tensor_bytes / (us / 1e6) / 1e9
+        out[name] = {"us": round(us, 1), "GBps": round(gbs, 1), "frac": round(gbs / hbm, 4),
+                     "bytes": ntensors * tensor_bytes, "launches": iters}
+    return out
 
 
 # ---------------------------------------------------------------------------

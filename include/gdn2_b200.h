@@ -245,6 +245,70 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all,
                   int32_t forward, const float* init, float* state_out,
                   void* stream);
 
+/* ---- block prologue / epilogue -------------------------------------------
+ * Causal depthwise convolution with optional SiLU, one per q / k / v
+ * projection (ShortConvolution, gdn2.py:372-430), over x [B][T][D]:
+ *   c[b,t,d] = round(bias[d] + sum_{j<W} weight[d][j] * x[b, t-W+1+j, d])
+ *   y[b,t,d] = silu(c) (activation 1) or c (activation 0), rounded
+ * round() is the token dtype's rounding: the reference's convolution output
+ * is in that dtype before its activation.  Rows before t = 0 come from
+ * `prefix` (W-1 rows per batch entry; element (b, i, d) at prefix[b*sb +
+ * i*sw + d*sd]; the previous span's last tokens under sequence parallelism,
+ * or a decode cache [B][D][W-1] through its strides) or are zero when NULL.
+ * weight [D][W] and bias [D] (or NULL) are fp32 copies of the parameters.
+ * new_state (or NULL) receives the last W-1 rows of [prefix; x] as
+ * [B][D][W-1] (the reference's conv cache layout).  D % 8 == 0, W <= 4, and
+ * x / y / dy / dx start on 16-byte boundaries. */
+typedef struct gdn2_conv_problem {
+    int32_t B, T, D, W;
+    int32_t dtype;
+    int32_t activation;          /* 0: none, 1: silu */
+    int64_t prefix_sb, prefix_sw, prefix_sd;  /* element strides of prefix */
+} gdn2_conv_problem;
+
+int gdn2_conv_fwd(const gdn2_conv_problem* p, const void* x, const float* weight,
+                  const float* bias, const void* prefix, void* y, void* new_state,
+                  void* stream);
+/* Backward: dx [B][T][D] (token dtype); dweight [D][W] and dbias [D] (or
+ * NULL) fp32, written; dprefix (or NULL) fp32 [B][W-1][D] contiguous, the
+ * gradient of the prefix rows (sent back to the previous span's owner under
+ * sequence parallelism).  Deterministic: per-block partial sums go through
+ * `workspace` and are reduced in a fixed order. */
+size_t gdn2_conv_bwd_workspace_bytes(const gdn2_conv_problem* p);
+int gdn2_conv_bwd(const gdn2_conv_problem* p, const void* x, const float* weight,
+                  const float* bias, const void* prefix, const void* dy, void* dx,
+                  float* dweight, float* dbias, float* dprefix, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* SiLU-gated RMSNorm of the block epilogue (RMSNormGated, gdn2.py:433-452)
+ * over the last dimension N of x, z [rows][N]:
+ *   y = x * rsqrt(mean(x^2) + eps) * weight * silu(z)
+ * evaluated as the reference does, in the input dtype: every intermediate
+ * (x^2, the mean, mean + eps, its rsqrt, the products, silu(z)) is rounded
+ * to `dtype`; a product with an fp32 weight is fp32, and y has the promoted
+ * type (dtype, weight_dtype).  weight_dtype is `dtype` or fp32.  With
+ * fp32_math = 1 (the reference under torch.autocast, where pow and rsqrt run
+ * in fp32): x^2, the mean, rsqrt and every product stay fp32, silu(z) is
+ * still rounded to `dtype`, and y is fp32 (weight_dtype must be fp32).
+ * N % 8 == 0 and N <= 256. */
+typedef struct gdn2_norm_problem {
+    int64_t rows;
+    int32_t N;
+    int32_t dtype;          /* x, z, dx, dz */
+    int32_t weight_dtype;   /* weight; dy and y have the promoted type */
+    float eps;
+    int32_t fp32_math;
+} gdn2_norm_problem;
+
+int gdn2_gated_norm_fwd(const gdn2_norm_problem* p, const void* x, const void* z,
+                        const void* weight, void* y, void* stream);
+/* Backward (fp32 arithmetic): dx, dz in `dtype`; dweight fp32 [N], written. */
+size_t gdn2_gated_norm_bwd_workspace_bytes(const gdn2_norm_problem* p);
+int gdn2_gated_norm_bwd(const gdn2_norm_problem* p, const void* x, const void* z,
+                        const void* weight, const void* dy, void* dx, void* dz,
+                        float* dweight, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
 /* Device-side fault bits.  Kernels that wait on asynchronous copies or on
  * tensor-core completion bound every wait in time (about one second); a wait
  * that runs out makes the kernel release its tensor memory, return without

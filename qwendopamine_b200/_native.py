@@ -40,6 +40,12 @@ EXPORTS = (
     "gdn2_cp_fwd_prescan",
     "gdn2_cp_bwd_prescan",
     "gdn2_cp_merge",
+    "gdn2_conv_fwd",
+    "gdn2_conv_bwd_workspace_bytes",
+    "gdn2_conv_bwd",
+    "gdn2_gated_norm_fwd",
+    "gdn2_gated_norm_bwd_workspace_bytes",
+    "gdn2_gated_norm_bwd",
     "gdn2_fault_status",
 )
 
@@ -97,6 +103,31 @@ class RecurrentProblem(ctypes.Structure):
     ]
 
 
+class ConvProblem(ctypes.Structure):
+    _fields_ = [
+        ("B", c_int32),
+        ("T", c_int32),
+        ("D", c_int32),
+        ("W", c_int32),
+        ("dtype", c_int32),
+        ("activation", c_int32),
+        ("prefix_sb", c_int64),
+        ("prefix_sw", c_int64),
+        ("prefix_sd", c_int64),
+    ]
+
+
+class NormProblem(ctypes.Structure):
+    _fields_ = [
+        ("rows", c_int64),
+        ("N", c_int32),
+        ("dtype", c_int32),
+        ("weight_dtype", c_int32),
+        ("eps", c_float),
+        ("fp32_math", c_int32),
+    ]
+
+
 class GDN2Error(RuntimeError):
     """A libgdn2_b200 entry point returned an error status."""
 
@@ -113,6 +144,8 @@ def _declare(lib):
     P = ctypes.POINTER
     cp = P(ChunkProblem)
     rp = P(RecurrentProblem)
+    vp = P(ConvProblem)
+    np_ = P(NormProblem)
     v = c_void_p
     sig = {
         "gdn2_version": ([], ctypes.c_char_p),
@@ -136,6 +169,12 @@ def _declare(lib):
         "gdn2_cp_bwd_prescan": ([cp, v, c_size_t, v, v, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_cp_merge": ([cp, v, v, c_int32, c_int32, c_int32, v, v, v], ctypes.c_int),
         "gdn2_fault_status": ([v, c_int32], ctypes.c_int),
+        "gdn2_conv_fwd": ([vp, v, v, v, v, v, v, v], ctypes.c_int),
+        "gdn2_conv_bwd_workspace_bytes": ([vp], c_size_t),
+        "gdn2_conv_bwd": ([vp, v, v, v, v, v, v, v, v, v, v, c_size_t, v], ctypes.c_int),
+        "gdn2_gated_norm_fwd": ([np_, v, v, v, v, v], ctypes.c_int),
+        "gdn2_gated_norm_bwd_workspace_bytes": ([np_], c_size_t),
+        "gdn2_gated_norm_bwd": ([np_, v, v, v, v, v, v, v, v, c_size_t, v], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -1,0 +1,765 @@
+// block_ops.cu -- the GDN-2 block's prologue and epilogue around the core
+// recurrence, and their extern "C" entry points:
+//
+// * causal depthwise convolution + SiLU over [B][T][D] token rows
+//   (ShortConvolution, gdn2.py:372-430): forward, backward (dx, the prefix
+//   gradient, and dweight / dbias through per-block partial sums reduced in a
+//   fixed order), and the decode-cache update;
+// * SiLU-gated RMSNorm over the last dimension (RMSNormGated,
+//   gdn2.py:433-452), forward with the reference's input-dtype rounding after
+//   every step, backward in fp32.
+//
+// Both are HBM-bound streaming kernels: each thread owns a few consecutive
+// channels (one 8- or 16-byte vector of a row), a warp covers a contiguous
+// run of a row's channels, and rows are loaded a run at a time before any
+// arithmetic so every thread keeps several loads in flight.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdint>
+#include <type_traits>
+
+#include "../../include/gdn2_b200.h"
+
+#include "common.cuh"
+
+namespace gdn2 {
+int set_error(int code, const char* msg);  // abi.cu: the per-thread last error
+namespace {
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  return set_error(code, buf);
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(GDN2_ERR_CUDA, "%s: CUDA error %d (%s)", where, (int)e, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+// 8-element vectors
+// ---------------------------------------------------------------------------
+// CPT consecutive elements of one row, moved as one 8-, 16- or 32-byte access.
+template <typename T, int CPT> struct Pack {
+  static constexpr int kBytes = CPT * (int)sizeof(T);
+  static constexpr int kWords = kBytes / 8;  // 8-byte words
+  uint2 u[kWords];
+};
+
+template <typename T, int CPT> __device__ __forceinline__ Pack<T, CPT> ldv(const T* p) {
+  Pack<T, CPT> r;
+  if constexpr (Pack<T, CPT>::kBytes == 8) {
+    r.u[0] = __ldg(reinterpret_cast<const uint2*>(p));
+  } else {
+#pragma unroll
+    for (int i = 0; i < Pack<T, CPT>::kBytes / 16; ++i) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + i);
+      r.u[2 * i] = make_uint2(v.x, v.y);
+      r.u[2 * i + 1] = make_uint2(v.z, v.w);
+    }
+  }
+  return r;
+}
+
+template <typename T, int CPT>
+__device__ __forceinline__ void unpackv(const Pack<T, CPT>& r, float (&f)[CPT]) {
+  const T* e = reinterpret_cast<const T*>(r.u);
+#pragma unroll
+  for (int i = 0; i < CPT; ++i) f[i] = to_f<T>(e[i]);
+}
+
+template <typename T, int CPT> __device__ __forceinline__ void stv(T* p, const float (&f)[CPT]) {
+  Pack<T, CPT> r;
+  T* e = reinterpret_cast<T*>(r.u);
+#pragma unroll
+  for (int i = 0; i < CPT; ++i) e[i] = from_f<T>(f[i]);
+  if constexpr (Pack<T, CPT>::kBytes == 8) {
+    *reinterpret_cast<uint2*>(p) = r.u[0];
+  } else {
+#pragma unroll
+    for (int i = 0; i < Pack<T, CPT>::kBytes / 16; ++i)
+      reinterpret_cast<uint4*>(p)[i] = make_uint4(r.u[2 * i].x, r.u[2 * i].y, r.u[2 * i + 1].x,
+                                                  r.u[2 * i + 1].y);
+  }
+}
+
+template <typename T, int CPT> __device__ __forceinline__ void zerov(Pack<T, CPT>& r) {
+#pragma unroll
+  for (int i = 0; i < Pack<T, CPT>::kWords; ++i) r.u[i] = make_uint2(0, 0);
+}
+
+// Rounding to the token dtype (identity for fp32).
+template <typename T> __device__ __forceinline__ float rnd(float x) { return to_f<T>(from_f<T>(x)); }
+
+// SiLU as the reference evaluates it for every dtype: x / (1 + exp(-x)) in fp32.
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+
+// d silu / dx times dy, in the same fp32 form as the reference's SiLU backward.
+__device__ __forceinline__ float silu_bwd_f(float dy, float x) {
+  const float s = 1.f / (1.f + expf(-x));
+  return dy * s * (1.f + x * (1.f - s));
+}
+
+// ---------------------------------------------------------------------------
+// causal depthwise convolution
+// ---------------------------------------------------------------------------
+constexpr int kConvWarps = 8;   // token strips per CTA
+constexpr int kConvStrip = 64;  // tokens per strip (one warp)
+constexpr int kConvMaxW = 4;
+
+struct ConvArgs {
+  int B, T, D;
+  const void* x;
+  const float* w;     // [D][W]
+  const float* bias;  // [D] or null
+  const void* prefix;
+  int64_t psb, psw, psd;
+  void* y;
+  void* new_state;    // [B][D][W-1] or null
+  const void* dy;
+  void* dx;
+  float* part;        // [nblk][W+1][D]
+  float* dprefix;     // [B][W-1][D] or null
+  float* dweight;     // [D][W]
+  float* dbias;       // [D] or null
+};
+
+template <int W, int CPT>
+__device__ __forceinline__ void load_weights(const ConvArgs& a, int d0, float (&wt)[W][CPT],
+                                             float (&bs)[CPT]) {
+#pragma unroll
+  for (int i = 0; i < CPT; ++i) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) wt[j][i] = __ldg(a.w + (int64_t)(d0 + i) * W + j);
+    bs[i] = a.bias ? __ldg(a.bias + d0 + i) : 0.f;
+  }
+}
+
+// Row r (< 0 reads the prefix, row W-1+r of it) of batch entry b, channels d0..d0+CPT-1.
+template <typename T, int W, int CPT>
+__device__ __forceinline__ void load_row(const ConvArgs& a, const T* xb, int b, int d0, int r,
+                                         float (&f)[CPT]) {
+  if (r >= 0) {
+    unpackv<T, CPT>(ldv<T, CPT>(xb + (int64_t)r * a.D), f);
+  } else if (a.prefix) {
+    const T* p = reinterpret_cast<const T*>(a.prefix) + b * a.psb + (W - 1 + r) * a.psw;
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) f[i] = to_f<T>(p[(int64_t)(d0 + i) * a.psd]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) f[i] = 0.f;
+  }
+}
+
+// Channels per thread: 4 (a warp covers 128 channels, 256 bytes of a bf16
+// row), which keeps the forward near 100 registers (two CTAs per SM with the
+// register window, weights and 8 rows in flight) and the backward at 128.
+constexpr int kFwdCPT = 4;
+constexpr int kBwdCPT = 4;
+
+// y = act(round(bias + sum_j w_j x_{t-W+1+j})): grid (D/(32*CPT), strips of
+// 8*64 tokens, B); one warp per 64-token strip, registers carry the W-1
+// previous rows.
+template <typename T, int W, int ACT>
+__global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
+  constexpr int CPT = kFwdCPT;
+  constexpr int R = 8;  // rows loaded per run
+  constexpr int WP = W > 1 ? W - 1 : 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int d0 = (blockIdx.x * 32 + lane) * CPT;
+  const int b = blockIdx.z;
+  const int tb = (blockIdx.y * kConvWarps + warp) * kConvStrip;
+  if (d0 >= a.D || tb >= a.T) return;
+  const int te = min(tb + kConvStrip, a.T);
+  float wt[W][CPT], bs[CPT];
+  load_weights<W, CPT>(a, d0, wt, bs);
+  const T* xb = reinterpret_cast<const T*>(a.x) + (int64_t)b * a.T * a.D + d0;
+  T* yb = reinterpret_cast<T*>(a.y) + (int64_t)b * a.T * a.D + d0;
+  float win[WP][CPT];
+#pragma unroll
+  for (int i = 0; i < W - 1; ++i) load_row<T, W, CPT>(a, xb, b, d0, tb - (W - 1) + i, win[i]);
+  for (int t0 = tb; t0 < te; t0 += R) {
+    Pack<T, CPT> raw[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (t0 + r < te) raw[r] = ldv<T, CPT>(xb + (int64_t)(t0 + r) * a.D);
+      else zerov<T, CPT>(raw[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (t0 + r >= te) continue;  // (predicated: the loop stays unrolled)
+      float cur[CPT], o[CPT];
+      unpackv<T, CPT>(raw[r], cur);
+#pragma unroll
+      for (int i = 0; i < CPT; ++i) {
+        float acc = bs[i];
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j) acc = fmaf(wt[j][i], win[j][i], acc);
+        acc = fmaf(wt[W - 1][i], cur[i], acc);
+        const float c = rnd<T>(acc);
+        o[i] = ACT ? silu_f(c) : c;
+      }
+      stv<T, CPT>(yb + (int64_t)(t0 + r) * a.D, o);
+#pragma unroll
+      for (int j = 0; j + 1 < W - 1; ++j)
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) win[j][i] = win[j + 1][i];
+      if (W > 1) {
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) win[WP - 1][i] = cur[i];
+      }
+    }
+  }
+  // the strip holding the last row leaves rows T-W+1 .. T-1 in its window
+  if (a.new_state && te == a.T && W > 1) {
+    T* ns = reinterpret_cast<T*>(a.new_state) + ((int64_t)b * a.D + d0) * (W - 1);
+#pragma unroll
+    for (int i = 0; i < CPT; ++i)
+#pragma unroll
+      for (int j = 0; j < W - 1; ++j) ns[i * (W - 1) + j] = from_f<T>(win[j][i]);
+  }
+}
+
+// Backward over the strip's rows s in [tb, te + W - 1): dc_s = act'(c_s) dy_s
+// (rounded to the token dtype, as the reference's activation backward is),
+// dx_t = sum_j w_j dc_{t+W-1-j} emitted at s = t + W - 1, dw_j += dc_s
+// x_{s-W+1+j} and dbias += dc_s for s < te.  Rows t < 0 of the first strip
+// are the prefix rows (dprefix).  Per-CTA sums of dw / dbias go to
+// part[blk][j][d] through shared memory in a fixed order.
+template <typename T, int W, int ACT>
+__global__ void __launch_bounds__(256, 2) k_conv_bwd(ConvArgs a) {
+  constexpr int CPT = kBwdCPT;
+  constexpr int R = 4;
+  constexpr int WP = W > 1 ? W - 1 : 1;
+  __shared__ float red[kConvWarps][32 * CPT];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int d0 = (blockIdx.x * 32 + lane) * CPT;
+  const int b = blockIdx.z;
+  const int tb = (blockIdx.y * kConvWarps + warp) * kConvStrip;
+  const bool active = d0 < a.D && tb < a.T;
+  float dwp[W + 1][CPT];
+#pragma unroll
+  for (int j = 0; j <= W; ++j)
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) dwp[j][i] = 0.f;
+  if (active) {
+    const int te = min(tb + kConvStrip, a.T);
+    float wt[W][CPT], bs[CPT];
+    load_weights<W, CPT>(a, d0, wt, bs);
+    const T* xb = reinterpret_cast<const T*>(a.x) + (int64_t)b * a.T * a.D + d0;
+    const T* dyb = reinterpret_cast<const T*>(a.dy) + (int64_t)b * a.T * a.D + d0;
+    T* dxb = reinterpret_cast<T*>(a.dx) + (int64_t)b * a.T * a.D + d0;
+    float win[WP][CPT], dcw[WP][CPT];  // previous W-1 input rows and dc values
+#pragma unroll
+    for (int i = 0; i < W - 1; ++i) {
+      load_row<T, W, CPT>(a, xb, b, d0, tb - (W - 1) + i, win[i]);
+#pragma unroll
+      for (int e = 0; e < CPT; ++e) dcw[i][e] = 0.f;
+    }
+    const int send = te + W - 1;
+    const bool want_dprefix = a.dprefix && tb == 0;
+    for (int s0 = tb; s0 < send; s0 += R) {
+      Pack<T, CPT> rx[R], rdy[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int s = s0 + r;
+        if (s < a.T && s < send) {
+          rx[r] = ldv<T, CPT>(xb + (int64_t)s * a.D);
+          rdy[r] = ldv<T, CPT>(dyb + (int64_t)s * a.D);
+        } else {
+          zerov<T, CPT>(rx[r]);
+          zerov<T, CPT>(rdy[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int s = s0 + r;
+        if (s >= send) continue;  // (predicated: the loop stays unrolled)
+        float cur[CPT], dc[CPT];
+        unpackv<T, CPT>(rx[r], cur);
+        unpackv<T, CPT>(rdy[r], dc);
+        if (s < a.T) {
+#pragma unroll
+          for (int i = 0; i < CPT; ++i) {
+            if (ACT) {
+              float acc = bs[i];
+#pragma unroll
+              for (int j = 0; j < W - 1; ++j) acc = fmaf(wt[j][i], win[j][i], acc);
+              acc = fmaf(wt[W - 1][i], cur[i], acc);
+              dc[i] = rnd<T>(silu_bwd_f(dc[i], rnd<T>(acc)));
+            }
+          }
+          if (s < te) {
+#pragma unroll
+            for (int i = 0; i < CPT; ++i) {
+#pragma unroll
+              for (int j = 0; j < W - 1; ++j) dwp[j][i] = fmaf(dc[i], win[j][i], dwp[j][i]);
+              dwp[W - 1][i] = fmaf(dc[i], cur[i], dwp[W - 1][i]);
+              dwp[W][i] += dc[i];
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < CPT; ++i) dc[i] = 0.f;
+        }
+        // emit input row t = s - W + 1
+        const int t = s - (W - 1);
+        if (t >= tb || (want_dprefix && t >= -(W - 1))) {
+          float o[CPT];
+#pragma unroll
+          for (int i = 0; i < CPT; ++i) {
+            float acc = wt[0][i] * dc[i];
+#pragma unroll
+            for (int j = 1; j < W; ++j) acc = fmaf(wt[j][i], dcw[W - 1 - j][i], acc);
+            o[i] = acc;
+          }
+          if (t >= tb) {
+            if (t < te) stv<T, CPT>(dxb + (int64_t)t * a.D, o);
+          } else {
+            float* dp = a.dprefix + ((int64_t)b * (W - 1) + (t + W - 1)) * a.D + d0;
+#pragma unroll
+            for (int i = 0; i < CPT; ++i) dp[i] = o[i];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j + 1 < W - 1; ++j)
+#pragma unroll
+          for (int i = 0; i < CPT; ++i) {
+            win[j][i] = win[j + 1][i];
+            dcw[j][i] = dcw[j + 1][i];
+          }
+        if (W > 1) {
+#pragma unroll
+          for (int i = 0; i < CPT; ++i) {
+            win[WP - 1][i] = cur[i];
+            dcw[WP - 1][i] = dc[i];
+          }
+        }
+      }
+    }
+  }
+  // CTA sum over the 8 strips, one (tap, 32*CPT-channel) slice at a time
+  const int blk = blockIdx.z * gridDim.y + blockIdx.y;
+  const int dc0 = blockIdx.x * 32 * CPT;
+#pragma unroll
+  for (int j = 0; j <= W; ++j) {
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) red[warp][lane * CPT + i] = dwp[j][i];
+    __syncthreads();
+    const int c = threadIdx.x;
+    if (c < 32 * CPT && dc0 + c < a.D) {
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < kConvWarps; ++k) sum += red[k][c];
+      a.part[((int64_t)blk * (W + 1) + j) * a.D + dc0 + c] = sum;
+    }
+    __syncthreads();
+  }
+}
+
+// dweight[d][j] (j < W) and dbias[d] (j = W): sum of part[k][j][d] over k in order.
+__global__ void k_conv_reduce(const float* part, int nblk, int W, int D, float* dw, float* dbias) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (W + 1) * D) return;
+  const int j = idx / D, d = idx - j * D;
+  float sum = 0.f;
+  for (int k = 0; k < nblk; ++k) sum += part[(int64_t)k * (W + 1) * D + idx];
+  if (j < W) dw[(int64_t)d * W + j] = sum;
+  else if (dbias) dbias[d] = sum;
+}
+
+int conv_nblk(const gdn2_conv_problem* p) {
+  const int per = kConvWarps * kConvStrip;
+  return p->B * ((p->T + per - 1) / per);
+}
+
+template <typename T, int W>
+cudaError_t launch_conv(const gdn2_conv_problem* p, const ConvArgs& a, bool bwd, cudaStream_t st) {
+  const int per = kConvWarps * kConvStrip;
+  const int cpt = bwd ? kBwdCPT : kFwdCPT;
+  dim3 grid((p->D + 32 * cpt - 1) / (32 * cpt), (p->T + per - 1) / per, p->B);
+  if (!bwd) {
+    if (p->activation) k_conv_fwd<T, W, 1><<<grid, 256, 0, st>>>(a);
+    else k_conv_fwd<T, W, 0><<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+  }
+  if (p->activation) k_conv_bwd<T, W, 1><<<grid, 256, 0, st>>>(a);
+  else k_conv_bwd<T, W, 0><<<grid, 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int n = (W + 1) * p->D;
+  k_conv_reduce<<<(n + 255) / 256, 256, 0, st>>>(a.part, conv_nblk(p), W, p->D, a.dweight,
+                                                  a.dbias);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// SiLU-gated RMSNorm
+// ---------------------------------------------------------------------------
+constexpr int kNormMaxBlocks = 1024;
+
+struct NormArgs {
+  int64_t rows;
+  int N;
+  float eps;
+  const void* x;
+  const void* z;
+  const void* w;
+  void* y;
+  const void* dy;
+  void* dx;
+  void* dz;
+  float* part;     // [nblk][N]
+  float* dweight;  // [N]
+};
+
+// TPR threads per row, 8 columns each (col = 8 * (v * TPR + sub)); the row's
+// sums are reduced over the TPR lanes with shuffles.
+template <int TPR> __device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = TPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename TW> __device__ __forceinline__ void load_w8(const TW* w, int c, int N,
+                                                             float (&f)[8]) {
+  if (c < N) {
+    unpackv<TW, 8>(ldv<TW, 8>(w + c), f);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = 0.f;
+  }
+}
+
+// Forward, in the reference's order and input-dtype rounding:
+//   var = round(mean(round(x^2))), r = round(rsqrt(round(var + eps))),
+//   n = round(x r), n = round(n w) (or n w in fp32 for an fp32 weight),
+//   y = round_out(n round(silu(z))).
+// F32 (the reference under autocast): the same steps without rounding,
+// except silu(z), which runs in the input dtype.
+template <typename T, typename TW, typename TO, int TPR, bool F32>
+__global__ void __launch_bounds__(256) k_gnorm_fwd(NormArgs a) {
+  constexpr int RPC = 256 / TPR;
+  const int sub = threadIdx.x % TPR, slot = threadIdx.x / TPR;
+  const int c = 8 * sub;
+  const bool live = c < a.N;
+  float w[8];
+  load_w8<TW>(reinterpret_cast<const TW*>(a.w), c, a.N, w);
+  const float inv_n = 1.f / (float)a.N;
+  // the trip count is uniform across the CTA: the row's lanes share a warp
+  // with other rows' lanes, and every lane joins the shuffles of each trip
+  for (int64_t base = (int64_t)blockIdx.x * RPC; base < a.rows; base += (int64_t)gridDim.x * RPC) {
+    const int64_t row = base + slot;
+    const bool on = live && row < a.rows;
+    float x[8], z[8];
+    if (on) {
+      unpackv<T, 8>(ldv<T, 8>(reinterpret_cast<const T*>(a.x) + row * a.N + c), x);
+      unpackv<T, 8>(ldv<T, 8>(reinterpret_cast<const T*>(a.z) + row * a.N + c), z);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = z[i] = 0.f;
+    }
+    using TR = typename std::conditional<F32, float, T>::type;  // intermediate rounding
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += rnd<TR>(x[i] * x[i]);
+    ss = group_sum<TPR>(ss);
+    const float var = rnd<TR>(ss * inv_n);
+    const float r = rnd<TR>(rsqrtf(rnd<TR>(var + a.eps)));
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float n = rnd<TR>(x[i] * r);
+      n = rnd<typename std::conditional<F32, float, TW>::type>(n * w[i]);
+      y[i] = n * rnd<T>(silu_f(z[i]));
+    }
+    if (on) stv<TO, 8>(reinterpret_cast<TO*>(a.y) + row * a.N + c, y);
+  }
+}
+
+// Backward in fp32: r = rsqrt(mean(x^2) + eps), n = x r, s = silu(z),
+//   dn = dy w s, dx = r (dn - n mean(dn n)), dz = dy n w silu'(z),
+//   dweight = sum_rows dy n s (per-CTA partials, reduced in a fixed order).
+template <typename T, typename TW, typename TO, int TPR>
+__global__ void __launch_bounds__(256) k_gnorm_bwd(NormArgs a) {
+  constexpr int RPC = 256 / TPR;
+  __shared__ float red[256 * 8];
+  const int sub = threadIdx.x % TPR, slot = threadIdx.x / TPR;
+  const int c = 8 * sub;
+  const bool live = c < a.N;
+  float w[8], dwp[8];
+  load_w8<TW>(reinterpret_cast<const TW*>(a.w), c, a.N, w);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) dwp[i] = 0.f;
+  const float inv_n = 1.f / (float)a.N;
+  // CTA-uniform trip count (see the forward)
+  for (int64_t base = (int64_t)blockIdx.x * RPC; base < a.rows; base += (int64_t)gridDim.x * RPC) {
+    const int64_t row = base + slot;
+    const bool on = live && row < a.rows;
+    float x[8], z[8], dy[8];
+    if (on) {
+      unpackv<T, 8>(ldv<T, 8>(reinterpret_cast<const T*>(a.x) + row * a.N + c), x);
+      unpackv<T, 8>(ldv<T, 8>(reinterpret_cast<const T*>(a.z) + row * a.N + c), z);
+      unpackv<TO, 8>(ldv<TO, 8>(reinterpret_cast<const TO*>(a.dy) + row * a.N + c), dy);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = z[i] = dy[i] = 0.f;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+    ss = group_sum<TPR>(ss);
+    const float r = rsqrtf(ss * inv_n + a.eps);
+    float n[8], dn[8], dz[8], dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float sg = 1.f / (1.f + expf(-z[i]));
+      const float s = z[i] * sg;
+      n[i] = x[i] * r;
+      dn[i] = dy[i] * w[i] * s;
+      dot = fmaf(dn[i], n[i], dot);
+      dz[i] = dy[i] * n[i] * w[i] * sg * (1.f + z[i] * (1.f - sg));
+      dwp[i] = fmaf(dy[i] * n[i], s, dwp[i]);
+    }
+    dot = group_sum<TPR>(dot) * inv_n;
+    float dx[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dx[i] = r * (dn[i] - n[i] * dot);
+    if (on) {
+      stv<T, 8>(reinterpret_cast<T*>(a.dx) + row * a.N + c, dx);
+      stv<T, 8>(reinterpret_cast<T*>(a.dz) + row * a.N + c, dz);
+    }
+  }
+  // CTA sum over the RPC row slots, column by column in a fixed order
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[slot * (TPR * 8) + c + i] = dwp[i];
+  __syncthreads();
+  for (int col = threadIdx.x; col < TPR * 8; col += 256) {
+    float sum = 0.f;
+    for (int k = 0; k < RPC; ++k) sum += red[k * (TPR * 8) + col];
+    if (col < a.N) a.part[(int64_t)blockIdx.x * a.N + col] = sum;
+  }
+}
+
+__global__ void k_norm_reduce(const float* part, int nblk, int N, float* dw) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= N) return;
+  float sum = 0.f;
+  for (int k = 0; k < nblk; ++k) sum += part[(int64_t)k * N + col];
+  dw[col] = sum;
+}
+
+int norm_tpr(int N) {
+  if (N % 8 != 0 || N <= 0 || N > 256) return 0;
+  return N <= 64 ? 8 : (N <= 128 ? 16 : 32);
+}
+
+int norm_nblk(const gdn2_norm_problem* p) {
+  const int rpc = 256 / norm_tpr(p->N);
+  const int64_t need = (p->rows + rpc - 1) / rpc;
+  return (int)(need < kNormMaxBlocks ? need : kNormMaxBlocks);
+}
+
+template <typename T, typename TW, typename TO, int TPR>
+cudaError_t launch_gnorm2(const gdn2_norm_problem* p, const NormArgs& a, bool bwd,
+                          cudaStream_t st) {
+  const int nblk = norm_nblk(p);
+  if (!bwd) {
+    if (p->fp32_math) k_gnorm_fwd<T, TW, TO, TPR, true><<<nblk, 256, 0, st>>>(a);
+    else k_gnorm_fwd<T, TW, TO, TPR, false><<<nblk, 256, 0, st>>>(a);
+    return cudaGetLastError();
+  }
+  k_gnorm_bwd<T, TW, TO, TPR><<<nblk, 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  k_norm_reduce<<<(p->N + 127) / 128, 128, 0, st>>>(a.part, nblk, p->N, a.dweight);
+  return cudaGetLastError();
+}
+
+template <typename T, typename TW, typename TO>
+cudaError_t launch_gnorm(const gdn2_norm_problem* p, const NormArgs& a, bool bwd, cudaStream_t st) {
+  switch (norm_tpr(p->N)) {
+    case 8: return launch_gnorm2<T, TW, TO, 8>(p, a, bwd, st);
+    case 16: return launch_gnorm2<T, TW, TO, 16>(p, a, bwd, st);
+    default: return launch_gnorm2<T, TW, TO, 32>(p, a, bwd, st);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// entry-point helpers
+// ---------------------------------------------------------------------------
+bool dtype_valid(int dt) {
+  return dt == GDN2_DTYPE_F32 || dt == GDN2_DTYPE_BF16 || dt == GDN2_DTYPE_F16;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int check_conv(const gdn2_conv_problem* p, const char* fn) {
+  if (!p) return fail(GDN2_ERR_INVALID, "%s: null problem", fn);
+  if (p->B <= 0 || p->T <= 0 || p->D <= 0 || p->W <= 0)
+    return fail(GDN2_ERR_INVALID, "%s: B, T, D, W must be positive (got %d, %d, %d, %d)", fn,
+                p->B, p->T, p->D, p->W);
+  if (!dtype_valid(p->dtype)) return fail(GDN2_ERR_INVALID, "%s: bad dtype %d", fn, p->dtype);
+  if (p->activation != 0 && p->activation != 1)
+    return fail(GDN2_ERR_INVALID, "%s: activation must be 0 or 1", fn);
+  if (p->W > kConvMaxW || p->D % 8 != 0)
+    return fail(GDN2_ERR_UNSUPPORTED, "%s: needs W <= %d and D %% 8 == 0 (W=%d, D=%d)", fn,
+                kConvMaxW, p->W, p->D);
+  return GDN2_OK;
+}
+
+template <typename T>
+cudaError_t conv_dispatch_w(const gdn2_conv_problem* p, const ConvArgs& a, bool bwd,
+                            cudaStream_t st) {
+  switch (p->W) {
+    case 1: return launch_conv<T, 1>(p, a, bwd, st);
+    case 2: return launch_conv<T, 2>(p, a, bwd, st);
+    case 3: return launch_conv<T, 3>(p, a, bwd, st);
+    default: return launch_conv<T, 4>(p, a, bwd, st);
+  }
+}
+
+cudaError_t conv_dispatch(const gdn2_conv_problem* p, const ConvArgs& a, bool bwd,
+                          cudaStream_t st) {
+  switch (p->dtype) {
+    case GDN2_DTYPE_F32: return conv_dispatch_w<float>(p, a, bwd, st);
+    case GDN2_DTYPE_BF16: return conv_dispatch_w<__nv_bfloat16>(p, a, bwd, st);
+    default: return conv_dispatch_w<__half>(p, a, bwd, st);
+  }
+}
+
+int check_norm(const gdn2_norm_problem* p, const char* fn) {
+  if (!p) return fail(GDN2_ERR_INVALID, "%s: null problem", fn);
+  if (p->rows < 0 || p->N <= 0)
+    return fail(GDN2_ERR_INVALID, "%s: rows >= 0 and N > 0 required", fn);
+  if (!dtype_valid(p->dtype) || !dtype_valid(p->weight_dtype))
+    return fail(GDN2_ERR_INVALID, "%s: bad dtype", fn);
+  if (p->weight_dtype != p->dtype && p->weight_dtype != GDN2_DTYPE_F32)
+    return fail(GDN2_ERR_UNSUPPORTED, "%s: weight dtype must be the input dtype or fp32", fn);
+  if (p->fp32_math != 0 && p->fp32_math != 1)
+    return fail(GDN2_ERR_INVALID, "%s: fp32_math must be 0 or 1", fn);
+  if (p->fp32_math && p->weight_dtype != GDN2_DTYPE_F32)
+    return fail(GDN2_ERR_INVALID, "%s: fp32_math needs an fp32 weight", fn);
+  if (!norm_tpr(p->N))
+    return fail(GDN2_ERR_UNSUPPORTED, "%s: N %% 8 == 0 and N <= 256 required (N=%d)", fn, p->N);
+  return GDN2_OK;
+}
+
+cudaError_t norm_dispatch(const gdn2_norm_problem* p, const NormArgs& a, bool bwd,
+                          cudaStream_t st) {
+  const bool wf = p->weight_dtype == GDN2_DTYPE_F32;
+  switch (p->dtype) {
+    case GDN2_DTYPE_F32: return launch_gnorm<float, float, float>(p, a, bwd, st);
+    case GDN2_DTYPE_BF16:
+      return wf ? launch_gnorm<__nv_bfloat16, float, float>(p, a, bwd, st)
+                : launch_gnorm<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(p, a, bwd, st);
+    default:
+      return wf ? launch_gnorm<__half, float, float>(p, a, bwd, st)
+                : launch_gnorm<__half, __half, __half>(p, a, bwd, st);
+  }
+}
+
+}  // namespace
+}  // namespace gdn2
+
+using namespace gdn2;
+
+extern "C" {
+
+int gdn2_conv_fwd(const gdn2_conv_problem* p, const void* x, const float* weight,
+                  const float* bias, const void* prefix, void* y, void* new_state,
+                  void* stream) {
+  int rc = check_conv(p, "gdn2_conv_fwd");
+  if (rc) return rc;
+  if (!x || !weight || !y) return fail(GDN2_ERR_INVALID, "gdn2_conv_fwd: null pointer");
+  if (!al16(x) || !al16(y))
+    return fail(GDN2_ERR_INVALID, "gdn2_conv_fwd: x and y must start on a 16-byte boundary");
+  ConvArgs a{};
+  a.B = p->B; a.T = p->T; a.D = p->D;
+  a.x = x; a.w = weight; a.bias = bias; a.prefix = prefix;
+  a.psb = p->prefix_sb; a.psw = p->prefix_sw; a.psd = p->prefix_sd;
+  a.y = y; a.new_state = new_state;
+  cudaError_t e = conv_dispatch(p, a, false, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_conv_fwd");
+}
+
+size_t gdn2_conv_bwd_workspace_bytes(const gdn2_conv_problem* p) {
+  if (check_conv(p, "gdn2_conv_bwd_workspace_bytes") != GDN2_OK) return 0;
+  return (size_t)conv_nblk(p) * (p->W + 1) * p->D * sizeof(float);
+}
+
+int gdn2_conv_bwd(const gdn2_conv_problem* p, const void* x, const float* weight,
+                  const float* bias, const void* prefix, const void* dy, void* dx,
+                  float* dweight, float* dbias, float* dprefix, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  int rc = check_conv(p, "gdn2_conv_bwd");
+  if (rc) return rc;
+  if (!x || !weight || !dy || !dx || !dweight || !workspace)
+    return fail(GDN2_ERR_INVALID, "gdn2_conv_bwd: null pointer");
+  if (!al16(x) || !al16(dy) || !al16(dx))
+    return fail(GDN2_ERR_INVALID, "gdn2_conv_bwd: x, dy, dx must start on a 16-byte boundary");
+  const size_t need = gdn2_conv_bwd_workspace_bytes(p);
+  if (workspace_bytes < need)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_conv_bwd: workspace %zu < %zu bytes", workspace_bytes,
+                need);
+  ConvArgs a{};
+  a.B = p->B; a.T = p->T; a.D = p->D;
+  a.x = x; a.w = weight; a.bias = bias; a.prefix = prefix;
+  a.psb = p->prefix_sb; a.psw = p->prefix_sw; a.psd = p->prefix_sd;
+  a.dy = dy; a.dx = dx; a.part = static_cast<float*>(workspace);
+  a.dprefix = dprefix; a.dweight = dweight; a.dbias = dbias;
+  cudaError_t e = conv_dispatch(p, a, true, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_conv_bwd");
+}
+
+int gdn2_gated_norm_fwd(const gdn2_norm_problem* p, const void* x, const void* z,
+                        const void* weight, void* y, void* stream) {
+  int rc = check_norm(p, "gdn2_gated_norm_fwd");
+  if (rc) return rc;
+  if (p->rows == 0) return GDN2_OK;
+  if (!x || !z || !weight || !y) return fail(GDN2_ERR_INVALID, "gdn2_gated_norm_fwd: null pointer");
+  if (!al16(x) || !al16(z) || !al16(weight) || !al16(y))
+    return fail(GDN2_ERR_INVALID, "gdn2_gated_norm_fwd: tensors must start on a 16-byte boundary");
+  NormArgs a{};
+  a.rows = p->rows; a.N = p->N; a.eps = p->eps;
+  a.x = x; a.z = z; a.w = weight; a.y = y;
+  cudaError_t e = norm_dispatch(p, a, false, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_gated_norm_fwd");
+}
+
+size_t gdn2_gated_norm_bwd_workspace_bytes(const gdn2_norm_problem* p) {
+  if (check_norm(p, "gdn2_gated_norm_bwd_workspace_bytes") != GDN2_OK) return 0;
+  return (size_t)(norm_nblk(p) > 0 ? norm_nblk(p) : 1) * p->N * sizeof(float);
+}
+
+int gdn2_gated_norm_bwd(const gdn2_norm_problem* p, const void* x, const void* z,
+                        const void* weight, const void* dy, void* dx, void* dz,
+                        float* dweight, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  int rc = check_norm(p, "gdn2_gated_norm_bwd");
+  if (rc) return rc;
+  if (!dweight) return fail(GDN2_ERR_INVALID, "gdn2_gated_norm_bwd: null dweight");
+  if (p->rows == 0) {
+    cudaError_t e = cudaMemsetAsync(dweight, 0, (size_t)p->N * sizeof(float), (cudaStream_t)stream);
+    return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_gated_norm_bwd");
+  }
+  if (!x || !z || !weight || !dy || !dx || !dz || !workspace)
+    return fail(GDN2_ERR_INVALID, "gdn2_gated_norm_bwd: null pointer");
+  if (!al16(x) || !al16(z) || !al16(weight) || !al16(dy) || !al16(dx) || !al16(dz))
+    return fail(GDN2_ERR_INVALID, "gdn2_gated_norm_bwd: tensors must start on a 16-byte boundary");
+  const size_t need = gdn2_gated_norm_bwd_workspace_bytes(p);
+  if (workspace_bytes < need)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_gated_norm_bwd: workspace %zu < %zu bytes",
+                workspace_bytes, need);
+  NormArgs a{};
+  a.rows = p->rows; a.N = p->N; a.eps = p->eps;
+  a.x = x; a.z = z; a.w = weight; a.dy = dy; a.dx = dx; a.dz = dz;
+  a.part = static_cast<float*>(workspace); a.dweight = dweight;
+  cudaError_t e = norm_dispatch(p, a, true, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_gated_norm_bwd");
+}
+
+}  // extern "C"

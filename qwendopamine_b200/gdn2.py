@@ -40,6 +40,7 @@ try:
 except ImportError:  # pragma: no cover
     LinearAttentionCacheLayerMixin = type(None)  # type: ignore[misc, assignment]
 
+from .gdn2_ops.block_ops import gated_rms_norm, short_conv
 from .gdn2_ops.chunk_gdn2 import chunk_gdn2
 from .gdn2_ops.fused_recurrent_gdn2 import fused_recurrent_gdn2
 
@@ -71,8 +72,10 @@ def resolve_gdn2_backend(requested: str, *, training: bool, seq_len: int) -> str
 
 class ShortConvolution(nn.Module):
     """Causal depthwise 1-D convolution with optional SiLU (reference
-    gdn2.py:372-430).  With a cache and a single new token, the cached
-    ``kernel_size - 1`` inputs are prepended instead of zero padding."""
+    gdn2.py:372-430), computed by ``gdn2_conv_fwd`` / ``gdn2_conv_bwd``.
+    With a cache and a single new token, the cached ``kernel_size - 1``
+    inputs are prepended instead of zero padding; a longer input ignores the
+    cache, as the reference does."""
 
     def __init__(self, hidden_size: int, kernel_size: int = 4, bias: bool = False,
                  activation: str | None = "silu") -> None:
@@ -86,21 +89,24 @@ class ShortConvolution(nn.Module):
     def forward(self, x: torch.Tensor, cache: torch.Tensor | None = None,
                 output_final_state: bool = False, cu_seqlens: torch.Tensor | None = None
                 ) -> tuple[torch.Tensor, torch.Tensor | None]:
+        if not x.is_cuda:
+            raise RuntimeError("ShortConvolution (B200 build) runs on CUDA devices only")
         batch, t, d = x.shape
-        xc = x.transpose(1, 2)
         keep = self.kernel_size - 1
+        weight, bias = self.conv1d.weight, self.conv1d.bias
+        if torch.is_autocast_enabled("cuda"):
+            x = x.to(torch.get_autocast_dtype("cuda"))  # F.conv1d's autocast cast
+        elif weight.dtype != x.dtype:
+            raise RuntimeError(f"Input type ({x.dtype}) and weight type ({weight.dtype}) "
+                               "should be the same")
         if cache is None and output_final_state and t == 1:
             cache = x.new_zeros(batch, d, keep)
         if cache is not None and t == 1:
-            window = torch.cat([cache, xc], dim=-1)
-            new_cache = window[:, :, 1:] if output_final_state else None
-            y = F.conv1d(window, self.conv1d.weight, self.conv1d.bias, groups=d)
-        else:
-            new_cache = xc[:, :, -keep:] if output_final_state else None
-            y = F.conv1d(xc, self.conv1d.weight, self.conv1d.bias, padding=keep, groups=d)[:, :, :t]
-        if self.activation == "silu":
-            y = F.silu(y)
-        return y.transpose(1, 2), new_cache
+            return short_conv(x, weight, bias, self.activation, prefix=cache.transpose(1, 2),
+                              output_final_state=output_final_state)
+        new_cache = x.transpose(1, 2)[:, :, -keep:] if output_final_state else None
+        y, _ = short_conv(x, weight, bias, self.activation)
+        return y, new_cache
 
 
 class RMSNormGated(nn.Module):
@@ -114,8 +120,9 @@ class RMSNormGated(nn.Module):
         self.weight = nn.Parameter(torch.ones(hidden_size))
 
     def forward(self, x: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
-        rms = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps)
-        return x * rms * self.weight * F.silu(z)
+        # one kernel (gdn2_gated_norm_fwd / _bwd); under CUDA autocast the
+        # reference's pow / rsqrt run in fp32 and so does the kernel
+        return gated_rms_norm(x, z, self.weight, self.eps)
 
 
 def _unpad_info(mask: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, int]:
@@ -369,9 +376,17 @@ class GatedDeltaNet2(nn.Module):
         else:
             q, k, v = F.silu(self.q_proj(x)), F.silu(self.k_proj(x)), F.silu(self.v_proj(x))
 
-        decay = self.A_log.float().exp().repeat_interleave(self.head_k_dim)
-        g = -decay * F.softplus(self.f_proj(x).float() + self.dt_bias)
-        g = g.float() if self.fp32_decay else g.to(x.dtype)
+        # With fp32 decays the kernels apply the gate themselves
+        # (use_gate_in_kernel: -exp(A_log) * softplus(f + dt_bias) on the raw
+        # projection, the reference's gdn2.py:840-845 formula); otherwise g is
+        # formed here and rounded to the token dtype as the reference does.
+        gate_in_kernel = self.fp32_decay
+        if gate_in_kernel:
+            g = self.f_proj(x).float()
+        else:
+            decay = self.A_log.float().exp().repeat_interleave(self.head_k_dim)
+            g = (-decay * F.softplus(self.f_proj(x).float() + self.dt_bias)).to(x.dtype)
+        A_log, dt_bias = self.A_log, self.dt_bias
         b = self.b_proj(x).sigmoid()
         w = self.w_proj(x).sigmoid()
 
@@ -381,6 +396,8 @@ class GatedDeltaNet2(nn.Module):
         if self.num_v_heads > self.num_heads:
             rep = self.num_v_heads // self.num_heads
             q, k, g, b = (t.repeat_interleave(rep, dim=-2) for t in (q, k, g, b))
+            A_log = A_log.repeat_interleave(rep)
+            dt_bias = dt_bias.view(self.num_heads, dk).repeat_interleave(rep, dim=0).reshape(-1)
         if self.allow_neg_eigval:
             b = b * 2.0
 
@@ -388,9 +405,10 @@ class GatedDeltaNet2(nn.Module):
             recurrent_state = recurrent_state.float()
         op = chunk_gdn2 if mode == "chunk" else fused_recurrent_gdn2
         o, recurrent_state = op(
-            q=q, k=k, v=v, g=g, b=b, w=w, A_log=self.A_log, dt_bias=self.dt_bias,
+            q=q, k=k, v=v, g=g, b=b, w=w, A_log=A_log, dt_bias=dt_bias,
             initial_state=recurrent_state, output_final_state=want_cache,
-            use_qk_l2norm_in_kernel=True, use_gate_in_kernel=False, cu_seqlens=cu_seqlens)
+            use_qk_l2norm_in_kernel=True, use_gate_in_kernel=gate_in_kernel,
+            cu_seqlens=cu_seqlens)
 
         if use_cache or past_key_values is not None:
             self._update_cache(past_key_values, recurrent_state,

@@ -154,6 +154,75 @@ def decode_case(rec):
     np.savez_compressed(os.path.join(HERE, "decode.npz"), **out)
 
 
+def block_ops_case():
+    """The reference's ShortConvolution and RMSNormGated (gdn2.py:372-452):
+    fp32 with autograd gradients, a one-token decode step through the cache,
+    and bf16 forwards (the reference evaluates both in the input dtype)."""
+    from qwendopamine.models.gdn2.gdn2 import RMSNormGated, ShortConvolution
+
+    out = {}
+    torch.manual_seed(11)
+    B, T, D = 2, 37, 48
+    for tag, W, bias, act in (("a", 4, True, "silu"), ("b", 3, False, None)):
+        m = ShortConvolution(D, kernel_size=W, bias=bias, activation=act)
+        with torch.no_grad():
+            m.conv1d.weight.normal_(0.0, 0.5)
+            if bias:
+                m.conv1d.bias.normal_(0.0, 0.5)
+        x = torch.randn(B, T, D, requires_grad=True)
+        y, cache = m(x, output_final_state=True)
+        dy = torch.randn_like(y)
+        params = [x, m.conv1d.weight] + ([m.conv1d.bias] if bias else [])
+        gr = torch.autograd.grad((y * dy).sum(), params)
+        out[f"conv_{tag}_x"] = _np(x)
+        out[f"conv_{tag}_w"] = _np(m.conv1d.weight)
+        if bias:
+            out[f"conv_{tag}_bias"] = _np(m.conv1d.bias)
+            out[f"conv_{tag}_dbias"] = _np(gr[2])
+        out[f"conv_{tag}_y"] = _np(y)
+        out[f"conv_{tag}_cache"] = _np(cache)
+        out[f"conv_{tag}_dy"] = _np(dy)
+        out[f"conv_{tag}_dx"] = _np(gr[0])
+        out[f"conv_{tag}_dw"] = _np(gr[1])
+        if tag == "a":
+            # one decode step with a cache: the cache is prepended
+            c0 = torch.randn(B, D, W - 1)
+            xt = torch.randn(B, 1, D)
+            with torch.no_grad():
+                yt, c1 = m(xt, cache=c0, output_final_state=True)
+            out["conv_dec_cache"], out["conv_dec_x"] = _np(c0), _np(xt)
+            out["conv_dec_y"], out["conv_dec_new_cache"] = _np(yt), _np(c1)
+            # bf16 forward
+            mb = ShortConvolution(D, kernel_size=W, bias=bias, activation=act).bfloat16()
+            with torch.no_grad():
+                mb.conv1d.weight.copy_(m.conv1d.weight)
+                mb.conv1d.bias.copy_(m.conv1d.bias)
+                yb, _ = mb(x.detach().bfloat16())
+            out["conv_bf16_w"] = _np(mb.conv1d.weight)
+            out["conv_bf16_bias"] = _np(mb.conv1d.bias)
+            out["conv_bf16_y"] = _np(yb)
+
+    N = 32
+    norm = RMSNormGated(N, eps=1e-5)
+    with torch.no_grad():
+        norm.weight.normal_(1.0, 0.3)
+    x = torch.randn(2, 9, 3, N, requires_grad=True)
+    z = torch.randn(2, 9, 3, N, requires_grad=True)
+    y = norm(x, z)
+    dy = torch.randn_like(y)
+    gx, gz, gw = torch.autograd.grad((y * dy).sum(), (x, z, norm.weight))
+    out.update(norm_x=_np(x), norm_z=_np(z), norm_w=_np(norm.weight), norm_y=_np(y),
+               norm_dy=_np(dy), norm_dx=_np(gx), norm_dz=_np(gz), norm_dw=_np(gw))
+    with torch.no_grad():
+        xb, zb = x.detach().bfloat16(), z.detach().bfloat16()
+        out["norm_bf16_y"] = _np(norm.bfloat16()(xb, zb))           # bf16 weight
+        out["norm_bf16_w"] = _np(norm.weight)
+        norm32 = RMSNormGated(N, eps=1e-5)
+        norm32.weight.copy_(torch.from_numpy(out["norm_w"]))
+        out["norm_bf16w32_y"] = _np(norm32(xb, zb))                # fp32 weight: fp32 result
+    np.savez_compressed(os.path.join(HERE, "block_ops.npz"), **out)
+
+
 def main():
     rec, chk = _ref()
     torch.set_num_threads(8)
@@ -161,6 +230,7 @@ def main():
     config0_case(rec, chk)
     strong_decay_case(rec, chk)
     decode_case(rec)
+    block_ops_case()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

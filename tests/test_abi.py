@@ -154,3 +154,32 @@ def test_gate_in_kernel_arguments_are_checked(lib):
     f32 = _problem(dtype=0)
     f32.gate, f32.A_log = 2, 0x1000
     assert lib.gdn2_chunk_fwd_intra(f32, *([None] * 6), None, 0, None) == N.ERR_UNSUPPORTED
+
+
+def test_conv_and_norm_arguments_are_checked(lib):
+    """Block prologue / epilogue entry points: shapes, dtypes and workspace
+    sizes are validated before any CUDA call."""
+    conv = N.ConvProblem(2, 100, 64, 4, 1, 1)
+    # 512-token blocks per batch entry; (W + 1) fp32 partial sums per channel
+    assert lib.gdn2_conv_bwd_workspace_bytes(conv) == 2 * 1 * 5 * 64 * 4
+    for bad, code in ((N.ConvProblem(2, 100, 64, 5, 1, 1), N.ERR_UNSUPPORTED),
+                      (N.ConvProblem(2, 100, 60, 4, 1, 1), N.ERR_UNSUPPORTED),
+                      (N.ConvProblem(2, 0, 64, 4, 1, 1), N.ERR_INVALID),
+                      (N.ConvProblem(2, 100, 64, 4, 7, 1), N.ERR_INVALID),
+                      (N.ConvProblem(2, 100, 64, 4, 1, 2), N.ERR_INVALID)):
+        assert lib.gdn2_conv_fwd(bad, *([None] * 6), None) == code
+    fake, odd = ctypes.c_void_p(0x1000), ctypes.c_void_p(0x1008)
+    assert lib.gdn2_conv_fwd(conv, odd, fake, None, None, fake, None, None) == N.ERR_INVALID
+    assert b"16-byte" in lib.gdn2_last_error()
+    rc = lib.gdn2_conv_bwd(conv, fake, fake, None, None, fake, fake, fake, None, None, fake, 8,
+                           None)
+    assert rc == N.ERR_WORKSPACE
+    norm = N.NormProblem(1000, 128, 1, 1, 1e-5, 0)
+    assert lib.gdn2_gated_norm_bwd_workspace_bytes(norm) == 63 * 128 * 4  # ceil(1000 / 16) blocks
+    for bad, code in ((N.NormProblem(10, 300, 1, 1, 1e-5, 0), N.ERR_UNSUPPORTED),
+                      (N.NormProblem(10, 12, 1, 1, 1e-5, 0), N.ERR_UNSUPPORTED),
+                      (N.NormProblem(10, 64, 1, 2, 1e-5, 0), N.ERR_UNSUPPORTED),
+                      (N.NormProblem(10, 64, 1, 1, 1e-5, 1), N.ERR_INVALID),
+                      (N.NormProblem(10, 64, 1, 0, 1e-5, 3), N.ERR_INVALID)):
+        assert lib.gdn2_gated_norm_fwd(bad, *([None] * 4), None) == code
+    assert lib.gdn2_gated_norm_fwd(N.NormProblem(0, 64, 1, 1, 1e-5, 0), *([None] * 4), None) == 0

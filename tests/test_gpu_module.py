@@ -21,6 +21,19 @@ def _layer(dev, dtype=torch.float32, **kw):
     return GatedDeltaNet2(**kw).to(device=dev, dtype=dtype)
 
 
+def _log_decay(kw):
+    """The log-decay the core applies: the module hands the kernels the raw
+    gate projection with use_gate_in_kernel (fp32 decays), so form
+    -exp(A_log) * softplus(g + dt_bias) here (float64), and its derivative."""
+    g = kw["g"].detach().double()
+    if not kw.get("use_gate_in_kernel"):
+        return g.cpu().numpy(), None
+    H, K = g.shape[-2:]
+    x = g + kw["dt_bias"].detach().double().view(H, K)
+    a = kw["A_log"].detach().double().exp().view(H, 1)
+    return (-a * torch.nn.functional.softplus(x)).cpu().numpy(), (-a * torch.sigmoid(x)).cpu().numpy()
+
+
 def test_module_core_matches_oracle_on_its_own_inputs(cuda_device, monkeypatch):
     import qwendopamine_b200.gdn2 as M
 
@@ -39,6 +52,7 @@ def test_module_core_matches_oracle_on_its_own_inputs(cuda_device, monkeypatch):
     out, attn, _ = layer(x)
     assert out.shape == (2, 100, 256) and attn is None
     args = [seen[n].detach().double().cpu().numpy() for n in ("q", "k", "v", "g", "b", "w")]
+    args[3] = _log_decay(seen)[0]
     ro, _ = O.recurrent_fwd(*args, norm_mode="fla")
     assert rel(seen["o"], ro) < 1e-4
 
@@ -65,6 +79,7 @@ def test_module_gradients_match_oracle_core(cuda_device, monkeypatch):
         for n in ("q", "k", "v", "g", "b", "w"):
             kw[n].retain_grad()
             grabbed[n] = kw[n]
+        grabbed["kw"] = kw
         o, ht = real(**kw)
         o.retain_grad()
         grabbed["o"] = o
@@ -76,7 +91,10 @@ def test_module_gradients_match_oracle_core(cuda_device, monkeypatch):
     out, _, _ = layer(x)
     (out * torch.randn_like(out)).sum().backward()
     args = [grabbed[n].detach().double().cpu().numpy() for n in ("q", "k", "v", "g", "b", "w")]
-    ref = O.recurrent_bwd(*args, grabbed["o"].grad.double().cpu().numpy(), norm_mode="fla")
+    args[3], dgate = _log_decay(grabbed["kw"])
+    ref = list(O.recurrent_bwd(*args, grabbed["o"].grad.double().cpu().numpy(), norm_mode="fla"))
+    if dgate is not None:  # chain rule through the gate to the raw projection
+        ref[3] = ref[3] * dgate
     for n, r in zip(("q", "k", "v", "g", "b", "w"), ref):
         assert rel(grabbed[n].grad, r) < 1e-4, n
 
