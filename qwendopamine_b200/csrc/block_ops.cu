@@ -42,23 +42,31 @@ int cuda_fail(cudaError_t e, const char* where) {
 // ---------------------------------------------------------------------------
 // 8-element vectors
 // ---------------------------------------------------------------------------
-// CPT consecutive elements of one row, moved as one 8-, 16- or 32-byte access.
+// CPT consecutive elements of one row, moved as one 4-, 8-, 16- or 32-byte
+// access (two 16-byte accesses for the last).
 template <typename T, int CPT> struct Pack {
   static constexpr int kBytes = CPT * (int)sizeof(T);
-  static constexpr int kWords = kBytes / 8;  // 8-byte words
-  uint2 u[kWords];
+  static_assert(kBytes == 4 || kBytes == 8 || kBytes % 16 == 0, "vector width");
+  uint32_t u[kBytes / 4];
 };
 
 template <typename T, int CPT> __device__ __forceinline__ Pack<T, CPT> ldv(const T* p) {
   Pack<T, CPT> r;
-  if constexpr (Pack<T, CPT>::kBytes == 8) {
-    r.u[0] = __ldg(reinterpret_cast<const uint2*>(p));
+  constexpr int nb = Pack<T, CPT>::kBytes;
+  if constexpr (nb == 4) {
+    r.u[0] = __ldg(reinterpret_cast<const unsigned int*>(p));
+  } else if constexpr (nb == 8) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    r.u[0] = v.x;
+    r.u[1] = v.y;
   } else {
 #pragma unroll
-    for (int i = 0; i < Pack<T, CPT>::kBytes / 16; ++i) {
+    for (int i = 0; i < nb / 16; ++i) {
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + i);
-      r.u[2 * i] = make_uint2(v.x, v.y);
-      r.u[2 * i + 1] = make_uint2(v.z, v.w);
+      r.u[4 * i] = v.x;
+      r.u[4 * i + 1] = v.y;
+      r.u[4 * i + 2] = v.z;
+      r.u[4 * i + 3] = v.w;
     }
   }
   return r;
@@ -76,38 +84,45 @@ template <typename T, int CPT> __device__ __forceinline__ void stv(T* p, const f
   T* e = reinterpret_cast<T*>(r.u);
 #pragma unroll
   for (int i = 0; i < CPT; ++i) e[i] = from_f<T>(f[i]);
-  if constexpr (Pack<T, CPT>::kBytes == 8) {
-    *reinterpret_cast<uint2*>(p) = r.u[0];
+  constexpr int nb = Pack<T, CPT>::kBytes;
+  if constexpr (nb == 4) {
+    *reinterpret_cast<unsigned int*>(p) = r.u[0];
+  } else if constexpr (nb == 8) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(r.u[0], r.u[1]);
   } else {
 #pragma unroll
-    for (int i = 0; i < Pack<T, CPT>::kBytes / 16; ++i)
-      reinterpret_cast<uint4*>(p)[i] = make_uint4(r.u[2 * i].x, r.u[2 * i].y, r.u[2 * i + 1].x,
-                                                  r.u[2 * i + 1].y);
+    for (int i = 0; i < nb / 16; ++i)
+      reinterpret_cast<uint4*>(p)[i] = make_uint4(r.u[4 * i], r.u[4 * i + 1], r.u[4 * i + 2],
+                                                  r.u[4 * i + 3]);
   }
 }
 
 template <typename T, int CPT> __device__ __forceinline__ void zerov(Pack<T, CPT>& r) {
 #pragma unroll
-  for (int i = 0; i < Pack<T, CPT>::kWords; ++i) r.u[i] = make_uint2(0, 0);
+  for (int i = 0; i < Pack<T, CPT>::kBytes / 4; ++i) r.u[i] = 0u;
 }
 
 // Rounding to the token dtype (identity for fp32).
 template <typename T> __device__ __forceinline__ float rnd(float x) { return to_f<T>(from_f<T>(x)); }
 
-// SiLU as the reference evaluates it for every dtype: x / (1 + exp(-x)) in fp32.
-__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+// SiLU in the reference's fp32 form x / (1 + exp(-x)), with the fast
+// exponential and division intrinsics: a few fp32 ulps from the exact form,
+// which after rounding to bf16 changed no output of the config-1 conv and
+// norm forwards (the exact form cost 1.8x the conv forward's time).
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
-// d silu / dx times dy, in the same fp32 form as the reference's SiLU backward.
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+
+// d silu / dx times dy, in the reference's fp32 form of the SiLU backward.
 __device__ __forceinline__ float silu_bwd_f(float dy, float x) {
-  const float s = 1.f / (1.f + expf(-x));
+  const float s = sigmoid_f(x);
   return dy * s * (1.f + x * (1.f - s));
 }
 
 // ---------------------------------------------------------------------------
 // causal depthwise convolution
 // ---------------------------------------------------------------------------
-constexpr int kConvWarps = 8;   // token strips per CTA
-constexpr int kConvStrip = 64;  // tokens per strip (one warp)
+constexpr int kConvStrip = 64;  // tokens per CTA (one strip of rows)
 constexpr int kConvMaxW = 4;
 
 struct ConvArgs {
@@ -159,20 +174,21 @@ __device__ __forceinline__ void load_row(const ConvArgs& a, const T* xb, int b, 
 // register window, weights and 8 rows in flight) and the backward at 128.
 constexpr int kFwdCPT = 4;
 constexpr int kBwdCPT = 4;
+constexpr int kConvChannels = 256 * 4;  // channels per CTA (256 threads x 4)
 
-// y = act(round(bias + sum_j w_j x_{t-W+1+j})): grid (D/(32*CPT), strips of
-// 8*64 tokens, B); one warp per 64-token strip, registers carry the W-1
-// previous rows.
+// y = act(round(bias + sum_j w_j x_{t-W+1+j})): grid (D/1024, T/64, B); a
+// CTA walks a 64-token strip of 1024 contiguous channels (every row access of
+// the CTA is 2 KB contiguous), each thread 4 channels, with the W-1 previous
+// rows carried in registers.
 template <typename T, int W, int ACT>
 __global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
   constexpr int CPT = kFwdCPT;
-  constexpr int R = 8;  // rows loaded per run
+  constexpr int R = 4;  // rows loaded per run
   constexpr int WP = W > 1 ? W - 1 : 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int d0 = (blockIdx.x * 32 + lane) * CPT;
+  const int d0 = (blockIdx.x * 256 + threadIdx.x) * CPT;
   const int b = blockIdx.z;
-  const int tb = (blockIdx.y * kConvWarps + warp) * kConvStrip;
-  if (d0 >= a.D || tb >= a.T) return;
+  const int tb = blockIdx.y * kConvStrip;
+  if (d0 >= a.D) return;
   const int te = min(tb + kConvStrip, a.T);
   float wt[W][CPT], bs[CPT];
   load_weights<W, CPT>(a, d0, wt, bs);
@@ -227,160 +243,169 @@ __global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
 // (rounded to the token dtype, as the reference's activation backward is),
 // dx_t = sum_j w_j dc_{t+W-1-j} emitted at s = t + W - 1, dw_j += dc_s
 // x_{s-W+1+j} and dbias += dc_s for s < te.  Rows t < 0 of the first strip
-// are the prefix rows (dprefix).  Per-CTA sums of dw / dbias go to
-// part[blk][j][d] through shared memory in a fixed order.
+// are the prefix rows (dprefix).  Each thread's sums of dw / dbias for its
+// channels go to part[blk][j][d] (blk = the CTA's strip), reduced over the
+// strips in a fixed order by k_col_sum.
 template <typename T, int W, int ACT>
 __global__ void __launch_bounds__(256, 2) k_conv_bwd(ConvArgs a) {
   constexpr int CPT = kBwdCPT;
   constexpr int R = 4;
   constexpr int WP = W > 1 ? W - 1 : 1;
-  __shared__ float red[kConvWarps][32 * CPT];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int d0 = (blockIdx.x * 32 + lane) * CPT;
+  const int d0 = (blockIdx.x * 256 + threadIdx.x) * CPT;
   const int b = blockIdx.z;
-  const int tb = (blockIdx.y * kConvWarps + warp) * kConvStrip;
-  const bool active = d0 < a.D && tb < a.T;
+  const int tb = blockIdx.y * kConvStrip;
+  if (d0 >= a.D) return;
   float dwp[W + 1][CPT];
 #pragma unroll
   for (int j = 0; j <= W; ++j)
 #pragma unroll
     for (int i = 0; i < CPT; ++i) dwp[j][i] = 0.f;
-  if (active) {
-    const int te = min(tb + kConvStrip, a.T);
-    float wt[W][CPT], bs[CPT];
-    load_weights<W, CPT>(a, d0, wt, bs);
-    const T* xb = reinterpret_cast<const T*>(a.x) + (int64_t)b * a.T * a.D + d0;
-    const T* dyb = reinterpret_cast<const T*>(a.dy) + (int64_t)b * a.T * a.D + d0;
-    T* dxb = reinterpret_cast<T*>(a.dx) + (int64_t)b * a.T * a.D + d0;
-    float win[WP][CPT], dcw[WP][CPT];  // previous W-1 input rows and dc values
+  const int te = min(tb + kConvStrip, a.T);
+  float wt[W][CPT], bs[CPT];
+  load_weights<W, CPT>(a, d0, wt, bs);
+  const T* xb = reinterpret_cast<const T*>(a.x) + (int64_t)b * a.T * a.D + d0;
+  const T* dyb = reinterpret_cast<const T*>(a.dy) + (int64_t)b * a.T * a.D + d0;
+  T* dxb = reinterpret_cast<T*>(a.dx) + (int64_t)b * a.T * a.D + d0;
+  float win[WP][CPT], dcw[WP][CPT];  // previous W-1 input rows and dc values
 #pragma unroll
-    for (int i = 0; i < W - 1; ++i) {
-      load_row<T, W, CPT>(a, xb, b, d0, tb - (W - 1) + i, win[i]);
+  for (int i = 0; i < W - 1; ++i) {
+    load_row<T, W, CPT>(a, xb, b, d0, tb - (W - 1) + i, win[i]);
 #pragma unroll
-      for (int e = 0; e < CPT; ++e) dcw[i][e] = 0.f;
+    for (int e = 0; e < CPT; ++e) dcw[i][e] = 0.f;
+  }
+  const int send = te + W - 1;
+  const bool want_dprefix = a.dprefix && tb == 0;
+  for (int s0 = tb; s0 < send; s0 += R) {
+    Pack<T, CPT> rx[R], rdy[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int s = s0 + r;
+      if (s < a.T && s < send) {
+        rx[r] = ldv<T, CPT>(xb + (int64_t)s * a.D);
+        rdy[r] = ldv<T, CPT>(dyb + (int64_t)s * a.D);
+      } else {
+        zerov<T, CPT>(rx[r]);
+        zerov<T, CPT>(rdy[r]);
+      }
     }
-    const int send = te + W - 1;
-    const bool want_dprefix = a.dprefix && tb == 0;
-    for (int s0 = tb; s0 < send; s0 += R) {
-      Pack<T, CPT> rx[R], rdy[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int s = s0 + r;
-        if (s < a.T && s < send) {
-          rx[r] = ldv<T, CPT>(xb + (int64_t)s * a.D);
-          rdy[r] = ldv<T, CPT>(dyb + (int64_t)s * a.D);
+    for (int r = 0; r < R; ++r) {
+      const int s = s0 + r;
+      if (s >= send) continue;  // (predicated: the loop stays unrolled)
+      float cur[CPT], dc[CPT];
+      unpackv<T, CPT>(rx[r], cur);
+      unpackv<T, CPT>(rdy[r], dc);
+      if (s < a.T) {
+        if (ACT) {
+#pragma unroll
+          for (int i = 0; i < CPT; ++i) {
+            float acc = bs[i];
+#pragma unroll
+            for (int j = 0; j < W - 1; ++j) acc = fmaf(wt[j][i], win[j][i], acc);
+            acc = fmaf(wt[W - 1][i], cur[i], acc);
+            dc[i] = rnd<T>(silu_bwd_f(dc[i], rnd<T>(acc)));
+          }
+        }
+        if (s < te) {
+#pragma unroll
+          for (int i = 0; i < CPT; ++i) {
+#pragma unroll
+            for (int j = 0; j < W - 1; ++j) dwp[j][i] = fmaf(dc[i], win[j][i], dwp[j][i]);
+            dwp[W - 1][i] = fmaf(dc[i], cur[i], dwp[W - 1][i]);
+            dwp[W][i] += dc[i];
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) dc[i] = 0.f;
+      }
+      // emit input row t = s - W + 1
+      const int t = s - (W - 1);
+      if (t >= tb || (want_dprefix && t >= -(W - 1))) {
+        float o[CPT];
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+          float acc = wt[0][i] * dc[i];
+#pragma unroll
+          for (int j = 1; j < W; ++j) acc = fmaf(wt[j][i], dcw[W - 1 - j][i], acc);
+          o[i] = acc;
+        }
+        if (t >= tb) {
+          if (t < te) stv<T, CPT>(dxb + (int64_t)t * a.D, o);
         } else {
-          zerov<T, CPT>(rx[r]);
-          zerov<T, CPT>(rdy[r]);
+          float* dp = a.dprefix + ((int64_t)b * (W - 1) + (t + W - 1)) * a.D + d0;
+#pragma unroll
+          for (int i = 0; i < CPT; ++i) dp[i] = o[i];
         }
       }
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int s = s0 + r;
-        if (s >= send) continue;  // (predicated: the loop stays unrolled)
-        float cur[CPT], dc[CPT];
-        unpackv<T, CPT>(rx[r], cur);
-        unpackv<T, CPT>(rdy[r], dc);
-        if (s < a.T) {
+      for (int j = 0; j + 1 < W - 1; ++j)
 #pragma unroll
-          for (int i = 0; i < CPT; ++i) {
-            if (ACT) {
-              float acc = bs[i];
-#pragma unroll
-              for (int j = 0; j < W - 1; ++j) acc = fmaf(wt[j][i], win[j][i], acc);
-              acc = fmaf(wt[W - 1][i], cur[i], acc);
-              dc[i] = rnd<T>(silu_bwd_f(dc[i], rnd<T>(acc)));
-            }
-          }
-          if (s < te) {
-#pragma unroll
-            for (int i = 0; i < CPT; ++i) {
-#pragma unroll
-              for (int j = 0; j < W - 1; ++j) dwp[j][i] = fmaf(dc[i], win[j][i], dwp[j][i]);
-              dwp[W - 1][i] = fmaf(dc[i], cur[i], dwp[W - 1][i]);
-              dwp[W][i] += dc[i];
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < CPT; ++i) dc[i] = 0.f;
+        for (int i = 0; i < CPT; ++i) {
+          win[j][i] = win[j + 1][i];
+          dcw[j][i] = dcw[j + 1][i];
         }
-        // emit input row t = s - W + 1
-        const int t = s - (W - 1);
-        if (t >= tb || (want_dprefix && t >= -(W - 1))) {
-          float o[CPT];
+      if (W > 1) {
 #pragma unroll
-          for (int i = 0; i < CPT; ++i) {
-            float acc = wt[0][i] * dc[i];
-#pragma unroll
-            for (int j = 1; j < W; ++j) acc = fmaf(wt[j][i], dcw[W - 1 - j][i], acc);
-            o[i] = acc;
-          }
-          if (t >= tb) {
-            if (t < te) stv<T, CPT>(dxb + (int64_t)t * a.D, o);
-          } else {
-            float* dp = a.dprefix + ((int64_t)b * (W - 1) + (t + W - 1)) * a.D + d0;
-#pragma unroll
-            for (int i = 0; i < CPT; ++i) dp[i] = o[i];
-          }
-        }
-#pragma unroll
-        for (int j = 0; j + 1 < W - 1; ++j)
-#pragma unroll
-          for (int i = 0; i < CPT; ++i) {
-            win[j][i] = win[j + 1][i];
-            dcw[j][i] = dcw[j + 1][i];
-          }
-        if (W > 1) {
-#pragma unroll
-          for (int i = 0; i < CPT; ++i) {
-            win[WP - 1][i] = cur[i];
-            dcw[WP - 1][i] = dc[i];
-          }
+        for (int i = 0; i < CPT; ++i) {
+          win[WP - 1][i] = cur[i];
+          dcw[WP - 1][i] = dc[i];
         }
       }
     }
   }
-  // CTA sum over the 8 strips, one (tap, 32*CPT-channel) slice at a time
   const int blk = blockIdx.z * gridDim.y + blockIdx.y;
-  const int dc0 = blockIdx.x * 32 * CPT;
 #pragma unroll
   for (int j = 0; j <= W; ++j) {
+    float* pp = a.part + ((int64_t)blk * (W + 1) + j) * a.D + d0;
 #pragma unroll
-    for (int i = 0; i < CPT; ++i) red[warp][lane * CPT + i] = dwp[j][i];
-    __syncthreads();
-    const int c = threadIdx.x;
-    if (c < 32 * CPT && dc0 + c < a.D) {
-      float sum = 0.f;
-#pragma unroll
-      for (int k = 0; k < kConvWarps; ++k) sum += red[k][c];
-      a.part[((int64_t)blk * (W + 1) + j) * a.D + dc0 + c] = sum;
-    }
-    __syncthreads();
+    for (int i = 0; i < CPT; ++i) pp[i] = dwp[j][i];
   }
 }
 
-// dweight[d][j] (j < W) and dbias[d] (j = W): sum of part[k][j][d] over k in order.
-__global__ void k_conv_reduce(const float* part, int nblk, int W, int D, float* dw, float* dbias) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (W + 1) * D) return;
-  const int j = idx / D, d = idx - j * D;
-  float sum = 0.f;
-  for (int k = 0; k < nblk; ++k) sum += part[(int64_t)k * (W + 1) * D + idx];
-  if (j < W) dw[(int64_t)d * W + j] = sum;
-  else if (dbias) dbias[d] = sum;
+// Column sums of part[nblk][ncol] in a fixed order: a CTA takes 32 columns;
+// its 8 warps take the rows k = g, g + 8, ... (four loads in flight each) and
+// the 8 partial sums are added in warp order.  The sum of column col goes to
+// out[col] (W == 0), or, for the convolution's [W+1][D] partials, to
+// dweight[d][j] (col = j D + d, j < W) and dbias[d] (j = W).
+__global__ void __launch_bounds__(256) k_col_sum(const float* part, int nblk, int ncol, int W,
+                                                 int D, float* out, float* dbias) {
+  __shared__ float red[8][32];
+  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (col < ncol) {
+    int k = g;
+    for (; k + 24 < nblk; k += 32) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] += part[(int64_t)(k + 8 * u) * ncol + col];
+    }
+    for (; k < nblk; k += 8) acc[0] += part[(int64_t)k * ncol + col];
+  }
+  red[g][lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  __syncthreads();
+  if (g == 0 && col < ncol) {
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum += red[i][lane];
+    if (W == 0) {
+      out[col] = sum;
+    } else {
+      const int j = col / D, d = col - j * D;
+      if (j < W) out[(int64_t)d * W + j] = sum;
+      else if (dbias) dbias[d] = sum;
+    }
+  }
 }
 
 int conv_nblk(const gdn2_conv_problem* p) {
-  const int per = kConvWarps * kConvStrip;
-  return p->B * ((p->T + per - 1) / per);
+  return p->B * ((p->T + kConvStrip - 1) / kConvStrip);
 }
 
 template <typename T, int W>
 cudaError_t launch_conv(const gdn2_conv_problem* p, const ConvArgs& a, bool bwd, cudaStream_t st) {
-  const int per = kConvWarps * kConvStrip;
-  const int cpt = bwd ? kBwdCPT : kFwdCPT;
-  dim3 grid((p->D + 32 * cpt - 1) / (32 * cpt), (p->T + per - 1) / per, p->B);
+  static_assert(kFwdCPT * 256 == kConvChannels && kBwdCPT * 256 == kConvChannels, "CTA width");
+  dim3 grid((p->D + kConvChannels - 1) / kConvChannels, (p->T + kConvStrip - 1) / kConvStrip, p->B);
   if (!bwd) {
     if (p->activation) k_conv_fwd<T, W, 1><<<grid, 256, 0, st>>>(a);
     else k_conv_fwd<T, W, 0><<<grid, 256, 0, st>>>(a);
@@ -391,8 +416,7 @@ cudaError_t launch_conv(const gdn2_conv_problem* p, const ConvArgs& a, bool bwd,
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int n = (W + 1) * p->D;
-  k_conv_reduce<<<(n + 255) / 256, 256, 0, st>>>(a.part, conv_nblk(p), W, p->D, a.dweight,
-                                                  a.dbias);
+  k_col_sum<<<(n + 31) / 32, 256, 0, st>>>(a.part, conv_nblk(p), n, W, p->D, a.dweight, a.dbias);
   return cudaGetLastError();
 }
 
@@ -400,6 +424,7 @@ cudaError_t launch_conv(const gdn2_conv_problem* p, const ConvArgs& a, bool bwd,
 // SiLU-gated RMSNorm
 // ---------------------------------------------------------------------------
 constexpr int kNormMaxBlocks = 1024;
+constexpr int kNormUnroll = 1;  // row groups loaded per trip (2 measured slower)
 
 struct NormArgs {
   int64_t rows;
@@ -442,41 +467,53 @@ template <typename TW> __device__ __forceinline__ void load_w8(const TW* w, int 
 // except silu(z), which runs in the input dtype.
 template <typename T, typename TW, typename TO, int TPR, bool F32>
 __global__ void __launch_bounds__(256) k_gnorm_fwd(NormArgs a) {
-  constexpr int RPC = 256 / TPR;
+  constexpr int RPC = 256 / TPR, U = kNormUnroll;
   const int sub = threadIdx.x % TPR, slot = threadIdx.x / TPR;
   const int c = 8 * sub;
   const bool live = c < a.N;
   float w[8];
   load_w8<TW>(reinterpret_cast<const TW*>(a.w), c, a.N, w);
   const float inv_n = 1.f / (float)a.N;
-  // the trip count is uniform across the CTA: the row's lanes share a warp
-  // with other rows' lanes, and every lane joins the shuffles of each trip
-  for (int64_t base = (int64_t)blockIdx.x * RPC; base < a.rows; base += (int64_t)gridDim.x * RPC) {
-    const int64_t row = base + slot;
-    const bool on = live && row < a.rows;
-    float x[8], z[8];
-    if (on) {
-      unpackv<T, 8>(ldv<T, 8>(reinterpret_cast<const T*>(a.x) + row * a.N + c), x);
-      unpackv<T, 8>(ldv<T, 8>(reinterpret_cast<const T*>(a.z) + row * a.N + c), z);
-    } else {
+  // The trip count is uniform across the CTA: a row's lanes share a warp
+  // with other rows' lanes, and every lane joins the shuffles of each trip.
+  // Each trip loads U row groups before any arithmetic.
+  for (int64_t base = (int64_t)blockIdx.x * RPC * U; base < a.rows;
+       base += (int64_t)gridDim.x * RPC * U) {
+    Pack<T, 8> px[U], pz[U];
+    bool on[U];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = z[i] = 0.f;
+    for (int u = 0; u < U; ++u) {
+      const int64_t row = base + u * RPC + slot;
+      on[u] = live && row < a.rows;
+      if (on[u]) {
+        px[u] = ldv<T, 8>(reinterpret_cast<const T*>(a.x) + row * a.N + c);
+        pz[u] = ldv<T, 8>(reinterpret_cast<const T*>(a.z) + row * a.N + c);
+      } else {
+        zerov<T, 8>(px[u]);
+        zerov<T, 8>(pz[u]);
+      }
     }
-    using TR = typename std::conditional<F32, float, T>::type;  // intermediate rounding
-    float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += rnd<TR>(x[i] * x[i]);
-    ss = group_sum<TPR>(ss);
-    const float var = rnd<TR>(ss * inv_n);
-    const float r = rnd<TR>(rsqrtf(rnd<TR>(var + a.eps)));
-    float y[8];
+    for (int u = 0; u < U; ++u) {
+      float x[8], z[8];
+      unpackv<T, 8>(px[u], x);
+      unpackv<T, 8>(pz[u], z);
+      using TR = typename std::conditional<F32, float, T>::type;  // intermediate rounding
+      float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float n = rnd<TR>(x[i] * r);
-      n = rnd<typename std::conditional<F32, float, TW>::type>(n * w[i]);
-      y[i] = n * rnd<T>(silu_f(z[i]));
+      for (int i = 0; i < 8; ++i) ss += rnd<TR>(x[i] * x[i]);
+      ss = group_sum<TPR>(ss);
+      const float var = rnd<TR>(ss * inv_n);
+      const float r = rnd<TR>(rsqrtf(rnd<TR>(var + a.eps)));
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float n = rnd<TR>(x[i] * r);
+        n = rnd<typename std::conditional<F32, float, TW>::type>(n * w[i]);
+        y[i] = n * rnd<T>(silu_f(z[i]));
+      }
+      if (on[u]) stv<TO, 8>(reinterpret_cast<TO*>(a.y) + (base + u * RPC + slot) * a.N + c, y);
     }
-    if (on) stv<TO, 8>(reinterpret_cast<TO*>(a.y) + row * a.N + c, y);
   }
 }
 
@@ -485,7 +522,7 @@ __global__ void __launch_bounds__(256) k_gnorm_fwd(NormArgs a) {
 //   dweight = sum_rows dy n s (per-CTA partials, reduced in a fixed order).
 template <typename T, typename TW, typename TO, int TPR>
 __global__ void __launch_bounds__(256) k_gnorm_bwd(NormArgs a) {
-  constexpr int RPC = 256 / TPR;
+  constexpr int RPC = 256 / TPR, U = kNormUnroll;
   __shared__ float red[256 * 8];
   const int sub = threadIdx.x % TPR, slot = threadIdx.x / TPR;
   const int c = 8 * sub;
@@ -495,42 +532,57 @@ __global__ void __launch_bounds__(256) k_gnorm_bwd(NormArgs a) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) dwp[i] = 0.f;
   const float inv_n = 1.f / (float)a.N;
-  // CTA-uniform trip count (see the forward)
-  for (int64_t base = (int64_t)blockIdx.x * RPC; base < a.rows; base += (int64_t)gridDim.x * RPC) {
-    const int64_t row = base + slot;
-    const bool on = live && row < a.rows;
-    float x[8], z[8], dy[8];
-    if (on) {
-      unpackv<T, 8>(ldv<T, 8>(reinterpret_cast<const T*>(a.x) + row * a.N + c), x);
-      unpackv<T, 8>(ldv<T, 8>(reinterpret_cast<const T*>(a.z) + row * a.N + c), z);
-      unpackv<TO, 8>(ldv<TO, 8>(reinterpret_cast<const TO*>(a.dy) + row * a.N + c), dy);
-    } else {
+  // CTA-uniform trip count and U row groups loaded per trip (see the forward)
+  for (int64_t base = (int64_t)blockIdx.x * RPC * U; base < a.rows;
+       base += (int64_t)gridDim.x * RPC * U) {
+    Pack<T, 8> px[U], pz[U];
+    Pack<TO, 8> pd[U];
+    bool on[U];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = z[i] = dy[i] = 0.f;
+    for (int u = 0; u < U; ++u) {
+      const int64_t row = base + u * RPC + slot;
+      on[u] = live && row < a.rows;
+      if (on[u]) {
+        px[u] = ldv<T, 8>(reinterpret_cast<const T*>(a.x) + row * a.N + c);
+        pz[u] = ldv<T, 8>(reinterpret_cast<const T*>(a.z) + row * a.N + c);
+        pd[u] = ldv<TO, 8>(reinterpret_cast<const TO*>(a.dy) + row * a.N + c);
+      } else {
+        zerov<T, 8>(px[u]);
+        zerov<T, 8>(pz[u]);
+        zerov<TO, 8>(pd[u]);
+      }
     }
-    float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
-    ss = group_sum<TPR>(ss);
-    const float r = rsqrtf(ss * inv_n + a.eps);
-    float n[8], dn[8], dz[8], dot = 0.f;
+    for (int u = 0; u < U; ++u) {
+      float x[8], z[8], dy[8];
+      unpackv<T, 8>(px[u], x);
+      unpackv<T, 8>(pz[u], z);
+      unpackv<TO, 8>(pd[u], dy);
+      float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float sg = 1.f / (1.f + expf(-z[i]));
-      const float s = z[i] * sg;
-      n[i] = x[i] * r;
-      dn[i] = dy[i] * w[i] * s;
-      dot = fmaf(dn[i], n[i], dot);
-      dz[i] = dy[i] * n[i] * w[i] * sg * (1.f + z[i] * (1.f - sg));
-      dwp[i] = fmaf(dy[i] * n[i], s, dwp[i]);
-    }
-    dot = group_sum<TPR>(dot) * inv_n;
-    float dx[8];
+      for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+      ss = group_sum<TPR>(ss);
+      const float r = rsqrtf(ss * inv_n + a.eps);
+      float n[8], dn[8], dz[8], dot = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dx[i] = r * (dn[i] - n[i] * dot);
-    if (on) {
-      stv<T, 8>(reinterpret_cast<T*>(a.dx) + row * a.N + c, dx);
-      stv<T, 8>(reinterpret_cast<T*>(a.dz) + row * a.N + c, dz);
+      for (int i = 0; i < 8; ++i) {
+        const float sg = sigmoid_f(z[i]);
+        const float s = z[i] * sg;
+        n[i] = x[i] * r;
+        dn[i] = dy[i] * w[i] * s;
+        dot = fmaf(dn[i], n[i], dot);
+        dz[i] = dy[i] * n[i] * w[i] * sg * (1.f + z[i] * (1.f - sg));
+        dwp[i] = fmaf(dy[i] * n[i], s, dwp[i]);
+      }
+      dot = group_sum<TPR>(dot) * inv_n;
+      float dx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dx[i] = r * (dn[i] - n[i] * dot);
+      if (on[u]) {
+        const int64_t row = base + u * RPC + slot;
+        stv<T, 8>(reinterpret_cast<T*>(a.dx) + row * a.N + c, dx);
+        stv<T, 8>(reinterpret_cast<T*>(a.dz) + row * a.N + c, dz);
+      }
     }
   }
   // CTA sum over the RPC row slots, column by column in a fixed order
@@ -544,38 +596,47 @@ __global__ void __launch_bounds__(256) k_gnorm_bwd(NormArgs a) {
   }
 }
 
-__global__ void k_norm_reduce(const float* part, int nblk, int N, float* dw) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= N) return;
-  float sum = 0.f;
-  for (int k = 0; k < nblk; ++k) sum += part[(int64_t)k * N + col];
-  dw[col] = sum;
-}
-
 int norm_tpr(int N) {
   if (N % 8 != 0 || N <= 0 || N > 256) return 0;
   return N <= 64 ? 8 : (N <= 128 ? 16 : 32);
 }
 
+// Upper bound of the CTA count (the backward's partial-sum rows).
 int norm_nblk(const gdn2_norm_problem* p) {
-  const int rpc = 256 / norm_tpr(p->N);
-  const int64_t need = (p->rows + rpc - 1) / rpc;
+  const int per = 256 / norm_tpr(p->N) * kNormUnroll;
+  const int64_t need = (p->rows + per - 1) / per;
   return (int)(need < kNormMaxBlocks ? need : kNormMaxBlocks);
+}
+
+// CTAs actually launched: no more than fit on the GPU at once, so the
+// row-group loop has no partial last wave.
+template <typename K>
+cudaError_t norm_grid(K kernel, const gdn2_norm_problem* p, int* grid) {
+  int sms = 0, occ = 0;
+  cudaError_t e = num_sms(&sms);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, 256, 0);
+  if (e != cudaSuccess) return e;
+  const int cap = sms * (occ > 0 ? occ : 1), ub = norm_nblk(p);
+  *grid = ub < cap ? ub : cap;
+  return cudaSuccess;
 }
 
 template <typename T, typename TW, typename TO, int TPR>
 cudaError_t launch_gnorm2(const gdn2_norm_problem* p, const NormArgs& a, bool bwd,
                           cudaStream_t st) {
-  const int nblk = norm_nblk(p);
+  int nblk = 0;
+  cudaError_t e;
   if (!bwd) {
-    if (p->fp32_math) k_gnorm_fwd<T, TW, TO, TPR, true><<<nblk, 256, 0, st>>>(a);
-    else k_gnorm_fwd<T, TW, TO, TPR, false><<<nblk, 256, 0, st>>>(a);
+    auto k = p->fp32_math ? k_gnorm_fwd<T, TW, TO, TPR, true> : k_gnorm_fwd<T, TW, TO, TPR, false>;
+    if ((e = norm_grid(k, p, &nblk)) != cudaSuccess) return e;
+    k<<<nblk, 256, 0, st>>>(a);
     return cudaGetLastError();
   }
+  if ((e = norm_grid(k_gnorm_bwd<T, TW, TO, TPR>, p, &nblk)) != cudaSuccess) return e;
   k_gnorm_bwd<T, TW, TO, TPR><<<nblk, 256, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  k_norm_reduce<<<(p->N + 127) / 128, 128, 0, st>>>(a.part, nblk, p->N, a.dweight);
+  k_col_sum<<<(p->N + 31) / 32, 256, 0, st>>>(a.part, nblk, p->N, 0, 0, a.dweight, nullptr);
   return cudaGetLastError();
 }
 

@@ -160,8 +160,8 @@ def test_conv_and_norm_arguments_are_checked(lib):
     """Block prologue / epilogue entry points: shapes, dtypes and workspace
     sizes are validated before any CUDA call."""
     conv = N.ConvProblem(2, 100, 64, 4, 1, 1)
-    # 512-token blocks per batch entry; (W + 1) fp32 partial sums per channel
-    assert lib.gdn2_conv_bwd_workspace_bytes(conv) == 2 * 1 * 5 * 64 * 4
+    # 64-token strips per batch entry; (W + 1) fp32 partial sums per channel
+    assert lib.gdn2_conv_bwd_workspace_bytes(conv) == 2 * 2 * 5 * 64 * 4
     for bad, code in ((N.ConvProblem(2, 100, 64, 5, 1, 1), N.ERR_UNSUPPORTED),
                       (N.ConvProblem(2, 100, 60, 4, 1, 1), N.ERR_UNSUPPORTED),
                       (N.ConvProblem(2, 0, 64, 4, 1, 1), N.ERR_INVALID),
