@@ -549,7 +549,7 @@ def run_decode(dev, lib, N):
             "peak_source": kind, "gpu_launches": DEC_STEPS}
 
 
-def run_block_ops(dev, lib, N, iters=20):
+def run_block_ops(dev, lib, N, iters=20, warm=3):
     """Conv + SiLU and gated RMSNorm kernels at config-1 shapes (bf16)."""
     bf = torch.bfloat16
     gen = torch.Generator(device=dev).manual_seed(9)
@@ -589,7 +589,7 @@ def run_block_ops(dev, lib, N, iters=20):
     tensor_bytes = B * T * D * 2
     for name, (fn, ntensors) in calls.items():
         src = nsets if name.startswith("norm") else sets
-        for i in range(3):
+        for i in range(warm):
             N.check(fn(src[i % 2]), name)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -702,14 +702,24 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--workload", choices=("config1", "sp", "heads"), default="config1",
-                    help="config1 (headline), or config 4 sequence-parallel / head-sharded")
+    ap.add_argument("--workload", choices=("config1", "sp", "heads", "block"), default="config1",
+                    help="config1 (headline), config 4 sequence-parallel / head-sharded, or "
+                         "block: only the prologue / epilogue kernels (--steps timed launches "
+                         "each after --warmup, one GPU)")
     ap.add_argument("--profile", action="store_true",
                     help="small ncu case: config-1 phases at --batch, nothing else")
     ap.add_argument("--batch", type=int, default=2, help="batch of the --profile case")
     args = ap.parse_args(argv)
     if args.profile:
         run_profile_case(args, int(os.environ.get("LOCAL_RANK", "0")))
+        return
+    if args.workload == "block":
+        from qwendopamine_b200 import _native as N
+
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        blk = run_block_ops(dev, N.load(), N, iters=args.steps, warm=args.warmup)
+        print(json.dumps({"workload": "block", "block_ops": blk}), flush=True)
         return
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3

@@ -22,6 +22,13 @@ backward:
     4. ``gdn2_chunk_bwd`` with that end-state gradient.
 Each rank's local backward then yields exact gradients for its own inputs.
 
+The block's causal short convolution needs the W - 1 tokens before a span
+(``pre_num_conv_tokens`` in FLA-CP's context, ``fla/ops/cp/context.py``):
+:func:`short_conv_cp` gathers every span's last W - 1 rows, runs the
+convolution with the previous span's rows as its prefix, and in the backward
+sends the prefix gradient back to the rank that owns those rows, so the whole
+block, not only the core recurrence, runs sequence-parallel.
+
 The gather is a plain function argument so the same code runs over NCCL,
 over gloo (CPU tests of the exchange) or emulated inside one process.
 """
@@ -35,7 +42,8 @@ import torch
 from .. import _native as N
 from .chunk_gdn2 import _aligned16, _require_cuda
 
-__all__ = ["chunk_gdn2_cp", "CPChunkGDN2Function", "gather_span_maps"]
+__all__ = ["chunk_gdn2_cp", "CPChunkGDN2Function", "ConvHaloFunction", "gather_span_maps",
+           "short_conv_cp"]
 
 Gather = Callable[[torch.Tensor], torch.Tensor]
 
@@ -176,3 +184,48 @@ def chunk_gdn2_cp(q, k, v, g, b, w, *, rank: int, world: int, gather: Gather,
     with torch.cuda.device(q.device):
         return CPChunkGDN2Function.apply(q, k, v, g, b, w, initial_state, scale,
                                          use_qk_l2norm_in_kernel, rank, world, gather)
+
+
+class ConvHaloFunction(torch.autograd.Function):
+    """Boundary rows of the causal convolution across spans.
+
+    forward: every rank contributes its span's last W - 1 rows ``tail``
+    ``[B, W-1, D]``; rank r receives rank r-1's rows as its prefix (zeros on
+    rank 0, the sequence start).  backward: the prefix gradients are gathered
+    and rank r takes rank r+1's as the gradient of its own tail (zero on the
+    last rank).  Every rank takes part in both gathers."""
+
+    @staticmethod
+    def forward(ctx, tail, rank, world, gather):
+        ctx.rank, ctx.world, ctx.gather = rank, world, gather
+        tails = gather(tail.contiguous())
+        return tails[rank - 1].clone() if rank > 0 else torch.zeros_like(tail)
+
+    @staticmethod
+    def backward(ctx, dprefix):
+        grads = ctx.gather(dprefix.contiguous())
+        dtail = (grads[ctx.rank + 1].clone() if ctx.rank + 1 < ctx.world
+                 else torch.zeros_like(dprefix))
+        return dtail, None, None, None
+
+
+def short_conv_cp(x, weight, bias=None, activation="silu", *, rank: int, world: int,
+                  gather: Gather):
+    """Sequence-parallel ``ShortConvolution`` (gdn2.py:372-430) for rank r's
+    contiguous span ``x`` ``[B, T_r, D]`` of every sequence (T_r >= W - 1):
+    the outputs equal the single-device convolution's rows of that span, and
+    the backward gives this span's dx, including the part that reaches it
+    through the next span's prefix.  The weight and bias gradients are this
+    span's share; summing them over the ranks (as a data-parallel all-reduce
+    of parameter gradients does) gives the whole sequence's."""
+    from .block_ops import short_conv
+
+    W = weight.shape[-1]
+    if W == 1 or world == 1:
+        return short_conv(x, weight, bias, activation)[0]
+    if x.shape[1] < W - 1:
+        raise ValueError(f"rank {rank} holds {x.shape[1]} tokens; the convolution's halo needs "
+                         f"at least {W - 1} per span")
+    prefix = ConvHaloFunction.apply(x[:, -(W - 1):], rank, world, gather)
+    return short_conv(x, weight, bias, activation, prefix=prefix)[0]
+

@@ -3,7 +3,10 @@
 Every rank builds the same seeded sequence, runs its span through
 chunk_gdn2_cp with the NCCL all-gather, and checks outputs, the final state
 and all gradients of its span against chunk_gdn2 run on the whole sequence on
-its own GPU.  Exit status 0 means every rank agreed.
+its own GPU.  The same for the block's short convolution through
+short_conv_cp (the W-1-row halo exchanged over NCCL, its gradient returned
+to the previous rank; weight gradients all-reduced).  Exit status 0 means
+every rank agreed.
 """
 
 import datetime
@@ -16,7 +19,8 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from qwendopamine_b200 import chunk_gdn2  # noqa: E402
-from qwendopamine_b200.gdn2_ops.cp import chunk_gdn2_cp, gather_span_maps  # noqa: E402
+from qwendopamine_b200.gdn2_ops.block_ops import short_conv  # noqa: E402
+from qwendopamine_b200.gdn2_ops.cp import chunk_gdn2_cp, gather_span_maps, short_conv_cp  # noqa: E402
 
 
 def rel(a, b):
@@ -66,6 +70,27 @@ def main():
         errs["d" + n] = rel(loc[n].grad, full[n].grad[:, a:e])
     if rank == 0:
         errs["dh0"] = rel(hl.grad, hf.grad)
+    # the block's short convolution, sequence-parallel
+    D, W = 512, 4
+    xc = torch.randn(2, T, D, device=dev, generator=gen).to(bf)
+    wc = (torch.randn(D, 1, W, device=dev, generator=gen) * 0.5).to(bf)
+    bc = (torch.randn(D, device=dev, generator=gen) * 0.5).to(bf)
+    dyc = torch.randn(2, T, D, device=dev, generator=gen).to(bf)
+    xf, wf, bff = (t.clone().requires_grad_() for t in (xc, wc, bc))
+    yf, _ = short_conv(xf, wf, bff)
+    (yf.float() * dyc.float()).sum().backward()
+    xl = xc[:, a:e].clone().requires_grad_()
+    wl, bl = wc.clone().requires_grad_(), bc.clone().requires_grad_()
+    yl = short_conv_cp(xl, wl, bl, rank=rank, world=world,
+                       gather=lambda t: gather_span_maps(t, None))
+    (yl.float() * dyc[:, a:e].float()).sum().backward()
+    dwl, dbl = wl.grad.float(), bl.grad.float()
+    dist.all_reduce(dwl)
+    dist.all_reduce(dbl)
+    errs["conv_y"] = 0.0 if torch.equal(yl, yf[:, a:e]) else 1.0
+    errs["conv_dx"] = rel(xl.grad, xf.grad[:, a:e])
+    errs["conv_dw"] = rel(dwl, wf.grad.float())
+    errs["conv_db"] = rel(dbl, bff.grad.float())
     bad = {n: x for n, x in errs.items() if not x < 2e-2}
     print(f"rank {rank}: " + " ".join(f"{n}={x:.1e}" for n, x in errs.items()), flush=True)
     dist.barrier()

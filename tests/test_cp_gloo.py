@@ -111,6 +111,51 @@ def _worker_fail(rank, world, port, out_q):
         out_q.put((rank, f"error:{type(exc).__name__}"))
 
 
+def _worker_conv_halo(rank, world, port, out_q):
+    """Sequence-parallel short-convolution halo over gloo: each rank's prefix
+    is its predecessor's last W-1 rows; the prefix gradient returns to that
+    predecessor.  The oracle convolution of each span with its received
+    prefix must equal the whole sequence's rows of that span, and the
+    gradients routed back must complete each span's dx."""
+    import sys
+
+    sys.path.insert(0, ROOT)
+    from oracle import block_oracle as BO
+    from qwendopamine_b200.gdn2_ops.cp import ConvHaloFunction, gather_span_maps
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        gen = torch.Generator().manual_seed(5)
+        B, T, D, W = 2, 7 * world, 8, 4
+        x = torch.randn(B, T, D, generator=gen, dtype=torch.float64)
+        wt = torch.randn(D, W, generator=gen, dtype=torch.float64)
+        dy = torch.randn(B, T, D, generator=gen, dtype=torch.float64)
+        span = T // world
+        a, e = rank * span, (rank + 1) * span
+        xs = x[:, a:e].clone().requires_grad_()
+        prefix = ConvHaloFunction.apply(xs[:, -(W - 1):], rank, world,
+                                        lambda t: gather_span_maps(t, None))
+        want = x[:, a - (W - 1):a] if rank > 0 else torch.zeros(B, W - 1, D, dtype=x.dtype)
+        prefix_ok = bool(torch.equal(prefix.detach(), want))
+        y = BO.conv_fwd(xs.detach().numpy(), wt.numpy(), prefix=prefix.detach().numpy())
+        y_full = BO.conv_fwd(x.numpy(), wt.numpy())[:, a:e]
+        fwd_err = float(np.abs(y - y_full).max())
+        # backward: this span's local dx and prefix gradient from the oracle,
+        # the prefix gradient routed to the previous rank through the halo
+        dx, _, _, dpre = BO.conv_bwd(xs.detach().numpy(), wt.numpy(), dy[:, a:e].numpy(),
+                                     prefix=prefix.detach().numpy())
+        prefix.backward(torch.from_numpy(dpre))
+        dx_total = dx + xs.grad.numpy()
+        dx_full = BO.conv_bwd(x.numpy(), wt.numpy(), dy.numpy())[0][:, a:e]
+        bwd_err = float(np.abs(dx_total - dx_full).max())
+        out_q.put((rank, prefix_ok, fwd_err, bwd_err))
+    finally:
+        dist.destroy_process_group()
+
+
 def _run(fn, world, timeout):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -141,3 +186,13 @@ def test_dead_rank_surfaces_as_error_not_hang():
     res = _run(_worker_fail, 2, timeout=120)
     assert res[1] == (1, "raised")
     assert res[0][0] == 0 and res[0][1].startswith("error:")
+
+
+def test_conv_halo_exchange_over_gloo():
+    res = _run(_worker_conv_halo, 3, timeout=120)
+    assert [r[0] for r in res] == [0, 1, 2]
+    for rank, prefix_ok, fwd_err, bwd_err in res:
+        assert prefix_ok, rank
+        assert fwd_err < 1e-12, (rank, fwd_err)
+        assert bwd_err < 1e-12, (rank, bwd_err)
+

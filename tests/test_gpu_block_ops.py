@@ -277,3 +277,90 @@ def test_gated_norm_empty_rows(cuda_device):
     assert y.shape == (0, 64)
     y.sum().backward()
     assert torch.equal(w.grad, torch.zeros_like(w))
+
+
+class _ThreadGather:
+    """All-gather among ``world`` threads of one process (emulated ranks)."""
+
+    def __init__(self, world):
+        import threading
+
+        self.world = world
+        self.slots = [None] * world
+        self.barrier = threading.Barrier(world, timeout=60)
+
+    def __call__(self, rank):
+        def gather(t):
+            torch.cuda.synchronize()
+            self.slots[rank] = t
+            self.barrier.wait()
+            out = torch.stack([s.to(t.device) for s in self.slots])
+            self.barrier.wait()
+            return out
+        return gather
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_short_conv_sequence_parallel_equals_single_device(cuda_device, dtype):
+    """short_conv_cp over 3 emulated ranks (threads, one GPU) gives the spans
+    of the single-device convolution.  Gradients: each span's local backward
+    with the halo as a prefix, plus the prefix gradient returned to the
+    previous span (the routing ConvHaloFunction does over a process group,
+    tested over gloo in test_cp_gloo.py), equal the single-device dx; the
+    spans' weight / bias gradients sum to the single-device ones.  (The
+    emulation stops at the forward: on one GPU every rank's backward runs on
+    torch's one autograd thread per device, so a blocking gather there
+    cannot be emulated.)"""
+    import threading
+
+    from qwendopamine_b200.gdn2_ops.block_ops import short_conv
+    from qwendopamine_b200.gdn2_ops.cp import short_conv_cp
+
+    world, B, T, D, W = 3, 2, 3 * 50, 256, 4
+    x, w, b = _conv_inputs(B, T, D, W, True, dtype, cuda_device, seed=21)
+    dy = torch.randn(B, T, D, device=cuda_device).to(dtype)
+    xf, wf, bf = (t.clone().requires_grad_() for t in (x, w, b))
+    yf, _ = short_conv(xf, wf, bf)
+    (yf.float() * dy.float()).sum().backward()
+    span = T // world
+
+    gat = _ThreadGather(world)
+    outs, errs = [None] * world, []
+
+    def run(r):
+        try:
+            torch.cuda.set_device(cuda_device)
+            with torch.no_grad():
+                outs[r] = short_conv_cp(x[:, r * span:(r + 1) * span], w, b, rank=r, world=world,
+                                        gather=gat(r))
+            torch.cuda.synchronize()
+        except Exception as exc:  # surfaced below
+            errs.append(exc)
+            gat.barrier.abort()
+
+    ths = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join(timeout=120)
+    assert not errs, errs
+    assert torch.equal(torch.cat(outs, 1), yf.detach())
+
+    dxs, dws, dbs, dpres = [], [], [], []
+    for r in range(world):
+        xs = x[:, r * span:(r + 1) * span].clone().requires_grad_()
+        ws, bs = w.clone().requires_grad_(), b.clone().requires_grad_()
+        pre = (x[:, r * span - (W - 1):r * span] if r else torch.zeros_like(x[:, :W - 1]))
+        pre = pre.clone().requires_grad_()
+        y, _ = short_conv(xs, ws, bs, prefix=pre)
+        (y.float() * dy[:, r * span:(r + 1) * span].float()).sum().backward()
+        dxs.append(xs.grad.float())
+        dws.append(ws.grad.float())
+        dbs.append(bs.grad.float())
+        dpres.append(pre.grad.float())
+    for r in range(world - 1):  # the next span's prefix gradient belongs to this span's tail
+        dxs[r][:, -(W - 1):] += dpres[r + 1]
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert rel(torch.cat(dxs, 1), xf.grad) < tol
+    assert rel(sum(dws), wf.grad.float()) < tol
+    assert rel(sum(dbs), bf.grad.float()) < tol
