@@ -201,16 +201,23 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     T* ws = slotp(cur, L::vWg);
     for (int i = tid; i < kChunk * 16; i += NTH) {
       const int r = i >> 4, cc = (i & 15) * 2;
-      const float z0 = to_f<T>(vs[r * LDS + cc]) * to_f<T>(ws[r * LDS + cc]);
-      const float z1 = to_f<T>(vs[r * LDS + cc + 1]) * to_f<T>(ws[r * LDS + cc + 1]);
-      *reinterpret_cast<uint32_t*>(sZ + r * LDS + cc) = pack2<T>(z0, z1);
+      const float2 v2 = ld2<T>(vs + r * LDS + cc), w2 = ld2<T>(ws + r * LDS + cc);
+      *reinterpret_cast<uint32_t*>(sZ + r * LDS + cc) = pack2<T>(v2.x * w2.x, v2.y * w2.y);
     }
-    if (tid < D) {
+    // dgl[row] += sum over the slice's 32 columns of h * dh: 4 threads per
+    // row, 8 columns each, combined with two shuffles
+    for (int i = tid; i < 4 * D; i += NTH) {
+      const int row = i >> 2, part = i & 3;
       float acc = 0.f;
-#pragma unroll 8
-      for (int cc = 0; cc < 32; ++cc)
-        acc += to_f<T>(hs[tid * LDS + cc]) * to_f<T>(dhs[tid * LDS + cc]);
-      dgl[tid] += acc;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int cc = 8 * part + 2 * u;
+        const float2 h2 = ld2<T>(hs + row * LDS + cc), d2 = ld2<T>(dhs + row * LDS + cc);
+        acc += h2.x * d2.x + h2.y * d2.y;
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (part == 0) dgl[row] += acc;
     }
     __syncthreads();
     warp_mma16<1, NTO, true, true>(accQ, dos, LDS, 16 * wr, hs, LDS, wc * DQ, 32);
@@ -276,10 +283,10 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   // E = b * k_n * 2^G
   for (int i = tid; i < kChunk * (D / 2); i += NTH) {
     const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
-    const float e0 = to_f<T>(sb[r * LDK + cc]) * to_f<T>(sk[r * LDK + cc]) * rk[r] *
-                     fast_exp2(sG[r * LDG + cc]);
-    const float e1 = to_f<T>(sb[r * LDK + cc + 1]) * to_f<T>(sk[r * LDK + cc + 1]) * rk[r] *
-                     fast_exp2(sG[r * LDG + cc + 1]);
+    const float2 b2 = ld2<T>(sb + r * LDK + cc), k2 = ld2<T>(sk + r * LDK + cc);
+    const float2 G2 = ld2<float>(sG + r * LDG + cc);
+    const float e0 = b2.x * k2.x * rk[r] * fast_exp2(G2.x);
+    const float e1 = b2.y * k2.y * rk[r] * fast_exp2(G2.y);
     *reinterpret_cast<uint32_t*>(sE + r * LDK + cc) = pack2<T>(e0, e1);
   }
   __syncthreads();
@@ -328,23 +335,33 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   float (&dkb)[1][NTO][4] = accE;
   float (&dkn)[1][NTO][4] = accKd;
   float (&dG)[1][NTO][4] = accW;
+  // (owner elements come in column pairs: e = 2 hf + t is row 16 wr + gid +
+  // 8 hf, column wc DQ + 8 j + 2 tig + t, so each pair is one 32-bit access)
   float X[NTO][4];
 #pragma unroll
   for (int j = 0; j < NTO; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
-      const float G = sG[r * LDG + cl], GL = sG[(kChunk - 1) * LDG + cl];
-      const float gam = fast_exp2(G);
-      const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
-      const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
-      const float bb = to_f<T>(sb[r * LDK + cl]);
-      dq[0][j][e] = scale * gam * dq[0][j][e];
-      dkb[0][j][e] = gam * dkb[0][j][e];
-      const float kd = dkn[0][j][e] * fast_exp2(GL - G);
-      dkn[0][j][e] = kd;
-      X[j][e] = kn * kd;
-      dG[0][j][e] = qn * dq[0][j][e] + bb * kn * dkb[0][j][e];
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
+      const float2 G2 = ld2<float>(sG + r * LDG + c0);
+      const float2 GL2 = ld2<float>(sG + (kChunk - 1) * LDG + c0);
+      const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
+      const float2 b2 = ld2<T>(sb + r * LDK + c0);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int e = 2 * hf + t;
+        const float G = sel2(G2, t), GL = sel2(GL2, t);
+        const float gam = fast_exp2(G);
+        const float qn = sel2(q2, t) * rq[r];
+        const float kn = sel2(k2, t) * rk[r];
+        const float bb = sel2(b2, t);
+        dq[0][j][e] = scale * gam * dq[0][j][e];
+        dkb[0][j][e] = gam * dkb[0][j][e];
+        const float kd = dkn[0][j][e] * fast_exp2(GL - G);
+        dkn[0][j][e] = kd;
+        X[j][e] = kn * kd;
+        dG[0][j][e] = qn * dq[0][j][e] + bb * kn * dkb[0][j][e];
+      }
     }
   __syncthreads();  // sDW / sE / sT* are dead; R2 becomes the score tiles
 
@@ -362,15 +379,19 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   for (int i = tid; i < kChunk * (D / 2); i += NTH) {
     const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
     const int rb = r & ~15, re = rb + 15;
+    const float2 G2 = ld2<float>(sG + r * LDG + cc), Gb2 = ld2<float>(sG + rb * LDG + cc);
+    const float2 Ge2 = ld2<float>(sG + re * LDG + cc);
+    const float2 qv = ld2<T>(sq + r * LDK + cc), kv = ld2<T>(sk + r * LDK + cc);
+    const float2 bv = ld2<T>(sb + r * LDK + cc);
     float q2[2], kb2[2], k2[2];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      const float G = sG[r * LDG + cc + t];
-      const float f = fast_exp2(G - sG[rb * LDG + cc + t]);
-      const float fe = fast_exp2(sG[re * LDG + cc + t] - G);
-      const float kn = to_f<T>(sk[r * LDK + cc + t]) * rk[r];
-      q2[t] = scale * to_f<T>(sq[r * LDK + cc + t]) * rq[r] * f;
-      kb2[t] = to_f<T>(sb[r * LDK + cc + t]) * kn * f;
+      const float G = sel2(G2, t);
+      const float f = fast_exp2(G - sel2(Gb2, t));
+      const float fe = fast_exp2(sel2(Ge2, t) - G);
+      const float kn = sel2(kv, t) * rk[r];
+      q2[t] = scale * sel2(qv, t) * rq[r] * f;
+      kb2[t] = sel2(bv, t) * kn * f;
       k2[t] = kn * fe;
     }
     *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(q2[0], q2[1]);
@@ -401,26 +422,36 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
                                         wc * DQ, 16);
         const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
 #pragma unroll
-        for (int j = 0; j < NTO; ++j)
+        for (int j = 0; j < NTO; ++j) {
+          const float2 F2 = ld2<float>(FIJ + wc * DQ + 8 * j + 2 * tig);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float F = FIJ[wc * DQ + 8 * j + 2 * tig + (e & 1)];
+            const float F = sel2(F2, e & 1);
             tq[0][j][e] += F * pq[0][j][e];
             tk[0][j][e] += F * pk[0][j][e];
           }
+        }
       }
 #pragma unroll
       for (int j = 0; j < NTO; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
-          const float f = fast_exp2(sG[r * LDG + cl] - sG[(16 * I) * LDG + cl]);
-          const float xq = scale * tq[0][j][e] * f, xk = tk[0][j][e] * f;
-          const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
-          const float kb = to_f<T>(sb[r * LDK + cl]) * to_f<T>(sk[r * LDK + cl]) * rk[r];
-          dq[0][j][e] += xq;
-          dkb[0][j][e] += xk;
-          dG[0][j][e] += qn * xq + kb * xk;
+        for (int hf = 0; hf < 2; ++hf) {
+          const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
+          const float2 G2 = ld2<float>(sG + r * LDG + c0);
+          const float2 Gb2 = ld2<float>(sG + (16 * I) * LDG + c0);
+          const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
+          const float2 b2 = ld2<T>(sb + r * LDK + c0);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int e = 2 * hf + t;
+            const float f = fast_exp2(sel2(G2, t) - sel2(Gb2, t));
+            const float xq = scale * tq[0][j][e] * f, xk = tk[0][j][e] * f;
+            const float qn = sel2(q2, t) * rq[r];
+            const float kb = sel2(b2, t) * sel2(k2, t) * rk[r];
+            dq[0][j][e] += xq;
+            dkb[0][j][e] += xk;
+            dG[0][j][e] += qn * xq + kb * xk;
+          }
         }
     }
     // Y products: columns of block J = wr, from block rows I >= J; the key
@@ -441,21 +472,28 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
                                        sKBs + 16 * I * LDK, LDK, wc * DQ, 16);
       const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
 #pragma unroll
-      for (int j = 0; j < NTO; ++j)
+      for (int j = 0; j < NTO; ++j) {
+        const float2 F2 = ld2<float>(FIJ + wc * DQ + 8 * j + 2 * tig);
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          ys[j][e] += FIJ[wc * DQ + 8 * j + 2 * tig + (e & 1)] * ty[0][j][e];
+        for (int e = 0; e < 4; ++e) ys[j][e] += sel2(F2, e & 1) * ty[0][j][e];
+      }
     }
 #pragma unroll
     for (int j = 0; j < NTO; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
-        const float fe = fast_exp2(sG[(16 * J + 15) * LDG + cl] - sG[r * LDG + cl]);
-        const float y = ys[j][e] * fe;
-        const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
-        dkn[0][j][e] += y;
-        dG[0][j][e] -= kn * y;
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
+        const float2 Ge2 = ld2<float>(sG + (16 * J + 15) * LDG + c0);
+        const float2 G2 = ld2<float>(sG + r * LDG + c0);
+        const float2 k2 = ld2<T>(sk + r * LDK + c0);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int e = 2 * hf + t;
+          const float y = ys[j][e] * fast_exp2(sel2(Ge2, t) - sel2(G2, t));
+          const float kn = sel2(k2, t) * rk[r];
+          dkn[0][j][e] += y;
+          dG[0][j][e] -= kn * y;
+        }
       }
     if (!safe) {
       // exact diagonal block, off-diagonal pairs only
@@ -498,12 +536,17 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
 #pragma unroll
   for (int j = 0; j < NTO; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = 16 * wr + gid + ((e >> 1) << 3), cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
-      float v = dG[0][j][e];
-      if (r == len - 1) v += dgl[cl] * exp2f(sG[(kChunk - 1) * LDG + cl]);
-      sdG[r * LDG + cl] = v;
-      if (r + 1 < kChunk) sX[(r + 1) * LDG + cl] = X[j][e];
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
+      float2 v = make_float2(dG[0][j][2 * hf], dG[0][j][2 * hf + 1]);
+      if (r == len - 1) {
+        v.x += dgl[c0] * exp2f(sG[(kChunk - 1) * LDG + c0]);
+        v.y += dgl[c0 + 1] * exp2f(sG[(kChunk - 1) * LDG + c0 + 1]);
+      }
+      *reinterpret_cast<float2*>(sdG + r * LDG + c0) = v;
+      if (r + 1 < kChunk)
+        *reinterpret_cast<float2*>(sX + (r + 1) * LDG + c0) =
+            make_float2(X[j][2 * hf], X[j][2 * hf + 1]);
     }
   for (int i = tid; i < D; i += NTH) sX[i] = 0.f;
   __syncthreads();
@@ -575,19 +618,24 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
 #pragma unroll
   for (int j = 0; j < NTO; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int hf = e >> 1;
-      const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig + (e & 1);
-      const float qn = to_f<T>(sq[r * LDK + cl]) * rq[r];
-      const float kn = to_f<T>(sk[r * LDK + cl]) * rk[r];
-      const float bb = to_f<T>(sb[r * LDK + cl]);
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
+      const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
+      const float2 b2 = ld2<T>(sb + r * LDK + c0);
       const float dgn = scale * sDiag[r];
-      const float dkbv = dkb[0][j][e];
-      dq[0][j][e] += dgn * kn;
-      dkn[0][j][e] += dkbv * bb + dgn * qn;
-      dkb[0][j][e] = dkbv * kn;  // db
-      pq[hf] += qn * dq[0][j][e];
-      pk[hf] += kn * dkn[0][j][e];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int e = 2 * hf + t;
+        const float qn = sel2(q2, t) * rq[r];
+        const float kn = sel2(k2, t) * rk[r];
+        const float bb = sel2(b2, t);
+        const float dkbv = dkb[0][j][e];
+        dq[0][j][e] += dgn * kn;
+        dkn[0][j][e] += dkbv * bb + dgn * qn;
+        dkb[0][j][e] = dkbv * kn;  // db
+        pq[hf] += qn * dq[0][j][e];
+        pk[hf] += kn * dkn[0][j][e];
+      }
     }
   if (a.l2norm) {
 #pragma unroll
@@ -611,6 +659,15 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     for (int i = 0; i < NTH / 32; ++i) sA += sDApart[i];
     atomicAdd(a.gate.dA_log + h, sA);
   }
+  float dotq[2] = {0.f, 0.f}, dotk[2] = {0.f, 0.f};
+  if (a.l2norm) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = 16 * wr + gid + 8 * hf;
+      dotq[hf] = pdq[r] + pdq[64 + r] + pdq[128 + r] + pdq[192 + r];
+      dotk[hf] = pdk[r] + pdk[64 + r] + pdk[128 + r] + pdk[192 + r];
+    }
+  }
 #pragma unroll
   for (int j = 0; j < NTO; ++j)
 #pragma unroll
@@ -618,17 +675,14 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
       const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
       if (r >= len || cl >= K) continue;
       float oq[2], ok[2];
-      const float dotq = a.l2norm ? pdq[r] + pdq[64 + r] + pdq[128 + r] + pdq[192 + r] : 0.f;
-      const float dotk = a.l2norm ? pdk[r] + pdk[64 + r] + pdk[128 + r] + pdk[192 + r] : 0.f;
+      const float2 q2 = ld2<T>(sq + r * LDK + cl), k2 = ld2<T>(sk + r * LDK + cl);
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         const int e = 2 * hf + t;
         float vq = dq[0][j][e], vk = dkn[0][j][e];
         if (a.l2norm) {
-          const float qn = to_f<T>(sq[r * LDK + cl + t]) * rq[r];
-          const float kn = to_f<T>(sk[r * LDK + cl + t]) * rk[r];
-          vq = (vq - qn * dotq) * rq[r];
-          vk = (vk - kn * dotk) * rk[r];
+          vq = (vq - sel2(q2, t) * rq[r] * dotq[hf]) * rq[r];
+          vk = (vk - sel2(k2, t) * rk[r] * dotk[hf]) * rk[r];
         }
         oq[t] = vq;
         ok[t] = vk;

@@ -116,6 +116,20 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float x, float y) 
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Two adjacent elements (the first 4- or 8-byte aligned) as floats: one
+// shared-memory access instead of two.
+template <typename T> __device__ __forceinline__ float2 ld2(const T* p);
+template <> __device__ __forceinline__ float2 ld2<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+template <> __device__ __forceinline__ float2 ld2<__half>(const __half* p) {
+  return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
+template <> __device__ __forceinline__ float2 ld2<float>(const float* p) {
+  return *reinterpret_cast<const float2*>(p);
+}
+__device__ __forceinline__ float sel2(const float2& v, int t) { return t ? v.y : v.x; }
+
 // ---------------------------------------------------------------------------
 // cp.async
 // ---------------------------------------------------------------------------
