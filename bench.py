@@ -503,7 +503,7 @@ def run_config4(args, world, rank, local, mode):
     }), flush=True)
 
 
-def run_decode(dev, lib, N):
+def run_decode(dev, lib, N, steps=DEC_STEPS, warm=16):
     """Config 2: one in-place recurrent step over B=256 sequences per call."""
     gen = torch.Generator(device=dev).manual_seed(7)
     bf = torch.bfloat16
@@ -530,23 +530,23 @@ def run_decode(dev, lib, N):
         N.check(lib.gdn2_recurrent_fwd(prob, *p[:6], N.ptr(state), p[6], N.ptr(state), st),
                 "decode")
 
-    for i in range(16):
+    for i in range(warm):
         one(i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(DEC_STEPS):
+    for i in range(steps):
         one(i)
     e1.record(stream)
     torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / DEC_STEPS
+    us = e0.elapsed_time(e1) * 1e3 / steps
     nbytes = 2 * DEC_B * H * K * V * 4
     hbm, _, kind = peaks()
     gbs = nbytes / (us / 1e6) / 1e9
     return {"workload": "config2: B=256 H=16 K=V=128 fp32 state, in-place step, bf16 inputs",
-            "steps": DEC_STEPS, "us_per_step": round(us, 2), "GBps": round(gbs, 1),
+            "steps": steps, "us_per_step": round(us, 2), "GBps": round(gbs, 1),
             "frac": round(gbs / hbm, 4), "state_bytes_per_step": nbytes,
-            "peak_source": kind, "gpu_launches": DEC_STEPS}
+            "peak_source": kind, "gpu_launches": steps}
 
 
 def run_block_ops(dev, lib, N, iters=20, warm=3):
@@ -702,10 +702,11 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--workload", choices=("config1", "sp", "heads", "block"), default="config1",
-                    help="config1 (headline), config 4 sequence-parallel / head-sharded, or "
+    ap.add_argument("--workload", choices=("config1", "sp", "heads", "block", "decode"),
+                    default="config1",
+                    help="config1 (headline), config 4 sequence-parallel / head-sharded, "
                          "block: only the prologue / epilogue kernels (--steps timed launches "
-                         "each after --warmup, one GPU)")
+                         "each after --warmup, one GPU), or decode: only the config-2 step")
     ap.add_argument("--profile", action="store_true",
                     help="small ncu case: config-1 phases at --batch, nothing else")
     ap.add_argument("--batch", type=int, default=2, help="batch of the --profile case")
@@ -720,6 +721,14 @@ def main(argv=None):
         torch.cuda.set_device(dev)
         blk = run_block_ops(dev, N.load(), N, iters=args.steps, warm=args.warmup)
         print(json.dumps({"workload": "block", "block_ops": blk}), flush=True)
+        return
+    if args.workload == "decode":
+        from qwendopamine_b200 import _native as N
+
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        dec = run_decode(dev, N.load(), N, steps=args.steps, warm=args.warmup)
+        print(json.dumps({"workload": "decode", "decode": dec}), flush=True)
         return
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3

@@ -272,8 +272,8 @@ struct RecStreamSmem {
   static constexpr uint32_t oState = 0;
   static constexpr uint32_t oRaw = NBUF * state;
   static constexpr uint32_t oF = oRaw + NBUF * raw;                // sq sk sg sb sv sw floats
-  static constexpr uint32_t oRed = oF + 6 * D * 4;                 // red[RG][D]
-  static constexpr uint32_t oUnit = oRed + RG * D * 4;             // RecUnit[NBUF]
+  static constexpr uint32_t oRed = oF + 6 * D * 4;                 // red[2][RG][D]
+  static constexpr uint32_t oUnit = oRed + 2 * RG * D * 4;         // RecUnit[NBUF]
   static constexpr uint32_t oBar = oUnit + NBUF * sizeof(RecUnit);  // mbarrier[NBUF]
   static constexpr uint32_t oNorm = oBar + 8 * NBUF;
   static constexpr uint32_t bytes = oNorm + 16 + 128;
@@ -291,10 +291,12 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
   float* sb = sg + D;
   float* sv = sb + D;
   float* sw = sv + D;
-  float(*red)[D] = reinterpret_cast<float(*)[D]>(sm + S_::oRed);
+  // column partial sums over the row groups: red0 for the erase-read, red1
+  // for the read-out, so one barrier per reduction is enough
+  float(*red0)[D] = reinterpret_cast<float(*)[D]>(sm + S_::oRed);
+  float(*red1)[D] = red0 + RG;
   RecUnit* sUnit = reinterpret_cast<RecUnit*>(sm + S_::oUnit);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + S_::oBar);
-  float* snorm = reinterpret_cast<float*>(sm + S_::oNorm);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = a.H, HV = a.HV;
@@ -372,6 +374,7 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
     for (int64_t t = 0; t < ui.Tn; ++t) {
       const int64_t row = ui.bos + t;
       const int64_t oq = (row * H + ui.hq) * D, og = (row * HV + ui.hv) * D;
+      if (t > 0) __syncthreads();  // the previous token's read-out is done with sq .. sw, red1
       if (t == 0) {
         const unsigned char* r = raw_q(buf);
         for (int idx = tid; idx < D; idx += NTH) {
@@ -394,18 +397,19 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
         }
       }
       __syncthreads();
-      if (warp < 2) {
-        const float* x = warp == 0 ? sq : sk;
-        float s = 0.f;
-        for (int idx = lane; idx < D; idx += 32) s += x[idx] * x[idx];
-        s = warp_sum(s);
-        if (lane == 0) {
-          const float inv = a.l2norm ? rsqrtf(s + kNormEps) : 1.f;
-          snorm[warp] = warp == 0 ? inv * a.scale : inv;
+      // every warp forms the q and k norms itself (no barrier)
+      float nq, nk;
+      {
+        float s1 = 0.f, s2 = 0.f;
+        for (int idx = lane; idx < D; idx += 32) {
+          s1 += sq[idx] * sq[idx];
+          s2 += sk[idx] * sk[idx];
         }
+        s1 = warp_sum(s1);
+        s2 = warp_sum(s2);
+        nq = (a.l2norm ? rsqrtf(s1 + kNormEps) : 1.f) * a.scale;
+        nk = a.l2norm ? rsqrtf(s2 + kNormEps) : 1.f;
       }
-      __syncthreads();
-      const float nq = snorm[0], nk = snorm[1];
       // decay, then erase-read r = S^T (b*k)
       float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -419,17 +423,16 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
         }
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) red[rg][col0 + j] = part[j];
+      for (int j = 0; j < 4; ++j) red0[rg][col0 + j] = part[j];
       __syncthreads();
       float dlt[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         float s = 0.f;
 #pragma unroll
-        for (int x = 0; x < RG; ++x) s += red[x][col0 + j];
+        for (int x = 0; x < RG; ++x) s += red0[x][col0 + j];
         dlt[j] = sw[col0 + j] * sv[col0 + j] - s;
       }
-      __syncthreads();
       // rank-1 write and read-out
 #pragma unroll
       for (int j = 0; j < 4; ++j) part[j] = 0.f;
@@ -444,15 +447,16 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_stream(RecArgs a) {
         }
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) red[rg][col0 + j] = part[j];
+      for (int j = 0; j < 4; ++j) red1[rg][col0 + j] = part[j];
       __syncthreads();
       for (int idx = tid; idx < D; idx += NTH) {
         float s = 0.f;
 #pragma unroll
-        for (int x = 0; x < RG; ++x) s += red[x][idx];
+        for (int x = 0; x < RG; ++x) s += red1[x][idx];
         o[og + idx] = from_f<T>(s);
       }
-      __syncthreads();
+      // (the next token's first barrier, or the next unit's, orders these
+      // reads of red1 and sq .. sw before they are overwritten)
       if (ui.tok_idx && a.ht) {  // the state after token t goes to its own slot
         const int64_t slot = ui.tok_idx[t];
         if (slot >= 0) {
