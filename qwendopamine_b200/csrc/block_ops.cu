@@ -176,13 +176,38 @@ constexpr int kFwdCPT = 4;
 constexpr int kBwdCPT = 4;
 constexpr int kConvChannels = 256 * 4;  // channels per CTA (256 threads x 4)
 
+// Channel pairs: the per-channel FMAs run as packed fp32x2 operations
+// (__ffma2_rn and friends: two fp32 FMAs per instruction with the same
+// rounding as fmaf, so the results equal the one-channel-at-a-time form).
+template <int W, int CPT>
+__device__ __forceinline__ void load_weight_pairs(const ConvArgs& a, int d0,
+                                                  float2 (&wt)[W][CPT / 2], float2 (&bs)[CPT / 2]) {
+  float w1[W][CPT], b1[CPT];
+  load_weights<W, CPT>(a, d0, w1, b1);
+#pragma unroll
+  for (int p = 0; p < CPT / 2; ++p) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) wt[j][p] = make_float2(w1[j][2 * p], w1[j][2 * p + 1]);
+    bs[p] = make_float2(b1[2 * p], b1[2 * p + 1]);
+  }
+}
+
+template <typename T, int W, int CPT>
+__device__ __forceinline__ void load_row_pairs(const ConvArgs& a, const T* xb, int b, int d0,
+                                               int r, float2 (&f2)[CPT / 2]) {
+  float f[CPT];
+  load_row<T, W, CPT>(a, xb, b, d0, r, f);
+#pragma unroll
+  for (int p = 0; p < CPT / 2; ++p) f2[p] = make_float2(f[2 * p], f[2 * p + 1]);
+}
+
 // y = act(round(bias + sum_j w_j x_{t-W+1+j})): grid (D/1024, T/64, B); a
 // CTA walks a 64-token strip of 1024 contiguous channels (every row access of
 // the CTA is 2 KB contiguous), each thread 4 channels, with the W-1 previous
 // rows carried in registers.
 template <typename T, int W, int ACT>
 __global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
-  constexpr int CPT = kFwdCPT;
+  constexpr int CPT = kFwdCPT, CP = CPT / 2;
   constexpr int R = 4;  // rows loaded per run
   constexpr int WP = W > 1 ? W - 1 : 1;
   const int d0 = (blockIdx.x * 256 + threadIdx.x) * CPT;
@@ -190,13 +215,14 @@ __global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
   const int tb = blockIdx.y * kConvStrip;
   if (d0 >= a.D) return;
   const int te = min(tb + kConvStrip, a.T);
-  float wt[W][CPT], bs[CPT];
-  load_weights<W, CPT>(a, d0, wt, bs);
+  float2 wt[W][CP], bs[CP];
+  load_weight_pairs<W, CPT>(a, d0, wt, bs);
   const T* xb = reinterpret_cast<const T*>(a.x) + (int64_t)b * a.T * a.D + d0;
   T* yb = reinterpret_cast<T*>(a.y) + (int64_t)b * a.T * a.D + d0;
-  float win[WP][CPT];
+  float2 win[WP][CP];
 #pragma unroll
-  for (int i = 0; i < W - 1; ++i) load_row<T, W, CPT>(a, xb, b, d0, tb - (W - 1) + i, win[i]);
+  for (int i = 0; i < W - 1; ++i)
+    load_row_pairs<T, W, CPT>(a, xb, b, d0, tb - (W - 1) + i, win[i]);
   for (int t0 = tb; t0 < te; t0 += R) {
     Pack<T, CPT> raw[R];
 #pragma unroll
@@ -210,32 +236,32 @@ __global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
       float cur[CPT], o[CPT];
       unpackv<T, CPT>(raw[r], cur);
 #pragma unroll
-      for (int i = 0; i < CPT; ++i) {
-        float acc = bs[i];
+      for (int p = 0; p < CP; ++p) {
+        const float2 c2 = make_float2(cur[2 * p], cur[2 * p + 1]);
+        float2 acc = bs[p];
 #pragma unroll
-        for (int j = 0; j < W - 1; ++j) acc = fmaf(wt[j][i], win[j][i], acc);
-        acc = fmaf(wt[W - 1][i], cur[i], acc);
-        const float c = rnd<T>(acc);
-        o[i] = ACT ? silu_f(c) : c;
+        for (int j = 0; j < W - 1; ++j) acc = __ffma2_rn(wt[j][p], win[j][p], acc);
+        acc = __ffma2_rn(wt[W - 1][p], c2, acc);
+        const float c0 = rnd<T>(acc.x), c1 = rnd<T>(acc.y);
+        o[2 * p] = ACT ? silu_f(c0) : c0;
+        o[2 * p + 1] = ACT ? silu_f(c1) : c1;
+#pragma unroll
+        for (int j = 0; j + 1 < W - 1; ++j) win[j][p] = win[j + 1][p];
+        if (W > 1) win[WP - 1][p] = c2;
       }
       stv<T, CPT>(yb + (int64_t)(t0 + r) * a.D, o);
-#pragma unroll
-      for (int j = 0; j + 1 < W - 1; ++j)
-#pragma unroll
-        for (int i = 0; i < CPT; ++i) win[j][i] = win[j + 1][i];
-      if (W > 1) {
-#pragma unroll
-        for (int i = 0; i < CPT; ++i) win[WP - 1][i] = cur[i];
-      }
     }
   }
   // the strip holding the last row leaves rows T-W+1 .. T-1 in its window
   if (a.new_state && te == a.T && W > 1) {
     T* ns = reinterpret_cast<T*>(a.new_state) + ((int64_t)b * a.D + d0) * (W - 1);
 #pragma unroll
-    for (int i = 0; i < CPT; ++i)
+    for (int p = 0; p < CP; ++p)
 #pragma unroll
-      for (int j = 0; j < W - 1; ++j) ns[i * (W - 1) + j] = from_f<T>(win[j][i]);
+      for (int j = 0; j < W - 1; ++j) {
+        ns[(2 * p) * (W - 1) + j] = from_f<T>(win[j][p].x);
+        ns[(2 * p + 1) * (W - 1) + j] = from_f<T>(win[j][p].y);
+      }
   }
 }
 
@@ -248,30 +274,30 @@ __global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
 // strips in a fixed order by k_col_sum.
 template <typename T, int W, int ACT>
 __global__ void __launch_bounds__(256, 2) k_conv_bwd(ConvArgs a) {
-  constexpr int CPT = kBwdCPT;
+  constexpr int CPT = kBwdCPT, CP = CPT / 2;
   constexpr int R = 4;
   constexpr int WP = W > 1 ? W - 1 : 1;
   const int d0 = (blockIdx.x * 256 + threadIdx.x) * CPT;
   const int b = blockIdx.z;
   const int tb = blockIdx.y * kConvStrip;
   if (d0 >= a.D) return;
-  float dwp[W + 1][CPT];
+  float2 dwp[W + 1][CP];
 #pragma unroll
   for (int j = 0; j <= W; ++j)
 #pragma unroll
-    for (int i = 0; i < CPT; ++i) dwp[j][i] = 0.f;
+    for (int p = 0; p < CP; ++p) dwp[j][p] = make_float2(0.f, 0.f);
   const int te = min(tb + kConvStrip, a.T);
-  float wt[W][CPT], bs[CPT];
-  load_weights<W, CPT>(a, d0, wt, bs);
+  float2 wt[W][CP], bs[CP];
+  load_weight_pairs<W, CPT>(a, d0, wt, bs);
   const T* xb = reinterpret_cast<const T*>(a.x) + (int64_t)b * a.T * a.D + d0;
   const T* dyb = reinterpret_cast<const T*>(a.dy) + (int64_t)b * a.T * a.D + d0;
   T* dxb = reinterpret_cast<T*>(a.dx) + (int64_t)b * a.T * a.D + d0;
-  float win[WP][CPT], dcw[WP][CPT];  // previous W-1 input rows and dc values
+  float2 win[WP][CP], dcw[WP][CP];  // previous W-1 input rows and dc values
 #pragma unroll
   for (int i = 0; i < W - 1; ++i) {
-    load_row<T, W, CPT>(a, xb, b, d0, tb - (W - 1) + i, win[i]);
+    load_row_pairs<T, W, CPT>(a, xb, b, d0, tb - (W - 1) + i, win[i]);
 #pragma unroll
-    for (int e = 0; e < CPT; ++e) dcw[i][e] = 0.f;
+    for (int p = 0; p < CP; ++p) dcw[i][p] = make_float2(0.f, 0.f);
   }
   const int send = te + W - 1;
   const bool want_dprefix = a.dprefix && tb == 0;
@@ -292,65 +318,52 @@ __global__ void __launch_bounds__(256, 2) k_conv_bwd(ConvArgs a) {
     for (int r = 0; r < R; ++r) {
       const int s = s0 + r;
       if (s >= send) continue;  // (predicated: the loop stays unrolled)
-      float cur[CPT], dc[CPT];
+      float cur[CPT], dy[CPT], o[CPT];
       unpackv<T, CPT>(rx[r], cur);
-      unpackv<T, CPT>(rdy[r], dc);
-      if (s < a.T) {
-        if (ACT) {
+      unpackv<T, CPT>(rdy[r], dy);
+      const int t = s - (W - 1);  // the input row emitted at this step
 #pragma unroll
-          for (int i = 0; i < CPT; ++i) {
-            float acc = bs[i];
+      for (int p = 0; p < CP; ++p) {
+        const float2 c2 = make_float2(cur[2 * p], cur[2 * p + 1]);
+        float2 dc = make_float2(0.f, 0.f);
+        if (s < a.T) {
+          dc = make_float2(dy[2 * p], dy[2 * p + 1]);
+          if (ACT) {
+            float2 acc = bs[p];
 #pragma unroll
-            for (int j = 0; j < W - 1; ++j) acc = fmaf(wt[j][i], win[j][i], acc);
-            acc = fmaf(wt[W - 1][i], cur[i], acc);
-            dc[i] = rnd<T>(silu_bwd_f(dc[i], rnd<T>(acc)));
+            for (int j = 0; j < W - 1; ++j) acc = __ffma2_rn(wt[j][p], win[j][p], acc);
+            acc = __ffma2_rn(wt[W - 1][p], c2, acc);
+            dc.x = rnd<T>(silu_bwd_f(dc.x, rnd<T>(acc.x)));
+            dc.y = rnd<T>(silu_bwd_f(dc.y, rnd<T>(acc.y)));
+          }
+          if (s < te) {
+#pragma unroll
+            for (int j = 0; j < W - 1; ++j) dwp[j][p] = __ffma2_rn(dc, win[j][p], dwp[j][p]);
+            dwp[W - 1][p] = __ffma2_rn(dc, c2, dwp[W - 1][p]);
+            dwp[W][p] = __fadd2_rn(dwp[W][p], dc);
           }
         }
-        if (s < te) {
+        float2 acc = __fmul2_rn(wt[0][p], dc);
 #pragma unroll
-          for (int i = 0; i < CPT; ++i) {
+        for (int j = 1; j < W; ++j) acc = __ffma2_rn(wt[j][p], dcw[W - 1 - j][p], acc);
+        o[2 * p] = acc.x;
+        o[2 * p + 1] = acc.y;
 #pragma unroll
-            for (int j = 0; j < W - 1; ++j) dwp[j][i] = fmaf(dc[i], win[j][i], dwp[j][i]);
-            dwp[W - 1][i] = fmaf(dc[i], cur[i], dwp[W - 1][i]);
-            dwp[W][i] += dc[i];
-          }
+        for (int j = 0; j + 1 < W - 1; ++j) {
+          win[j][p] = win[j + 1][p];
+          dcw[j][p] = dcw[j + 1][p];
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < CPT; ++i) dc[i] = 0.f;
-      }
-      // emit input row t = s - W + 1
-      const int t = s - (W - 1);
-      if (t >= tb || (want_dprefix && t >= -(W - 1))) {
-        float o[CPT];
-#pragma unroll
-        for (int i = 0; i < CPT; ++i) {
-          float acc = wt[0][i] * dc[i];
-#pragma unroll
-          for (int j = 1; j < W; ++j) acc = fmaf(wt[j][i], dcw[W - 1 - j][i], acc);
-          o[i] = acc;
-        }
-        if (t >= tb) {
-          if (t < te) stv<T, CPT>(dxb + (int64_t)t * a.D, o);
-        } else {
-          float* dp = a.dprefix + ((int64_t)b * (W - 1) + (t + W - 1)) * a.D + d0;
-#pragma unroll
-          for (int i = 0; i < CPT; ++i) dp[i] = o[i];
+        if (W > 1) {
+          win[WP - 1][p] = c2;
+          dcw[WP - 1][p] = dc;
         }
       }
+      if (t >= tb) {
+        if (t < te) stv<T, CPT>(dxb + (int64_t)t * a.D, o);
+      } else if (want_dprefix && t >= -(W - 1)) {
+        float* dp = a.dprefix + ((int64_t)b * (W - 1) + (t + W - 1)) * a.D + d0;
 #pragma unroll
-      for (int j = 0; j + 1 < W - 1; ++j)
-#pragma unroll
-        for (int i = 0; i < CPT; ++i) {
-          win[j][i] = win[j + 1][i];
-          dcw[j][i] = dcw[j + 1][i];
-        }
-      if (W > 1) {
-#pragma unroll
-        for (int i = 0; i < CPT; ++i) {
-          win[WP - 1][i] = cur[i];
-          dcw[WP - 1][i] = dc[i];
-        }
+        for (int i = 0; i < CPT; ++i) dp[i] = o[i];
       }
     }
   }
@@ -359,7 +372,10 @@ __global__ void __launch_bounds__(256, 2) k_conv_bwd(ConvArgs a) {
   for (int j = 0; j <= W; ++j) {
     float* pp = a.part + ((int64_t)blk * (W + 1) + j) * a.D + d0;
 #pragma unroll
-    for (int i = 0; i < CPT; ++i) pp[i] = dwp[j][i];
+    for (int p = 0; p < CP; ++p) {
+      pp[2 * p] = dwp[j][p].x;
+      pp[2 * p + 1] = dwp[j][p].y;
+    }
   }
 }
 
