@@ -79,6 +79,12 @@ PHASE_FLOPS = {
     "bwd_state": 6 * K * V + 2 * C * V,
     "bwd_intra": 6 * K * V + 6 * C * V + 12 * C * K + 4 * C * C,
 }
+# The metric's "% TC peak": the reference schedule's fwd+bwd FLOPs per
+# token-head, 20CK + 14CV + 22KV + 4C^2 = 655,360, over the step time, against
+# the measured bf16 peak and against the HBM-limited ceiling min(peak, AI x
+# HBM GB/s) with AI = 655,360 / 6,900 minimum bytes per token-head.
+STEP_FLOPS = 20 * C * K + 14 * C * V + 22 * K * V + 4 * C * C
+STEP_MIN_BYTES = 6900
 # DRAM traffic (read + write) of the dominant kernel, k_bwd_intra16, per
 # token-head, from one ncu --set full capture at batch 2 (701.3 MB over
 # 131,072 token-heads; traffic grows with token-heads, so it scales to a
@@ -389,6 +395,7 @@ def run_b200(args, world, rank, local):
                      "bytes_per_token_head": PHASE_BYTES[dom]},
         "phases": phase_info,
         "tensor_peak_tflops": tflops_peak,
+        "tc_peak": tc_peak_line(th * world, ms_step, tflops_peak, hbm),
         "decode": dec,
         "block_ops": blk,
         "clocks": clocks,
@@ -501,6 +508,15 @@ def run_config4(args, world, rank, local, mode):
                                    if mode == "sp" else f"head-sharded x{world}, no collective")},
         "gpu_launches": launches * args.steps,
     }), flush=True)
+
+
+def tc_peak_line(token_heads, ms, peak_tflops, hbm_gbs):
+    """Whole-step tensor-core fraction as the metric names it."""
+    tf = STEP_FLOPS * token_heads / (ms / 1e3) / 1e12
+    ceiling = min(peak_tflops, STEP_FLOPS / STEP_MIN_BYTES * hbm_gbs / 1e3)
+    return {"flops_per_token_head": STEP_FLOPS, "tflops": round(tf, 1),
+            "frac_of_bf16_peak": round(tf / peak_tflops, 4),
+            "hbm_ceiling_tflops": round(ceiling, 1), "frac_of_ceiling": round(tf / ceiling, 4)}
 
 
 def run_decode(dev, lib, N, steps=DEC_STEPS, warm=16):
