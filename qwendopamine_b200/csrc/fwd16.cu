@@ -474,7 +474,9 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
     if (tid == 0 && next < n_items) issue_qkbg(next, (int)nxt.row0);  // q, k, b, g are dead
 
     // ---- A = (I + Akk)^-1 ----------------------------------------------------------
-    unit_lower_inverse_mma<LDF>(sAkk, sInv, reinterpret_cast<float*>(R + L::rT));
+    // (single-term TF32 products: A is stored in bf16 and feeds bf16 products,
+    // and the reference's solve uses TF32 products here as well)
+    unit_lower_inverse_mma<LDF, 1>(sAkk, sInv, reinterpret_cast<float*>(R + L::rT));
     T* gA = reinterpret_cast<T*>(a.saved + a.L.a) + ch * kChunk * kChunk;
     for (int i = tid; i < kChunk * 32; i += NTH) {
       const int r = i >> 5, cc = (i & 31) * 2;

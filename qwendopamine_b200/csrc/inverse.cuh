@@ -50,13 +50,16 @@ __device__ void unit_lower_inverse(const float* sL, float* sInv, float* sTmp) {
   }
 }
 
-// acc (16 x 16) = A (16 x KD) B (KD x 16) on the tensor cores with the
-// 3-term TF32 split (hi*hi + hi*lo + lo*hi, about fp32 accuracy); the three
-// accumulator chains run independently.  A(m,k) = A[m*lda + k],
-// B(k,n) = B[k*ldb + n] (fp32 shared memory).
-template <int KD>
+// acc (16 x 16) = A (16 x KD) B (KD x 16) on the tensor cores, TERMS = 3:
+// the 3-term TF32 split (hi*hi + hi*lo + lo*hi, about fp32 accuracy; the
+// three accumulator chains run independently); TERMS = 1: plain TF32
+// operands, fp32 accumulation (the precision the reference's solve_tril
+// products use on GPUs of this class, chunk_gdn2.py:464).
+// A(m,k) = A[m*lda + k], B(k,n) = B[k*ldb + n] (fp32 shared memory).
+template <int KD, int TERMS = 3>
 __device__ __forceinline__ void mma16x16_tf32x3(float (&acc)[1][2][4], const float* A, int lda,
                                                 const float* B, int ldb) {
+  static_assert(TERMS == 1 || TERMS == 3, "TF32 terms");
   const int lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
   float hh[2][4], lh[2][4], hl[2][4];
@@ -82,8 +85,10 @@ __device__ __forceinline__ void mma16x16_tf32x3(float (&acc)[1][2][4], const flo
       const uint32_t bl0 = tf32_bits(y0 - __uint_as_float(bh0));
       const uint32_t bl1 = tf32_bits(y1 - __uint_as_float(bh1));
       mma_tf32(hh[j], ah, bh0, bh1);
-      mma_tf32(lh[j], al, bh0, bh1);
-      mma_tf32(hl[j], ah, bl0, bl1);
+      if (TERMS == 3) {
+        mma_tf32(lh[j], al, bh0, bh1);
+        mma_tf32(hl[j], ah, bl0, bl1);
+      }
     }
   }
 #pragma unroll
@@ -94,18 +99,18 @@ __device__ __forceinline__ void mma16x16_tf32x3(float (&acc)[1][2][4], const flo
 
 // Blocks at distance d = I - J of the inverse, one warp per block:
 //   T = sum_{M=J}^{I-1} L_IM Inv_MJ,   Inv_IJ = -Inv_II T.
-template <int LDC, int DIST>
+template <int LDC, int DIST, int TERMS>
 __device__ __forceinline__ void inverse_level(const float* sL, float* sInv, float* sT) {
   const int warp = threadIdx.x >> 5;
   if (warp < 4 - DIST) {
     const int J = warp, I = warp + DIST;
     float* t = sT + warp * (16 * 20);
     float acc[1][2][4];
-    mma16x16_tf32x3<16 * DIST>(acc, sL + 16 * I * LDC + 16 * J, LDC, sInv + 16 * J * LDC + 16 * J,
-                               LDC);
+    mma16x16_tf32x3<16 * DIST, TERMS>(acc, sL + 16 * I * LDC + 16 * J, LDC,
+                                      sInv + 16 * J * LDC + 16 * J, LDC);
     acc_foreach(acc, [&](int r, int c, float v) { t[r * 20 + c] = v; });
     __syncwarp();
-    mma16x16_tf32x3<16>(acc, sInv + 16 * I * LDC + 16 * I, LDC, t, 20);
+    mma16x16_tf32x3<16, TERMS>(acc, sInv + 16 * I * LDC + 16 * I, LDC, t, 20);
     acc_foreach(acc, [&](int r, int c, float v) { sInv[(16 * I + r) * LDC + 16 * J + c] = -v; });
   }
 }
@@ -115,9 +120,9 @@ __device__ __forceinline__ void inverse_level(const float* sL, float* sInv, floa
 // written; callers treat them as zero).  The diagonal 16x16 blocks are
 // solved right-looking in registers (lane j of warp I holds column j of
 // Inv_II, so the dependent chain is one FMA per row); the off-diagonal blocks
-// follow by distance with 3-term TF32 tensor-core products (inverse_level).
-// sT holds 3 [16][20] fp32 tiles.
-template <int LDC>
+// follow by distance with TF32 tensor-core products (inverse_level; TERMS as
+// for mma16x16_tf32x3).  sT holds 3 [16][20] fp32 tiles.
+template <int LDC, int TERMS = 3>
 __device__ void unit_lower_inverse_mma(const float* sL, float* sInv, float* sT) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp < 4 && lane < 16) {
@@ -134,11 +139,11 @@ __device__ void unit_lower_inverse_mma(const float* sL, float* sInv, float* sT) 
     for (int r = 0; r < 16; ++r) sInv[(o + r) * LDC + o + j] = x[r];
   }
   __syncthreads();
-  inverse_level<LDC, 1>(sL, sInv, sT);
+  inverse_level<LDC, 1, TERMS>(sL, sInv, sT);
   __syncthreads();
-  inverse_level<LDC, 2>(sL, sInv, sT);
+  inverse_level<LDC, 2, TERMS>(sL, sInv, sT);
   __syncthreads();
-  inverse_level<LDC, 3>(sL, sInv, sT);
+  inverse_level<LDC, 3, TERMS>(sL, sInv, sT);
   __syncthreads();
 }
 
