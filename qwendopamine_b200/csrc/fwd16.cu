@@ -15,7 +15,7 @@
 // carries exactly 2^(G_r - G_i).  The scores, W = A E and U = A Z are
 // mma.sync m16n8k16 products from ldmatrix fragments; the unit-lower inverse
 // A = (I+Akk)^-1 stays in fp32 (register substitution for the diagonal
-// blocks, 3-pass TF32 products for the rest).  Diagonal blocks whose 16-row
+// blocks, TF32 products for the rest, as the reference's solve does).  Diagonal blocks whose 16-row
 // decay range exceeds the fp32 exponent budget are recomputed elementwise.
 #include "chunk_args.cuh"
 #include "inverse.cuh"
@@ -196,8 +196,8 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
   // Items (chunk c, head h) = (item / H, item % H), strided over the grid.
   // Thread 0 requests each item's tiles as TMA boxes (3-D views [rows][H][D],
   // 64 rows x 128 bytes each) completing on an mbarrier: q, k, b, g of the
-  // next item once this item's scores are done (they are dead from there
-  // on), v, w once its W / U products are done.
+  // next item once this item's fused pass (or, with an exact diagonal block,
+  // its scores) is done with them, v, w once its W / U products are done.
   // (row0 of the item's chunk comes from the sequence tables, looked up one
   // item ahead so the dependent global loads stay off the critical path)
   auto issue_qkbg = [&](int item, int row0) {
@@ -413,7 +413,12 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
         *reinterpret_cast<uint32_t*>(sv + o16) = pack2<T>(z2[0], z2[1]);
       }
     }
+    tc::fence_async_smem();
     __syncthreads();
+    // With safe diagonal blocks nothing reads q, k, b, g after the fused pass,
+    // so the next item's copies start now (the exact diagonal path below
+    // still reads them: then they start after the scores).
+    if (safe && tid == 0 && next < n_items) issue_qkbg(next, (int)nxt.row0);
 
     // ---- score blocks: warp (I = wr, column block J = wc <= I) --------------------
     // key i of block J enters block row I as Kb[i] 2^(G_16I - G_(16J+15)), so
@@ -471,7 +476,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
     }
     tc::fence_async_smem();
     __syncthreads();
-    if (tid == 0 && next < n_items) issue_qkbg(next, (int)nxt.row0);  // q, k, b, g are dead
+    if (!safe && tid == 0 && next < n_items) issue_qkbg(next, (int)nxt.row0);  // now dead
 
     // ---- A = (I + Akk)^-1 ----------------------------------------------------------
     // (single-term TF32 products: A is stored in bf16 and feeds bf16 products,
