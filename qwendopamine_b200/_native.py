@@ -272,6 +272,27 @@ def _tables_from_lengths(lens, device) -> SeqTables:
     return SeqTables(mk(cu), mk(coff), mk(cseq), len(lens), len(cseq), cu[-1])
 
 
+def split_tables(B: int, T: int, S: int, device) -> SeqTables:
+    """Tables that cut each of B fixed-length sequences of T tokens into S
+    sub-spans of whole 64-token chunks (the last one takes the remainder),
+    listed sequence by sequence: the kernels treat them as B*S sequences.
+    The chunks, and so every per-chunk buffer, are the same as for B
+    sequences; only where the state passes start and stop changes."""
+    key = ("split", B, T, S, str(device))
+    tab = _table_cache.get(key)
+    if tab is None:
+        nch = (T + CHUNK - 1) // CHUNK
+        cuts = [CHUNK * (nch * j // S) for j in range(S)] + [T]
+        lens = [cuts[j + 1] - cuts[j] for j in range(S)]
+        if any(L <= 0 for L in lens):
+            raise ValueError(f"cannot cut {T} tokens into {S} chunk-aligned sub-spans")
+        tab = _tables_from_lengths(lens * B, device)
+        if len(_table_cache) > 64:
+            _table_cache.clear()
+        _table_cache[key] = tab
+    return tab
+
+
 def seq_tables(B: int, T: int, device, cu_seqlens=None, cu_seqlens_cpu=None) -> SeqTables:
     """Tables for fixed-length [B, T] input (cached) or packed cu_seqlens."""
     if cu_seqlens is None:

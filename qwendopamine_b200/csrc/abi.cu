@@ -153,11 +153,14 @@ cudaError_t launch_state16(const BwdStateArgs& a, cudaStream_t st) {
   return launch_bwd_state16<T, D, BV>(a, st);
 }
 
+// Column slices of 64 double the CTAs of a latency-bound pass; only worth it
+// while the doubled grid still fits one wave (a CTA walks all of its
+// sequence's chunks, so a second wave would start only after the first ends).
 template <typename T, typename Args>
 cudaError_t run_state16(const Args& a, int bucket, int cols, int n_seqs, int H, cudaStream_t st) {
   if (bucket == 64) return launch_state16<T, 64, 64>(a, st);
   const long ctas128 = (long)n_seqs * H * ((cols + 127) / 128);
-  if (ctas128 >= 148) return launch_state16<T, 128, 128>(a, st);
+  if (2 * ctas128 > 148) return launch_state16<T, 128, 128>(a, st);
   return launch_state16<T, 128, 64>(a, st);
 }
 

@@ -69,6 +69,71 @@ def _problem(H, K, V, dtype, l2norm, scale, tables):
                           tables.struct())
 
 
+def _sub_spans(B, T, H, dtype):
+    """Sub-spans per sequence inside a rank's span.  The pre-scans and state
+    passes walk their span's chunks one after another with one CTA (or a few
+    column slices) per sequence-head; cutting the span in two halves every
+    such chain and doubles the CTAs, which pays while the forward pre-scan
+    ([h | M], two 128-column slices per sequence-head) still fits one wave
+    and each half keeps enough chunks."""
+    if dtype != torch.bfloat16:
+        return 1
+    nch = (T + N.CHUNK - 1) // N.CHUNK
+    return 2 if (B * H * 2 * 2 <= 148 and nch >= 64) else 1
+
+
+# The span-map folds run in float64 torch on the device: a few batched
+# K x K by K x (V+K) products per step, exact regardless of TF32 settings.
+def _compose_maps(hm_sub):
+    """[h_e | M] of consecutive sub-spans ([B, S, H, K, V+K]) -> the map of the
+    whole span: x = [0 | I];  x = M_s x + [h_e_s | 0]  for s = 0 .. S-1."""
+    B, S, H, K, VK = hm_sub.shape
+    V = VK - K
+    m = hm_sub.double()
+    x = m[:, 0].clone()
+    for j in range(1, S):
+        x = torch.matmul(m[:, j, ..., V:], x)
+        x[..., :V] += m[:, j, ..., :V]
+    return x.float().contiguous()
+
+
+def _unfold_states(h0, hm_sub):
+    """Initial state of every sub-span from the span's: s_0 = h0,
+    s_j = M_{j-1} s_{j-1} + h_e_{j-1}.  Returns [B*S, H, K, V]."""
+    B, S, H, K, VK = hm_sub.shape
+    V = VK - K
+    m = hm_sub.double()
+    out = [h0.double()]
+    for j in range(1, S):
+        out.append(torch.matmul(m[:, j - 1, ..., V:], out[-1]) + m[:, j - 1, ..., :V])
+    return torch.stack(out, 1).float().reshape(B * S, H, K, V).contiguous()
+
+
+def _compose_grads(dhm_sub, hm_sub, dht):
+    """Span-start gradient of consecutive sub-spans' outputs (dhm_sub
+    [B, S, H, K, V], zero end gradient each) and of the span's end-state
+    gradient dht (or None): x = dht;  x = M_s^T x + dhm_s  for s = S-1 .. 0."""
+    B, S, H, K, V = dhm_sub.shape
+    m = hm_sub.double()
+    x = dht.double() if dht is not None else torch.zeros_like(dhm_sub[:, 0], dtype=torch.float64)
+    for j in range(S - 1, -1, -1):
+        x = torch.matmul(m[:, j, ..., V:].transpose(-1, -2), x) + dhm_sub[:, j].double()
+    return x.float().contiguous()
+
+
+def _unfold_grads(dht_span, dhm_sub, hm_sub):
+    """End-state gradient of every sub-span from the span's: g_{S-1} =
+    dht_span,  g_j = M_{j+1}^T g_{j+1} + dhm_{j+1}.  Returns [B*S, H, K, V]."""
+    B, S, H, K, V = dhm_sub.shape
+    m = hm_sub.double()
+    out = [dht_span.double()]
+    for j in range(S - 2, -1, -1):
+        out.append(torch.matmul(m[:, j + 1, ..., V:].transpose(-1, -2), out[-1]) +
+                   dhm_sub[:, j + 1].double())
+    out.reverse()
+    return torch.stack(out, 1).float().reshape(B * S, H, K, V).contiguous()
+
+
 class CPChunkGDN2Function(torch.autograd.Function):
     """Autograd wrapper of the sequence-parallel forward/backward for one rank."""
 
@@ -79,38 +144,46 @@ class CPChunkGDN2Function(torch.autograd.Function):
         B, T, H, K = q.shape
         V = v.shape[-1]
         dev = q.device
-        tables = N.seq_tables(B, T, dev)
+        S = _sub_spans(B, T, H, q.dtype)
+        # the kernels see the span as B*S sequences (same chunks)
+        tables = N.split_tables(B, T, S, dev) if S > 1 else N.seq_tables(B, T, dev)
         prob = _problem(H, K, V, q.dtype, l2norm, scale, tables)
+        prob_span = _problem(H, K, V, q.dtype, l2norm, scale, N.seq_tables(B, T, dev))
         st = N.stream_of(dev)
         sbytes = lib.gdn2_chunk_saved_bytes(prob)
         saved = torch.empty(max(sbytes, 1), dtype=torch.uint8, device=dev)
         N.check(lib.gdn2_chunk_fwd_intra(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
                                          N.ptr(w), N.ptr(saved), sbytes, st),
                 "gdn2_chunk_fwd_intra")
-        hm = torch.empty(B, H, K, V + K, dtype=torch.float32, device=dev)
-        N.check(lib.gdn2_cp_fwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(hm), None, 0, st),
+        hm_sub = torch.empty(B * S, H, K, V + K, dtype=torch.float32, device=dev)
+        N.check(lib.gdn2_cp_fwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(hm_sub), None, 0, st),
                 "gdn2_cp_fwd_prescan")
-        hm_all = gather(hm)
+        hm_sub = hm_sub.view(B, S, H, K, V + K)
+        hm = hm_sub[:, 0] if S == 1 else _compose_maps(hm_sub)
+        hm_all = gather(hm.contiguous())
         h0 = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
-        N.check(lib.gdn2_cp_merge(prob, N.ptr(hm_all), None, rank, world, 1,
+        N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), None, rank, world, 1,
                                   N.ptr(initial_state), N.ptr(h0), st), "gdn2_cp_merge")
+        h0_sub = h0 if S == 1 else _unfold_states(h0, hm_sub)
         o = torch.empty_like(v)
-        ht = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
-        N.check(lib.gdn2_chunk_fwd_state(prob, N.ptr(h0), N.ptr(o), N.ptr(ht), N.ptr(saved),
-                                         sbytes, st), "gdn2_chunk_fwd_state")
-        ctx.save_for_backward(q, k, v, g, b, w, saved, h0, hm_all)
-        ctx.meta = (scale, l2norm, rank, world, gather, tables, initial_state is not None)
+        ht_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
+        N.check(lib.gdn2_chunk_fwd_state(prob, N.ptr(h0_sub), N.ptr(o), N.ptr(ht_sub),
+                                         N.ptr(saved), sbytes, st), "gdn2_chunk_fwd_state")
+        ht = ht_sub.view(B, S, H, K, V)[:, S - 1].contiguous()
+        ctx.save_for_backward(q, k, v, g, b, w, saved, h0, hm_all, hm_sub)
+        ctx.meta = (scale, l2norm, rank, world, gather, tables, initial_state is not None, S)
         return o, ht
 
     @staticmethod
     def backward(ctx, do, dht):
-        q, k, v, g, b, w, saved, h0, hm_all = ctx.saved_tensors
-        scale, l2norm, rank, world, gather, tables, had_h0 = ctx.meta
+        q, k, v, g, b, w, saved, h0, hm_all, hm_sub = ctx.saved_tensors
+        scale, l2norm, rank, world, gather, tables, had_h0, S = ctx.meta
         lib = N.load()
         B, T, H, K = q.shape
         V = v.shape[-1]
         dev = q.device
         prob = _problem(H, K, V, q.dtype, l2norm, scale, tables)
+        prob_span = _problem(H, K, V, q.dtype, l2norm, scale, N.seq_tables(B, T, dev))
         st = N.stream_of(dev)
         sbytes = lib.gdn2_chunk_saved_bytes(prob)
         (do,) = _aligned16(do.to(q.dtype).contiguous())
@@ -118,9 +191,17 @@ class CPChunkGDN2Function(torch.autograd.Function):
         # Only the last rank's end state is the sequence's final state.
         dht_final = dht.float().contiguous() if (last and dht is not None) else None
         # Span-start gradient of the local outputs (and of the final state).
-        dhm = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
-        N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do), N.ptr(dht_final),
-                                        N.ptr(dhm), None, 0, st), "gdn2_cp_bwd_prescan")
+        if S == 1:
+            dhm = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
+            N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do),
+                                            N.ptr(dht_final), N.ptr(dhm), None, 0, st),
+                    "gdn2_cp_bwd_prescan")
+        else:
+            dhm_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
+            N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do), None,
+                                            N.ptr(dhm_sub), None, 0, st), "gdn2_cp_bwd_prescan")
+            dhm_sub = dhm_sub.view(B, S, H, K, V)
+            dhm = _compose_grads(dhm_sub, hm_sub, dht_final)
         wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
         ws = torch.empty(max(wbytes, 1), dtype=torch.uint8, device=dev)
         dhm_all = gather(dhm)
@@ -128,14 +209,18 @@ class CPChunkGDN2Function(torch.autograd.Function):
             dht_local = dht_final
         else:
             dht_local = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
-            N.check(lib.gdn2_cp_merge(prob, N.ptr(hm_all), N.ptr(dhm_all), rank, world, 0, None,
-                                      N.ptr(dht_local), st), "gdn2_cp_merge (backward)")
+            N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), N.ptr(dhm_all), rank, world, 0,
+                                      None, N.ptr(dht_local), st), "gdn2_cp_merge (backward)")
+        if S > 1:
+            end = dht_local if dht_local is not None else torch.zeros_like(h0)
+            dht_local = _unfold_grads(end, dhm_sub, hm_sub)
         grads = {n: torch.empty_like(t) for n, t in zip("qkvgbw", (q, k, v, g, b, w))}
-        dh0 = torch.empty_like(h0)
+        dh0_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
         N.check(lib.gdn2_chunk_bwd(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
                                    N.ptr(w), N.ptr(saved), sbytes, N.ptr(do), N.ptr(dht_local),
-                                   *(N.ptr(grads[n]) for n in "qkvgbw"), N.ptr(dh0), N.ptr(ws),
-                                   wbytes, st), "gdn2_chunk_bwd")
+                                   *(N.ptr(grads[n]) for n in "qkvgbw"), N.ptr(dh0_sub),
+                                   N.ptr(ws), wbytes, st), "gdn2_chunk_bwd")
+        dh0 = dh0_sub.view(B, S, H, K, V)[:, 0].contiguous()
         # dh0 on rank 0 is the gradient of the global initial state; on later
         # ranks the initial state is an internal value whose gradient has been
         # routed to the earlier ranks through their end-state gradients.

@@ -35,14 +35,16 @@ def main():
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = torch.device("cuda", local)
     B, H, K, V = 1, 4, 128, 128
-    T = 256 * world
+    T = 64 * 64 * world  # 64 chunks per rank: the span is cut into two sub-spans
     gen = torch.Generator(device=dev).manual_seed(0)
     bf = torch.bfloat16
     q = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf)
     k = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf)
     v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
-    g = -torch.rand(B, T, H, K, device=dev, generator=gen)
-    b = torch.sigmoid(torch.randn(B, T, H, K, device=dev, generator=gen)).to(bf)
+    # long memory (tiny decays, small erase gates) so the state entering a
+    # span, and a sub-span, still matters thousands of tokens later
+    g = -5e-4 * torch.rand(B, T, H, K, device=dev, generator=gen)
+    b = (0.05 * torch.sigmoid(torch.randn(B, T, H, K, device=dev, generator=gen))).to(bf)
     w = torch.sigmoid(torch.randn(B, T, H, V, device=dev, generator=gen)).to(bf)
     h0 = torch.randn(B, H, K, V, device=dev, generator=gen) * 0.1
     do = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
@@ -91,6 +93,12 @@ def main():
     errs["conv_dx"] = rel(xl.grad, xf.grad[:, a:e])
     errs["conv_dw"] = rel(dwl, wf.grad.float())
     errs["conv_db"] = rel(dbl, bff.grad.float())
+    # the spans are coupled: this rank's output differs from running its span
+    # from a zero state (rank 0 has the global initial state, so check r > 0)
+    if rank > 0:
+        o0, _ = chunk_gdn2(*(loc[n].detach() for n in names), output_final_state=True,
+                           use_qk_l2norm_in_kernel=True)
+        errs["coupling"] = 0.0 if rel(o0, o_ref[:, a:e]) > 1e-2 else 1.0
     bad = {n: x for n, x in errs.items() if not x < 2e-2}
     print(f"rank {rank}: " + " ".join(f"{n}={x:.1e}" for n, x in errs.items()), flush=True)
     dist.barrier()

@@ -196,3 +196,51 @@ def test_conv_halo_exchange_over_gloo():
         assert fwd_err < 1e-12, (rank, fwd_err)
         assert bwd_err < 1e-12, (rank, bwd_err)
 
+
+
+def test_sub_span_folds_match_the_whole_span():
+    """The sequence-parallel path cuts a rank's span into sub-spans; the
+    folds that join them (qwendopamine_b200.gdn2_ops.cp) must reproduce the
+    whole span: composed maps = the span's map, unfolded initial states = the
+    recurrence's state at each cut, composed / unfolded gradients = the
+    reverse pass's.  Float64 oracle maps on the CPU."""
+    import sys
+
+    sys.path.insert(0, ROOT)
+    from oracle import gdn2_oracle as O
+    from qwendopamine_b200.gdn2_ops import cp
+
+    q, k, v, g, b, w, h0, do = _inputs()
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    cuts = [0, 40, 64, T]  # three sub-spans
+    args = (q, k, v, g, b, w)
+    sub = [tuple(x[:, a:e] for x in args) for a, e in zip(cuts[:-1], cuts[1:])]
+    maps = [O.span_transition(*s, norm_mode="torch") for s in sub]
+    hm_sub = torch.from_numpy(np.stack([np.concatenate([he, M], -1) for M, he in maps], 1))
+    M_all, he_all = O.span_transition(*args, norm_mode="torch")
+    comp = cp._compose_maps(hm_sub.float()).double().numpy()
+    assert np.abs(comp[..., :V] - he_all).max() < 1e-5
+    assert np.abs(comp[..., V:] - M_all).max() < 1e-5
+    # initial state of every sub-span
+    states = cp._unfold_states(torch.from_numpy(h0).float(), hm_sub.float()).view(B, 3, H, K, V)
+    for j, a in enumerate(cuts[:-1]):
+        ref = h0 if a == 0 else O.recurrent_fwd(*(x[:, :a] for x in args), h0, norm_mode="torch")[1]
+        assert np.abs(states[:, j].double().numpy() - ref).max() < 1e-5, j
+    # gradients: each sub-span's start gradient from its own outputs (zero end
+    # gradient), composed with a final-state gradient, vs the whole span's
+    dht = np.random.default_rng(1).standard_normal((B, H, K, V))
+    dhm = []
+    for (a, e), s in zip(zip(cuts[:-1], cuts[1:]), sub):
+        dhm.append(O.recurrent_bwd(*s, do[:, a:e], None, None, norm_mode="torch")[-1])
+    dhm_sub = torch.from_numpy(np.stack(dhm, 1)).float()
+    start = cp._compose_grads(dhm_sub, hm_sub.float(), torch.from_numpy(dht).float())
+    ref_start = O.recurrent_bwd(*args, do, None, dht, norm_mode="torch")[-1]
+    assert np.abs(start.double().numpy() - ref_start).max() < 1e-4
+    ends = cp._unfold_grads(torch.from_numpy(dht).float(), dhm_sub, hm_sub.float())
+    ends = ends.view(B, 3, H, K, V)
+    for j, e in enumerate(cuts[1:]):
+        ref_end = (dht if e == T else
+                   O.recurrent_bwd(*(x[:, e:] for x in args), do[:, e:], None, dht,
+                                   norm_mode="torch")[-1])
+        assert np.abs(ends[:, j].double().numpy() - ref_end).max() < 1e-4, j
