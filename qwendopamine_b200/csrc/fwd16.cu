@@ -302,19 +302,12 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
           s2[rr] += y * y;
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-          s1[rr] += __shfl_xor_sync(0xffffffffu, s1[rr], o);
-          s2[rr] += __shfl_xor_sync(0xffffffffu, s2[rr], o);
-        }
-      if (lane < 4) {
-        const int r = 4 * warp + lane;
-        const float x1 = lane == 0 ? s1[0] : lane == 1 ? s1[1] : lane == 2 ? s1[2] : s1[3];
-        const float x2 = lane == 0 ? s2[0] : lane == 1 ? s2[1] : lane == 2 ? s2[2] : s2[3];
-        rq[r] = a.l2norm ? rsqrtf(x1 + kNormEps) : 1.f;
-        rk[r] = a.l2norm ? rsqrtf(x2 + kNormEps) : 1.f;
+      const float v8[8] = {s1[0], s1[1], s1[2], s1[3], s2[0], s2[1], s2[2], s2[3]};
+      const float tot = warp_reduce8(v8, lane);
+      if ((lane & 3) == 0) {
+        const int idx = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+        const int r = 4 * warp + (idx & 3);
+        (idx < 4 ? rq : rk)[r] = a.l2norm ? rsqrtf(tot + kNormEps) : 1.f;
       }
     }
     // per-block decay factors, diagonal-block safety, gl out

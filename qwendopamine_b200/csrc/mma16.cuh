@@ -242,6 +242,31 @@ __device__ __forceinline__ void col_scan64_reg(float* s, int lds, float* tmp, fl
   __syncthreads();
 }
 
+// Sums over the warp's 32 lanes of eight values per lane, reduce-scatter
+// order (4 + 2 + 1 + 1 + 1 = 9 shuffles instead of 8 x 5): returns the total
+// of value idx = 4 * bit4 + 2 * bit3 + bit2 of the lane id, held by the 4
+// lanes that share those bits.
+__device__ __forceinline__ float warp_reduce8(const float (&v)[8], int lane) {
+  const bool h4 = lane & 16, h3 = lane & 8, h2 = lane & 4;
+  float a[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = h4 ? v[i] : v[4 + i];
+    a[i] = (h4 ? v[4 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float b2[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = h3 ? a[i] : a[2 + i];
+    b2[i] = (h3 ? a[2 + i] : a[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  const float send = h2 ? b2[0] : b2[1];
+  float c = (h2 ? b2[1] : b2[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
+}
+
 // Row norms of the 64-row q and k tiles (row stride ld): each warp owns
 // 64 / (NTH/32) consecutive rows and reduces them together.
 // rq[r] = rsqrt(sum q^2 + eps) (1 without l2norm), same for rk.
@@ -266,20 +291,30 @@ __device__ __forceinline__ void row_norms16(const T* sq, const T* sk, int ld, fl
       s2[rr] += y * y;
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int rr = 0; rr < RPW; ++rr) {
-      s1[rr] += __shfl_xor_sync(0xffffffffu, s1[rr], o);
-      s2[rr] += __shfl_xor_sync(0xffffffffu, s2[rr], o);
+  if constexpr (RPW == 4) {
+    const float v[8] = {s1[0], s1[1], s1[2], s1[3], s2[0], s2[1], s2[2], s2[3]};
+    const float tot = warp_reduce8(v, lane);
+    if ((lane & 3) == 0) {
+      const int idx = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+      const int r = RPW * warp + (idx & 3);
+      (idx < 4 ? rq : rk)[r] = l2norm ? rsqrtf(tot + kNormEps) : 1.f;
     }
+  } else {
 #pragma unroll
-  for (int rr = 0; rr < RPW; ++rr)
-    if (lane == rr) {
-      const int r = RPW * warp + rr;
-      rq[r] = l2norm ? rsqrtf(s1[rr] + kNormEps) : 1.f;
-      rk[r] = l2norm ? rsqrtf(s2[rr] + kNormEps) : 1.f;
-    }
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int rr = 0; rr < RPW; ++rr) {
+        s1[rr] += __shfl_xor_sync(0xffffffffu, s1[rr], o);
+        s2[rr] += __shfl_xor_sync(0xffffffffu, s2[rr], o);
+      }
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr)
+      if (lane == rr) {
+        const int r = RPW * warp + rr;
+        rq[r] = l2norm ? rsqrtf(s1[rr] + kNormEps) : 1.f;
+        rk[r] = l2norm ? rsqrtf(s2[rr] + kNormEps) : 1.f;
+      }
+  }
 }
 
 // Per-16-row-block decay factors F[I(I+1)/2 + J][c] = 2^(G_16I - G_(16J+15))
