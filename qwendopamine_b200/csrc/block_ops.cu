@@ -170,8 +170,9 @@ __device__ __forceinline__ void load_row(const ConvArgs& a, const T* xb, int b, 
 }
 
 // Channels per thread: 4 (a warp covers 128 channels, 256 bytes of a bf16
-// row), which keeps the forward near 100 registers (two CTAs per SM with the
-// register window, weights and 8 rows in flight) and the backward at 128.
+// row; a CTA 1024 contiguous channels), which keeps the forward at 64
+// registers (four CTAs per SM) and the backward under 128 (two), with the
+// register window, the weights and a 4-row run in flight.
 constexpr int kFwdCPT = 4;
 constexpr int kBwdCPT = 4;
 constexpr int kConvChannels = 256 * 4;  // channels per CTA (256 threads x 4)

@@ -214,7 +214,9 @@ __global__ void __launch_bounds__(kThreads, 3) k_recurrent(RecArgs a) {
 // so HBM streams the next state while this one is updated; the new state
 // leaves from registers with 128-bit streaming stores.  Same arithmetic,
 // order and reductions as k_recurrent (thread (rg, cg) holds rows
-// [rg*RPT, +RPT) x columns [4cg, 4cg+4)).
+// [rg*RPT, +RPT) x columns [4cg, 4cg+4)); every warp forms the q / k norms
+// itself and the two column reductions have separate buffers, so a token
+// costs four block barriers.
 struct RecUnit {
   int64_t bos, Tn;
   const float* h0;
@@ -275,8 +277,7 @@ struct RecStreamSmem {
   static constexpr uint32_t oRed = oF + 6 * D * 4;                 // red[2][RG][D]
   static constexpr uint32_t oUnit = oRed + 2 * RG * D * 4;         // RecUnit[NBUF]
   static constexpr uint32_t oBar = oUnit + NBUF * sizeof(RecUnit);  // mbarrier[NBUF]
-  static constexpr uint32_t oNorm = oBar + 8 * NBUF;
-  static constexpr uint32_t bytes = oNorm + 16 + 128;
+  static constexpr uint32_t bytes = oBar + 8 * NBUF + 128;
 };
 
 template <typename T, int D>
