@@ -153,3 +153,22 @@ def test_dtype_codes():
     assert N.dtype_code(torch.float16) == 2
     with pytest.raises(TypeError):
         N.dtype_code(torch.int8)
+
+
+def test_split_tables_keep_the_chunks():
+    """Sub-span tables (sequence parallelism): each of B sequences cut into S
+    chunk-aligned sub-spans, listed sequence by sequence; the chunks are the
+    same as without the cut, so every per-chunk buffer keeps its layout."""
+    full = N.seq_tables(2, 300, "cpu")
+    t = N.split_tables(2, 300, 2, "cpu")
+    assert t.n_seqs == 4 and t.total == 600 and t.n_chunks == full.n_chunks == 10
+    assert t.cu.tolist() == [0, 128, 300, 428, 600]
+    assert all(c % 64 == 0 for c in (128, 428 - 300))
+    # chunk c starts at the same row in both tables
+    starts_full = [int(full.cu[s]) + 64 * (c - int(full.coff[s]))
+                   for c, s in enumerate(full.cseq.tolist())]
+    starts = [int(t.cu[s]) + 64 * (c - int(t.coff[s])) for c, s in enumerate(t.cseq.tolist())]
+    assert starts == starts_full
+    with pytest.raises(ValueError):
+        N.split_tables(1, 64, 2, "cpu")  # one chunk cannot make two sub-spans
+    assert N.split_tables(2, 300, 2, "cpu") is t  # cached
