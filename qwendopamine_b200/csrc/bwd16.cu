@@ -416,10 +416,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
         float pq[1][NTO][4], pk[1][NTO][4];
         acc_zero(pq);
         acc_zero(pk);
-        warp_mma16<1, NTO, true, false>(pq, sDAqk + 16 * J, LDC, 16 * I, sKb + 16 * J * LDK, LDK,
-                                        wc * DQ, 16);
-        warp_mma16<1, NTO, true, false>(pk, sDAkk + 16 * J, LDC, 16 * I, sKb + 16 * J * LDK, LDK,
-                                        wc * DQ, 16);
+        warp_mma16_2a<NTO, true, false>(pq, pk, sDAqk + 16 * J, sDAkk + 16 * J, LDC, 16 * I,
+                                        sKb + 16 * J * LDK, LDK, wc * DQ, 16);
         const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
 #pragma unroll
         for (int j = 0; j < NTO; ++j) {

@@ -105,6 +105,30 @@ __device__ __forceinline__ void warp_mma16(float (&acc)[MT][NT][4], const T* A, 
   }
 }
 
+// acc1 += A1 B and acc2 += A2 B with the B fragments loaded once (the two A
+// tiles share lda / m0 / kd).
+template <int NT, bool A_KMAJOR, bool B_KMAJOR, typename T>
+__device__ __forceinline__ void warp_mma16_2a(float (&acc1)[1][NT][4], float (&acc2)[1][NT][4],
+                                              const T* A1, const T* A2, int lda, int m0,
+                                              const T* B, int ldb, int n0, int kd) {
+  static_assert(NT % 2 == 0, "NT must be even");
+#pragma unroll
+  for (int k0 = 0; k0 < kd; k0 += 16) {
+    uint32_t a1[4], a2[4];
+    load_a16<A_KMAJOR>(a1, A1, lda, m0, k0);
+    load_a16<A_KMAJOR>(a2, A2, lda, m0, k0);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      load_b16x2<B_KMAJOR>(b, B, ldb, k0, n0 + 8 * j);
+      Mma16<T>::run(acc1[0][j], a1, b[0], b[1]);
+      Mma16<T>::run(acc1[0][j + 1], a1, b[2], b[3]);
+      Mma16<T>::run(acc2[0][j], a2, b[0], b[1]);
+      Mma16<T>::run(acc2[0][j + 1], a2, b[2], b[3]);
+    }
+  }
+}
+
 // Pack two floats into a 16-bit pair (low half = first).
 template <typename T> __device__ __forceinline__ uint32_t pack2(float x, float y);
 template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float x, float y) {
