@@ -285,9 +285,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
     const float2 b2 = ld2<T>(sb + r * LDK + cc), k2 = ld2<T>(sk + r * LDK + cc);
     const float2 G2 = ld2<float>(sG + r * LDG + cc);
-    const float e0 = b2.x * k2.x * rk[r] * fast_exp2(G2.x);
-    const float e1 = b2.y * k2.y * rk[r] * fast_exp2(G2.y);
-    *reinterpret_cast<uint32_t*>(sE + r * LDK + cc) = pack2<T>(e0, e1);
+    const float2 e = mul2(mul2(mul2(b2, k2), f2(rk[r])), exp2_2(G2));
+    *reinterpret_cast<uint32_t*>(sE + r * LDK + cc) = pack2<T>(e.x, e.y);
   }
   __syncthreads();
   // dA += dW E^T ; dAkk = -tril_strict(A^T dA A^T)
@@ -347,21 +346,16 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
       const float2 GL2 = ld2<float>(sG + (kChunk - 1) * LDG + c0);
       const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
       const float2 b2 = ld2<T>(sb + r * LDK + c0);
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int e = 2 * hf + t;
-        const float G = sel2(G2, t), GL = sel2(GL2, t);
-        const float gam = fast_exp2(G);
-        const float qn = sel2(q2, t) * rq[r];
-        const float kn = sel2(k2, t) * rk[r];
-        const float bb = sel2(b2, t);
-        dq[0][j][e] = scale * gam * dq[0][j][e];
-        dkb[0][j][e] = gam * dkb[0][j][e];
-        const float kd = dkn[0][j][e] * fast_exp2(GL - G);
-        dkn[0][j][e] = kd;
-        X[j][e] = kn * kd;
-        dG[0][j][e] = qn * dq[0][j][e] + bb * kn * dkb[0][j][e];
-      }
+      const float2 gam = exp2_2(G2);
+      const float2 qn = mul2(q2, f2(rq[r])), kn = mul2(k2, f2(rk[r]));
+      const float2 dqv = mul2(mul2(f2(scale), gam), pr(dq[0][j], hf));
+      const float2 dkbv = mul2(gam, pr(dkb[0][j], hf));
+      const float2 kd = mul2(pr(dkn[0][j], hf), exp2_2(make_float2(GL2.x - G2.x, GL2.y - G2.y)));
+      setpr(dq[0][j], hf, dqv);
+      setpr(dkb[0][j], hf, dkbv);
+      setpr(dkn[0][j], hf, kd);
+      setpr(X[j], hf, mul2(kn, kd));
+      setpr(dG[0][j], hf, fma2(qn, dqv, mul2(mul2(b2, kn), dkbv)));
     }
   __syncthreads();  // sDW / sE / sT* are dead; R2 becomes the score tiles
 
@@ -383,20 +377,15 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     const float2 Ge2 = ld2<float>(sG + re * LDG + cc);
     const float2 qv = ld2<T>(sq + r * LDK + cc), kv = ld2<T>(sk + r * LDK + cc);
     const float2 bv = ld2<T>(sb + r * LDK + cc);
-    float q2[2], kb2[2], k2[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const float G = sel2(G2, t);
-      const float f = fast_exp2(G - sel2(Gb2, t));
-      const float fe = fast_exp2(sel2(Ge2, t) - G);
-      const float kn = sel2(kv, t) * rk[r];
-      q2[t] = scale * sel2(qv, t) * rq[r] * f;
-      kb2[t] = sel2(bv, t) * kn * f;
-      k2[t] = kn * fe;
-    }
-    *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(q2[0], q2[1]);
-    *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kb2[0], kb2[1]);
-    *reinterpret_cast<uint32_t*>(sKb + r * LDK + cc) = pack2<T>(k2[0], k2[1]);
+    const float2 f = exp2_2(make_float2(G2.x - Gb2.x, G2.y - Gb2.y));
+    const float2 fe = exp2_2(make_float2(Ge2.x - G2.x, Ge2.y - G2.y));
+    const float2 kn = mul2(kv, f2(rk[r]));
+    const float2 q2 = mul2(mul2(mul2(f2(scale), qv), f2(rq[r])), f);
+    const float2 kb2 = mul2(mul2(bv, kn), f);
+    const float2 k2 = mul2(kn, fe);
+    *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(q2.x, q2.y);
+    *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kb2.x, kb2.y);
+    *reinterpret_cast<uint32_t*>(sKb + r * LDK + cc) = pack2<T>(k2.x, k2.y);
   }
   for (int i = tid; i < 4 * D; i += NTH) {
     const int bI = i / D, cc = i - bI * D;
@@ -423,10 +412,9 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
         for (int j = 0; j < NTO; ++j) {
           const float2 F2 = ld2<float>(FIJ + wc * DQ + 8 * j + 2 * tig);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float F = sel2(F2, e & 1);
-            tq[0][j][e] += F * pq[0][j][e];
-            tk[0][j][e] += F * pk[0][j][e];
+          for (int hf = 0; hf < 2; ++hf) {
+            setpr(tq[0][j], hf, fma2(F2, pr(pq[0][j], hf), pr(tq[0][j], hf)));
+            setpr(tk[0][j], hf, fma2(F2, pr(pk[0][j], hf), pr(tk[0][j], hf)));
           }
         }
       }
@@ -439,17 +427,14 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
           const float2 Gb2 = ld2<float>(sG + (16 * I) * LDG + c0);
           const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
           const float2 b2 = ld2<T>(sb + r * LDK + c0);
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int e = 2 * hf + t;
-            const float f = fast_exp2(sel2(G2, t) - sel2(Gb2, t));
-            const float xq = scale * tq[0][j][e] * f, xk = tk[0][j][e] * f;
-            const float qn = sel2(q2, t) * rq[r];
-            const float kb = sel2(b2, t) * sel2(k2, t) * rk[r];
-            dq[0][j][e] += xq;
-            dkb[0][j][e] += xk;
-            dG[0][j][e] += qn * xq + kb * xk;
-          }
+          const float2 f = exp2_2(make_float2(G2.x - Gb2.x, G2.y - Gb2.y));
+          const float2 xq = mul2(mul2(f2(scale), pr(tq[0][j], hf)), f);
+          const float2 xk = mul2(pr(tk[0][j], hf), f);
+          const float2 qn = mul2(q2, f2(rq[r]));
+          const float2 kb = mul2(mul2(b2, k2), f2(rk[r]));
+          setpr(dq[0][j], hf, add2(pr(dq[0][j], hf), xq));
+          setpr(dkb[0][j], hf, add2(pr(dkb[0][j], hf), xk));
+          setpr(dG[0][j], hf, add2(pr(dG[0][j], hf), fma2(qn, xq, mul2(kb, xk))));
         }
     }
     // Y products: columns of block J = wr, from block rows I >= J; the key
@@ -473,7 +458,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
       for (int j = 0; j < NTO; ++j) {
         const float2 F2 = ld2<float>(FIJ + wc * DQ + 8 * j + 2 * tig);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) ys[j][e] += sel2(F2, e & 1) * ty[0][j][e];
+        for (int hf = 0; hf < 2; ++hf) setpr(ys[j], hf, fma2(F2, pr(ty[0][j], hf), pr(ys[j], hf)));
       }
     }
 #pragma unroll
@@ -484,14 +469,10 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
         const float2 Ge2 = ld2<float>(sG + (16 * J + 15) * LDG + c0);
         const float2 G2 = ld2<float>(sG + r * LDG + c0);
         const float2 k2 = ld2<T>(sk + r * LDK + c0);
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const int e = 2 * hf + t;
-          const float y = ys[j][e] * fast_exp2(sel2(Ge2, t) - sel2(G2, t));
-          const float kn = sel2(k2, t) * rk[r];
-          dkn[0][j][e] += y;
-          dG[0][j][e] -= kn * y;
-        }
+        const float2 y = mul2(pr(ys[j], hf), exp2_2(make_float2(Ge2.x - G2.x, Ge2.y - G2.y)));
+        const float2 kn = mul2(k2, f2(rk[r]));
+        setpr(dkn[0][j], hf, add2(pr(dkn[0][j], hf), y));
+        setpr(dG[0][j], hf, fma2(neg2(kn), y, pr(dG[0][j], hf)));
       }
     if (!safe) {
       // exact diagonal block, off-diagonal pairs only
@@ -620,20 +601,16 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
       const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
       const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
       const float2 b2 = ld2<T>(sb + r * LDK + c0);
-      const float dgn = scale * sDiag[r];
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int e = 2 * hf + t;
-        const float qn = sel2(q2, t) * rq[r];
-        const float kn = sel2(k2, t) * rk[r];
-        const float bb = sel2(b2, t);
-        const float dkbv = dkb[0][j][e];
-        dq[0][j][e] += dgn * kn;
-        dkn[0][j][e] += dkbv * bb + dgn * qn;
-        dkb[0][j][e] = dkbv * kn;  // db
-        pq[hf] += qn * dq[0][j][e];
-        pk[hf] += kn * dkn[0][j][e];
-      }
+      const float2 dgn = f2(scale * sDiag[r]);
+      const float2 qn = mul2(q2, f2(rq[r])), kn = mul2(k2, f2(rk[r]));
+      const float2 dkbv = pr(dkb[0][j], hf);
+      const float2 dqv = fma2(dgn, kn, pr(dq[0][j], hf));
+      const float2 dknv = add2(pr(dkn[0][j], hf), fma2(dkbv, b2, mul2(dgn, qn)));
+      setpr(dq[0][j], hf, dqv);
+      setpr(dkn[0][j], hf, dknv);
+      setpr(dkb[0][j], hf, mul2(dkbv, kn));  // db
+      pq[hf] = fmaf(qn.y, dqv.y, fmaf(qn.x, dqv.x, pq[hf]));
+      pk[hf] = fmaf(kn.y, dknv.y, fmaf(kn.x, dknv.x, pk[hf]));
     }
   if (a.l2norm) {
 #pragma unroll

@@ -369,41 +369,26 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
         const uint32_t ub = *reinterpret_cast<const uint32_t*>(sb + o16);
         const uint32_t uv = *reinterpret_cast<const uint32_t*>(sv + o16);
         const uint32_t uw = *reinterpret_cast<const uint32_t*>(sw + o16);
-        const T* pq = reinterpret_cast<const T*>(&uq);
-        const T* pk = reinterpret_cast<const T*>(&uk);
-        const T* pb = reinterpret_cast<const T*>(&ub);
-        const T* pv = reinterpret_cast<const T*>(&uv);
-        const T* pw = reinterpret_cast<const T*>(&uw);
-        const float nq = rq[r], nk = rk[r];
-        const float g2[2] = {G.x, G.y}, gb2[2] = {Gb.x, Gb.y}, ge2[2] = {Ge.x, Ge.y};
-        const float pb2[2] = {Pb.x, Pb.y}, qe2[2] = {Qe.x, Qe.y};
-        float qg[2], kd[2], qs[2], kbs[2], kb[2], e2[2], z2[2];
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const float f = fast_exp2(g2[t] - gb2[t]);   // <= 1
-          const float fe = fast_exp2(ge2[t] - g2[t]);  // <= 1
-          const float qn = to_f<T>(pq[t]) * nq;
-          const float kn = to_f<T>(pk[t]) * nk;
-          const float bkn = to_f<T>(pb[t]) * kn;
-          const float eG = pb2[t] * f;   // 2^G
-          const float eK = qe2[t] * fe;  // 2^(G_63 - G)
-          qg[t] = scale * qn * eG;
-          kd[t] = kn * eK;
-          qs[t] = scale * qn * f;
-          kbs[t] = bkn * f;
-          kb[t] = kn * fe;
-          e2[t] = bkn * eG;
-          z2[t] = to_f<T>(pv[t]) * to_f<T>(pw[t]);
-        }
+        const float2 f = exp2_2(make_float2(G.x - Gb.x, G.y - Gb.y));   // <= 1
+        const float2 fe = exp2_2(make_float2(Ge.x - G.x, Ge.y - G.y));  // <= 1
+        const float2 qn = mul2(unpack2<T>(uq), f2(rq[r]));
+        const float2 kn = mul2(unpack2<T>(uk), f2(rk[r]));
+        const float2 bkn = mul2(unpack2<T>(ub), kn);
+        const float2 eG = mul2(Pb, f);   // 2^G
+        const float2 eK = mul2(Qe, fe);  // 2^(G_63 - G)
+        const float2 sqn = mul2(f2(scale), qn);
+        const float2 qg = mul2(sqn, eG), kd = mul2(kn, eK), qs = mul2(sqn, f);
+        const float2 kbs = mul2(bkn, f), kb = mul2(kn, fe), e2 = mul2(bkn, eG);
+        const float2 z2 = mul2(unpack2<T>(uv), unpack2<T>(uw));
         if (cc < K) {
-          *reinterpret_cast<uint32_t*>(gQg + r * K + cc) = pack2<T>(qg[0], qg[1]);
-          *reinterpret_cast<uint32_t*>(gKd + r * K + cc) = pack2<T>(kd[0], kd[1]);
+          *reinterpret_cast<uint32_t*>(gQg + r * K + cc) = pack2<T>(qg.x, qg.y);
+          *reinterpret_cast<uint32_t*>(gKd + r * K + cc) = pack2<T>(kd.x, kd.y);
         }
-        *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(qs[0], qs[1]);
-        *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kbs[0], kbs[1]);
-        *reinterpret_cast<uint32_t*>(sKb + r * LDK + cc) = pack2<T>(kb[0], kb[1]);
-        *reinterpret_cast<uint32_t*>(sw + o16) = pack2<T>(e2[0], e2[1]);
-        *reinterpret_cast<uint32_t*>(sv + o16) = pack2<T>(z2[0], z2[1]);
+        *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(qs.x, qs.y);
+        *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kbs.x, kbs.y);
+        *reinterpret_cast<uint32_t*>(sKb + r * LDK + cc) = pack2<T>(kb.x, kb.y);
+        *reinterpret_cast<uint32_t*>(sw + o16) = pack2<T>(e2.x, e2.y);
+        *reinterpret_cast<uint32_t*>(sv + o16) = pack2<T>(z2.x, z2.y);
       }
     }
     tc::fence_async_smem();

@@ -153,6 +153,30 @@ template <> __device__ __forceinline__ float2 ld2<float>(const float* p) {
   return *reinterpret_cast<const float2*>(p);
 }
 __device__ __forceinline__ float sel2(const float2& v, int t) { return t ? v.y : v.x; }
+// The two 16-bit elements of a 32-bit word as floats.
+template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t x) {
+  return ld2<T>(reinterpret_cast<const T*>(&x));
+}
+
+// Packed fp32x2 arithmetic: one instruction for both elements of a column
+// pair, each rounded as the scalar operation is.  pr / setpr view elements
+// (2 hf, 2 hf + 1) of an mma fragment -- one row, two adjacent columns -- as
+// such a pair.
+__device__ __forceinline__ float2 f2(float s) { return make_float2(s, s); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
+__device__ __forceinline__ float2 exp2_2(float2 x) {
+  return make_float2(fast_exp2(x.x), fast_exp2(x.y));
+}
+__device__ __forceinline__ float2 pr(const float (&a)[4], int hf) {
+  return make_float2(a[2 * hf], a[2 * hf + 1]);
+}
+__device__ __forceinline__ void setpr(float (&a)[4], int hf, float2 v) {
+  a[2 * hf] = v.x;
+  a[2 * hf + 1] = v.y;
+}
 
 // ---------------------------------------------------------------------------
 // cp.async
