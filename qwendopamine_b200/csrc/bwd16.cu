@@ -202,19 +202,20 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     for (int i = tid; i < kChunk * 16; i += NTH) {
       const int r = i >> 4, cc = (i & 15) * 2;
       const float2 v2 = ld2<T>(vs + r * LDS + cc), w2 = ld2<T>(ws + r * LDS + cc);
-      *reinterpret_cast<uint32_t*>(sZ + r * LDS + cc) = pack2<T>(v2.x * w2.x, v2.y * w2.y);
+      const float2 z2 = mul2(v2, w2);
+      *reinterpret_cast<uint32_t*>(sZ + r * LDS + cc) = pack2<T>(z2.x, z2.y);
     }
     // dgl[row] += sum over the slice's 32 columns of h * dh: 4 threads per
     // row, 8 columns each, combined with two shuffles
     for (int i = tid; i < 4 * D; i += NTH) {
       const int row = i >> 2, part = i & 3;
-      float acc = 0.f;
+      float2 acc2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int cc = 8 * part + 2 * u;
-        const float2 h2 = ld2<T>(hs + row * LDS + cc), d2 = ld2<T>(dhs + row * LDS + cc);
-        acc += h2.x * d2.x + h2.y * d2.y;
+        acc2 = fma2(ld2<T>(hs + row * LDS + cc), ld2<T>(dhs + row * LDS + cc), acc2);
       }
+      float acc = acc2.x + acc2.y;
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
       if (part == 0) dgl[row] += acc;
@@ -236,11 +237,11 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
         for (int hf = 0; hf < 2; ++hf) {
           const int r = zm + gid + 8 * hf, cl = zn + 8 * j + 2 * tig;
           if (r < len && cl < nv) {
-            const float z0 = accZ[0][j][2 * hf], z1 = accZ[0][j][2 * hf + 1];
-            const float w0 = to_f<T>(ws[r * LDS + cl]), w1 = to_f<T>(ws[r * LDS + cl + 1]);
-            const float x0 = to_f<T>(vs[r * LDS + cl]), x1 = to_f<T>(vs[r * LDS + cl + 1]);
-            *reinterpret_cast<uint32_t*>(gdv + r * ldv + v0 + cl) = pack2<T>(z0 * w0, z1 * w1);
-            *reinterpret_cast<uint32_t*>(gdw + r * ldv + v0 + cl) = pack2<T>(z0 * x0, z1 * x1);
+            const float2 z2 = pr(accZ[0][j], hf);
+            const float2 dv2 = mul2(z2, ld2<T>(ws + r * LDS + cl));
+            const float2 dw2 = mul2(z2, ld2<T>(vs + r * LDS + cl));
+            *reinterpret_cast<uint32_t*>(gdv + r * ldv + v0 + cl) = pack2<T>(dv2.x, dv2.y);
+            *reinterpret_cast<uint32_t*>(gdw + r * ldv + v0 + cl) = pack2<T>(dw2.x, dw2.y);
           }
         }
     }
@@ -395,85 +396,97 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   __syncthreads();
   const bool safe = sFlag[0] != 0;
   {
-    // X products: rows of block I = wr, one 16-key block J at a time
+    // X products: rows of block I = wr, one 16-key block J at a time, the
+    // owner columns in halves of NXH n8 tiles (fewer live accumulators)
     const int I = wr, nJ = safe ? I + 1 : I;
     if (nJ > 0) {
-      float tq[1][NTO][4], tk[1][NTO][4];
-      acc_zero(tq);
-      acc_zero(tk);
-      for (int J = 0; J < nJ; ++J) {
-        float pq[1][NTO][4], pk[1][NTO][4];
-        acc_zero(pq);
-        acc_zero(pk);
-        warp_mma16_2a<NTO, true, false>(pq, pk, sDAqk + 16 * J, sDAkk + 16 * J, LDC, 16 * I,
-                                        sKb + 16 * J * LDK, LDK, wc * DQ, 16);
-        const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
+      constexpr int NXH = NTO >= 4 ? NTO / 2 : NTO;
 #pragma unroll
-        for (int j = 0; j < NTO; ++j) {
-          const float2 F2 = ld2<float>(FIJ + wc * DQ + 8 * j + 2 * tig);
+      for (int h0 = 0; h0 < NTO; h0 += NXH) {
+        float tq[1][NXH][4], tk[1][NXH][4];
+        acc_zero(tq);
+        acc_zero(tk);
+        for (int J = 0; J < nJ; ++J) {
+          float pq[1][NXH][4], pk[1][NXH][4];
+          acc_zero(pq);
+          acc_zero(pk);
+          warp_mma16_2a<NXH, true, false>(pq, pk, sDAqk + 16 * J, sDAkk + 16 * J, LDC, 16 * I,
+                                          sKb + 16 * J * LDK, LDK, wc * DQ + 8 * h0, 16);
+          const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            setpr(tq[0][j], hf, fma2(F2, pr(pq[0][j], hf), pr(tq[0][j], hf)));
-            setpr(tk[0][j], hf, fma2(F2, pr(pk[0][j], hf), pr(tk[0][j], hf)));
+          for (int j = 0; j < NXH; ++j) {
+            const float2 F2 = ld2<float>(FIJ + wc * DQ + 8 * (h0 + j) + 2 * tig);
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              setpr(tq[0][j], hf, fma2(F2, pr(pq[0][j], hf), pr(tq[0][j], hf)));
+              setpr(tk[0][j], hf, fma2(F2, pr(pk[0][j], hf), pr(tk[0][j], hf)));
+            }
           }
         }
+#pragma unroll
+        for (int j = 0; j < NXH; ++j)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int jj = h0 + j;
+            const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * jj + 2 * tig;
+            const float2 G2 = ld2<float>(sG + r * LDG + c0);
+            const float2 Gb2 = ld2<float>(sG + (16 * I) * LDG + c0);
+            const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
+            const float2 b2 = ld2<T>(sb + r * LDK + c0);
+            const float2 f = exp2_2(make_float2(G2.x - Gb2.x, G2.y - Gb2.y));
+            const float2 xq = mul2(mul2(f2(scale), pr(tq[0][j], hf)), f);
+            const float2 xk = mul2(pr(tk[0][j], hf), f);
+            const float2 qn = mul2(q2, f2(rq[r]));
+            const float2 kb = mul2(mul2(b2, k2), f2(rk[r]));
+            setpr(dq[0][jj], hf, add2(pr(dq[0][jj], hf), xq));
+            setpr(dkb[0][jj], hf, add2(pr(dkb[0][jj], hf), xk));
+            setpr(dG[0][jj], hf, add2(pr(dG[0][jj], hf), fma2(qn, xq, mul2(kb, xk))));
+          }
       }
-#pragma unroll
-      for (int j = 0; j < NTO; ++j)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
-          const float2 G2 = ld2<float>(sG + r * LDG + c0);
-          const float2 Gb2 = ld2<float>(sG + (16 * I) * LDG + c0);
-          const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
-          const float2 b2 = ld2<T>(sb + r * LDK + c0);
-          const float2 f = exp2_2(make_float2(G2.x - Gb2.x, G2.y - Gb2.y));
-          const float2 xq = mul2(mul2(f2(scale), pr(tq[0][j], hf)), f);
-          const float2 xk = mul2(pr(tk[0][j], hf), f);
-          const float2 qn = mul2(q2, f2(rq[r]));
-          const float2 kb = mul2(mul2(b2, k2), f2(rk[r]));
-          setpr(dq[0][j], hf, add2(pr(dq[0][j], hf), xq));
-          setpr(dkb[0][j], hf, add2(pr(dkb[0][j], hf), xk));
-          setpr(dG[0][j], hf, add2(pr(dG[0][j], hf), fma2(qn, xq, mul2(kb, xk))));
-        }
     }
     // Y products: columns of block J = wr, from block rows I >= J; the key
     // side factor 2^(G_16I - G_r) = F_IJ 2^(G_(16J+15) - G_r)
     const int J = wr;
-    float ys[NTO][4];
+    constexpr int NYH = NTO >= 4 ? NTO / 2 : NTO;
 #pragma unroll
-    for (int j = 0; j < NTO; ++j)
+    for (int h0 = 0; h0 < NTO; h0 += NYH) {
+      float ys[NYH][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) ys[j][e] = 0.f;
-    for (int I = J; I < 4; ++I) {
-      if (I == J && !safe) continue;
-      float ty[1][NTO][4];
-      acc_zero(ty);
-      warp_mma16<1, NTO, false, false>(ty, sDAqk + 16 * I * LDC, LDC, 16 * J,
-                                       sQs + 16 * I * LDK, LDK, wc * DQ, 16);
-      warp_mma16<1, NTO, false, false>(ty, sDAkk + 16 * I * LDC, LDC, 16 * J,
-                                       sKBs + 16 * I * LDK, LDK, wc * DQ, 16);
-      const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
+      for (int j = 0; j < NYH; ++j)
 #pragma unroll
-      for (int j = 0; j < NTO; ++j) {
-        const float2 F2 = ld2<float>(FIJ + wc * DQ + 8 * j + 2 * tig);
+        for (int e = 0; e < 4; ++e) ys[j][e] = 0.f;
+      for (int I = J; I < 4; ++I) {
+        if (I == J && !safe) continue;
+        float ty[1][NYH][4];
+        acc_zero(ty);
+        warp_mma16<1, NYH, false, false>(ty, sDAqk + 16 * I * LDC, LDC, 16 * J,
+                                         sQs + 16 * I * LDK, LDK, wc * DQ + 8 * h0, 16);
+        warp_mma16<1, NYH, false, false>(ty, sDAkk + 16 * I * LDC, LDC, 16 * J,
+                                         sKBs + 16 * I * LDK, LDK, wc * DQ + 8 * h0, 16);
+        const float* FIJ = sF + (I * (I + 1) / 2 + J) * D;
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) setpr(ys[j], hf, fma2(F2, pr(ty[0][j], hf), pr(ys[j], hf)));
+        for (int j = 0; j < NYH; ++j) {
+          const float2 F2 = ld2<float>(FIJ + wc * DQ + 8 * (h0 + j) + 2 * tig);
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf)
+            setpr(ys[j], hf, fma2(F2, pr(ty[0][j], hf), pr(ys[j], hf)));
+        }
       }
+#pragma unroll
+      for (int j = 0; j < NYH; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int jj = h0 + j;
+          const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * jj + 2 * tig;
+          const float2 Ge2 = ld2<float>(sG + (16 * J + 15) * LDG + c0);
+          const float2 G2 = ld2<float>(sG + r * LDG + c0);
+          const float2 k2 = ld2<T>(sk + r * LDK + c0);
+          const float2 y = mul2(pr(ys[j], hf), exp2_2(make_float2(Ge2.x - G2.x, Ge2.y - G2.y)));
+          const float2 kn = mul2(k2, f2(rk[r]));
+          setpr(dkn[0][jj], hf, add2(pr(dkn[0][jj], hf), y));
+          setpr(dG[0][jj], hf, fma2(neg2(kn), y, pr(dG[0][jj], hf)));
+        }
     }
-#pragma unroll
-    for (int j = 0; j < NTO; ++j)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
-        const float2 Ge2 = ld2<float>(sG + (16 * J + 15) * LDG + c0);
-        const float2 G2 = ld2<float>(sG + r * LDG + c0);
-        const float2 k2 = ld2<T>(sk + r * LDK + c0);
-        const float2 y = mul2(pr(ys[j], hf), exp2_2(make_float2(Ge2.x - G2.x, Ge2.y - G2.y)));
-        const float2 kn = mul2(k2, f2(rk[r]));
-        setpr(dkn[0][j], hf, add2(pr(dkn[0][j], hf), y));
-        setpr(dG[0][j], hf, fma2(neg2(kn), y, pr(dG[0][j], hf)));
-      }
     if (!safe) {
       // exact diagonal block, off-diagonal pairs only
 #pragma unroll
@@ -649,21 +662,15 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     for (int hf = 0; hf < 2; ++hf) {
       const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
       if (r >= len || cl >= K) continue;
-      float oq[2], ok[2];
-      const float2 q2 = ld2<T>(sq + r * LDK + cl), k2 = ld2<T>(sk + r * LDK + cl);
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int e = 2 * hf + t;
-        float vq = dq[0][j][e], vk = dkn[0][j][e];
-        if (a.l2norm) {
-          vq = (vq - sel2(q2, t) * rq[r] * dotq[hf]) * rq[r];
-          vk = (vk - sel2(k2, t) * rk[r] * dotk[hf]) * rk[r];
-        }
-        oq[t] = vq;
-        ok[t] = vk;
+      float2 oq = pr(dq[0][j], hf), ok = pr(dkn[0][j], hf);
+      if (a.l2norm) {
+        const float2 q2 = ld2<T>(sq + r * LDK + cl), k2 = ld2<T>(sk + r * LDK + cl);
+        const float2 nq = f2(rq[r]), nk = f2(rk[r]);
+        oq = mul2(fma2(neg2(mul2(q2, nq)), f2(dotq[hf]), oq), nq);
+        ok = mul2(fma2(neg2(mul2(k2, nk)), f2(dotk[hf]), ok), nk);
       }
-      *reinterpret_cast<uint32_t*>(stq + r * LDK + cl) = pack2<T>(oq[0], oq[1]);
-      *reinterpret_cast<uint32_t*>(stk + r * LDK + cl) = pack2<T>(ok[0], ok[1]);
+      *reinterpret_cast<uint32_t*>(stq + r * LDK + cl) = pack2<T>(oq.x, oq.y);
+      *reinterpret_cast<uint32_t*>(stk + r * LDK + cl) = pack2<T>(ok.x, ok.y);
       *reinterpret_cast<uint32_t*>(stb + r * LDK + cl) =
           pack2<T>(dkb[0][j][2 * hf], dkb[0][j][2 * hf + 1]);
     }
