@@ -226,24 +226,22 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
     warp_mma16<1, NTO, false, true>(accW, dvns, LDT, 16 * wr, hs, LDS, wc * DQ, 32);
     warp_mma16<1, 2, true, false>(accAqk, dos, LDS, 16 * wr, vns, LDT, 16 * wc, 32);
     warp_mma16<1, 2, false, true>(accDA, dvns, LDT, 16 * wr, sZ, LDS, 16 * wc, 32);
-    if (warp < 8) {
-      float accZ[1][2][4];
-      acc_zero(accZ);
-      const int zm = 16 * (warp & 3), zn = 16 * (warp >> 2);
-      warp_mma16<1, 2, false, true>(accZ, sA, LDC, zm, dvns, LDT, zn, kChunk);
+    {
+      // Z = A^T dVN (64 tokens x the slice's 32 columns): a 16 x 8 tile per warp
+      float accZ[4] = {0.f, 0.f, 0.f, 0.f};
+      const int zm = 16 * (warp & 3), zn = 8 * (warp >> 2);
+      warp_mma16_n8<false>(accZ, sA, LDC, zm, dvns, LDT, zn, kChunk);
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const int r = zm + gid + 8 * hf, cl = zn + 8 * j + 2 * tig;
-          if (r < len && cl < nv) {
-            const float2 z2 = pr(accZ[0][j], hf);
-            const float2 dv2 = mul2(z2, ld2<T>(ws + r * LDS + cl));
-            const float2 dw2 = mul2(z2, ld2<T>(vs + r * LDS + cl));
-            *reinterpret_cast<uint32_t*>(gdv + r * ldv + v0 + cl) = pack2<T>(dv2.x, dv2.y);
-            *reinterpret_cast<uint32_t*>(gdw + r * ldv + v0 + cl) = pack2<T>(dw2.x, dw2.y);
-          }
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = zm + gid + 8 * hf, cl = zn + 2 * tig;
+        if (r < len && cl < nv) {
+          const float2 z2 = pr(accZ, hf);
+          const float2 dv2 = mul2(z2, ld2<T>(ws + r * LDS + cl));
+          const float2 dw2 = mul2(z2, ld2<T>(vs + r * LDS + cl));
+          *reinterpret_cast<uint32_t*>(gdv + r * ldv + v0 + cl) = pack2<T>(dv2.x, dv2.y);
+          *reinterpret_cast<uint32_t*>(gdw + r * ldv + v0 + cl) = pack2<T>(dw2.x, dw2.y);
         }
+      }
     }
   }
   __syncthreads();  // phase V buffers are dead from here on; q, k, b, g have landed
@@ -276,10 +274,13 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
 #pragma unroll
   for (int j = 0; j < 2; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int r = 16 * wr + gid + ((e >> 1) << 3), i = 16 * wc + 8 * j + 2 * tig + (e & 1);
-      sDAqk[r * LDC + i] = from_f<T>(i < r ? accAqk[0][j][e] : 0.f);
-      if (i == r) sDiag[r] = accAqk[0][j][e];
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = 16 * wr + gid + 8 * hf, i0 = 16 * wc + 8 * j + 2 * tig;
+      const float x0 = accAqk[0][j][2 * hf], x1 = accAqk[0][j][2 * hf + 1];
+      *reinterpret_cast<uint32_t*>(sDAqk + r * LDC + i0) =
+          pack2<T>(i0 < r ? x0 : 0.f, i0 + 1 < r ? x1 : 0.f);
+      if (i0 == r) sDiag[r] = x0;
+      if (i0 + 1 == r) sDiag[r] = x1;
     }
   // E = b * k_n * 2^G
   for (int i = tid; i < kChunk * (D / 2); i += NTH) {
@@ -318,9 +319,10 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
 #pragma unroll
     for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = 16 * wr + gid + ((e >> 1) << 3), i = 16 * wc + 8 * j + 2 * tig + (e & 1);
-        sDAkk[r * LDC + i] = from_f<T>(i < r ? -t[0][j][e] : 0.f);
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = 16 * wr + gid + 8 * hf, i0 = 16 * wc + 8 * j + 2 * tig;
+        *reinterpret_cast<uint32_t*>(sDAkk + r * LDC + i0) =
+            pack2<T>(i0 < r ? -t[0][j][2 * hf] : 0.f, i0 + 1 < r ? -t[0][j][2 * hf + 1] : 0.f);
       }
   }
   // dE = A^T dW (owner tile)

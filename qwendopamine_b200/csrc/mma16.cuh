@@ -31,6 +31,12 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
                : "r"(smem_u32(p)));
 }
 
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(smem_u32(p)));
+}
+
 template <typename T> struct Mma16;
 template <> struct Mma16<__nv_bfloat16> {
   static __device__ __forceinline__ void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
@@ -102,6 +108,22 @@ __device__ __forceinline__ void warp_mma16(float (&acc)[MT][NT][4], const T* A, 
         Mma16<T>::run(acc[i][j + 1], a[i], b[2], b[3]);
       }
     }
+  }
+}
+
+// acc (16 x 8) += A[rows m0.., k 0..kd) * B[k 0..kd, cols n0..n0+7) with B
+// K-major (row n holds B[., n]): one n8 tile per warp.
+template <bool A_KMAJOR, typename T>
+__device__ __forceinline__ void warp_mma16_n8(float (&acc)[4], const T* A, int lda, int m0,
+                                              const T* B, int ldb, int n0, int kd) {
+  const int lane = threadIdx.x & 31;
+  const int rr = lane & 7, kh = (lane >> 3) & 1;
+#pragma unroll
+  for (int k0 = 0; k0 < kd; k0 += 16) {
+    uint32_t a[4], b[2];
+    load_a16<A_KMAJOR>(a, A, lda, m0, k0);
+    ldsm_x2(b, B + (n0 + rr) * ldb + k0 + 8 * kh);
+    Mma16<T>::run(acc, a, b[0], b[1]);
   }
 }
 
