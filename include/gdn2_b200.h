@@ -312,7 +312,9 @@ int gdn2_gated_norm_bwd(const gdn2_norm_problem* p, const void* x, const void* z
 /* Device-side fault bits.  Kernels that wait on asynchronous copies or on
  * tensor-core completion bound every wait in time (about one second); a wait
  * that runs out makes the kernel release its tensor memory, return without
- * finishing, and set bit 0 of a per-device fault word.  gdn2_fault_status
+ * finishing, and set a bit of a per-device fault word (bit 0: state passes,
+ * bit 1: forward intra-chunk kernel, bit 2: decode, bit 3: backward
+ * intra-chunk kernel).  gdn2_fault_status
  * synchronises `stream` (the default stream when NULL), returns the fault
  * word of the current device (0 = no fault) and resets it when `clear` is
  * nonzero; a negative return is a CUDA error.  No counterpart in the

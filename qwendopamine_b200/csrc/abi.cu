@@ -439,6 +439,7 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.ws = static_cast<const unsigned char*>(workspace);
   a.BL = BL;
   a.dq = dq; a.dk = dk; a.dv = dv; a.dg = dg; a.db = db; a.dw = dw;
+  a.total_rows = p->seqs.total_tokens;
   cudaError_t e = fault_word(&a.fault);
   if (e != cudaSuccess) return cuda_fail(e, "gdn2_chunk_bwd_intra");
   e = bwd_intra_dispatch(p, a, (cudaStream_t)stream);

@@ -2,10 +2,12 @@
 //
 // One CTA of 16 warps per (chunk, head).  Same mathematics as k_bwd_intra
 // (chunk_bwd.cu), organised so that almost nothing waits on memory:
-//   * one cp.async round trip brings q, k, b (16-bit), g (fp32) and A;
+//   * every tile arrives by TMA, requested by one thread (issuing the copies
+//     thread by thread with cp.async kept the CTA waiting on the load queue):
+//     q, k, b (16-bit), g (fp32) and A once;
 //   * the value side streams 32-column slices of h, dh, dO, VN, dVN, v, w
 //     (VN and dVN are stored value-major, [V][64], by the bf16 state passes)
-//     through a cp.async double buffer while the previous slice computes
+//     through a two-slot buffer while the previous slice computes
 //     (dQg = dO h^T, dKd = VN dh^T, dW = -dVN h^T, dAqk = dO VN^T,
 //      dA = dVN (w v)^T, dZ = A^T dVN -> dv, dw);
 //   * the key side needs no further loads.  Each warp owns a 16-row x D/4
@@ -19,6 +21,7 @@
 // scan of the Kd terms.
 #include "chunk_args.cuh"
 #include "mma16.cuh"
+#include "tc.cuh"
 
 namespace gdn2 {
 
@@ -39,9 +42,9 @@ struct Bwd16Layout {
   static constexpr int oA = oG + kChunk * LDG * 4;
   static constexpr int oMisc = oA + kChunk * LDC * 2;
   // misc floats: rq[64] rk[64] dgl[D] diag[64] pdq[4][64] pdk[4][64] flag[4] F[10][D]
-  //              dApart[16]
+  //              dApart[16], then 3 mbarriers (as 6 floats, 8-byte aligned)
   static constexpr int nMisc = 64 + 64 + D + 64 + 256 + 256 + 4 + 10 * D + 16;
-  static constexpr int oW = oMisc + nMisc * 4;
+  static constexpr int oW = (oMisc + nMisc * 4 + 3 * 8 + 127) / 128 * 128;  // TMA targets: 128-B
   // phase V (offsets inside W)
   static constexpr int vH = 0;
   static constexpr int vDH = vH + D * LDS * 2;
@@ -71,21 +74,35 @@ struct Bwd16Layout {
   static constexpr int kScanEnd = kTmp + 2 * kThreadsB16 * 4;
   static constexpr int W = phaseV > kEnd ? (phaseV > kScanEnd ? phaseV : kScanEnd)
                                          : (kEnd > kScanEnd ? kEnd : kScanEnd);
-  static constexpr size_t bytes = (size_t)oW + W;
+  static constexpr size_t bytes = (size_t)oW + W + 128;  // + base alignment slack
   static_assert(kT2 + kChunk * LDC * 2 <= kEnd || kT2 + kChunk * LDC * 2 <= W, "layout");
-  static_assert(oW % 16 == 0 && slot % 16 == 0, "alignment");
+  static_assert(oW % 128 == 0 && slot % 128 == 0 && oK % 128 == 0 && oB % 128 == 0 &&
+                    oG % 128 == 0 && oA % 128 == 0 && vDH % 128 == 0 && vDO % 128 == 0 &&
+                    vVN % 128 == 0 && vDVN % 128 == 0 && vV % 128 == 0 && vWg % 128 == 0,
+                "TMA destinations are 128-byte aligned");
+  static_assert((oMisc + nMisc * 4) % 8 == 0, "mbarrier alignment");
   static_assert(32 * LDT <= kChunk * LDS, "VN^T slice fits its region");
   static_assert(3 * kChunk * LDK * 2 <= W, "gradient staging fits the work region");
 };
 
+// TMA views of every tile the kernel reads (built per launch on the host).
+struct Bwd16Maps {
+  CUtensorMap q, k, b, g;       // [rows][H][K] token rows (g fp32)
+  CUtensorMap a, h, dh;         // per (chunk, head): A [64][64], h / dh [K][V]
+  CUtensorMap dout, v, w;       // [rows][H][V] token rows
+  CUtensorMap vn, dvn;          // per (chunk, head): VN / dVN stored [V][64]
+};
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) {
+__global__ void __launch_bounds__(kThreadsB16, 1)
+    k_bwd_intra16(BwdIntraArgs a, const __grid_constant__ Bwd16Maps mp) {
   using L = Bwd16Layout<D>;
   constexpr int LDK = L::LDK, LDG = L::LDG, LDC = L::LDC, LDS = L::LDS, LDT = L::LDT;
   constexpr int NTH = kThreadsB16;
   constexpr int DQ = D / 4;    // owner tile width
   constexpr int NTO = DQ / 8;  // n8 fragments per owner tile
-  extern __shared__ __align__(16) unsigned char sm[];
+  extern __shared__ unsigned char smraw[];
+  unsigned char* sm = smraw + ((128u - (smem_u32(smraw) & 127u)) & 127u);
   T* sq = reinterpret_cast<T*>(sm + L::oQ);
   T* sk = reinterpret_cast<T*>(sm + L::oK);
   T* sb = reinterpret_cast<T*>(sm + L::oB);
@@ -101,6 +118,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   int* sFlag = reinterpret_cast<int*>(pdk + 256);
   float* sF = pdk + 256 + 4;  // [10][D] 2^(G_16I - G_(16J+15)), pair I(I+1)/2 + J
   float* sDApart = sF + 10 * D;  // [16] per-warp dL/dA_log partial sums (gate in kernel)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDApart + 16);  // [0], [1] slots, [2] q k b g
   unsigned char* W = sm + L::oW;
 
   const int c = blockIdx.x, h = blockIdx.y;
@@ -116,55 +134,85 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   const size_t ch = (size_t)c * H + h;
   const float scale = a.scale;
 
-  const T* gh = reinterpret_cast<const T*>(a.saved + a.L.h) + ch * (size_t)K * V;
-  const T* gdh = reinterpret_cast<const T*>(a.ws + a.BL.dh) + ch * (size_t)K * V;
-  const T* gvn = reinterpret_cast<const T*>(a.saved + a.L.vn) + ch * (size_t)kChunk * V;
-  const T* gdvn = reinterpret_cast<const T*>(a.ws + a.BL.dvn) + ch * (size_t)kChunk * V;
-  const T* gdo = reinterpret_cast<const T*>(a.dout) + offv;
-  const T* gv = reinterpret_cast<const T*>(a.v) + offv;
-  const T* gw = reinterpret_cast<const T*>(a.w) + offv;
-
+  // Every tile arrives by TMA (one thread issues, the others keep computing)
+  // as a box whose rows are as wide as the padded shared-memory rows, so the
+  // pad columns come along (or read as zero past the tensor's edge).  Slices
+  // of the value side complete on the mbarrier of their slot, q, k, b, g on
+  // a third.  Rows past a partial chunk's end hold the next sequence's
+  // tokens and are zeroed after landing.
+  const int nslices = (V + 31) / 32;
+  const int crow = (int)cp.row0;
+  const uint32_t txSlice = (uint32_t)(2 * LDS * 2 * K + 3 * LDS * 2 * kChunk + 2 * LDT * 2 * 32);
+  const uint32_t txA = (uint32_t)(LDC * 2 * kChunk);
+  const uint32_t txKey = (uint32_t)(3 * LDK * 2 * kChunk + LDG * 4 * kChunk);
   auto slotp = [&](int s, int off) { return reinterpret_cast<T*>(W + s * L::slot + off); };
-  auto issue_slice = [&](int v0, int s) {
-    const int nv = min(32, V - v0);
-    cp_tile16<T, D, 32, NTH>(slotp(s, L::vH), LDS, gh + v0, V, K, nv);
-    cp_tile16<T, D, 32, NTH>(slotp(s, L::vDH), LDS, gdh + v0, V, K, nv);
-    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vDO), LDS, gdo + v0, ldv, len, nv);
-    cp_tile16<T, 32, kChunk, NTH>(slotp(s, L::vVN), LDT, gvn + (size_t)v0 * kChunk, kChunk, nv,
-                                  kChunk);
-    cp_tile16<T, 32, kChunk, NTH>(slotp(s, L::vDVN), LDT, gdvn + (size_t)v0 * kChunk, kChunk, nv,
-                                  kChunk);
-    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vV), LDS, gv + v0, ldv, len, nv);
-    cp_tile16<T, kChunk, 32, NTH>(slotp(s, L::vWg), LDS, gw + v0, ldv, len, nv);
+  auto issue_slice = [&](int v0, int s) {  // thread 0
+    tc::tma_load_2d(slotp(s, L::vH), &mp.h, v0, (int)ch * K, &bars[s]);
+    tc::tma_load_2d(slotp(s, L::vDH), &mp.dh, v0, (int)ch * K, &bars[s]);
+    tc::tma_load_3d(slotp(s, L::vDO), &mp.dout, v0, h, crow, &bars[s]);
+    tc::tma_load_2d(slotp(s, L::vVN), &mp.vn, 0, (int)ch * V + v0, &bars[s]);
+    tc::tma_load_2d(slotp(s, L::vDVN), &mp.dvn, 0, (int)ch * V + v0, &bars[s]);
+    tc::tma_load_3d(slotp(s, L::vV), &mp.v, v0, h, crow, &bars[s]);
+    tc::tma_load_3d(slotp(s, L::vWg), &mp.w, v0, h, crow, &bars[s]);
   };
-
   // The value side needs only A and the value slices; q, k, b, g (key side)
-  // ride along with the next-slice copies (q with slice 1, k and b with
+  // are requested after the next-slice copies (q with slice 1, k and b with
   // slice 2, g with slice 3; all remaining ones with the last) so their
   // latency hides behind the value-side products.
-  auto issue_key_part = [&](int part) {
+  auto issue_key_part = [&](int part) {  // thread 0
     if (part == 0) {
-      cp_tile16<T, kChunk, D, NTH>(sq, LDK, reinterpret_cast<const T*>(a.q) + offk, ldk, len, K);
+      tc::tma_load_3d(sq, &mp.q, 0, h, crow, &bars[2]);
     } else if (part == 1) {
-      cp_tile16<T, kChunk, D, NTH>(sk, LDK, reinterpret_cast<const T*>(a.k) + offk, ldk, len, K);
-      cp_tile16<T, kChunk, D, NTH>(sb, LDK, reinterpret_cast<const T*>(a.b) + offk, ldk, len, K);
+      tc::tma_load_3d(sk, &mp.k, 0, h, crow, &bars[2]);
+      tc::tma_load_3d(sb, &mp.b, 0, h, crow, &bars[2]);
     } else {
-      cp_tile32<kChunk, D, NTH>(sG, LDG, a.g + offk, ldk, len, K);
+      tc::tma_load_3d(sG, &mp.g, 0, h, crow, &bars[2]);
+    }
+  };
+  // rows [r0, r1) of a tile of 16-byte-multiple rows (generic-proxy zeros)
+  auto zero_rows = [&](void* t, int row_bytes, int r0, int r1) {
+    const int n16 = row_bytes / 16;
+    for (int e = tid; e < (r1 - r0) * n16; e += NTH) {
+      const int r = r0 + e / n16, c = e - (e / n16) * n16;
+      reinterpret_cast<uint4*>(static_cast<unsigned char*>(t) + (size_t)r * row_bytes)[c] =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  // A wait that ran out: let the copies still in flight land (bounded),
+  // flag the fault and leave.
+  // (slices 0 .. last_slice have been requested; slice t fills slot t & 1 in
+  // that slot's phase t >> 1)
+  auto drain = [&](int last_slice) {
+    if (tid == 0) {
+      for (int t = last_slice > 1 ? last_slice - 1 : 0; t <= last_slice; ++t)
+        tc::mbar_wait(&bars[t & 1], (t >> 1) & 1);
+      tc::mbar_wait(&bars[2], 0);
+      atomicOr(a.fault, 8u);
     }
   };
 
   // ---- phase 0: A and the first slice --------------------------------------
-  cp_tile16<T, kChunk, kChunk, NTH>(
-      sA, LDC, reinterpret_cast<const T*>(a.saved + a.L.a) + ch * kChunk * kChunk, kChunk, kChunk,
-      kChunk);
-  issue_slice(0, 0);
-  cp_async_commit();
-  const int nslices = (V + 31) / 32;
-  if (nslices == 1) {
-    for (int part = 0; part < 3; ++part) issue_key_part(part);
-    cp_async_commit();
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) tc::mbar_init(&bars[i], 1);
+    tc::fence_mbar_init();
+  }
+  if (K < D) {  // h / dh rows past K are never loaded
+    for (int sl = 0; sl < 2; ++sl) {
+      zero_rows(slotp(sl, L::vH), LDS * 2, K, D);
+      zero_rows(slotp(sl, L::vDH), LDS * 2, K, D);
+    }
   }
   for (int i = tid; i < D; i += NTH) dgl[i] = 0.f;
+  tc::fence_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tc::mbar_expect_tx(&bars[2], txKey);
+    tc::mbar_expect_tx(&bars[0], txSlice + txA);
+    tc::tma_load_2d(sA, &mp.a, 0, (int)ch * kChunk, &bars[0]);
+    issue_slice(0, 0);
+    if (nslices == 1)
+      for (int part = 0; part < 3; ++part) issue_key_part(part);
+  }
 
   // ---- phase V --------------------------------------------------------------
   float accQ[1][NTO][4], accKd[1][NTO][4], accW[1][NTO][4], accAqk[1][2][4], accDA[1][2][4];
@@ -179,19 +227,34 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
   for (int s = 0; s < nslices; ++s) {
     const int cur = s & 1, v0 = 32 * s, nv = min(32, V - v0);
     if (s + 1 < nslices) {
-      __syncthreads();  // the other slot's last readers are done
-      issue_slice(v0 + 32, cur ^ 1);
-      if (s + 2 == nslices) {
-        for (int part = s; part < 3; ++part) issue_key_part(part);
-      } else if (s < 3) {
-        issue_key_part(s);
+      tc::fence_async_smem();
+      __syncthreads();  // the other slot's last readers (and zeroing writers) are done
+      if (tid == 0) {
+        tc::mbar_expect_tx(&bars[cur ^ 1], txSlice);
+        issue_slice(v0 + 32, cur ^ 1);
+        if (s + 2 == nslices) {
+          for (int part = s; part < 3; ++part) issue_key_part(part);
+        } else if (s < 3) {
+          issue_key_part(s);
+        }
       }
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
     }
-    __syncthreads();
+    if (__syncthreads_or(!tc::mbar_wait(&bars[cur], (s >> 1) & 1))) {
+      drain(s + 1 < nslices ? s + 1 : s);
+      return;
+    }
+    if (len < kChunk || nv < 32) {
+      if (len < kChunk) {
+        zero_rows(slotp(cur, L::vDO), LDS * 2, len, kChunk);
+        zero_rows(slotp(cur, L::vV), LDS * 2, len, kChunk);
+        zero_rows(slotp(cur, L::vWg), LDS * 2, len, kChunk);
+      }
+      if (nv < 32) {  // VN / dVN rows past the last value column belong to the next head
+        zero_rows(slotp(cur, L::vVN), LDT * 2, nv, 32);
+        zero_rows(slotp(cur, L::vDVN), LDT * 2, nv, 32);
+      }
+      __syncthreads();
+    }
     T* hs = slotp(cur, L::vH);
     T* dhs = slotp(cur, L::vDH);
     T* dos = slotp(cur, L::vDO);
@@ -244,7 +307,18 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
       }
     }
   }
-  __syncthreads();  // phase V buffers are dead from here on; q, k, b, g have landed
+  // phase V buffers are dead from here on; q, k, b, g have landed
+  if (__syncthreads_or(!tc::mbar_wait(&bars[2], 0))) {
+    drain(nslices - 1);
+    return;
+  }
+  if (len < kChunk) {
+    zero_rows(sq, LDK * 2, len, kChunk);
+    zero_rows(sk, LDK * 2, len, kChunk);
+    zero_rows(sb, LDK * 2, len, kChunk);
+    zero_rows(sG, LDG * 4, len, kChunk);
+    __syncthreads();
+  }
   if (a.gate.mode) {  // gate in kernel: raw input -> log-decay (valid rows / channels)
     for (int i = tid; i < kChunk * D; i += NTH) {
       const int r = i / D, cc = i - r * D;
@@ -282,6 +356,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
       if (i0 == r) sDiag[r] = x0;
       if (i0 + 1 == r) sDiag[r] = x1;
     }
+  __syncthreads();  // every warp's row norms are in (the E pass reads all rows)
   // E = b * k_n * 2^G
   for (int i = tid; i < kChunk * (D / 2); i += NTH) {
     const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
@@ -684,15 +759,44 @@ __global__ void __launch_bounds__(kThreadsB16, 1) k_bwd_intra16(BwdIntraArgs a) 
 
 template <typename T, int D>
 cudaError_t launch_bwd_intra16(const BwdIntraArgs& a, cudaStream_t st) {
+  using L = Bwd16Layout<D>;
   auto kern = k_bwd_intra16<T, D>;
+  const uint64_t nch = (uint64_t)a.seqs.n_chunks, H = (uint64_t)a.H, K = (uint64_t)a.K,
+                 V = (uint64_t)a.V, rows = (uint64_t)a.total_rows;
+  if (nch == 0 || H == 0) return cudaSuccess;
+  // TMA coordinates are 32-bit
+  const uint64_t lim = (uint64_t)1 << 31;
+  if (rows >= lim || nch * H * (K > V ? K : V) >= lim || nch * H * kChunk >= lim)
+    return cudaErrorInvalidValue;
+  Bwd16Maps m;
+  const uint64_t dK[3] = {K, H, rows}, sK[2] = {K * 2, H * K * 2}, sG[2] = {K * 4, H * K * 4};
+  const uint64_t dV[3] = {V, H, rows}, sV[2] = {V * 2, H * V * 2};
+  const uint32_t bK[3] = {(uint32_t)L::LDK, 1, kChunk}, bG[3] = {(uint32_t)L::LDG, 1, kChunk};
+  const uint32_t bV[3] = {(uint32_t)L::LDS, 1, kChunk};
+  const uint64_t dH[2] = {V, nch * H * K}, sH[1] = {V * 2};
+  const uint32_t bH[2] = {(uint32_t)L::LDS, (uint32_t)K};
+  const uint64_t dVN[2] = {kChunk, nch * H * V}, dA[2] = {kChunk, nch * H * kChunk};
+  const uint64_t s64[1] = {kChunk * 2};
+  const uint32_t bVN[2] = {(uint32_t)L::LDT, 32}, bA[2] = {(uint32_t)L::LDC, kChunk};
+  const unsigned char* sv = a.saved;
+  const unsigned char* wv = a.ws;
+  if (!tmap_plain(&m.q, a.q, 3, dK, sK, bK, 2) || !tmap_plain(&m.k, a.k, 3, dK, sK, bK, 2) ||
+      !tmap_plain(&m.b, a.b, 3, dK, sK, bK, 2) || !tmap_plain(&m.g, a.g, 3, dK, sG, bG, 4) ||
+      !tmap_plain(&m.dout, a.dout, 3, dV, sV, bV, 2) || !tmap_plain(&m.v, a.v, 3, dV, sV, bV, 2) ||
+      !tmap_plain(&m.w, a.w, 3, dV, sV, bV, 2) ||
+      !tmap_plain(&m.h, sv + a.L.h, 2, dH, sH, bH, 2) ||
+      !tmap_plain(&m.dh, wv + a.BL.dh, 2, dH, sH, bH, 2) ||
+      !tmap_plain(&m.vn, sv + a.L.vn, 2, dVN, s64, bVN, 2) ||
+      !tmap_plain(&m.dvn, wv + a.BL.dvn, 2, dVN, s64, bVN, 2) ||
+      !tmap_plain(&m.a, sv + a.L.a, 2, dA, s64, bA, 2))
+    return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)Bwd16Layout<D>::bytes);
+                                       (int)L::bytes);
   if (e != cudaSuccess) return e;
   dim3 grid(a.seqs.n_chunks, a.H);
-  kern<<<grid, kThreadsB16, Bwd16Layout<D>::bytes, st>>>(a);
+  kern<<<grid, kThreadsB16, L::bytes, st>>>(a, m);
   return cudaGetLastError();
 }
-
 template cudaError_t launch_bwd_intra16<__nv_bfloat16, 64>(const BwdIntraArgs&, cudaStream_t);
 template cudaError_t launch_bwd_intra16<__nv_bfloat16, 128>(const BwdIntraArgs&, cudaStream_t);
 

@@ -113,6 +113,7 @@ struct BwdIntraArgs {
   void* db;
   void* dw;
   unsigned int* fault;  // device fault word (bounded waits that ran out)
+  int64_t total_rows;   // token rows of q, k, v, g, b, w, dout (bounds of their TMA views)
 };
 
 struct RecArgs {

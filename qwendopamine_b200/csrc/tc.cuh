@@ -205,6 +205,12 @@ bool tmap_2d_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t row
                   bool swizzle);
 // 3-D map over token rows [rows][H][D] of 2- or 4-byte elements: box box_x
 // columns (128 bytes) x 1 head x 64 rows, 128-byte swizzle.
+// Unswizzled 2-D or 3-D map (dims innermost first, strides of the outer
+// dimensions in bytes): a box lands in shared memory densely, so a box wider
+// than the data it needs gives padded rows; elements outside the tensor read
+// as zero.
+bool tmap_plain(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, int elem_bytes);
 bool tmap_rows(CUtensorMap* m, const void* base, uint64_t D, uint64_t H, uint64_t rows,
                uint32_t box_x, int elem_bytes);
 

@@ -60,4 +60,21 @@ bool tmap_rows(CUtensorMap* m, const void* base, uint64_t D, uint64_t H, uint64_
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool tmap_plain(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, int elem_bytes) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc || rank < 2 || rank > 3) return false;
+  cuuint64_t d[3], st[2];
+  cuuint32_t bx[3], estr[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  return enc(m, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+             (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace gdn2

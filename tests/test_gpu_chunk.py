@@ -319,6 +319,59 @@ def test_backward_is_deterministic(cuda_device):
         assert torch.equal(g1[n], g2[n]), n
 
 
+def test_backward_16bit_rows_of_varied_norm(cuda_device):
+    """q / k rows whose norms span two decades (normalised in the kernel), on
+    enough chunks that every SM runs several CTAs one after another: the bf16
+    gradients follow the fp64 oracle and repeat bit for bit.  A row norm read
+    before the warp that owns the row has written it picks up another CTA's
+    value, which this case turns into a large, run-dependent error."""
+    B, T, H, K, V = 4, 512, 8, 128, 128  # 256 (chunk, head) CTAs
+    d = make_inputs(B, T, H, K, V, seed=77, dtype=torch.bfloat16, h0=False)
+    gen = torch.Generator().manual_seed(78)
+    for n in ("q", "k"):
+        row_scale = 10.0 ** (2.0 * torch.rand(B, T, H, 1, generator=gen) - 1.0)
+        d[n] = (d[n] * row_scale).bfloat16().float()
+    do = torch.randn(B, T, H, V, generator=gen).bfloat16().float()
+    dht = torch.zeros(B, H, K, V)
+    g1 = _grads(d, cuda_device, torch.bfloat16, do, dht)
+    ref = O.recurrent_bwd(*np_(d, NAMES), do.numpy(), None, None, norm_mode="fla")
+    for n, r in zip(NAMES, ref):
+        assert rel(g1[n], r) < TOL[torch.bfloat16], n
+
+
+def test_backward_16bit_repeats_bit_for_bit_at_config1_size(cuda_device):
+    """Config-1 shapes (8192 (chunk, head) CTAs, dozens per SM) with row norms
+    spanning two decades: two forward + backward passes give identical
+    outputs and gradients."""
+    from qwendopamine_b200 import chunk_gdn2
+
+    B, T, H, K, V = 8, 4096, 16, 128, 128
+    gen = torch.Generator(device=cuda_device).manual_seed(5)
+
+    def rnd(*shape):
+        return torch.randn(*shape, device=cuda_device, generator=gen)
+
+    def spread(x):
+        return x * 10.0 ** (2.0 * torch.rand(B, T, H, 1, device=cuda_device, generator=gen) - 1.0)
+
+    q = spread(rnd(B, T, H, K)).bfloat16()
+    k = spread(rnd(B, T, H, K)).bfloat16()
+    v = rnd(B, T, H, V).bfloat16()
+    b = torch.sigmoid(rnd(B, T, H, K)).bfloat16()
+    w = torch.sigmoid(rnd(B, T, H, V)).bfloat16()
+    g = F.logsigmoid(rnd(B, T, H, 1) + 3.0).expand(B, T, H, K).contiguous()
+    do = rnd(B, T, H, V).bfloat16()
+    runs = []
+    for _ in range(2):
+        leaves = [t.clone().requires_grad_() for t in (q, k, v, g, b, w)]
+        o, _ = chunk_gdn2(*leaves, use_qk_l2norm_in_kernel=True)
+        o.backward(do)
+        runs.append([o.detach()] + [t.grad for t in leaves])
+        del leaves, o
+    for n, x, y in zip(("o", *NAMES), *runs):
+        assert torch.equal(x, y), n
+
+
 @pytest.mark.parametrize("B,T,H,K,V", [
     (10, 70, 16, 128, 128),   # >= 148 sequence-heads: 128-column state tiles
     (3, 150, 4, 64, 64),      # 64-wide head bucket
