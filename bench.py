@@ -89,7 +89,7 @@ STEP_MIN_BYTES = 6900
 # token-head, from one ncu --set full capture at batch 2 (701.3 MB over
 # 131,072 token-heads; traffic grows with token-heads, so it scales to a
 # config-1 launch).  Summary under profiles/.
-NCU_TRAFFIC_PER_TOKEN_HEAD = 5342.0
+NCU_TRAFFIC_PER_TOKEN_HEAD = 5309.6
 
 
 def peaks():
