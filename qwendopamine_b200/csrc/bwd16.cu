@@ -30,7 +30,7 @@ constexpr int kThreadsB16 = 512;
 template <int D>
 struct Bwd16Layout {
   static constexpr int LDK = D + 8;      // 16-bit 64 x D tiles
-  static constexpr int LDG = D + 4;      // fp32 64 x D tiles
+  static constexpr int LDG = D + 8;      // fp32 64 x D tiles (8-byte pairs conflict-free)
   static constexpr int LDC = kChunk + 8; // 16-bit 64 x 64 tiles
   static constexpr int LDS = 32 + 8;     // 16-bit value slices
   static constexpr int LDT = kChunk + 8; // 16-bit VN^T / dVN^T slices [32][64]
