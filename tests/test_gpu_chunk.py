@@ -449,6 +449,27 @@ def test_ragged_lengths_16bit_forward_backward(cuda_device, T, KV):
         assert rel(gr[n], r) < TOL[torch.bfloat16], n
 
 
+@pytest.mark.parametrize("KV", [(96, 72), (32, 40), (128, 104), (40, 128)])
+def test_uneven_head_sizes_16bit_forward_backward(cuda_device, KV):
+    """bf16 head sizes that fill neither the kernels' 64 / 128-wide tiles nor
+    whole 32-column value slices (key rows past K, value columns past V and
+    the last slice's short rows come from zero fill), with a partial chunk."""
+    K, V = KV
+    d = make_inputs(2, 130, 3, K, V, seed=K * 7 + V, dtype=torch.bfloat16)
+    o, ht = _chunk(d, cuda_device, torch.bfloat16)
+    ro, rh = O.recurrent_fwd(*np_(d, NAMES), d["h0"].numpy(), norm_mode="fla")
+    assert rel(o, ro) < TOL[torch.bfloat16], "o"
+    assert rel(ht, rh) < TOL[torch.bfloat16], "ht"
+    gen = torch.Generator().manual_seed(K + V)
+    do = torch.randn(2, 130, 3, V, generator=gen).bfloat16().float()
+    dht = torch.randn(2, 3, K, V, generator=gen)
+    gr = _grads(d, cuda_device, torch.bfloat16, do, dht)
+    ref = O.recurrent_bwd(*np_(d, NAMES), do.numpy(), d["h0"].numpy(), dht.numpy(),
+                          norm_mode="fla")
+    for n, r in zip((*NAMES, "h0"), ref):
+        assert rel(gr[n], r) < TOL[torch.bfloat16], n
+
+
 def test_misaligned_16bit_views_give_the_same_result(cuda_device):
     """Views that do not start on a 16-byte boundary are copied by the wrapper
     before the bulk-copy kernels see them."""
