@@ -357,6 +357,8 @@ int gdn2_chunk_fwd_state(const gdn2_chunk_problem* p, const float* h0, void* o, 
   if (saved_bytes < L.total)
     return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_fwd_state: saved buffer %zu < %zu bytes",
                 saved_bytes, L.total);
+  rc = check_aligned16(p, "gdn2_chunk_fwd_state", {h0, o, ht, saved});
+  if (rc) return rc;
   FwdStateArgs a;
   a.seqs = make_seqs(p);
   a.H = p->H; a.K = p->K; a.V = p->V;
@@ -392,6 +394,8 @@ int gdn2_chunk_bwd_state(const gdn2_chunk_problem* p, const void* saved, size_t 
     return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_bwd_state: workspace %zu < %zu bytes",
                 workspace_bytes, BL.total);
   if (p->seqs.n_seqs == 0) return GDN2_OK;
+  rc = check_aligned16(p, "gdn2_chunk_bwd_state", {saved, dout, dht, dh0, workspace});
+  if (rc) return rc;
   BwdStateArgs s;
   s.seqs = make_seqs(p);
   s.H = p->H; s.K = p->K; s.V = p->V;
@@ -424,7 +428,8 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
     return fail(GDN2_ERR_WORKSPACE, "gdn2_chunk_bwd_intra: workspace %zu < %zu bytes",
                 workspace_bytes, BL.total);
   if (p->seqs.n_chunks == 0) return GDN2_OK;
-  rc = check_aligned16(p, "gdn2_chunk_bwd_intra", {q, k, v, g, b, w, saved, dout, workspace});
+  rc = check_aligned16(p, "gdn2_chunk_bwd_intra",
+                       {q, k, v, g, b, w, saved, dout, workspace, dq, dk, dv, dg, db, dw});
   if (rc) return rc;
   BwdIntraArgs a;
   a.seqs = make_seqs(p);

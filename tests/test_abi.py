@@ -103,6 +103,17 @@ def test_misaligned_16bit_tensors_are_rejected(lib):
     rc = lib.gdn2_chunk_bwd_intra(prob, ok, ok, ok, ok, ok, ok, ok, big, odd, *([ok] * 6), ok, big,
                                   None)
     assert rc == N.ERR_INVALID and b"16-byte" in lib.gdn2_last_error()
+    # outputs and the state passes' buffers too
+    for i in range(6):
+        grads = [ok] * 6
+        grads[i] = odd
+        rc = lib.gdn2_chunk_bwd_intra(prob, ok, ok, ok, ok, ok, ok, ok, big, ok, *grads, ok, big,
+                                      None)
+        assert rc == N.ERR_INVALID and b"16-byte" in lib.gdn2_last_error(), i
+    rc = lib.gdn2_chunk_fwd_state(prob, None, odd, None, ok, big, None)
+    assert rc == N.ERR_INVALID and b"16-byte" in lib.gdn2_last_error()
+    rc = lib.gdn2_chunk_bwd_state(prob, ok, big, odd, None, None, ok, big, None)
+    assert rc == N.ERR_INVALID and b"16-byte" in lib.gdn2_last_error()
 
 
 def test_recurrent_argument_checks(lib):
