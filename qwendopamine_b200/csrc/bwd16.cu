@@ -262,8 +262,9 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
     T* dvns = slotp(cur, L::vDVN);
     T* vs = slotp(cur, L::vV);
     T* ws = slotp(cur, L::vWg);
+    // Z = v w: a warp takes rows r and r + 4 (80-byte rows: 32 distinct banks)
     for (int i = tid; i < kChunk * 16; i += NTH) {
-      const int r = i >> 4, cc = (i & 15) * 2;
+      const int b5 = i >> 5, r = (b5 >> 2) * 8 + (b5 & 3) + 4 * ((i >> 4) & 1), cc = (i & 15) * 2;
       const float2 v2 = ld2<T>(vs + r * LDS + cc), w2 = ld2<T>(ws + r * LDS + cc);
       const float2 z2 = mul2(v2, w2);
       *reinterpret_cast<uint32_t*>(sZ + r * LDS + cc) = pack2<T>(z2.x, z2.y);
@@ -272,23 +273,45 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
     // row, 8 columns each, combined with two shuffles
     for (int i = tid; i < 4 * D; i += NTH) {
       const int row = i >> 2, part = i & 3;
-      float2 acc2 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int cc = 8 * part + 2 * u;
-        acc2 = fma2(ld2<T>(hs + row * LDS + cc), ld2<T>(dhs + row * LDS + cc), acc2);
-      }
+      const uint4 h8 = *reinterpret_cast<const uint4*>(hs + row * LDS + 8 * part);
+      const uint4 d8 = *reinterpret_cast<const uint4*>(dhs + row * LDS + 8 * part);
+      float2 acc2 = mul2(unpack2<T>(h8.x), unpack2<T>(d8.x));
+      acc2 = fma2(unpack2<T>(h8.y), unpack2<T>(d8.y), acc2);
+      acc2 = fma2(unpack2<T>(h8.z), unpack2<T>(d8.z), acc2);
+      acc2 = fma2(unpack2<T>(h8.w), unpack2<T>(d8.w), acc2);
       float acc = acc2.x + acc2.y;
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
       if (part == 0) dgl[row] += acc;
     }
     __syncthreads();
-    warp_mma16<1, NTO, true, true>(accQ, dos, LDS, 16 * wr, hs, LDS, wc * DQ, 32);
-    warp_mma16<1, NTO, false, true>(accKd, vns, LDT, 16 * wr, dhs, LDS, wc * DQ, 32);
-    warp_mma16<1, NTO, false, true>(accW, dvns, LDT, 16 * wr, hs, LDS, wc * DQ, 32);
-    warp_mma16<1, 2, true, false>(accAqk, dos, LDS, 16 * wr, vns, LDT, 16 * wc, 32);
-    warp_mma16<1, 2, false, true>(accDA, dvns, LDT, 16 * wr, sZ, LDS, 16 * wc, 32);
+    // dQg += dO h^T, dKd += VN dh^T, dW += dVN h^T (owner tiles), dAqk += dO
+    // VN^T, dA += dVN Z^T (16 x 16 tiles): each A fragment (dO, dVN, VN) and
+    // each B fragment of h loaded once for the products that share it
+#pragma unroll
+    for (int k0 = 0; k0 < 32; k0 += 16) {
+      uint32_t aDo[4], aDvn[4], aVn[4], b[4];
+      load_a16<true>(aDo, dos, LDS, 16 * wr, k0);
+      load_a16<false>(aDvn, dvns, LDT, 16 * wr, k0);
+      load_a16<false>(aVn, vns, LDT, 16 * wr, k0);
+#pragma unroll
+      for (int j = 0; j < NTO; j += 2) {
+        load_b16x2<true>(b, hs, LDS, k0, wc * DQ + 8 * j);
+        Mma16<T>::run(accQ[0][j], aDo, b[0], b[1]);
+        Mma16<T>::run(accQ[0][j + 1], aDo, b[2], b[3]);
+        Mma16<T>::run(accW[0][j], aDvn, b[0], b[1]);
+        Mma16<T>::run(accW[0][j + 1], aDvn, b[2], b[3]);
+        load_b16x2<true>(b, dhs, LDS, k0, wc * DQ + 8 * j);
+        Mma16<T>::run(accKd[0][j], aVn, b[0], b[1]);
+        Mma16<T>::run(accKd[0][j + 1], aVn, b[2], b[3]);
+      }
+      load_b16x2<false>(b, vns, LDT, k0, 16 * wc);
+      Mma16<T>::run(accAqk[0][0], aDo, b[0], b[1]);
+      Mma16<T>::run(accAqk[0][1], aDo, b[2], b[3]);
+      load_b16x2<true>(b, sZ, LDS, k0, 16 * wc);
+      Mma16<T>::run(accDA[0][0], aDvn, b[0], b[1]);
+      Mma16<T>::run(accDA[0][1], aDvn, b[2], b[3]);
+    }
     {
       // Z = A^T dVN (64 tokens x the slice's 32 columns): a 16 x 8 tile per warp
       float accZ[4] = {0.f, 0.f, 0.f, 0.f};
