@@ -99,11 +99,13 @@ __device__ __forceinline__ void score_block16(float (&aq)[1][2][4], float (&ak)[
   }
 }
 
-// acc (16 x 8*NT) += A (16 rows at m0 of a padded K-major tile, kd columns)
-// times B (kd rows x 8*NT columns at n0 of a swizzled [64][D] tile).
+// acc1 += A B1 and acc2 += A B2: A = 16 rows at m0 of a padded K-major tile
+// (kd columns, its fragments loaded once), B1 / B2 = kd rows x 8*NT columns
+// at n0 of swizzled [64][D] tiles.
 template <int NT, typename T>
-__device__ __forceinline__ void mma_a_swb(float (&acc)[1][NT][4], const T* A, int lda, int m0,
-                                          const unsigned char* Bsw, int n0, int kd) {
+__device__ __forceinline__ void mma_a_swb2(float (&acc1)[1][NT][4], float (&acc2)[1][NT][4],
+                                           const T* A, int lda, int m0, const unsigned char* B1,
+                                           const unsigned char* B2, int n0, int kd) {
   const int lane = threadIdx.x & 31;
   const int j8 = lane >> 3, rr = lane & 7;
 #pragma unroll
@@ -114,9 +116,12 @@ __device__ __forceinline__ void mma_a_swb(float (&acc)[1][NT][4], const T* A, in
     for (int j = 0; j < NT; j += 2) {
       uint32_t b[4];
       const int k = k0 + rr + ((j8 & 1) << 3), n = n0 + 8 * j + ((j8 >> 1) << 3);
-      ldsm_x4_t(b, Bsw + swz<2>(k, n));
-      Mma16<T>::run(acc[0][j], a, b[0], b[1]);
-      Mma16<T>::run(acc[0][j + 1], a, b[2], b[3]);
+      ldsm_x4_t(b, B1 + swz<2>(k, n));
+      Mma16<T>::run(acc1[0][j], a, b[0], b[1]);
+      Mma16<T>::run(acc1[0][j + 1], a, b[2], b[3]);
+      ldsm_x4_t(b, B2 + swz<2>(k, n));
+      Mma16<T>::run(acc2[0][j], a, b[0], b[1]);
+      Mma16<T>::run(acc2[0][j + 1], a, b[2], b[3]);
     }
   }
 }
@@ -474,26 +479,19 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
     {
       T* stW = reinterpret_cast<T*>(R + L::rInv);     // Inv is dead after the pack
       T* stU = reinterpret_cast<T*>(R + L::rEndInv);  // past sA16 (read by both products)
-      float acc[1][NTO][4];
-      acc_zero(acc);
-      mma_a_swb<NTO, T>(acc, sA16, LDC, 16 * wr, sw, wc * DQ, kChunk);
+      float accW[1][NTO][4], accU[1][NTO][4];
+      acc_zero(accW);
+      acc_zero(accU);
+      mma_a_swb2<NTO, T>(accW, accU, sA16, LDC, 16 * wr, sw, sv, wc * DQ, kChunk);
 #pragma unroll
       for (int j = 0; j < NTO; ++j)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
           *reinterpret_cast<uint32_t*>(stW + r * LDK + cl) =
-              pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
-        }
-      acc_zero(acc);
-      mma_a_swb<NTO, T>(acc, sA16, LDC, 16 * wr, sv, wc * DQ, kChunk);
-#pragma unroll
-      for (int j = 0; j < NTO; ++j)
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
+              pack2<T>(accW[0][j][2 * hf], accW[0][j][2 * hf + 1]);
           *reinterpret_cast<uint32_t*>(stU + r * LDK + cl) =
-              pack2<T>(acc[0][j][2 * hf], acc[0][j][2 * hf + 1]);
+              pack2<T>(accU[0][j][2 * hf], accU[0][j][2 * hf + 1]);
         }
       tc::fence_async_smem();
       __syncthreads();
