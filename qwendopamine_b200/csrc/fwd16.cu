@@ -127,7 +127,7 @@ __device__ __forceinline__ void mma_a_swb2(float (&acc1)[1][NT][4], float (&acc2
 }
 
 // Inclusive prefix sum down the 64 rows of a swizzled fp32 tile, times mul
-// (register-staged, same summation order as col_scan64_t).
+// (register-staged, same summation order as col_scan64_reg).
 template <int NC, int NTH>
 __device__ __forceinline__ void col_scan64_sw(unsigned char* s, float* tmp, float mul) {
   constexpr int NSEG = NTH / NC;

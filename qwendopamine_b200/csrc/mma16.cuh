@@ -174,7 +174,6 @@ template <> __device__ __forceinline__ float2 ld2<__half>(const __half* p) {
 template <> __device__ __forceinline__ float2 ld2<float>(const float* p) {
   return *reinterpret_cast<const float2*>(p);
 }
-__device__ __forceinline__ float sel2(const float2& v, int t) { return t ? v.y : v.x; }
 // The two 16-bit elements of a 32-bit word as floats.
 template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t x) {
   return ld2<T>(reinterpret_cast<const T*>(&x));
@@ -234,56 +233,11 @@ __device__ __forceinline__ void cp_tile16(T* s, int lds, const T* g, int64_t ldg
   }
 }
 
-// Copy a ROWS x COLS fp32 tile (16-byte aligned rows) asynchronously; rows
-// >= nrows / cols >= ncols (ncols a multiple of 4) are zero-filled.
-template <int ROWS, int COLS, int NTH>
-__device__ __forceinline__ void cp_tile32(float* s, int lds, const float* g, int64_t ldg,
-                                          int nrows, int ncols) {
-  constexpr int CPR = COLS / 4;
-  constexpr int TOTAL = ROWS * CPR;
-#pragma unroll
-  for (int it = 0; it < (TOTAL + NTH - 1) / NTH; ++it) {
-    const int idx = threadIdx.x + it * NTH;
-    if (idx < TOTAL) {
-      const int r = idx / CPR, c = (idx - r * CPR) * 4;
-      const bool ok = r < nrows && c < ncols;
-      cp_async16(s + r * lds + c, ok ? (const void*)(g + (int64_t)r * ldg + c) : (const void*)g,
-                 ok);
-    }
-  }
-}
-
 // Segmented inclusive scan down the 64 rows of an fp32 tile with NC columns
 // (row stride lds) using NTH threads: prefix sums (REV false) or suffix sums
-// (REV true).  `tmp` holds NTH floats.  Contains __syncthreads().
-template <int NC, int NTH, bool REV>
-__device__ __forceinline__ void col_scan64_t(float* s, int lds, float* tmp) {
-  constexpr int NSEG = NTH / NC;
-  constexpr int RPS = kChunk / NSEG;
-  static_assert(NSEG * NC == NTH && RPS * NSEG == kChunk, "scan shape");
-  const int col = threadIdx.x % NC, seg = threadIdx.x / NC;
-  float run = 0.f;
-#pragma unroll
-  for (int i = 0; i < RPS; ++i) {
-    const int r = REV ? (kChunk - 1 - (seg * RPS + i)) : (seg * RPS + i);
-    run += s[r * lds + col];
-    s[r * lds + col] = run;
-  }
-  tmp[seg * NC + col] = run;
-  __syncthreads();
-  float off = 0.f;
-  for (int j = 0; j < seg; ++j) off += tmp[j * NC + col];
-#pragma unroll
-  for (int i = 0; i < RPS; ++i) {
-    const int r = REV ? (kChunk - 1 - (seg * RPS + i)) : (seg * RPS + i);
-    s[r * lds + col] += off;
-  }
-  __syncthreads();
-}
-
-// Register-staged variant of col_scan64_t: each thread loads its whole row
-// segment first, scans it in registers, and writes (prefix + offset) * mul
-// once.  Same summation order as col_scan64_t.  Contains __syncthreads().
+// (REV true), times mul.  Thread (column, segment) loads its segment of rows,
+// scans it in registers, adds the totals of the earlier segments (from
+// `tmp`, NTH floats) and writes each element once.  Contains __syncthreads().
 template <int NC, int NTH, bool REV>
 __device__ __forceinline__ void col_scan64_reg(float* s, int lds, float* tmp, float mul) {
   constexpr int NSEG = NTH / NC;
