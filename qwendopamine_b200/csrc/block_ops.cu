@@ -482,54 +482,70 @@ template <typename TW> __device__ __forceinline__ void load_w8(const TW* w, int 
 //   y = round_out(n round(silu(z))).
 // F32 (the reference under autocast): the same steps without rounding,
 // except silu(z), which runs in the input dtype.
-template <typename T, typename TW, typename TO, int TPR, bool F32>
+template <typename T, typename TW, typename TO, int TPR, bool F32, int EPT>
 __global__ void __launch_bounds__(256) k_gnorm_fwd(NormArgs a) {
-  constexpr int RPC = 256 / TPR, U = kNormUnroll;
+  // EPT columns per lane (8, or 16 when the row is exactly 16 TPR wide: half
+  // the lanes per row, so half the shuffles)
+  constexpr int RPC = 256 / TPR, U = kNormUnroll, NP = EPT / 8;
+  static_assert(EPT == 8 || EPT == 16, "8 or 16 columns per lane");
   const int sub = threadIdx.x % TPR, slot = threadIdx.x / TPR;
-  const int c = 8 * sub;
+  const int c = EPT * sub;
   const bool live = c < a.N;
-  float w[8];
-  load_w8<TW>(reinterpret_cast<const TW*>(a.w), c, a.N, w);
+  float w[NP][8];
+#pragma unroll
+  for (int p = 0; p < NP; ++p) load_w8<TW>(reinterpret_cast<const TW*>(a.w), c + 8 * p, a.N, w[p]);
   const float inv_n = 1.f / (float)a.N;
   // The trip count is uniform across the CTA: a row's lanes share a warp
   // with other rows' lanes, and every lane joins the shuffles of each trip.
   // Each trip loads U row groups before any arithmetic.
   for (int64_t base = (int64_t)blockIdx.x * RPC * U; base < a.rows;
        base += (int64_t)gridDim.x * RPC * U) {
-    Pack<T, 8> px[U], pz[U];
+    Pack<T, 8> px[U][NP], pz[U][NP];
     bool on[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t row = base + u * RPC + slot;
       on[u] = live && row < a.rows;
-      if (on[u]) {
-        px[u] = ldv<T, 8>(reinterpret_cast<const T*>(a.x) + row * a.N + c);
-        pz[u] = ldv<T, 8>(reinterpret_cast<const T*>(a.z) + row * a.N + c);
-      } else {
-        zerov<T, 8>(px[u]);
-        zerov<T, 8>(pz[u]);
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        if (on[u]) {
+          px[u][p] = ldv<T, 8>(reinterpret_cast<const T*>(a.x) + row * a.N + c + 8 * p);
+          pz[u][p] = ldv<T, 8>(reinterpret_cast<const T*>(a.z) + row * a.N + c + 8 * p);
+        } else {
+          zerov<T, 8>(px[u][p]);
+          zerov<T, 8>(pz[u][p]);
+        }
       }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      float x[8], z[8];
-      unpackv<T, 8>(px[u], x);
-      unpackv<T, 8>(pz[u], z);
+      float x[NP][8], z[NP][8];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        unpackv<T, 8>(px[u][p], x[p]);
+        unpackv<T, 8>(pz[u][p], z[p]);
+      }
       using TR = typename std::conditional<F32, float, T>::type;  // intermediate rounding
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += rnd<TR>(x[i] * x[i]);
+      for (int p = 0; p < NP; ++p)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += rnd<TR>(x[p][i] * x[p][i]);
       ss = group_sum<TPR>(ss);
       const float var = rnd<TR>(ss * inv_n);
       const float r = rnd<TR>(rsqrtf(rnd<TR>(var + a.eps)));
-      float y[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float n = rnd<TR>(x[i] * r);
-        n = rnd<typename std::conditional<F32, float, TW>::type>(n * w[i]);
-        y[i] = n * rnd<T>(silu_f(z[i]));
+      for (int p = 0; p < NP; ++p) {
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float n = rnd<TR>(x[p][i] * r);
+          n = rnd<typename std::conditional<F32, float, TW>::type>(n * w[p][i]);
+          y[i] = n * rnd<T>(silu_f(z[p][i]));
+        }
+        if (on[u])
+          stv<TO, 8>(reinterpret_cast<TO*>(a.y) + (base + u * RPC + slot) * a.N + c + 8 * p, y);
       }
-      if (on[u]) stv<TO, 8>(reinterpret_cast<TO*>(a.y) + (base + u * RPC + slot) * a.N + c, y);
     }
   }
 }
@@ -644,7 +660,8 @@ cudaError_t launch_gnorm2(const gdn2_norm_problem* p, const NormArgs& a, bool bw
   int nblk = 0;
   cudaError_t e;
   if (!bwd) {
-    auto k = p->fp32_math ? k_gnorm_fwd<T, TW, TO, TPR, true> : k_gnorm_fwd<T, TW, TO, TPR, false>;
+    auto k = p->fp32_math ? k_gnorm_fwd<T, TW, TO, TPR, true, 8>
+                          : k_gnorm_fwd<T, TW, TO, TPR, false, 8>;
     if ((e = norm_grid(k, p, &nblk)) != cudaSuccess) return e;
     k<<<nblk, 256, 0, st>>>(a);
     return cudaGetLastError();
@@ -657,8 +674,22 @@ cudaError_t launch_gnorm2(const gdn2_norm_problem* p, const NormArgs& a, bool bw
   return cudaGetLastError();
 }
 
+// Forward over rows of 16 TPR columns, 16 per lane.
+template <typename T, typename TW, typename TO, int TPR>
+cudaError_t launch_gnorm_fwd16(const gdn2_norm_problem* p, const NormArgs& a, cudaStream_t st) {
+  auto k = p->fp32_math ? k_gnorm_fwd<T, TW, TO, TPR, true, 16>
+                        : k_gnorm_fwd<T, TW, TO, TPR, false, 16>;
+  int nblk = 0;
+  const cudaError_t e = norm_grid(k, p, &nblk);
+  if (e != cudaSuccess) return e;
+  k<<<nblk, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
 template <typename T, typename TW, typename TO>
 cudaError_t launch_gnorm(const gdn2_norm_problem* p, const NormArgs& a, bool bwd, cudaStream_t st) {
+  if (!bwd && p->N == 128) return launch_gnorm_fwd16<T, TW, TO, 8>(p, a, st);
+  if (!bwd && p->N == 256) return launch_gnorm_fwd16<T, TW, TO, 16>(p, a, st);
   switch (norm_tpr(p->N)) {
     case 8: return launch_gnorm2<T, TW, TO, 8>(p, a, bwd, st);
     case 16: return launch_gnorm2<T, TW, TO, 16>(p, a, bwd, st);
