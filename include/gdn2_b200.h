@@ -157,7 +157,9 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p,
  *   - Problems whose gdn2_chunk_bwd_workspace_bytes() exceeds the built-in
  *     size are rejected with GDN2_ERR_WORKSPACE (the message gives both sizes).
  *   - The first call on a device (with that device current) looks up the
- *     array's device address once; make it before any stream capture.
+ *     array's device address once; make it before any stream capture.  The
+ *     address stays cached for the process's life, so do not call this again
+ *     on a device after cudaDeviceReset (its primary context is re-created).
  *   - All calls on a device share the array and leave their data in it;
  *     nothing needs to start at zero.  Calls that overlap on the GPU race:
  *     order them (one stream, or events). */

@@ -16,7 +16,11 @@
 //   e.g. one 2,688-token sequence with 16 heads.)
 // * Set-up: the first call on a device, with that device current, looks the
 //   array's device address up once (cudaGetSymbolAddress) and caches it; make
-//   that first call before any stream capture on that device.
+//   that first call before any stream capture on that device.  The cache is
+//   kept per device for the life of the process: after cudaDeviceReset (or
+//   anything else that destroys and re-creates the device's primary context)
+//   the cached address is stale, so a process that resets a device must not
+//   call this entry point on it again.
 // * Sharing: every call on a device uses the same array and leaves its
 //   contents behind.  Nothing in it has to start at zero -- the reverse state
 //   pass writes every byte the per-chunk pass later reads -- so it is never

@@ -15,10 +15,11 @@ forward (rank r owns a contiguous span of whole 64-token chunks):
     5. ``gdn2_chunk_fwd_state`` from ``x``: local outputs and end state.
 backward:
     1. ``gdn2_cp_bwd_prescan``: the span-start state gradient produced by the
-       local outputs (plus, on the last rank, the final-state gradient);
+       local outputs and by the gradient of the returned end state ``S_r``;
     2. all-gather of it;
-    3. ``gdn2_cp_merge``: ``x = 0;  x = M_j^T x + dh_j`` for ``j > r`` -- the
-       gradient w.r.t. this span's end state;
+    3. ``gdn2_cp_merge``: ``x = 0;  x = M_j^T x + dh_j`` for ``j > r``, plus
+       the gradient of ``S_r`` itself -- the gradient w.r.t. this span's end
+       state;
     4. ``gdn2_chunk_bwd`` with that end-state gradient.
 Each rank's local backward then yields exact gradients for its own inputs.
 
@@ -188,29 +189,36 @@ class CPChunkGDN2Function(torch.autograd.Function):
         sbytes = lib.gdn2_chunk_saved_bytes(prob)
         (do,) = _aligned16(do.to(q.dtype).contiguous())
         last = rank == world - 1
-        # Only the last rank's end state is the sequence's final state.
-        dht_final = dht.float().contiguous() if (last and dht is not None) else None
-        # Span-start gradient of the local outputs (and of the final state).
+        # dht is the gradient that reaches this rank's end state S_r directly
+        # (a loss on the returned state; on the last rank S_r is the
+        # sequence's final state).  It enters the span-start gradient sent to
+        # the earlier ranks, and it adds to what the later ranks' outputs
+        # send back through S_r.
+        dht_direct = dht.float().contiguous() if dht is not None else None
+        # Span-start gradient of the local outputs and of dht_direct.
         if S == 1:
             dhm = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
             N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do),
-                                            N.ptr(dht_final), N.ptr(dhm), None, 0, st),
+                                            N.ptr(dht_direct), N.ptr(dhm), None, 0, st),
                     "gdn2_cp_bwd_prescan")
         else:
             dhm_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
             N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do), None,
                                             N.ptr(dhm_sub), None, 0, st), "gdn2_cp_bwd_prescan")
             dhm_sub = dhm_sub.view(B, S, H, K, V)
-            dhm = _compose_grads(dhm_sub, hm_sub, dht_final)
+            dhm = _compose_grads(dhm_sub, hm_sub, dht_direct)
         wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
         ws = torch.empty(max(wbytes, 1), dtype=torch.uint8, device=dev)
         dhm_all = gather(dhm)
         if last:
-            dht_local = dht_final
+            dht_local = dht_direct
         else:
+            # x = 0;  x = M_j^T x + dh_j  for j = world-1 .. r+1, then + dht_direct
             dht_local = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
             N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), N.ptr(dhm_all), rank, world, 0,
                                       None, N.ptr(dht_local), st), "gdn2_cp_merge (backward)")
+            if dht_direct is not None:
+                dht_local += dht_direct
         if S > 1:
             end = dht_local if dht_local is not None else torch.zeros_like(h0)
             dht_local = _unfold_grads(end, dhm_sub, hm_sub)
@@ -242,7 +250,10 @@ def chunk_gdn2_cp(q, k, v, g, b, w, *, rank: int, world: int, gather: Gather,
     (:func:`gather_span_maps` over a process group).
 
     Returns ``(o_r, S_r)``: the local outputs and the state at the end of this
-    rank's span (on the last rank: the sequence's final state).
+    rank's span (on the last rank: the sequence's final state).  Both are
+    differentiable on every rank: a loss on a middle rank's ``S_r`` sends its
+    gradient to this rank's inputs and, through the gathered span-start
+    gradients, to every earlier rank's.
     """
     _require_cuda(q, k, v, g, b, w, initial_state)
     assert q.shape == k.shape == g.shape == b.shape, "q, k, g, b must have the same shape."

@@ -94,7 +94,9 @@ def fused_recurrent_gdn2_fwd(
     g = g.float().contiguous()
 
     if out is None:
-        out = torch.empty_like(v)
+        # zeros, as the reference allocates them: the kernel skips the tokens
+        # of sequences whose state slot is negative (padding in a pool)
+        out = torch.zeros_like(v)
     else:
         assert out.shape == v.shape
     h0 = initial_state

@@ -42,6 +42,12 @@ def _inputs():
     return [x.double().numpy() for x in (q, k, v, g, b, w, h0, do)]
 
 
+def _end_state_grads(world, B, H, K, V):
+    """A distinct seeded gradient for every rank's end state S_r."""
+    rng = np.random.default_rng(11)
+    return [rng.standard_normal((B, H, K, V)) for _ in range(world)]
+
+
 def _worker_exchange(rank, world, port, out_q):
     import sys
 
@@ -71,20 +77,28 @@ def _worker_exchange(rank, world, port, out_q):
         _, ref_state = O.recurrent_fwd(*(x_[:, :a] for x_ in (q, k, v, g, b, w)), h0,
                                        norm_mode="torch")
         fwd_err = float(np.abs(x - ref_state[0]).max()) if a > 0 else float(np.abs(x - h0[0]).max())
-        # backward: span-start gradient of the local outputs with zero end gradient
+        # backward, with a loss on every rank's end state S_j as well as on
+        # the outputs (dht_j the gradient that reaches S_j directly): the
+        # span-start gradient of the local outputs and of dht_r ...
+        dhts = _end_state_grads(world, q.shape[0], q.shape[2], K, V)
         *_, dh_start = O.recurrent_bwd(*(sl(x_) for x_ in (q, k, v, g, b, w)), sl(do), x[None],
-                                       None, norm_mode="torch")
+                                       dhts[rank], norm_mode="torch")
         dh_all = gather_span_maps(torch.from_numpy(dh_start[0]), None).numpy()
+        # ... folded from the later ranks, plus this rank's own dht_r, is the
+        # total gradient of S_r
         y = np.zeros_like(dh_start[0])
         for j in range(world - 1, rank, -1):
             y = np.einsum("hmk,hmv->hkv", hm_all[j][..., V:], y) + dh_all[j]
-        # reference end-state gradient: gradient of the later outputs w.r.t. S_e
-        if rank < world - 1:
-            *_, ref_dh = O.recurrent_bwd(*(x_[:, e:] for x_ in (q, k, v, g, b, w)), do[:, e:],
-                                         np.zeros((1,) + y.shape), None, norm_mode="torch")
-            bwd_err = float(np.abs(y - ref_dh[0]).max())
-        else:
-            bwd_err = float(np.abs(y).max())
+        y = y + dhts[rank][0]
+        # reference: walk the later spans backwards from the final state,
+        # adding each span end's own gradient
+        ref = dhts[world - 1]
+        for j in range(world - 1, rank, -1):
+            a_j, e_j = j * span, (j + 1) * span
+            *_, ref = O.recurrent_bwd(*(x_[:, a_j:e_j] for x_ in (q, k, v, g, b, w)),
+                                      do[:, a_j:e_j], np.zeros_like(ref), ref, norm_mode="torch")
+            ref = ref + dhts[j - 1]
+        bwd_err = float(np.abs(y - ref[0]).max())
         order_ok = bool(np.allclose(hm_all[rank], hm))
         out_q.put((rank, fwd_err, bwd_err, order_ok))
     finally:
@@ -173,9 +187,13 @@ def _run(fn, world, timeout):
     return sorted(results)
 
 
-def test_span_map_exchange_and_fold_over_gloo():
-    res = _run(_worker_exchange, 2, timeout=120)
-    assert [r[0] for r in res] == [0, 1]
+@pytest.mark.parametrize("world", [2, 3])
+def test_span_map_exchange_and_fold_over_gloo(world):
+    """Forward folds give every rank the whole sequence's state at its span
+    start; backward folds, with a loss on the outputs and on every rank's end
+    state, give every rank the whole loss's gradient of its end state."""
+    res = _run(_worker_exchange, world, timeout=120)
+    assert [r[0] for r in res] == list(range(world))
     for rank, fwd_err, bwd_err, order_ok in res:
         assert order_ok, rank
         assert fwd_err < 1e-10, (rank, fwd_err)
