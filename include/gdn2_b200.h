@@ -323,6 +323,21 @@ int gdn2_gated_norm_bwd(const gdn2_norm_problem* p, const void* x, const void* z
  * reference, whose kernels contain no bounded waits. */
 int gdn2_fault_status(void* stream, int32_t clear);
 
+/* ---- test hook: the bounded-wait abort path ---------------------------------
+ * No counterpart in the reference.  Runs the forward state pass
+ * (gdn2_chunk_fwd_state, no initial or final state) with chunk `skip_chunk`'s
+ * tiles never requested and every wait limited to `wait_ns` nanoseconds
+ * (1 .. 1e9), so that the wait for that chunk runs out: the kernel drains its
+ * copies and products in flight, frees its tensor memory, sets bit 0 of the
+ * fault word and returns.  Nothing faults and nothing waits without a limit;
+ * the context stays usable and gdn2_fault_status(stream, 1) reports the bit.
+ * Only problems the tcgen05 state pass serves (bf16, K = V = 128) are
+ * accepted (GDN2_ERR_UNSUPPORTED otherwise).  The outputs are incomplete: a
+ * test of the failure path, not a compute entry point. */
+int gdn2_test_fwd_state_wait_timeout(const gdn2_chunk_problem* p, void* o, void* saved,
+                                     size_t saved_bytes, int32_t skip_chunk, uint64_t wait_ns,
+                                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,7 @@ core recurrence.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -47,6 +48,7 @@ EXPORTS = (
     "gdn2_gated_norm_bwd_workspace_bytes",
     "gdn2_gated_norm_bwd",
     "gdn2_fault_status",
+    "gdn2_test_fwd_state_wait_timeout",
 )
 
 
@@ -169,6 +171,8 @@ def _declare(lib):
         "gdn2_cp_bwd_prescan": ([cp, v, c_size_t, v, v, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_cp_merge": ([cp, v, v, c_int32, c_int32, c_int32, v, v, v], ctypes.c_int),
         "gdn2_fault_status": ([v, c_int32], ctypes.c_int),
+        "gdn2_test_fwd_state_wait_timeout": ([cp, v, v, c_size_t, c_int32, ctypes.c_uint64, v],
+                                             ctypes.c_int),
         "gdn2_conv_fwd": ([vp, v, v, v, v, v, v, v], ctypes.c_int),
         "gdn2_conv_bwd_workspace_bytes": ([vp], c_size_t),
         "gdn2_conv_bwd": ([vp, v, v, v, v, v, v, v, v, v, v, c_size_t, v], ctypes.c_int),
@@ -221,6 +225,46 @@ def fault_status(device=None, clear: bool = True) -> int:
     if r < 0:
         raise GDN2Error(ERR_CUDA, f"gdn2_fault_status: {lib.gdn2_last_error().decode()}")
     return r
+
+
+# ---------------------------------------------------------------------------
+# optional per-phase timing: CUDA events on the launching stream around each
+# library phase (forward intra / state pass, pre-scans, exchange, merges,
+# backward state / intra pass).  Off unless a caller opens phase_timing().
+# The record list is process-wide, not per thread, because autograd runs the
+# backward on its own device thread.
+# ---------------------------------------------------------------------------
+_phase_records = None
+
+
+@contextlib.contextmanager
+def phase_timing():
+    """Collect ``(name, start_event, end_event)`` for every phase the package
+    runs inside the block (events recorded on the current stream; read them
+    after a synchronize).  For benchmarks; one collector at a time."""
+    global _phase_records
+    prev, rec = _phase_records, []
+    _phase_records = rec
+    try:
+        yield rec
+    finally:
+        _phase_records = prev
+
+
+@contextlib.contextmanager
+def phase(name: str):
+    """Bracket one phase with CUDA events while :func:`phase_timing` is open."""
+    rec = _phase_records
+    if rec is None:
+        yield
+        return
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    try:
+        yield
+    finally:
+        e.record()
+        rec.append((name, s, e))
 
 
 def ptr(t):

@@ -585,6 +585,39 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all, const float*
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_merge");
 }
 
+int gdn2_test_fwd_state_wait_timeout(const gdn2_chunk_problem* p, void* o, void* saved,
+                                     size_t saved_bytes, int32_t skip_chunk, uint64_t wait_ns,
+                                     void* stream) {
+  int rc = check_problem(p, "gdn2_test_fwd_state_wait_timeout");
+  if (rc) return rc;
+  if (!o || !saved)
+    return fail(GDN2_ERR_INVALID, "gdn2_test_fwd_state_wait_timeout: null o or saved");
+  if (wait_ns == 0 || wait_ns > 1000000000ull)
+    return fail(GDN2_ERR_INVALID,
+                "gdn2_test_fwd_state_wait_timeout: wait_ns must be in 1 .. 1e9 (got %llu)",
+                (unsigned long long)wait_ns);
+  SavedLayout L = layout_of(p);
+  if (saved_bytes < L.total)
+    return fail(GDN2_ERR_WORKSPACE, "gdn2_test_fwd_state_wait_timeout: saved buffer too small");
+  if (p->seqs.n_seqs == 0) return GDN2_OK;
+  FwdStateArgs a;
+  a.seqs = make_seqs(p);
+  a.H = p->H; a.K = p->K; a.V = p->V;
+  a.h0 = nullptr; a.o = o; a.ht = nullptr;
+  a.saved = static_cast<unsigned char*>(saved);
+  a.L = L;
+  a.prescan = 0;
+  a.hm = nullptr;
+  a.wait_ns = wait_ns;
+  a.skip_chunk = skip_chunk;
+  if (!fwd_state_tc_ok(a, p->dtype == GDN2_DTYPE_BF16))
+    return fail(GDN2_ERR_UNSUPPORTED,
+                "gdn2_test_fwd_state_wait_timeout: only problems of the tcgen05 state pass "
+                "(bf16, K = V = 128, 16-byte aligned buffers)");
+  cudaError_t e = launch_fwd_state_tc(a, (cudaStream_t)stream);
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_test_fwd_state_wait_timeout");
+}
+
 int gdn2_fault_status(void* stream, int32_t clear) {
   cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
   if (e != cudaSuccess) {

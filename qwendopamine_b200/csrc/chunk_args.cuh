@@ -73,6 +73,11 @@ struct FwdStateArgs {
   // pre-scan mode: carry [h | M] over V+K columns from [0 | I]; write hm.
   int prescan;
   float* hm;         // [N,H,K,V+K]
+  // Test of the bounded-wait abort path (tcgen05 pass only): every mbarrier
+  // wait gives up after wait_ns (0: the built-in limit) and chunk
+  // skip_chunk's tiles are never requested (-1: none).
+  uint64_t wait_ns = 0;
+  int skip_chunk = -1;
 };
 
 struct BwdStateArgs {

@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int64_t ldo = (int64_t)H * V;
   const float* h0 = a.h0 ? a.h0 + (int64_t)nh * K * V : nullptr;
   float* ht = a.ht ? a.ht + (int64_t)nh * K * V : nullptr;
+  const uint64_t lim = a.wait_ns ? a.wait_ns : tc::kWaitLimitNs;
 
   if (c_begin >= c_end) {  // empty sequence: the state passes through
     if (ht)
@@ -144,6 +145,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   int next_issue = c_begin;  // meaningful in thread 0 only
   int mma1_commits = 0, mma2_commits = 0;
   auto issue = [&](int c) {
+    if (c == a.skip_chunk) {  // test of the abort path: this chunk never arrives
+      next_issue = c + 1;
+      return;
+    }
     const int slot = (c - c_begin) & 1;
     unsigned char* p = sm + slot * kSlotBytes;
     const size_t ch = (size_t)c * H + h;
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   // ---- initial state ----------------------------------------------------------
   {
-    const bool ok = tc::warp_wait(&full[0], 0);
+    const bool ok = tc::warp_wait(&full[0], 0, lim);
     if (ok) {
       float s[64];
       if (h0) {
@@ -265,7 +270,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // 1. VN^T = h^T W^T,  o^T = h^T Qg^T;  meanwhile the checkpoint of
       //    chunk c and the previous chunk's o leave through the copy units.
       if (tid == 0) {
-        if (!tc::mbar_wait(&full[slot], par_full)) {
+        if (!tc::mbar_wait(&full[slot], par_full, lim)) {
           *sAbort = 1;
         } else {
           tc::tc_fence_after();
@@ -285,8 +290,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (c > c_begin) copy_o(c - 1);
       // 2. VN = U - W h  -> bf16 VN^T operand tile
       {
-        bool ok = tc::warp_wait(mma1, par_mma);
-        if (ok) ok = tc::warp_wait(&full[slot], par_full);
+        bool ok = tc::warp_wait(mma1, par_mma, lim);
+        if (ok) ok = tc::warp_wait(&full[slot], par_full, lim);
         if (ok) {
           tc::tc_fence_after();
           uint32_t x[32];
@@ -336,8 +341,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       //    scaled in place by the next chunk's 2^G_last
       {
         const bool has_next = c + 1 < c_end;
-        bool ok = tc::warp_wait(mma2, par_mma);
-        if (ok && has_next) ok = tc::warp_wait(&full[slot ^ 1], ((i + 1) >> 1) & 1);
+        bool ok = tc::warp_wait(mma2, par_mma, lim);
+        if (ok && has_next) ok = tc::warp_wait(&full[slot ^ 1], ((i + 1) >> 1) & 1, lim);
         if (ok) {
           tc::tc_fence_after();
           {
@@ -389,10 +394,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // and tensor memory they target is released (each wait bounded)
     for (int j = c; j < next_issue; ++j) {
       const int ij = j - c_begin;
-      tc::mbar_wait(&full[ij & 1], (ij >> 1) & 1);
+      tc::mbar_wait(&full[ij & 1], (ij >> 1) & 1, lim);
     }
-    if (mma1_commits > 0) tc::mbar_wait(mma1, (mma1_commits - 1) & 1);
-    if (mma2_commits > 0) tc::mbar_wait(mma2, (mma2_commits - 1) & 1);
+    if (mma1_commits > 0) tc::mbar_wait(mma1, (mma1_commits - 1) & 1, lim);
+    if (mma2_commits > 0) tc::mbar_wait(mma2, (mma2_commits - 1) & 1, lim);
     atomicOr(&g_gdn2_fault, 1u);
   }
   tc::tc_fence_before();

@@ -45,20 +45,22 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase with the given parity; false if the time limit ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (long r = 0; r < kMaxPollRounds; ++r) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   }
   return false;
 }
 // Same, decided for the whole warp: true only if every lane saw the phase.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  const bool ok = mbar_wait(bar, parity);
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
+  const bool ok = mbar_wait(bar, parity, limit_ns);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 

@@ -86,9 +86,14 @@ def chunk_gdn2_fwd(q, k, v, g, b, w, scale, initial_state, output_final_state, t
     ht = (q.new_empty(tables.n_seqs, H, K, V, dtype=torch.float32)
           if output_final_state else None)
     st = N.stream_of(q.device)
-    N.check(lib.gdn2_chunk_fwd(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b), N.ptr(w),
-                               N.ptr(initial_state), N.ptr(o), N.ptr(ht), N.ptr(saved), nbytes,
-                               st), "gdn2_chunk_fwd")
+    # gdn2_chunk_fwd's two phases, called one by one so each can be timed
+    with N.phase("fwd_intra"):
+        N.check(lib.gdn2_chunk_fwd_intra(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
+                                         N.ptr(w), N.ptr(saved), nbytes, st),
+                "gdn2_chunk_fwd_intra")
+    with N.phase("fwd_state"):
+        N.check(lib.gdn2_chunk_fwd_state(prob, N.ptr(initial_state), N.ptr(o), N.ptr(ht),
+                                         N.ptr(saved), nbytes, st), "gdn2_chunk_fwd_state")
     return o, ht, (saved if keep_saved else None)
 
 
@@ -120,10 +125,16 @@ def chunk_gdn2_bwd(q, k, v, g, b, w, saved, do, dht, scale, initial_state, table
         for t in (dq, dk, dv, db, dw, dg):
             t.zero_()
     st = N.stream_of(q.device)
-    N.check(lib.gdn2_chunk_bwd(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b), N.ptr(w),
-                               N.ptr(saved), nbytes, N.ptr(do), N.ptr(dht), N.ptr(dq), N.ptr(dk),
-                               N.ptr(dv), N.ptr(dg), N.ptr(db), N.ptr(dw), N.ptr(dh0), N.ptr(ws),
-                               wbytes, st), "gdn2_chunk_bwd")
+    # gdn2_chunk_bwd's two phases, called one by one so each can be timed
+    with N.phase("bwd_state"):
+        N.check(lib.gdn2_chunk_bwd_state(prob, N.ptr(saved), nbytes, N.ptr(do), N.ptr(dht),
+                                         N.ptr(dh0), N.ptr(ws), wbytes, st),
+                "gdn2_chunk_bwd_state")
+    with N.phase("bwd_intra"):
+        N.check(lib.gdn2_chunk_bwd_intra(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
+                                         N.ptr(w), N.ptr(saved), nbytes, N.ptr(do), N.ptr(dq),
+                                         N.ptr(dk), N.ptr(dv), N.ptr(dg), N.ptr(db), N.ptr(dw),
+                                         N.ptr(ws), wbytes, st), "gdn2_chunk_bwd_intra")
     if gate is not None:
         return dq, dk, dv, dg, db, dw, dh0, dA_log, ddt_bias
     return dq, dk, dv, dg, db, dw, dh0

@@ -153,23 +153,30 @@ class CPChunkGDN2Function(torch.autograd.Function):
         st = N.stream_of(dev)
         sbytes = lib.gdn2_chunk_saved_bytes(prob)
         saved = torch.empty(max(sbytes, 1), dtype=torch.uint8, device=dev)
-        N.check(lib.gdn2_chunk_fwd_intra(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
-                                         N.ptr(w), N.ptr(saved), sbytes, st),
-                "gdn2_chunk_fwd_intra")
+        with N.phase("fwd_intra"):
+            N.check(lib.gdn2_chunk_fwd_intra(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g),
+                                             N.ptr(b), N.ptr(w), N.ptr(saved), sbytes, st),
+                    "gdn2_chunk_fwd_intra")
         hm_sub = torch.empty(B * S, H, K, V + K, dtype=torch.float32, device=dev)
-        N.check(lib.gdn2_cp_fwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(hm_sub), None, 0, st),
-                "gdn2_cp_fwd_prescan")
+        with N.phase("fwd_prescan"):
+            N.check(lib.gdn2_cp_fwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(hm_sub), None, 0,
+                                            st), "gdn2_cp_fwd_prescan")
         hm_sub = hm_sub.view(B, S, H, K, V + K)
-        hm = hm_sub[:, 0] if S == 1 else _compose_maps(hm_sub)
-        hm_all = gather(hm.contiguous())
+        with N.phase("fwd_fold"):
+            hm = hm_sub[:, 0] if S == 1 else _compose_maps(hm_sub)
+        with N.phase("fwd_gather"):
+            hm_all = gather(hm.contiguous())
         h0 = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
-        N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), None, rank, world, 1,
-                                  N.ptr(initial_state), N.ptr(h0), st), "gdn2_cp_merge")
-        h0_sub = h0 if S == 1 else _unfold_states(h0, hm_sub)
+        with N.phase("fwd_merge"):
+            N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), None, rank, world, 1,
+                                      N.ptr(initial_state), N.ptr(h0), st), "gdn2_cp_merge")
+        with N.phase("fwd_fold"):
+            h0_sub = h0 if S == 1 else _unfold_states(h0, hm_sub)
         o = torch.empty_like(v)
         ht_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
-        N.check(lib.gdn2_chunk_fwd_state(prob, N.ptr(h0_sub), N.ptr(o), N.ptr(ht_sub),
-                                         N.ptr(saved), sbytes, st), "gdn2_chunk_fwd_state")
+        with N.phase("fwd_state"):
+            N.check(lib.gdn2_chunk_fwd_state(prob, N.ptr(h0_sub), N.ptr(o), N.ptr(ht_sub),
+                                             N.ptr(saved), sbytes, st), "gdn2_chunk_fwd_state")
         ht = ht_sub.view(B, S, H, K, V)[:, S - 1].contiguous()
         ctx.save_for_backward(q, k, v, g, b, w, saved, h0, hm_all, hm_sub)
         ctx.meta = (scale, l2norm, rank, world, gather, tables, initial_state is not None, S)
@@ -198,36 +205,50 @@ class CPChunkGDN2Function(torch.autograd.Function):
         # Span-start gradient of the local outputs and of dht_direct.
         if S == 1:
             dhm = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
-            N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do),
-                                            N.ptr(dht_direct), N.ptr(dhm), None, 0, st),
-                    "gdn2_cp_bwd_prescan")
+            with N.phase("bwd_prescan"):
+                N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do),
+                                                N.ptr(dht_direct), N.ptr(dhm), None, 0, st),
+                        "gdn2_cp_bwd_prescan")
         else:
             dhm_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
-            N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do), None,
-                                            N.ptr(dhm_sub), None, 0, st), "gdn2_cp_bwd_prescan")
+            with N.phase("bwd_prescan"):
+                N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do), None,
+                                                N.ptr(dhm_sub), None, 0, st),
+                        "gdn2_cp_bwd_prescan")
             dhm_sub = dhm_sub.view(B, S, H, K, V)
-            dhm = _compose_grads(dhm_sub, hm_sub, dht_direct)
+            with N.phase("bwd_fold"):
+                dhm = _compose_grads(dhm_sub, hm_sub, dht_direct)
         wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
         ws = torch.empty(max(wbytes, 1), dtype=torch.uint8, device=dev)
-        dhm_all = gather(dhm)
+        with N.phase("bwd_gather"):
+            dhm_all = gather(dhm)
         if last:
             dht_local = dht_direct
         else:
             # x = 0;  x = M_j^T x + dh_j  for j = world-1 .. r+1, then + dht_direct
             dht_local = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
-            N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), N.ptr(dhm_all), rank, world, 0,
-                                      None, N.ptr(dht_local), st), "gdn2_cp_merge (backward)")
-            if dht_direct is not None:
-                dht_local += dht_direct
+            with N.phase("bwd_merge"):
+                N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), N.ptr(dhm_all), rank, world,
+                                          0, None, N.ptr(dht_local), st),
+                        "gdn2_cp_merge (backward)")
+                if dht_direct is not None:
+                    dht_local += dht_direct
         if S > 1:
             end = dht_local if dht_local is not None else torch.zeros_like(h0)
-            dht_local = _unfold_grads(end, dhm_sub, hm_sub)
+            with N.phase("bwd_fold"):
+                dht_local = _unfold_grads(end, dhm_sub, hm_sub)
         grads = {n: torch.empty_like(t) for n, t in zip("qkvgbw", (q, k, v, g, b, w))}
         dh0_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
-        N.check(lib.gdn2_chunk_bwd(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g), N.ptr(b),
-                                   N.ptr(w), N.ptr(saved), sbytes, N.ptr(do), N.ptr(dht_local),
-                                   *(N.ptr(grads[n]) for n in "qkvgbw"), N.ptr(dh0_sub),
-                                   N.ptr(ws), wbytes, st), "gdn2_chunk_bwd")
+        # gdn2_chunk_bwd's two phases, called one by one so each can be timed
+        with N.phase("bwd_state"):
+            N.check(lib.gdn2_chunk_bwd_state(prob, N.ptr(saved), sbytes, N.ptr(do),
+                                             N.ptr(dht_local), N.ptr(dh0_sub), N.ptr(ws), wbytes,
+                                             st), "gdn2_chunk_bwd_state")
+        with N.phase("bwd_intra"):
+            N.check(lib.gdn2_chunk_bwd_intra(prob, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(g),
+                                             N.ptr(b), N.ptr(w), N.ptr(saved), sbytes, N.ptr(do),
+                                             *(N.ptr(grads[n]) for n in "qkvgbw"), N.ptr(ws),
+                                             wbytes, st), "gdn2_chunk_bwd_intra")
         dh0 = dh0_sub.view(B, S, H, K, V)[:, 0].contiguous()
         # dh0 on rank 0 is the gradient of the global initial state; on later
         # ranks the initial state is an internal value whose gradient has been

@@ -6,9 +6,10 @@ Run once in a container where the reference checkout is importable:
 
 It imports the reference's own pure-PyTorch GDN-2 functions
 (``qwendopamine.models.gdn2.gdn2.torch_recurrent_gdn2`` and
-``torch_chunk_gdn2``, gdn2.py:100-369), runs them on seeded inputs, and stores
-inputs, outputs, final states and autograd gradients as ``.npz`` files next to
-this script.  Nothing at test time imports the reference: the GPU box has no
+``torch_chunk_gdn2``, gdn2.py:100-369), its block pieces and its whole
+``GatedDeltaNet2`` module, runs them on seeded inputs, and stores inputs,
+outputs, final states, caches, state_dicts and autograd gradients as ``.npz``
+files next to this script.  Nothing at test time imports the reference: the GPU box has no
 copy of it, and the fixtures travel instead.
 """
 
@@ -223,6 +224,63 @@ def block_ops_case():
     np.savez_compressed(os.path.join(HERE, "block_ops.npz"), **out)
 
 
+def module_case():
+    """The reference's whole ``GatedDeltaNet2`` module (gdn2.py:488-1004),
+    fp32, on its exact token-serial backend (``torch-recurrent``): for each
+    case the seeded initial state_dict, a training-mode forward with the cache
+    returned (output, recurrent state, the three conv states), the gradients
+    of sum(out * dy) for every parameter, and (unpadded cases) one eval-mode
+    decode step through that cache.
+
+    The padded case packs a single sequence: with one sequence per batch the
+    reference's pure-PyTorch core (which does not take ``cu_seqlens``) and its
+    GPU core (which does) agree, and the B200 module follows the GPU core.
+    """
+    from qwendopamine.models.gdn2.gdn2 import GatedDeltaNet2
+
+    sys.path.insert(0, os.path.dirname(HERE))
+    from module_cases import MODULE_CASES
+
+    out = {}
+    for name, (kw, seed, Bs, Ts, pad) in MODULE_CASES.items():
+        torch.manual_seed(seed)
+        m = GatedDeltaNet2(layer_idx=0, backend="torch-recurrent", **kw)
+        for n, p in m.state_dict().items():
+            out[f"{name}.sd.{n}"] = _np(p)
+        m.train()
+        gen = torch.Generator().manual_seed(100 + seed)
+        x = torch.randn(Bs, Ts, kw["hidden_size"], generator=gen)
+        dy = torch.randn(Bs, Ts, kw["hidden_size"], generator=gen)
+        out[f"{name}.x"], out[f"{name}.dy"] = _np(x), _np(dy)
+        if pad:
+            mask = torch.ones(Bs, Ts, dtype=torch.long)
+            mask[0, :pad] = 0
+            out[f"{name}.mask"] = mask.numpy()
+            y, _, _ = m(x, attention_mask=mask)
+        else:
+            cache = {}
+            y, _, cache = m(x, past_key_values=cache, use_cache=True)
+            out[f"{name}.rec"] = _np(cache["recurrent_state"])
+            for tag, c in zip("qkv", cache["conv_state"]):
+                out[f"{name}.conv_{tag}"] = _np(c)
+        out[f"{name}.out"] = _np(y)
+        params = dict(m.named_parameters())
+        gr = torch.autograd.grad((y * dy).sum(), list(params.values()))
+        for n, g_ in zip(params, gr):
+            out[f"{name}.grad.{n}"] = _np(g_)
+        if not pad:
+            # one decode step through the cache (eval: the recurrent mode)
+            m.eval()
+            x1 = torch.randn(Bs, 1, kw["hidden_size"], generator=gen)
+            with torch.no_grad():
+                y1, _, cache = m(x1, past_key_values=cache, use_cache=True)
+            out[f"{name}.x1"], out[f"{name}.out1"] = _np(x1), _np(y1)
+            out[f"{name}.rec1"] = _np(cache["recurrent_state"])
+            for tag, c in zip("qkv", cache["conv_state"]):
+                out[f"{name}.conv1_{tag}"] = _np(c)
+    np.savez_compressed(os.path.join(HERE, "module.npz"), **out)
+
+
 def main():
     rec, chk = _ref()
     torch.set_num_threads(8)
@@ -231,6 +289,7 @@ def main():
     strong_decay_case(rec, chk)
     decode_case(rec)
     block_ops_case()
+    module_case()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -370,6 +370,16 @@ def test_backward_16bit_repeats_bit_for_bit_at_config1_size(cuda_device):
         del leaves, o
     for n, x, y in zip(("o", *NAMES), *runs):
         assert torch.equal(x, y), n
+    # and one sequence x two heads of that full-size run against the fp64
+    # oracle (the same launch, not a smaller stand-in)
+    s, hs = 5, [3, 12]
+    sel = lambda t: t[s:s + 1, :, hs].double().cpu().numpy()
+    args = [sel(t) for t in (q, k, v, g, b, w)]
+    ro, _ = O.recurrent_fwd(*args, None, norm_mode="fla")
+    assert rel(runs[0][0][s:s + 1, :, hs], ro) < TOL[torch.bfloat16], "o"
+    ref = O.recurrent_bwd(*args, sel(do), None, None, norm_mode="fla")
+    for n, x, r in zip(NAMES, runs[0][1:], ref):
+        assert rel(x[s:s + 1, :, hs], r) < TOL[torch.bfloat16], n
 
 
 @pytest.mark.parametrize("B,T,H,K,V", [

@@ -123,3 +123,61 @@ def test_tc_state_backward_varlen_ragged_and_empty(cuda_device):
             assert rel(leaves[n].grad[:, a_:e_], r) < TOL[BF], (s, n)
         assert rel(h0d.grad[s:s + 1], ref[6]) < TOL[BF], (s, "h0")
     assert _fault_word() == 0
+
+
+def test_tc_state_bounded_wait_runs_out_cleanly(cuda_device):
+    """The device-side failure path, made to happen without a fault: the
+    test hook runs the tcgen05 forward state pass with one chunk's tiles never
+    requested and a 50 us limit on every wait.  The wait for that chunk runs
+    out, the CTA drains its copies and products in flight, frees its tensor
+    memory and sets bit 0 of the fault word; the launch itself succeeds.  The
+    same context then runs a normal forward + backward that matches the
+    oracle with a clean fault word."""
+    from qwendopamine_b200 import _native as N
+    from qwendopamine_b200 import chunk_gdn2
+
+    lib = N.load()
+    _fault_word()
+    B, T, H = 1, 8 * 64, 2
+    d = make_inputs(B, T, H, 128, 128, seed=43, dtype=BF, decay="baseline", h0=False)
+    x = to_dev(d, cuda_device, BF)
+    tables = N.seq_tables(B, T, cuda_device)
+    prob = N.ChunkProblem(H, 128, 128, N.dtype_code(BF), 1, 128 ** -0.5, tables.struct())
+    sb = lib.gdn2_chunk_saved_bytes(prob)
+    saved = torch.empty(sb, dtype=torch.uint8, device=cuda_device)
+    o = torch.zeros_like(x["v"])
+    st = N.stream_of(cuda_device)
+    N.check(lib.gdn2_chunk_fwd_intra(prob, *(N.ptr(x[n]) for n in NAMES), N.ptr(saved), sb, st),
+            "gdn2_chunk_fwd_intra")
+    rc = lib.gdn2_test_fwd_state_wait_timeout(prob, N.ptr(o), N.ptr(saved), sb, 3, 50_000, st)
+    N.check(rc, "gdn2_test_fwd_state_wait_timeout")
+    assert _fault_word() & 1 == 1
+    # the context is intact: a normal pass on it is correct and raises no bit
+    leaves = {n: x[n].clone().requires_grad_() for n in NAMES}
+    o, _ = chunk_gdn2(*(leaves[n] for n in NAMES), use_qk_l2norm_in_kernel=True)
+    do = torch.randn(B, T, H, 128, generator=torch.Generator().manual_seed(9)).bfloat16()
+    o.backward(do.to(cuda_device))
+    ro, _ = O.recurrent_fwd(*np_(d, NAMES), None, norm_mode="fla")
+    assert rel(o, ro) < TOL[BF]
+    ref = O.recurrent_bwd(*np_(d, NAMES), do.float().numpy(), None, None, norm_mode="fla")
+    for n, r in zip(NAMES, ref):
+        assert rel(leaves[n].grad, r) < TOL[BF], n
+    assert _fault_word() == 0
+
+
+def test_tc_state_wait_timeout_hook_argument_checks(cuda_device):
+    from qwendopamine_b200 import _native as N
+
+    lib = N.load()
+    tables = N.seq_tables(1, 128, cuda_device)
+    buf = torch.empty(1 << 20, dtype=torch.uint8, device=cuda_device)
+    st = N.stream_of(cuda_device)
+    # fp32 problems never take the tcgen05 pass
+    p32 = N.ChunkProblem(1, 128, 128, N.dtype_code(torch.float32), 1, 0.1, tables.struct())
+    big = torch.empty(lib.gdn2_chunk_saved_bytes(p32), dtype=torch.uint8, device=cuda_device)
+    assert lib.gdn2_test_fwd_state_wait_timeout(p32, N.ptr(buf), N.ptr(big), big.numel(), 0,
+                                                1000, st) == N.ERR_UNSUPPORTED
+    pbf = N.ChunkProblem(1, 128, 128, N.dtype_code(BF), 1, 0.1, tables.struct())
+    assert lib.gdn2_test_fwd_state_wait_timeout(pbf, N.ptr(buf), N.ptr(big), big.numel(), 0,
+                                                0, st) == N.ERR_INVALID
+    assert _fault_word() == 0
