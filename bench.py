@@ -38,6 +38,10 @@ time is the max over ranks.
 * ``decode``: BASELINE config 2 (B=256 H=16 K=V=128 fp32 state, in-place
   recurrent step, bf16 inputs), state read+write GB/s, and the CPU decode
   step timed beside it.
+* ``config3``: BASELINE config 3, a 24-layer decoder (hidden 2048, 16 heads
+  of 128, SwiGLU 5632, vocab 151,936, bf16) with the drop-in block in every
+  layer: one optimizer step over B=8 x T=8192 token ids per GPU, data-
+  parallel (DDP, NCCL gradient all-reduce) at N>1; tokens/s/GPU.
 * ``config0``: BASELINE config 0 (fp32 forward, B=1 T=512 H=4 K=V=64): GPU
   latency of ``chunk_gdn2`` and the CPU chunk and recurrent paths' times.
 * ``block_ops``: the block's prologue / epilogue kernels at config-1 shapes.
@@ -507,9 +511,9 @@ def sp_parity(world, rank, local, x, fwd):
             a, b = a.double(), b.double()
             return float((a - b).norm() / b.norm().clamp_min(1e-30))
 
-        out = {n: round(rel(torch.cat(list(gathered[n].unbind(0)), 1), refs[n]), 6)
-               for n in refs}
-        out["ht"] = round(rel(ht_last, ht_ref), 6)
+        sig = lambda x: float(f"{x:.3e}")
+        out = {n: sig(rel(torch.cat(list(gathered[n].unbind(0)), 1), refs[n])) for n in refs}
+        out["ht"] = sig(rel(ht_last, ht_ref))
         out["heads"] = hs
         out["reference"] = "chunk_gdn2 on the whole 262,144-token sequence on one GPU"
         out["tolerance"] = 2e-2
@@ -818,6 +822,144 @@ def run_block_ops(dev, lib, N, iters=20, warm=3):
 
 
 # ---------------------------------------------------------------------------
+# config 3: a 24-layer decoder with the drop-in block in every layer, DDP
+# ---------------------------------------------------------------------------
+C3 = dict(layers=24, hidden=2048, heads=16, head_dim=128, mlp=5632, vocab=151936, batch=8,
+          seq=8192, micro=1, warmup=2, steps=3)
+
+
+def build_config3_model(dev):
+    """Random-init decoder shaped as BASELINE config 3 (the reference host's
+    block structure, gdn2_gpt/model.py:176-248 and :251-380): embedding, 24 x
+    [RMSNorm -> GatedDeltaNet2 -> residual -> RMSNorm -> SwiGLU -> residual],
+    final RMSNorm, LM head; bf16 parameters."""
+    from torch import nn
+
+    from qwendopamine_b200 import GatedDeltaNet2
+
+    class RMSNorm(nn.Module):
+        def __init__(self, n, eps=1e-5):
+            super().__init__()
+            self.weight = nn.Parameter(torch.ones(n))
+            self.eps = eps
+
+        def forward(self, x):
+            return F.rms_norm(x, (x.shape[-1],), self.weight, self.eps)
+
+    class Block(nn.Module):
+        def __init__(self, i):
+            super().__init__()
+            d = C3["hidden"]
+            self.norm_1, self.norm_2 = RMSNorm(d), RMSNorm(d)
+            self.attn = GatedDeltaNet2(hidden_size=d, num_heads=C3["heads"],
+                                       head_dim=C3["head_dim"], layer_idx=i)
+            self.w1 = nn.Linear(d, C3["mlp"], bias=False)
+            self.w2 = nn.Linear(d, C3["mlp"], bias=False)
+            self.w3 = nn.Linear(C3["mlp"], d, bias=False)
+
+        def forward(self, x):
+            x = x + self.attn(self.norm_1(x))[0]
+            n2 = self.norm_2(x)
+            return x + self.w3(F.silu(self.w1(n2)) * self.w2(n2))
+
+    class Decoder(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.wte = nn.Embedding(C3["vocab"], C3["hidden"])
+            self.h = nn.ModuleList([Block(i) for i in range(C3["layers"])])
+            self.ln_f = RMSNorm(C3["hidden"])
+            self.lm_head = nn.Linear(C3["hidden"], C3["vocab"], bias=False)
+
+        def forward(self, idx, targets):
+            x = self.wte(idx)
+            for blk in self.h:
+                x = blk(x)
+            x = self.ln_f(x)
+            loss = 0.0
+            for a in range(0, idx.shape[1], 2048):  # bounded logits memory
+                logits = self.lm_head(x[:, a:a + 2048]).float()
+                loss = loss + F.cross_entropy(logits.flatten(0, 1), targets[:, a:a + 2048].flatten(),
+                                              reduction="sum")
+            return loss / idx.numel()
+
+    with torch.device(dev):
+        model = Decoder()
+    return model.to(torch.bfloat16)
+
+
+def run_config3(world, rank, local):
+    """Config 3: one optimizer step per timed step over B=8 x T=8192 token ids
+    per GPU (micro-batches of one sequence, gradients accumulated, NCCL
+    all-reduce of the gradients by DDP at N>1), AdamW on bf16 parameters."""
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    model = build_config3_model(dev)
+    n_params = sum(p.numel() for p in model.parameters())
+    gdn_params = sum(p.numel() for blk in model.h for p in blk.attn.parameters())
+    ddp = model
+    if world > 1:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+
+        ddp = DDP(model, device_ids=[local], bucket_cap_mb=256, gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    gen = torch.Generator(device=dev).manual_seed(3 + rank)
+    idx = torch.randint(0, C3["vocab"], (C3["batch"], C3["seq"] + 1), device=dev, generator=gen)
+    nmb = C3["batch"] // C3["micro"]
+
+    def step():
+        for m in range(nmb):
+            sl = slice(m * C3["micro"], (m + 1) * C3["micro"])
+            ctx = ddp.no_sync() if (world > 1 and m + 1 < nmb) else _nullctx()
+            with ctx:
+                loss = ddp(idx[sl, :-1], idx[sl, 1:])
+                (loss / nmb).backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for _ in range(C3["warmup"]):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(C3["steps"]):
+        loss = step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / C3["steps"], world)
+    tokens_gpu = C3["batch"] * C3["seq"]
+    # dense work: 6 N tokens (fwd + bwd of every weight), plus the gdn2 core
+    flops = 6 * n_params * tokens_gpu + C3["layers"] * STEP_FLOPS * C3["heads"] * tokens_gpu
+    peak = peaks()[1]
+    out = {"workload": "config3: 24 x [RMSNorm, GatedDeltaNet2 (B200 kernels), RMSNorm, "
+                       "SwiGLU 5632] decoder, hidden 2048, 16 heads x 128, vocab 151936, bf16; "
+                       "B=8 x T=8192 token ids per GPU as 8 micro-batches of one sequence, "
+                       "AdamW (fused, bf16 parameters) step included",
+           "parallelism": (f"data-parallel x{world} (DDP, NCCL all-reduce of gradients)"
+                           if world > 1 else "single GPU"),
+           "params": n_params, "gdn2_block_params": gdn_params,
+           "ms_per_step": round(ms, 2), "steps": C3["steps"], "warmup": C3["warmup"],
+           "tokens_per_s_per_gpu": round(tokens_gpu / (ms / 1e3), 1),
+           "tokens_per_s": round(world * tokens_gpu / (ms / 1e3), 1),
+           "model_tflops_per_gpu": round(flops / (ms / 1e3) / 1e12, 1),
+           "frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / peak, 4),
+           "loss": round(float(loss), 4)}
+    del ddp, model, opt
+    torch.cuda.empty_cache()
+    return out
+
+
+class _nullctx:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+# ---------------------------------------------------------------------------
 # CPU baselines (reference algorithm, PyTorch CPU restatement)
 # ---------------------------------------------------------------------------
 CPU_SAMPLE_T, CPU_SAMPLE_HEADS = 8192, 8
@@ -982,6 +1124,7 @@ def run_b200(args, world, rank, local):
     torch.cuda.empty_cache()
     c1 = run_config1(args, world, rank, local)
     torch.cuda.empty_cache()
+    c3 = run_config3(world, rank, local) if not args.skip_model else None
     dec = c0 = blk = None
     if rank == 0 and world == 1:
         lib = N.load()
@@ -1037,6 +1180,7 @@ def run_b200(args, world, rank, local):
         "sp_parity": parity,
         "heads": heads,
         "config1": c1,
+        "config3": c3,
         "decode": dec,
         "config0": c0,
         "block_ops": blk,
@@ -1056,6 +1200,8 @@ def main(argv=None):
                     help="config4 (headline, with every sub-record), or only the block "
                          "prologue / epilogue kernels (--steps timed launches each after "
                          "--warmup, one GPU), or only the config-2 decode step")
+    ap.add_argument("--skip-model", action="store_true",
+                    help="leave out the config-3 model step (24-layer decoder)")
     ap.add_argument("--profile", action="store_true",
                     help="small ncu case: config-1 phases at --batch, nothing else")
     ap.add_argument("--batch", type=int, default=2, help="batch of the --profile case")
