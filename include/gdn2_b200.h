@@ -45,7 +45,7 @@ enum {
 enum {
     GDN2_OK = 0,
     GDN2_ERR_INVALID = 1,     /* bad argument: shape, dtype, null pointer, size */
-    GDN2_ERR_UNSUPPORTED = 2, /* valid but not implemented (e.g. K > 128)       */
+    GDN2_ERR_UNSUPPORTED = 2, /* valid but not implemented (e.g. K > 256)       */
     GDN2_ERR_CUDA = 3,        /* a CUDA runtime call failed                     */
     GDN2_ERR_WORKSPACE = 4    /* caller-provided buffer too small               */
 };
@@ -137,13 +137,15 @@ int gdn2_chunk_bwd_state(const gdn2_chunk_problem* p, const void* saved,
                          size_t saved_bytes, const void* dout, const float* dht,
                          float* dh0, void* workspace, size_t workspace_bytes,
                          void* stream);
-/* phase 2: per-chunk gradients (fully parallel over chunks and heads) */
+/* phase 2: per-chunk gradients (fully parallel over chunks and heads); reads
+ * what phase 1 left in `workspace` (and, for heads above 128 channels, uses a
+ * further section of it as scratch) */
 int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p,
                          const void* q, const void* k, const void* v, const float* g,
                          const void* b, const void* w,
                          const void* saved, size_t saved_bytes, const void* dout,
                          void* dq, void* dk, void* dv, float* dg, void* db, void* dw,
-                         const void* workspace, size_t workspace_bytes, void* stream);
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- chunkwise backward without allocation -------------------------------
  * No counterpart in the reference.  gdn2_chunk_bwd with its workspace taken

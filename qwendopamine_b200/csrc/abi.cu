@@ -21,6 +21,10 @@ template <typename T, int D, int BV> cudaError_t launch_fwd_state16(const FwdSta
 template <typename T, int D, int BV> cudaError_t launch_bwd_state16(const BwdStateArgs&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_bwd_intra16(const BwdIntraArgs&, cudaStream_t);
 template <typename T, int D> cudaError_t launch_fwd_intra16(const FwdIntraArgs&, cudaStream_t);
+template <typename T> cudaError_t launch_fwd_intra_wide(const FwdIntraArgs&, cudaStream_t);
+template <typename T> cudaError_t launch_fwd_state_wide(const FwdStateArgs&, cudaStream_t);
+template <typename T> cudaError_t launch_bwd_state_wide(const BwdStateArgs&, cudaStream_t);
+template <typename T> cudaError_t launch_bwd_intra_wide(const BwdIntraArgs&, cudaStream_t);
 bool fwd_state_tc_ok(const FwdStateArgs&, int dtype_bf16);
 cudaError_t launch_fwd_state_tc(const FwdStateArgs&, cudaStream_t);
 bool bwd_state_tc_ok(const BwdStateArgs&, int dtype_bf16);
@@ -55,10 +59,11 @@ bool dtype_ok(int dtype) {
   return dtype == GDN2_DTYPE_F32 || dtype == GDN2_DTYPE_BF16 || dtype == GDN2_DTYPE_F16;
 }
 
-// Head size bucket: kernels are compiled for padded head sizes 64 and 128.
+// Head size bucket: the chunk kernels are compiled for padded head sizes 64
+// and 128 (larger heads take chunk_wide.cu), the decode kernel also for 256.
 int head_bucket(int K, int V) {
   int m = K > V ? K : V;
-  return m <= 64 ? 64 : 128;
+  return m <= 64 ? 64 : (m <= 128 ? 128 : 256);
 }
 
 int check_problem(const gdn2_chunk_problem* p, const char* fn) {
@@ -66,8 +71,8 @@ int check_problem(const gdn2_chunk_problem* p, const char* fn) {
   if (p->H <= 0 || p->K <= 0 || p->V <= 0)
     return fail(GDN2_ERR_INVALID, "%s: H, K, V must be positive (got %d, %d, %d)", fn, p->H, p->K,
                 p->V);
-  if (p->K > 128 || p->V > 128)
-    return fail(GDN2_ERR_UNSUPPORTED, "%s: head sizes up to 128 are supported (K=%d, V=%d)", fn,
+  if (p->K > 256 || p->V > 256)
+    return fail(GDN2_ERR_UNSUPPORTED, "%s: head sizes up to 256 are supported (K=%d, V=%d)", fn,
                 p->K, p->V);
   if (!dtype_ok(p->dtype)) return fail(GDN2_ERR_INVALID, "%s: unknown dtype %d", fn, p->dtype);
   if (p->seqs.n_seqs < 0 || p->seqs.n_chunks < 0)
@@ -80,9 +85,11 @@ int check_problem(const gdn2_chunk_problem* p, const char* fn) {
     return fail(GDN2_ERR_UNSUPPORTED, "%s: too many chunks", fn);
   if (p->gate < 0 || p->gate > 2 || (p->gate && !p->A_log))
     return fail(GDN2_ERR_INVALID, "%s: gate %d needs A_log (modes 0..2)", fn, p->gate);
-  if (p->gate && !(p->dtype == GDN2_DTYPE_BF16 && p->K % 8 == 0 && p->V % 8 == 0))
+  if (p->gate && !(p->dtype == GDN2_DTYPE_BF16 && p->K % 8 == 0 && p->V % 8 == 0 &&
+                   p->K <= 128 && p->V <= 128))
     return fail(GDN2_ERR_UNSUPPORTED,
-                "%s: the gate in kernel is served by the bf16 kernels (K, V multiples of 8)", fn);
+                "%s: the gate in kernel is served by the bf16 kernels (K, V multiples of 8, "
+                "up to 128)", fn);
   return GDN2_OK;
 }
 
@@ -139,6 +146,14 @@ template <typename T, int D> struct RunBwdIntra {
 template <typename T, int D> struct RunRec {
   static cudaError_t run(const RecArgs& a, cudaStream_t s) { return launch_recurrent<T, D>(a, s); }
 };
+cudaError_t dispatch_rec(int dtype, int bucket, const RecArgs& a, cudaStream_t st) {
+  if (bucket == 256) {
+    if (dtype == GDN2_DTYPE_F32) return launch_recurrent<float, 256>(a, st);
+    if (dtype == GDN2_DTYPE_BF16) return launch_recurrent<__nv_bfloat16, 256>(a, st);
+    return launch_recurrent<__half, 256>(a, st);
+  }
+  return dispatch<RunRec>(dtype, bucket, a, st);
+}
 
 // State passes: 16-bit inputs whose head sizes are multiples of 8 take the
 // ldmatrix / m16n8k16 kernels (state16.cu); everything else the generic ones.
@@ -169,8 +184,32 @@ cudaError_t run_state16(const Args& a, int bucket, int cols, int n_seqs, int H, 
 // bf16 represents (8-bit exponent) and fp16 does not, so fp16 problems stay
 // on the fp32-staged kernels.
 bool use16(const gdn2_chunk_problem* p) {
-  return p->dtype == GDN2_DTYPE_BF16 && (p->K % 8) == 0 && (p->V % 8) == 0;
+  return p->dtype == GDN2_DTYPE_BF16 && (p->K % 8) == 0 && (p->V % 8) == 0 && p->K <= 128 &&
+         p->V <= 128;
 }
+
+// Heads above 128 channels (K or V) take the slab-walking kernels of
+// chunk_wide.cu, for every dtype.
+bool use_wide(const gdn2_chunk_problem* p) { return wide_heads(p->K, p->V); }
+
+template <template <typename> class F, typename Args>
+cudaError_t dispatch_wide(int dtype, const Args& a, cudaStream_t st) {
+  if (dtype == GDN2_DTYPE_F32) return F<float>::run(a, st);
+  if (dtype == GDN2_DTYPE_BF16) return F<__nv_bfloat16>::run(a, st);
+  return F<__half>::run(a, st);
+}
+template <typename T> struct RunFwdIntraW {
+  static cudaError_t run(const FwdIntraArgs& a, cudaStream_t s) { return launch_fwd_intra_wide<T>(a, s); }
+};
+template <typename T> struct RunFwdStateW {
+  static cudaError_t run(const FwdStateArgs& a, cudaStream_t s) { return launch_fwd_state_wide<T>(a, s); }
+};
+template <typename T> struct RunBwdStateW {
+  static cudaError_t run(const BwdStateArgs& a, cudaStream_t s) { return launch_bwd_state_wide<T>(a, s); }
+};
+template <typename T> struct RunBwdIntraW {
+  static cudaError_t run(const BwdIntraArgs& a, cudaStream_t s) { return launch_bwd_intra_wide<T>(a, s); }
+};
 
 bool aligned16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; }
 
@@ -189,6 +228,7 @@ int check_aligned16(const gdn2_chunk_problem* p, const char* fn,
 // bf16 with K = V = 128 (the pre-scan excepted) runs the forward state pass
 // on tcgen05 / TMEM / TMA (state_tc.cu).
 cudaError_t fwd_state_dispatch(const gdn2_chunk_problem* p, const FwdStateArgs& a, cudaStream_t st) {
+  if (use_wide(p)) return dispatch_wide<RunFwdStateW>(p->dtype, a, st);
   const int bucket = head_bucket(p->K, p->V);
   if (fwd_state_tc_ok(a, p->dtype == GDN2_DTYPE_BF16)) return launch_fwd_state_tc(a, st);
   if (use16(p)) {
@@ -199,6 +239,7 @@ cudaError_t fwd_state_dispatch(const gdn2_chunk_problem* p, const FwdStateArgs& 
 }
 
 cudaError_t bwd_state_dispatch(const gdn2_chunk_problem* p, const BwdStateArgs& a, cudaStream_t st) {
+  if (use_wide(p)) return dispatch_wide<RunBwdStateW>(p->dtype, a, st);
   const int bucket = head_bucket(p->K, p->V);
   if (bwd_state_tc_ok(a, p->dtype == GDN2_DTYPE_BF16)) return launch_bwd_state_tc(a, st);
   if (use16(p)) {
@@ -208,6 +249,7 @@ cudaError_t bwd_state_dispatch(const gdn2_chunk_problem* p, const BwdStateArgs& 
 }
 
 cudaError_t fwd_intra_dispatch(const gdn2_chunk_problem* p, const FwdIntraArgs& a, cudaStream_t st) {
+  if (use_wide(p)) return dispatch_wide<RunFwdIntraW>(p->dtype, a, st);
   const int bucket = head_bucket(p->K, p->V);
   if (use16(p)) {
     return bucket == 64 ? launch_fwd_intra16<__nv_bfloat16, 64>(a, st)
@@ -217,6 +259,7 @@ cudaError_t fwd_intra_dispatch(const gdn2_chunk_problem* p, const FwdIntraArgs& 
 }
 
 cudaError_t bwd_intra_dispatch(const gdn2_chunk_problem* p, const BwdIntraArgs& a, cudaStream_t st) {
+  if (use_wide(p)) return dispatch_wide<RunBwdIntraW>(p->dtype, a, st);
   const int bucket = head_bucket(p->K, p->V);
   if (use16(p)) {
     return bucket == 64 ? launch_bwd_intra16<__nv_bfloat16, 64>(a, st)
@@ -414,7 +457,7 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
                          const void* v, const float* g, const void* b, const void* w,
                          const void* saved, size_t saved_bytes, const void* dout, void* dq,
                          void* dk, void* dv, float* dg, void* db, void* dw,
-                         const void* workspace, size_t workspace_bytes, void* stream) {
+                         void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_problem(p, "gdn2_chunk_bwd_intra");
   if (rc) return rc;
   if (!q || !k || !v || !g || !b || !w || !saved || !dout || !dq || !dk || !dv || !dg || !db || !dw)
@@ -441,7 +484,7 @@ int gdn2_chunk_bwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.dout = dout;
   a.saved = static_cast<const unsigned char*>(saved);
   a.L = L;
-  a.ws = static_cast<const unsigned char*>(workspace);
+  a.ws = static_cast<unsigned char*>(workspace);
   a.BL = BL;
   a.dq = dq; a.dk = dk; a.dv = dv; a.dg = dg; a.db = db; a.dw = dw;
   a.total_rows = p->seqs.total_tokens;
@@ -473,8 +516,8 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p, const void* q, const voi
   if (p->HV % p->H != 0)
     return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: HV=%d is not a multiple of H=%d", p->HV,
                 p->H);
-  if (p->K > 128 || p->V > 128)
-    return fail(GDN2_ERR_UNSUPPORTED, "gdn2_recurrent_fwd: head sizes up to 128 are supported");
+  if (p->K > 256 || p->V > 256)
+    return fail(GDN2_ERR_UNSUPPORTED, "gdn2_recurrent_fwd: head sizes up to 256 are supported");
   if (!dtype_ok(p->dtype)) return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: unknown dtype");
   if (p->cu_seqlens && p->B != 1)
     return fail(GDN2_ERR_INVALID, "gdn2_recurrent_fwd: cu_seqlens requires B == 1 (got %d)", p->B);
@@ -513,7 +556,7 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p, const void* q, const voi
   a.h0 = h0; a.o = o; a.ht = ht;
   cudaError_t e = fault_word(&a.fault);
   if (e != cudaSuccess) return cuda_fail(e, "gdn2_recurrent_fwd");
-  e = dispatch<RunRec>(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
+  e = dispatch_rec(p->dtype, head_bucket(p->K, p->V), a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_recurrent_fwd");
 }
 

@@ -109,7 +109,7 @@ struct BwdIntraArgs {
   const void* dout;
   const unsigned char* saved;
   SavedLayout L;
-  const unsigned char* ws;
+  unsigned char* ws;   // dh, dVN (read); the wide kernels' fp32 dq / dk rows (written)
   BwdLayout BL;
   void* dq;
   void* dk;

@@ -340,10 +340,13 @@ __host__ __device__ inline SavedLayout saved_layout(int64_t n_chunks, int H, int
 
 // Backward workspace per (chunk, head):  dh : [K][V] (T)  gradient w.r.t. the
 // state leaving the chunk;  dVN : [64][V] (T), stored transposed ([V][64]) by
-// the bf16 tensor-core path, like VN.
+// the bf16 tensor-core path, like VN;  for head sizes above 128 only, qk :
+// [2][64][K] fp32, the pre-norm dq and dk rows (chunk_wide.cu).
 struct BwdLayout {
-  size_t dh, dvn, total;
+  size_t dh, dvn, qk, total;
 };
+
+__host__ __device__ inline bool wide_heads(int K, int V) { return K > 128 || V > 128; }
 
 __host__ __device__ inline BwdLayout bwd_layout(int64_t n_chunks, int H, int K, int V,
                                                 int esize) {
@@ -352,6 +355,8 @@ __host__ __device__ inline BwdLayout bwd_layout(int64_t n_chunks, int H, int K, 
   size_t off = 0;
   L.dh = off; off = align256(off + nh * (size_t)K * V * esize);
   L.dvn = off; off = align256(off + nh * kChunk * V * esize);
+  L.qk = off;
+  if (wide_heads(K, V)) off = align256(off + nh * 2 * kChunk * (size_t)K * sizeof(float));
   L.total = off;
   return L;
 }

@@ -503,7 +503,8 @@ bool recurrent_stream_ok(const RecArgs& a) {
 
 template <typename T, int D>
 cudaError_t launch_recurrent(const RecArgs& a, cudaStream_t st) {
-  if (recurrent_stream_ok<T, D>(a)) {
+  if constexpr (D <= 128) {  // a 256 x 256 state ring would not fit shared memory
+   if (recurrent_stream_ok<T, D>(a)) {
     const int n_units = a.n_seqs * a.HV;
     if (n_units == 0) return cudaSuccess;
     auto kern = k_recurrent_stream<T, D>;
@@ -516,8 +517,11 @@ cudaError_t launch_recurrent(const RecArgs& a, cudaStream_t st) {
     const int grid = n_units < sms ? n_units : sms;
     kern<<<grid, 512, RecStreamSmem<D>::bytes, st>>>(a);
     return cudaGetLastError();
+   }
   }
-  constexpr int VB = 64;
+  // 256-row states take 32-column slices (32 state floats per thread, as
+  // the 64-column slices of 128-row states)
+  constexpr int VB = D > 128 ? 32 : 64;
   const int nvs = (a.V + VB - 1) / VB;
   dim3 grid(a.n_seqs * a.HV * nvs);
   k_recurrent<T, D, VB><<<grid, kThreads, 0, st>>>(a);
@@ -531,5 +535,8 @@ GDN2_INST_REC(__nv_bfloat16, 64)
 GDN2_INST_REC(__nv_bfloat16, 128)
 GDN2_INST_REC(__half, 64)
 GDN2_INST_REC(__half, 128)
+GDN2_INST_REC(float, 256)
+GDN2_INST_REC(__nv_bfloat16, 256)
+GDN2_INST_REC(__half, 256)
 
 }  // namespace gdn2

@@ -48,8 +48,9 @@ def _problem(H, K, V, dtype, l2norm, scale, tables, gate=None, dA_log=None, ddt_
 
 def _gate_in_kernel_ok(dtype, K, V):
     """The bf16 kernels apply the gate themselves (the C ABI's 16-bit path:
-    bf16, K and V multiples of 8); other problems gate with torch ops."""
-    return dtype == torch.bfloat16 and K % 8 == 0 and V % 8 == 0
+    bf16, K and V multiples of 8 up to 128); other problems gate with torch
+    ops."""
+    return dtype == torch.bfloat16 and K % 8 == 0 and V % 8 == 0 and K <= 128 and V <= 128
 
 
 def _require_cuda(*ts):

@@ -69,8 +69,10 @@ def test_invalid_problem_is_rejected_with_message(lib):
     bad = _problem(K=0)
     assert lib.gdn2_chunk_saved_bytes(bad) == 0
     assert b"positive" in lib.gdn2_last_error()
-    big = _problem(K=256)
+    big = _problem(K=264)  # the reference accepts K <= 256 (chunk_gdn2.py:1380)
     assert lib.gdn2_chunk_fwd_intra(big, *([None] * 6), None, 0, None) == N.ERR_UNSUPPORTED
+    assert b"up to 256" in lib.gdn2_last_error()
+    assert lib.gdn2_chunk_saved_bytes(_problem(K=256, V=256)) > 0
     with pytest.raises(NotImplementedError):
         N.check(N.ERR_UNSUPPORTED, "x")
     nodtype = _problem(dtype=7)
@@ -127,7 +129,7 @@ def test_recurrent_argument_checks(lib):
     args = [f] * 6 + [None, f, None, None]
     assert lib.gdn2_recurrent_fwd(rp(HV=3), *args) == N.ERR_INVALID
     assert b"multiple" in lib.gdn2_last_error()
-    assert lib.gdn2_recurrent_fwd(rp(K=200), *args) == N.ERR_UNSUPPORTED
+    assert lib.gdn2_recurrent_fwd(rp(K=300), *args) == N.ERR_UNSUPPORTED
     assert lib.gdn2_recurrent_fwd(rp(cu_seqlens=0x1000), *args) == N.ERR_INVALID
     assert lib.gdn2_recurrent_fwd(rp(n_seqs=3), *args) == N.ERR_INVALID
     assert lib.gdn2_recurrent_fwd(rp(state_indices=0x1000, state_stride=5), *args) == N.ERR_INVALID
