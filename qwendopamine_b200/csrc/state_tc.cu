@@ -725,6 +725,375 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Forward state pass split over value columns: two CTAs per (sequence, head),
+// each owning 64 of the 128 value columns, for launches whose full-width
+// grid would leave most SMs idle (B*H well below the SM count).  Each chunk's
+// serial chain then carries half the tensor-memory traffic and half the
+// products.  Every product keeps M = 128 by stacking:
+//   D[0:64)   = W h_half      -> VN = U - W h      (lanes = tokens)
+//   D[64:128) = Qg h_half     -> o = Qg h + Aqk VN (lanes = tokens)
+//   A = [W ; Qg] (K-major, two 64-row TMA boxes back to back per key half);
+//   o: D += [0 ; Aqk] VN      (a zero box in front of Aqk; the upper lanes
+//                              only gain zeros)
+//   h_half += Kd^T VN         (A = Kd, MN-major; B = VN [t][v], MN-major)
+// TMEM: cols [0,64) D, cols [64,128) h_half (lane = key row).  Same rounding
+// points as k_fwd_state_tc; VN leaves value-major ([V][64]) as the backward
+// reads it.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kHOffWQ = 0;                 // [W_k0 | Qg_k0 | W_k1 | Qg_k1]
+constexpr uint32_t kHOffKd = 4 * kBox;          // [Kd_k0 | Kd_k1]
+constexpr uint32_t kHOffZ = 6 * kBox;           // zeros, then Aqk right after
+constexpr uint32_t kHOffAqk = 7 * kBox;
+constexpr uint32_t kHOffU = 8 * kBox;           // U columns of this half, swizzled
+constexpr uint32_t kHOffGl = 9 * kBox;          // [128] fp32
+constexpr uint32_t kHSlotBytes = 9 * kBox + 1024;
+constexpr uint32_t kHTxBytes = 8 * kBox + kGlBytes;  // the zero box is not copied
+constexpr uint32_t kHOffH = 2 * kHSlotBytes;    // bf16 h_half [k][64 v], MN-major (16 KB)
+constexpr uint32_t kHOffVN = kHOffH + 2 * kBox; // bf16 VN [t][64 v], MN-major (8 KB)
+constexpr uint32_t kHOffVT = kHOffVN + kBox;    // bf16 VN^T [64 v][t], plain (8 KB)
+constexpr uint32_t kHOffO = kHOffVT + kBox;     // bf16 o [t][64 v], chunk-swizzled (8 KB)
+constexpr uint32_t kHOffBar = kHOffO + kBox;
+constexpr uint32_t kHSmemBytes = kHOffBar + 64 + 1024;
+constexpr uint32_t kHColD = 0, kHColH = 64, kHTmemCols = 128;
+constexpr uint32_t kIdWQh = tc::idesc_bf16(128, 64, 0, 1);  // [W;Qg] h_half, [0;Aqk] VN
+constexpr uint32_t kIdKVh = tc::idesc_bf16(128, 64, 1, 1);  // Kd^T VN
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    k_fwd_state_tc_half(FwdStateArgs a, const __grid_constant__ CUtensorMap mW,
+                        const __grid_constant__ CUtensorMap mQg,
+                        const __grid_constant__ CUtensorMap mKd,
+                        const __grid_constant__ CUtensorMap mAqk,
+                        const __grid_constant__ CUtensorMap mU) {
+  using T = __nv_bfloat16;
+  constexpr int K = 128, V = 128;
+  extern __shared__ unsigned char smraw[];
+  unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kHOffBar);  // [2]
+  uint64_t* mma1 = full + 2;
+  uint64_t* mma2 = full + 3;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(full + 4);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+  unsigned char* sH = sm + kHOffH;
+  unsigned char* sVN = sm + kHOffVN;
+  unsigned char* sVT = sm + kHOffVT;
+  unsigned char* sO = sm + kHOffO;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int row = quad * 32 + lane;      // the TMEM lane this thread reads
+  const int H = a.H;
+  const int nh = blockIdx.x >> 1, vh = blockIdx.x & 1, n = nh / H, h = nh - n * H;
+  const int v0 = 64 * vh;                // this CTA's value columns [v0, v0 + 64)
+  const int c_begin = a.seqs.coff[n], c_end = a.seqs.coff[n + 1];
+  const int64_t bos = a.seqs.cu[n], eos = a.seqs.cu[n + 1];
+  const int64_t ldo = (int64_t)H * V;
+  const float* h0 = a.h0 ? a.h0 + (int64_t)nh * K * V : nullptr;
+  float* ht = a.ht ? a.ht + (int64_t)nh * K * V : nullptr;
+  const uint64_t lim = a.wait_ns ? a.wait_ns : tc::kWaitLimitNs;
+
+  if (c_begin >= c_end) {  // empty sequence: the state passes through
+    if (ht)
+      for (int i = tid; i < K * 64; i += kTcThreads) {
+        const int k = i >> 6, v = v0 + (i & 63);
+        ht[(size_t)k * V + v] = h0 ? h0[(size_t)k * V + v] : 0.f;
+      }
+    return;
+  }
+
+  // the zero boxes stacked over Aqk (never written by TMA)
+  for (int i = tid; i < 2 * (int)(kBox / 16); i += kTcThreads) {
+    const int slot = i / (int)(kBox / 16), e = i - slot * (int)(kBox / 16);
+    st_shared_v4(sm + slot * kHSlotBytes + kHOffZ + 16 * e, make_uint4(0u, 0u, 0u, 0u));
+  }
+  if (tid == 0) {
+    tc::mbar_init(&full[0], 1);
+    tc::mbar_init(&full[1], 1);
+    tc::mbar_init(mma1, 1);
+    tc::mbar_init(mma2, 1);
+    *sAbort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(sTmem, kHTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const uint32_t tlane = tmem + ((uint32_t)(quad * 32) << 16);
+
+  int next_issue = c_begin;
+  int mma1_commits = 0, mma2_commits = 0;
+  auto issue = [&](int c) {
+    if (c == a.skip_chunk) {  // test of the abort path: this chunk never arrives
+      next_issue = c + 1;
+      return;
+    }
+    const int slot = (c - c_begin) & 1;
+    unsigned char* p = sm + slot * kHSlotBytes;
+    const size_t ch = (size_t)c * H + h;
+    const int y = (int)(ch * kChunk);
+    tc::mbar_expect_tx(&full[slot], kHTxBytes);
+    tc::tma_load_2d(p + kHOffWQ, &mW, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kHOffWQ + kBox, &mQg, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kHOffWQ + 2 * kBox, &mW, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kHOffWQ + 3 * kBox, &mQg, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kHOffKd, &mKd, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kHOffKd + kBox, &mKd, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kHOffAqk, &mAqk, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kHOffU, &mU, v0, y, &full[slot]);
+    tc::bulk_load(p + kHOffGl, a.saved + a.L.gl + ch * K * sizeof(float), kGlBytes, &full[slot]);
+    next_issue = c + 1;
+  };
+  if (tid == 0) {
+    issue(c_begin);
+    if (c_begin + 1 < c_end) issue(c_begin + 1);
+  }
+
+  // bf16 copy of this thread's 32 state values (key row `row`, value columns
+  // 32*half ..) into the MN-major operand tile
+  auto emit_state = [&](const float (&s)[32]) {
+    unsigned char* srow = sH + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 x;
+      x.x = pack2<T>(s[8 * q + 0], s[8 * q + 1]);
+      x.y = pack2<T>(s[8 * q + 2], s[8 * q + 3]);
+      x.z = pack2<T>(s[8 * q + 4], s[8 * q + 5]);
+      x.w = pack2<T>(s[8 * q + 6], s[8 * q + 7]);
+      st_shared_v4(srow + (((4 * half + q) ^ (row & 7)) << 4), x);
+    }
+  };
+  auto scale_store = [&](const float (&s)[32], int slot) {
+    const float gl = reinterpret_cast<const float*>(sm + slot * kHSlotBytes + kHOffGl)[row];
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = s[i] * gl;
+    tc::tmem_st32(tlane + kHColH + 32 * half, x);
+  };
+  auto copy_ckpt = [&](int c) {  // sH -> checkpoint rows, columns [v0, v0 + 64)
+    T* gh = reinterpret_cast<T*>(a.saved + a.L.h) + ((size_t)c * H + h) * (size_t)K * V + v0;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int k = idx >> 3, ci = idx & 7;
+      const uint4 x = ld_shared_v4(sH + (k >> 3) * 1024 + (k & 7) * 128 + ((ci ^ (k & 7)) << 4));
+      *reinterpret_cast<uint4*>(gh + (size_t)k * V + 8 * ci) = x;
+    }
+  };
+  auto copy_vt = [&](int c) {  // sVT -> VN^T rows [v0, v0 + 64) of chunk c
+    T* gv = reinterpret_cast<T*>(a.saved + a.L.vn) + ((size_t)c * H + h) * (size_t)kChunk * V +
+            (size_t)v0 * kChunk;
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int v = idx >> 3, ci = idx & 7;
+      *reinterpret_cast<uint4*>(gv + (size_t)v * kChunk + 8 * ci) =
+          ld_shared_v4(sVT + v * 128 + ci * 16);
+    }
+  };
+  auto copy_o = [&](int c) {  // sO -> output rows of chunk c, columns [v0, v0 + 64)
+    const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
+    T* go = reinterpret_cast<T*>(a.o) + cp.row0 * ldo + (int64_t)h * V + v0;
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int t = idx >> 3, ci = idx & 7;
+      if (t < cp.len)
+        *reinterpret_cast<uint4*>(go + (int64_t)t * ldo + 8 * ci) =
+            ld_shared_v4(sO + t * 128 + ((ci ^ (t & 7)) << 4));
+    }
+  };
+
+  // ---- initial state ----------------------------------------------------------
+  {
+    const bool ok = tc::warp_wait(&full[0], 0, lim);
+    if (ok) {
+      float s[32];
+      if (h0) {
+        const float4* src = reinterpret_cast<const float4*>(h0 + (size_t)row * V + v0 + 32 * half);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 x = src[i];
+          s[4 * i] = x.x;
+          s[4 * i + 1] = x.y;
+          s[4 * i + 2] = x.z;
+          s[4 * i + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = 0.f;
+      }
+      emit_state(s);
+      scale_store(s, 0);
+    } else if (lane == 0) {
+      *sAbort = 1;
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+  }
+
+  int c = c_begin;
+  if (!*sAbort) {
+    for (; c < c_end; ++c) {
+      const int i = c - c_begin, slot = i & 1;
+      unsigned char* p = sm + slot * kHSlotBytes;
+      const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
+
+      // 1. D = [W ; Qg] h_half;  meanwhile the checkpoint of chunk c and the
+      //    previous chunk's o leave through the copy units
+      if (tid == 0) {
+        if (!tc::mbar_wait(&full[slot], par_full, lim)) {
+          *sAbort = 1;
+        } else {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::umma_bf16(tmem + kHColD, desc_k(p + kHOffWQ + (j >> 2) * 2 * kBox + (j & 3) * 32),
+                          desc_mn(sH + j * 2048, kBox), kIdWQh, j > 0);
+          tc::umma_commit(mma1);
+          ++mma1_commits;
+        }
+      }
+      copy_ckpt(c);
+      if (c > c_begin) copy_o(c - 1);
+      // 2. VN = U - W h (lanes 0-63): bf16 VN [t][v] operand tile and its
+      //    value-major copy for the saved buffer
+      {
+        bool ok = tc::warp_wait(mma1, par_mma, lim);
+        if (ok) ok = tc::warp_wait(&full[slot], par_full, lim);
+        if (ok && quad < 2) {
+          tc::tc_fence_after();
+          uint32_t x[32];
+          tc::tmem_ld32(tlane + kHColD + 32 * half, x);
+          const int t = row;  // token
+          uint4 u4[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            u4[q] = ld_shared_v4(p + kHOffU + (t >> 3) * 1024 + (t & 7) * 128 +
+                                 (((4 * half + q) ^ (t & 7)) << 4));
+          tc::tmem_wait_ld();
+          unsigned char* vrow = sVN + (t >> 3) * 1024 + (t & 7) * 128;
+          T* vt = reinterpret_cast<T*>(sVT) + t;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t uw[4] = {u4[q].x, u4[q].y, u4[q].z, u4[q].w};
+            float vn[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 u2 = unpack2<T>(uw[e]);
+              vn[2 * e] = u2.x - __uint_as_float(x[8 * q + 2 * e]);
+              vn[2 * e + 1] = u2.y - __uint_as_float(x[8 * q + 2 * e + 1]);
+            }
+            uint4 y;
+            y.x = pack2<T>(vn[0], vn[1]);
+            y.y = pack2<T>(vn[2], vn[3]);
+            y.z = pack2<T>(vn[4], vn[5]);
+            y.w = pack2<T>(vn[6], vn[7]);
+            st_shared_v4(vrow + (((4 * half + q) ^ (t & 7)) << 4), y);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              vt[(32 * half + 8 * q + e) * kChunk] = from_f<T>(vn[e]);
+          }
+        }
+        if (!ok && lane == 0) *sAbort = 1;
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+      // 3. o += [0 ; Aqk] VN,  h_half += Kd^T VN;  meanwhile VN^T leaves
+      if (tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_bf16(tmem + kHColD, desc_k(p + kHOffZ + j * 32), desc_mn(sVN + j * 2048, kBox),
+                        kIdWQh, 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_bf16(tmem + kHColH, desc_mn(p + kHOffKd + j * 2048, kBox),
+                        desc_mn(sVN + j * 2048, kBox), kIdKVh, 1);
+        tc::umma_commit(mma2);
+        ++mma2_commits;
+      }
+      copy_vt(c);
+      // 4. o (lanes 64-127) -> staging; new state -> bf16 operand tile (the
+      //    next checkpoint), scaled in place by the next chunk's 2^G_last
+      {
+        const bool has_next = c + 1 < c_end;
+        bool ok = tc::warp_wait(mma2, par_mma, lim);
+        if (ok && has_next) ok = tc::warp_wait(&full[slot ^ 1], ((i + 1) >> 1) & 1, lim);
+        if (ok) {
+          tc::tc_fence_after();
+          if (quad >= 2) {
+            uint32_t x[32];
+            tc::tmem_ld32(tlane + kHColD + 32 * half, x);
+            tc::tmem_wait_ld();
+            const int t = row - 64;
+            unsigned char* orow = sO + t * 128;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 y;
+              y.x = pack2<T>(__uint_as_float(x[8 * q + 0]), __uint_as_float(x[8 * q + 1]));
+              y.y = pack2<T>(__uint_as_float(x[8 * q + 2]), __uint_as_float(x[8 * q + 3]));
+              y.z = pack2<T>(__uint_as_float(x[8 * q + 4]), __uint_as_float(x[8 * q + 5]));
+              y.w = pack2<T>(__uint_as_float(x[8 * q + 6]), __uint_as_float(x[8 * q + 7]));
+              st_shared_v4(orow + (((4 * half + q) ^ (t & 7)) << 4), y);
+            }
+          }
+          float s[32];
+          {
+            uint32_t hx[32];
+            tc::tmem_ld32(tlane + kHColH + 32 * half, hx);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(hx[e]);
+          }
+          if (has_next) {
+            emit_state(s);
+            scale_store(s, slot ^ 1);
+          } else if (ht) {
+            float4* dst = reinterpret_cast<float4*>(ht + (size_t)row * V + v0 + 32 * half);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              dst[e] = make_float4(s[4 * e], s[4 * e + 1], s[4 * e + 2], s[4 * e + 3]);
+          }
+        } else if (lane == 0) {
+          *sAbort = 1;
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+      if (tid == 0 && c + 2 < c_end) issue(c + 2);
+    }
+  }
+
+  // ---- teardown ---------------------------------------------------------------
+  const bool aborted = *sAbort != 0;
+  if (!aborted) copy_o(c_end - 1);
+  if (aborted && tid == 0) {
+    for (int j = c; j < next_issue; ++j) {
+      const int ij = j - c_begin;
+      tc::mbar_wait(&full[ij & 1], (ij >> 1) & 1, lim);
+    }
+    if (mma1_commits > 0) tc::mbar_wait(mma1, (mma1_commits - 1) & 1, lim);
+    if (mma2_commits > 0) tc::mbar_wait(mma2, (mma2_commits - 1) & 1, lim);
+    atomicOr(&g_gdn2_fault, 1u);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kHTmemCols);
+  }
+}
+
 // ---- host side -----------------------------------------------------------------
 bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_x,
               bool swizzle) {
@@ -788,11 +1157,24 @@ cudaError_t launch_fwd_state_tc(const FwdStateArgs& a, cudaStream_t st) {
       !make_map(&mAqk, a.saved + a.L.aqk, 64, rows, 64, true) ||
       !make_map(&mU, a.saved + a.L.u, 128, rows, 128, false))
     return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k_fwd_state_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmemBytes);
-  if (e != cudaSuccess) return e;
   const int grid = a.seqs.n_seqs * a.H;
   if (grid == 0) return cudaSuccess;
+  int sms = 0;
+  cudaError_t e = num_sms(&sms);
+  if (e != cudaSuccess) return e;
+  if (2 * grid <= sms) {
+    // few sequence-heads: two CTAs each, one per half of the value columns
+    CUtensorMap mUh;
+    if (!make_map(&mUh, a.saved + a.L.u, 128, rows, 64, true)) return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(k_fwd_state_tc_half, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kHSmemBytes);
+    if (e != cudaSuccess) return e;
+    k_fwd_state_tc_half<<<2 * grid, kTcThreads, kHSmemBytes, st>>>(a, mW, mQg, mKd, mAqk, mUh);
+    return cudaGetLastError();
+  }
+  e = cudaFuncSetAttribute(k_fwd_state_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
   k_fwd_state_tc<<<grid, kTcThreads, kSmemBytes, st>>>(a, mW, mQg, mKd, mAqk, mU);
   return cudaGetLastError();
 }
