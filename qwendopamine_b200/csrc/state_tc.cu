@@ -1094,6 +1094,339 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Backward state pass split over value columns (as k_fwd_state_tc_half):
+// two CTAs per (sequence, head), 64 value columns each.  Products keep
+// M = 128 by stacking zero boxes under the token-major operands:
+//   D[0:64) = dVN_half = Aqk^T dO_half + Kd dh_half   (lanes = tokens)
+//     A = [Aqk^T ; 0] (MN-major, the zero box one M-atom further) and
+//     A = [Kd ; 0]    (K-major, a zero box after each Kd key-half box)
+//   dh_half += Qg^T dO_half + W^T (-dVN_half)          (lanes = key rows)
+// TMEM: cols [0,64) D, cols [64,128) dh_half.  Same rounding points as
+// k_bwd_state_tc; dVN leaves value-major ([V][64]).
+// ---------------------------------------------------------------------------
+constexpr uint32_t kBOffAZ = 0;                  // [Aqk | 0]
+constexpr uint32_t kBOffKZ = 2 * kBox;           // [Kd_k0 | 0 | Kd_k1 | 0]
+constexpr uint32_t kBOffQg = 6 * kBox;           // [Qg_k0 | Qg_k1]
+constexpr uint32_t kBOffW = 8 * kBox;            // [W_k0 | W_k1]
+constexpr uint32_t kBOffDO = 10 * kBox;          // dO columns of this half, swizzled
+constexpr uint32_t kBOffGl = 11 * kBox;          // [128] fp32
+constexpr uint32_t kBSlotBytes = 11 * kBox + 1024;
+constexpr uint32_t kBTxBytes = 8 * kBox + kGlBytes;  // zero boxes are not copied
+constexpr uint32_t kBOffH = 2 * kBSlotBytes;     // bf16 dh_half [k][64 v], MN-major (16 KB)
+constexpr uint32_t kBOffVN = kBOffH + 2 * kBox;  // bf16 -dVN [t][64 v], MN-major (8 KB)
+constexpr uint32_t kBOffVT = kBOffVN + kBox;     // bf16 dVN^T [64 v][t], plain (8 KB)
+constexpr uint32_t kBOffBar = kBOffVT + kBox;
+constexpr uint32_t kBSmemBytes = kBOffBar + 64 + 1024;
+constexpr uint32_t kIdMNh = tc::idesc_bf16(128, 64, 1, 1);  // MN-major A, MN-major B
+constexpr uint32_t kIdKNh = tc::idesc_bf16(128, 64, 0, 1);  // K-major A, MN-major B
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    k_bwd_state_tc_half(BwdStateArgs a, const __grid_constant__ CUtensorMap mW,
+                        const __grid_constant__ CUtensorMap mQg,
+                        const __grid_constant__ CUtensorMap mKd,
+                        const __grid_constant__ CUtensorMap mAqk,
+                        const __grid_constant__ CUtensorMap mDO) {
+  using T = __nv_bfloat16;
+  constexpr int K = 128, V = 128;
+  extern __shared__ unsigned char smraw[];
+  unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kBOffBar);  // [2]
+  uint64_t* mma1 = full + 2;
+  uint64_t* mma2 = full + 3;
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(full + 4);
+  volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
+  unsigned char* sH = sm + kBOffH;
+  unsigned char* sVN = sm + kBOffVN;
+  unsigned char* sVT = sm + kBOffVT;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int row = quad * 32 + lane;
+  const int H = a.H;
+  const int nh = blockIdx.x >> 1, vh = blockIdx.x & 1, n = nh / H, h = nh - n * H;
+  const int v0 = 64 * vh;
+  const int c_begin = a.seqs.coff[n], c_end = a.seqs.coff[n + 1];
+  const int64_t bos = a.seqs.cu[n], eos = a.seqs.cu[n + 1];
+  const float* dht = a.dht ? a.dht + (int64_t)nh * K * V : nullptr;
+  float* dh0 = a.dh0 ? a.dh0 + (int64_t)nh * K * V : nullptr;
+
+  if (c_begin >= c_end) {  // empty sequence: the gradient passes through
+    if (dh0)
+      for (int i = tid; i < K * 64; i += kTcThreads) {
+        const int k = i >> 6, v = v0 + (i & 63);
+        dh0[(size_t)k * V + v] = dht ? dht[(size_t)k * V + v] : 0.f;
+      }
+    return;
+  }
+
+  // zero boxes stacked under Aqk^T and Kd (never written by TMA)
+  for (int i = tid; i < 2 * 3 * (int)(kBox / 16); i += kTcThreads) {
+    const int slot = i / (3 * (int)(kBox / 16)), e = i - slot * 3 * (int)(kBox / 16);
+    const int box = e / (int)(kBox / 16), o = e - box * (int)(kBox / 16);
+    const uint32_t off = box == 0 ? kBOffAZ + kBox : (box == 1 ? kBOffKZ + kBox : kBOffKZ + 3 * kBox);
+    st_shared_v4(sm + slot * kBSlotBytes + off + 16 * o, make_uint4(0u, 0u, 0u, 0u));
+  }
+  if (tid == 0) {
+    tc::mbar_init(&full[0], 1);
+    tc::mbar_init(&full[1], 1);
+    tc::mbar_init(mma1, 1);
+    tc::mbar_init(mma2, 1);
+    *sAbort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(sTmem, kHTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const uint32_t tlane = tmem + ((uint32_t)(quad * 32) << 16);
+
+  // chunk c sits in slot (c_end - 1 - c) & 1
+  int next_issue = c_end - 1;
+  int mma1_commits = 0, mma2_commits = 0;
+  auto issue = [&](int c) {
+    const int slot = (c_end - 1 - c) & 1;
+    unsigned char* p = sm + slot * kBSlotBytes;
+    const size_t ch = (size_t)c * H + h;
+    const int y = (int)(ch * kChunk);
+    const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
+    tc::mbar_expect_tx(&full[slot], kBTxBytes);
+    tc::tma_load_2d(p + kBOffAZ, &mAqk, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kBOffKZ, &mKd, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kBOffKZ + 2 * kBox, &mKd, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kBOffQg, &mQg, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kBOffQg + kBox, &mQg, 64, y, &full[slot]);
+    tc::tma_load_2d(p + kBOffW, &mW, 0, y, &full[slot]);
+    tc::tma_load_2d(p + kBOffW + kBox, &mW, 64, y, &full[slot]);
+    tc::tma_load_3d(p + kBOffDO, &mDO, v0, h, (int)cp.row0, &full[slot]);
+    tc::bulk_load(p + kBOffGl, a.saved + a.L.gl + ch * K * sizeof(float), kGlBytes, &full[slot]);
+    next_issue = c - 1;
+  };
+  if (tid == 0) {
+    issue(c_end - 1);
+    if (c_end - 2 >= c_begin) issue(c_end - 2);
+  }
+
+  auto emit_state = [&](const float (&s)[32]) {
+    unsigned char* srow = sH + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 x;
+      x.x = pack2<T>(s[8 * q + 0], s[8 * q + 1]);
+      x.y = pack2<T>(s[8 * q + 2], s[8 * q + 3]);
+      x.z = pack2<T>(s[8 * q + 4], s[8 * q + 5]);
+      x.w = pack2<T>(s[8 * q + 6], s[8 * q + 7]);
+      st_shared_v4(srow + (((4 * half + q) ^ (row & 7)) << 4), x);
+    }
+  };
+  auto scale_store = [&](const float (&s)[32], int slot) {
+    const float gl = reinterpret_cast<const float*>(sm + slot * kBSlotBytes + kBOffGl)[row];
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = s[i] * gl;
+    tc::tmem_st32(tlane + kHColH + 32 * half, x);
+  };
+  auto copy_ckpt = [&](int c) {  // sH -> dh of chunk c, columns [v0, v0 + 64)
+    T* gh = reinterpret_cast<T*>(a.ws + a.BL.dh) + ((size_t)c * H + h) * (size_t)K * V + v0;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int k = idx >> 3, ci = idx & 7;
+      const uint4 x = ld_shared_v4(sH + (k >> 3) * 1024 + (k & 7) * 128 + ((ci ^ (k & 7)) << 4));
+      *reinterpret_cast<uint4*>(gh + (size_t)k * V + 8 * ci) = x;
+    }
+  };
+  auto copy_dvt = [&](int c) {  // sVT -> dVN^T rows [v0, v0 + 64) of chunk c
+    T* gv = reinterpret_cast<T*>(a.ws + a.BL.dvn) + ((size_t)c * H + h) * (size_t)kChunk * V +
+            (size_t)v0 * kChunk;
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int idx = tid + it * kTcThreads;
+      const int v = idx >> 3, ci = idx & 7;
+      *reinterpret_cast<uint4*>(gv + (size_t)v * kChunk + 8 * ci) =
+          ld_shared_v4(sVT + v * 128 + ci * 16);
+    }
+  };
+
+  // ---- initial gradient -----------------------------------------------------
+  {
+    const bool ok = tc::warp_wait(&full[0], 0);
+    if (ok) {
+      float s[32];
+      if (dht) {
+        const float4* src = reinterpret_cast<const float4*>(dht + (size_t)row * V + v0 + 32 * half);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 x = src[i];
+          s[4 * i] = x.x;
+          s[4 * i + 1] = x.y;
+          s[4 * i + 2] = x.z;
+          s[4 * i + 3] = x.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = 0.f;
+      }
+      emit_state(s);
+      scale_store(s, 0);
+    } else if (lane == 0) {
+      *sAbort = 1;
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+  }
+
+  int c = c_end - 1;
+  if (!*sAbort) {
+    for (; c >= c_begin; --c) {
+      const int i = c_end - 1 - c, slot = i & 1;
+      unsigned char* p = sm + slot * kBSlotBytes;
+      const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
+      const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
+
+      // 0. a partial chunk's dO rows past the sequence end belong to the
+      //    next sequence: zero them before any product reads the tile
+      if (cp.len < kChunk) {
+        const bool ok = tc::warp_wait(&full[slot], par_full);
+        if (ok) {
+          for (int e = tid; e < (kChunk - cp.len) * 8; e += kTcThreads) {
+            const int r = cp.len + (e >> 3), ci = e & 7;
+            st_shared_v4(p + kBOffDO + r * 128 + ci * 16, make_uint4(0u, 0u, 0u, 0u));
+          }
+        } else if (lane == 0) {
+          *sAbort = 1;
+        }
+        tc::fence_async_smem();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+
+      // 1. dVN_half = Aqk^T dO_half + Kd dh_half;  meanwhile dh is checkpointed
+      if (tid == 0) {
+        if (!tc::mbar_wait(&full[slot], par_full)) {
+          *sAbort = 1;
+        } else {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tc::umma_bf16(tmem + kHColD, desc_mn(p + kBOffAZ + j * 2048, kBox),
+                          desc_mn(p + kBOffDO + j * 2048, kBox), kIdMNh, j > 0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::umma_bf16(tmem + kHColD, desc_k(p + kBOffKZ + (j >> 2) * 2 * kBox + (j & 3) * 32),
+                          desc_mn(sH + j * 2048, kBox), kIdKNh, 1);
+          tc::umma_commit(mma1);
+          ++mma1_commits;
+        }
+      }
+      copy_ckpt(c);
+      // 2. -dVN [t][v] -> bf16 operand tile; dVN^T -> staging (lanes 0-63)
+      {
+        const bool ok = tc::warp_wait(mma1, par_mma);
+        if (ok && quad < 2) {
+          tc::tc_fence_after();
+          uint32_t x[32];
+          tc::tmem_ld32(tlane + kHColD + 32 * half, x);
+          tc::tmem_wait_ld();
+          const int t = row;
+          unsigned char* vrow = sVN + (t >> 3) * 1024 + (t & 7) * 128;
+          T* vt = reinterpret_cast<T*>(sVT) + t;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 y;
+            y.x = pack2<T>(-__uint_as_float(x[8 * q + 0]), -__uint_as_float(x[8 * q + 1]));
+            y.y = pack2<T>(-__uint_as_float(x[8 * q + 2]), -__uint_as_float(x[8 * q + 3]));
+            y.z = pack2<T>(-__uint_as_float(x[8 * q + 4]), -__uint_as_float(x[8 * q + 5]));
+            y.w = pack2<T>(-__uint_as_float(x[8 * q + 6]), -__uint_as_float(x[8 * q + 7]));
+            st_shared_v4(vrow + (((4 * half + q) ^ (t & 7)) << 4), y);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              vt[(32 * half + 8 * q + e) * kChunk] = from_f<T>(__uint_as_float(x[8 * q + e]));
+          }
+        }
+        if (!ok && lane == 0) *sAbort = 1;
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+      // 3. dh_half += Qg^T dO_half + W^T (-dVN_half);  meanwhile dVN^T leaves
+      if (tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_bf16(tmem + kHColH, desc_mn(p + kBOffQg + j * 2048, kBox),
+                        desc_mn(p + kBOffDO + j * 2048, kBox), kIdMNh, 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_bf16(tmem + kHColH, desc_mn(p + kBOffW + j * 2048, kBox),
+                        desc_mn(sVN + j * 2048, kBox), kIdMNh, 1);
+        tc::umma_commit(mma2);
+        ++mma2_commits;
+      }
+      copy_dvt(c);
+      // 4. new dh_half -> bf16 operand tile (the next checkpoint), scaled in
+      //    place by the next chunk's 2^G_last; or dh0
+      {
+        const bool has_next = c - 1 >= c_begin;
+        bool ok = tc::warp_wait(mma2, par_mma);
+        if (ok && has_next) ok = tc::warp_wait(&full[slot ^ 1], ((i + 1) >> 1) & 1);
+        if (ok) {
+          tc::tc_fence_after();
+          float s[32];
+          {
+            uint32_t hx[32];
+            tc::tmem_ld32(tlane + kHColH + 32 * half, hx);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(hx[e]);
+          }
+          if (has_next) {
+            emit_state(s);
+            scale_store(s, slot ^ 1);
+          } else if (dh0) {
+            float4* dst = reinterpret_cast<float4*>(dh0 + (size_t)row * V + v0 + 32 * half);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              dst[e] = make_float4(s[4 * e], s[4 * e + 1], s[4 * e + 2], s[4 * e + 3]);
+          }
+        } else if (lane == 0) {
+          *sAbort = 1;
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        __syncthreads();
+        if (*sAbort) break;
+      }
+      if (tid == 0 && c - 2 >= c_begin) issue(c - 2);
+    }
+  }
+
+  // ---- teardown ---------------------------------------------------------------
+  const bool aborted = *sAbort != 0;
+  if (aborted && tid == 0) {
+    for (int j = c; j > next_issue; --j) {
+      const int ij = c_end - 1 - j;
+      tc::mbar_wait(&full[ij & 1], (ij >> 1) & 1);
+    }
+    if (mma1_commits > 0) tc::mbar_wait(mma1, (mma1_commits - 1) & 1);
+    if (mma2_commits > 0) tc::mbar_wait(mma2, (mma2_commits - 1) & 1);
+    atomicOr(&g_gdn2_fault, 1u);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kHTmemCols);
+  }
+}
+
 // ---- host side -----------------------------------------------------------------
 bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_x,
               bool swizzle) {
@@ -1128,11 +1461,21 @@ cudaError_t launch_bwd_state_tc(const BwdStateArgs& a, cudaStream_t st) {
       !make_map(&mAqk, a.saved + a.L.aqk, 64, rows, 64, true) ||
       !make_map_rows(&mDO, a.dout, 128, (uint64_t)a.H, (uint64_t)a.total_rows))
     return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(k_bwd_state_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmemBytes);
-  if (e != cudaSuccess) return e;
   const int grid = a.seqs.n_seqs * a.H;
   if (grid == 0) return cudaSuccess;
+  int sms = 0;
+  cudaError_t e = num_sms(&sms);
+  if (e != cudaSuccess) return e;
+  if (2 * grid <= sms) {  // few sequence-heads: one CTA per half of the value columns
+    e = cudaFuncSetAttribute(k_bwd_state_tc_half, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kBSmemBytes);
+    if (e != cudaSuccess) return e;
+    k_bwd_state_tc_half<<<2 * grid, kTcThreads, kBSmemBytes, st>>>(a, mW, mQg, mKd, mAqk, mDO);
+    return cudaGetLastError();
+  }
+  e = cudaFuncSetAttribute(k_bwd_state_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
   k_bwd_state_tc<<<grid, kTcThreads, kSmemBytes, st>>>(a, mW, mQg, mKd, mAqk, mDO);
   return cudaGetLastError();
 }
