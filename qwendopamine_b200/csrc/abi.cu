@@ -269,51 +269,95 @@ cudaError_t bwd_intra_dispatch(const gdn2_chunk_problem* p, const BwdIntraArgs& 
 }
 
 // ---- context-parallel merge ----------------------------------------------
-// One CTA per (sequence, head, 32-column tile of the state); the running
-// state tile x (K x 32) lives in shared memory and each folded rank applies
-// x <- M x + h_e (forward) or x <- M^T x + dh_e (backward), reading M from
-// the gathered buffer.
-__global__ void k_cp_merge(int N, int H, int K, int V, const float* hm_all, const float* dhm_all,
-                           int rank, int world, int forward, const float* init, float* out) {
-  extern __shared__ float sx[];   // [2][K][32]
-  float* x = sx;
-  float* y = sx + K * 32;
+// One CTA per (sequence, head, 32-column tile of the state).  The running
+// tile x (K x 32, fp32) and its successor stay in shared memory; for each
+// folded rank j the CTA applies x <- M_j x + h_e_j (forward) or
+// x <- M_j^T x + dh_j (backward), staging M_j in blocks of 64 output rows
+// (64 x K rows of M, or K x 64 columns of it for the transpose, read
+// coalesced) and multiplying on the tensor cores with the 3-term TF32 split
+// (about fp32 accuracy).
+constexpr int kMergeRows = 64;
+constexpr int kMergeLDX = 32 + 4;
+constexpr int kMergeLDB = kMergeRows + 4;  // row stride of a staged K x 64 column block
+
+__host__ __device__ inline int merge_depth(int K) { return (K + 7) & ~7; }
+// floats of the staged block: 64 rows of M (stride depth + 4) or depth rows
+// of 64 columns (stride kMergeLDB)
+__host__ __device__ inline int merge_block_floats(int K) {
+  const int kd = merge_depth(K);
+  const int f = kMergeRows * (kd + 4), b = kd * kMergeLDB;
+  return f > b ? f : b;
+}
+size_t merge_smem_bytes(int K) {
+  return (size_t)(2 * merge_depth(K) * kMergeLDX + merge_block_floats(K)) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(kThreads) k_cp_merge(int N, int H, int K, int V,
+                                                      const float* hm_all, const float* dhm_all,
+                                                      int rank, int world, int forward,
+                                                      const float* init, float* out) {
+  extern __shared__ __align__(16) float smem[];
+  const int kd = merge_depth(K);  // product depth; rows K .. kd-1 of x stay zero
+  const int ldm = forward ? kd + 4 : kMergeLDB;
+  float* x = smem;
+  float* y = x + kd * kMergeLDX;
+  float* sM = y + kd * kMergeLDX;
   const int nh = blockIdx.y, v0 = blockIdx.x * 32;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int VK = V + K;
   const int64_t per_rank_hm = (int64_t)N * H * K * VK;
   const int64_t per_rank_dh = (int64_t)N * H * K * V;
-  for (int idx = tid; idx < K * 32; idx += blockDim.x) {
-    int r = idx >> 5, c = idx & 31, col = v0 + c;
-    x[idx] = (init && col < V) ? init[((int64_t)nh * K + r) * V + col] : 0.f;
+  for (int idx = tid; idx < kd * 32; idx += kThreads) {
+    const int r = idx >> 5, c = idx & 31, col = v0 + c;
+    x[r * kMergeLDX + c] =
+        (init && r < K && col < V) ? init[((int64_t)nh * K + r) * V + col] : 0.f;
+    y[r * kMergeLDX + c] = 0.f;
   }
   __syncthreads();
-  const int j_begin = forward ? 0 : world - 1;
-  const int j_end = forward ? rank : rank;  // exclusive bound in the walking direction
-  for (int j = j_begin; forward ? (j < j_end) : (j > j_end); j += forward ? 1 : -1) {
+  const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 16;
+  for (int step = 0; step < (forward ? rank : world - 1 - rank); ++step) {
+    const int j = forward ? step : world - 1 - step;
     const float* hm = hm_all + j * per_rank_hm + (int64_t)nh * K * VK;
-    for (int idx = tid; idx < K * 32; idx += blockDim.x) {
-      int r = idx >> 5, c = idx & 31, col = v0 + c;
-      float s = 0.f;
-      if (col < V) {
-        if (forward) {
-          for (int m = 0; m < K; ++m) s += hm[(int64_t)r * VK + V + m] * x[m * 32 + c];
-          s += hm[(int64_t)r * VK + col];
-        } else {
-          for (int m = 0; m < K; ++m) s += hm[(int64_t)m * VK + V + r] * x[m * 32 + c];
-          s += dhm_all[j * per_rank_dh + ((int64_t)nh * K + r) * V + col];
+    for (int r0 = 0; r0 < K; r0 += kMergeRows) {
+      const int nr = min(kMergeRows, K - r0);
+      // stage the block of M (rows r0.. of M, or its columns r0.. for M^T)
+      if (forward) {
+        for (int idx = tid; idx < kMergeRows * kd; idx += kThreads) {
+          const int r = idx / kd, m = idx - r * kd;
+          sM[r * ldm + m] = (r < nr && m < K) ? hm[(int64_t)(r0 + r) * VK + V + m] : 0.f;
+        }
+      } else {
+        for (int idx = tid; idx < kd * kMergeRows; idx += kThreads) {
+          const int m = idx / kMergeRows, r = idx - m * kMergeRows;
+          sM[m * ldm + r] = (r < nr && m < K) ? hm[(int64_t)m * VK + V + r0 + r] : 0.f;
         }
       }
-      y[idx] = s;
+      __syncthreads();
+      float acc[1][2][4];
+      acc_zero(acc);
+      if (forward)
+        warp_mma<1, 2, 3>(acc, sM + m0 * ldm, ldm, 1, x + n0, kMergeLDX, 1, kd);
+      else
+        warp_mma<1, 2, 3>(acc, sM + m0, 1, ldm, x + n0, kMergeLDX, 1, kd);
+      acc_foreach(acc, [&](int rr, int cc, float val) {
+        const int r = r0 + m0 + rr, c = n0 + cc, col = v0 + c;
+        if (r < K) {
+          float b = 0.f;
+          if (col < V)
+            b = forward ? hm[(int64_t)r * VK + col]
+                        : dhm_all[j * per_rank_dh + ((int64_t)nh * K + r) * V + col];
+          y[r * kMergeLDX + c] = val + b;
+        }
+      });
+      __syncthreads();
     }
-    __syncthreads();
     float* t = x;
     x = y;
     y = t;
   }
-  for (int idx = tid; idx < K * 32; idx += blockDim.x) {
-    int r = idx >> 5, c = idx & 31, col = v0 + c;
-    if (col < V) out[((int64_t)nh * K + r) * V + col] = x[idx];
+  for (int idx = tid; idx < K * 32; idx += kThreads) {
+    const int r = idx >> 5, c = idx & 31, col = v0 + c;
+    if (col < V) out[((int64_t)nh * K + r) * V + col] = x[r * kMergeLDX + c];
   }
 }
 
@@ -621,10 +665,13 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all, const float*
   const int N = p->seqs.n_seqs;
   if (N == 0) return GDN2_OK;
   dim3 grid((p->V + 31) / 32, N * p->H);
-  size_t smem = 2 * (size_t)p->K * 32 * sizeof(float);
-  k_cp_merge<<<grid, 256, smem, (cudaStream_t)stream>>>(N, p->H, p->K, p->V, hm_all, dhm_all, rank,
-                                                        world, forward, init, state_out);
-  cudaError_t e = cudaGetLastError();
+  const size_t smem = merge_smem_bytes(p->K);
+  cudaError_t e = cudaFuncSetAttribute(k_cp_merge, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn2_cp_merge");
+  k_cp_merge<<<grid, kThreads, smem, (cudaStream_t)stream>>>(N, p->H, p->K, p->V, hm_all, dhm_all,
+                                                             rank, world, forward, init, state_out);
+  e = cudaGetLastError();
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_merge");
 }
 
