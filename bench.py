@@ -448,11 +448,13 @@ def run_config4(args, world, rank, local, clocks_out):
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with N.phase_timing() as rec:
+        torch.cuda.nvtx.range_push("config4_timed")  # lets a profiler select the timed steps
         e0.record(stream)
         for _ in range(args.steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     barrier(world)
     if sampler:
         clocks_out.append(sampler.stop())
@@ -648,20 +650,23 @@ def run_config1(args, world, rank, local):
 
 
 def run_profile_case(args, local):
-    """Small case for ncu captures: the config-1 step at batch ``args.batch``
-    (inputs still larger than L2), ``args.warmup`` + ``args.steps`` steps of
-    the four phases, nothing else."""
+    """Small case for ncu captures: the step's four phases through the C ABI
+    at ``--batch`` x ``--seq`` tokens x ``--heads`` heads (config-1 shapes by
+    default; ``--batch 1 --seq 32768 --heads 32`` is a config-4-shaped slice),
+    inputs still larger than L2, ``--warmup`` + ``--steps`` steps, nothing
+    else."""
     from qwendopamine_b200 import _native as N
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     lib = N.load()
+    Bp, Tp, Hp = args.batch, args.seq, args.heads
     gen = torch.Generator(device=dev).manual_seed(99)
-    d = _draw(gen, dev, (args.batch, T1), H1)
+    d = _draw(gen, dev, (Bp, Tp), Hp)
     b, w, g = broadcast_gates(d["beta"], d["gs"])
     x = dict(q=d["q"], k=d["k"], v=d["v"], g=g, b=b, w=w, do=d["do"])
-    tables = N.seq_tables(args.batch, T1, dev)
-    prob = N.ChunkProblem(H1, K, V, N.dtype_code(torch.bfloat16), 1, K ** -0.5, tables.struct())
+    tables = N.seq_tables(Bp, Tp, dev)
+    prob = N.ChunkProblem(Hp, K, V, N.dtype_code(torch.bfloat16), 1, K ** -0.5, tables.struct())
     sbytes = lib.gdn2_chunk_saved_bytes(prob)
     wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
     saved = torch.empty(sbytes, dtype=torch.uint8, device=dev)
@@ -678,7 +683,7 @@ def run_profile_case(args, local):
                                    N.ptr(saved), sbytes, P["do"], None, G["q"], G["k"], G["v"],
                                    G["g"], G["b"], G["w"], None, N.ptr(ws), wbytes, st), "bwd")
     torch.cuda.synchronize()
-    print(json.dumps({"profile_case": {"batch": args.batch, "T": T1, "H": H1, "K": K, "V": V,
+    print(json.dumps({"profile_case": {"batch": Bp, "T": Tp, "H": Hp, "K": K, "V": V,
                                        "launches_per_step": 4,
                                        "steps": args.warmup + args.steps}}))
 
@@ -945,7 +950,7 @@ def run_config3(world, rank, local):
            "tokens_per_s": round(world * tokens_gpu / (ms / 1e3), 1),
            "model_tflops_per_gpu": round(flops / (ms / 1e3) / 1e12, 1),
            "frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / peak, 4),
-           "loss": round(float(loss), 4)}
+           "loss": round(float(loss.detach()), 4)}
     del ddp, model, opt
     torch.cuda.empty_cache()
     return out
@@ -1205,6 +1210,8 @@ def main(argv=None):
     ap.add_argument("--profile", action="store_true",
                     help="small ncu case: config-1 phases at --batch, nothing else")
     ap.add_argument("--batch", type=int, default=2, help="batch of the --profile case")
+    ap.add_argument("--seq", type=int, default=T1, help="sequence length of the --profile case")
+    ap.add_argument("--heads", type=int, default=H1, help="heads of the --profile case")
     args = ap.parse_args(argv)
     if args.profile:
         run_profile_case(args, int(os.environ.get("LOCAL_RANK", "0")))
