@@ -27,7 +27,7 @@ namespace gdn2 {
 
 constexpr int kThreadsB16 = 512;
 
-template <int D>
+template <int D, bool TC = false>
 struct Bwd16Layout {
   static constexpr int LDK = D + 8;      // 16-bit 64 x D tiles
   static constexpr int LDG = D + 8;      // fp32 64 x D tiles (8-byte pairs conflict-free)
@@ -44,7 +44,10 @@ struct Bwd16Layout {
   // misc floats: rq[64] rk[64] dgl[D] diag[64] pdq[4][64] pdk[4][64] flag[4] F[10][D]
   //              dApart[16], then 3 mbarriers (as 6 floats, 8-byte aligned)
   static constexpr int nMisc = 64 + 64 + D + 64 + 256 + 256 + 4 + 10 * D + 16;
-  static constexpr int oW = (oMisc + nMisc * 4 + 3 * 8 + 127) / 128 * 128;  // TMA targets: 128-B
+  // TMA targets: 128-byte aligned; 1024 with the tcgen05 value phase, whose
+  // 128-byte-swizzled tiles need it (and 4 mbarriers + the TMEM address)
+  static constexpr int oW = TC ? (oMisc + nMisc * 4 + 6 * 8 + 1023) / 1024 * 1024
+                               : (oMisc + nMisc * 4 + 3 * 8 + 127) / 128 * 128;
   // phase V (offsets inside W)
   static constexpr int vH = 0;
   static constexpr int vDH = vH + D * LDS * 2;
@@ -72,9 +75,21 @@ struct Bwd16Layout {
   static constexpr int kX = kdG + kChunk * LDG * 4;
   static constexpr int kTmp = kX + kChunk * LDG * 4;
   static constexpr int kScanEnd = kTmp + 2 * kThreadsB16 * 4;
-  static constexpr int W = phaseV > kEnd ? (phaseV > kScanEnd ? phaseV : kScanEnd)
-                                         : (kEnd > kScanEnd ? kEnd : kScanEnd);
-  static constexpr size_t bytes = (size_t)oW + W + 128;  // + base alignment slack
+  // tcgen05 value phase (K = V = 128): two 64-column slices of 128-byte-
+  // swizzled tiles; h / dh [128][64] single-buffered, dO, VN^T, dVN^T, v, w
+  // [64][64] in two slots, Z = v w; after it, a fp32 [64][LDG] transpose
+  // buffer at kE and the scan scratch beyond it
+  static constexpr int tH = 0, tDH = 16384, tSlot0 = 32768, tSlotBytes = 40960;
+  static constexpr int tDO = 0, tVN = 8192, tDVN = 16384, tV = 24576, tWg = 32768;
+  static constexpr int tZ = tSlot0 + 2 * tSlotBytes;
+  static constexpr int tEnd = tZ + 8192;
+  static constexpr int tTr = kE;
+  static constexpr int tScan = (tTr + kChunk * LDG * 4 + 1023) / 1024 * 1024;
+  static constexpr int W0 = phaseV > kEnd ? (phaseV > kScanEnd ? phaseV : kScanEnd)
+                                          : (kEnd > kScanEnd ? kEnd : kScanEnd);
+  static constexpr int Wtc = tEnd > tScan + 4 * kThreadsB16 ? tEnd : tScan + 4 * kThreadsB16;
+  static constexpr int W = TC ? (W0 > Wtc ? W0 : Wtc) : W0;
+  static constexpr size_t bytes = (size_t)oW + W + (TC ? 1024 : 128);  // + base alignment slack
   static_assert(kT2 + kChunk * LDC * 2 <= kEnd || kT2 + kChunk * LDC * 2 <= W, "layout");
   static_assert(oW % 128 == 0 && slot % 128 == 0 && oK % 128 == 0 && oB % 128 == 0 &&
                     oG % 128 == 0 && oA % 128 == 0 && vDH % 128 == 0 && vDO % 128 == 0 &&
@@ -83,6 +98,9 @@ struct Bwd16Layout {
   static_assert((oMisc + nMisc * 4) % 8 == 0, "mbarrier alignment");
   static_assert(32 * LDT <= kChunk * LDS, "VN^T slice fits its region");
   static_assert(3 * kChunk * LDK * 2 <= W, "gradient staging fits the work region");
+  static_assert(!TC || D == 128, "the tcgen05 value phase serves K = V = 128");
+  static_assert(!TC || (tTr >= kDW + kChunk * LDK * 2), "transpose buffer clear of dW");
+  static_assert(!TC || bytes <= 232448, "shared memory per CTA");
 };
 
 // TMA views of every tile the kernel reads (built per launch on the host).
@@ -93,16 +111,17 @@ struct Bwd16Maps {
   CUtensorMap vn, dvn;          // per (chunk, head): VN / dVN stored [V][64]
 };
 
-template <typename T, int D>
+template <typename T, int D, bool TC>
 __global__ void __launch_bounds__(kThreadsB16, 1)
     k_bwd_intra16(BwdIntraArgs a, const __grid_constant__ Bwd16Maps mp) {
-  using L = Bwd16Layout<D>;
+  using L = Bwd16Layout<D, TC>;
   constexpr int LDK = L::LDK, LDG = L::LDG, LDC = L::LDC, LDS = L::LDS, LDT = L::LDT;
   constexpr int NTH = kThreadsB16;
   constexpr int DQ = D / 4;    // owner tile width
   constexpr int NTO = DQ / 8;  // n8 fragments per owner tile
   extern __shared__ unsigned char smraw[];
-  unsigned char* sm = smraw + ((128u - (smem_u32(smraw) & 127u)) & 127u);
+  constexpr uint32_t kAlign = TC ? 1024u : 128u;
+  unsigned char* sm = smraw + ((kAlign - (smem_u32(smraw) & (kAlign - 1))) & (kAlign - 1));
   T* sq = reinterpret_cast<T*>(sm + L::oQ);
   T* sk = reinterpret_cast<T*>(sm + L::oK);
   T* sb = reinterpret_cast<T*>(sm + L::oB);
@@ -191,6 +210,243 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
     }
   };
 
+  // ---- phase V --------------------------------------------------------------
+  float accQ[1][NTO][4], accKd[1][NTO][4], accW[1][NTO][4], accAqk[1][2][4], accDA[1][2][4];
+  acc_zero(accQ);
+  acc_zero(accKd);
+  acc_zero(accW);
+  acc_zero(accAqk);
+  acc_zero(accDA);
+  T* sZ = reinterpret_cast<T*>(W + L::vZ);
+  T* gdv = reinterpret_cast<T*>(a.dv) + offv;
+  T* gdw = reinterpret_cast<T*>(a.dw) + offv;
+  // ---- tcgen05 value phase (K = V = 128) -------------------------------------
+  // Two 64-column value slices in 128-byte-swizzled tiles.  One thread issues
+  //   dQg^T += h dO^T,  dKd^T += dh VN^T,  dW'^T += h dVN^T   (TMEM cols 0,
+  //   64, 128; M = 128 key rows, N = 64 tokens, K = the slice's 64 columns)
+  // while the warps form Z = v w and d(gl), the 16 x 16 products dAqk += dO
+  // VN^T and dA += dVN Z^T, and dZ = A^T dVN -> dv, dw on mma.sync.  The h /
+  // dh tiles of slice 1 replace slice 0's once its products have read them.
+  // Afterwards dW goes from TMEM straight to its bf16 tile and dQg, dKd reach
+  // the owner-tile registers through one fp32 shared-memory transpose each.
+  uint32_t tmem = 0;
+  if constexpr (TC) {
+    uint64_t* barMma = bars + 3;
+    uint32_t* sTmemAddr = reinterpret_cast<uint32_t*>(bars + 4);
+    if (tid == 0) {
+      for (int i = 0; i < 4; ++i) tc::mbar_init(&bars[i], 1);
+      tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+      tc::tmem_alloc(sTmemAddr, 256);
+      tc::tmem_relinquish();
+    }
+    for (int i = tid; i < D; i += NTH) dgl[i] = 0.f;
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    tmem = *sTmemAddr;
+    constexpr uint32_t kTxSlice = 2 * 16384 + 5 * 8192;  // h, dh, dO, VN^T, dVN^T, v, w
+    auto tp = [&](int off) { return reinterpret_cast<T*>(W + off); };
+    auto slot_off = [&](int sl, int off) { return L::tSlot0 + sl * L::tSlotBytes + off; };
+    int mma_commits = 0;  // thread 0
+    auto drain_tc = [&]() {
+      if (tid == 0) {
+        for (int i = 0; i < 3; ++i) tc::mbar_wait(&bars[i], 0);
+        if (mma_commits > 0) tc::mbar_wait(barMma, (mma_commits - 1) & 1);
+        atomicOr(a.fault, 8u);
+      }
+      tc::tc_fence_before();
+      __syncthreads();
+      if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 256);
+      }
+    };
+    if (tid == 0) {
+      tc::mbar_expect_tx(&bars[0], kTxSlice + txA);
+      tc::tma_load_2d(sA, &mp.a, 0, (int)ch * kChunk, &bars[0]);
+      tc::tma_load_2d(tp(L::tH), &mp.h, 0, (int)ch * K, &bars[0]);
+      tc::tma_load_2d(tp(L::tDH), &mp.dh, 0, (int)ch * K, &bars[0]);
+      for (int sl = 0; sl < 2; ++sl) {
+        if (sl == 1) tc::mbar_expect_tx(&bars[1], kTxSlice);  // h / dh follow later
+        tc::tma_load_3d(tp(slot_off(sl, L::tDO)), &mp.dout, 64 * sl, h, crow, &bars[sl]);
+        tc::tma_load_2d(tp(slot_off(sl, L::tVN)), &mp.vn, 0, (int)ch * V + 64 * sl, &bars[sl]);
+        tc::tma_load_2d(tp(slot_off(sl, L::tDVN)), &mp.dvn, 0, (int)ch * V + 64 * sl, &bars[sl]);
+        tc::tma_load_3d(tp(slot_off(sl, L::tV)), &mp.v, 64 * sl, h, crow, &bars[sl]);
+        tc::tma_load_3d(tp(slot_off(sl, L::tWg)), &mp.w, 64 * sl, h, crow, &bars[sl]);
+      }
+      tc::mbar_expect_tx(&bars[2], txKey);
+      for (int part = 0; part < 3; ++part) issue_key_part(part);
+    }
+    T* th = tp(L::tH);
+    T* tdh = tp(L::tDH);
+    T* tz = tp(L::tZ);
+    constexpr uint32_t kIdKK = tc::idesc_bf16(128, 64, 0, 0);  // K-major A, K-major B
+    constexpr uint32_t kIdKM = tc::idesc_bf16(128, 64, 0, 1);  // K-major A, MN-major B
+    for (int sl = 0; sl < 2; ++sl) {
+      T* tdo = tp(slot_off(sl, L::tDO));
+      T* tvn = tp(slot_off(sl, L::tVN));
+      T* tdvn = tp(slot_off(sl, L::tDVN));
+      T* tv = tp(slot_off(sl, L::tV));
+      T* tw = tp(slot_off(sl, L::tWg));
+      if (__syncthreads_or(!tc::mbar_wait(&bars[sl], 0))) {
+        drain_tc();
+        return;
+      }
+      if (len < kChunk) {  // rows past a partial chunk hold the next sequence's tokens
+        zero_rows(tdo, 128, len, kChunk);
+        zero_rows(tv, 128, len, kChunk);
+        zero_rows(tw, 128, len, kChunk);
+        tc::fence_async_smem();
+        __syncthreads();
+      }
+      if (tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t acc = (sl > 0 || j > 0) ? 1u : 0u;
+          tc::umma_bf16(tmem + 0, tc::sdesc(th + 16 * j, 16, 1024, tc::kSwizzle128),
+                        tc::sdesc(tdo + 16 * j, 16, 1024, tc::kSwizzle128), kIdKK, acc);
+          tc::umma_bf16(tmem + 64, tc::sdesc(tdh + 16 * j, 16, 1024, tc::kSwizzle128),
+                        tc::sdesc(tvn + 1024 * j, 8192, 1024, tc::kSwizzle128), kIdKM, acc);
+          tc::umma_bf16(tmem + 128, tc::sdesc(th + 16 * j, 16, 1024, tc::kSwizzle128),
+                        tc::sdesc(tdvn + 1024 * j, 8192, 1024, tc::kSwizzle128), kIdKM, acc);
+        }
+        tc::umma_commit(barMma);
+        ++mma_commits;
+      }
+      // Z = v w (same swizzle as v, w): one 16-byte chunk per thread
+      {
+        const int r = tid >> 3, c = tid & 7;
+        const int off = r * 128 + ((c ^ (r & 7)) << 4);
+        const uint4 v8 = *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(tv) + off);
+        const uint4 w8 = *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(tw) + off);
+        uint4 z8;
+        float2 p;
+        p = mul2(unpack2<T>(v8.x), unpack2<T>(w8.x)); z8.x = pack2<T>(p.x, p.y);
+        p = mul2(unpack2<T>(v8.y), unpack2<T>(w8.y)); z8.y = pack2<T>(p.x, p.y);
+        p = mul2(unpack2<T>(v8.z), unpack2<T>(w8.z)); z8.z = pack2<T>(p.x, p.y);
+        p = mul2(unpack2<T>(v8.w), unpack2<T>(w8.w)); z8.w = pack2<T>(p.x, p.y);
+        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(tz) + off) = z8;
+      }
+      // dgl[k] += sum over the slice's 64 columns of h * dh: 4 threads per
+      // key row, two 16-byte chunks each, combined with two shuffles
+      {
+        const int row = tid >> 2, part = tid & 3;
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int c = 2 * part + q;
+          const int off = row * 128 + ((c ^ (row & 7)) << 4);
+          const uint4 h8 = *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(th) + off);
+          const uint4 d8 = *reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned char*>(tdh) + off);
+          float2 acc2 = mul2(unpack2<T>(h8.x), unpack2<T>(d8.x));
+          acc2 = fma2(unpack2<T>(h8.y), unpack2<T>(d8.y), acc2);
+          acc2 = fma2(unpack2<T>(h8.z), unpack2<T>(d8.z), acc2);
+          acc2 = fma2(unpack2<T>(h8.w), unpack2<T>(d8.w), acc2);
+          acc += acc2.x + acc2.y;
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (part == 0) dgl[row] += acc;
+      }
+      __syncthreads();  // Z is complete; every read of h / dh by the threads is done
+      if (sl == 0 && tid == 0) {
+        // h / dh of slice 1 once slice 0's products have read them
+        if (tc::mbar_wait(barMma, 0)) {
+          tc::tma_load_2d(th, &mp.h, 64, (int)ch * K, &bars[1]);
+          tc::tma_load_2d(tdh, &mp.dh, 64, (int)ch * K, &bars[1]);
+        }
+      }
+      // dAqk += dO VN^T, dA += dVN Z^T (16 x 16 tiles)
+#pragma unroll
+      for (int k0 = 0; k0 < 64; k0 += 16) {
+        uint32_t aDo[4], aDvn[4], b[4];
+        load_a16_sw<true>(aDo, tdo, 16 * wr, k0);
+        load_a16_sw<false>(aDvn, tdvn, 16 * wr, k0);
+        load_b16x2_sw<false>(b, tvn, k0, 16 * wc);
+        Mma16<T>::run(accAqk[0][0], aDo, b[0], b[1]);
+        Mma16<T>::run(accAqk[0][1], aDo, b[2], b[3]);
+        load_b16x2_sw<true>(b, tz, k0, 16 * wc);
+        Mma16<T>::run(accDA[0][0], aDvn, b[0], b[1]);
+        Mma16<T>::run(accDA[0][1], aDvn, b[2], b[3]);
+      }
+      {
+        // dZ = A^T dVN (64 tokens x the slice's 64 columns): 16 x 16 per warp
+        float accZ[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const int zm = 16 * (warp & 3), zn = 16 * (warp >> 2);
+        const int rr8 = lane & 7, kh = (lane >> 3) & 1;
+#pragma unroll
+        for (int k0 = 0; k0 < kChunk; k0 += 16) {
+          uint32_t af[4];
+          load_a16<false>(af, sA, LDC, zm, k0);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t bf[2];
+            ldsm_x2(bf, sw128(tdvn, zn + 8 * h2 + rr8, k0 + 8 * kh));
+            Mma16<T>::run(accZ[h2], af, bf[0], bf[1]);
+          }
+        }
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int r = zm + gid + 8 * hf, cl = zn + 8 * h2 + 2 * tig;
+            if (r < len) {
+              const float2 z2 = pr(accZ[h2], hf);
+              const float2 dv2 = mul2(z2, ld2<T>(sw128_elem(tw, r, cl)));
+              const float2 dw2 = mul2(z2, ld2<T>(sw128_elem(tv, r, cl)));
+              *reinterpret_cast<uint32_t*>(gdv + r * ldv + 64 * sl + cl) = pack2<T>(dv2.x, dv2.y);
+              *reinterpret_cast<uint32_t*>(gdw + r * ldv + 64 * sl + cl) = pack2<T>(dw2.x, dw2.y);
+            }
+          }
+      }
+    }
+    // every product of both slices has landed in TMEM
+    if (__syncthreads_or(!tc::warp_wait(barMma, 1))) {
+      drain_tc();
+      return;
+    }
+    tc::tc_fence_after();
+    {
+      const int q4 = warp & 3, cg = warp >> 2;  // TMEM lanes 32 q4 .., token columns 16 cg ..
+      const uint32_t tl = tmem + ((uint32_t)(32 * q4) << 16);
+      const int kk = 32 * q4 + lane;            // key channel of this thread's lane
+      float* sTr = reinterpret_cast<float*>(W + L::tTr);
+      T* sDWt = reinterpret_cast<T*>(W + L::kDW);
+      uint32_t x[16];
+      tc::tmem_ld16(tl + 128 + 16 * cg, x);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) sDWt[(16 * cg + e) * LDK + kk] = from_f<T>(-__uint_as_float(x[e]));
+      tc::tmem_ld16(tl + 0 + 16 * cg, x);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) sTr[(16 * cg + e) * LDG + kk] = __uint_as_float(x[e]);
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < NTO; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
+          setpr(accQ[0][j], hf, ld2<float>(sTr + r * LDG + c0));
+        }
+      __syncthreads();
+      tc::tmem_ld16(tl + 64 + 16 * cg, x);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) sTr[(16 * cg + e) * LDG + kk] = __uint_as_float(x[e]);
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < NTO; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
+          setpr(accKd[0][j], hf, ld2<float>(sTr + r * LDG + c0));
+        }
+    }
+  } else {
   // ---- phase 0: A and the first slice --------------------------------------
   if (tid == 0) {
     for (int i = 0; i < 3; ++i) tc::mbar_init(&bars[i], 1);
@@ -214,16 +470,6 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
       for (int part = 0; part < 3; ++part) issue_key_part(part);
   }
 
-  // ---- phase V --------------------------------------------------------------
-  float accQ[1][NTO][4], accKd[1][NTO][4], accW[1][NTO][4], accAqk[1][2][4], accDA[1][2][4];
-  acc_zero(accQ);
-  acc_zero(accKd);
-  acc_zero(accW);
-  acc_zero(accAqk);
-  acc_zero(accDA);
-  T* sZ = reinterpret_cast<T*>(W + L::vZ);
-  T* gdv = reinterpret_cast<T*>(a.dv) + offv;
-  T* gdw = reinterpret_cast<T*>(a.dw) + offv;
   for (int s = 0; s < nslices; ++s) {
     const int cur = s & 1, v0 = 32 * s, nv = min(32, V - v0);
     if (s + 1 < nslices) {
@@ -330,9 +576,20 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
       }
     }
   }
+  }
   // phase V buffers are dead from here on; q, k, b, g have landed
   if (__syncthreads_or(!tc::mbar_wait(&bars[2], 0))) {
-    drain(nslices - 1);
+    if constexpr (TC) {
+      if (tid == 0) atomicOr(a.fault, 8u);
+      tc::tc_fence_before();
+      __syncthreads();
+      if (warp == 0) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 256);
+      }
+    } else {
+      drain(nslices - 1);
+    }
     return;
   }
   if (len < kChunk) {
@@ -350,7 +607,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
     __syncthreads();
   }
   // chunk-local log2 cumulative decay; row norms
-  col_scan64_reg<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(W + L::vZ), kLog2e);
+  col_scan64_reg<D, NTH, false>(sG, LDG, reinterpret_cast<float*>(W + (TC ? L::tScan : L::vZ)),
+                                kLog2e);
   row_norms16<T, D, NTH>(sq, sk, LDK, rq, rk, a.l2norm);
 
   // ---- dump dW and dAqk ------------------------------------------------------
@@ -360,14 +618,16 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
   T* sE = reinterpret_cast<T*>(W + L::kE);
   T* sT1 = reinterpret_cast<T*>(W + L::kT1);
   T* sT2 = reinterpret_cast<T*>(W + L::kT2);
+  if constexpr (!TC) {  // (the tcgen05 value phase wrote sDW from TMEM)
 #pragma unroll
-  for (int j = 0; j < NTO; ++j)
+    for (int j = 0; j < NTO; ++j)
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
-      *reinterpret_cast<uint32_t*>(sDW + r * LDK + cl) =
-          pack2<T>(-accW[0][j][2 * hf], -accW[0][j][2 * hf + 1]);
-    }
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = 16 * wr + gid + 8 * hf, cl = wc * DQ + 8 * j + 2 * tig;
+        *reinterpret_cast<uint32_t*>(sDW + r * LDK + cl) =
+            pack2<T>(-accW[0][j][2 * hf], -accW[0][j][2 * hf + 1]);
+      }
+  }
 #pragma unroll
   for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -778,12 +1038,54 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
   store_tile16<T, kChunk, D, NTH>(gdq, ldk, stq, LDK, len, K);
   store_tile16<T, kChunk, D, NTH>(gdk, ldk, stk, LDK, len, K);
   store_tile16<T, kChunk, D, NTH>(gdb, ldk, stb, LDK, len, K);
+  if constexpr (TC) {
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+      tc::tc_fence_after();
+      tc::tmem_dealloc(tmem, 256);
+    }
+  }
+}
+
+// K = V = 128 takes the tcgen05 value phase: h / dh as [128][64] and dO, v,
+// w, VN^T, dVN^T as [64][64] boxes of 128-byte-swizzled tiles; A, q, k, b, g
+// keep their padded unswizzled boxes.
+template <typename T>
+cudaError_t launch_bwd_intra16_tc(const BwdIntraArgs& a, cudaStream_t st) {
+  using L = Bwd16Layout<128, true>;
+  auto kern = k_bwd_intra16<T, 128, true>;
+  const uint64_t nch = (uint64_t)a.seqs.n_chunks, H = (uint64_t)a.H, rows = (uint64_t)a.total_rows;
+  constexpr uint64_t K = 128, V = 128;
+  Bwd16Maps m;
+  const uint64_t dK[3] = {K, H, rows}, sK[2] = {K * 2, H * K * 2}, sG[2] = {K * 4, H * K * 4};
+  const uint32_t bK[3] = {(uint32_t)L::LDK, 1, kChunk}, bG[3] = {(uint32_t)L::LDG, 1, kChunk};
+  const uint64_t dA[2] = {kChunk, nch * H * kChunk}, s64[1] = {kChunk * 2};
+  const uint32_t bA[2] = {(uint32_t)L::LDC, kChunk};
+  const unsigned char* sv = a.saved;
+  const unsigned char* wv = a.ws;
+  if (!tmap_plain(&m.q, a.q, 3, dK, sK, bK, 2) || !tmap_plain(&m.k, a.k, 3, dK, sK, bK, 2) ||
+      !tmap_plain(&m.b, a.b, 3, dK, sK, bK, 2) || !tmap_plain(&m.g, a.g, 3, dK, sG, bG, 4) ||
+      !tmap_plain(&m.a, sv + a.L.a, 2, dA, s64, bA, 2) ||
+      !tmap_rows(&m.dout, a.dout, V, H, rows, 64, 2) || !tmap_rows(&m.v, a.v, V, H, rows, 64, 2) ||
+      !tmap_rows(&m.w, a.w, V, H, rows, 64, 2) ||
+      !tmap_2d_box_bf16(&m.h, sv + a.L.h, V, nch * H * K, 64, 128) ||
+      !tmap_2d_box_bf16(&m.dh, wv + a.BL.dh, V, nch * H * K, 64, 128) ||
+      !tmap_2d_bf16(&m.vn, sv + a.L.vn, kChunk, nch * H * V, 64, true) ||
+      !tmap_2d_bf16(&m.dvn, wv + a.BL.dvn, kChunk, nch * H * V, 64, true))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)L::bytes);
+  if (e != cudaSuccess) return e;
+  dim3 grid(a.seqs.n_chunks, a.H);
+  kern<<<grid, kThreadsB16, L::bytes, st>>>(a, m);
+  return cudaGetLastError();
 }
 
 template <typename T, int D>
 cudaError_t launch_bwd_intra16(const BwdIntraArgs& a, cudaStream_t st) {
   using L = Bwd16Layout<D>;
-  auto kern = k_bwd_intra16<T, D>;
+  auto kern = k_bwd_intra16<T, D, false>;
   const uint64_t nch = (uint64_t)a.seqs.n_chunks, H = (uint64_t)a.H, K = (uint64_t)a.K,
                  V = (uint64_t)a.V, rows = (uint64_t)a.total_rows;
   if (nch == 0 || H == 0) return cudaSuccess;
@@ -791,6 +1093,9 @@ cudaError_t launch_bwd_intra16(const BwdIntraArgs& a, cudaStream_t st) {
   const uint64_t lim = (uint64_t)1 << 31;
   if (rows >= lim || nch * H * (K > V ? K : V) >= lim || nch * H * kChunk >= lim)
     return cudaErrorInvalidValue;
+  if constexpr (D == 128) {
+    if (K == 128 && V == 128 && tmap_available()) return launch_bwd_intra16_tc<T>(a, st);
+  }
   Bwd16Maps m;
   const uint64_t dK[3] = {K, H, rows}, sK[2] = {K * 2, H * K * 2}, sG[2] = {K * 4, H * K * 4};
   const uint64_t dV[3] = {V, H, rows}, sV[2] = {V * 2, H * V * 2};

@@ -151,6 +151,38 @@ __device__ __forceinline__ void warp_mma16_2a(float (&acc1)[1][NT][4], float (&a
   }
 }
 
+// ---- the same fragments from 128-byte-swizzled tiles ------------------------
+// Tiles of 64 16-bit elements per 128-byte row as TMA writes them with
+// 128-byte swizzle (the 16-byte chunk c of row r sits at chunk c ^ (r & 7));
+// `col` is a multiple of 8.
+__device__ __forceinline__ const void* sw128(const void* base, int row, int col) {
+  return static_cast<const unsigned char*>(base) + row * 128 + ((((col >> 3) ^ (row & 7))) << 4);
+}
+// Element address inside such a tile (any col).
+template <typename T>
+__device__ __forceinline__ const T* sw128_elem(const T* base, int row, int col) {
+  return reinterpret_cast<const T*>(sw128(base, row, col & ~7)) + (col & 7);
+}
+template <bool A_KMAJOR, typename T>
+__device__ __forceinline__ void load_a16_sw(uint32_t (&a)[4], const T* A, int m0, int k0) {
+  const int lane = threadIdx.x & 31;
+  if (A_KMAJOR) {
+    ldsm_x4(a, sw128(A, m0 + (lane & 15), k0 + ((lane >> 4) << 3)));
+  } else {
+    const int j = lane >> 3, rr = lane & 7;
+    ldsm_x4_t(a, sw128(A, k0 + rr + ((j >> 1) << 3), m0 + ((j & 1) << 3)));
+  }
+}
+template <bool B_KMAJOR, typename T>
+__device__ __forceinline__ void load_b16x2_sw(uint32_t (&b)[4], const T* B, int k0, int n0) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane >> 3, rr = lane & 7;
+  if (B_KMAJOR)
+    ldsm_x4(b, sw128(B, n0 + rr + ((j >> 1) << 3), k0 + ((j & 1) << 3)));
+  else
+    ldsm_x4_t(b, sw128(B, k0 + rr + ((j & 1) << 3), n0 + ((j >> 1) << 3)));
+}
+
 // Pack two floats into a 16-bit pair (low half = first).
 template <typename T> __device__ __forceinline__ uint32_t pack2(float x, float y);
 template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float x, float y) {

@@ -132,6 +132,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 16 consecutive fp32 columns of this thread's TMEM lane (same lane rule).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
@@ -205,6 +215,9 @@ bool tmap_available();
 // 128-byte swizzle (or none).
 bool tmap_2d_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_x,
                   bool swizzle);
+// Same with a box of box_x x box_y rows (box_x * 2 = 128 bytes), 128-byte swizzle.
+bool tmap_2d_box_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+                      uint32_t box_x, uint32_t box_y);
 // 3-D map over token rows [rows][H][D] of 2- or 4-byte elements: box box_x
 // columns (128 bytes) x 1 head x 64 rows, 128-byte swizzle.
 // Unswizzled 2-D or 3-D map (dims innermost first, strides of the outer

@@ -45,6 +45,19 @@ bool tmap_2d_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t row
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool tmap_2d_box_bf16(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+                      uint32_t box_x, uint32_t box_y) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc || box_x * 2 != 128 || box_y == 0 || box_y > 256) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_x, box_y};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool tmap_rows(CUtensorMap* m, const void* base, uint64_t D, uint64_t H, uint64_t rows,
                uint32_t box_x, int elem_bytes) {
   EncodeTiledFn enc = encode_fn();
