@@ -79,11 +79,28 @@ __device__ __forceinline__ void unpackv(const Pack<T, CPT>& r, float (&f)[CPT]) 
   for (int i = 0; i < CPT; ++i) f[i] = to_f<T>(e[i]);
 }
 
+// Two fp32 values -> one 32-bit word of two 16-bit values (one packed
+// round-to-nearest-even conversion).
+template <typename T> __device__ __forceinline__ uint32_t pack_pair(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack_pair<__half>(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 template <typename T, int CPT> __device__ __forceinline__ void stv(T* p, const float (&f)[CPT]) {
   Pack<T, CPT> r;
-  T* e = reinterpret_cast<T*>(r.u);
+  if constexpr (sizeof(T) == 2) {
 #pragma unroll
-  for (int i = 0; i < CPT; ++i) e[i] = from_f<T>(f[i]);
+    for (int i = 0; i < CPT / 2; ++i) r.u[i] = pack_pair<T>(f[2 * i], f[2 * i + 1]);
+  } else {
+    T* e = reinterpret_cast<T*>(r.u);
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) e[i] = from_f<T>(f[i]);
+  }
   constexpr int nb = Pack<T, CPT>::kBytes;
   if constexpr (nb == 4) {
     *reinterpret_cast<unsigned int*>(p) = r.u[0];
@@ -104,6 +121,19 @@ template <typename T, int CPT> __device__ __forceinline__ void zerov(Pack<T, CPT
 
 // Rounding to the token dtype (identity for fp32).
 template <typename T> __device__ __forceinline__ float rnd(float x) { return to_f<T>(from_f<T>(x)); }
+
+// Two values rounded at once: one packed conversion instead of two scalar
+// ones (scalar float -> 16-bit conversions issue on the special-function
+// pipe, which the SiLU's exponential and reciprocal already load).  Same
+// round-to-nearest-even result per element.
+template <typename T> __device__ __forceinline__ float2 rnd2(float2 v);
+template <> __device__ __forceinline__ float2 rnd2<float>(float2 v) { return v; }
+template <> __device__ __forceinline__ float2 rnd2<__nv_bfloat16>(float2 v) {
+  return __bfloat1622float2(__floats2bfloat162_rn(v.x, v.y));
+}
+template <> __device__ __forceinline__ float2 rnd2<__half>(float2 v) {
+  return __half22float2(__floats2half2_rn(v.x, v.y));
+}
 
 // SiLU in the reference's fp32 form x / (1 + exp(-x)), with the fast
 // exponential and division intrinsics: a few fp32 ulps from the exact form,
@@ -140,6 +170,7 @@ struct ConvArgs {
   float* dprefix;     // [B][W-1][D] or null
   float* dweight;     // [D][W]
   float* dbias;       // [D] or null
+  int seg;            // backward: rows per strip (grid.y strips per batch entry)
 };
 
 template <int W, int CPT>
@@ -243,9 +274,9 @@ __global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
 #pragma unroll
         for (int j = 0; j < W - 1; ++j) acc = __ffma2_rn(wt[j][p], win[j][p], acc);
         acc = __ffma2_rn(wt[W - 1][p], c2, acc);
-        const float c0 = rnd<T>(acc.x), c1 = rnd<T>(acc.y);
-        o[2 * p] = ACT ? silu_f(c0) : c0;
-        o[2 * p + 1] = ACT ? silu_f(c1) : c1;
+        const float2 cr = rnd2<T>(acc);
+        o[2 * p] = ACT ? silu_f(cr.x) : cr.x;
+        o[2 * p + 1] = ACT ? silu_f(cr.y) : cr.y;
 #pragma unroll
         for (int j = 0; j + 1 < W - 1; ++j) win[j][p] = win[j + 1][p];
         if (W > 1) win[WP - 1][p] = c2;
@@ -266,28 +297,115 @@ __global__ void __launch_bounds__(256, 2) k_conv_fwd(ConvArgs a) {
   }
 }
 
-// Backward over the strip's rows s in [tb, te + W - 1): dc_s = act'(c_s) dy_s
-// (rounded to the token dtype, as the reference's activation backward is),
-// dx_t = sum_j w_j dc_{t+W-1-j} emitted at s = t + W - 1, dw_j += dc_s
-// x_{s-W+1+j} and dbias += dc_s for s < te.  Rows t < 0 of the first strip
-// are the prefix rows (dprefix).  Each thread's sums of dw / dbias for its
+// One row of the backward (see k_conv_bwd): dc_s from dy_s and the
+// recomputed pre-activation, the dweight / dbias partial sums, and dx_t for
+// t = s - W + 1 out of the W-1 previous dc values.  EDGE = false is the
+// strip interior (s < T, s < te, tb <= t < te), where every test drops out.
+template <typename T, int W, int ACT, bool EDGE>
+__device__ __forceinline__ void conv_bwd_row(const ConvArgs& a, int s, int tb, int te, int send,
+                                             bool want_dprefix, int b, int d0,
+                                             const Pack<T, kBwdCPT>& rx,
+                                             const Pack<T, kBwdCPT>& rdy,
+                                             const float2 (&wt)[W][kBwdCPT / 2],
+                                             const float2 (&bs)[kBwdCPT / 2],
+                                             float2 (&win)[W > 1 ? W - 1 : 1][kBwdCPT / 2],
+                                             float2 (&dcw)[W > 1 ? W - 1 : 1][kBwdCPT / 2],
+                                             float2 (&dwp)[W + 1][kBwdCPT / 2], T* dxb) {
+  constexpr int CPT = kBwdCPT, CP = CPT / 2, WP = W > 1 ? W - 1 : 1;
+  if (EDGE && s >= send) return;
+  float cur[CPT], dy[CPT], o[CPT];
+  unpackv<T, CPT>(rx, cur);
+  unpackv<T, CPT>(rdy, dy);
+  const int t = s - (W - 1);  // the input row emitted at this step
+#pragma unroll
+  for (int p = 0; p < CP; ++p) {
+    const float2 c2 = make_float2(cur[2 * p], cur[2 * p + 1]);
+    float2 dc = make_float2(0.f, 0.f);
+    if (!EDGE || s < a.T) {
+      dc = make_float2(dy[2 * p], dy[2 * p + 1]);
+      if (ACT) {
+        float2 acc = bs[p];
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j) acc = __ffma2_rn(wt[j][p], win[j][p], acc);
+        acc = __ffma2_rn(wt[W - 1][p], c2, acc);
+        const float2 cr = rnd2<T>(acc);
+        dc = rnd2<T>(make_float2(silu_bwd_f(dc.x, cr.x), silu_bwd_f(dc.y, cr.y)));
+      }
+      if (!EDGE || s < te) {
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j) dwp[j][p] = __ffma2_rn(dc, win[j][p], dwp[j][p]);
+        dwp[W - 1][p] = __ffma2_rn(dc, c2, dwp[W - 1][p]);
+        dwp[W][p] = __fadd2_rn(dwp[W][p], dc);
+      }
+    }
+    float2 acc = __fmul2_rn(wt[0][p], dc);
+#pragma unroll
+    for (int j = 1; j < W; ++j) acc = __ffma2_rn(wt[j][p], dcw[W - 1 - j][p], acc);
+    o[2 * p] = acc.x;
+    o[2 * p + 1] = acc.y;
+#pragma unroll
+    for (int j = 0; j + 1 < W - 1; ++j) {
+      win[j][p] = win[j + 1][p];
+      dcw[j][p] = dcw[j + 1][p];
+    }
+    if (W > 1) {
+      win[WP - 1][p] = c2;
+      dcw[WP - 1][p] = dc;
+    }
+  }
+  if (!EDGE) {
+    stv<T, CPT>(dxb + (int64_t)t * a.D, o);
+  } else if (t >= tb) {
+    if (t < te) stv<T, CPT>(dxb + (int64_t)t * a.D, o);
+  } else if (want_dprefix && t >= -(W - 1)) {
+    float* dp = a.dprefix + ((int64_t)b * (W - 1) + (t + W - 1)) * a.D + d0;
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) dp[i] = o[i];
+  }
+}
+
+// x and dy rows s0 .. s0+R-1 (zeros past T or past the strip's last row).
+template <typename T, int R>
+__device__ __forceinline__ void conv_bwd_loads(const ConvArgs& a, const T* xb, const T* dyb,
+                                               int s0, int send, Pack<T, kBwdCPT> (&rx)[R],
+                                               Pack<T, kBwdCPT> (&rdy)[R]) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int s = s0 + r;
+    if (s < a.T && s < send) {
+      rx[r] = ldv<T, kBwdCPT>(xb + (int64_t)s * a.D);
+      rdy[r] = ldv<T, kBwdCPT>(dyb + (int64_t)s * a.D);
+    } else {
+      zerov<T, kBwdCPT>(rx[r]);
+      zerov<T, kBwdCPT>(rdy[r]);
+    }
+  }
+}
+
+// Backward over the strip's rows s in [tb, te + W - 1) (strip = a.seg rows):
+// dc_s = act'(c_s) dy_s (rounded to the token dtype, as the reference's
+// activation backward is), dx_t = sum_j w_j dc_{t+W-1-j} emitted at
+// s = t + W - 1, dw_j += dc_s x_{s-W+1+j} and dbias += dc_s for s < te.
+// Rows t < 0 of the first strip are the prefix rows (dprefix).  Rows go R at
+// a time, the next R rows' loads issued before this run's arithmetic (two
+// runs in flight per thread).  Each thread's sums of dw / dbias for its
 // channels go to part[blk][j][d] (blk = the CTA's strip), reduced over the
 // strips in a fixed order by k_col_sum.
 template <typename T, int W, int ACT>
 __global__ void __launch_bounds__(256, 2) k_conv_bwd(ConvArgs a) {
   constexpr int CPT = kBwdCPT, CP = CPT / 2;
-  constexpr int R = 4;
+  constexpr int R = sizeof(T) == 4 ? 2 : 4;  // (fp32 rows are twice as many registers)
   constexpr int WP = W > 1 ? W - 1 : 1;
   const int d0 = (blockIdx.x * 256 + threadIdx.x) * CPT;
   const int b = blockIdx.z;
-  const int tb = blockIdx.y * kConvStrip;
+  const int tb = blockIdx.y * a.seg;
   if (d0 >= a.D) return;
   float2 dwp[W + 1][CP];
 #pragma unroll
   for (int j = 0; j <= W; ++j)
 #pragma unroll
     for (int p = 0; p < CP; ++p) dwp[j][p] = make_float2(0.f, 0.f);
-  const int te = min(tb + kConvStrip, a.T);
+  const int te = min(tb + a.seg, a.T);
   float2 wt[W][CP], bs[CP];
   load_weight_pairs<W, CPT>(a, d0, wt, bs);
   const T* xb = reinterpret_cast<const T*>(a.x) + (int64_t)b * a.T * a.D + d0;
@@ -302,70 +420,26 @@ __global__ void __launch_bounds__(256, 2) k_conv_bwd(ConvArgs a) {
   }
   const int send = te + W - 1;
   const bool want_dprefix = a.dprefix && tb == 0;
+  Pack<T, CPT> rx[R], rdy[R];
+  conv_bwd_loads<T, R>(a, xb, dyb, tb, send, rx, rdy);
   for (int s0 = tb; s0 < send; s0 += R) {
-    Pack<T, CPT> rx[R], rdy[R];
+    Pack<T, CPT> nx[R], ndy[R];
+    if (s0 + R < send) conv_bwd_loads<T, R>(a, xb, dyb, s0 + R, send, nx, ndy);
+    if (s0 >= tb + W - 1 && s0 + R <= te) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int s = s0 + r;
-      if (s < a.T && s < send) {
-        rx[r] = ldv<T, CPT>(xb + (int64_t)s * a.D);
-        rdy[r] = ldv<T, CPT>(dyb + (int64_t)s * a.D);
-      } else {
-        zerov<T, CPT>(rx[r]);
-        zerov<T, CPT>(rdy[r]);
-      }
+      for (int r = 0; r < R; ++r)
+        conv_bwd_row<T, W, ACT, false>(a, s0 + r, tb, te, send, want_dprefix, b, d0, rx[r],
+                                       rdy[r], wt, bs, win, dcw, dwp, dxb);
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        conv_bwd_row<T, W, ACT, true>(a, s0 + r, tb, te, send, want_dprefix, b, d0, rx[r],
+                                      rdy[r], wt, bs, win, dcw, dwp, dxb);
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      const int s = s0 + r;
-      if (s >= send) continue;  // (predicated: the loop stays unrolled)
-      float cur[CPT], dy[CPT], o[CPT];
-      unpackv<T, CPT>(rx[r], cur);
-      unpackv<T, CPT>(rdy[r], dy);
-      const int t = s - (W - 1);  // the input row emitted at this step
-#pragma unroll
-      for (int p = 0; p < CP; ++p) {
-        const float2 c2 = make_float2(cur[2 * p], cur[2 * p + 1]);
-        float2 dc = make_float2(0.f, 0.f);
-        if (s < a.T) {
-          dc = make_float2(dy[2 * p], dy[2 * p + 1]);
-          if (ACT) {
-            float2 acc = bs[p];
-#pragma unroll
-            for (int j = 0; j < W - 1; ++j) acc = __ffma2_rn(wt[j][p], win[j][p], acc);
-            acc = __ffma2_rn(wt[W - 1][p], c2, acc);
-            dc.x = rnd<T>(silu_bwd_f(dc.x, rnd<T>(acc.x)));
-            dc.y = rnd<T>(silu_bwd_f(dc.y, rnd<T>(acc.y)));
-          }
-          if (s < te) {
-#pragma unroll
-            for (int j = 0; j < W - 1; ++j) dwp[j][p] = __ffma2_rn(dc, win[j][p], dwp[j][p]);
-            dwp[W - 1][p] = __ffma2_rn(dc, c2, dwp[W - 1][p]);
-            dwp[W][p] = __fadd2_rn(dwp[W][p], dc);
-          }
-        }
-        float2 acc = __fmul2_rn(wt[0][p], dc);
-#pragma unroll
-        for (int j = 1; j < W; ++j) acc = __ffma2_rn(wt[j][p], dcw[W - 1 - j][p], acc);
-        o[2 * p] = acc.x;
-        o[2 * p + 1] = acc.y;
-#pragma unroll
-        for (int j = 0; j + 1 < W - 1; ++j) {
-          win[j][p] = win[j + 1][p];
-          dcw[j][p] = dcw[j + 1][p];
-        }
-        if (W > 1) {
-          win[WP - 1][p] = c2;
-          dcw[WP - 1][p] = dc;
-        }
-      }
-      if (t >= tb) {
-        if (t < te) stv<T, CPT>(dxb + (int64_t)t * a.D, o);
-      } else if (want_dprefix && t >= -(W - 1)) {
-        float* dp = a.dprefix + ((int64_t)b * (W - 1) + (t + W - 1)) * a.D + d0;
-#pragma unroll
-        for (int i = 0; i < CPT; ++i) dp[i] = o[i];
-      }
+      rx[r] = nx[r];
+      rdy[r] = ndy[r];
     }
   }
   const int blk = blockIdx.z * gridDim.y + blockIdx.y;
@@ -415,25 +489,53 @@ __global__ void __launch_bounds__(256) k_col_sum(const float* part, int nblk, in
   }
 }
 
+// Upper bound of the backward's strip count (the partial-sum rows): never
+// more than ceil(T / kConvStrip) strips per batch entry.
 int conv_nblk(const gdn2_conv_problem* p) {
   return p->B * ((p->T + kConvStrip - 1) / kConvStrip);
 }
 
+// Backward strips: one wave.  With `slots` CTAs resident on the GPU and
+// B x ceil(D / 1024) channel columns, each column of T rows is cut into
+// floor(slots / columns) strips (at least one, at most ceil(T / kConvStrip)),
+// so every SM gets the same number of rows and no CTA waits for a second
+// wave; many columns (more than the slots) fall back to one strip each.
+template <typename K>
+cudaError_t conv_bwd_strip(K kernel, const gdn2_conv_problem* p, int* seg) {
+  int sms = 0, occ = 0;
+  cudaError_t e = num_sms(&sms);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, 256, 0);
+  if (e != cudaSuccess) return e;
+  const int64_t cols = (int64_t)p->B * ((p->D + kConvChannels - 1) / kConvChannels);
+  const int64_t slots = (int64_t)sms * (occ > 0 ? occ : 1);
+  const int64_t most = (p->T + kConvStrip - 1) / kConvStrip;
+  int64_t n = slots / cols;
+  n = n < 1 ? 1 : (n > most ? most : n);
+  *seg = (int)((p->T + n - 1) / n);
+  return cudaSuccess;
+}
+
 template <typename T, int W>
-cudaError_t launch_conv(const gdn2_conv_problem* p, const ConvArgs& a, bool bwd, cudaStream_t st) {
+cudaError_t launch_conv(const gdn2_conv_problem* p, const ConvArgs& a0, bool bwd,
+                        cudaStream_t st) {
   static_assert(kFwdCPT * 256 == kConvChannels && kBwdCPT * 256 == kConvChannels, "CTA width");
-  dim3 grid((p->D + kConvChannels - 1) / kConvChannels, (p->T + kConvStrip - 1) / kConvStrip, p->B);
+  const int gx = (p->D + kConvChannels - 1) / kConvChannels;
   if (!bwd) {
-    if (p->activation) k_conv_fwd<T, W, 1><<<grid, 256, 0, st>>>(a);
-    else k_conv_fwd<T, W, 0><<<grid, 256, 0, st>>>(a);
+    dim3 grid(gx, (p->T + kConvStrip - 1) / kConvStrip, p->B);
+    if (p->activation) k_conv_fwd<T, W, 1><<<grid, 256, 0, st>>>(a0);
+    else k_conv_fwd<T, W, 0><<<grid, 256, 0, st>>>(a0);
     return cudaGetLastError();
   }
-  if (p->activation) k_conv_bwd<T, W, 1><<<grid, 256, 0, st>>>(a);
-  else k_conv_bwd<T, W, 0><<<grid, 256, 0, st>>>(a);
-  cudaError_t e = cudaGetLastError();
+  ConvArgs a = a0;
+  auto kern = p->activation ? k_conv_bwd<T, W, 1> : k_conv_bwd<T, W, 0>;
+  cudaError_t e = conv_bwd_strip(kern, p, &a.seg);
+  if (e != cudaSuccess) return e;
+  const int nseg = (p->T + a.seg - 1) / a.seg;
+  kern<<<dim3(gx, nseg, p->B), 256, 0, st>>>(a);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int n = (W + 1) * p->D;
-  k_col_sum<<<(n + 31) / 32, 256, 0, st>>>(a.part, conv_nblk(p), n, W, p->D, a.dweight, a.dbias);
+  k_col_sum<<<(n + 31) / 32, 256, 0, st>>>(a.part, p->B * nseg, n, W, p->D, a.dweight, a.dbias);
   return cudaGetLastError();
 }
 
@@ -530,18 +632,25 @@ __global__ void __launch_bounds__(256) k_gnorm_fwd(NormArgs a) {
 #pragma unroll
       for (int p = 0; p < NP; ++p)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss += rnd<TR>(x[p][i] * x[p][i]);
+        for (int i = 0; i < 8; i += 2) {
+          const float2 sq = rnd2<TR>(make_float2(x[p][i] * x[p][i], x[p][i + 1] * x[p][i + 1]));
+          ss += sq.x;
+          ss += sq.y;
+        }
       ss = group_sum<TPR>(ss);
       const float var = rnd<TR>(ss * inv_n);
       const float r = rnd<TR>(rsqrtf(rnd<TR>(var + a.eps)));
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
+        using TN = typename std::conditional<F32, float, TW>::type;  // the n * w rounding
         float y[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float n = rnd<TR>(x[p][i] * r);
-          n = rnd<typename std::conditional<F32, float, TW>::type>(n * w[p][i]);
-          y[i] = n * rnd<T>(silu_f(z[p][i]));
+        for (int i = 0; i < 8; i += 2) {
+          float2 n = rnd2<TR>(make_float2(x[p][i] * r, x[p][i + 1] * r));
+          n = rnd2<TN>(make_float2(n.x * w[p][i], n.y * w[p][i + 1]));
+          const float2 s = rnd2<T>(make_float2(silu_f(z[p][i]), silu_f(z[p][i + 1])));
+          y[i] = n.x * s.x;
+          y[i + 1] = n.y * s.y;
         }
         if (on[u])
           stv<TO, 8>(reinterpret_cast<TO*>(a.y) + (base + u * RPC + slot) * a.N + c + 8 * p, y);
