@@ -235,7 +235,12 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_problem* p,
  *   forward=1:  x = init (or 0);  for j = 0 .. rank-1:        x = M_j x + h_e_j
  *   forward=0:  x = init (or 0);  for j = world-1 .. rank+1:  x = M_j^T x + dhm_j
  * and state_out = x ([N,H,K,V] fp32).  `init` is the global initial state
- * (forward) or the gradient of the global final state (backward). */
+ * (forward) or the gradient of the global final state (backward).
+ * Workspace: gdn2_cp_workspace_bytes(p) is 0 or the size of a buffer that
+ * lets gdn2_cp_bwd_prescan run the tensor-core backward state pass (bf16,
+ * K = V = 128); given one at least that large (a gdn2_chunk_bwd workspace
+ * is), the pre-scan writes scratch tiles into it, otherwise it runs the
+ * register-state pass.  gdn2_cp_fwd_prescan takes no workspace (pass NULL). */
 size_t gdn2_cp_workspace_bytes(const gdn2_chunk_problem* p);
 int gdn2_cp_fwd_prescan(const gdn2_chunk_problem* p, const void* saved,
                         size_t saved_bytes, float* hm, void* workspace,

@@ -399,9 +399,12 @@ size_t gdn2_chunk_bwd_workspace_bytes(const gdn2_chunk_problem* p) {
   return bwd_layout_of(p).total;
 }
 
+// The backward pre-scan can run as the tensor-core state pass (bf16, K = V =
+// 128), which writes its per-chunk gradient tiles to a backward workspace.
 size_t gdn2_cp_workspace_bytes(const gdn2_chunk_problem* p) {
-  (void)p;
-  return 0;
+  if (check_problem(p, "gdn2_cp_workspace_bytes") != GDN2_OK) return 0;
+  if (p->dtype != GDN2_DTYPE_BF16 || p->K != 128 || p->V != 128) return 0;
+  return bwd_layout_of(p).total;
 }
 
 int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p, const void* q, const void* k, const void* v,
@@ -630,8 +633,6 @@ int gdn2_cp_fwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t s
 int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t saved_bytes,
                         const void* dout, const float* dht, float* dhm, void* workspace,
                         size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   int rc = check_problem(p, "gdn2_cp_bwd_prescan");
   if (rc) return rc;
   if (!saved || !dout || !dhm) return fail(GDN2_ERR_INVALID, "gdn2_cp_bwd_prescan: null pointer");
@@ -649,6 +650,20 @@ int gdn2_cp_bwd_prescan(const gdn2_chunk_problem* p, const void* saved, size_t s
   s.BL = bwd_layout_of(p);
   s.prescan = 1;
   s.total_rows = p->seqs.total_tokens;
+  // With a workspace of gdn2_cp_workspace_bytes() the span-start gradient
+  // comes from the tensor-core backward state pass (its dh0 output, dht as
+  // the end gradient); the per-chunk dh / dVN tiles it also writes land in
+  // the workspace and are not used.  Without one, the register-state pre-scan.
+  const size_t need = gdn2_cp_workspace_bytes(p);
+  if (workspace && need && workspace_bytes >= need) {
+    BwdStateArgs t = s;
+    t.ws = static_cast<unsigned char*>(workspace);
+    t.prescan = 0;
+    if (bwd_state_tc_ok(t, 1)) {
+      cudaError_t e = launch_bwd_state_tc(t, (cudaStream_t)stream);
+      return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_bwd_prescan");
+    }
+  }
   cudaError_t e = bwd_state_dispatch(p, s, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_bwd_prescan");
 }

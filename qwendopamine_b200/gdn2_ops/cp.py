@@ -202,24 +202,28 @@ class CPChunkGDN2Function(torch.autograd.Function):
         # the earlier ranks, and it adds to what the later ranks' outputs
         # send back through S_r.
         dht_direct = dht.float().contiguous() if dht is not None else None
+        # The backward workspace also serves the pre-scan (it then runs as the
+        # tensor-core state pass, whose per-chunk tiles the real pass rewrites).
+        wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
+        ws = torch.empty(max(wbytes, 1), dtype=torch.uint8, device=dev)
+        pbytes = lib.gdn2_cp_workspace_bytes(prob)
+        pws, pwb = (N.ptr(ws), wbytes) if 0 < pbytes <= wbytes else (None, 0)
         # Span-start gradient of the local outputs and of dht_direct.
         if S == 1:
             dhm = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
             with N.phase("bwd_prescan"):
                 N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do),
-                                                N.ptr(dht_direct), N.ptr(dhm), None, 0, st),
+                                                N.ptr(dht_direct), N.ptr(dhm), pws, pwb, st),
                         "gdn2_cp_bwd_prescan")
         else:
             dhm_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
             with N.phase("bwd_prescan"):
                 N.check(lib.gdn2_cp_bwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(do), None,
-                                                N.ptr(dhm_sub), None, 0, st),
+                                                N.ptr(dhm_sub), pws, pwb, st),
                         "gdn2_cp_bwd_prescan")
             dhm_sub = dhm_sub.view(B, S, H, K, V)
             with N.phase("bwd_fold"):
                 dhm = _compose_grads(dhm_sub, hm_sub, dht_direct)
-        wbytes = lib.gdn2_chunk_bwd_workspace_bytes(prob)
-        ws = torch.empty(max(wbytes, 1), dtype=torch.uint8, device=dev)
         with N.phase("bwd_gather"):
             dhm_all = gather(dhm)
         if last:

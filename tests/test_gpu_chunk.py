@@ -430,8 +430,10 @@ def test_extreme_decay_16bit_forward_backward(cuda_device, decay, KV):
         tol = TOL[torch.bfloat16]
         if n == "b" and K == 64:
             # d_beta (key side) with 64-wide heads under decays of >= 6 nats per
-            # token: the signal is O(e^-6) and the 16-bit intermediates leave
-            # 2.1e-2 (1.0e-2 at K = 128; 7e-6 on the fp32 path).
+            # token: 2.1e-2 here (1.0e-2 at K = 128; 7e-6 on the fp32 path).
+            # The bf16 storage of Kd, dh and dVN between kernels -- the
+            # reference's storage precision -- alone gives 1.9e-2 on this case
+            # in otherwise exact arithmetic (test_bf16_storage_bound.py).
             tol = 3e-2
         assert rel(gr[n], r) < tol, n
     # dg where it carries signal: compare on the channels / rows with |dg| large

@@ -26,7 +26,7 @@ def _spans(T, P):
     return [(cuts[r], cuts[r + 1]) for r in range(P)]
 
 
-def _emulate(d, P, dtype, dev, do, dht):
+def _emulate(d, P, dtype, dev, do, dht, prescan_ws=False):
     lib = N.load()
     B, T, H, K = d["q"].shape
     V = d["v"].shape[-1]
@@ -62,9 +62,11 @@ def _emulate(d, P, dtype, dev, do, dht):
     for i, r in enumerate(ranks):
         r["do"] = dod[:, r["a"]:r["e"]].contiguous()
         r["dhm"] = torch.empty(B, H, K, V, device=dev)
+        pb = lib.gdn2_cp_workspace_bytes(r["prob"]) if prescan_ws else 0
+        pws = torch.empty(max(pb, 1), dtype=torch.uint8, device=dev)
         N.check(lib.gdn2_cp_bwd_prescan(r["prob"], N.ptr(r["saved"]), r["sb"], N.ptr(r["do"]),
                                         N.ptr(dhtd) if i == P - 1 else None, N.ptr(r["dhm"]),
-                                        None, 0, st), "bwd pre")
+                                        N.ptr(pws) if pb else None, pb, st), "bwd pre")
     dhm_all = torch.stack([r["dhm"] for r in ranks])
     grads = {n: [] for n in (*NAMES, "h0")}
     for i, r in enumerate(ranks):
@@ -109,21 +111,25 @@ def test_sequence_parallel_matches_full_sequence_fp32(cuda_device, P, T):
         assert rel(g[n], r) < 1e-4, n
 
 
-def test_sequence_parallel_config4_recipe_bf16(cuda_device):
+@pytest.mark.parametrize("prescan_ws", [False, True])
+def test_sequence_parallel_config4_recipe_bf16(cuda_device, prescan_ws):
     """Config-4 recipe (scalar beta / decay broadcast, bf16) on 8 spans of a
-    shortened sequence with H=32 heads."""
+    shortened sequence with H=32 heads; the backward pre-scan as the
+    register-state pass and, given a workspace, as the tensor-core state
+    pass."""
     P, B, T, H, K, V = 8, 1, 8 * 128, 32, 128, 128
     d = make_inputs(B, T, H, K, V, seed=4, decay="baseline", dtype=torch.bfloat16,
                     scalar_gates=True, h0=False)
     d["h0"] = torch.zeros(B, H, K, V)
     gen = torch.Generator().manual_seed(8)
     do = torch.randn(B, T, H, V, generator=gen).bfloat16().float()
-    dht = torch.zeros(B, H, K, V)
-    o, ht, g = _emulate(d, P, torch.bfloat16, cuda_device, do, dht)
+    dht = torch.randn(B, H, K, V, generator=gen) if prescan_ws else torch.zeros(B, H, K, V)
+    o, ht, g = _emulate(d, P, torch.bfloat16, cuda_device, do, dht, prescan_ws=prescan_ws)
     args = np_(d, NAMES)
     ro, rh = O.recurrent_fwd(*args, None, norm_mode="fla")
     assert rel(o, ro) < 2e-2 and rel(ht, rh) < 2e-2
-    ref = O.recurrent_bwd(*args, do.numpy(), None, None, norm_mode="fla")
+    ref = O.recurrent_bwd(*args, do.numpy(), None, dht.numpy() if prescan_ws else None,
+                          norm_mode="fla")
     for n, r in zip(NAMES, ref):
         assert rel(g[n], r) < 2e-2, n
 
