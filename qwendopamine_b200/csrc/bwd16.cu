@@ -305,13 +305,16 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
         tc::tc_fence_after();
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
+          // descriptors: layout constants OR the tile address in 16-byte units
           const uint32_t acc = (sl > 0 || j > 0) ? 1u : 0u;
-          tc::umma_bf16(tmem + 0, tc::sdesc(th + 16 * j, 16, 1024, tc::kSwizzle128),
-                        tc::sdesc(tdo + 16 * j, 16, 1024, tc::kSwizzle128), kIdKK, acc);
-          tc::umma_bf16(tmem + 64, tc::sdesc(tdh + 16 * j, 16, 1024, tc::kSwizzle128),
-                        tc::sdesc(tvn + 1024 * j, 8192, 1024, tc::kSwizzle128), kIdKM, acc);
-          tc::umma_bf16(tmem + 128, tc::sdesc(th + 16 * j, 16, 1024, tc::kSwizzle128),
-                        tc::sdesc(tdvn + 1024 * j, 8192, 1024, tc::kSwizzle128), kIdKM, acc);
+          const uint32_t w16 = smem_u32(W) >> 4, s16 = w16 + (slot_off(sl, 0) >> 4);
+          const uint64_t dK = tc::sdesc_layout(16, 1024, tc::kSwizzle128);
+          const uint64_t dM = tc::sdesc_layout(8192, 1024, tc::kSwizzle128);
+          const uint64_t dH = dK | (w16 + (L::tH >> 4) + 2 * j);
+          tc::umma_bf16(tmem + 0, dH, dK | (s16 + (L::tDO >> 4) + 2 * j), kIdKK, acc);
+          tc::umma_bf16(tmem + 64, dK | (w16 + (L::tDH >> 4) + 2 * j),
+                        dM | (s16 + (L::tVN >> 4) + 128 * j), kIdKM, acc);
+          tc::umma_bf16(tmem + 128, dH, dM | (s16 + (L::tDVN >> 4) + 128 * j), kIdKM, acc);
         }
         tc::umma_commit(barMma);
         ++mma_commits;
@@ -688,27 +691,43 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
   acc_zero(accE);
   warp_mma16<1, NTO, false, false>(accE, sA, LDC, 16 * wr, sDW, LDK, wc * DQ, kChunk);
 
-  // ---- owner initialisation ---------------------------------------------
+  // every read of sDW / sE / sT* is done: R2 becomes the score operands
+  if (tid == 0) sFlag[0] = 1;
+  __syncthreads();
+
+  // ---- owner initialisation and score operands ----------------------------
   // dq <- scale 2^G dQg, dkb <- 2^G dE, dk <- Kd part, X <- k_n * Kd part,
-  // dG <- q_n dq + b k_n dkb
+  // dG <- q_n dq + b k_n dkb; in the same pass (same loads) the score
+  // backward's operands with per-16-row-block references (every factor <= 1):
+  //   Qs[r] = scale q_n[r] 2^(G_r - G_b(r)),  KBs[r] = (b k_n)[r] 2^(G_r - G_b(r)),
+  //   Kb[i] = k_n[i] 2^(G_e(i) - G_i);
+  // key block J enters block row I scaled by F_IJ = 2^(G_16I - G_(16J+15)).
   float (&dq)[1][NTO][4] = accQ;
   float (&dkb)[1][NTO][4] = accE;
   float (&dkn)[1][NTO][4] = accKd;
   float (&dG)[1][NTO][4] = accW;
+  T* sQs = reinterpret_cast<T*>(W + L::kQs);
+  T* sKBs = reinterpret_cast<T*>(W + L::kKBs);
+  T* sKb = reinterpret_cast<T*>(W + L::kKb);
+  block_factors<D, NTH>(sG, LDG, sF);
   // (owner elements come in column pairs: e = 2 hf + t is row 16 wr + gid +
   // 8 hf, column wc DQ + 8 j + 2 tig + t, so each pair is one 32-bit access)
   float X[NTO][4];
 #pragma unroll
-  for (int j = 0; j < NTO; ++j)
+  for (int j = 0; j < NTO; ++j) {
+    const int c0 = wc * DQ + 8 * j + 2 * tig;
+    const float2 GL2 = ld2<float>(sG + (kChunk - 1) * LDG + c0);
+    const float2 Gb2 = ld2<float>(sG + (16 * wr) * LDG + c0);
+    const float2 Ge2 = ld2<float>(sG + (16 * wr + 15) * LDG + c0);
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
-      const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
+      const int r = 16 * wr + gid + 8 * hf;
       const float2 G2 = ld2<float>(sG + r * LDG + c0);
-      const float2 GL2 = ld2<float>(sG + (kChunk - 1) * LDG + c0);
       const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
       const float2 b2 = ld2<T>(sb + r * LDK + c0);
       const float2 gam = exp2_2(G2);
       const float2 qn = mul2(q2, f2(rq[r])), kn = mul2(k2, f2(rk[r]));
+      const float2 bkn = mul2(b2, kn);
       const float2 dqv = mul2(mul2(f2(scale), gam), pr(dq[0][j], hf));
       const float2 dkbv = mul2(gam, pr(dkb[0][j], hf));
       const float2 kd = mul2(pr(dkn[0][j], hf), exp2_2(make_float2(GL2.x - G2.x, GL2.y - G2.y)));
@@ -716,37 +735,16 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
       setpr(dkb[0][j], hf, dkbv);
       setpr(dkn[0][j], hf, kd);
       setpr(X[j], hf, mul2(kn, kd));
-      setpr(dG[0][j], hf, fma2(qn, dqv, mul2(mul2(b2, kn), dkbv)));
+      setpr(dG[0][j], hf, fma2(qn, dqv, mul2(bkn, dkbv)));
+      const float2 f = exp2_2(make_float2(G2.x - Gb2.x, G2.y - Gb2.y));
+      const float2 fe = exp2_2(make_float2(Ge2.x - G2.x, Ge2.y - G2.y));
+      const float2 qs = mul2(mul2(f2(scale), qn), f);
+      const float2 kbs = mul2(bkn, f);
+      const float2 kb = mul2(kn, fe);
+      *reinterpret_cast<uint32_t*>(sQs + r * LDK + c0) = pack2<T>(qs.x, qs.y);
+      *reinterpret_cast<uint32_t*>(sKBs + r * LDK + c0) = pack2<T>(kbs.x, kbs.y);
+      *reinterpret_cast<uint32_t*>(sKb + r * LDK + c0) = pack2<T>(kb.x, kb.y);
     }
-  __syncthreads();  // sDW / sE / sT* are dead; R2 becomes the score tiles
-
-  // ---- score backward ---------------------------------------------------------
-  // Operands with per-16-row-block references (every factor <= 1):
-  //   Qs[r] = scale q_n[r] 2^(G_r - G_b(r)),  KBs[r] = (b k_n)[r] 2^(G_r - G_b(r)),
-  //   Kb[i] = k_n[i] 2^(G_e(i) - G_i);
-  // key block J enters block row I scaled by F_IJ = 2^(G_16I - G_(16J+15)).
-  T* sQs = reinterpret_cast<T*>(W + L::kQs);
-  T* sKBs = reinterpret_cast<T*>(W + L::kKBs);
-  T* sKb = reinterpret_cast<T*>(W + L::kKb);
-  if (tid == 0) sFlag[0] = 1;
-  block_factors<D, NTH>(sG, LDG, sF);
-  __syncthreads();
-  for (int i = tid; i < kChunk * (D / 2); i += NTH) {
-    const int r = i / (D / 2), cc = (i - r * (D / 2)) * 2;
-    const int rb = r & ~15, re = rb + 15;
-    const float2 G2 = ld2<float>(sG + r * LDG + cc), Gb2 = ld2<float>(sG + rb * LDG + cc);
-    const float2 Ge2 = ld2<float>(sG + re * LDG + cc);
-    const float2 qv = ld2<T>(sq + r * LDK + cc), kv = ld2<T>(sk + r * LDK + cc);
-    const float2 bv = ld2<T>(sb + r * LDK + cc);
-    const float2 f = exp2_2(make_float2(G2.x - Gb2.x, G2.y - Gb2.y));
-    const float2 fe = exp2_2(make_float2(Ge2.x - G2.x, Ge2.y - G2.y));
-    const float2 kn = mul2(kv, f2(rk[r]));
-    const float2 q2 = mul2(mul2(mul2(f2(scale), qv), f2(rq[r])), f);
-    const float2 kb2 = mul2(mul2(bv, kn), f);
-    const float2 k2 = mul2(kn, fe);
-    *reinterpret_cast<uint32_t*>(sQs + r * LDK + cc) = pack2<T>(q2.x, q2.y);
-    *reinterpret_cast<uint32_t*>(sKBs + r * LDK + cc) = pack2<T>(kb2.x, kb2.y);
-    *reinterpret_cast<uint32_t*>(sKb + r * LDK + cc) = pack2<T>(k2.x, k2.y);
   }
   for (int i = tid; i < 4 * D; i += NTH) {
     const int bI = i / D, cc = i - bI * D;

@@ -68,11 +68,13 @@ constexpr uint32_t kIdHW = tc::idesc_bf16(128, 64, 1, 0);    // h^T W^T, h^T Qg^
 constexpr uint32_t kIdVA = tc::idesc_bf16(128, 64, 0, 0);    // VN^T Aqk^T
 constexpr uint32_t kIdKV = tc::idesc_bf16(128, 128, 1, 0);   // Kd^T VN
 
-__device__ __forceinline__ uint64_t desc_k(const void* p) {  // K-major, 128B swizzle
-  return tc::sdesc(p, 16, 1024, tc::kSwizzle128);
+// Operand descriptors from shared-memory addresses in 16-byte units (tile
+// bases are 1024-byte aligned, so every offset below is a whole unit).
+__device__ __forceinline__ uint64_t desc_k(uint32_t a16) {  // K-major, 128B swizzle
+  return tc::sdesc_layout(16, 1024, tc::kSwizzle128) | a16;
 }
-__device__ __forceinline__ uint64_t desc_mn(const void* p, uint32_t mn_stride) {  // MN-major
-  return tc::sdesc(p, mn_stride, 1024, tc::kSwizzle128);
+__device__ __forceinline__ uint64_t desc_mn(uint32_t a16, uint32_t mn_stride) {  // MN-major
+  return tc::sdesc_layout(mn_stride, 1024, tc::kSwizzle128) | a16;
 }
 
 __device__ __forceinline__ void st_shared_v4(void* p, uint4 x) {
@@ -102,7 +104,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(full + 4);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
   unsigned char* sH = sm + kOffH;
+  const uint32_t sH16 = (smem_u32(sm) >> 4) + (kOffH >> 4);
   unsigned char* sVN = sm + kOffVN;
+  const uint32_t sVN16 = (smem_u32(sm) >> 4) + (kOffVN >> 4);
   unsigned char* sO = sm + kOffO;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -265,6 +269,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (; c < c_end; ++c) {
       const int i = c - c_begin, slot = i & 1;
       unsigned char* p = sm + slot * kSlotBytes;
+      const uint32_t p16 = (smem_u32(sm) >> 4) + slot * (kSlotBytes >> 4);
       const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
 
       // 1. VN^T = h^T W^T,  o^T = h^T Qg^T;  meanwhile the checkpoint of
@@ -276,12 +281,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            tc::umma_bf16(tmem + kColVN, desc_mn(sH + j * 2048, kHalfH),
-                          desc_k(p + kOffW + (j >> 2) * kBox + (j & 3) * 32), kIdHW, j > 0);
+            tc::umma_bf16(tmem + kColVN, desc_mn(sH16 + ((j * 2048) >> 4), kHalfH),
+                          desc_k(p16 + ((kOffW + (j >> 2) * kBox + (j & 3) * 32) >> 4)), kIdHW, j > 0);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            tc::umma_bf16(tmem + kColO, desc_mn(sH + j * 2048, kHalfH),
-                          desc_k(p + kOffQg + (j >> 2) * kBox + (j & 3) * 32), kIdHW, j > 0);
+            tc::umma_bf16(tmem + kColO, desc_mn(sH16 + ((j * 2048) >> 4), kHalfH),
+                          desc_k(p16 + ((kOffQg + (j >> 2) * kBox + (j & 3) * 32) >> 4)), kIdHW, j > 0);
           tc::umma_commit(mma1);
           ++mma1_commits;
         }
@@ -328,10 +333,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc::tc_fence_after();
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::umma_bf16(tmem + kColO, desc_k(sVN + j * 32), desc_k(p + kOffAqk + j * 32), kIdVA, 1);
+          tc::umma_bf16(tmem + kColO, desc_k(sVN16 + ((j * 32) >> 4)), desc_k(p16 + ((kOffAqk + j * 32) >> 4)), kIdVA, 1);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::umma_bf16(tmem + kColH, desc_mn(p + kOffKd + j * 2048, kBox), desc_k(sVN + j * 32),
+          tc::umma_bf16(tmem + kColH, desc_mn(p16 + ((kOffKd + j * 2048) >> 4), kBox), desc_k(sVN16 + ((j * 32) >> 4)),
                         kIdKV, 1);
         tc::umma_commit(mma2);
         ++mma2_commits;
@@ -439,7 +444,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(full + 4);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
   unsigned char* sH = sm + kOffH;    // bf16 dh [k][v], MN-major
+  const uint32_t sH16 = (smem_u32(sm) >> 4) + (kOffH >> 4);
   unsigned char* sVN = sm + kOffVN;  // bf16 -dVN^T [v][t], K-major
+  const uint32_t sVN16 = (smem_u32(sm) >> 4) + (kOffVN >> 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2;
@@ -585,6 +592,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (; c >= c_begin; --c) {
       const int i = c_end - 1 - c, slot = i & 1;
       unsigned char* p = sm + slot * kSlotBytes;
+      const uint32_t p16 = (smem_u32(sm) >> 4) + slot * (kSlotBytes >> 4);
       const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
       const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
 
@@ -613,12 +621,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            tc::umma_bf16(tmem + kColVN, desc_mn(p + kOffDO + j * 2048, kBox),
-                          desc_mn(p + kOffAqk + j * 2048, kBox), kIdOA, j > 0);
+            tc::umma_bf16(tmem + kColVN, desc_mn(p16 + ((kOffDO + j * 2048) >> 4), kBox),
+                          desc_mn(p16 + ((kOffAqk + j * 2048) >> 4), kBox), kIdOA, j > 0);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            tc::umma_bf16(tmem + kColVN, desc_mn(sH + j * 2048, kHalfH),
-                          desc_k(p + kOffKd + (j >> 2) * kBox + (j & 3) * 32), kIdHW, 1);
+            tc::umma_bf16(tmem + kColVN, desc_mn(sH16 + ((j * 2048) >> 4), kHalfH),
+                          desc_k(p16 + ((kOffKd + (j >> 2) * kBox + (j & 3) * 32) >> 4)), kIdHW, 1);
           tc::umma_commit(mma1);
           ++mma1_commits;
         }
@@ -655,11 +663,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc::tc_fence_after();
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::umma_bf16(tmem + kColH, desc_mn(p + kOffQg + j * 2048, kBox),
-                        desc_mn(p + kOffDO + j * 2048, kBox), kIdQO, 1);
+          tc::umma_bf16(tmem + kColH, desc_mn(p16 + ((kOffQg + j * 2048) >> 4), kBox),
+                        desc_mn(p16 + ((kOffDO + j * 2048) >> 4), kBox), kIdQO, 1);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::umma_bf16(tmem + kColH, desc_mn(p + kOffW + j * 2048, kBox), desc_k(sVN + j * 32),
+          tc::umma_bf16(tmem + kColH, desc_mn(p16 + ((kOffW + j * 2048) >> 4), kBox), desc_k(sVN16 + ((j * 32) >> 4)),
                         kIdKV, 1);
         tc::umma_commit(mma2);
         ++mma2_commits;
@@ -775,7 +783,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(full + 4);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
   unsigned char* sH = sm + kHOffH;
+  const uint32_t sH16 = (smem_u32(sm) >> 4) + (kHOffH >> 4);
   unsigned char* sVN = sm + kHOffVN;
+  const uint32_t sVN16 = (smem_u32(sm) >> 4) + (kHOffVN >> 4);
   unsigned char* sVT = sm + kHOffVT;
   unsigned char* sO = sm + kHOffO;
 
@@ -942,6 +952,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (; c < c_end; ++c) {
       const int i = c - c_begin, slot = i & 1;
       unsigned char* p = sm + slot * kHSlotBytes;
+      const uint32_t p16 = (smem_u32(sm) >> 4) + slot * (kHSlotBytes >> 4);
       const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
 
       // 1. D = [W ; Qg] h_half;  meanwhile the checkpoint of chunk c and the
@@ -953,8 +964,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            tc::umma_bf16(tmem + kHColD, desc_k(p + kHOffWQ + (j >> 2) * 2 * kBox + (j & 3) * 32),
-                          desc_mn(sH + j * 2048, kBox), kIdWQh, j > 0);
+            tc::umma_bf16(tmem + kHColD, desc_k(p16 + ((kHOffWQ + (j >> 2) * 2 * kBox + (j & 3) * 32) >> 4)),
+                          desc_mn(sH16 + ((j * 2048) >> 4), kBox), kIdWQh, j > 0);
           tc::umma_commit(mma1);
           ++mma1_commits;
         }
@@ -1011,12 +1022,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc::tc_fence_after();
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::umma_bf16(tmem + kHColD, desc_k(p + kHOffZ + j * 32), desc_mn(sVN + j * 2048, kBox),
+          tc::umma_bf16(tmem + kHColD, desc_k(p16 + ((kHOffZ + j * 32) >> 4)), desc_mn(sVN16 + ((j * 2048) >> 4), kBox),
                         kIdWQh, 1);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::umma_bf16(tmem + kHColH, desc_mn(p + kHOffKd + j * 2048, kBox),
-                        desc_mn(sVN + j * 2048, kBox), kIdKVh, 1);
+          tc::umma_bf16(tmem + kHColH, desc_mn(p16 + ((kHOffKd + j * 2048) >> 4), kBox),
+                        desc_mn(sVN16 + ((j * 2048) >> 4), kBox), kIdKVh, 1);
         tc::umma_commit(mma2);
         ++mma2_commits;
       }
@@ -1137,7 +1148,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(full + 4);
   volatile int* sAbort = reinterpret_cast<volatile int*>(sTmem + 1);
   unsigned char* sH = sm + kBOffH;
+  const uint32_t sH16 = (smem_u32(sm) >> 4) + (kBOffH >> 4);
   unsigned char* sVN = sm + kBOffVN;
+  const uint32_t sVN16 = (smem_u32(sm) >> 4) + (kBOffVN >> 4);
   unsigned char* sVT = sm + kBOffVT;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1287,6 +1300,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (; c >= c_begin; --c) {
       const int i = c_end - 1 - c, slot = i & 1;
       unsigned char* p = sm + slot * kBSlotBytes;
+      const uint32_t p16 = (smem_u32(sm) >> 4) + slot * (kBSlotBytes >> 4);
       const uint32_t par_full = (i >> 1) & 1, par_mma = i & 1;
       const ChunkPos cp = chunk_pos_in_seq(bos, eos, c_begin, c);
 
@@ -1315,12 +1329,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tc::tc_fence_after();
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            tc::umma_bf16(tmem + kHColD, desc_mn(p + kBOffAZ + j * 2048, kBox),
-                          desc_mn(p + kBOffDO + j * 2048, kBox), kIdMNh, j > 0);
+            tc::umma_bf16(tmem + kHColD, desc_mn(p16 + ((kBOffAZ + j * 2048) >> 4), kBox),
+                          desc_mn(p16 + ((kBOffDO + j * 2048) >> 4), kBox), kIdMNh, j > 0);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            tc::umma_bf16(tmem + kHColD, desc_k(p + kBOffKZ + (j >> 2) * 2 * kBox + (j & 3) * 32),
-                          desc_mn(sH + j * 2048, kBox), kIdKNh, 1);
+            tc::umma_bf16(tmem + kHColD, desc_k(p16 + ((kBOffKZ + (j >> 2) * 2 * kBox + (j & 3) * 32) >> 4)),
+                          desc_mn(sH16 + ((j * 2048) >> 4), kBox), kIdKNh, 1);
           tc::umma_commit(mma1);
           ++mma1_commits;
         }
@@ -1361,12 +1375,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc::tc_fence_after();
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::umma_bf16(tmem + kHColH, desc_mn(p + kBOffQg + j * 2048, kBox),
-                        desc_mn(p + kBOffDO + j * 2048, kBox), kIdMNh, 1);
+          tc::umma_bf16(tmem + kHColH, desc_mn(p16 + ((kBOffQg + j * 2048) >> 4), kBox),
+                        desc_mn(p16 + ((kBOffDO + j * 2048) >> 4), kBox), kIdMNh, 1);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::umma_bf16(tmem + kHColH, desc_mn(p + kBOffW + j * 2048, kBox),
-                        desc_mn(sVN + j * 2048, kBox), kIdMNh, 1);
+          tc::umma_bf16(tmem + kHColH, desc_mn(p16 + ((kBOffW + j * 2048) >> 4), kBox),
+                        desc_mn(sVN16 + ((j * 2048) >> 4), kBox), kIdMNh, 1);
         tc::umma_commit(mma2);
         ++mma2_commits;
       }

@@ -179,6 +179,14 @@ __device__ __forceinline__ uint64_t sdesc(const void* p, uint32_t lbo, uint32_t 
   return d;
 }
 constexpr uint32_t kSwizzle128 = 2;
+// The same descriptor with its start-address field zero: OR in a shared-
+// memory address in 16-byte units (addresses stay below 2^18, so the field's
+// 14 bits hold it) -- the layout bits fold to constants and each descriptor
+// of a fixed tile costs one add and one OR.
+__host__ __device__ constexpr uint64_t sdesc_layout(uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)(layout & 7u) << 61);
+}
 
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 accumulation.
 // a_mn / b_mn: operand is MN-major (else K-major).
