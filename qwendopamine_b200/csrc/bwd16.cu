@@ -84,6 +84,10 @@ struct Bwd16Layout {
   static constexpr int tZ = tSlot0 + 2 * tSlotBytes;
   static constexpr int tEnd = tZ + 8192;
   static constexpr int tTr = kE;
+  // the Kd terms X (fp32 [64][LDG], shifted down one row) wait here from the
+  // owner initialisation until the dg scan, clear of the score operands and
+  // of the scan's own tiles
+  static constexpr int tXs = (kScanEnd + 1023) / 1024 * 1024;
   static constexpr int tScan = (tTr + kChunk * LDG * 4 + 1023) / 1024 * 1024;
   static constexpr int W0 = phaseV > kEnd ? (phaseV > kScanEnd ? phaseV : kScanEnd)
                                           : (kEnd > kScanEnd ? kEnd : kScanEnd);
@@ -101,6 +105,8 @@ struct Bwd16Layout {
   static_assert(!TC || D == 128, "the tcgen05 value phase serves K = V = 128");
   static_assert(!TC || (tTr >= kDW + kChunk * LDK * 2), "transpose buffer clear of dW");
   static_assert(!TC || bytes <= 232448, "shared memory per CTA");
+  static_assert(!TC || tXs + kChunk * LDG * 4 <= W, "X tile fits the work region");
+  static_assert(!TC || tXs >= kEnd, "X tile clear of the score operands");
 };
 
 // TMA views of every tile the kernel reads (built per launch on the host).
@@ -234,7 +240,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
     uint64_t* barMma = bars + 3;
     uint32_t* sTmemAddr = reinterpret_cast<uint32_t*>(bars + 4);
     if (tid == 0) {
-      for (int i = 0; i < 4; ++i) tc::mbar_init(&bars[i], 1);
+      for (int i = 0; i < 3; ++i) tc::mbar_init(&bars[i], 1);
+      tc::mbar_init(barMma, 3);
       tc::fence_mbar_init();
     }
     if (warp == 0) {
@@ -301,23 +308,29 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
         tc::fence_async_smem();
         __syncthreads();
       }
-      if (tid == 0) {
+      // lane 0 of warps 0, 1, 2 each issue one product and commit (barMma
+      // counts three arrivals), so no warp carries all twelve issues
+      if (lane == 0 && warp < 3) {
         tc::tc_fence_after();
+        // descriptors: layout constants OR the tile address in 16-byte units
+        const uint32_t w16 = smem_u32(W) >> 4, s16 = w16 + (slot_off(sl, 0) >> 4);
+        const uint64_t dK = tc::sdesc_layout(16, 1024, tc::kSwizzle128);
+        const uint64_t dM = tc::sdesc_layout(8192, 1024, tc::kSwizzle128);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          // descriptors: layout constants OR the tile address in 16-byte units
           const uint32_t acc = (sl > 0 || j > 0) ? 1u : 0u;
-          const uint32_t w16 = smem_u32(W) >> 4, s16 = w16 + (slot_off(sl, 0) >> 4);
-          const uint64_t dK = tc::sdesc_layout(16, 1024, tc::kSwizzle128);
-          const uint64_t dM = tc::sdesc_layout(8192, 1024, tc::kSwizzle128);
-          const uint64_t dH = dK | (w16 + (L::tH >> 4) + 2 * j);
-          tc::umma_bf16(tmem + 0, dH, dK | (s16 + (L::tDO >> 4) + 2 * j), kIdKK, acc);
-          tc::umma_bf16(tmem + 64, dK | (w16 + (L::tDH >> 4) + 2 * j),
-                        dM | (s16 + (L::tVN >> 4) + 128 * j), kIdKM, acc);
-          tc::umma_bf16(tmem + 128, dH, dM | (s16 + (L::tDVN >> 4) + 128 * j), kIdKM, acc);
+          if (warp == 0)
+            tc::umma_bf16(tmem + 0, dK | (w16 + (L::tH >> 4) + 2 * j),
+                          dK | (s16 + (L::tDO >> 4) + 2 * j), kIdKK, acc);
+          else if (warp == 1)
+            tc::umma_bf16(tmem + 64, dK | (w16 + (L::tDH >> 4) + 2 * j),
+                          dM | (s16 + (L::tVN >> 4) + 128 * j), kIdKM, acc);
+          else
+            tc::umma_bf16(tmem + 128, dK | (w16 + (L::tH >> 4) + 2 * j),
+                          dM | (s16 + (L::tDVN >> 4) + 128 * j), kIdKM, acc);
         }
         tc::umma_commit(barMma);
-        ++mma_commits;
+        if (warp == 0) ++mma_commits;
       }
       // Z = v w (same swizzle as v, w): one 16-byte chunk per thread
       {
@@ -712,7 +725,10 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
   block_factors<D, NTH>(sG, LDG, sF);
   // (owner elements come in column pairs: e = 2 hf + t is row 16 wr + gid +
   // 8 hf, column wc DQ + 8 j + 2 tig + t, so each pair is one 32-bit access)
-  float X[NTO][4];
+  // The Kd terms X wait for the dg scan in registers, or (tcgen05 layout,
+  // fewer live registers through the score backward) in shared memory.
+  float X[TC ? 1 : NTO][4];
+  float* sXs = reinterpret_cast<float*>(W + (TC ? L::tXs : 0));
 #pragma unroll
   for (int j = 0; j < NTO; ++j) {
     const int c0 = wc * DQ + 8 * j + 2 * tig;
@@ -734,7 +750,11 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
       setpr(dq[0][j], hf, dqv);
       setpr(dkb[0][j], hf, dkbv);
       setpr(dkn[0][j], hf, kd);
-      setpr(X[j], hf, mul2(kn, kd));
+      if constexpr (TC) {
+        if (r + 1 < kChunk) *reinterpret_cast<float2*>(sXs + (r + 1) * LDG + c0) = mul2(kn, kd);
+      } else {
+        setpr(X[j], hf, mul2(kn, kd));
+      }
       setpr(dG[0][j], hf, fma2(qn, dqv, mul2(bkn, dkbv)));
       const float2 f = exp2_2(make_float2(G2.x - Gb2.x, G2.y - Gb2.y));
       const float2 fe = exp2_2(make_float2(Ge2.x - G2.x, Ge2.y - G2.y));
@@ -881,7 +901,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
 
   // ---- dg = suffix scan of dG + prefix scan of the Kd terms -----------------
   float* sdG = reinterpret_cast<float*>(W + L::kdG);
-  float* sX = reinterpret_cast<float*>(W + L::kX);
+  float* sX = TC ? sXs : reinterpret_cast<float*>(W + L::kX);
   float* sTmp = reinterpret_cast<float*>(W + L::kTmp);
 #pragma unroll
   for (int j = 0; j < NTO; ++j)
@@ -894,9 +914,11 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
         v.y += dgl[c0 + 1] * exp2f(sG[(kChunk - 1) * LDG + c0 + 1]);
       }
       *reinterpret_cast<float2*>(sdG + r * LDG + c0) = v;
-      if (r + 1 < kChunk)
-        *reinterpret_cast<float2*>(sX + (r + 1) * LDG + c0) =
-            make_float2(X[j][2 * hf], X[j][2 * hf + 1]);
+      if constexpr (!TC) {
+        if (r + 1 < kChunk)
+          *reinterpret_cast<float2*>(sX + (r + 1) * LDG + c0) =
+              make_float2(X[j][2 * hf], X[j][2 * hf + 1]);
+      }
     }
   for (int i = tid; i < D; i += NTH) sX[i] = 0.f;
   __syncthreads();
