@@ -289,6 +289,20 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
     T* th = tp(L::tH);
     T* tdh = tp(L::tDH);
     T* tz = tp(L::tZ);
+    // dv / dw of slice sl (staged over its w / v tiles) -> global rows, one
+    // 16-byte chunk per thread and tile; callers are past a barrier
+    auto copy_dvdw = [&](int sl) {
+      const int r = tid >> 3, c = tid & 7;
+      if (r < len) {
+        const unsigned char* sw_ = reinterpret_cast<const unsigned char*>(tp(slot_off(sl, L::tWg)));
+        const unsigned char* sv_ = reinterpret_cast<const unsigned char*>(tp(slot_off(sl, L::tV)));
+        const int off = r * 128 + ((c ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(gdv + r * ldv + 64 * sl + 8 * c) =
+            *reinterpret_cast<const uint4*>(sw_ + off);
+        *reinterpret_cast<uint4*>(gdw + r * ldv + 64 * sl + 8 * c) =
+            *reinterpret_cast<const uint4*>(sv_ + off);
+      }
+    };
     constexpr uint32_t kIdKK = tc::idesc_bf16(128, 64, 0, 0);  // K-major A, K-major B
     constexpr uint32_t kIdKM = tc::idesc_bf16(128, 64, 0, 1);  // K-major A, MN-major B
     for (int sl = 0; sl < 2; ++sl) {
@@ -301,6 +315,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
         drain_tc();
         return;
       }
+      if (sl == 1) copy_dvdw(0);
       if (len < kChunk) {  // rows past a partial chunk hold the next sequence's tokens
         zero_rows(tdo, 128, len, kChunk);
         zero_rows(tv, 128, len, kChunk);
@@ -404,18 +419,21 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
             Mma16<T>::run(accZ[h2], af, bf[0], bf[1]);
           }
         }
+        // dv = dZ w and dw = dZ v replace w and v element by element (each
+        // element is read and written by this thread only; nothing else reads
+        // v, w after Z); they leave as whole rows after the next barrier
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
             const int r = zm + gid + 8 * hf, cl = zn + 8 * h2 + 2 * tig;
-            if (r < len) {
-              const float2 z2 = pr(accZ[h2], hf);
-              const float2 dv2 = mul2(z2, ld2<T>(sw128_elem(tw, r, cl)));
-              const float2 dw2 = mul2(z2, ld2<T>(sw128_elem(tv, r, cl)));
-              *reinterpret_cast<uint32_t*>(gdv + r * ldv + 64 * sl + cl) = pack2<T>(dv2.x, dv2.y);
-              *reinterpret_cast<uint32_t*>(gdw + r * ldv + 64 * sl + cl) = pack2<T>(dw2.x, dw2.y);
-            }
+            const float2 z2 = pr(accZ[h2], hf);
+            T* pw = const_cast<T*>(sw128_elem(tw, r, cl));
+            T* pv = const_cast<T*>(sw128_elem(tv, r, cl));
+            const float2 dv2 = mul2(z2, ld2<T>(pw));
+            const float2 dw2 = mul2(z2, ld2<T>(pv));
+            *reinterpret_cast<uint32_t*>(pw) = pack2<T>(dv2.x, dv2.y);
+            *reinterpret_cast<uint32_t*>(pv) = pack2<T>(dw2.x, dw2.y);
           }
       }
     }
@@ -424,6 +442,7 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
       drain_tc();
       return;
     }
+    copy_dvdw(1);  // (slot 1 stays untouched until the owner initialisation)
     tc::tc_fence_after();
     {
       const int q4 = warp & 3, cg = warp >> 2;  // TMEM lanes 32 q4 .., token columns 16 cg ..
