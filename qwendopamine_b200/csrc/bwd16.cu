@@ -74,7 +74,7 @@ struct Bwd16Layout {
   static constexpr int kdG = 0;
   static constexpr int kX = kdG + kChunk * LDG * 4;
   static constexpr int kTmp = kX + kChunk * LDG * 4;
-  static constexpr int kScanEnd = kTmp + 2 * kThreadsB16 * 4;
+  static constexpr int kScanEnd = kTmp + 4 * kThreadsB16 * 4;
   // tcgen05 value phase (K = V = 128): two 64-column slices of 128-byte-
   // swizzled tiles; h / dh [128][64] single-buffered, dO, VN^T, dVN^T, v, w
   // [64][64] in two slots, Z = v w; after it, a fp32 [64][LDG] transpose
@@ -942,55 +942,64 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
   for (int i = tid; i < D; i += NTH) sX[i] = 0.f;
   __syncthreads();
   // one register-staged pass: suffix sums of dG and prefix sums of the
-  // shifted Kd terms down each column, added and stored straight to dg
+  // shifted Kd terms down each column pair, added and stored straight to dg
   {
-    constexpr int NSEG = NTH / D, RPS = kChunk / NSEG;
-    static_assert(NSEG * D == NTH && RPS * NSEG == kChunk, "scan shape");
-    const int col = tid % D, seg = tid / D;
-    float su[RPS], pr[RPS];
+    constexpr int NC2 = D / 2, NSEG = NTH / NC2, RPS = kChunk / NSEG;
+    static_assert(NSEG * NC2 == NTH && RPS * NSEG == kChunk, "scan shape");
+    const int cp2 = tid % NC2, seg = tid / NC2, col = 2 * cp2;
+    float2 su[RPS], px[RPS];
 #pragma unroll
     for (int i = 0; i < RPS; ++i) {
-      su[i] = sdG[(seg * RPS + i) * LDG + col];
-      pr[i] = sX[(seg * RPS + i) * LDG + col];
+      su[i] = ld2<float>(sdG + (seg * RPS + i) * LDG + col);
+      px[i] = ld2<float>(sX + (seg * RPS + i) * LDG + col);
     }
 #pragma unroll
-    for (int i = 1; i < RPS; ++i) pr[i] += pr[i - 1];
+    for (int i = 1; i < RPS; ++i) px[i] = add2(px[i], px[i - 1]);
 #pragma unroll
-    for (int i = RPS - 2; i >= 0; --i) su[i] += su[i + 1];
-    sTmp[seg * D + col] = pr[RPS - 1];
-    sTmp[NTH + seg * D + col] = su[0];
+    for (int i = RPS - 2; i >= 0; --i) su[i] = add2(su[i], su[i + 1]);
+    float2* tP = reinterpret_cast<float2*>(sTmp);  // [NSEG][NC2] prefix, then suffix totals
+    tP[seg * NC2 + cp2] = px[RPS - 1];
+    tP[NTH + seg * NC2 + cp2] = su[0];
     __syncthreads();
-    float offp = 0.f, offs = 0.f;
+    float2 offp = make_float2(0.f, 0.f), offs = make_float2(0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < NSEG; ++j) {
-      if (j < seg) offp += sTmp[j * D + col];
-      if (j > seg) offs += sTmp[NTH + j * D + col];
+      if (j < seg) offp = add2(offp, tP[j * NC2 + cp2]);
+      if (j > seg) offs = add2(offs, tP[NTH + j * NC2 + cp2]);
     }
     float* gdg = a.dg + offk;
     if (!a.gate.mode) {
 #pragma unroll
       for (int i = 0; i < RPS; ++i) {
         const int r = seg * RPS + i;
-        if (r < len && col < K) gdg[(int64_t)r * ldk + col] = (su[i] + offs) + (pr[i] + offp);
+        if (r < len && col < K)
+          *reinterpret_cast<float2*>(gdg + (int64_t)r * ldk + col) =
+              add2(add2(su[i], offs), add2(px[i], offp));
       }
     } else {
       // gate in kernel: dg of the raw input, plus this chunk's share of
       // dL/d dt_bias (per channel) and dL/dA_log (per head)
       const float* graw = a.g + offk;
-      float sdt = 0.f, sA = 0.f;
+      float sdt[2] = {0.f, 0.f}, sA = 0.f;
 #pragma unroll
       for (int i = 0; i < RPS; ++i) {
         const int r = seg * RPS + i;
         if (r < len && col < K) {
-          float dAc;
-          const float dg = gate_grad(a.gate, graw[(int64_t)r * ldk + col],
-                                     (su[i] + offs) + (pr[i] + offp), h, col, K, &dAc);
-          gdg[(int64_t)r * ldk + col] = dg;
-          sdt += dg;
-          sA += dAc;
+          const float2 dyg = add2(add2(su[i], offs), add2(px[i], offp));
+          float dA0, dA1;
+          const float dg0 = gate_grad(a.gate, graw[(int64_t)r * ldk + col], dyg.x, h, col, K, &dA0);
+          const float dg1 =
+              gate_grad(a.gate, graw[(int64_t)r * ldk + col + 1], dyg.y, h, col + 1, K, &dA1);
+          *reinterpret_cast<float2*>(gdg + (int64_t)r * ldk + col) = make_float2(dg0, dg1);
+          sdt[0] += dg0;
+          sdt[1] += dg1;
+          sA += dA0 + dA1;
         }
       }
-      if (a.gate.ddt_bias && col < K) atomicAdd(a.gate.ddt_bias + h * K + col, sdt);
+      if (a.gate.ddt_bias && col < K) {
+        atomicAdd(a.gate.ddt_bias + h * K + col, sdt[0]);
+        atomicAdd(a.gate.ddt_bias + h * K + col + 1, sdt[1]);
+      }
       sA = warp_sum(sA);
       if (lane == 0) sDApart[warp] = sA;
     }
@@ -1005,13 +1014,18 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
   T* stq = reinterpret_cast<T*>(W);
   T* stk = stq + kChunk * LDK;
   T* stb = stk + kChunk * LDK;
+  // db is final here and goes to its staging tile at once; q and k stay
+  // packed in registers for the l2norm pass
   float pq[2] = {0.f, 0.f}, pk[2] = {0.f, 0.f};
+  uint32_t qpk[NTO][2], kpk[NTO][2];
 #pragma unroll
   for (int j = 0; j < NTO; ++j)
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int r = 16 * wr + gid + 8 * hf, c0 = wc * DQ + 8 * j + 2 * tig;
-      const float2 q2 = ld2<T>(sq + r * LDK + c0), k2 = ld2<T>(sk + r * LDK + c0);
+      qpk[j][hf] = *reinterpret_cast<const uint32_t*>(sq + r * LDK + c0);
+      kpk[j][hf] = *reinterpret_cast<const uint32_t*>(sk + r * LDK + c0);
+      const float2 q2 = unpack2<T>(qpk[j][hf]), k2 = unpack2<T>(kpk[j][hf]);
       const float2 b2 = ld2<T>(sb + r * LDK + c0);
       const float2 dgn = f2(scale * sDiag[r]);
       const float2 qn = mul2(q2, f2(rq[r])), kn = mul2(k2, f2(rk[r]));
@@ -1020,7 +1034,8 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
       const float2 dknv = add2(pr(dkn[0][j], hf), fma2(dkbv, b2, mul2(dgn, qn)));
       setpr(dq[0][j], hf, dqv);
       setpr(dkn[0][j], hf, dknv);
-      setpr(dkb[0][j], hf, mul2(dkbv, kn));  // db
+      const float2 db2 = mul2(dkbv, kn);
+      *reinterpret_cast<uint32_t*>(stb + r * LDK + c0) = pack2<T>(db2.x, db2.y);
       pq[hf] = fmaf(qn.y, dqv.y, fmaf(qn.x, dqv.x, pq[hf]));
       pk[hf] = fmaf(kn.y, dknv.y, fmaf(kn.x, dknv.x, pk[hf]));
     }
@@ -1063,15 +1078,13 @@ __global__ void __launch_bounds__(kThreadsB16, 1)
       if (r >= len || cl >= K) continue;
       float2 oq = pr(dq[0][j], hf), ok = pr(dkn[0][j], hf);
       if (a.l2norm) {
-        const float2 q2 = ld2<T>(sq + r * LDK + cl), k2 = ld2<T>(sk + r * LDK + cl);
+        const float2 q2 = unpack2<T>(qpk[j][hf]), k2 = unpack2<T>(kpk[j][hf]);
         const float2 nq = f2(rq[r]), nk = f2(rk[r]);
         oq = mul2(fma2(neg2(mul2(q2, nq)), f2(dotq[hf]), oq), nq);
         ok = mul2(fma2(neg2(mul2(k2, nk)), f2(dotk[hf]), ok), nk);
       }
       *reinterpret_cast<uint32_t*>(stq + r * LDK + cl) = pack2<T>(oq.x, oq.y);
       *reinterpret_cast<uint32_t*>(stk + r * LDK + cl) = pack2<T>(ok.x, ok.y);
-      *reinterpret_cast<uint32_t*>(stb + r * LDK + cl) =
-          pack2<T>(dkb[0][j][2 * hf], dkb[0][j][2 * hf + 1]);
     }
   __syncthreads();
   store_tile16<T, kChunk, D, NTH>(gdq, ldk, stq, LDK, len, K);
