@@ -151,6 +151,56 @@ __device__ __forceinline__ void col_scan64_sw(unsigned char* s, float* tmp, floa
   __syncthreads();
 }
 
+// The same scan for 128 columns (four 64-row segments of 16 rows: segment I
+// is row block I), whose epilogue also writes the per-block decay factors
+// from the values it stores (so they equal what a later read would give):
+//   Pb[I] = 2^G_16I,  Qe[I] = 2^(G_63 - G_(16I+15)),
+//   F[I(I+1)/2 + J] = 2^min(G_16I - G_(16J+15), 120)  (J <= I),
+// clears *safe when block I's decay range exceeds kSafeLog2Range, and writes
+// gl = 2^G_63 for the first K columns.
+template <int NTH>
+__device__ __forceinline__ void col_scan64_sw_factors(unsigned char* s, float* tmp, float mul,
+                                                      float* sPb, float* sQe, float* sF,
+                                                      int* safe, float* gl, int K) {
+  constexpr int NC = 128, NSEG = NTH / NC, RPS = kChunk / NSEG;
+  static_assert(NSEG == 4 && RPS == 16, "one 16-row block per segment");
+  const int col = threadIdx.x % NC, I = threadIdx.x / NC;
+  float x[RPS];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i) x[i] = *reinterpret_cast<const float*>(s + swz<4>(I * RPS + i, col));
+#pragma unroll
+  for (int i = 1; i < RPS; ++i) x[i] += x[i - 1];
+  tmp[I * NC + col] = x[RPS - 1];
+  __syncthreads();
+  float off[NSEG];  // off[j]: sum of the segment totals before segment j
+  off[0] = 0.f;
+#pragma unroll
+  for (int j = 1; j < NSEG; ++j) off[j] = off[j - 1] + tmp[(j - 1) * NC + col];
+  float o = 0.f;
+#pragma unroll
+  for (int j = 0; j < NSEG; ++j)
+    if (j == I) o = off[j];
+#pragma unroll
+  for (int i = 0; i < RPS; ++i)
+    *reinterpret_cast<float*>(s + swz<4>(I * RPS + i, col)) = (x[i] + o) * mul;
+  float glast[NSEG];  // G at each block's last row, as stored
+#pragma unroll
+  for (int j = 0; j < NSEG; ++j) glast[j] = (tmp[j * NC + col] + off[j]) * mul;
+  const float gfirst = (x[0] + o) * mul, GL = glast[NSEG - 1];
+  float gl_I = glast[0];
+#pragma unroll
+  for (int j = 1; j < NSEG; ++j)
+    if (j == I) gl_I = glast[j];
+  sPb[I * NC + col] = fast_exp2(gfirst);
+  sQe[I * NC + col] = fast_exp2(GL - gl_I);
+#pragma unroll
+  for (int J = 0; J < NSEG; ++J)
+    if (J <= I) sF[(I * (I + 1) / 2 + J) * NC + col] = fast_exp2(fminf(gfirst - glast[J], 120.f));
+  if (!(gfirst - gl_I <= kSafeLog2Range)) *safe = 0;
+  if (I == NSEG - 1 && col < K) gl[col] = exp2f(GL);
+  __syncthreads();
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreadsF16, 1)
     k_fwd_intra16(FwdIntraArgs a, const __grid_constant__ CUtensorMap mQ,
@@ -277,8 +327,14 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
       }
       __syncthreads();
     }
-    // chunk-local log2 cumulative decay
-    col_scan64_sw<D, NTH>(sG, reinterpret_cast<float*>(R), kLog2e);
+    // chunk-local log2 cumulative decay (for 128 columns with the per-block
+    // decay factors, diagonal-block safety and gl in the same pass)
+    float* gGl = reinterpret_cast<float*>(a.saved + a.L.gl) + ch * K;
+    if constexpr (D == 128)
+      col_scan64_sw_factors<NTH>(sG, reinterpret_cast<float*>(R), kLog2e, sPb, sQe, sF, sFlag,
+                                 gGl, K);
+    else
+      col_scan64_sw<D, NTH>(sG, reinterpret_cast<float*>(R), kLog2e);
     // row norms: warp w owns rows 4w .. 4w+3
     {
       constexpr int EPL = D / 32;
@@ -315,8 +371,8 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
         (idx < 4 ? rq : rk)[r] = a.l2norm ? rsqrtf(tot + kNormEps) : 1.f;
       }
     }
-    // per-block decay factors, diagonal-block safety, gl out
-    float* gGl = reinterpret_cast<float*>(a.saved + a.L.gl) + ch * K;
+    // per-block decay factors, diagonal-block safety, gl out (64 columns)
+    if constexpr (D != 128) {
     for (int i = tid; i < 18 * D; i += NTH) {
       const int p = i / D, cc = i - p * D;
       const float GL = G_(kChunk - 1, cc);
@@ -339,6 +395,7 @@ __global__ void __launch_bounds__(kThreadsF16, 1)
       if (!(rng <= kSafeLog2Range)) sFlag[0] = 0;
     }
     for (int i = tid; i < K; i += NTH) gGl[i] = exp2f(G_(kChunk - 1, i));
+    }
     if (!tc::mbar_wait(barB, phase)) fault = 1;  // v, w
     if (__syncthreads_or(fault)) break;
     if (len < kChunk) {
