@@ -107,11 +107,13 @@ NATIVE_PHASES = ("fwd_intra", "fwd_prescan", "fwd_merge", "fwd_state", "bwd_pres
 STEP_FLOPS = 20 * C * K + 14 * C * V + 22 * K * V + 4 * C * C
 STEP_MIN_BYTES = 6900
 # DRAM traffic (read + write) of the dominant kernel, k_bwd_intra16, per
-# token-head, from one ncu --set full capture at config-1 shapes, batch 2
-# (701.3 MB over 131,072 token-heads).  The kernel runs one CTA per (chunk,
-# head) whatever the sequence layout, so its traffic grows with token-heads
-# and scales to a config-1 or config-4 launch.  Summary under profiles/.
-NCU_TRAFFIC_PER_TOKEN_HEAD = 5309.6
+# token-head, from ncu --set full captures: a config-4-shaped slice (B=1,
+# T=32,768, H=32: 5.743 GB over 1,048,576 token-heads) and config-1 shapes at
+# batch 2 (689.5 MB over 131,072 token-heads).  The kernel runs one CTA per
+# (chunk, head) whatever the sequence layout, so its traffic grows with
+# token-heads and scales to a full config-4 or config-1 launch.  Summaries
+# under profiles/.
+NCU_TRAFFIC_PER_TOKEN_HEAD = {"config4": 5476.6, "config1": 5260.8}
 
 
 def peaks():
@@ -310,13 +312,14 @@ def phase_summary(records, steps):
     return {n: {"ms": round(t / steps, 4), "launches": cnt[n]} for n, t in tot.items()}
 
 
-def roofline_of(phases, token_heads, hbm, peak_kind):
-    """Live roofline of the slowest phase with known algorithmic bytes."""
+def roofline_of(phases, token_heads, hbm, peak_kind, shape):
+    """Live roofline of the slowest phase with known algorithmic bytes
+    (``shape``: "config4" or "config1", the ncu capture its traffic uses)."""
     known = [p for p in PHASE_BYTES if p in phases]
     dom = max(known, key=lambda p: phases[p]["ms"])
     ach = PHASE_BYTES[dom] * token_heads / (phases[dom]["ms"] / 1e3) / 1e9
-    traffic = (round(NCU_TRAFFIC_PER_TOKEN_HEAD * token_heads)
-               if NCU_TRAFFIC_PER_TOKEN_HEAD and dom == "bwd_intra" else None)
+    per = NCU_TRAFFIC_PER_TOKEN_HEAD.get(shape)
+    traffic = round(per * token_heads) if per and dom == "bwd_intra" else None
     for p in known:
         t_s = phases[p]["ms"] / 1e3
         phases[p]["GBps"] = round(PHASE_BYTES[p] * token_heads / t_s / 1e9, 1)
@@ -632,7 +635,7 @@ def run_config1(args, world, rank, local):
     del host
     th = B1 * T1 * H1
     hbm, tflops_peak, kind = peaks()
-    roof = roofline_of(phase_ms, th, hbm, kind)
+    roof = roofline_of(phase_ms, th, hbm, kind, "config1")
     return {
         "workload": "config1: chunk_gdn2 forward+backward, B=8 T=4096 H=16 K=V=128 bf16 per "
                     f"rank, batch-sharded x{world} (weak, no data-path collective); the four "
@@ -1141,7 +1144,7 @@ def run_b200(args, world, rank, local):
         return
     hbm, tflops_peak, peak_kind = peaks()
     phases = c4["phases"]
-    roof = roofline_of(phases, c4["token_heads"], hbm, peak_kind)
+    roof = roofline_of(phases, c4["token_heads"], hbm, peak_kind, "config4")
     ms = c4["ms"]
     cpu = None
     if world == 1:
