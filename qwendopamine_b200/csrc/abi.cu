@@ -10,6 +10,7 @@
 #include "../../include/gdn2_b200.h"
 
 #include "chunk_args.cuh"
+#include "mma16.cuh"
 
 namespace gdn2 {
 template <typename T, int D> cudaError_t launch_fwd_intra(const FwdIntraArgs&, cudaStream_t);
@@ -361,6 +362,90 @@ __global__ void __launch_bounds__(kThreads) k_cp_merge(int N, int H, int K, int 
   }
 }
 
+// The same fold for K <= 128 (a multiple of 16, V a multiple of 4): the whole
+// M of the next folded rank and its state slice arrive by 16-byte cp.async
+// while the current fold multiplies, so each fold costs its products and not
+// a round trip to memory.  M stays row-major in both directions (the
+// backward reads it transposed); the row strides keep both fragment reads
+// free of bank conflicts.
+constexpr int kMerge2MaxK = 128;
+size_t merge2_smem_bytes() {
+  return (size_t)(4 * kMerge2MaxK * kMergeLDX + 2 * kMerge2MaxK * 136) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(kThreads) k_cp_merge2(int N, int H, int K, int V,
+                                                       const float* hm_all, const float* dhm_all,
+                                                       int rank, int world, int forward,
+                                                       const float* init, float* out) {
+  extern __shared__ __align__(16) float smem[];
+  const int ldm = forward ? 132 : 136;
+  float* x = smem;                                // [128][36] running tile
+  float* y = x + kMerge2MaxK * kMergeLDX;         // its successor
+  float* hb = y + kMerge2MaxK * kMergeLDX;        // [2][128][36] h_e_j / dh_j slices
+  float* Mb = hb + 2 * kMerge2MaxK * kMergeLDX;   // [2][128][136] M_j
+  const int nh = blockIdx.y, v0 = blockIdx.x * 32;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int VK = V + K;
+  const int64_t per_rank_hm = (int64_t)N * H * K * VK;
+  const int64_t per_rank_dh = (int64_t)N * H * K * V;
+  const int nsteps = forward ? rank : world - 1 - rank;
+  auto issue = [&](int step, int buf) {
+    const int j = forward ? step : world - 1 - step;
+    const float* hm = hm_all + j * per_rank_hm + (int64_t)nh * K * VK;
+    float* sM = Mb + buf * kMerge2MaxK * 136;
+    const int cpr = K / 4;  // 16-byte chunks per row of M
+    for (int idx = tid; idx < K * cpr; idx += kThreads) {
+      const int r = idx / cpr, c4 = idx - r * cpr;
+      cp_async16(sM + r * ldm + 4 * c4, hm + (int64_t)r * VK + V + 4 * c4, true);
+    }
+    float* sh = hb + buf * kMerge2MaxK * kMergeLDX;
+    for (int idx = tid; idx < K * 8; idx += kThreads) {
+      const int r = idx >> 3, col = v0 + 4 * (idx & 7);
+      const float* src = forward ? hm + (int64_t)r * VK + col
+                                 : dhm_all + j * per_rank_dh + ((int64_t)nh * K + r) * V + col;
+      cp_async16(sh + r * kMergeLDX + 4 * (idx & 7), col < V ? src : hm, col < V);
+    }
+    cp_async_commit();
+  };
+  for (int idx = tid; idx < K * 32; idx += kThreads) {
+    const int r = idx >> 5, c = idx & 31, col = v0 + c;
+    x[r * kMergeLDX + c] = (init && col < V) ? init[((int64_t)nh * K + r) * V + col] : 0.f;
+  }
+  if (nsteps > 0) issue(0, 0);
+  for (int step = 0; step < nsteps; ++step) {
+    const int buf = step & 1;
+    if (step + 1 < nsteps) {
+      issue(step + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // M_j, its slice and the running tile are in
+    const float* sM = Mb + buf * kMerge2MaxK * 136;
+    const float* sh = hb + buf * kMerge2MaxK * kMergeLDX;
+    if (16 * warp < K) {  // warp w: output rows 16 w .. 16 w + 15, all 32 columns
+      float acc[1][4][4];
+      acc_zero(acc);
+      if (forward)
+        warp_mma<1, 4, 3>(acc, sM + 16 * warp * ldm, ldm, 1, x, kMergeLDX, 1, K);
+      else
+        warp_mma<1, 4, 3>(acc, sM + 16 * warp, 1, ldm, x, kMergeLDX, 1, K);
+      acc_foreach(acc, [&](int rr, int cc, float val) {
+        const int r = 16 * warp + rr;
+        y[r * kMergeLDX + cc] = val + sh[r * kMergeLDX + cc];
+      });
+    }
+    __syncthreads();  // y complete; this step's buffers may be refilled
+    float* t = x;
+    x = y;
+    y = t;
+  }
+  for (int idx = tid; idx < K * 32; idx += kThreads) {
+    const int r = idx >> 5, c = idx & 31, col = v0 + c;
+    if (col < V) out[((int64_t)nh * K + r) * V + col] = x[r * kMergeLDX + c];
+  }
+}
+
 }  // namespace
 
 namespace gdn2 {
@@ -680,6 +765,17 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all, const float*
   const int N = p->seqs.n_seqs;
   if (N == 0) return GDN2_OK;
   dim3 grid((p->V + 31) / 32, N * p->H);
+  const uintptr_t al = reinterpret_cast<uintptr_t>(hm_all) | reinterpret_cast<uintptr_t>(dhm_all);
+  if (p->K <= kMerge2MaxK && p->K % 16 == 0 && p->V % 4 == 0 && (al & 15) == 0) {
+    const size_t smem = merge2_smem_bytes();
+    cudaError_t e = cudaFuncSetAttribute(k_cp_merge2, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "gdn2_cp_merge");
+    k_cp_merge2<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
+        N, p->H, p->K, p->V, hm_all, dhm_all, rank, world, forward, init, state_out);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_merge");
+  }
   const size_t smem = merge_smem_bytes(p->K);
   cudaError_t e = cudaFuncSetAttribute(k_cp_merge, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);

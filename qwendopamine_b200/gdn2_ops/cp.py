@@ -83,19 +83,29 @@ def _sub_spans(B, T, H, dtype):
     return 2 if (B * H * 2 * 2 <= 148 and nch >= 64) else 1
 
 
-# The span-map folds run in float64 torch on the device: a few batched
-# K x K by K x (V+K) products per step, exact regardless of TF32 settings.
+# The span-map folds run as fp32 torch products on the device (a few batched
+# K x K by K x (V+K) products per step) with TF32 switched off for their
+# duration, so they keep fp32 accuracy whatever the caller's matmul setting.
+class _NoTF32:
+    def __enter__(self):
+        self.prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self.prev
+
+
 def _compose_maps(hm_sub):
     """[h_e | M] of consecutive sub-spans ([B, S, H, K, V+K]) -> the map of the
     whole span: x = [0 | I];  x = M_s x + [h_e_s | 0]  for s = 0 .. S-1."""
     B, S, H, K, VK = hm_sub.shape
     V = VK - K
-    m = hm_sub.double()
-    x = m[:, 0].clone()
-    for j in range(1, S):
-        x = torch.matmul(m[:, j, ..., V:], x)
-        x[..., :V] += m[:, j, ..., :V]
-    return x.float().contiguous()
+    x = hm_sub[:, 0].clone()
+    with _NoTF32():
+        for j in range(1, S):
+            x = torch.matmul(hm_sub[:, j, ..., V:], x)
+            x[..., :V] += hm_sub[:, j, ..., :V]
+    return x.contiguous()
 
 
 def _unfold_states(h0, hm_sub):
@@ -103,11 +113,13 @@ def _unfold_states(h0, hm_sub):
     s_j = M_{j-1} s_{j-1} + h_e_{j-1}.  Returns [B*S, H, K, V]."""
     B, S, H, K, VK = hm_sub.shape
     V = VK - K
-    m = hm_sub.double()
-    out = [h0.double()]
-    for j in range(1, S):
-        out.append(torch.matmul(m[:, j - 1, ..., V:], out[-1]) + m[:, j - 1, ..., :V])
-    return torch.stack(out, 1).float().reshape(B * S, H, K, V).contiguous()
+    out = [h0]
+    with _NoTF32():
+        for j in range(1, S):
+            out.append(torch.baddbmm(hm_sub[:, j - 1, ..., :V].reshape(B * H, K, V),
+                                     hm_sub[:, j - 1, ..., V:].reshape(B * H, K, K),
+                                     out[-1].reshape(B * H, K, V)).view(B, H, K, V))
+    return torch.stack(out, 1).reshape(B * S, H, K, V).contiguous()
 
 
 def _compose_grads(dhm_sub, hm_sub, dht):
@@ -115,24 +127,27 @@ def _compose_grads(dhm_sub, hm_sub, dht):
     [B, S, H, K, V], zero end gradient each) and of the span's end-state
     gradient dht (or None): x = dht;  x = M_s^T x + dhm_s  for s = S-1 .. 0."""
     B, S, H, K, V = dhm_sub.shape
-    m = hm_sub.double()
-    x = dht.double() if dht is not None else torch.zeros_like(dhm_sub[:, 0], dtype=torch.float64)
-    for j in range(S - 1, -1, -1):
-        x = torch.matmul(m[:, j, ..., V:].transpose(-1, -2), x) + dhm_sub[:, j].double()
-    return x.float().contiguous()
+    x = dht if dht is not None else torch.zeros_like(dhm_sub[:, 0])
+    with _NoTF32():
+        for j in range(S - 1, -1, -1):
+            x = torch.baddbmm(dhm_sub[:, j].reshape(B * H, K, V),
+                              hm_sub[:, j, ..., V:].reshape(B * H, K, K).transpose(-1, -2),
+                              x.reshape(B * H, K, V)).view(B, H, K, V)
+    return x.contiguous()
 
 
 def _unfold_grads(dht_span, dhm_sub, hm_sub):
     """End-state gradient of every sub-span from the span's: g_{S-1} =
     dht_span,  g_j = M_{j+1}^T g_{j+1} + dhm_{j+1}.  Returns [B*S, H, K, V]."""
     B, S, H, K, V = dhm_sub.shape
-    m = hm_sub.double()
-    out = [dht_span.double()]
-    for j in range(S - 2, -1, -1):
-        out.append(torch.matmul(m[:, j + 1, ..., V:].transpose(-1, -2), out[-1]) +
-                   dhm_sub[:, j + 1].double())
+    out = [dht_span]
+    with _NoTF32():
+        for j in range(S - 2, -1, -1):
+            out.append(torch.baddbmm(dhm_sub[:, j + 1].reshape(B * H, K, V),
+                                     hm_sub[:, j + 1, ..., V:].reshape(B * H, K, K).transpose(-1, -2),
+                                     out[-1].reshape(B * H, K, V)).view(B, H, K, V))
     out.reverse()
-    return torch.stack(out, 1).float().reshape(B * S, H, K, V).contiguous()
+    return torch.stack(out, 1).reshape(B * S, H, K, V).contiguous()
 
 
 class CPChunkGDN2Function(torch.autograd.Function):

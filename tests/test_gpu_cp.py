@@ -154,3 +154,69 @@ def test_cp_autograd_function_single_rank_equals_chunk(cuda_device):
     ((o2 * do).sum() + (h2 * dh).sum()).backward()
     for n in (*NAMES, "h0"):
         assert rel(l1[n].grad, l2[n].grad) < 1e-6, n
+
+
+def test_sequence_parallel_subspans_emulated_in_one_process(cuda_device):
+    """Four ranks of chunk_gdn2_cp in one process, bf16, each rank's span of
+    64 chunks cut into two sub-spans joined by the fp32 span-map folds, a
+    slow decay so every span's state reaches the next ones, a loss on the
+    outputs and on the last rank's end state: outputs, end state and all six
+    gradients against chunk_gdn2 on the whole sequence.  The all-gathers are
+    emulated in two passes (a span's map and its span-start gradient depend
+    on that span alone, so a first pass records them)."""
+    from qwendopamine_b200 import chunk_gdn2
+    from qwendopamine_b200.gdn2_ops.cp import CPChunkGDN2Function
+
+    P, B, T, H, K, V = 4, 1, 4 * 4096, 2, 128, 128
+    Tr = T // P
+    d = make_inputs(B, T, H, K, V, seed=21, decay=-0.0005, dtype=torch.bfloat16, h0=False)
+    d["b"] = (d["b"] * 0.01).bfloat16().float()  # weak erasure: the state outlives a span
+    x = to_dev(d, cuda_device, torch.bfloat16)
+    gen = torch.Generator(device=cuda_device).manual_seed(5)
+    do = torch.randn(B, T, H, V, device=cuda_device, generator=gen).bfloat16()
+    dht = torch.randn(B, H, K, V, device=cuda_device, generator=gen)
+
+    # whole sequence on one GPU
+    full = {n: x[n].clone().requires_grad_() for n in NAMES}
+    o_ref, ht_ref = chunk_gdn2(*(full[n] for n in NAMES), output_final_state=True,
+                               use_qk_l2norm_in_kernel=True)
+    ((o_ref.float() * do.float()).sum() + (ht_ref * dht).sum()).backward()
+
+    # the spans are coupled: span 1 from a zero state differs from the truth
+    with torch.no_grad():
+        o_alone, _ = chunk_gdn2(*(x[n][:, Tr:2 * Tr] for n in NAMES), use_qk_l2norm_in_kernel=True)
+    assert rel(o_alone, o_ref[:, Tr:2 * Tr]) > 5e-2
+
+    rec = {"f": [None] * P, "b": [None] * P}
+
+    def make_gather(r):
+        def gather(t):
+            key = "f" if t.shape[-1] == V + K else "b"
+            rec[key][r] = t.detach().clone()
+            return torch.stack([z if z is not None else torch.zeros_like(t) for z in rec[key]])
+        return gather
+
+    def run():
+        outs, hts, leaves = [], [], []
+        for r in range(P):
+            loc = {n: x[n][:, r * Tr:(r + 1) * Tr].detach().clone().requires_grad_() for n in NAMES}
+            o, ht = CPChunkGDN2Function.apply(*(loc[n] for n in NAMES), None, K ** -0.5, True, r,
+                                              P, make_gather(r))
+            outs.append(o)
+            hts.append(ht)
+            leaves.append(loc)
+        grads = [None] * P
+        for r in reversed(range(P)):  # later ranks' span-start gradients first
+            loss = (outs[r].float() * do[:, r * Tr:(r + 1) * Tr].float()).sum()
+            if r == P - 1:
+                loss = loss + (hts[r] * dht).sum()
+            grads[r] = torch.autograd.grad(loss, [leaves[r][n] for n in NAMES])
+        return outs, hts, grads
+
+    run()  # records every span's map and span-start gradient
+    outs, hts, grads = run()
+    torch.cuda.synchronize(cuda_device)
+    assert rel(torch.cat(outs, 1), o_ref) < 2e-2
+    assert rel(hts[-1], ht_ref) < 2e-2
+    for i, n in enumerate(NAMES):
+        assert rel(torch.cat([g[i] for g in grads], 1), full[n].grad) < 2e-2, n
