@@ -73,13 +73,18 @@ def _problem(H, K, V, dtype, l2norm, scale, tables):
 def _sub_spans(B, T, H, dtype):
     """Sub-spans per sequence inside a rank's span.  The pre-scans and state
     passes walk their span's chunks one after another with one CTA (or a few
-    column slices) per sequence-head; cutting the span in two halves every
-    such chain and doubles the CTAs, which pays while the forward pre-scan
-    ([h | M], two 128-column slices per sequence-head) still fits one wave
-    and each half keeps enough chunks."""
+    column slices) per sequence-head; cutting the span into S pieces cuts
+    every such chain S-fold and multiplies the CTAs by S.  Four pieces while
+    the full-width tensor-core state passes (one CTA per sequence-head) still
+    fit one wave and each piece keeps 32 chunks; else two while the forward
+    pre-scan ([h | M], two 128-column slices per sequence-head) fits one
+    wave; else one.  (The forward pre-scan at four pieces runs two waves of
+    half-length chains: the same time as one wave at two.)"""
     if dtype != torch.bfloat16:
         return 1
     nch = (T + N.CHUNK - 1) // N.CHUNK
+    if B * H * 4 <= 148 and nch >= 4 * 32:
+        return 4
     return 2 if (B * H * 2 * 2 <= 148 and nch >= 64) else 1
 
 

@@ -158,18 +158,19 @@ def test_cp_autograd_function_single_rank_equals_chunk(cuda_device):
 
 def test_sequence_parallel_subspans_emulated_in_one_process(cuda_device):
     """Four ranks of chunk_gdn2_cp in one process, bf16, each rank's span of
-    64 chunks cut into two sub-spans joined by the fp32 span-map folds, a
+    128 chunks cut into four sub-spans joined by the fp32 span-map folds, a
     slow decay so every span's state reaches the next ones, a loss on the
     outputs and on the last rank's end state: outputs, end state and all six
     gradients against chunk_gdn2 on the whole sequence.  The all-gathers are
     emulated in two passes (a span's map and its span-start gradient depend
     on that span alone, so a first pass records them)."""
     from qwendopamine_b200 import chunk_gdn2
-    from qwendopamine_b200.gdn2_ops.cp import CPChunkGDN2Function
+    from qwendopamine_b200.gdn2_ops.cp import CPChunkGDN2Function, _sub_spans
 
-    P, B, T, H, K, V = 4, 1, 4 * 4096, 2, 128, 128
+    P, B, T, H, K, V = 4, 1, 4 * 8192, 2, 128, 128
     Tr = T // P
-    d = make_inputs(B, T, H, K, V, seed=21, decay=-0.0005, dtype=torch.bfloat16, h0=False)
+    assert _sub_spans(B, Tr, H, torch.bfloat16) == 4
+    d = make_inputs(B, T, H, K, V, seed=21, decay=-0.00025, dtype=torch.bfloat16, h0=False)
     d["b"] = (d["b"] * 0.01).bfloat16().float()  # weak erasure: the state outlives a span
     x = to_dev(d, cuda_device, torch.bfloat16)
     gen = torch.Generator(device=cuda_device).manual_seed(5)
