@@ -253,6 +253,17 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all,
                   const float* dhm_all, int32_t rank, int32_t world,
                   int32_t forward, const float* init, float* state_out,
                   void* stream);
+/* The same folds over the n_sub consecutive sub-spans of one span, keeping
+ * every intermediate (the chunk_kda.py:509-697 merge run as a scan): with
+ * hm_sub [n_sub, N, H, K, V+K] and dhm_sub [n_sub, N, H, K, V] (sub-span
+ * major) it writes states [n_sub, N, H, K, V]:
+ *   forward=1:  states[0] = init;  states[s+1] = M_s states[s] + h_e_s
+ *   forward=0:  states[n_sub-1] = init;  states[s] = M_{s+1}^T states[s+1] + dhm_{s+1}
+ * i.e. the start state (end-state gradient) of every sub-span.  K <= 128 (a
+ * multiple of 16), V a multiple of 4; GDN2_ERR_UNSUPPORTED otherwise. */
+int gdn2_cp_unfold(const gdn2_chunk_problem* p, const float* hm_sub,
+                   const float* dhm_sub, int32_t n_sub, int32_t forward,
+                   const float* init, float* states, void* stream);
 
 /* ---- block prologue / epilogue -------------------------------------------
  * Causal depthwise convolution with optional SiLU, one per q / k / v

@@ -41,6 +41,7 @@ EXPORTS = (
     "gdn2_cp_fwd_prescan",
     "gdn2_cp_bwd_prescan",
     "gdn2_cp_merge",
+    "gdn2_cp_unfold",
     "gdn2_conv_fwd",
     "gdn2_conv_bwd_workspace_bytes",
     "gdn2_conv_bwd",
@@ -170,6 +171,7 @@ def _declare(lib):
         "gdn2_cp_fwd_prescan": ([cp, v, c_size_t, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_cp_bwd_prescan": ([cp, v, c_size_t, v, v, v, v, c_size_t, v], ctypes.c_int),
         "gdn2_cp_merge": ([cp, v, v, c_int32, c_int32, c_int32, v, v, v], ctypes.c_int),
+        "gdn2_cp_unfold": ([cp, v, v, c_int32, c_int32, v, v, v], ctypes.c_int),
         "gdn2_fault_status": ([v, c_int32], ctypes.c_int),
         "gdn2_test_fwd_state_wait_timeout": ([cp, v, v, c_size_t, c_int32, ctypes.c_uint64, v],
                                              ctypes.c_int),

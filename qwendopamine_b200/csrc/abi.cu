@@ -373,10 +373,16 @@ size_t merge2_smem_bytes() {
   return (size_t)(4 * kMerge2MaxK * kMergeLDX + 2 * kMerge2MaxK * 136) * sizeof(float);
 }
 
+// With `all` set the kernel also writes every intermediate tile: all[0] is
+// the initial tile and all[s + 1] the tile after fold s (forward), or
+// all[world - 1] the initial tile and all[world - 2 - s] the tile after fold s
+// (backward) -- the start states (end-state gradients) of consecutive
+// sub-spans.  `out` may then be null.
 __global__ void __launch_bounds__(kThreads) k_cp_merge2(int N, int H, int K, int V,
                                                        const float* hm_all, const float* dhm_all,
                                                        int rank, int world, int forward,
-                                                       const float* init, float* out) {
+                                                       const float* init, float* out,
+                                                       float* all) {
   extern __shared__ __align__(16) float smem[];
   const int ldm = forward ? 132 : 136;
   float* x = smem;                                // [128][36] running tile
@@ -407,10 +413,18 @@ __global__ void __launch_bounds__(kThreads) k_cp_merge2(int N, int H, int K, int
     }
     cp_async_commit();
   };
+  // one intermediate tile of `all` (index i) from the running tile
+  auto write_all = [&](const float* t, int i) {
+    for (int idx = tid; idx < K * 32; idx += kThreads) {
+      const int r = idx >> 5, c = idx & 31, col = v0 + c;
+      if (col < V) all[i * per_rank_dh + ((int64_t)nh * K + r) * V + col] = t[r * kMergeLDX + c];
+    }
+  };
   for (int idx = tid; idx < K * 32; idx += kThreads) {
     const int r = idx >> 5, c = idx & 31, col = v0 + c;
     x[r * kMergeLDX + c] = (init && col < V) ? init[((int64_t)nh * K + r) * V + col] : 0.f;
   }
+  if (all) write_all(x, forward ? 0 : world - 1);  // (each thread its own elements)
   if (nsteps > 0) issue(0, 0);
   for (int step = 0; step < nsteps; ++step) {
     const int buf = step & 1;
@@ -436,14 +450,16 @@ __global__ void __launch_bounds__(kThreads) k_cp_merge2(int N, int H, int K, int
       });
     }
     __syncthreads();  // y complete; this step's buffers may be refilled
+    if (all) write_all(y, forward ? step + 1 : world - 2 - step);
     float* t = x;
     x = y;
     y = t;
   }
-  for (int idx = tid; idx < K * 32; idx += kThreads) {
-    const int r = idx >> 5, c = idx & 31, col = v0 + c;
-    if (col < V) out[((int64_t)nh * K + r) * V + col] = x[r * kMergeLDX + c];
-  }
+  if (out)
+    for (int idx = tid; idx < K * 32; idx += kThreads) {
+      const int r = idx >> 5, c = idx & 31, col = v0 + c;
+      if (col < V) out[((int64_t)nh * K + r) * V + col] = x[r * kMergeLDX + c];
+    }
 }
 
 }  // namespace
@@ -772,7 +788,7 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all, const float*
                                          (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "gdn2_cp_merge");
     k_cp_merge2<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
-        N, p->H, p->K, p->V, hm_all, dhm_all, rank, world, forward, init, state_out);
+        N, p->H, p->K, p->V, hm_all, dhm_all, rank, world, forward, init, state_out, nullptr);
     e = cudaGetLastError();
     return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_merge");
   }
@@ -784,6 +800,33 @@ int gdn2_cp_merge(const gdn2_chunk_problem* p, const float* hm_all, const float*
                                                              rank, world, forward, init, state_out);
   e = cudaGetLastError();
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_merge");
+}
+
+int gdn2_cp_unfold(const gdn2_chunk_problem* p, const float* hm_sub, const float* dhm_sub,
+                   int32_t n_sub, int32_t forward, const float* init, float* states,
+                   void* stream) {
+  int rc = check_problem(p, "gdn2_cp_unfold");
+  if (rc) return rc;
+  if (n_sub <= 0) return fail(GDN2_ERR_INVALID, "gdn2_cp_unfold: %d sub-spans", n_sub);
+  if (!hm_sub || !states || (!forward && !dhm_sub))
+    return fail(GDN2_ERR_INVALID, "gdn2_cp_unfold: null pointer");
+  const uintptr_t al = reinterpret_cast<uintptr_t>(hm_sub) | reinterpret_cast<uintptr_t>(dhm_sub);
+  if (p->K > kMerge2MaxK || p->K % 16 != 0 || p->V % 4 != 0 || (al & 15) != 0)
+    return fail(GDN2_ERR_UNSUPPORTED,
+                "gdn2_cp_unfold: needs K <= 128 (a multiple of 16), V a multiple of 4 and "
+                "16-byte aligned maps");
+  const int N = p->seqs.n_seqs;
+  if (N == 0) return GDN2_OK;
+  dim3 grid((p->V + 31) / 32, N * p->H);
+  const size_t smem = merge2_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(k_cp_merge2, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn2_cp_unfold");
+  k_cp_merge2<<<grid, kThreads, smem, (cudaStream_t)stream>>>(
+      N, p->H, p->K, p->V, hm_sub, dhm_sub, forward ? n_sub - 1 : 0, n_sub, forward, init,
+      nullptr, states);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_cp_unfold");
 }
 
 int gdn2_test_fwd_state_wait_timeout(const gdn2_chunk_problem* p, void* o, void* saved,

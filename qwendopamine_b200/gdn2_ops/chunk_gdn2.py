@@ -325,8 +325,20 @@ def chunk_gdn2(
             if ht is not None and transpose_state_layout:
                 ht = ht.transpose(-1, -2)
             return o, ht, hs
-        o, ht = ChunkGDN2Function.apply(q, k, v, g, b, w, scale, h0, output_final_state,
-                                        use_qk_l2norm_in_kernel, tables, g_dtype, A32, dt32, lb)
+        from .cp import CPChunkGDN2Function, sub_spans_single
+
+        if (cu_seqlens is None and A32 is None and
+                sub_spans_single(B, T, H, K, v.shape[-1], dt) > 1):
+            # few sequence-heads over long sequences: the sub-span pre-scan,
+            # the unfold of the start states and S-fold shorter state passes
+            o, ht = CPChunkGDN2Function.apply(q, k, v, g, b, w, h0, scale,
+                                              use_qk_l2norm_in_kernel, 0, 1, None)
+            if not output_final_state:
+                ht = None
+        else:
+            o, ht = ChunkGDN2Function.apply(q, k, v, g, b, w, scale, h0, output_final_state,
+                                            use_qk_l2norm_in_kernel, tables, g_dtype, A32, dt32,
+                                            lb)
     if ht is not None and transpose_state_layout:
         ht = ht.transpose(-1, -2)
     return o, ht

@@ -88,6 +88,28 @@ def _sub_spans(B, T, H, dtype):
     return 2 if (B * H * 2 * 2 <= 148 and nch >= 64) else 1
 
 
+def sub_spans_single(B, T, H, K, V, dtype):
+    """Sub-spans for whole sequences on one GPU (world 1) when few
+    sequence-heads would leave the state passes' chains on a handful of SMs:
+    the pre-scan, the unfold of the start states and the state passes on S
+    pieces replace one walk over every chunk.  The largest power of two with
+    B*H*S full-width state-pass CTAs in one wave and 64 chunks per piece,
+    used from S = 8 on (below that the pre-scan costs what it saves); 1 means
+    the plain chunk path."""
+    if dtype != torch.bfloat16 or K != 128 or V != 128:
+        return 1
+    nch = (T + N.CHUNK - 1) // N.CHUNK
+    S = 1
+    while B * H * S * 2 <= 148 and nch // (S * 2) >= 64:
+        S *= 2
+    return S if S >= 8 else 1
+
+
+def _unfold_kernel_ok(hm_sub):
+    B, S, H, K, VK = hm_sub.shape
+    return B == 1 and K == 128 and VK - K == 128 and hm_sub.is_cuda
+
+
 # The span-map folds run as fp32 torch products on the device (a few batched
 # K x K by K x (V+K) products per step) with TF32 switched off for their
 # duration, so they keep fp32 accuracy whatever the caller's matmul setting.
@@ -113,11 +135,19 @@ def _compose_maps(hm_sub):
     return x.contiguous()
 
 
-def _unfold_states(h0, hm_sub):
+def _unfold_states(h0, hm_sub, kern=None):
     """Initial state of every sub-span from the span's: s_0 = h0,
-    s_j = M_{j-1} s_{j-1} + h_e_{j-1}.  Returns [B*S, H, K, V]."""
+    s_j = M_{j-1} s_{j-1} + h_e_{j-1}.  Returns [B*S, H, K, V].  With
+    ``kern = (lib, prob_span, stream)`` and one sequence, one gdn2_cp_unfold
+    launch does the whole scan."""
     B, S, H, K, VK = hm_sub.shape
     V = VK - K
+    if kern is not None and _unfold_kernel_ok(hm_sub):
+        lib, prob_span, st = kern
+        out = torch.empty(B * S, H, K, V, dtype=torch.float32, device=hm_sub.device)
+        N.check(lib.gdn2_cp_unfold(prob_span, N.ptr(hm_sub), None, S, 1, N.ptr(h0), N.ptr(out),
+                                   st), "gdn2_cp_unfold")
+        return out
     out = [h0]
     with _NoTF32():
         for j in range(1, S):
@@ -141,10 +171,19 @@ def _compose_grads(dhm_sub, hm_sub, dht):
     return x.contiguous()
 
 
-def _unfold_grads(dht_span, dhm_sub, hm_sub):
+def _unfold_grads(dht_span, dhm_sub, hm_sub, kern=None):
     """End-state gradient of every sub-span from the span's: g_{S-1} =
-    dht_span,  g_j = M_{j+1}^T g_{j+1} + dhm_{j+1}.  Returns [B*S, H, K, V]."""
+    dht_span,  g_j = M_{j+1}^T g_{j+1} + dhm_{j+1}.  Returns [B*S, H, K, V]
+    (one gdn2_cp_unfold launch with ``kern`` and one sequence)."""
     B, S, H, K, V = dhm_sub.shape
+    if kern is not None and _unfold_kernel_ok(hm_sub):
+        lib, prob_span, st = kern
+        out = torch.empty(B * S, H, K, V, dtype=torch.float32, device=hm_sub.device)
+        dhm = dhm_sub.contiguous()
+        N.check(lib.gdn2_cp_unfold(prob_span, N.ptr(hm_sub), N.ptr(dhm), S, 0,
+                                   N.ptr(dht_span.contiguous()), N.ptr(out), st),
+                "gdn2_cp_unfold (backward)")
+        return out
     out = [dht_span]
     with _NoTF32():
         for j in range(S - 2, -1, -1):
@@ -165,7 +204,7 @@ class CPChunkGDN2Function(torch.autograd.Function):
         B, T, H, K = q.shape
         V = v.shape[-1]
         dev = q.device
-        S = _sub_spans(B, T, H, q.dtype)
+        S = sub_spans_single(B, T, H, K, V, q.dtype) if world == 1 else _sub_spans(B, T, H, q.dtype)
         # the kernels see the span as B*S sequences (same chunks)
         tables = N.split_tables(B, T, S, dev) if S > 1 else N.seq_tables(B, T, dev)
         prob = _problem(H, K, V, q.dtype, l2norm, scale, tables)
@@ -182,16 +221,22 @@ class CPChunkGDN2Function(torch.autograd.Function):
             N.check(lib.gdn2_cp_fwd_prescan(prob, N.ptr(saved), sbytes, N.ptr(hm_sub), None, 0,
                                             st), "gdn2_cp_fwd_prescan")
         hm_sub = hm_sub.view(B, S, H, K, V + K)
+        kern = (lib, prob_span, st)
+        if world > 1:
+            with N.phase("fwd_fold"):
+                hm = hm_sub[:, 0] if S == 1 else _compose_maps(hm_sub)
+            with N.phase("fwd_gather"):
+                hm_all = gather(hm.contiguous())
+            h0 = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
+            with N.phase("fwd_merge"):
+                N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), None, rank, world, 1,
+                                          N.ptr(initial_state), N.ptr(h0), st), "gdn2_cp_merge")
+        else:  # one span: no maps to exchange, its start state is the initial state
+            hm_all = hm_sub.new_empty(0)
+            h0 = (initial_state.float().contiguous() if initial_state is not None
+                  else torch.zeros(B, H, K, V, dtype=torch.float32, device=dev))
         with N.phase("fwd_fold"):
-            hm = hm_sub[:, 0] if S == 1 else _compose_maps(hm_sub)
-        with N.phase("fwd_gather"):
-            hm_all = gather(hm.contiguous())
-        h0 = torch.empty(B, H, K, V, dtype=torch.float32, device=dev)
-        with N.phase("fwd_merge"):
-            N.check(lib.gdn2_cp_merge(prob_span, N.ptr(hm_all), None, rank, world, 1,
-                                      N.ptr(initial_state), N.ptr(h0), st), "gdn2_cp_merge")
-        with N.phase("fwd_fold"):
-            h0_sub = h0 if S == 1 else _unfold_states(h0, hm_sub)
+            h0_sub = h0 if S == 1 else _unfold_states(h0, hm_sub, kern)
         o = torch.empty_like(v)
         ht_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
         with N.phase("fwd_state"):
@@ -242,10 +287,12 @@ class CPChunkGDN2Function(torch.autograd.Function):
                                                 N.ptr(dhm_sub), pws, pwb, st),
                         "gdn2_cp_bwd_prescan")
             dhm_sub = dhm_sub.view(B, S, H, K, V)
-            with N.phase("bwd_fold"):
-                dhm = _compose_grads(dhm_sub, hm_sub, dht_direct)
-        with N.phase("bwd_gather"):
-            dhm_all = gather(dhm)
+            if world > 1:
+                with N.phase("bwd_fold"):
+                    dhm = _compose_grads(dhm_sub, hm_sub, dht_direct)
+        if world > 1:
+            with N.phase("bwd_gather"):
+                dhm_all = gather(dhm)
         if last:
             dht_local = dht_direct
         else:
@@ -260,7 +307,7 @@ class CPChunkGDN2Function(torch.autograd.Function):
         if S > 1:
             end = dht_local if dht_local is not None else torch.zeros_like(h0)
             with N.phase("bwd_fold"):
-                dht_local = _unfold_grads(end, dhm_sub, hm_sub)
+                dht_local = _unfold_grads(end, dhm_sub, hm_sub, (lib, prob_span, st))
         grads = {n: torch.empty_like(t) for n, t in zip("qkvgbw", (q, k, v, g, b, w))}
         dh0_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
         # gdn2_chunk_bwd's two phases, called one by one so each can be timed

@@ -141,6 +141,10 @@ def test_cp_merge_argument_checks(lib):
     f = ctypes.c_void_p(0x1000)
     assert lib.gdn2_cp_merge(prob, f, f, 3, 2, 1, None, f, None) == N.ERR_INVALID
     assert lib.gdn2_cp_merge(prob, f, None, 0, 2, 0, None, f, None) == N.ERR_INVALID
+    # the sub-span scan: sizes, null pointers and the supported shapes
+    assert lib.gdn2_cp_unfold(prob, f, f, 0, 1, None, f, None) == N.ERR_INVALID
+    assert lib.gdn2_cp_unfold(prob, f, None, 4, 0, None, f, None) == N.ERR_INVALID
+    assert lib.gdn2_cp_unfold(prob, None, f, 4, 1, None, f, None) == N.ERR_INVALID
 
 
 def test_status_maps_to_python_exceptions(lib):

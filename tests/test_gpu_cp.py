@@ -221,3 +221,39 @@ def test_sequence_parallel_subspans_emulated_in_one_process(cuda_device):
     assert rel(hts[-1], ht_ref) < 2e-2
     for i, n in enumerate(NAMES):
         assert rel(torch.cat([g[i] for g in grads], 1), full[n].grad) < 2e-2, n
+
+
+def test_chunk_gdn2_few_heads_long_sequence_takes_subspans(cuda_device):
+    """chunk_gdn2 with few sequence-heads over a long sequence (B=1, H=2,
+    T=32,768) runs the single-GPU sub-span path (eight sub-spans of 64
+    chunks: pre-scan, one gdn2_cp_unfold launch per direction, state passes
+    on the pieces); on spans that carry state into each other its outputs,
+    final state and all gradients, the initial state's included, match the
+    plain chunk path."""
+    from qwendopamine_b200 import chunk_gdn2
+    from qwendopamine_b200.gdn2_ops.chunk_gdn2 import ChunkGDN2Function
+    from qwendopamine_b200.gdn2_ops.cp import sub_spans_single
+
+    B, T, H, K, V = 1, 32768, 2, 128, 128
+    assert sub_spans_single(B, T, H, K, V, torch.bfloat16) == 8
+    d = make_inputs(B, T, H, K, V, seed=31, decay=-0.0005, dtype=torch.bfloat16, h0=True)
+    d["b"] = (d["b"] * 0.01).bfloat16().float()  # weak erasure: the state outlives a piece
+    x = to_dev(d, cuda_device, torch.bfloat16)
+    gen = torch.Generator(device=cuda_device).manual_seed(6)
+    do = torch.randn(B, T, H, V, device=cuda_device, generator=gen).bfloat16()
+    dht = torch.randn(B, H, K, V, device=cuda_device, generator=gen)
+
+    l1 = {n: x[n].clone().requires_grad_() for n in (*NAMES, "h0")}
+    o1, h1 = chunk_gdn2(*(l1[n] for n in NAMES), initial_state=l1["h0"], output_final_state=True,
+                        use_qk_l2norm_in_kernel=True)
+    ((o1.float() * do.float()).sum() + (h1 * dht).sum()).backward()
+
+    l2 = {n: x[n].clone().requires_grad_() for n in (*NAMES, "h0")}
+    tables = N.seq_tables(B, T, cuda_device)
+    o2, h2 = ChunkGDN2Function.apply(*(l2[n] for n in NAMES), K ** -0.5, l2["h0"], True, True,
+                                     tables, torch.float32, None, None, None)
+    ((o2.float() * do.float()).sum() + (h2 * dht).sum()).backward()
+    torch.cuda.synchronize(cuda_device)
+    assert rel(o1, o2) < 2e-2 and rel(h1, h2) < 2e-2
+    for n in (*NAMES, "h0"):
+        assert rel(l1[n].grad, l2[n].grad) < 2e-2, n
