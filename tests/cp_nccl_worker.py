@@ -71,7 +71,7 @@ def main():
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = torch.device("cuda", local)
     B, H, K, V = 1, 4, 128, 128
-    T = 64 * 64 * world  # 64 chunks per rank: the span is cut into two sub-spans
+    T = 128 * 64 * world  # 128 chunks per rank: the span is cut into four sub-spans
     gen = torch.Generator(device=dev).manual_seed(0)
     bf = torch.bfloat16
     q = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf)
