@@ -98,8 +98,8 @@ PHASE_FLOPS = {
 }
 # Library phases that are one kernel launch each (the rest of a step's
 # phases -- the span-map folds, the NCCL all-gathers -- are torch / NCCL).
-NATIVE_PHASES = ("fwd_intra", "fwd_prescan", "fwd_merge", "fwd_state", "bwd_prescan",
-                 "bwd_merge", "bwd_state", "bwd_intra")
+NATIVE_PHASES = ("fwd_intra", "fwd_prescan", "fwd_merge", "fwd_unfold", "fwd_state",
+                 "bwd_prescan", "bwd_merge", "bwd_unfold", "bwd_state", "bwd_intra")
 # The metric's "% TC peak": the reference schedule's fwd+bwd FLOPs per
 # token-head, 20CK + 14CV + 22KV + 4C^2 = 655,360, over the step time, against
 # the measured bf16 peak and against the HBM-limited ceiling min(peak, AI x
@@ -554,10 +554,15 @@ def run_heads(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    from qwendopamine_b200.gdn2_ops.cp import sub_spans_single
+
+    S = sub_spans_single(1, T4, hper, K, V, torch.bfloat16)
+    path = (f"single-GPU sub-span path, {S} pieces (pre-scan, unfold, state passes on the "
+            "pieces)" if S > 1 else "plain chunk path")
     return {"workload": f"config4 head-sharded: {hper} of {H4} heads of the whole sequence "
-                        "per rank, no collective",
+                        f"per rank, no collective; {path}",
             "ms_per_step": round(ms, 3), "value": round(T4 / (ms / 1e3), 1),
-            "unit": "tokens/s", "gpu_launches": 4 * args.steps}
+            "unit": "tokens/s", "gpu_launches": (8 if S > 1 else 4) * args.steps}
 
 
 # ---------------------------------------------------------------------------

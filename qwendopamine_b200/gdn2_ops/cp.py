@@ -235,7 +235,7 @@ class CPChunkGDN2Function(torch.autograd.Function):
             hm_all = hm_sub.new_empty(0)
             h0 = (initial_state.float().contiguous() if initial_state is not None
                   else torch.zeros(B, H, K, V, dtype=torch.float32, device=dev))
-        with N.phase("fwd_fold"):
+        with N.phase("fwd_unfold" if S > 1 and _unfold_kernel_ok(hm_sub) else "fwd_fold"):
             h0_sub = h0 if S == 1 else _unfold_states(h0, hm_sub, kern)
         o = torch.empty_like(v)
         ht_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
@@ -306,7 +306,7 @@ class CPChunkGDN2Function(torch.autograd.Function):
                     dht_local += dht_direct
         if S > 1:
             end = dht_local if dht_local is not None else torch.zeros_like(h0)
-            with N.phase("bwd_fold"):
+            with N.phase("bwd_unfold" if _unfold_kernel_ok(hm_sub) else "bwd_fold"):
                 dht_local = _unfold_grads(end, dhm_sub, hm_sub, (lib, prob_span, st))
         grads = {n: torch.empty_like(t) for n, t in zip("qkvgbw", (q, k, v, g, b, w))}
         dh0_sub = torch.empty(B * S, H, K, V, dtype=torch.float32, device=dev)
