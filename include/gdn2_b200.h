@@ -86,6 +86,16 @@ typedef struct gdn2_chunk_problem {
     float lower_bound;
     float* dA_log;
     float* ddt_bias;
+    /* SM budget of one launch; 0 = the whole GPU.  No counterpart in the
+     * reference: a caller that runs a state pass and an intra-chunk kernel
+     * on two streams at the same time divides the SMs between them this way.
+     *   - gdn2_chunk_fwd_intra (bf16, head sizes up to 128): the persistent
+     *     kernel launches at most max_ctas CTAs (one per SM otherwise);
+     *   - gdn2_chunk_fwd_state / gdn2_chunk_bwd_state (bf16, K = V = 128):
+     *     the split of each sequence-head's value columns over two CTAs is
+     *     used only while it stays within max_ctas CTAs; otherwise one CTA
+     *     per sequence-head walks the whole state. */
+    int32_t max_ctas;
 } gdn2_chunk_problem;
 
 /* ---- library information ------------------------------------------------ */

@@ -79,6 +79,7 @@ class ChunkProblem(ctypes.Structure):
         ("lower_bound", c_float),
         ("dA_log", c_void_p),
         ("ddt_bias", c_void_p),
+        ("max_ctas", c_int32),
     ]
 
 
@@ -254,18 +255,19 @@ def phase_timing():
 
 
 @contextlib.contextmanager
-def phase(name: str):
-    """Bracket one phase with CUDA events while :func:`phase_timing` is open."""
+def phase(name: str, stream=None):
+    """Bracket one phase with CUDA events while :func:`phase_timing` is open
+    (on ``stream``, a ``torch.cuda.Stream``, or the current stream)."""
     rec = _phase_records
     if rec is None:
         yield
         return
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
+    s.record(stream)
     try:
         yield
     finally:
-        e.record()
+        e.record(stream)
         rec.append((name, s, e))
 
 

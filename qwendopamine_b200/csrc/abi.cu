@@ -84,6 +84,8 @@ int check_problem(const gdn2_chunk_problem* p, const char* fn) {
     return fail(GDN2_ERR_INVALID, "%s: missing chunk table", fn);
   if ((int64_t)p->seqs.n_chunks * p->H > 2147483647LL)
     return fail(GDN2_ERR_UNSUPPORTED, "%s: too many chunks", fn);
+  if (p->max_ctas < 0)
+    return fail(GDN2_ERR_INVALID, "%s: max_ctas must be >= 0 (got %d)", fn, p->max_ctas);
   if (p->gate < 0 || p->gate > 2 || (p->gate && !p->A_log))
     return fail(GDN2_ERR_INVALID, "%s: gate %d needs A_log (modes 0..2)", fn, p->gate);
   if (p->gate && !(p->dtype == GDN2_DTYPE_BF16 && p->K % 8 == 0 && p->V % 8 == 0 &&
@@ -532,6 +534,7 @@ int gdn2_chunk_fwd_intra(const gdn2_chunk_problem* p, const void* q, const void*
   a.saved = static_cast<unsigned char*>(saved);
   a.L = L;
   a.total_rows = p->seqs.total_tokens;
+  a.max_ctas = p->max_ctas;
   cudaError_t e = fault_word(&a.fault);
   if (e != cudaSuccess) return cuda_fail(e, "gdn2_chunk_fwd_intra");
   e = fwd_intra_dispatch(p, a, (cudaStream_t)stream);
@@ -558,6 +561,7 @@ int gdn2_chunk_fwd_state(const gdn2_chunk_problem* p, const float* h0, void* o, 
   a.L = L;
   a.prescan = 0;
   a.hm = nullptr;
+  a.max_ctas = p->max_ctas;
   cudaError_t e = fwd_state_dispatch(p, a, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_fwd_state");
 }
@@ -597,6 +601,7 @@ int gdn2_chunk_bwd_state(const gdn2_chunk_problem* p, const void* saved, size_t 
   s.BL = BL;
   s.prescan = 0;
   s.total_rows = p->seqs.total_tokens;
+  s.max_ctas = p->max_ctas;
   cudaError_t e = bwd_state_dispatch(p, s, (cudaStream_t)stream);
   return e == cudaSuccess ? GDN2_OK : cuda_fail(e, "gdn2_chunk_bwd_state");
 }

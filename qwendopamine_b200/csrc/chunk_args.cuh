@@ -60,6 +60,7 @@ struct FwdIntraArgs {
   SavedLayout L;
   unsigned int* fault;  // device fault word (bounded waits that ran out)
   int64_t total_rows;   // token rows of q, k, v, g, b, w (bounds of their TMA views)
+  int max_ctas = 0;     // persistent kernel: at most this many CTAs (0: one per SM)
 };
 
 struct FwdStateArgs {
@@ -78,6 +79,7 @@ struct FwdStateArgs {
   // skip_chunk's tiles are never requested (-1: none).
   uint64_t wait_ns = 0;
   int skip_chunk = -1;
+  int max_ctas = 0;  // tcgen05 pass: the value-half split only within this many CTAs (0: SMs)
 };
 
 struct BwdStateArgs {
@@ -92,6 +94,7 @@ struct BwdStateArgs {
   BwdLayout BL;
   int prescan;        // 1: write nothing per chunk, only the span-start gradient
   int64_t total_rows; // token rows of dout (bounds of its TMA view)
+  int max_ctas = 0;   // tcgen05 pass: the value-half split only within this many CTAs (0: SMs)
 };
 
 struct BwdIntraArgs {

@@ -587,7 +587,10 @@ cudaError_t launch_fwd_intra16(const FwdIntraArgs& a, cudaStream_t st) {
   int sms = 0;
   e = num_sms(&sms);
   if (e != cudaSuccess) return e;
-  const int grid = n_items < sms ? n_items : sms;  // persistent: one CTA per SM
+  // persistent: one CTA per SM, or fewer when the caller leaves SMs to a
+  // state pass running beside this launch
+  if (a.max_ctas > 0 && a.max_ctas < sms) sms = a.max_ctas;
+  const int grid = n_items < sms ? n_items : sms;
   kern<<<grid, kThreadsF16, Fwd16Layout<D>::bytes, st>>>(a, mQ, mK, mB, mV, mW, mG);
   return cudaGetLastError();
 }

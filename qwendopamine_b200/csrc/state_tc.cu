@@ -1480,6 +1480,7 @@ cudaError_t launch_bwd_state_tc(const BwdStateArgs& a, cudaStream_t st) {
   int sms = 0;
   cudaError_t e = num_sms(&sms);
   if (e != cudaSuccess) return e;
+  if (a.max_ctas > 0 && a.max_ctas < sms) sms = a.max_ctas;
   if (2 * grid <= sms) {  // few sequence-heads: one CTA per half of the value columns
     e = cudaFuncSetAttribute(k_bwd_state_tc_half, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kBSmemBytes);
@@ -1519,6 +1520,7 @@ cudaError_t launch_fwd_state_tc(const FwdStateArgs& a, cudaStream_t st) {
   int sms = 0;
   cudaError_t e = num_sms(&sms);
   if (e != cudaSuccess) return e;
+  if (a.max_ctas > 0 && a.max_ctas < sms) sms = a.max_ctas;
   if (2 * grid <= sms) {
     // few sequence-heads: two CTAs each, one per half of the value columns
     CUtensorMap mUh;

@@ -326,15 +326,24 @@ def chunk_gdn2(
                 ht = ht.transpose(-1, -2)
             return o, ht, hs
         from .cp import CPChunkGDN2Function, sub_spans_single
+        from .overlap import OverlapChunkGDN2Function, overlap_pieces
 
-        if (cu_seqlens is None and A32 is None and
-                sub_spans_single(B, T, H, K, v.shape[-1], dt) > 1):
+        V = v.shape[-1]
+        pieces = overlap_pieces(B, T, H, K, V, dt, q.device) if cu_seqlens is None else 1
+        if (cu_seqlens is None and A32 is None and sub_spans_single(B, T, H, K, V, dt) > 1):
             # few sequence-heads over long sequences: the sub-span pre-scan,
             # the unfold of the start states and S-fold shorter state passes
             o, ht = CPChunkGDN2Function.apply(q, k, v, g, b, w, h0, scale,
                                               use_qk_l2norm_in_kernel, 0, 1, None)
             if not output_final_state:
                 ht = None
+        elif pieces > 1:
+            # one long sequence, a few dozen heads: the state passes of the
+            # sequence's pieces overlap the intra-chunk kernels of their
+            # neighbours on a second stream
+            o, ht = OverlapChunkGDN2Function.apply(q, k, v, g, b, w, scale, h0,
+                                                   output_final_state, use_qk_l2norm_in_kernel,
+                                                   pieces, A32, dt32, lb)
         else:
             o, ht = ChunkGDN2Function.apply(q, k, v, g, b, w, scale, h0, output_final_state,
                                             use_qk_l2norm_in_kernel, tables, g_dtype, A32, dt32,

@@ -182,3 +182,36 @@ def test_split_tables_keep_the_chunks():
     with pytest.raises(ValueError):
         N.split_tables(1, 64, 2, "cpu")  # one chunk cannot make two sub-spans
     assert N.split_tables(2, 300, 2, "cpu") is t  # cached
+
+
+def test_overlap_piece_cuts_and_routing(monkeypatch):
+    """The overlapped path's pieces cover the sequence in whole chunks, and it
+    is chosen only for one long bf16 sequence (K = V = 128) whose value-half
+    state passes leave SMs to the intra kernels."""
+    from qwendopamine_b200.gdn2_ops import overlap as OV
+
+    for T, P in [(262144, 16), (64 * 70 + 17, 3), (577, 2), (4096, 4)]:
+        cuts = OV._cuts(T, P)
+        assert cuts[0] == 0 and cuts[-1] == T and len(cuts) == P + 1
+        assert all(c % 64 == 0 for c in cuts[:-1])
+        assert all(a < b for a, b in zip(cuts, cuts[1:]))
+    monkeypatch.setattr(OV, "_sm_count", lambda dev: 148)
+    monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": True, "bwd": True})
+    bf = torch.bfloat16
+    assert OV.overlap_pieces(1, 262144, 32, 128, 128, bf, None) == 16
+    assert OV.overlap_pieces(1, 32768, 32, 128, 128, bf, None) == 2
+    assert OV.overlap_pieces(1, 16384, 32, 128, 128, bf, None) == 1   # one piece's worth
+    assert OV.overlap_pieces(2, 262144, 32, 128, 128, bf, None) == 1  # batch > 1
+    assert OV.overlap_pieces(1, 262144, 64, 128, 128, bf, None) == 16  # 84 SMs left
+    assert OV.overlap_pieces(1, 262144, 120, 128, 128, bf, None) == 1  # 28 SMs left
+    assert OV.overlap_pieces(1, 262144, 32, 64, 64, bf, None) == 1
+    assert OV.overlap_pieces(1, 262144, 32, 128, 128, torch.float32, None) == 1
+    monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": True, "bwd": False})
+    assert OV.overlap_pieces(1, 262144, 64, 128, 128, bf, None) == 1  # value halves: 20 left
+    # the cost model's choice: 32 heads take full width both ways; with 16
+    # heads the forward's chain is the limit and the value halves win
+    monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": None, "bwd": None})
+    assert OV.full_width("fwd", 4096, 32, 148) and OV.full_width("bwd", 4096, 32, 148)
+    assert not OV.full_width("fwd", 4096, 16, 148) and OV.full_width("bwd", 4096, 16, 148)
+    assert OV.full_width("fwd", 4096, 64, 148)  # value halves would leave 20 SMs
+    assert OV.overlap_pieces(1, 262144, 16, 128, 128, bf, None) == 16
