@@ -99,14 +99,15 @@ def test_overlap_equals_one_stream_path(cuda_device, one_stream_widths, T, H, pi
             assert rel(a, r) < 1e-5, f"{n}: rel {rel(a, r):.3e}"
 
 
-@pytest.mark.parametrize("full", [True, False])
-def test_overlap_matches_oracle(cuda_device, monkeypatch, full):
+@pytest.mark.parametrize("fwd_full,bwd_full", [(True, True), (False, False), (False, True)])
+def test_overlap_matches_oracle(cuda_device, monkeypatch, fwd_full, bwd_full):
     """Two heads of an overlapped run against the float64 token-serial
-    recurrence and its reverse pass, with the state passes at full width
-    and in value halves."""
+    recurrence and its reverse pass, with the state passes at full width, in
+    value halves, and mixed (value-half forward, full-width backward: what
+    the cost model picks for 16 heads)."""
     from qwendopamine_b200.gdn2_ops import overlap as OV
 
-    monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": full, "bwd": full})
+    monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": fwd_full, "bwd": bwd_full})
     T, H = 64 * 40 + 5, 10
     d, x, do, dht, _ = _inputs(cuda_device, T, H, seed=7)
     o, ht, grads = _run_overlap(x, x["h0"], do, dht, 4)
