@@ -19,12 +19,15 @@ backward: on the side stream state(P-1), ..., state(0), each from the start-
           leaves.
 
 Beside the intra kernels the state passes may run at full width (H CTAs, a
-longer chain) rather than in value halves (2H CTAs): a small cost model
-picks, per direction, whichever it expects to finish sooner.  With 32 heads
-over 4,096 chunks both directions take full width (one B200: 41.4 ms per
-forward + backward on one stream, 36.4 ms overlapped in value halves, 33.4 ms
-overlapped at full width); with 16 heads the forward keeps the value halves,
-whose shorter chain is then the limit.
+longer chain) rather than in value halves (2H CTAs), and a state pass that
+runs alone (the backward's first, the forward's once every intra kernel is
+done) takes the faster value halves.  A small cost model from measured
+per-chunk costs makes both choices.  With 32 heads over 4,096 chunks the
+forward runs its first pieces at full width and its last ones in halves,
+the backward at full width (one B200: 41.4 ms per forward + backward on one
+stream, 36.4 ms overlapped in value halves, 33.4 ms at full width); with 16
+heads the forward keeps the value halves, whose shorter chain is then the
+limit.
 
 The kernels, their per-chunk work and the fp32 state handed from piece to
 piece are those of the one-stream path; at the one-stream path's width the
@@ -109,6 +112,43 @@ def _state_ctas(direction: str, nch: int, H: int, sms: int) -> int:
     return H if full_width(direction, nch, H, sms) else 2 * H
 
 
+def _model_fwd(ns, H: int, sms: int, j: int) -> float:
+    """Modelled forward time (ms) over pieces of ``ns`` chunks when the first
+    ``j`` state passes run at full width beside the intra kernels and the
+    rest in value halves: with j = 0 every pass runs in halves beside the
+    intra kernels, otherwise the half-width passes wait for the last intra
+    kernel and have the GPU to themselves."""
+    cap = sms - (H if j > 0 else 2 * H)
+    t, ends = 0.0, []
+    for p, n in enumerate(ns):
+        t += n * H * INTRA_SM_MS["fwd"] / (sms if p == 0 else cap)
+        ends.append(t)
+    side = 0.0
+    for p, n in enumerate(ns):
+        full = p < j
+        ready = ends[p] if (full or j == 0) else ends[-1]
+        side = max(side, ready) + n * CHAIN_MS[("fwd", full)]
+    return max(t, side)
+
+
+def forward_plan(ns, H: int, sms: int) -> int:
+    """How many leading pieces' forward state passes run at full width (the
+    others in value halves; see :func:`_model_fwd`): all of them or none when
+    FULL_WIDTH forces it, else the count the model expects to end soonest
+    among those that leave MIN_FREE_SMS SMs to the intra kernels."""
+    P = len(ns)
+    forced = FULL_WIDTH["fwd"]
+    if forced is not None:
+        return P if forced else 0
+    cands = [j for j in range(P + 1) if sms - (H if j > 0 else 2 * H) >= MIN_FREE_SMS]
+    return min(cands, key=lambda j: _model_fwd(ns, H, sms, j))
+
+
+def _piece_chunks(T: int, P: int):
+    cuts = _cuts(T, P)
+    return [(cuts[p + 1] + N.CHUNK - 1) // N.CHUNK - cuts[p] // N.CHUNK for p in range(P)]
+
+
 def overlap_pieces(B, T, H, K, V, dtype, device) -> int:
     """Pieces for the overlapped path (1: not used).  Used for one fixed-length
     bf16 sequence with K = V = 128 whose state passes leave at least
@@ -118,7 +158,9 @@ def overlap_pieces(B, T, H, K, V, dtype, device) -> int:
         return 1
     sms = _sm_count(device)
     nch = (T + N.CHUNK - 1) // N.CHUNK
-    if any(sms - _state_ctas(d, nch, H, sms) < MIN_FREE_SMS for d in FULL_WIDTH):
+    if sms - _state_ctas("bwd", nch, H, sms) < MIN_FREE_SMS:
+        return 1
+    if sms - (2 * H if FULL_WIDTH["fwd"] is False else H) < MIN_FREE_SMS:
         return 1
     P = min(MAX_PIECES, nch // MIN_PIECE_CHUNKS)
     return P if P >= 2 else 1
@@ -177,25 +219,33 @@ def _fwd(q, k, v, g, b, w, scale, h0, want_ht, l2, gate, P):
     ht = q.new_empty(1, H, K, V, dtype=torch.float32) if want_ht else None
     main, side = torch.cuda.current_stream(dev), _side_stream(dev)
     sms = _sm_count(dev)
-    nch = (T + N.CHUNK - 1) // N.CHUNK
-    state_ctas = _state_ctas("fwd", nch, H, sms)
-    cap = sms - state_ctas
+    j = forward_plan(_piece_chunks(T, P), H, sms)
+    cap = sms - (H if j > 0 else 2 * H)
     side.wait_stream(main)
     ms, ss = N.c_void_p(main.cuda_stream), N.c_void_p(side.cuda_stream)
+    done = []  # per piece: an event after its intra kernel
     for p in range(P):
         prob = pc.probs[p]
         prob.max_ctas = 0 if p == 0 else cap
-        sv = N.c_void_p(saved.data_ptr() + pc.so[p])
         with N.phase("fwd_intra", main):
             N.check(lib.gdn2_chunk_fwd_intra(prob, *(N.ptr(pc.rows(t, p)) for t in (q, k, v, g, b, w)),
-                                             sv, pc.sb[p], ms), "gdn2_chunk_fwd_intra")
-        side.wait_stream(main)
+                                             N.c_void_p(saved.data_ptr() + pc.so[p]), pc.sb[p], ms),
+                    "gdn2_chunk_fwd_intra")
+        done.append(torch.cuda.Event())
+        done[-1].record(main)
+    for p in range(P):
+        prob = pc.probs[p]
+        full = p < j
+        # a half-width pass after full-width ones waits for every intra
+        # kernel: it then has the GPU to itself
+        side.wait_event(done[p] if (full or j == 0) else done[-1])
         h_in = h0 if p == 0 else carry[p - 1]
         h_out = carry[p] if p < P - 1 else ht
-        prob.max_ctas = state_ctas
+        prob.max_ctas = H if full else 2 * H
         with N.phase("fwd_state", side):
             N.check(lib.gdn2_chunk_fwd_state(prob, N.ptr(h_in), N.ptr(pc.rows(o, p)), N.ptr(h_out),
-                                             sv, pc.sb[p], ss), "gdn2_chunk_fwd_state")
+                                             N.c_void_p(saved.data_ptr() + pc.so[p]), pc.sb[p], ss),
+                    "gdn2_chunk_fwd_state")
     main.wait_stream(side)
     return o, ht, saved, pc
 
@@ -220,6 +270,9 @@ def _bwd(q, k, v, g, b, w, saved, pc, do, dht, h0, gate):
     dcarry = torch.empty(max(P - 1, 1), 1, H, K, V, dtype=torch.float32, device=dev)
     main, side = torch.cuda.current_stream(dev), _side_stream(dev)
     state_ctas = _state_ctas("bwd", (T + N.CHUNK - 1) // N.CHUNK, H, _sm_count(dev))
+    # the last piece's pass runs before any intra kernel can: in value halves
+    # unless a width is forced
+    first_ctas = 2 * H if FULL_WIDTH["bwd"] is None else state_ctas
     side.wait_stream(main)
     ms, ss = N.c_void_p(main.cuda_stream), N.c_void_p(side.cuda_stream)
     for p in reversed(range(P)):
@@ -228,7 +281,7 @@ def _bwd(q, k, v, g, b, w, saved, pc, do, dht, h0, gate):
         wv = N.c_void_p(ws.data_ptr() + pc.wo[p])
         d_end = dht if p == P - 1 else dcarry[p]
         d_start = dh0 if p == 0 else dcarry[p - 1]
-        prob.max_ctas = state_ctas
+        prob.max_ctas = first_ctas if p == P - 1 else state_ctas
         with N.phase("bwd_state", side):
             N.check(lib.gdn2_chunk_bwd_state(prob, sv, pc.sb[p], N.ptr(pc.rows(do, p)), N.ptr(d_end),
                                              N.ptr(d_start), wv, pc.wb[p], ss),

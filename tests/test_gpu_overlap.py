@@ -108,11 +108,28 @@ def test_overlap_matches_oracle(cuda_device, monkeypatch, fwd_full, bwd_full):
     from qwendopamine_b200.gdn2_ops import overlap as OV
 
     monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": fwd_full, "bwd": bwd_full})
-    T, H = 64 * 40 + 5, 10
-    d, x, do, dht, _ = _inputs(cuda_device, T, H, seed=7)
-    o, ht, grads = _run_overlap(x, x["h0"], do, dht, 4)
+    _check_oracle(cuda_device, 64 * 40 + 5, 10, 4, seed=7, hs=slice(3, 5))
+
+
+def test_overlap_cost_model_plan_matches_oracle(cuda_device, monkeypatch):
+    """The widths the cost model picks for 32 heads over three pieces: the
+    first two forward state passes at full width beside the intra kernels,
+    the third in value halves after them, the backward's first pass in
+    value halves and the others at full width."""
+    from qwendopamine_b200.gdn2_ops import overlap as OV
+
+    monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": None, "bwd": None})
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    if sms == 148:
+        assert OV.forward_plan([32] * 3, 32, sms) == 2
+        assert OV.full_width("bwd", 96, 32, sms)
+    _check_oracle(cuda_device, 64 * 96, 32, 3, seed=11, hs=slice(30, 32))
+
+
+def _check_oracle(dev, T, H, pieces, seed, hs):
+    d, x, do, dht, _ = _inputs(dev, T, H, seed=seed)
+    o, ht, grads = _run_overlap(x, x["h0"], do, dht, pieces)
     torch.cuda.synchronize()
-    hs = slice(3, 5)
     sub = {n: d[n][:, :, hs] for n in NAMES}
     args = np_(sub, NAMES)
     h0 = d["h0"][:, hs].double().numpy()

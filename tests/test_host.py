@@ -208,10 +208,19 @@ def test_overlap_piece_cuts_and_routing(monkeypatch):
     assert OV.overlap_pieces(1, 262144, 32, 128, 128, torch.float32, None) == 1
     monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": True, "bwd": False})
     assert OV.overlap_pieces(1, 262144, 64, 128, 128, bf, None) == 1  # value halves: 20 left
-    # the cost model's choice: 32 heads take full width both ways; with 16
-    # heads the forward's chain is the limit and the value halves win
+    # the cost model's choices: with 32 heads the forward runs 13 of 16
+    # pieces at full width beside the intra kernels and the last 3 in value
+    # halves after them, the backward at full width; with 16 heads the
+    # forward's chain is the limit and the value halves win throughout
     monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": None, "bwd": None})
-    assert OV.full_width("fwd", 4096, 32, 148) and OV.full_width("bwd", 4096, 32, 148)
-    assert not OV.full_width("fwd", 4096, 16, 148) and OV.full_width("bwd", 4096, 16, 148)
-    assert OV.full_width("fwd", 4096, 64, 148)  # value halves would leave 20 SMs
+    ns = [256] * 16
+    assert OV.forward_plan(ns, 32, 148) == 13
+    assert OV._model_fwd(ns, 32, 148, 13) < OV._model_fwd(ns, 32, 148, 16) < OV._model_fwd(ns, 32, 148, 0)
+    assert OV.forward_plan(ns, 16, 148) == 0
+    assert OV.forward_plan(ns, 64, 148) > 0  # value halves beside the intra kernels: 20 SMs
+    assert OV.full_width("bwd", 4096, 32, 148) and OV.full_width("bwd", 4096, 16, 148)
     assert OV.overlap_pieces(1, 262144, 16, 128, 128, bf, None) == 16
+    monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": True, "bwd": True})
+    assert OV.forward_plan(ns, 32, 148) == 16
+    monkeypatch.setattr(OV, "FULL_WIDTH", {"fwd": False, "bwd": True})
+    assert OV.forward_plan(ns, 32, 148) == 0
