@@ -695,6 +695,39 @@ def run_config1(args, world, rank, local):
     }
 
 
+def run_step4(args):
+    """Only the headline's timed loop: config-4 forward + backward steps on
+    one GPU through ``chunk_gdn2`` (the overlapped path), ``--warmup`` +
+    ``--steps`` steps with per-phase CUDA events; no end-to-end leg, CPU
+    baseline or sub-record (a short program for ncu launch lists)."""
+    from qwendopamine_b200 import _native as N
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    N.load()
+    x = config4_scalars(dev, 0, T4)
+    leaves = leaves_of(x)
+    fwd = config4_step_fn(1, 0)
+
+    def step():
+        torch.autograd.grad(fwd(leaves), leaves, x["do"])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with N.phase_timing() as rec:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    return {"ms_per_step": round(ms, 4), "tokens_per_s": round(T4 / (ms / 1e3), 1),
+            "phases": phase_summary(rec, args.steps),
+            "gpu_launches": sum(1 for n, _, _ in rec if n in NATIVE_PHASES)}
+
+
 def run_profile_case(args, local):
     """Small case for ncu captures: the step's four phases through the C ABI
     at ``--batch`` x ``--seq`` tokens x ``--heads`` heads (config-1 shapes by
@@ -1260,8 +1293,10 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--workload", choices=("config4", "block", "decode"), default="config4",
-                    help="config4 (headline, with every sub-record), or only the block "
+    ap.add_argument("--workload", choices=("config4", "step4", "block", "decode"),
+                    default="config4",
+                    help="config4 (headline, with every sub-record), or only the headline's "
+                         "timed config-4 steps on one GPU (step4), or only the block "
                          "prologue / epilogue kernels (--steps timed launches each after "
                          "--warmup, one GPU), or only the config-2 decode step")
     ap.add_argument("--skip-model", action="store_true",
@@ -1274,6 +1309,9 @@ def main(argv=None):
     args = ap.parse_args(argv)
     if args.profile:
         run_profile_case(args, int(os.environ.get("LOCAL_RANK", "0")))
+        return
+    if args.workload == "step4":
+        print(json.dumps({"workload": "step4", "step4": run_step4(args)}), flush=True)
         return
     if args.workload in ("block", "decode"):
         from qwendopamine_b200 import _native as N
