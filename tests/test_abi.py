@@ -200,3 +200,16 @@ def test_conv_and_norm_arguments_are_checked(lib):
                       (N.NormProblem(10, 64, 1, 0, 1e-5, 3), N.ERR_INVALID)):
         assert lib.gdn2_gated_norm_fwd(bad, *([None] * 4), None) == code
     assert lib.gdn2_gated_norm_fwd(N.NormProblem(0, 64, 1, 1, 1e-5, 0), *([None] * 4), None) == 0
+
+
+def test_negative_sm_budget_is_rejected(lib):
+    """max_ctas (the SM budget a two-stream caller gives one launch) must be
+    >= 0; 0, the default, keeps the whole GPU."""
+    p = _problem()
+    assert p.max_ctas == 0 and lib.gdn2_chunk_saved_bytes(p) > 0
+    p.max_ctas = -1
+    assert lib.gdn2_chunk_saved_bytes(p) == 0
+    assert b"max_ctas" in lib.gdn2_last_error()
+    assert lib.gdn2_chunk_fwd_intra(p, *([None] * 6), None, 0, None) == N.ERR_INVALID
+    p.max_ctas = 116
+    assert lib.gdn2_chunk_saved_bytes(p) > 0
