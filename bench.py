@@ -593,14 +593,22 @@ def run_heads(args, world, rank, local):
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     from qwendopamine_b200.gdn2_ops.cp import sub_spans_single
+    from qwendopamine_b200.gdn2_ops.overlap import overlap_pieces
 
     S = sub_spans_single(1, T4, hper, K, V, torch.bfloat16)
-    path = (f"single-GPU sub-span path, {S} pieces (pre-scan, unfold, state passes on the "
-            "pieces)" if S > 1 else "plain chunk path")
+    P = overlap_pieces(1, T4, hper, K, V, torch.bfloat16, dev)
+    if S > 1:
+        path, per_step = (f"single-GPU sub-span path, {S} pieces (pre-scan, unfold, state "
+                          "passes on the pieces)"), 8
+    elif P > 1:
+        path, per_step = (f"overlapped path, {P} pieces (state passes on a second stream "
+                          "beside the intra kernels)"), 4 * P
+    else:
+        path, per_step = "plain chunk path", 4
     return {"workload": f"config4 head-sharded: {hper} of {H4} heads of the whole sequence "
                         f"per rank, no collective; {path}",
             "ms_per_step": round(ms, 3), "value": round(T4 / (ms / 1e3), 1),
-            "unit": "tokens/s", "gpu_launches": (8 if S > 1 else 4) * args.steps}
+            "unit": "tokens/s", "gpu_launches": per_step * args.steps}
 
 
 # ---------------------------------------------------------------------------
