@@ -125,6 +125,37 @@ def test_span_transition_composes_to_full_sequence(small):
     assert rel(h, full_h) < 1e-9
 
 
+def test_pieces_chained_by_state_and_state_gradient_give_the_whole_sequence(small):
+    """The identity the overlapped path (pieces of one sequence, each its own
+    problem) relies on: forward passes chained through their end states give
+    the whole sequence's outputs and final state, and backward passes walked
+    in reverse, each started from the start-state gradient of the piece after
+    it, give the whole sequence's gradients."""
+    d = small
+    names = ("q", "k", "v", "g", "b", "w")
+    x = {n: d[n][:1].astype(np.float64) for n in names}
+    h0, do, dht = d["h0"][:1], d["do"][:1], d["dht"][:1]
+    full_o, full_h = O.recurrent_fwd(*(x[n] for n in names), h0)
+    full_g = O.recurrent_bwd(*(x[n] for n in names), do, h0, dht)
+    cuts = [0, 13, 30, d["q"].shape[1]]
+    pieces = list(zip(cuts[:-1], cuts[1:]))
+    outs, starts, h = [], [], h0
+    for a, b in pieces:
+        starts.append(h)
+        o, h = O.recurrent_fwd(*(x[n][:, a:b] for n in names), h)
+        outs.append(o)
+    assert rel(np.concatenate(outs, axis=1), full_o) < 1e-12
+    assert rel(h, full_h) < 1e-12
+    grads, d_end = [None] * len(pieces), dht
+    for i in reversed(range(len(pieces))):
+        a, b = pieces[i]
+        grads[i] = O.recurrent_bwd(*(x[n][:, a:b] for n in names), do[:, a:b], starts[i], d_end)
+        d_end = grads[i][6]
+    for j, n in enumerate(("dq", "dk", "dv", "dg", "db", "dw")):
+        assert rel(np.concatenate([g[j] for g in grads], axis=1), full_g[j]) < 1e-12, n
+    assert rel(d_end, full_g[6]) < 1e-12
+
+
 def test_varlen_oracle_keeps_sequences_independent(small):
     d = small
     names = ("q", "k", "v", "g", "b", "w")
