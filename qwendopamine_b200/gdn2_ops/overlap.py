@@ -25,9 +25,9 @@ done) takes the faster value halves.  A small cost model from measured
 per-chunk costs makes both choices.  With 32 heads over 4,096 chunks the
 forward runs its first pieces at full width and its last ones in halves,
 the backward at full width (one B200: 41.4 ms per forward + backward on one
-stream, 36.4 ms overlapped in value halves, 33.4 ms at full width); with 16
-heads the forward keeps the value halves, whose shorter chain is then the
-limit.
+stream, 36.4 ms overlapped in value halves, 33.4 ms at full width, 32.7 ms
+with the planned widths); with 16 heads the forward keeps the value halves,
+whose shorter chain is then the limit (21.0 against 28.4 ms on one stream).
 
 The kernels, their per-chunk work and the fp32 state handed from piece to
 piece are those of the one-stream path; at the one-stream path's width the
